@@ -1,0 +1,353 @@
+#!/usr/bin/env python
+"""SSD chunked-scan forward + backward benchmark on B200 (rewrite of the reference's
+scripts/bench_ssd.py, which timed zenith.mamba3.ssd fwd+bwd on Apple MPS).
+
+One step = one forward and one backward of the SSD scan over one batch of the model-scale
+layer workload (B8 T2048 H24 P64 N128, chunk 64, bf16 vectors with fp32 per-token scalars,
+synthetic inputs with the Mamba-3 value distributions).  Multi-GPU: one process per GPU
+(torchrun); batch x heads are independent, so each rank runs its own batch of the workload
+(weak scaling, no collective on the data path); the timed region is bracketed by barriers
+and the slowest rank's CUDA-event time is reported.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  ``--impl reference`` times the reference algorithm on the
+host CPU cores instead (rank 0 only): the CPU restatement of zenith/mamba3.py:30-56 in
+fp32 under PyTorch autograd, the same torch work the reference does on a CPU.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import datetime
+import io
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "SSD fwd+bwd tokens/s"
+UNIT = "tokens/s"
+NAMES = ("x", "q", "k", "kp", "xp", "adt", "gamma", "beta")
+VEC = ("x", "q", "k", "kp", "xp")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", default="layer")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
+    return ap.parse_args()
+
+
+def algorithmic_bytes(shape, e_in=2, e_sc=4):
+    """Per token per head (each input read once per pass, each output written once):
+    fwd = e(2P + 3N/r) + 3 e_s + e P ;  bwd = e(2P + 3N/r) + 3 e_s + e P (dy) + e(2P + 3N/r) + 3 e_s."""
+    r = shape.H // shape.G
+    vin = e_in * (2 * shape.P + 3 * shape.N / r) + 3 * e_sc
+    fwd = vin + e_in * shape.P
+    bwd = vin + e_in * shape.P + vin
+    return fwd, bwd
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_from_profile(kernel: str):
+    """DRAM bytes per launch from the committed ncu summary (profiles/traffic.json), if any."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    v = d.get(kernel)
+    return None if v is None else float(v)
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling while the timed region runs."""
+
+    FIELDS = ("clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
+              "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+              "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            if not uuid.startswith("GPU-"):
+                uuid = "GPU-" + uuid
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={uuid}", "--query-gpu=" + ",".join(self.FIELDS), "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r for r in csv.reader(io.StringIO(out)) if len(r) >= len(self.FIELDS)]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+        sm = [num(r[0]) for r in rows if num(r[0]) is not None]
+        mx = [num(r[1]) for r in rows if num(r[1]) is not None]
+        reasons = set()
+        for r in rows:
+            for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), r[4:8]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def make_device_inputs(shape, rank, dev):
+    from zenith_b200.synthetic import make_inputs
+
+    inp = make_inputs(shape, seed=rank)
+    out = {}
+    for n in NAMES + ("dy",):
+        t = inp[n].to(torch.bfloat16) if (n in VEC or n == "dy") else inp[n]
+        out[n] = t.to(dev).contiguous()
+    return out
+
+
+# ------------------------------------------------------------------------------------------------
+# CPU baseline / reference arm
+
+
+def cpu_reference_sample(shape, seconds: float, max_reps: int | None = None):
+    """Time the reference algorithm (CPU restatement of zenith/mamba3.py:30-56, fp32, autograd)
+    on a one-sequence slice of the workload; returns (tokens/s, cores, reps, sample string)."""
+    from oracle.ssd_oracle import ssd_forward
+    from zenith_b200.synthetic import SsdShape, make_inputs
+
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    sl = SsdShape(1, shape.T, shape.H, shape.P, shape.N, shape.G, shape.chunk)
+    inp = make_inputs(sl, seed=0)
+    leaves = [(inp[n].to(torch.bfloat16).float() if n in VEC else inp[n]).requires_grad_() for n in NAMES]
+    dy = inp["dy"].to(torch.bfloat16).float()
+
+    def once():
+        y, _, _ = ssd_forward(*leaves, sl.chunk, dtype=torch.float32)
+        y.backward(dy)
+        for t in leaves:
+            t.grad = None
+
+    once()  # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        once()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or (max_reps is not None and reps >= max_reps):
+            break
+    tok_s = reps * sl.B * sl.T / el
+    sample = (f"reference algorithm fp32 + autograd on host CPU, 1 sequence (T{sl.T} H{sl.H} P{sl.P} N{sl.N} "
+              f"chunk {sl.chunk}) of the B{shape.B} workload, {reps} reps in {el:.1f} s, {cores} threads")
+    return tok_s, cores, reps, sample
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from zenith_b200.synthetic import SHAPES
+
+    shape = SHAPES[args.workload]
+    seconds = max(3.0, min(120.0, 2.0 * (args.steps + args.warmup)))
+    tok_s, cores, reps, sample = cpu_reference_sample(shape, seconds)
+    ms = shape.B * shape.T / tok_s * 1e3
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tok_s, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": shape.name, "B": shape.B, "T": shape.T, "H": shape.H, "P": shape.P, "N": shape.N,
+                   "chunk": shape.chunk, "device": "host cpu"},
+        "cpu_baseline": {"value": tok_s, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": tok_s, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------------------------
+# our arm
+
+
+def run_ours(args):
+    import torch.distributed as dist
+
+    import zenith_b200
+    from zenith_b200 import _lib
+    from zenith_b200.ssd import ssd_bwd_op, ssd_fwd_op
+    from zenith_b200.synthetic import SHAPES
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    shape = SHAPES[args.workload]
+    inp = make_device_inputs(shape, rank, dev)
+    a = [inp[n] for n in NAMES]
+    dy = inp["dy"]
+    chunk = shape.chunk
+    fwd_b, bwd_b = algorithmic_bytes(shape)
+    th = shape.B * shape.T * shape.H
+
+    def step(ev=None):
+        if ev is not None:
+            ev[0].record()
+        y, fin, states = ssd_fwd_op(*a, chunk, None, True, False)
+        if ev is not None:
+            ev[1].record()
+        g = ssd_bwd_op(dy, *a, states, chunk, None, None, False)
+        if ev is not None:
+            ev[2].record()
+        return y, g
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    zenith_b200.check_status(dev)
+
+    # per-kernel durations (events around each op on the launching stream)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    launches0 = _lib.launch_count()
+    start.record()
+    for i in range(args.steps):
+        step(evs[i])
+    end.record()
+    torch.cuda.synchronize()
+    launches = _lib.launch_count() - launches0
+    barrier()
+    clocks = sampler.stop()
+    zenith_b200.check_status(dev)
+    elapsed_ms = start.elapsed_time(end)
+    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    t = torch.tensor([elapsed_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(t.item())
+    ms_per_step = elapsed_ms / args.steps
+    tokens_per_step = shape.B * shape.T * world
+    value = tokens_per_step / (ms_per_step / 1e3)
+
+    # end-to-end through the public API with host buffers (pinned), copies inside the timed region
+    host = {n: inp[n].cpu().pin_memory() for n in NAMES + ("dy",)}
+    outs = {n: torch.empty(host[n].shape, dtype=host[n].dtype).pin_memory() for n in ("x",) + NAMES}
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = sum(v.numel() * v.element_size() for v in outs.values())
+
+    def e2e_step():
+        leaves = [host[n].to(dev, non_blocking=True).requires_grad_() for n in NAMES]
+        d = host["dy"].to(dev, non_blocking=True)
+        y = zenith_b200.ssd(*leaves, chunk)
+        y.backward(d)
+        outs["x"].copy_(y.detach(), non_blocking=True)  # y shares x's shape/dtype
+        for n, lf in zip(NAMES, leaves):
+            outs[n].copy_(lf.grad, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 10))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2.record()
+    torch.cuda.synchronize()
+    zenith_b200.check_status(dev)
+    t2 = torch.tensor([s2.elapsed_time(e2)], device=dev)
+    if world > 1:
+        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+    e2e_value = tokens_per_step / (float(t2.item()) / e2e_steps / 1e3)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tok_s, cores, reps, sample = cpu_reference_sample(shape, args.cpu_seconds)
+        cpu = {"value": tok_s, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    peak, peak_kind = peaks()
+    kern = {"fwd": (fwd_ms, fwd_b * th, "ssd_fwd"), "bwd": (bwd_ms, bwd_b * th, "ssd_bwd")}
+    dom = max(kern, key=lambda k: kern[k][0])
+    dms, dbytes, dname = kern[dom]
+    achieved = dbytes / (dms / 1e3) / 1e9
+    step_gbs = (fwd_b + bwd_b) * th / (ms_per_step / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": shape.name, "B_per_gpu": shape.B, "T": shape.T, "H": shape.H, "P": shape.P,
+                   "N": shape.N, "chunk": shape.chunk, "vector_dtype": "bf16", "scalar_dtype": "fp32",
+                   "parallelism": f"batch-sharded x{world}", "l2": "inputs larger than L2 (1.3 GB/step)"},
+        "roofline": {"bound": "hbm", "kernel": dname, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic_from_profile(dname),
+                     "algorithmic_bytes_per_launch": dbytes, "launch_ms": dms},
+        "step_roofline": {"achieved_gbs": step_gbs, "frac": step_gbs / peak,
+                          "algorithmic_bytes_per_token_head": fwd_b + bwd_b, "fwd_ms": fwd_ms, "bwd_ms": bwd_ms},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

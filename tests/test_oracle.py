@@ -1,0 +1,70 @@
+"""The CPU oracle against the reference's golden vectors and the reference tests' properties."""
+import pytest
+import torch
+
+from oracle.ssd_oracle import max_rel_err, naive_recurrence, ssd_backward, ssd_forward
+from tests.golden_io import CASES, NAMES, load
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_oracle_forward_matches_reference_golden(case):
+    inp, out, L = load(case)
+    y, final, _ = ssd_forward(*(inp[n] for n in NAMES), L)
+    tol = 1e-12 if out["y"].dtype == torch.float64 else 1e-6
+    assert max_rel_err(y, out["y"]) < tol
+    assert max_rel_err(final, out["final_state"]) < tol
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_oracle_backward_matches_reference_autograd(case):
+    inp, out, L = load(case)
+    g = ssd_backward(inp["dy"], *(inp[n] for n in NAMES), L)
+    tol = 1e-11 if out["y"].dtype == torch.float64 else 1e-6
+    for n in NAMES:
+        assert max_rel_err(g["d" + n], out["d" + n]) < tol, n
+
+
+@pytest.mark.parametrize("chunk", [1, 4, 16, 64])
+def test_oracle_is_independent_of_chunk_size(chunk):
+    # property of the reference (tests/test_mamba3.py:46-54), extended to the backward
+    g = torch.Generator().manual_seed(1)
+    B, T, H, P, N = 1, 64, 2, 3, 5
+    x, xp = torch.randn(2, B, T, H, P, generator=g, dtype=torch.float64)
+    q, k, kp = torch.randn(3, B, T, H, N, generator=g, dtype=torch.float64)
+    adt = -torch.rand(B, T, H, generator=g, dtype=torch.float64)
+    ga, be = torch.rand(2, B, T, H, generator=g, dtype=torch.float64)
+    dy = torch.randn(B, T, H, P, generator=g, dtype=torch.float64)
+    args = (x, q, k, kp, xp, adt, ga, be)
+    y, fin, _ = ssd_forward(*args, chunk)
+    yn, hn = naive_recurrence(*args)
+    assert max_rel_err(y, yn) < 1e-12 and max_rel_err(fin, hn) < 1e-12
+    g1 = ssd_backward(dy, *args, chunk)
+    g64 = ssd_backward(dy, *args, 64)
+    for n in NAMES:
+        assert max_rel_err(g1["d" + n], g64["d" + n]) < 1e-11
+
+
+def test_oracle_initial_state_and_final_state_gradients_match_autograd():
+    g = torch.Generator().manual_seed(7)
+    B, T, H, P, N, L = 2, 32, 2, 4, 6, 8
+    ts = [torch.randn(B, T, H, P, generator=g, dtype=torch.float64) for _ in range(2)]
+    qs = [torch.randn(B, T, H, N, generator=g, dtype=torch.float64) for _ in range(3)]
+    adt = -torch.rand(B, T, H, generator=g, dtype=torch.float64)
+    ga, be = torch.rand(2, B, T, H, generator=g, dtype=torch.float64)
+    s0 = torch.randn(B, H, P, N, generator=g, dtype=torch.float64)
+    dy = torch.randn(B, T, H, P, generator=g, dtype=torch.float64)
+    dfin = torch.randn(B, H, P, N, generator=g, dtype=torch.float64)
+    leaves = [t.clone().requires_grad_() for t in (ts[0], qs[0], qs[1], qs[2], ts[1], adt, ga, be, s0)]
+    y, fin = naive_recurrence(*leaves[:8], initial_state=leaves[8])
+    (y * dy).sum().add_((fin * dfin).sum()).backward()
+    got = ssd_backward(dy, *[t.detach() for t in leaves[:8]], L, initial_state=s0, dfinal=dfin)
+    for n, leaf in zip(NAMES + ("initial_state",), leaves):
+        assert max_rel_err(got["d" + n], leaf.grad) < 1e-11, n
+
+
+def test_oracle_rejects_length_not_multiple_of_chunk():
+    t = torch.zeros(1, 10, 1, 2, dtype=torch.float64)
+    n = torch.zeros(1, 10, 1, 3, dtype=torch.float64)
+    a = torch.zeros(1, 10, 1, dtype=torch.float64)
+    with pytest.raises(AssertionError, match="multiple of chunk_size"):
+        ssd_forward(t, n, n, n, t, a, a, a, 4)

@@ -1,0 +1,8 @@
+"""zenith_b200: B200-native (sm_100a) SSD chunked scan for Mamba-3, a drop-in for the
+reference's ``zenith.mamba3.ssd`` behind ``Mamba3.scan``."""
+
+from ._lib import SsdError, check_status
+from .ssd import prepare_inputs, ssd, ssd_dinitial_state, ssd_final_state, use_b200_scan
+
+__all__ = ["ssd", "ssd_final_state", "ssd_dinitial_state", "use_b200_scan", "prepare_inputs", "check_status", "SsdError"]
+__version__ = "0.1.0"

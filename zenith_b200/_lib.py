@@ -1,0 +1,149 @@
+"""ctypes binding of libzenith_ssd.so (the C ABI declared in include/zb_ssd.h).
+
+The shared library is built in-tree by ``zenith_b200.build`` (nvcc, sm_100a).  There is no
+fallback: if the library is missing or fails to load, every op raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import pathlib
+import threading
+
+import torch
+
+LIB_PATH = pathlib.Path(__file__).resolve().parent / "libzenith_ssd.so"
+
+ZB_F32, ZB_BF16, ZB_F16, ZB_F64 = 0, 1, 2, 3
+ZB_FLAG_STATE_ONLY = 1
+ZB_ERR_SHAPE, ZB_ERR_TIMEOUT = 1, 5
+
+DTYPE_CODE = {torch.float32: ZB_F32, torch.bfloat16: ZB_BF16, torch.float16: ZB_F16, torch.float64: ZB_F64}
+
+
+class View(ctypes.Structure):
+    _fields_ = [("ptr", ctypes.c_void_p), ("sb", ctypes.c_int64), ("st", ctypes.c_int64), ("sh", ctypes.c_int64)]
+
+
+_VIEWS_FWD = ("x", "q", "k", "kp", "xp", "adt", "gamma", "beta")
+_VIEWS_BWD = ("dx", "dq", "dk", "dkp", "dxp", "dadt", "dgamma", "dbeta")
+
+
+class Args(ctypes.Structure):
+    _fields_ = (
+        [(n, ctypes.c_int64) for n in ("B", "T", "H", "G", "P", "N", "chunk_size")]
+        + [(n, ctypes.c_int32) for n in ("dtype", "scalar_dtype", "flags", "reserved")]
+        + [(n, View) for n in _VIEWS_FWD]
+        + [("y", View), ("initial_state", ctypes.c_void_p), ("final_state", ctypes.c_void_p), ("states", ctypes.c_void_p)]
+        + [("dy", View), ("dfinal_state", ctypes.c_void_p)]
+        + [(n, View) for n in _VIEWS_BWD]
+        + [("dinitial_state", ctypes.c_void_p), ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+           ("status", ctypes.c_void_p)]
+    )
+
+
+EXPORTS = (
+    "zb_version", "zb_strerror", "zb_last_cuda_error", "zb_ssd_states_bytes", "zb_ssd_workspace_bytes",
+    "zb_ssd_fwd", "zb_ssd_bwd", "zb_ssd_state_combine", "zb_ssd_total_decay", "zb_ssd_check_status",
+    "zb_launch_count",
+)
+
+_lib = None
+_lock = threading.Lock()
+
+
+class SsdError(RuntimeError):
+    def __init__(self, code: int, what: str):
+        self.code = code
+        super().__init__(f"{what}: zenith_b200 status {code} ({strerror(code)})")
+
+
+def lib() -> ctypes.CDLL:
+    """Load the library once; raise if it is missing (no CPU fallback exists)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m zenith_b200.build`")
+        L = ctypes.CDLL(str(LIB_PATH))
+        L.zb_version.restype = ctypes.c_int
+        L.zb_strerror.restype = ctypes.c_char_p
+        L.zb_strerror.argtypes = [ctypes.c_int]
+        L.zb_last_cuda_error.restype = ctypes.c_char_p
+        for fn in ("zb_ssd_states_bytes", "zb_ssd_workspace_bytes"):
+            getattr(L, fn).restype = ctypes.c_size_t
+        L.zb_ssd_states_bytes.argtypes = [ctypes.POINTER(Args)]
+        L.zb_ssd_workspace_bytes.argtypes = [ctypes.POINTER(Args), ctypes.c_int]
+        for fn in ("zb_ssd_fwd", "zb_ssd_bwd"):
+            getattr(L, fn).restype = ctypes.c_int
+            getattr(L, fn).argtypes = [ctypes.POINTER(Args), ctypes.c_void_p]
+        L.zb_ssd_state_combine.restype = ctypes.c_int
+        L.zb_ssd_state_combine.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p]
+        L.zb_ssd_total_decay.restype = ctypes.c_int
+        L.zb_ssd_total_decay.argtypes = [ctypes.POINTER(Args), ctypes.c_void_p, ctypes.c_void_p]
+        L.zb_ssd_check_status.restype = ctypes.c_int
+        L.zb_ssd_check_status.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        L.zb_launch_count.restype = ctypes.c_uint64
+        _lib = L
+    return _lib
+
+
+def launch_count() -> int:
+    """Kernels launched by the library so far in this process."""
+    return int(lib().zb_launch_count())
+
+
+def strerror(code: int) -> str:
+    try:
+        return lib().zb_strerror(code).decode()
+    except Exception:  # pragma: no cover - only when the library itself is broken
+        return "?"
+
+
+def check(code: int, what: str) -> None:
+    if code != 0:
+        extra = lib().zb_last_cuda_error().decode()
+        err = SsdError(code, what)
+        if extra:
+            err.args = (err.args[0] + f" [{extra}]",)
+        raise err
+
+
+def view(t: torch.Tensor | None) -> View:
+    """[B, T, H, D] (or [B, T, H]) tensor -> View; the innermost dimension must be contiguous."""
+    if t is None:
+        return View(None, 0, 0, 0)
+    if t.dim() == 4:
+        assert t.stride(-1) == 1 or t.shape[-1] == 1, "innermost dimension must be contiguous"
+    return View(t.data_ptr(), t.stride(0), t.stride(1), t.stride(2))
+
+
+def ptr(t: torch.Tensor | None):
+    return None if t is None or t.numel() == 0 else t.data_ptr()
+
+
+_status: dict[int, torch.Tensor] = {}
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """One int32 status word per device (0 = fine), shared by all calls."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _status.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status[idx] = t
+    return t
+
+
+def check_status(device: torch.device | None = None, reset: bool = True) -> None:
+    """Synchronise and raise if a kernel on ``device`` recorded an error (e.g. a timed-out wait)."""
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    st = status_word(dev)
+    code = lib().zb_ssd_check_status(st.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
+    if code != 0:
+        if reset:
+            st.zero_()
+        check(code, "kernel status")

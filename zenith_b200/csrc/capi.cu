@@ -1,0 +1,299 @@
+// extern "C" entry points of libzenith_ssd.so (declared in include/zb_ssd.h): argument
+// validation, workspace planning and dispatch to the kernel families.
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+
+#include "ssd_kernels.h"
+#include "ssd_tc.h"
+
+using namespace zb;
+
+namespace zb {
+static std::atomic<uint64_t> g_launches{0};
+void note_launches(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+}  // namespace zb
+
+namespace {
+
+thread_local char g_cuda_err[256] = "";
+
+int cuda_fail(cudaError_t e) {
+  snprintf(g_cuda_err, sizeof(g_cuda_err), "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
+  return ZB_ERR_CUDA;
+}
+
+size_t dtype_size(int dt) {
+  switch (dt) {
+    case ZB_F32: return 4;
+    case ZB_BF16: return 2;
+    case ZB_F16: return 2;
+    case ZB_F64: return 8;
+    default: return 0;
+  }
+}
+
+enum Kind { kSimt = 0, kTc = 1 };
+
+struct Plan {
+  Kind kind;
+  int L, nc;
+  size_t acc;           // bytes of one state element
+  size_t states_bytes;  // saved chunk states
+  size_t sync_bytes;    // ticket + flags
+  size_t gchain_bytes;  // backward gradient chain
+  size_t grp_bytes;     // per-head q/k/kp gradients when G < H
+  size_t tc_fwd_ws, tc_bwd_ws;
+};
+
+bool view_ok(const zb_view& v, size_t esz) {
+  return v.ptr != nullptr && (reinterpret_cast<uintptr_t>(v.ptr) % esz) == 0;
+}
+
+int validate(const zb_ssd_args* a, bool backward) {
+  if (!a) return ZB_ERR_LAYOUT;
+  if (a->B <= 0 || a->T <= 0 || a->H <= 0 || a->G <= 0 || a->P <= 0 || a->N <= 0 || a->chunk_size <= 0)
+    return ZB_ERR_SHAPE;
+  if (a->T % a->chunk_size != 0) return ZB_ERR_SHAPE;  // mamba3.py:33
+  if (a->H % a->G != 0) return ZB_ERR_SHAPE;
+  const size_t e = dtype_size(a->dtype), es = dtype_size(a->scalar_dtype);
+  if (!e || !es) return ZB_ERR_DTYPE;
+  if ((a->dtype == ZB_F64) != (a->scalar_dtype == ZB_F64)) return ZB_ERR_DTYPE;
+  const zb_view* vec[] = {&a->x, &a->q, &a->k, &a->kp, &a->xp};
+  for (auto v : vec)
+    if (!view_ok(*v, e)) return ZB_ERR_LAYOUT;
+  const zb_view* sc[] = {&a->adt, &a->gamma, &a->beta};
+  for (auto v : sc)
+    if (!view_ok(*v, es)) return ZB_ERR_LAYOUT;
+  if (!a->status) return ZB_ERR_LAYOUT;
+  const bool state_only = (a->flags & ZB_FLAG_STATE_ONLY) != 0;
+  if (!backward) {
+    if (!state_only && !view_ok(a->y, e)) return ZB_ERR_LAYOUT;
+  } else {
+    if (!a->states && !state_only) return ZB_ERR_WORKSPACE;
+    if (!view_ok(a->dy, e)) return ZB_ERR_LAYOUT;
+    if (!state_only) {
+      const zb_view* gv[] = {&a->dx, &a->dq, &a->dk, &a->dkp, &a->dxp};
+      for (auto v : gv)
+        if (!view_ok(*v, e)) return ZB_ERR_LAYOUT;
+      const zb_view* gs[] = {&a->dadt, &a->dgamma, &a->dbeta};
+      for (auto v : gs)
+        if (!view_ok(*v, es)) return ZB_ERR_LAYOUT;
+    }
+  }
+  return ZB_OK;
+}
+
+int make_plan(const zb_ssd_args* a, Plan* pl) {
+  const int64_t BH = a->B * a->H;
+  if (tc_supported(a)) {
+    pl->kind = kTc;
+    pl->L = tc_chunk();
+    pl->nc = (int)((a->T + pl->L - 1) / pl->L);
+    pl->acc = 4;
+    pl->states_bytes = tc_states_bytes(a);
+    pl->sync_bytes = chain_sync_bytes(BH * (pl->nc + 1));
+    pl->gchain_bytes = 0;
+    pl->grp_bytes = 0;
+    pl->tc_fwd_ws = tc_workspace_bytes(a, false);
+    pl->tc_bwd_ws = tc_workspace_bytes(a, true);
+    return ZB_OK;
+  }
+  const bool f64 = a->dtype == ZB_F64;
+  const int L = simt_pick_chunk((int)a->P, (int)a->N, f64);
+  if (L == 0) return ZB_ERR_UNSUPPORTED;
+  pl->kind = kSimt;
+  pl->L = L;
+  pl->nc = (int)((a->T + L - 1) / L);
+  pl->acc = f64 ? 8 : 4;
+  const size_t slots = (size_t)BH * (pl->nc + 1) * (size_t)a->P * (size_t)a->N;
+  pl->states_bytes = align_up(slots * pl->acc, 256);
+  pl->sync_bytes = chain_sync_bytes(BH * (pl->nc + 1));
+  pl->gchain_bytes = pl->states_bytes;
+  pl->grp_bytes = (a->G != a->H) ? align_up((size_t)a->B * a->T * a->H * 3 * a->N * sizeof(float), 256) : 0;
+  pl->tc_fwd_ws = pl->tc_bwd_ws = 0;
+  return ZB_OK;
+}
+
+View to_view(const zb_view& v) { return View{v.ptr, v.sb, v.st, v.sh}; }
+
+SimtParams simt_params(const zb_ssd_args* a, const Plan& pl) {
+  SimtParams p;
+  memset(&p, 0, sizeof(p));
+  p.B = a->B; p.T = a->T; p.H = a->H; p.G = a->G; p.P = a->P; p.N = a->N;
+  p.L = pl.L; p.nc = pl.nc; p.flags = a->flags;
+  p.x = to_view(a->x); p.q = to_view(a->q); p.k = to_view(a->k); p.kp = to_view(a->kp); p.xp = to_view(a->xp);
+  p.adt = to_view(a->adt); p.gamma = to_view(a->gamma); p.beta = to_view(a->beta);
+  p.y = to_view(a->y);
+  p.init = a->initial_state; p.fin = a->final_state;
+  p.status = a->status;
+  p.dy = to_view(a->dy); p.dfin = a->dfinal_state;
+  p.dx = to_view(a->dx); p.dq = to_view(a->dq); p.dk = to_view(a->dk); p.dkp = to_view(a->dkp); p.dxp = to_view(a->dxp);
+  p.dadt = to_view(a->dadt); p.dgamma = to_view(a->dgamma); p.dbeta = to_view(a->dbeta);
+  p.dinit = a->dinitial_state;
+  return p;
+}
+
+__global__ void state_combine_kernel(const float* s_prev, const float* decay, const float* f_prev, float* s_next,
+                                     int64_t BH, int64_t PN) {
+  const int64_t total = BH * PN;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
+    s_next[i] = decay[i / PN] * s_prev[i] + f_prev[i];
+}
+
+template <typename TS>
+__global__ void total_decay_kernel(View adt, int64_t T, int64_t H, float* out) {
+  const int64_t bh = blockIdx.x, b = bh / H, h = bh % H;
+  double acc = 0.0;
+  for (int64_t t = threadIdx.x; t < T; t += blockDim.x) acc += (double)ldv<float>(adt.row<TS>(b, t, h));
+  __shared__ double red[32];
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double s = 0.0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) s += red[i];
+    out[bh] = (float)exp(s);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int zb_version(void) { return 100; }
+
+const char* zb_strerror(int s) {
+  switch (s) {
+    case ZB_OK: return "ok";
+    case ZB_ERR_SHAPE: return "bad shape (sequence length must be a multiple of chunk_size; H % G == 0; sizes > 0)";
+    case ZB_ERR_DTYPE: return "unsupported dtype combination";
+    case ZB_ERR_LAYOUT: return "bad layout (NULL or misaligned pointer)";
+    case ZB_ERR_CUDA: return "CUDA error";
+    case ZB_ERR_TIMEOUT: return "timed out waiting for the preceding chunk's state";
+    case ZB_ERR_WORKSPACE: return "workspace or saved-states buffer missing, too small or misaligned";
+    case ZB_ERR_UNSUPPORTED: return "sizes not supported by the kernels";
+    default: return "unknown status";
+  }
+}
+
+const char* zb_last_cuda_error(void) { return g_cuda_err; }
+
+size_t zb_ssd_states_bytes(const zb_ssd_args* a) {
+  if (validate(a, false) != ZB_OK && validate(a, true) != ZB_OK) {
+    // shape/dtype check only: pointers may be unset when sizing
+    if (!a || a->B <= 0 || a->T <= 0 || a->H <= 0 || a->G <= 0 || a->P <= 0 || a->N <= 0) return 0;
+    if (a->chunk_size <= 0 || a->T % a->chunk_size || a->H % a->G) return 0;
+    if (!dtype_size(a->dtype) || !dtype_size(a->scalar_dtype)) return 0;
+  }
+  Plan pl;
+  if (make_plan(a, &pl) != ZB_OK) return 0;
+  return pl.states_bytes;
+}
+
+size_t zb_ssd_workspace_bytes(const zb_ssd_args* a, int backward) {
+  if (!a || a->B <= 0 || a->T <= 0 || a->H <= 0 || a->G <= 0 || a->P <= 0 || a->N <= 0) return 0;
+  if (a->chunk_size <= 0 || a->T % a->chunk_size || a->H % a->G) return 0;
+  if (!dtype_size(a->dtype) || !dtype_size(a->scalar_dtype)) return 0;
+  Plan pl;
+  if (make_plan(a, &pl) != ZB_OK) return 0;
+  if (pl.kind == kTc) return pl.sync_bytes + (backward ? pl.tc_bwd_ws : pl.tc_fwd_ws) + (backward ? 0 : pl.states_bytes);
+  if (!backward) return pl.sync_bytes + pl.states_bytes;  // chain lives here when no states buffer is given
+  return pl.sync_bytes + pl.gchain_bytes + pl.grp_bytes;
+}
+
+int zb_ssd_fwd(const zb_ssd_args* a, void* stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  int rc = validate(a, false);
+  if (rc) return rc;
+  Plan pl;
+  if ((rc = make_plan(a, &pl))) return rc;
+  const size_t need = zb_ssd_workspace_bytes(a, 0);
+  if (!a->workspace || a->workspace_bytes < need || reinterpret_cast<uintptr_t>(a->workspace) % 256) return ZB_ERR_WORKSPACE;
+  if (a->states && reinterpret_cast<uintptr_t>(a->states) % 256) return ZB_ERR_WORKSPACE;
+  char* ws = static_cast<char*>(a->workspace);
+  cudaError_t e = cudaMemsetAsync(ws, 0, pl.sync_bytes, stream);
+  if (e != cudaSuccess) return cuda_fail(e);
+  ChainSync sync{reinterpret_cast<unsigned int*>(ws), reinterpret_cast<int*>(ws + 256)};
+  void* chain = a->states ? a->states : static_cast<void*>(ws + pl.sync_bytes);
+  if (pl.kind == kTc) {
+    rc = tc_fwd(a, sync, chain, ws + pl.sync_bytes + (a->states ? 0 : pl.states_bytes), stream);
+  } else {
+    SimtParams p = simt_params(a, pl);
+    p.sync = sync;
+    p.chain = chain;
+    rc = simt_launch(p, a->dtype, a->scalar_dtype, false, stream);
+  }
+  if (rc == ZB_ERR_CUDA) return cuda_fail(cudaGetLastError());
+  return rc;
+}
+
+int zb_ssd_bwd(const zb_ssd_args* a, void* stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  int rc = validate(a, true);
+  if (rc) return rc;
+  Plan pl;
+  if ((rc = make_plan(a, &pl))) return rc;
+  const size_t need = zb_ssd_workspace_bytes(a, 1);
+  if (!a->workspace || a->workspace_bytes < need || reinterpret_cast<uintptr_t>(a->workspace) % 256) return ZB_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(a->states) % 256) return ZB_ERR_WORKSPACE;
+  char* ws = static_cast<char*>(a->workspace);
+  cudaError_t e = cudaMemsetAsync(ws, 0, pl.sync_bytes, stream);
+  if (e != cudaSuccess) return cuda_fail(e);
+  ChainSync sync{reinterpret_cast<unsigned int*>(ws), reinterpret_cast<int*>(ws + 256)};
+  if (pl.kind == kTc) {
+    rc = tc_bwd(a, sync, ws + pl.sync_bytes, stream);
+  } else {
+    SimtParams p = simt_params(a, pl);
+    p.sync = sync;
+    p.chain = a->states;
+    p.gchain = ws + pl.sync_bytes;
+    p.grp = pl.grp_bytes ? reinterpret_cast<float*>(ws + pl.sync_bytes + pl.gchain_bytes) : nullptr;
+    rc = simt_launch(p, a->dtype, a->scalar_dtype, true, stream);
+  }
+  if (rc == ZB_ERR_CUDA) return cuda_fail(cudaGetLastError());
+  return rc;
+}
+
+int zb_ssd_state_combine(const float* s_prev, const float* decay_prev, const float* f_prev, float* s_next, int64_t BH,
+                         int64_t PN, void* stream) {
+  if (!s_prev || !decay_prev || !f_prev || !s_next || BH <= 0 || PN <= 0) return ZB_ERR_LAYOUT;
+  const int64_t total = BH * PN;
+  const unsigned nb = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 8);
+  state_combine_kernel<<<nb, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(s_prev, decay_prev, f_prev, s_next, BH, PN);
+  note_launches(1);
+  cudaError_t e = cudaPeekAtLastError();
+  return e == cudaSuccess ? ZB_OK : cuda_fail(e);
+}
+
+int zb_ssd_total_decay(const zb_ssd_args* a, float* out, void* stream) {
+  if (!a || !out || !a->adt.ptr || a->B <= 0 || a->T <= 0 || a->H <= 0) return ZB_ERR_LAYOUT;
+  const unsigned nb = (unsigned)(a->B * a->H);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const View v = to_view(a->adt);
+  switch (a->scalar_dtype) {
+    case ZB_F32: total_decay_kernel<float><<<nb, 256, 0, s>>>(v, a->T, a->H, out); break;
+    case ZB_BF16: total_decay_kernel<__nv_bfloat16><<<nb, 256, 0, s>>>(v, a->T, a->H, out); break;
+    case ZB_F16: total_decay_kernel<__half><<<nb, 256, 0, s>>>(v, a->T, a->H, out); break;
+    case ZB_F64: total_decay_kernel<double><<<nb, 256, 0, s>>>(v, a->T, a->H, out); break;
+    default: return ZB_ERR_DTYPE;
+  }
+  note_launches(1);
+  cudaError_t e = cudaPeekAtLastError();
+  return e == cudaSuccess ? ZB_OK : cuda_fail(e);
+}
+
+int zb_ssd_check_status(const int32_t* status, void* stream) {
+  if (!status) return ZB_ERR_LAYOUT;
+  int32_t h = 0;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(&h, status, sizeof(h), cudaMemcpyDeviceToHost, s);
+  if (e != cudaSuccess) return cuda_fail(e);
+  e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e);
+  return h;
+}
+
+uint64_t zb_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+}  // extern "C"

@@ -1,0 +1,140 @@
+// Shared device helpers for the SSD kernels: dtype I/O, strided views and the chained
+// (ticket-ordered) state hand-off between the CTAs that own consecutive chunks.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "zb_ssd.h"
+
+namespace zb {
+
+// ---------------------------------------------------------------------------------------------
+// element conversion
+template <typename T> struct Conv;
+template <> struct Conv<float> {
+  static __device__ __forceinline__ float to_f(float v) { return v; }
+  static __device__ __forceinline__ float from_f(float v) { return v; }
+  static __device__ __forceinline__ double to_d(float v) { return v; }
+  static __device__ __forceinline__ float from_d(double v) { return (float)v; }
+};
+template <> struct Conv<double> {
+  static __device__ __forceinline__ float to_f(double v) { return (float)v; }
+  static __device__ __forceinline__ double from_f(float v) { return v; }
+  static __device__ __forceinline__ double to_d(double v) { return v; }
+  static __device__ __forceinline__ double from_d(double v) { return v; }
+};
+template <> struct Conv<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+  static __device__ __forceinline__ double to_d(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_d(double v) { return __float2bfloat16_rn((float)v); }
+};
+template <> struct Conv<__half> {
+  static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+  static __device__ __forceinline__ double to_d(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half from_d(double v) { return __float2half_rn((float)v); }
+};
+
+// load an element of type T as accumulator type TA / store TA as T
+template <typename TA, typename T> __device__ __forceinline__ TA ldv(const T* p) {
+  if constexpr (sizeof(TA) == 8) return Conv<T>::to_d(*p); else return Conv<T>::to_f(*p);
+}
+template <typename TA, typename T> __device__ __forceinline__ void stv(T* p, TA v) {
+  if constexpr (sizeof(TA) == 8) *p = Conv<T>::from_d(v); else *p = Conv<T>::from_f(v);
+}
+
+template <typename TA> __device__ __forceinline__ TA xexp(TA v);
+template <> __device__ __forceinline__ float xexp<float>(float v) { return expf(v); }
+template <> __device__ __forceinline__ double xexp<double>(double v) { return exp(v); }
+
+// A [B, T, H, D] view with element strides; the innermost dimension is contiguous.
+struct View {
+  const void* ptr;
+  int64_t sb, st, sh;
+  template <typename T> __device__ __forceinline__ const T* row(int64_t b, int64_t t, int64_t h) const {
+    return reinterpret_cast<const T*>(ptr) + b * sb + t * st + h * sh;
+  }
+  template <typename T> __device__ __forceinline__ T* wrow(int64_t b, int64_t t, int64_t h) const {
+    return const_cast<T*>(reinterpret_cast<const T*>(ptr)) + b * sb + t * st + h * sh;
+  }
+};
+
+// ---------------------------------------------------------------------------------------------
+// chained hand-off
+//
+// CTAs take a ticket from a global counter when they start, and the ticket (not blockIdx)
+// decides which chunk they own.  Tickets are handed out in chunk order, so the owner of the
+// chunk a CTA waits for started earlier and is resident: every wait ends.  Waits are still
+// bounded (about one second): on expiry the CTA records ZB_ERR_TIMEOUT in the status word,
+// marks its own hand-off as aborted (flag value 2) so that its successors stop at once, and
+// returns.
+
+constexpr int kFlagReady = 1;
+constexpr int kFlagAbort = 2;
+constexpr uint64_t kWaitTimeoutNs = 1000000000ull;  // 1 s
+constexpr uint32_t kWaitMaxIters = 1u << 22;         // independent cap, ~4 s with 1 us sleeps
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_volatile(const int32_t* p) { return *(volatile const int32_t*)p; }
+
+// Called by one thread. Returns kFlagReady, or kFlagAbort on an aborted predecessor / timeout.
+static __device__ __noinline__ int wait_flag(const int* flag, int32_t* status) {
+  const uint64_t t0 = globaltimer();
+  uint32_t sleep_ns = 32;
+  for (uint32_t it = 0; it < kWaitMaxIters; ++it) {
+    const int v = ld_acquire(flag);
+    if (v == kFlagReady) return kFlagReady;
+    if (v != 0) return kFlagAbort;
+    if ((it & 15) == 15) {
+      if (ld_volatile(status) != 0) return kFlagAbort;
+      if (globaltimer() - t0 > kWaitTimeoutNs) break;
+    }
+    __nanosleep(sleep_ns);
+    if (sleep_ns < 1024) sleep_ns <<= 1;
+  }
+  atomicCAS(status, 0, (int32_t)ZB_ERR_TIMEOUT);
+  return kFlagAbort;
+}
+
+// Scratch layout shared by all chained kernels: [ticket counter | pad to 256 | flags[n_flags]].
+struct ChainSync {
+  unsigned int* ticket;
+  int* flags;
+};
+
+__host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+inline size_t chain_sync_bytes(int64_t n_flags) { return align_up(256 + (size_t)n_flags * sizeof(int), 256); }
+
+// ---------------------------------------------------------------------------------------------
+// warp helpers
+template <typename TA> __device__ __forceinline__ TA warp_sum(TA v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+template <typename TA> __device__ __forceinline__ TA warp_incl_scan(TA v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    TA u = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += u;
+  }
+  return v;
+}
+
+}  // namespace zb

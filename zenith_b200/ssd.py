@@ -1,0 +1,265 @@
+"""Drop-in SSD chunked scan: ``ssd(x, q, k, kp, xp, adt, gamma, beta, chunk_size)``.
+
+Same signature, layouts, return value and error behaviour as the reference's
+``zenith.mamba3.ssd`` (zenith/mamba3.py:30-56), which ``Mamba3.forward`` calls through its
+``scan`` attribute as ``self.scan(x, q, k, kp, xp, ADT, gamma, beta, self.chunk_size)``
+(zenith/mamba3.py:77,118).  Forward and backward run in libzenith_ssd.so (sm_100a CUDA
+kernels) behind two ``torch.library`` custom ops with a registered autograd formula and fake
+(meta) implementations, so the op also works under ``torch.compile`` (the reference's
+``--compile_scan``, zenith/train.py:75-79).
+
+Extensions with no reference counterpart (the reference always starts from a zero state and
+drops the final state, zenith/mamba3.py:50-54):
+``initial_state=[B,H,P,N]`` and ``return_final_state=True`` (both differentiable).
+
+Precision: fp32/fp64 inputs are computed in fp32/fp64.  bf16/fp16 inputs are read as stored,
+multiplied with fp32 accumulation; scans, decays and states stay fp32.  Under CUDA autocast
+with a 16-bit dtype, fp32 vector inputs are cast to that dtype first, as the reference's
+matmuls are under autocast; y is returned in the caller's dtype.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+from torch import Tensor
+
+from . import _lib as L
+
+_VEC = ("x", "q", "k", "kp", "xp")
+_SCA = ("adt", "gamma", "beta")
+
+
+def _acc_dtype(vdt: torch.dtype) -> torch.dtype:
+    return torch.float64 if vdt == torch.float64 else torch.float32
+
+
+def _build_args(x, q, k, kp, xp, adt, gamma, beta, chunk_size, flags=0) -> L.Args:
+    B, T, H, P = x.shape
+    G, N = q.shape[2], q.shape[3]
+    a = L.Args()
+    a.B, a.T, a.H, a.G, a.P, a.N, a.chunk_size = B, T, H, G, P, N, chunk_size
+    a.dtype = L.DTYPE_CODE[x.dtype]
+    a.scalar_dtype = L.DTYPE_CODE[adt.dtype]
+    a.flags = flags
+    for n, t in zip(_VEC + _SCA, (x, q, k, kp, xp, adt, gamma, beta)):
+        setattr(a, n, L.view(t))
+    return a
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def states_nbytes(x, q, k, kp, xp, adt, gamma, beta, chunk_size) -> int:
+    a = _build_args(x, q, k, kp, xp, adt, gamma, beta, chunk_size)
+    return int(L.lib().zb_ssd_states_bytes(ctypes.byref(a)))
+
+
+# ------------------------------------------------------------------------------------------------
+# custom ops
+
+
+@torch.library.custom_op("zenith_b200::ssd_fwd", mutates_args=(), device_types="cuda")
+def ssd_fwd_op(x: Tensor, q: Tensor, k: Tensor, kp: Tensor, xp: Tensor, adt: Tensor, gamma: Tensor, beta: Tensor,
+               chunk_size: int, initial_state: Optional[Tensor], save_states: bool,
+               state_only: bool) -> tuple[Tensor, Tensor, Tensor]:
+    B, T, H, P = x.shape
+    N = q.shape[3]
+    dev = x.device
+    a = _build_args(x, q, k, kp, xp, adt, gamma, beta, chunk_size, L.ZB_FLAG_STATE_ONLY if state_only else 0)
+    lib = L.lib()
+    y = torch.empty((0,) if state_only else (B, T, H, P), dtype=x.dtype, device=dev)
+    final = torch.empty((B, H, P, N), dtype=_acc_dtype(x.dtype), device=dev)
+    states = torch.empty(lib.zb_ssd_states_bytes(ctypes.byref(a)) if save_states else 0, dtype=torch.uint8, device=dev)
+    ws_bytes = lib.zb_ssd_workspace_bytes(ctypes.byref(a), 0)
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    if not state_only:
+        a.y = L.view(y)
+    a.initial_state = L.ptr(initial_state)
+    a.final_state = final.data_ptr()
+    a.states = L.ptr(states)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    a.status = L.status_word(dev).data_ptr()
+    L.check(lib.zb_ssd_fwd(ctypes.byref(a), _stream(dev)), "zb_ssd_fwd")
+    return y, final, states
+
+
+@ssd_fwd_op.register_fake
+def _(x, q, k, kp, xp, adt, gamma, beta, chunk_size, initial_state, save_states, state_only):
+    B, T, H, P = x.shape
+    N = q.shape[3]
+    nbytes = states_nbytes(x, q, k, kp, xp, adt, gamma, beta, chunk_size) if save_states else 0
+    y = x.new_empty((0,) if state_only else (B, T, H, P))
+    return y, x.new_empty((B, H, P, N), dtype=_acc_dtype(x.dtype)), x.new_empty((nbytes,), dtype=torch.uint8)
+
+
+@torch.library.custom_op("zenith_b200::ssd_bwd", mutates_args=(), device_types="cuda")
+def ssd_bwd_op(dy: Tensor, x: Tensor, q: Tensor, k: Tensor, kp: Tensor, xp: Tensor, adt: Tensor, gamma: Tensor,
+               beta: Tensor, states: Tensor, chunk_size: int, initial_state: Optional[Tensor],
+               dfinal: Optional[Tensor], state_only: bool) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+    B, T, H, P = x.shape
+    dev = x.device
+    lib = L.lib()
+    a = _build_args(x, q, k, kp, xp, adt, gamma, beta, chunk_size, L.ZB_FLAG_STATE_ONLY if state_only else 0)
+    if state_only:
+        grads = [torch.empty(0, dtype=t.dtype, device=dev) for t in (x, q, k, kp, xp, adt, gamma, beta)]
+    else:
+        grads = [torch.empty(t.shape, dtype=t.dtype, device=dev) for t in (x, q, k, kp, xp, adt, gamma, beta)]
+        for n, g in zip(L._VIEWS_BWD, grads):
+            setattr(a, n, L.view(g))
+    dinit = torch.empty((B, H, P, q.shape[3]), dtype=_acc_dtype(x.dtype), device=dev)
+    ws_bytes = lib.zb_ssd_workspace_bytes(ctypes.byref(a), 1)
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    a.dy = L.view(dy)
+    a.initial_state = L.ptr(initial_state)
+    a.dfinal_state = L.ptr(dfinal)
+    a.states = L.ptr(states)
+    a.dinitial_state = dinit.data_ptr()
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    a.status = L.status_word(dev).data_ptr()
+    L.check(lib.zb_ssd_bwd(ctypes.byref(a), _stream(dev)), "zb_ssd_bwd")
+    # order of grads: x, q, k, kp, xp, adt, gamma, beta
+    return (*grads, dinit)
+
+
+@ssd_bwd_op.register_fake
+def _(dy, x, q, k, kp, xp, adt, gamma, beta, states, chunk_size, initial_state, dfinal, state_only):
+    B, T, H, P = x.shape
+    if state_only:
+        grads = [t.new_empty((0,)) for t in (x, q, k, kp, xp, adt, gamma, beta)]
+    else:
+        grads = [torch.empty_like(t, memory_format=torch.contiguous_format) for t in (x, q, k, kp, xp, adt, gamma, beta)]
+    return (*grads, x.new_empty((B, H, P, q.shape[3]), dtype=_acc_dtype(x.dtype)))
+
+
+def _setup_context(ctx, inputs, output):
+    x, q, k, kp, xp, adt, gamma, beta, chunk_size, initial_state, save_states, state_only = inputs
+    _, _, states = output
+    ctx.chunk_size = chunk_size
+    ctx.has_init = initial_state is not None
+    ctx.state_only = state_only
+    saved = [x, q, k, kp, xp, adt, gamma, beta, states]
+    if initial_state is not None:
+        saved.append(initial_state)
+    ctx.save_for_backward(*saved)
+
+
+def _backward(ctx, dy, dfinal, _dstates):
+    saved = ctx.saved_tensors
+    x, q, k, kp, xp, adt, gamma, beta, states = saved[:9]
+    init = saved[9] if ctx.has_init else None
+    if states.numel() == 0:
+        raise RuntimeError("zenith_b200.ssd: backward needs the forward to save its chunk states")
+    if ctx.state_only or dy is None or dy.numel() == 0:
+        dy = torch.zeros(x.shape, dtype=x.dtype, device=x.device)
+    dy = dy.to(x.dtype)
+    if dy.stride(-1) != 1:
+        dy = dy.contiguous()
+    if dfinal is not None:
+        dfinal = dfinal.to(_acc_dtype(x.dtype)).contiguous()
+    out = ssd_bwd_op(dy, x, q, k, kp, xp, adt, gamma, beta, states, ctx.chunk_size, init, dfinal, False)
+    dx, dq, dk, dkp, dxp, dadt, dgamma, dbeta, dinit = out
+    return dx, dq, dk, dkp, dxp, dadt, dgamma, dbeta, None, (dinit if ctx.has_init else None), None, None
+
+
+torch.library.register_autograd("zenith_b200::ssd_fwd", _backward, setup_context=_setup_context)
+
+
+# ------------------------------------------------------------------------------------------------
+# public entry point
+
+
+def _inner_contig(t: Tensor) -> Tensor:
+    return t if t.stride(-1) == 1 or t.shape[-1] == 1 else t.contiguous()
+
+
+def prepare_inputs(x, q, k, kp, xp, adt, gamma, beta):
+    """Unify dtypes (one for the five vectors, one for the three per-token scalars) and make the
+    innermost dimension contiguous.  Under CUDA autocast with a 16-bit dtype, fp32 vectors are
+    cast to that dtype (the reference's matmuls run in it under autocast)."""
+    vec = [x, q, k, kp, xp]
+    sca = [adt, gamma, beta]
+    vdt = vec[0].dtype
+    for t in vec[1:]:
+        vdt = torch.promote_types(vdt, t.dtype)
+    sdt = sca[0].dtype
+    for t in sca[1:]:
+        sdt = torch.promote_types(sdt, t.dtype)
+    if x.is_cuda and torch.is_autocast_enabled("cuda") and vdt == torch.float32:
+        vdt = torch.get_autocast_dtype("cuda")
+    if vdt not in L.DTYPE_CODE:
+        raise TypeError(f"zenith_b200.ssd: unsupported dtype {vdt}")
+    if vdt == torch.float64:
+        sdt = torch.float64
+    elif sdt == torch.float64 or sdt not in L.DTYPE_CODE:
+        sdt = torch.float32
+    vec = [_inner_contig(t.to(vdt)) for t in vec]
+    sca = [t.to(sdt) for t in sca]
+    return (*vec, *sca)
+
+
+def ssd(x, q, k, kp, xp, adt, gamma, beta, chunk_size, *, initial_state=None, return_final_state=False):
+    """SSD chunked scan on the GPU; drop-in for ``zenith.mamba3.ssd`` (zenith/mamba3.py:30-56).
+
+    x, xp: [B, T, H, P]; q, k, kp: [B, T, G, N] (G == H, or G dividing H with head h reading
+    group h // (H // G)); adt, gamma, beta: [B, T, H].  Returns y [B, T, H, P] in x's dtype, or
+    ``(y, final_state)`` with ``return_final_state=True`` (final_state [B, H, P, N] fp32, fp64
+    for fp64 inputs).  Raises AssertionError("sequence length must be a multiple of
+    chunk_size") like the reference.
+    """
+    Bsz, T, H, P = x.shape
+    N = q.shape[-1]
+    assert T % chunk_size == 0, "sequence length must be a multiple of chunk_size"
+    if not x.is_cuda:
+        raise RuntimeError("zenith_b200.ssd runs on CUDA tensors only (no CPU path)")
+    out_dtype = x.dtype
+    args = prepare_inputs(x, q, k, kp, xp, adt, gamma, beta)
+    if initial_state is not None:
+        if tuple(initial_state.shape) != (Bsz, H, P, N):
+            raise ValueError(f"initial_state must be [B, H, P, N] = {(Bsz, H, P, N)}")
+        initial_state = initial_state.to(_acc_dtype(args[0].dtype)).contiguous()
+    need_grad = torch.is_grad_enabled() and any(
+        t.requires_grad for t in (x, q, k, kp, xp, adt, gamma, beta, initial_state) if t is not None)
+    y, final, _ = torch.ops.zenith_b200.ssd_fwd(*args, int(chunk_size), initial_state, need_grad, False)
+    if y.dtype != out_dtype:
+        y = y.to(out_dtype)
+    if return_final_state:
+        return y, final
+    return y
+
+
+def ssd_final_state(x, q, k, kp, xp, adt, gamma, beta, chunk_size, *, initial_state=None):
+    """Forward without outputs: only the final state [B, H, P, N] (not differentiable).
+    Used by the context-parallel pre-pass."""
+    args = prepare_inputs(x, q, k, kp, xp, adt, gamma, beta)
+    with torch.no_grad():
+        _, final, _ = torch.ops.zenith_b200.ssd_fwd(*args, int(chunk_size), initial_state, False, True)
+    return final
+
+
+def ssd_dinitial_state(dy, x, q, k, kp, xp, adt, gamma, beta, chunk_size, *, dfinal=None):
+    """Backward state chain only: the gradient w.r.t. the initial state of a range given dy on
+    its outputs (and dfinal on its final state); not differentiable.  Used by the
+    context-parallel pre-pass of the backward."""
+    args = prepare_inputs(x, q, k, kp, xp, adt, gamma, beta)
+    with torch.no_grad():
+        states = torch.empty(0, dtype=torch.uint8, device=x.device)
+        dy = _inner_contig(dy.to(args[0].dtype))
+        if dfinal is not None:
+            dfinal = dfinal.to(_acc_dtype(args[0].dtype)).contiguous()
+        out = torch.ops.zenith_b200.ssd_bwd(dy, *args, states, int(chunk_size), None, dfinal, True)
+    return out[-1]
+
+
+def use_b200_scan(model: torch.nn.Module) -> int:
+    """Install :func:`ssd` as the scan of every Mamba-3 block (``module.scan``, the reference's
+    injection point, zenith/mamba3.py:77).  Returns the number of blocks patched."""
+    n = 0
+    for m in model.modules():
+        if type(m).__name__ == "Mamba3" and hasattr(m, "scan"):
+            m.scan = ssd
+            n += 1
+    return n
