@@ -88,29 +88,48 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device_index: int):
+        import threading
+
         self.proc = None
+        self.lines: list[str] = []
+        self.error = ""
+        self.first = threading.Event()
         try:
             uuid = str(torch.cuda.get_device_properties(device_index).uuid)
             if not uuid.startswith("GPU-"):
                 uuid = "GPU-" + uuid
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={uuid}", "--query-gpu=" + ",".join(self.FIELDS), "--format=csv,noheader,nounits",
-                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except Exception:
-            self.proc = None
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
+        except Exception as e:  # no nvidia-smi: report it in the line
+            self.error = repr(e)
+            return
+
+        def reader():
+            for line in self.proc.stdout:
+                self.lines.append(line)
+                self.first.set()
+            self.first.set()
+
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+        self.first.wait(timeout=10.0)  # nvidia-smi takes a moment to start: sample before timing
 
     def stop(self):
         if self.proc is None:
-            return None
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "error": self.error}
+        n_before = len(self.lines)
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=5)
+            _, err = self.proc.communicate(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-            out, _ = self.proc.communicate()
+            _, err = self.proc.communicate()
+        self.thread.join(timeout=5)
+        out = "".join(self.lines[:max(n_before, 1)])
         rows = [r for r in csv.reader(io.StringIO(out)) if len(r) >= len(self.FIELDS)]
         if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "error": (err or "")[-200:]}
 
         def num(v):
             try:

@@ -110,7 +110,7 @@ int make_plan(const zb_ssd_args* a, Plan* pl) {
   pl->states_bytes = align_up(slots * pl->acc, 256);
   pl->sync_bytes = chain_sync_bytes(BH * (pl->nc + 1));
   pl->gchain_bytes = pl->states_bytes;
-  pl->grp_bytes = (a->G != a->H) ? align_up((size_t)a->B * a->T * a->H * 3 * a->N * sizeof(float), 256) : 0;
+  pl->grp_bytes = (a->G != a->H) ? align_up((size_t)a->B * a->T * a->H * 3 * a->N * pl->acc, 256) : 0;
   pl->tc_fwd_ws = pl->tc_bwd_ws = 0;
   return ZB_OK;
 }
@@ -248,7 +248,7 @@ int zb_ssd_bwd(const zb_ssd_args* a, void* stream_) {
     p.sync = sync;
     p.chain = a->states;
     p.gchain = ws + pl.sync_bytes;
-    p.grp = pl.grp_bytes ? reinterpret_cast<float*>(ws + pl.sync_bytes + pl.gchain_bytes) : nullptr;
+    p.grp = pl.grp_bytes ? static_cast<void*>(ws + pl.sync_bytes + pl.gchain_bytes) : nullptr;
     rc = simt_launch(p, a->dtype, a->scalar_dtype, true, stream);
   }
   if (rc == ZB_ERR_CUDA) return cuda_fail(cudaGetLastError());

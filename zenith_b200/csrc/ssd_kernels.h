@@ -28,7 +28,7 @@ struct SimtParams {
   View dx, dq, dk, dkp, dxp, dadt, dgamma, dbeta;
   void* dinit;
   void* gchain;  // [B*H][nc+1][P][N]: slot j = gradient w.r.t. the state entering chunk j
-  float* grp;    // [B,T,H,3,N] fp32 per-head q/k/kp gradients when G < H
+  void* grp;     // [B,T,H,3,N] per-head q/k/kp gradients (accumulator type) when G < H
 };
 
 // Largest internal chunk (<= 32) whose forward and backward tiles fit in shared memory; 0 if none.

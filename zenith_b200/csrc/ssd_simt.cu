@@ -26,9 +26,10 @@ struct SmemLayout {
   __host__ __device__ size_t fwd_elems() const {
     return 5 * (size_t)L + 3 * (size_t)L * N1 + 2 * (size_t)L * P1 + 2 * (size_t)L * L1 + (size_t)P * N1;
   }
-  // backward: 10 scalars/token, q k kp [L][N1], x xp dy [L][P1], A Ap E Ep [L][L1], S G [P][N1], 64 scratch
+  // backward: 10 scalars/token, q k kp [L][N1], x xp dy [L][P1], A Ap E Ep Z Zg Zb [L][L1],
+  // S G [P][N1], 64 scratch
   __host__ __device__ size_t bwd_elems() const {
-    return 10 * (size_t)L + 3 * (size_t)L * N1 + 3 * (size_t)L * P1 + 4 * (size_t)L * L1 + 2 * (size_t)P * N1 + 64;
+    return 10 * (size_t)L + 3 * (size_t)L * N1 + 3 * (size_t)L * P1 + 7 * (size_t)L * L1 + 2 * (size_t)P * N1 + 64;
   }
 };
 
@@ -208,7 +209,10 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
   TA* s_Ap = s_A + L * L1;
   TA* s_E = s_Ap + L * L1;
   TA* s_Ep = s_E + L * L1;
-  TA* s_S = s_Ep + L * L1;  // S_in [P][N1]
+  TA* s_Z = s_Ep + L * L1;  // dA.A + dAp.Ap   (row sums - column sums -> dc)
+  TA* s_Zg = s_Z + L * L1;  // E (q.k)         (column sums -> dgamma)
+  TA* s_Zb = s_Zg + L * L1; // Ep (q.kp)       (column sums -> dbeta)
+  TA* s_S = s_Zb + L * L1;  // S_in [P][N1]
   TA* s_G = s_S + P * N1;   // Gn   [P][N1]
   TA* s_red = s_G + P * N1; // 64 scratch
   __shared__ int s_ticket, s_ready;
@@ -277,11 +281,12 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
   __syncthreads();
   const TA a_chunk = xexp(cl);
 
-  // intra-chunk score gradients: A = (q.k) g M, dA = dy.x, E = dA M, ...
+  // intra-chunk score gradients: A = (q.k) g M, dA = dy.x, E = dA M, ...  All reductions
+  // below run in a fixed order (no atomics), so results are bitwise reproducible.
   if (!state_only) {
     for (int i = tid; i < L * L; i += kThreads) {
       const int t = i / L, s = i % L;
-      TA vA = 0, vAp = 0, vE = 0, vEp = 0;
+      TA vA = 0, vAp = 0, vE = 0, vEp = 0, z = 0, zg = 0, zb = 0;
       if (s <= t && t < Lc) {
         TA qk = 0, qkp = 0, da = 0, dap = 0;
         for (int n = 0; n < N; ++n) {
@@ -299,16 +304,35 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
         vAp = qkp * s_b[s] * m;
         vE = da * m;
         vEp = dap * m;
-        const TA z = da * vA + dap * vAp;
-        atomicAdd(&s_dc[t], z);
-        atomicAdd(&s_dc[s], -z);
-        atomicAdd(&s_dg[s], vE * qk);
-        atomicAdd(&s_db[s], vEp * qkp);
+        z = da * vA + dap * vAp;
+        zg = vE * qk;
+        zb = vEp * qkp;
       }
       s_A[t * L1 + s] = vA;
       s_Ap[t * L1 + s] = vAp;
       s_E[t * L1 + s] = vE;
       s_Ep[t * L1 + s] = vEp;
+      s_Z[t * L1 + s] = z;
+      s_Zg[t * L1 + s] = zg;
+      s_Zb[t * L1 + s] = zb;
+    }
+    __syncthreads();
+    // one warp per token u: dc_u = sum_s Z[u][s] - sum_t Z[t][u]; dgamma_u, dbeta_u = column sums
+    for (int u = warp; u < L; u += kThreads / 32) {
+      TA dc = 0, dg = 0, db = 0;
+      if (lane < L) {
+        dc = s_Z[u * L1 + lane] - s_Z[lane * L1 + u];
+        dg = s_Zg[lane * L1 + u];
+        db = s_Zb[lane * L1 + u];
+      }
+      dc = warp_sum(dc);
+      dg = warp_sum(dg);
+      db = warp_sum(db);
+      if (lane == 0) {
+        s_dc[u] = dc;
+        s_dg[u] = dg;
+        s_db[u] = db;
+      }
     }
   }
   // dS_in_loc = sum_t e^{c_t} dy_t q_t^T, parked in this chunk's outgoing gradient slot
@@ -353,40 +377,52 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
   if (lane == 0) s_red[warp] = da_part;
   __syncthreads();
 
-  // dx, dxp and the state-term dot products
-  for (int i = tid; i < Lc * P; i += kThreads) {
-    const int s = i / P, pp = i % P;
-    TA u = 0, up = 0;
-    for (int n = 0; n < N; ++n) {
-      const TA gn = s_G[pp * N1 + n];
-      u += gn * s_k[s * N1 + n];
-      up += gn * s_kp[s * N1 + n];
+  // dx, dxp and the state-term dot products: one warp per token s, lanes over p
+  for (int s = warp; s < Lc; s += kThreads / 32) {
+    TA xu = 0, xpu = 0;
+    for (int pp = lane; pp < P; pp += 32) {
+      TA u = 0, up = 0;
+      for (int n = 0; n < N; ++n) {
+        const TA gn = s_G[pp * N1 + n];
+        u += gn * s_k[s * N1 + n];
+        up += gn * s_kp[s * N1 + n];
+      }
+      TA vx = 0, vxp = 0;
+      for (int t = s; t < Lc; ++t) {
+        const TA d = s_dy[t * P1 + pp];
+        vx += s_A[t * L1 + s] * d;
+        vxp += s_Ap[t * L1 + s] * d;
+      }
+      vx += s_w[s] * s_g[s] * u;
+      vxp += s_w[s] * s_b[s] * up;
+      stv<TA>(p.dx.wrow<TI>(b, t0 + s, h) + pp, vx);
+      stv<TA>(p.dxp.wrow<TI>(b, t0 + s, h) + pp, vxp);
+      xu += s_x[s * P1 + pp] * u;
+      xpu += s_xp[s * P1 + pp] * up;
     }
-    TA vx = 0, vxp = 0;
-    for (int t = s; t < Lc; ++t) {
-      const TA d = s_dy[t * P1 + pp];
-      vx += s_A[t * L1 + s] * d;
-      vxp += s_Ap[t * L1 + s] * d;
+    xu = warp_sum(xu);
+    xpu = warp_sum(xpu);
+    if (lane == 0) {
+      s_xu[s] = xu;
+      s_xpu[s] = xpu;
     }
-    vx += s_w[s] * s_g[s] * u;
-    vxp += s_w[s] * s_b[s] * up;
-    stv<TA>(p.dx.wrow<TI>(b, t0 + s, h) + pp, vx);
-    stv<TA>(p.dxp.wrow<TI>(b, t0 + s, h) + pp, vxp);
-    atomicAdd(&s_xu[s], s_x[s * P1 + pp] * u);
-    atomicAdd(&s_xpu[s], s_xp[s * P1 + pp] * up);
   }
   const bool grouped = p.G != p.H;
-  // dq (intra + inter) and its contribution to dc
-  for (int i = tid; i < Lc * N; i += kThreads) {
-    const int t = i / N, n = i % N;
-    TA acc = 0;
-    for (int s = 0; s <= t; ++s) acc += s_E[t * L1 + s] * s_g[s] * s_k[s * N1 + n] + s_Ep[t * L1 + s] * s_b[s] * s_kp[s * N1 + n];
-    TA r = 0;
-    for (int pp = 0; pp < P; ++pp) r += s_S[pp * N1 + n] * s_dy[t * P1 + pp];
-    acc += s_ec[t] * r;
-    atomicAdd(&s_dc[t], s_ec[t] * s_q[t * N1 + n] * r);
-    if (grouped) p.grp[((b * p.T + t0 + t) * p.H + h) * 3 * N + n] = (float)acc;
-    else stv<TA>(p.dq.wrow<TI>(b, t0 + t, h) + n, acc);
+  // dq (intra + inter) and its contribution to dc: one warp per token t, lanes over n
+  for (int t = warp; t < Lc; t += kThreads / 32) {
+    TA dct = 0;
+    for (int n = lane; n < N; n += 32) {
+      TA acc = 0;
+      for (int s = 0; s <= t; ++s) acc += s_E[t * L1 + s] * s_g[s] * s_k[s * N1 + n] + s_Ep[t * L1 + s] * s_b[s] * s_kp[s * N1 + n];
+      TA r = 0;
+      for (int pp = 0; pp < P; ++pp) r += s_S[pp * N1 + n] * s_dy[t * P1 + pp];
+      acc += s_ec[t] * r;
+      dct += s_ec[t] * s_q[t * N1 + n] * r;
+      if (grouped) reinterpret_cast<TA*>(p.grp)[((b * p.T + t0 + t) * p.H + h) * 3 * N + n] = acc;
+      else stv<TA>(p.dq.wrow<TI>(b, t0 + t, h) + n, acc);
+    }
+    dct = warp_sum(dct);
+    if (lane == 0) s_dc[t] += dct;
   }
   // dk, dkp
   for (int i = tid; i < Lc * N; i += kThreads) {
@@ -406,9 +442,9 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
     const TA vk = s_g[s] * (e + s_w[s] * gx);
     const TA vkp = s_b[s] * (ep + s_w[s] * gxp);
     if (grouped) {
-      float* gp = p.grp + ((b * p.T + t0 + s) * p.H + h) * 3 * N;
-      gp[N + n] = (float)vk;
-      gp[2 * N + n] = (float)vkp;
+      TA* gp = reinterpret_cast<TA*>(p.grp) + ((b * p.T + t0 + s) * p.H + h) * 3 * N;
+      gp[N + n] = vk;
+      gp[2 * N + n] = vkp;
     } else {
       stv<TA>(p.dk.wrow<TI>(b, t0 + s, h) + n, vk);
       stv<TA>(p.dkp.wrow<TI>(b, t0 + s, h) + n, vkp);
@@ -442,23 +478,23 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
   }
 }
 
-// sum the per-head q/k/kp gradients of each group: grp [B,T,H,3,N] fp32 -> dq/dk/dkp [B,T,G,N]
-template <typename TI>
+// sum the per-head q/k/kp gradients of each group: grp [B,T,H,3,N] (TA) -> dq/dk/dkp [B,T,G,N]
+template <typename TI, typename TA>
 __global__ void group_reduce_kernel(const SimtParams p) {
   const int64_t N = p.N, r = p.H / p.G;
   const int64_t total = p.B * p.T * p.G * N;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t n = i % N, g = (i / N) % p.G, t = (i / (N * p.G)) % p.T, b = i / (N * p.G * p.T);
-    float acc[3] = {0.f, 0.f, 0.f};
+    TA acc[3] = {0, 0, 0};
     for (int64_t u = 0; u < r; ++u) {
-      const float* gp = p.grp + ((b * p.T + t) * p.H + g * r + u) * 3 * N;
+      const TA* gp = reinterpret_cast<const TA*>(p.grp) + ((b * p.T + t) * p.H + g * r + u) * 3 * N;
       acc[0] += gp[n];
       acc[1] += gp[N + n];
       acc[2] += gp[2 * N + n];
     }
-    stv<float>(p.dq.wrow<TI>(b, t, g) + n, acc[0]);
-    stv<float>(p.dk.wrow<TI>(b, t, g) + n, acc[1]);
-    stv<float>(p.dkp.wrow<TI>(b, t, g) + n, acc[2]);
+    stv<TA>(p.dq.wrow<TI>(b, t, g) + n, acc[0]);
+    stv<TA>(p.dk.wrow<TI>(b, t, g) + n, acc[1]);
+    stv<TA>(p.dkp.wrow<TI>(b, t, g) + n, acc[2]);
   }
 }
 
@@ -491,7 +527,7 @@ static int launch_simt(const SimtParams& p, bool backward, cudaStream_t stream) 
     if (p.G != p.H && !(p.flags & ZB_FLAG_STATE_ONLY)) {
       const int64_t total = p.B * p.T * p.G * p.N;
       const unsigned nb = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16);
-      group_reduce_kernel<TI><<<nb, 256, 0, stream>>>(p);
+      group_reduce_kernel<TI, TA><<<nb, 256, 0, stream>>>(p);
       note_launches(1);
     }
   }
