@@ -43,7 +43,8 @@ typedef enum {
   ZB_ERR_CUDA = 4,         /* a CUDA runtime call failed (see zb_last_cuda_error) */
   ZB_ERR_TIMEOUT = 5,      /* a kernel gave up waiting for the preceding chunk's state */
   ZB_ERR_WORKSPACE = 6,    /* workspace or saved-states buffer too small / misaligned */
-  ZB_ERR_UNSUPPORTED = 7   /* sizes beyond what the kernels handle (e.g. P > 256) */
+  ZB_ERR_UNSUPPORTED = 7,  /* sizes beyond what the kernels handle (e.g. P > 256) */
+  ZB_ERR_SCRATCH_LIMIT = 8 /* zb_ssd_fwd_noalloc: the call needs more scratch than ZB_NOALLOC_SCRATCH_BYTES */
 } zb_status;
 
 typedef enum { ZB_F32 = 0, ZB_BF16 = 1, ZB_F16 = 2, ZB_F64 = 3 } zb_dtype;
@@ -128,6 +129,27 @@ ZB_API int zb_ssd_check_status(const int32_t* status, void* stream);
 /* Number of kernels this library has launched in this process (all devices, all threads).
  * No reference counterpart: lets a benchmark count the GPU launches of a timed region. */
 ZB_API uint64_t zb_launch_count(void);
+
+/* Size of the fixed device scratch array behind zb_ssd_fwd_noalloc (32 MiB per GPU). */
+#define ZB_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* Forward scan that allocates nothing.  This entry point has no counterpart in the reference.
+ *
+ * It is for callers that cannot obtain device memory for a call: a serving runtime that
+ * reserves all device memory up front and hands out no scratch, or a foreign-language binding
+ * that can pass tensors it was given but has no CUDA allocator of its own.  The caller passes
+ * the inputs and outputs exactly as for zb_ssd_fwd; `workspace` and `workspace_bytes` are
+ * ignored.  Scratch comes from one file-scope device array of ZB_NOALLOC_SCRATCH_BYTES that
+ * every GPU which loads the library holds until the process exits.
+ *
+ * - The first call on a device looks the array up for that device (cudaGetSymbolAddress);
+ *   make that first call before any stream capture on the device.
+ * - A call whose scratch need (zb_ssd_workspace_bytes(args, 0)) exceeds
+ *   ZB_NOALLOC_SCRATCH_BYTES returns ZB_ERR_SCRATCH_LIMIT and launches nothing.
+ * - All calls on a device share the array: calls that overlap on the GPU (different streams
+ *   without ordering) race and give wrong results.  Order them on one stream.
+ * - No cudaMalloc, cudaFree or allocating library routine is called. */
+ZB_API int zb_ssd_fwd_noalloc(const zb_ssd_args* args, void* stream);
 
 #ifdef __cplusplus
 }

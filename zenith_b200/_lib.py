@@ -16,7 +16,8 @@ LIB_PATH = pathlib.Path(__file__).resolve().parent / "libzenith_ssd.so"
 
 ZB_F32, ZB_BF16, ZB_F16, ZB_F64 = 0, 1, 2, 3
 ZB_FLAG_STATE_ONLY = 1
-ZB_ERR_SHAPE, ZB_ERR_TIMEOUT = 1, 5
+ZB_ERR_SHAPE, ZB_ERR_TIMEOUT, ZB_ERR_SCRATCH_LIMIT = 1, 5, 8
+ZB_NOALLOC_SCRATCH_BYTES = 32 << 20
 
 DTYPE_CODE = {torch.float32: ZB_F32, torch.bfloat16: ZB_BF16, torch.float16: ZB_F16, torch.float64: ZB_F64}
 
@@ -87,6 +88,8 @@ def lib() -> ctypes.CDLL:
         L.zb_ssd_check_status.restype = ctypes.c_int
         L.zb_ssd_check_status.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         L.zb_launch_count.restype = ctypes.c_uint64
+        L.zb_ssd_fwd_noalloc.restype = ctypes.c_int
+        L.zb_ssd_fwd_noalloc.argtypes = [ctypes.POINTER(Args), ctypes.c_void_p]
         _lib = L
     return _lib
 

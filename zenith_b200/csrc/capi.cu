@@ -173,6 +173,7 @@ const char* zb_strerror(int s) {
     case ZB_ERR_TIMEOUT: return "timed out waiting for the preceding chunk's state";
     case ZB_ERR_WORKSPACE: return "workspace or saved-states buffer missing, too small or misaligned";
     case ZB_ERR_UNSUPPORTED: return "sizes not supported by the kernels";
+    case ZB_ERR_SCRATCH_LIMIT: return "call needs more scratch than the fixed no-alloc array (ZB_NOALLOC_SCRATCH_BYTES)";
     default: return "unknown status";
   }
 }
