@@ -126,6 +126,11 @@ ZB_API int zb_ssd_total_decay(const zb_ssd_args* args, float* out, void* stream)
 /* Copy the device status word to the host (synchronises `stream`) and report it. */
 ZB_API int zb_ssd_check_status(const int32_t* status, void* stream);
 
+/* Which kernel family a call with these arguments uses: 0 = SIMT (fp32/fp64 FMA path),
+ * 1 = tensor-core (tcgen05) path.  `states_saved` says whether the forward saves states for a
+ * backward.  No reference counterpart (diagnostic); -1 on invalid arguments. */
+ZB_API int zb_ssd_kernel_family(const zb_ssd_args* args, int states_saved);
+
 /* Number of kernels this library has launched in this process (all devices, all threads).
  * No reference counterpart: lets a benchmark count the GPU launches of a timed region. */
 ZB_API uint64_t zb_launch_count(void);

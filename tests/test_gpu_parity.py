@@ -10,6 +10,7 @@ import torch.nn.functional as F
 import zenith_b200
 from oracle.ssd_oracle import max_rel_err, ssd_backward, ssd_forward
 from tests.golden_io import CASES, NAMES, load
+from zenith_b200.ssd import kernel_family
 from zenith_b200.synthetic import SHAPES, SsdShape, make_inputs
 
 pytestmark = pytest.mark.gpu
@@ -153,6 +154,26 @@ def test_no_grad_forward_matches():
         y = zenith_b200.ssd(*(inp[n].cuda() for n in NAMES), chunk)
     zenith_b200.check_status()
     assert max_rel_err(y, ref["y"]) < TOL[torch.float32]
+
+
+@pytest.mark.parametrize("shape", [SsdShape(2, 256, 4, 64, 128, 4, 64), SsdShape(2, 192, 8, 64, 64, 2, 64),
+                                   SsdShape(1, 512, 3, 64, 128, 1, 128), SsdShape(3, 64, 2, 64, 128, 2, 64)],
+                         ids=["n128", "n64-groups", "g1-chunk128", "one-chunk"])
+def test_tensor_core_forward_matches_oracle(shape):
+    """bf16 forward without saved states (the tcgen05 kernel), with initial and final state."""
+    inp = _cast(make_inputs(shape, seed=21), torch.bfloat16, torch.float32)
+    g = torch.Generator().manual_seed(5)
+    init = torch.randn(shape.B, shape.H, shape.P, shape.N, generator=g)
+    dev = "cuda"
+    prepared = zenith_b200.prepare_inputs(*(inp[n].to(dev) for n in NAMES))
+    assert kernel_family(*prepared, shape.chunk, states_saved=False) == "tensor-core"
+    with torch.no_grad():
+        y, fin = zenith_b200.ssd(*(inp[n].to(dev) for n in NAMES), shape.chunk, initial_state=init.to(dev),
+                                 return_final_state=True)
+    zenith_b200.check_status()
+    ref = oracle(inp, shape.chunk, init=init.double())
+    assert max_rel_err(y, ref["y"]) < TOL[torch.bfloat16]
+    assert max_rel_err(fin, ref["final_state"]) < TOL[torch.bfloat16]
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])

@@ -88,6 +88,8 @@ def lib() -> ctypes.CDLL:
         L.zb_ssd_check_status.restype = ctypes.c_int
         L.zb_ssd_check_status.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         L.zb_launch_count.restype = ctypes.c_uint64
+        L.zb_ssd_kernel_family.restype = ctypes.c_int
+        L.zb_ssd_kernel_family.argtypes = [ctypes.POINTER(Args), ctypes.c_int]
         L.zb_ssd_fwd_noalloc.restype = ctypes.c_int
         L.zb_ssd_fwd_noalloc.argtypes = [ctypes.POINTER(Args), ctypes.c_void_p]
         _lib = L

@@ -84,9 +84,12 @@ int validate(const zb_ssd_args* a, bool backward) {
   return ZB_OK;
 }
 
-int make_plan(const zb_ssd_args* a, Plan* pl) {
+// Kernel family for these arguments.  The tensor-core family is used for everything it has
+// both directions for (tc_has_backward); until then only for forwards that save no states,
+// so the saved-state layout a backward reads always matches the forward that wrote it.
+int make_plan(const zb_ssd_args* a, Plan* pl, bool stateless_forward) {
   const int64_t BH = a->B * a->H;
-  if (tc_supported(a)) {
+  if (tc_supported(a) && (tc_has_backward(a) || stateless_forward)) {
     pl->kind = kTc;
     pl->L = tc_chunk();
     pl->nc = (int)((a->T + pl->L - 1) / pl->L);
@@ -188,19 +191,31 @@ size_t zb_ssd_states_bytes(const zb_ssd_args* a) {
     if (!dtype_size(a->dtype) || !dtype_size(a->scalar_dtype)) return 0;
   }
   Plan pl;
-  if (make_plan(a, &pl) != ZB_OK) return 0;
+  if (make_plan(a, &pl, false) != ZB_OK) return 0;
   return pl.states_bytes;
 }
+
+namespace {
+// scratch a plan needs: [sync | TC ring] or [sync | SIMT chain (fwd) / gradient chain + groups (bwd)]
+size_t plan_workspace(const Plan& pl, bool backward) {
+  if (pl.kind == kTc) return pl.sync_bytes + (backward ? pl.tc_bwd_ws : pl.tc_fwd_ws);
+  if (!backward) return pl.sync_bytes + pl.states_bytes;  // the chain lives here when no states buffer is given
+  return pl.sync_bytes + pl.gchain_bytes + pl.grp_bytes;
+}
+}  // namespace
 
 size_t zb_ssd_workspace_bytes(const zb_ssd_args* a, int backward) {
   if (!a || a->B <= 0 || a->T <= 0 || a->H <= 0 || a->G <= 0 || a->P <= 0 || a->N <= 0) return 0;
   if (a->chunk_size <= 0 || a->T % a->chunk_size || a->H % a->G) return 0;
   if (!dtype_size(a->dtype) || !dtype_size(a->scalar_dtype)) return 0;
   Plan pl;
-  if (make_plan(a, &pl) != ZB_OK) return 0;
-  if (pl.kind == kTc) return pl.sync_bytes + (backward ? pl.tc_bwd_ws : pl.tc_fwd_ws) + (backward ? 0 : pl.states_bytes);
-  if (!backward) return pl.sync_bytes + pl.states_bytes;  // chain lives here when no states buffer is given
-  return pl.sync_bytes + pl.gchain_bytes + pl.grp_bytes;
+  if (make_plan(a, &pl, false) != ZB_OK) return 0;
+  size_t need = plan_workspace(pl, backward != 0);
+  if (!backward) {  // a forward may run with or without a states buffer: cover both plans
+    Plan p2;
+    if (make_plan(a, &p2, true) == ZB_OK) need = std::max(need, plan_workspace(p2, false));
+  }
+  return need;
 }
 
 int zb_ssd_fwd(const zb_ssd_args* a, void* stream_) {
@@ -208,8 +223,8 @@ int zb_ssd_fwd(const zb_ssd_args* a, void* stream_) {
   int rc = validate(a, false);
   if (rc) return rc;
   Plan pl;
-  if ((rc = make_plan(a, &pl))) return rc;
-  const size_t need = zb_ssd_workspace_bytes(a, 0);
+  if ((rc = make_plan(a, &pl, a->states == nullptr))) return rc;
+  const size_t need = plan_workspace(pl, false);
   if (!a->workspace || a->workspace_bytes < need || reinterpret_cast<uintptr_t>(a->workspace) % 256) return ZB_ERR_WORKSPACE;
   if (a->states && reinterpret_cast<uintptr_t>(a->states) % 256) return ZB_ERR_WORKSPACE;
   char* ws = static_cast<char*>(a->workspace);
@@ -218,7 +233,7 @@ int zb_ssd_fwd(const zb_ssd_args* a, void* stream_) {
   ChainSync sync{reinterpret_cast<unsigned int*>(ws), reinterpret_cast<int*>(ws + 256)};
   void* chain = a->states ? a->states : static_cast<void*>(ws + pl.sync_bytes);
   if (pl.kind == kTc) {
-    rc = tc_fwd(a, sync, chain, ws + pl.sync_bytes + (a->states ? 0 : pl.states_bytes), stream);
+    rc = tc_fwd(a, sync, a->states, ws + pl.sync_bytes, stream);
   } else {
     SimtParams p = simt_params(a, pl);
     p.sync = sync;
@@ -234,8 +249,8 @@ int zb_ssd_bwd(const zb_ssd_args* a, void* stream_) {
   int rc = validate(a, true);
   if (rc) return rc;
   Plan pl;
-  if ((rc = make_plan(a, &pl))) return rc;
-  const size_t need = zb_ssd_workspace_bytes(a, 1);
+  if ((rc = make_plan(a, &pl, false))) return rc;
+  const size_t need = plan_workspace(pl, true);
   if (!a->workspace || a->workspace_bytes < need || reinterpret_cast<uintptr_t>(a->workspace) % 256) return ZB_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(a->states) % 256) return ZB_ERR_WORKSPACE;
   char* ws = static_cast<char*>(a->workspace);
@@ -296,5 +311,14 @@ int zb_ssd_check_status(const int32_t* status, void* stream) {
 }
 
 uint64_t zb_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int zb_ssd_kernel_family(const zb_ssd_args* a, int states_saved) {
+  if (!a || a->B <= 0 || a->T <= 0 || a->H <= 0 || a->G <= 0 || a->P <= 0 || a->N <= 0) return -1;
+  if (a->chunk_size <= 0 || a->T % a->chunk_size || a->H % a->G) return -1;
+  if (!dtype_size(a->dtype) || !dtype_size(a->scalar_dtype)) return -1;
+  Plan pl;
+  if (make_plan(a, &pl, states_saved == 0) != ZB_OK) return -1;
+  return pl.kind == kTc ? 1 : 0;
+}
 
 }  // extern "C"

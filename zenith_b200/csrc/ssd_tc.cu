@@ -1,13 +1,438 @@
-// Tensor-core path (tcgen05) of the SSD chunked scan: not enabled yet.
+// Tensor-core path of the SSD chunked scan for bf16 vectors (P = 64, N = 64 or 128, fp32
+// per-token scalars): tcgen05 MMAs with fp32 accumulators in TMEM, operands staged in shared
+// memory by TMA (128-byte swizzle, no multicast).
+//
+// Forward, one CTA per (batch, head, 64-token chunk), 256 threads, 256 TMEM columns:
+//   MMA1  S   = Q [K;Kp]^T              M=64 (t)   N=128 (s|s')   K=N   A,B K-major
+//   MMA3  Sl' = [K;Kp]^T [wgX ; wbXp]   M=N (n)    N=64 (p)       K=128 A,B MN-major
+//   epilogue: Ps = (S * [g|b]_s * exp(c_t - c_s) masked to s <= t) -> bf16 smem
+//   MMA2  Yi  = Ps [X;Xp]               M=64 (t)   N=64 (p)       K=128 A K-major, B MN-major
+//   chain: wait for S_in[j]; S_in[j+1] = e^{c_L} S_in[j] + Sl'^T -> ring slot; publish
+//   MMA4  Ye  = Q S_in[j]^T             M=64 (t)   N=64 (p)       K=N   A K-major, B MN-major
+//   epilogue: y = Yi + e^{c_t} Ye -> bf16
+// TMEM columns: [0,128) S (M=64 layout: lanes 0-15 of each 32-lane sub-partition);
+// [128,192) Yi at lane offset 0 and Ye at lane offset 16 (two interleaved M=64 tiles);
+// [192,256) Sl' (M=128 layout for N=128: lane = n).
+// The fp32 state hand-off lives in a two-slot ring per (batch, head) that stays in L2; the
+// states the backward needs are saved in bf16 [B*H][nc][N][P].
+#include <cuda.h>
+
+#include <mutex>
+
 #include "ssd_tc.h"
+#include "ssd_kernels.h"
+#include "umma.cuh"
 
 namespace zb {
 
-bool tc_supported(const zb_ssd_args*) { return false; }
-int tc_chunk() { return 64; }
-size_t tc_states_bytes(const zb_ssd_args*) { return 0; }
-size_t tc_workspace_bytes(const zb_ssd_args*, bool) { return 0; }
-int tc_fwd(const zb_ssd_args*, ChainSync, void*, void*, cudaStream_t) { return ZB_ERR_UNSUPPORTED; }
+namespace {
+
+constexpr int kTcThreads = 256;
+constexpr int kL = 64;  // internal chunk length
+constexpr int kP = 64;
+
+template <int NS>
+struct FwdSmem {
+  static constexpr int QB = NS / 64;                      // 64-wide blocks along n
+  static constexpr uint32_t Q = 0;                        // [QB][64 t][64 n]
+  static constexpr uint32_t KK = Q + QB * 8192;           // [QB][K | Kp][64 s][64 n]; later Ps [2][64 t][64 s]
+  static constexpr uint32_t X = KK + QB * 16384;          // [64 s][64 p]
+  static constexpr uint32_t XP = X + 8192;
+  static constexpr uint32_t XS = XP + 8192;               // [wgX | wbXp]
+  static constexpr uint32_t SIN = XS + 16384;             // [NS n][64 p]
+  static constexpr uint32_t SCAL = SIN + NS * 128;        // c, ec, wg, wb, g, b (64 floats each)
+  static constexpr uint32_t BAR = SCAL + 6 * 64 * 4;      // 4 mbarriers
+  static constexpr uint32_t MISC = BAR + 4 * 8;           // tmem base, ticket, ready
+  static constexpr uint32_t TOTAL = MISC + 16;
+  static constexpr uint32_t ALLOC = TOTAL + 1024;         // slack to align the base to 1024
+};
+
+struct TcFwdParams {
+  CUtensorMap tq, tk, tkp, tx, txp;
+  int64_t B, T, H, G;
+  int nc;
+  const float* adt;
+  const float* gamma;
+  const float* beta;
+  int64_t ssb, sst, ssh;  // strides of the three scalar views (all equal: checked on the host)
+  int64_t asb, ast, ash, gsb, gst, gsh, bsb, bst, bsh;
+  __nv_bfloat16* y;
+  int64_t ysb, yst, ysh;
+  const float* init;
+  float* fin;
+  __nv_bfloat16* states;  // [B*H][nc][N][P] or nullptr
+  float* ring;            // [B*H][2][P][N]
+  unsigned int* ticket;
+  int* flags;             // [B*H][nc+1]
+  int32_t* status;
+};
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ float2 unpack_bf16(uint32_t u) {
+  __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&u);
+  return __bfloat1622float2(v);
+}
+
+template <int NS>
+__global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_constant__ TcFwdParams p) {
+  using S = FwdSmem<NS>;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sQ = sm + S::Q;
+  unsigned char* sKK = sm + S::KK;
+  unsigned char* sPs = sKK;  // reused once MMA1 and MMA3 have read K/Kp
+  unsigned char* sX = sm + S::X;
+  unsigned char* sXp = sm + S::XP;
+  unsigned char* sXs = sm + S::XS;
+  unsigned char* sSin = sm + S::SIN;
+  float* s_c = reinterpret_cast<float*>(sm + S::SCAL);
+  float* s_ec = s_c + 64;
+  float* s_wg = s_c + 128;
+  float* s_wb = s_c + 192;
+  float* s_g = s_c + 256;
+  float* s_b = s_c + 320;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::BAR);
+  uint32_t* misc = reinterpret_cast<uint32_t*>(sm + S::MISC);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    misc[1] = atomicAdd(p.ticket, 1u);
+    for (int i = 0; i < 4; ++i) umma::mbar_init(&bars[i], 1);
+    umma::mbar_fence_init();
+  }
+  if (warp == 0) {
+    umma::tmem_alloc(&misc[0], 256);
+    umma::tmem_relinquish();
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = misc[0];
+  const int64_t BH = p.B * p.H;
+  const int64_t tk = misc[1];
+  const int j = (int)(tk / BH);
+  const int64_t bh = tk % BH;
+  const int b = (int)(bh / p.H), h = (int)(bh % p.H);
+  const int g = (int)(h / (p.H / p.G));
+  const int t0 = j * kL;
+  int* flags = p.flags + bh * (p.nc + 1);
+
+  constexpr uint32_t kLoadBytes = S::QB * 8192 * 3 + 2 * 8192;
+  if (tid == 0) {
+    umma::mbar_arrive_expect_tx(&bars[0], kLoadBytes);
+#pragma unroll
+    for (int qb = 0; qb < S::QB; ++qb) {
+      umma::tma_load_4d(sQ + qb * 8192, &p.tq, &bars[0], qb * 64, g, t0, b);
+      umma::tma_load_4d(sKK + qb * 16384, &p.tk, &bars[0], qb * 64, g, t0, b);
+      umma::tma_load_4d(sKK + qb * 16384 + 8192, &p.tkp, &bars[0], qb * 64, g, t0, b);
+    }
+    umma::tma_load_4d(sX, &p.tx, &bars[0], 0, h, t0, b);
+    umma::tma_load_4d(sXp, &p.txp, &bars[0], 0, h, t0, b);
+  }
+  // per-token scalars and the in-chunk cumulative sum c (mamba3.py:40)
+  if (tid < 64) {
+    const int t = t0 + tid;
+    const float a = p.adt[b * p.asb + t * p.ast + h * p.ash];
+    s_g[tid] = p.gamma[b * p.gsb + t * p.gst + h * p.gsh];
+    s_b[tid] = p.beta[b * p.bsb + t * p.bst + h * p.bsh];
+    s_c[tid] = warp_incl_scan(a, lane);
+  }
+  __syncthreads();
+  if (tid >= 32 && tid < 64) s_c[tid] += s_c[31];
+  __syncthreads();
+  if (tid < 64) {
+    const float c = s_c[tid], w = expf(s_c[63] - c);
+    s_ec[tid] = expf(c);
+    s_wg[tid] = w * s_g[tid];
+    s_wb[tid] = w * s_b[tid];
+  }
+  const bool load_ok = umma::mbar_wait(&bars[0], 0, p.status);
+  __syncthreads();
+  const float a_chunk = expf(s_c[63]);
+  bool ok = __syncthreads_and(load_ok);
+
+  if (ok) {
+    // [wgX | wbXp]: scale each row s of X / Xp (a 16-byte chunk at byte offset o lies in row o / 128)
+    for (int i = tid; i < 1024; i += kTcThreads) {
+      const int tile = i >> 9;
+      const uint32_t off = (uint32_t)(i & 511) * 16u;
+      const float f = tile ? s_wb[off >> 7] : s_wg[off >> 7];
+      const uint4 v = *reinterpret_cast<const uint4*>((tile ? sXp : sX) + off);
+      uint4 o;
+      float2 e;
+      e = unpack_bf16(v.x); o.x = pack_bf16(e.x * f, e.y * f);
+      e = unpack_bf16(v.y); o.y = pack_bf16(e.x * f, e.y * f);
+      e = unpack_bf16(v.z); o.z = pack_bf16(e.x * f, e.y * f);
+      e = unpack_bf16(v.w); o.w = pack_bf16(e.x * f, e.y * f);
+      *reinterpret_cast<uint4*>(sXs + tile * 8192 + off) = o;
+    }
+    umma::fence_proxy_async_smem();
+    umma::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+      umma::fence_after_sync();
+      const uint32_t q0 = umma::smem_u32(sQ), kk0 = umma::smem_u32(sKK), xs0 = umma::smem_u32(sXs);
+      constexpr uint32_t id1 = umma::idesc_bf16(64, 128, false, false);
+#pragma unroll
+      for (int ks = 0; ks < NS / 16; ++ks) {
+        const uint32_t qb = ks >> 2, kin = ks & 3;
+        umma::mma_bf16(tmem, umma::desc_sw128(q0 + qb * 8192 + kin * 32, 16, 1024),
+                       umma::desc_sw128(kk0 + qb * 16384 + kin * 32, 16, 1024), id1, ks > 0);
+      }
+      constexpr uint32_t id3 = umma::idesc_bf16(NS, 64, true, true);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t part = ks >> 2, kin = ks & 3;
+        umma::mma_bf16(tmem + 192, umma::desc_sw128(kk0 + part * 8192 + kin * 2048, 16384, 1024),
+                       umma::desc_sw128(xs0 + part * 8192 + kin * 2048, 8192, 1024), id3, ks > 0);
+      }
+      umma::mma_commit(&bars[1]);
+    }
+    ok = __syncthreads_and(umma::mbar_wait(&bars[1], 0, p.status));
+  }
+  if (ok) {
+    umma::fence_after_sync();
+    // scores -> Ps (bf16, K-major [2][64 t][64 s]) over the K/Kp tiles
+    const int sp = warp & 3, half = warp >> 2;
+    const int t = 16 * sp + (lane & 15);
+    const float* coef = half ? s_b : s_g;
+    const float ct = s_c[t];
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      float v[32];
+      umma::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + half * 64 + cc * 32, v);
+      if (lane < 16) {
+#pragma unroll
+        for (int qd = 0; qd < 4; ++qd) {
+          uint32_t w4[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i0 = qd * 8 + 2 * e, s0 = cc * 32 + i0;
+            const float v0 = (s0 <= t) ? v[i0] * coef[s0] * expf(ct - s_c[s0]) : 0.f;
+            const float v1 = (s0 + 1 <= t) ? v[i0 + 1] * coef[s0 + 1] * expf(ct - s_c[s0 + 1]) : 0.f;
+            w4[e] = pack_bf16(v0, v1);
+          }
+          *reinterpret_cast<uint4*>(sPs + half * 8192 + umma::sw128_offset(t, cc * 4 + qd)) =
+              make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+      }
+    }
+    umma::fence_proxy_async_smem();
+    umma::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+      umma::fence_after_sync();
+      const uint32_t ps0 = umma::smem_u32(sPs), x0 = umma::smem_u32(sX), xp0 = umma::smem_u32(sXp);
+      constexpr uint32_t id2 = umma::idesc_bf16(64, 64, false, true);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t part = ks >> 2, kin = ks & 3;
+        umma::mma_bf16(tmem + 128, umma::desc_sw128(ps0 + part * 8192 + kin * 32, 16, 1024),
+                       umma::desc_sw128((part ? xp0 : x0) + kin * 2048, 8192, 1024), id2, ks > 0);
+      }
+      umma::mma_commit(&bars[2]);
+      misc[2] = (j == 0) ? kFlagReady : wait_flag(&flags[j], p.status);
+    }
+    __syncthreads();
+    ok = misc[2] == kFlagReady;
+    if (!ok) umma::mbar_wait(&bars[2], 0, p.status);  // let MMA2 finish before TMEM is freed
+  }
+  if (ok) {
+    // state hand-off: S_in[j+1] = e^{c_L} S_in[j] + S_loc (mamba3.py:52)
+    const int sp = warp & 3, ph = warp >> 2;
+    const bool rows128 = (NS == 128);
+    const int n = rows128 ? 32 * sp + lane : 16 * sp + (lane & 15);
+    const bool active = rows128 || lane < 16;
+    float sl[32];
+    umma::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + 192 + 32 * ph, sl);
+    if (active) {
+      const float* src = nullptr;
+      if (j == 0) src = p.init ? p.init + bh * (int64_t)kP * NS : nullptr;
+      else src = p.ring + (bh * 2 + (j & 1)) * (int64_t)kP * NS;
+      float* dst = p.ring + (bh * 2 + ((j + 1) & 1)) * (int64_t)kP * NS;
+      float* fin = (j == p.nc - 1 && p.fin) ? p.fin + bh * (int64_t)kP * NS : nullptr;
+      float sin[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) sin[i] = src ? __ldcg(src + (32 * ph + i) * NS + n) : 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float o = a_chunk * sin[i] + sl[i];
+        dst[(32 * ph + i) * NS + n] = o;
+        if (fin) fin[(32 * ph + i) * NS + n] = o;
+      }
+      // S_in[j] in bf16: B operand of MMA4 ([n][p], p contiguous) and the saved state
+      uint4 pk[4];
+#pragma unroll
+      for (int qd = 0; qd < 4; ++qd)
+        pk[qd] = make_uint4(pack_bf16(sin[qd * 8 + 0], sin[qd * 8 + 1]), pack_bf16(sin[qd * 8 + 2], sin[qd * 8 + 3]),
+                            pack_bf16(sin[qd * 8 + 4], sin[qd * 8 + 5]), pack_bf16(sin[qd * 8 + 6], sin[qd * 8 + 7]));
+#pragma unroll
+      for (int qd = 0; qd < 4; ++qd) *reinterpret_cast<uint4*>(sSin + umma::sw128_offset(n, 4 * ph + qd)) = pk[qd];
+      if (p.states) {
+        uint4* gs = reinterpret_cast<uint4*>(p.states + ((bh * p.nc + j) * (int64_t)NS + n) * kP + 32 * ph);
+#pragma unroll
+        for (int qd = 0; qd < 4; ++qd) gs[qd] = pk[qd];
+      }
+    }
+    __threadfence();
+    umma::fence_proxy_async_smem();
+    umma::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+      st_release(&flags[j + 1], kFlagReady);
+      umma::fence_after_sync();
+      const uint32_t q0 = umma::smem_u32(sQ), sin0 = umma::smem_u32(sSin);
+      constexpr uint32_t id4 = umma::idesc_bf16(64, 64, false, true);
+#pragma unroll
+      for (int ks = 0; ks < NS / 16; ++ks) {
+        const uint32_t qb = ks >> 2, kin = ks & 3;
+        umma::mma_bf16(tmem + 128 + (16u << 16), umma::desc_sw128(q0 + qb * 8192 + kin * 32, 16, 1024),
+                       umma::desc_sw128(sin0 + ks * 2048, 8192, 1024), id4, ks > 0);
+      }
+      umma::mma_commit(&bars[3]);
+    }
+    ok = __syncthreads_and(umma::mbar_wait(&bars[3], 0, p.status));
+  } else if (tid == 0) {
+    st_release(&flags[j + 1], kFlagAbort);
+  }
+  if (ok) {
+    umma::fence_after_sync();
+    // y = Yi + e^{c_t} Ye  (mamba3.py:55)
+    const int sp = warp & 3, ph = warp >> 2;
+    const int t = 16 * sp + (lane & 15);
+    float v[32];
+    umma::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + 128 + 32 * ph, v);
+    const float ect = s_ec[t];
+    uint32_t w[16];
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+      const float o0 = __shfl_xor_sync(0xffffffffu, v[i], 16);
+      const float o1 = __shfl_xor_sync(0xffffffffu, v[i + 1], 16);
+      w[i / 2] = pack_bf16(v[i] + ect * o0, v[i + 1] + ect * o1);
+    }
+    if (lane < 16) {
+      uint4* dst = reinterpret_cast<uint4*>(p.y + b * p.ysb + (int64_t)(t0 + t) * p.yst + h * p.ysh + 32 * ph);
+#pragma unroll
+      for (int qd = 0; qd < 4; ++qd) dst[qd] = make_uint4(w[4 * qd], w[4 * qd + 1], w[4 * qd + 2], w[4 * qd + 3]);
+    }
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tmem, 256);
+}
+
+// ---------------------------------------------------------------------------------------------
+// host side
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 4-D map over a [B, T, H(or G), D] bf16 view: dims (D, H, T, B), box (64, 1, 64, 1), 128-byte swizzle
+bool make_map(CUtensorMap* map, const zb_view& v, int64_t B, int64_t T, int64_t H, int64_t D) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)v.sh * 2, (cuuint64_t)v.st * 2, (cuuint64_t)v.sb * 2};
+  const cuuint32_t box[4] = {64, 1, 64, 1};
+  const cuuint32_t es[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, v.ptr, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+// TMA needs a 16-byte aligned base and positive strides that are multiples of 16 bytes.
+bool view_tma_ok(const zb_view& v) {
+  const auto a16 = [](int64_t x) { return x > 0 && (x * 2) % 16 == 0 && x * 2 < (1ll << 40); };
+  return v.ptr && reinterpret_cast<uintptr_t>(v.ptr) % 16 == 0 && a16(v.sh) && a16(v.st) && a16(v.sb);
+}
+
+template <int NS>
+int launch_fwd(const zb_ssd_args* a, ChainSync sync, void* states, void* ring, cudaStream_t stream) {
+  TcFwdParams p;
+  memset(&p, 0, sizeof(p));
+  if (!make_map(&p.tq, a->q, a->B, a->T, a->G, NS) || !make_map(&p.tk, a->k, a->B, a->T, a->G, NS) ||
+      !make_map(&p.tkp, a->kp, a->B, a->T, a->G, NS) || !make_map(&p.tx, a->x, a->B, a->T, a->H, kP) ||
+      !make_map(&p.txp, a->xp, a->B, a->T, a->H, kP))
+    return ZB_ERR_LAYOUT;
+  p.B = a->B; p.T = a->T; p.H = a->H; p.G = a->G;
+  p.nc = (int)(a->T / kL);
+  p.adt = static_cast<const float*>(a->adt.ptr);
+  p.gamma = static_cast<const float*>(a->gamma.ptr);
+  p.beta = static_cast<const float*>(a->beta.ptr);
+  p.asb = a->adt.sb; p.ast = a->adt.st; p.ash = a->adt.sh;
+  p.gsb = a->gamma.sb; p.gst = a->gamma.st; p.gsh = a->gamma.sh;
+  p.bsb = a->beta.sb; p.bst = a->beta.st; p.bsh = a->beta.sh;
+  p.y = static_cast<__nv_bfloat16*>(a->y.ptr);
+  p.ysb = a->y.sb; p.yst = a->y.st; p.ysh = a->y.sh;
+  p.init = static_cast<const float*>(a->initial_state);
+  p.fin = static_cast<float*>(a->final_state);
+  p.states = static_cast<__nv_bfloat16*>(states);
+  p.ring = static_cast<float*>(ring);
+  p.ticket = sync.ticket;
+  p.flags = sync.flags;
+  p.status = a->status;
+  auto k = ssd_fwd_tc_kernel<NS>;
+  const int smem = (int)FwdSmem<NS>::ALLOC;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return ZB_ERR_CUDA;
+  const dim3 grid((unsigned)(a->B * a->H * p.nc));
+  k<<<grid, kTcThreads, smem, stream>>>(p);
+  note_launches(1);
+  return cudaPeekAtLastError() == cudaSuccess ? ZB_OK : ZB_ERR_CUDA;
+}
+
+}  // namespace
+
+bool tc_supported(const zb_ssd_args* a) {
+  if (a->dtype != ZB_BF16 || a->scalar_dtype != ZB_F32) return false;
+  if (a->flags & ZB_FLAG_STATE_ONLY) return false;
+  if (a->P != kP || (a->N != 64 && a->N != 128)) return false;
+  if (a->T % kL != 0) return false;
+  if (a->T / kL >= (1 << 30) || a->B * a->H * (a->T / kL) >= (1ll << 31)) return false;
+  const zb_view* v[] = {&a->x, &a->q, &a->k, &a->kp, &a->xp};
+  for (auto x : v)
+    if (!view_tma_ok(*x)) return false;
+  if (a->y.ptr && (reinterpret_cast<uintptr_t>(a->y.ptr) % 16 || (a->y.sh * 2) % 16 || (a->y.st * 2) % 16 ||
+                   (a->y.sb * 2) % 16))
+    return false;
+  return encode_fn() != nullptr;
+}
+
+bool tc_has_backward(const zb_ssd_args*) { return false; }
+
+int tc_chunk() { return kL; }
+
+size_t tc_states_bytes(const zb_ssd_args* a) {
+  return align_up((size_t)a->B * a->H * (a->T / kL) * a->N * kP * 2, 256);
+}
+
+size_t tc_workspace_bytes(const zb_ssd_args* a, bool backward) {
+  if (!backward) return align_up((size_t)a->B * a->H * 2 * kP * a->N * sizeof(float), 256);
+  return 0;
+}
+
+int tc_fwd(const zb_ssd_args* a, ChainSync sync, void* states, void* ws, cudaStream_t stream) {
+  if (a->N == 128) return launch_fwd<128>(a, sync, states, ws, stream);
+  if (a->N == 64) return launch_fwd<64>(a, sync, states, ws, stream);
+  return ZB_ERR_UNSUPPORTED;
+}
+
 int tc_bwd(const zb_ssd_args*, ChainSync, void*, cudaStream_t) { return ZB_ERR_UNSUPPORTED; }
 
 }  // namespace zb

@@ -7,6 +7,8 @@ namespace zb {
 
 // True when the tcgen05 kernels handle these arguments (bf16 vectors, P and N they are built for).
 bool tc_supported(const zb_ssd_args* a);
+// True when the tensor-core backward exists for these arguments (else saved states use the SIMT layout).
+bool tc_has_backward(const zb_ssd_args* a);
 // Internal chunk length of the tensor-core path.
 int tc_chunk();
 size_t tc_states_bytes(const zb_ssd_args* a);

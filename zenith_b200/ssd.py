@@ -53,6 +53,14 @@ def _stream(dev: torch.device) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
 
 
+def kernel_family(x, q, k, kp, xp, adt, gamma, beta, chunk_size, *, states_saved=True) -> str:
+    """'tensor-core' or 'simt': which kernels the library runs for these (prepared) inputs."""
+    a = _build_args(x, q, k, kp, xp, adt, gamma, beta, chunk_size)
+    a.y = L.view(x)  # an output with the input's layout (only its alignment matters here)
+    fam = L.lib().zb_ssd_kernel_family(ctypes.byref(a), 1 if states_saved else 0)
+    return {1: "tensor-core", 0: "simt"}.get(fam, "invalid")
+
+
 def states_nbytes(x, q, k, kp, xp, adt, gamma, beta, chunk_size) -> int:
     a = _build_args(x, q, k, kp, xp, adt, gamma, beta, chunk_size)
     return int(L.lib().zb_ssd_states_bytes(ctypes.byref(a)))
