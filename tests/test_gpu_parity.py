@@ -84,6 +84,9 @@ def test_bf16_tiny_config_matches_oracle_on_rounded_inputs(sdtype):
 def test_model_shapes_match_oracle(dtype, shape):
     inp = make_inputs(shape, seed=3)
     inp = _cast(inp, dtype, torch.float32)
+    fam = kernel_family(*zenith_b200.prepare_inputs(*(inp[n].cuda() for n in NAMES)), shape.chunk)
+    # bf16 with one q/k group per head runs the tcgen05 forward and backward; the rest SIMT
+    assert fam == ("tensor-core" if dtype == torch.bfloat16 and shape.G == shape.H else "simt")
     compare(run_cuda(inp, shape.chunk), oracle(inp, shape.chunk), TOL[dtype])
 
 

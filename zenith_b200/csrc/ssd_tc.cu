@@ -272,9 +272,10 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
 #pragma unroll
       for (int qd = 0; qd < 4; ++qd) *reinterpret_cast<uint4*>(sSin + umma::sw128_offset(n, 4 * ph + qd)) = pk[qd];
       if (p.states) {
-        uint4* gs = reinterpret_cast<uint4*>(p.states + ((bh * p.nc + j) * (int64_t)NS + n) * kP + 32 * ph);
+        // saved in the shared-memory image (128-byte swizzle) so the backward can bulk-copy it
+        unsigned char* gs = reinterpret_cast<unsigned char*>(p.states) + (bh * p.nc + j) * (int64_t)NS * 128;
 #pragma unroll
-        for (int qd = 0; qd < 4; ++qd) gs[qd] = pk[qd];
+        for (int qd = 0; qd < 4; ++qd) *reinterpret_cast<uint4*>(gs + umma::sw128_offset(n, 4 * ph + qd)) = pk[qd];
       }
     }
     __threadfence();
@@ -322,6 +323,507 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
   umma::fence_before_sync();
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tmem, 256);
+}
+
+// ---------------------------------------------------------------------------------------------
+// backward
+//
+// One CTA per (batch, head, chunk), chunks taken in reverse order, 256 threads, 512 TMEM columns.
+//   MMA b  S      = Q [K;Kp]^T          M=64  N=128 K=N   -> R0 lanes +0
+//   MMA a  dA     = dY [X;Xp]^T         M=64  N=128 K=64  -> R0 lanes +16
+//   MMA g  dSl'   = Q^T dYe             M=N   N=64  K=64  -> R4     (dYe = e^{c_t} dY)
+//   MMA h  Ye     = Q S_in^T            M=64  N=64  K=N   -> R1 lanes +16
+//   MMA d  dQ     = dYe S_in            M=64  N=N   K=64  -> R1 lanes +0
+//   epilogue: A=S g M, Ap, E=dA M, Eg=E g, ... -> [A|Ap], [Eg|Epb] (bf16) and dc/dgamma/dbeta sums
+//   MMA c  dXc    = [A|Ap]^T dY         M=128 N=64  K=64  -> R2
+//   MMA d  dQ    += [Eg|Epb] [K;Kp]     M=64  N=N   K=128 -> R1 lanes +0
+//   MMA e  dK     = [Eg|Epb]^T Q        M=128 N=N   K=64  -> R0
+//   chain: wait for Gn = G[j+1]; G[j] = dSl'^T + e^{c_L} Gn -> ring; publish
+//   MMA e  dK    += [wgX;wbXp] Gn       M=128 N=N   K=64  -> R0
+//   MMA f  U      = [K;Kp] Gn^T         M=128 N=64  K=N   -> R3
+//   epilogue: dx = dXc + w g U, dk, dq, per-token scalars, reverse cumsum -> dadt
+// TMEM: R0 [0,128) R1 [128,256) R2 [256,320) R3 [320,384) R4 [384,448).
+
+template <int NS>
+struct BwdSmem {
+  static constexpr int QB = NS / 64;
+  static constexpr uint32_t Q = 0;                  // [QB][64 t][64 n]
+  static constexpr uint32_t KK = Q + QB * 8192;     // [QB][K | Kp]
+  static constexpr uint32_t XX = KK + QB * 16384;   // [X | Xp]  (128 rows)
+  static constexpr uint32_t DY = XX + 16384;
+  static constexpr uint32_t SIN = DY + 8192;        // [NS n][64 p]
+  static constexpr uint32_t PS = SIN + NS * 128;    // [A | Ap]   [2][64 t][64 s]
+  static constexpr uint32_t EG = PS + 16384;        // [Eg | Epb] [2][64 t][64 s]
+  static constexpr uint32_t DYE = EG + 16384;
+  static constexpr uint32_t XW = DYE + 8192;        // [wgX | wbXp] (128 rows)
+  static constexpr uint32_t GN = XW + 16384;        // [NS n][64 p]
+  static constexpr uint32_t SCAL = GN + NS * 128;   // c ec w wg wb g b (64 floats each)
+  static constexpr uint32_t RED = SCAL + 7 * 256;
+  // RED: rowZ[2][64] | colZ[4][128] | colE[4][128] | xu[2][128] | dcint[64] | da[8] | tmp[8]
+  static constexpr uint32_t RED_FLOATS = 128 + 512 + 512 + 256 + 64 + 8 + 8;
+  static constexpr uint32_t BAR = RED + RED_FLOATS * 4;
+  static constexpr uint32_t MISC = BAR + 4 * 8;
+  static constexpr uint32_t TOTAL = MISC + 16;
+  static constexpr uint32_t ALLOC = TOTAL + 1024;
+};
+
+struct TcBwdParams {
+  CUtensorMap tq, tk, tkp, tx, txp, tdy;
+  int64_t B, T, H, G;
+  int nc;
+  const float* adt;
+  const float* gamma;
+  const float* beta;
+  int64_t asb, ast, ash, gsb, gst, gsh, bsb, bst, bsh;
+  const __nv_bfloat16* states;  // [B*H][nc] images of S_in (swizzled [N][P] bf16)
+  const float* dfin;
+  float* dinit;
+  float* ring;                  // [B*H][2][P][N]
+  __nv_bfloat16 *dx, *dxp, *dq, *dk, *dkp;
+  int64_t dxsb, dxst, dxsh, dxpsb, dxpst, dxpsh, dqsb, dqst, dqsh, dksb, dkst, dksh, dkpsb, dkpst, dkpsh;
+  float *dadt, *dgamma, *dbeta;
+  int64_t dasb, dast, dash, dgsb, dgst, dgsh, dbsb, dbst, dbsh;
+  unsigned int* ticket;
+  int* flags;
+  int32_t* status;
+};
+
+// scale each 128-byte row r of a bf16 tile by f[r] (rows = bytes / 128), src -> dst
+__device__ __forceinline__ void scale_rows(const unsigned char* src, unsigned char* dst, uint32_t bytes, const float* f,
+                                           int tid) {
+  for (uint32_t off = (uint32_t)tid * 16u; off < bytes; off += kTcThreads * 16u) {
+    const float s = f[off >> 7];
+    const uint4 v = *reinterpret_cast<const uint4*>(src + off);
+    uint4 o;
+    float2 e;
+    e = unpack_bf16(v.x); o.x = pack_bf16(e.x * s, e.y * s);
+    e = unpack_bf16(v.y); o.y = pack_bf16(e.x * s, e.y * s);
+    e = unpack_bf16(v.z); o.z = pack_bf16(e.x * s, e.y * s);
+    e = unpack_bf16(v.w); o.w = pack_bf16(e.x * s, e.y * s);
+    *reinterpret_cast<uint4*>(dst + off) = o;
+  }
+}
+
+// 8 consecutive bf16 of row r (16-byte chunk c) of a swizzled tile, as floats
+__device__ __forceinline__ void load_chunk(const unsigned char* tile, int r, int c, float (&o)[8]) {
+  const uint4 v = *reinterpret_cast<const uint4*>(tile + umma::sw128_offset(r, c));
+  float2 e;
+  e = unpack_bf16(v.x); o[0] = e.x; o[1] = e.y;
+  e = unpack_bf16(v.y); o[2] = e.x; o[3] = e.y;
+  e = unpack_bf16(v.z); o[4] = e.x; o[5] = e.y;
+  e = unpack_bf16(v.w); o[6] = e.x; o[7] = e.y;
+}
+
+__device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float* v) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int qd = 0; qd < 4; ++qd)
+    d[qd] = make_uint4(pack_bf16(v[8 * qd], v[8 * qd + 1]), pack_bf16(v[8 * qd + 2], v[8 * qd + 3]),
+                       pack_bf16(v[8 * qd + 4], v[8 * qd + 5]), pack_bf16(v[8 * qd + 6], v[8 * qd + 7]));
+}
+
+template <int NS>
+__global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_constant__ TcBwdParams p) {
+  using S = BwdSmem<NS>;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sQ = sm + S::Q;
+  unsigned char* sKK = sm + S::KK;
+  unsigned char* sXX = sm + S::XX;
+  unsigned char* sDY = sm + S::DY;
+  unsigned char* sSin = sm + S::SIN;
+  unsigned char* sPS = sm + S::PS;
+  unsigned char* sEG = sm + S::EG;
+  unsigned char* sDYE = sm + S::DYE;
+  unsigned char* sXW = sm + S::XW;
+  unsigned char* sGN = sm + S::GN;
+  float* s_c = reinterpret_cast<float*>(sm + S::SCAL);
+  float* s_ec = s_c + 64;
+  float* s_w = s_c + 128;
+  float* s_wgb = s_c + 192;  // [wg (64) | wb (64)]
+  float* s_g = s_c + 320;
+  float* s_b = s_c + 384;
+  float* s_rowZ = reinterpret_cast<float*>(sm + S::RED);  // [2][64]
+  float* s_colZ = s_rowZ + 128;                           // [4][128]
+  float* s_colE = s_colZ + 512;                           // [4][128]
+  float* s_xu = s_colE + 512;                             // [2][128]
+  float* s_dcint = s_xu + 256;                            // [64]
+  float* s_da = s_dcint + 64;                             // [8]
+  float* s_tmp = s_da + 8;                                // [8]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::BAR);
+  uint32_t* misc = reinterpret_cast<uint32_t*>(sm + S::MISC);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    misc[1] = atomicAdd(p.ticket, 1u);
+    for (int i = 0; i < 4; ++i) umma::mbar_init(&bars[i], 1);
+    umma::mbar_fence_init();
+  }
+  if (warp == 0) {
+    umma::tmem_alloc(&misc[0], 512);
+    umma::tmem_relinquish();
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = misc[0];
+  const uint32_t R0 = tmem, R1 = tmem + 128, R2 = tmem + 256, R3 = tmem + 320, R4 = tmem + 384;
+  const int64_t BH = p.B * p.H;
+  const int64_t tk = misc[1];
+  const int j = p.nc - 1 - (int)(tk / BH);
+  const int64_t bh = tk % BH;
+  const int b = (int)(bh / p.H), h = (int)(bh % p.H);
+  const int g = (int)(h / (p.H / p.G));
+  const int t0 = j * kL;
+  int* flags = p.flags + bh * (p.nc + 1);
+
+  constexpr uint32_t kLoadBytes = S::QB * 8192 * 3 + 3 * 8192 + NS * 128;
+  if (tid == 0) {
+    umma::mbar_arrive_expect_tx(&bars[0], kLoadBytes);
+#pragma unroll
+    for (int qb = 0; qb < S::QB; ++qb) {
+      umma::tma_load_4d(sQ + qb * 8192, &p.tq, &bars[0], qb * 64, g, t0, b);
+      umma::tma_load_4d(sKK + qb * 16384, &p.tk, &bars[0], qb * 64, g, t0, b);
+      umma::tma_load_4d(sKK + qb * 16384 + 8192, &p.tkp, &bars[0], qb * 64, g, t0, b);
+    }
+    umma::tma_load_4d(sXX, &p.tx, &bars[0], 0, h, t0, b);
+    umma::tma_load_4d(sXX + 8192, &p.txp, &bars[0], 0, h, t0, b);
+    umma::tma_load_4d(sDY, &p.tdy, &bars[0], 0, h, t0, b);
+    umma::bulk_load(sSin, reinterpret_cast<const unsigned char*>(p.states) + (bh * p.nc + j) * (int64_t)NS * 128,
+                    NS * 128, &bars[0]);
+  }
+  if (tid < 64) {
+    const int t = t0 + tid;
+    const float a = p.adt[b * p.asb + t * p.ast + h * p.ash];
+    s_g[tid] = p.gamma[b * p.gsb + t * p.gst + h * p.gsh];
+    s_b[tid] = p.beta[b * p.bsb + t * p.bst + h * p.bsh];
+    s_c[tid] = warp_incl_scan(a, lane);
+  }
+  for (int i = tid; i < S::RED_FLOATS; i += kTcThreads) s_rowZ[i] = 0.f;
+  __syncthreads();
+  if (tid >= 32 && tid < 64) s_c[tid] += s_c[31];
+  __syncthreads();
+  if (tid < 64) {
+    const float c = s_c[tid], w = expf(s_c[63] - c);
+    s_ec[tid] = expf(c);
+    s_w[tid] = w;
+    s_wgb[tid] = w * s_g[tid];
+    s_wgb[64 + tid] = w * s_b[tid];
+  }
+  const bool load_ok = umma::mbar_wait(&bars[0], 0, p.status);
+  __syncthreads();
+  const float a_chunk = expf(s_c[63]);
+  bool ok = __syncthreads_and(load_ok);
+
+  if (ok) {
+    scale_rows(sXX, sXW, 16384, s_wgb, tid);  // [wgX | wbXp]
+    scale_rows(sDY, sDYE, 8192, s_ec, tid);   // e^{c_t} dY
+    umma::fence_proxy_async_smem();
+    umma::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+      umma::fence_after_sync();
+      const uint32_t q0 = umma::smem_u32(sQ), kk0 = umma::smem_u32(sKK), xx0 = umma::smem_u32(sXX);
+      const uint32_t dy0 = umma::smem_u32(sDY), dye0 = umma::smem_u32(sDYE), sin0 = umma::smem_u32(sSin);
+      // b: S = Q [K;Kp]^T
+      constexpr uint32_t idb = umma::idesc_bf16(64, 128, false, false);
+#pragma unroll
+      for (int ks = 0; ks < NS / 16; ++ks) {
+        const uint32_t qb = ks >> 2, kin = ks & 3;
+        umma::mma_bf16(R0, umma::desc_sw128(q0 + qb * 8192 + kin * 32, 16, 1024),
+                       umma::desc_sw128(kk0 + qb * 16384 + kin * 32, 16, 1024), idb, ks > 0);
+      }
+      // a: dA = dY [X;Xp]^T
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma::mma_bf16(R0 + (16u << 16), umma::desc_sw128(dy0 + ks * 32, 16, 1024),
+                       umma::desc_sw128(xx0 + ks * 32, 16, 1024), idb, ks > 0);
+      // g: dSl' = Q^T dYe   (M = n)
+      constexpr uint32_t idg = umma::idesc_bf16(NS, 64, true, true);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma::mma_bf16(R4, umma::desc_sw128(q0 + ks * 2048, 8192, 1024), umma::desc_sw128(dye0 + ks * 2048, 8192, 1024),
+                       idg, ks > 0);
+      // h: Ye = Q S_in^T
+      constexpr uint32_t idh = umma::idesc_bf16(64, 64, false, true);
+#pragma unroll
+      for (int ks = 0; ks < NS / 16; ++ks) {
+        const uint32_t qb = ks >> 2, kin = ks & 3;
+        umma::mma_bf16(R1 + (16u << 16), umma::desc_sw128(q0 + qb * 8192 + kin * 32, 16, 1024),
+                       umma::desc_sw128(sin0 + ks * 2048, 8192, 1024), idh, ks > 0);
+      }
+      // d (inter part): dQ = dYe S_in
+      constexpr uint32_t idd1 = umma::idesc_bf16(64, NS, false, false);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma::mma_bf16(R1, umma::desc_sw128(dye0 + ks * 32, 16, 1024), umma::desc_sw128(sin0 + ks * 32, 16, 1024), idd1,
+                       ks > 0);
+      umma::mma_commit(&bars[1]);
+    }
+    ok = __syncthreads_and(umma::mbar_wait(&bars[1], 0, p.status));
+  }
+  if (ok) {
+    umma::fence_after_sync();
+    // score-gradient epilogue.  Warp w: sub-partition sp = w % 4 (rows t = 16 sp + lane % 16),
+    // half = w / 4 (0: K part with gamma, 1: Kp part with beta).  Lanes 0-15 hold S, 16-31 hold dA.
+    const int sp = warp & 3, half = warp >> 2;
+    const int t = 16 * sp + (lane & 15);
+    const float* coef = half ? s_b : s_g;
+    const float ct = s_c[t];
+    float rowZ = 0.f;
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      float v[32];
+      umma::tmem_ld32(R0 + ((uint32_t)(32 * sp) << 16) + half * 64 + cc * 32, v);
+      uint32_t wa[16], we[16];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float other = __shfl_xor_sync(0xffffffffu, v[i], 16);
+        const float sv = (lane < 16) ? v[i] : 0.f;   // S_ts
+        const float dav = (lane < 16) ? other : 0.f; // dA_ts
+        const int s = cc * 32 + i;
+        const float m = (s <= t && lane < 16) ? expf(ct - s_c[s]) : 0.f;
+        const float A = sv * coef[s] * m;
+        const float E = dav * m;
+        const float z = dav * A;
+        const float es = E * sv;
+        rowZ += z;
+        // column sums over the 16 rows of this warp
+        float cz = z, ce = es;
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) {
+          cz += __shfl_xor_sync(0xffffffffu, cz, o);
+          ce += __shfl_xor_sync(0xffffffffu, ce, o);
+        }
+        if (lane == 0) {
+          s_colZ[sp * 128 + half * 64 + s] = cz;
+          s_colE[sp * 128 + half * 64 + s] = ce;
+        }
+        // pack A and E*coef in pairs of bf16
+        if ((i & 1) == 0) {
+          wa[i >> 1] = __float_as_uint(A);
+          we[i >> 1] = __float_as_uint(E * coef[s]);
+        } else {
+          wa[i >> 1] = pack_bf16(__uint_as_float(wa[i >> 1]), A);
+          we[i >> 1] = pack_bf16(__uint_as_float(we[i >> 1]), E * coef[s]);
+        }
+      }
+      if (lane < 16) {
+#pragma unroll
+        for (int qd = 0; qd < 4; ++qd) {
+          *reinterpret_cast<uint4*>(sPS + half * 8192 + umma::sw128_offset(t, cc * 4 + qd)) =
+              make_uint4(wa[4 * qd], wa[4 * qd + 1], wa[4 * qd + 2], wa[4 * qd + 3]);
+          *reinterpret_cast<uint4*>(sEG + half * 8192 + umma::sw128_offset(t, cc * 4 + qd)) =
+              make_uint4(we[4 * qd], we[4 * qd + 1], we[4 * qd + 2], we[4 * qd + 3]);
+        }
+      }
+    }
+    if (lane < 16) s_rowZ[half * 64 + t] = rowZ;
+    umma::fence_proxy_async_smem();
+    umma::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+      umma::fence_after_sync();
+      const uint32_t q0 = umma::smem_u32(sQ), kk0 = umma::smem_u32(sKK), dy0 = umma::smem_u32(sDY);
+      const uint32_t ps0 = umma::smem_u32(sPS), eg0 = umma::smem_u32(sEG);
+      // c: dXc = [A|Ap]^T dY   (M = s|s')
+      constexpr uint32_t idc = umma::idesc_bf16(128, 64, true, true);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma::mma_bf16(R2, umma::desc_sw128(ps0 + ks * 2048, 8192, 1024), umma::desc_sw128(dy0 + ks * 2048, 8192, 1024),
+                       idc, ks > 0);
+      // d (intra part): dQ += [Eg|Epb] [K;Kp]
+      constexpr uint32_t idd2 = umma::idesc_bf16(64, NS, false, true);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t part = ks >> 2, kin = ks & 3;
+        umma::mma_bf16(R1, umma::desc_sw128(eg0 + part * 8192 + kin * 32, 16, 1024),
+                       umma::desc_sw128(kk0 + part * 8192 + kin * 2048, 16384, 1024), idd2, 1);
+      }
+      // e: dK = [Eg|Epb]^T Q   (M = s|s')
+      constexpr uint32_t ide = umma::idesc_bf16(128, NS, true, true);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma::mma_bf16(R0, umma::desc_sw128(eg0 + ks * 2048, 8192, 1024), umma::desc_sw128(q0 + ks * 2048, 8192, 1024),
+                       ide, ks > 0);
+      umma::mma_commit(&bars[2]);
+      misc[2] = (j == p.nc - 1) ? kFlagReady : wait_flag(&flags[j + 1], p.status);
+    }
+    __syncthreads();
+    ok = misc[2] == kFlagReady;
+    if (!ok) umma::mbar_wait(&bars[2], 0, p.status);
+  }
+  if (ok) {
+    // reverse state hand-off: G[j] = dSl'^T + e^{c_L} G[j+1];  da = <G[j+1], S_in[j]>
+    const int sp = warp & 3, ph = warp >> 2;
+    const bool rows128 = (NS == 128);
+    const int n = rows128 ? 32 * sp + lane : 16 * sp + (lane & 15);
+    const bool active = rows128 || lane < 16;
+    float ds[32];
+    umma::tmem_ld32(R4 + ((uint32_t)(32 * sp) << 16) + 32 * ph, ds);
+    float da_part = 0.f;
+    if (active) {
+      const float* src = (j == p.nc - 1) ? (p.dfin ? p.dfin + bh * (int64_t)kP * NS : nullptr)
+                                         : p.ring + (bh * 2 + ((j + 1) & 1)) * (int64_t)kP * NS;
+      float* dst = p.ring + (bh * 2 + (j & 1)) * (int64_t)kP * NS;
+      float* dinit = (j == 0 && p.dinit) ? p.dinit + bh * (int64_t)kP * NS : nullptr;
+      float gn[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) gn[i] = src ? __ldcg(src + (32 * ph + i) * NS + n) : 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float o = ds[i] + a_chunk * gn[i];
+        dst[(32 * ph + i) * NS + n] = o;
+        if (dinit) dinit[(32 * ph + i) * NS + n] = o;
+      }
+#pragma unroll
+      for (int qd = 0; qd < 4; ++qd) {
+        float sv[8];
+        load_chunk(sSin, n, 4 * ph + qd, sv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) da_part += gn[8 * qd + e] * sv[e];
+        *reinterpret_cast<uint4*>(sGN + umma::sw128_offset(n, 4 * ph + qd)) =
+            make_uint4(pack_bf16(gn[8 * qd], gn[8 * qd + 1]), pack_bf16(gn[8 * qd + 2], gn[8 * qd + 3]),
+                       pack_bf16(gn[8 * qd + 4], gn[8 * qd + 5]), pack_bf16(gn[8 * qd + 6], gn[8 * qd + 7]));
+      }
+    }
+    da_part = warp_sum(da_part);
+    if (lane == 0) s_da[warp] = da_part;
+    __threadfence();
+    umma::fence_proxy_async_smem();
+    umma::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+      st_release(&flags[j], kFlagReady);
+      umma::fence_after_sync();
+      const uint32_t kk0 = umma::smem_u32(sKK), xw0 = umma::smem_u32(sXW), gn0 = umma::smem_u32(sGN);
+      // e (state part): dK += [wgX;wbXp] Gn
+      constexpr uint32_t ide2 = umma::idesc_bf16(128, NS, false, false);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma::mma_bf16(R0, umma::desc_sw128(xw0 + ks * 32, 16, 1024), umma::desc_sw128(gn0 + ks * 32, 16, 1024), ide2, 1);
+      // f: U = [K;Kp] Gn^T
+      constexpr uint32_t idf = umma::idesc_bf16(128, 64, false, true);
+#pragma unroll
+      for (int ks = 0; ks < NS / 16; ++ks) {
+        const uint32_t qb = ks >> 2, kin = ks & 3;
+        umma::mma_bf16(R3, umma::desc_sw128(kk0 + qb * 16384 + kin * 32, 16, 1024),
+                       umma::desc_sw128(gn0 + ks * 2048, 8192, 1024), idf, ks > 0);
+      }
+      umma::mma_commit(&bars[3]);
+    }
+    ok = __syncthreads_and(umma::mbar_wait(&bars[3], 0, p.status));
+  } else if (tid == 0) {
+    st_release(&flags[j], kFlagAbort);
+  }
+  if (ok) {
+    umma::fence_after_sync();
+    const int sp = warp & 3, ch = warp >> 2;
+    // (1) dQ rows (R1 lanes +0) and, for warps 0-3, Ye rows (R1 lanes +16) for the dc inter term
+    {
+      const int t = 16 * sp + (lane & 15);
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        float v[32];
+        umma::tmem_ld32(R1 + ((uint32_t)(32 * sp) << 16) + 64 * ch + 32 * cc, v);
+        if (lane < 16 && 64 * ch + 32 * cc < NS)
+          store_row32(p.dq + b * p.dqsb + (int64_t)(t0 + t) * p.dqst + g * p.dqsh + 64 * ch + 32 * cc, v);
+        if (lane >= 16 && ch == 0) {
+          float acc = 0.f;
+#pragma unroll
+          for (int qd = 0; qd < 4; ++qd) {
+            float dyv[8];
+            load_chunk(sDY, t, 4 * cc + qd, dyv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc += dyv[e] * v[8 * qd + e];
+          }
+          // cc = 0 writes, cc = 1 adds (same thread)
+          if (cc == 0) s_dcint[t] = acc;
+          else s_dcint[t] = s_ec[t] * (s_dcint[t] + acc);
+        }
+      }
+    }
+    // (2) dx / dxp rows: dXc (R2) + w g U (R3); x.U partial sums for dgamma / dbeta
+    {
+      const int r = 32 * sp + lane;  // 0-63: s of X, 64-127: s of Xp
+      const int s = r & 63;
+      float dxc[32], u[32];
+      umma::tmem_ld32(R2 + ((uint32_t)(32 * sp) << 16) + 32 * ch, dxc);
+      umma::tmem_ld32(R3 + ((uint32_t)(32 * sp) << 16) + 32 * ch, u);
+      const float wgt = s_wgb[r];  // wg for X rows, wb for Xp rows
+      float xu = 0.f;
+#pragma unroll
+      for (int qd = 0; qd < 4; ++qd) {
+        float xv[8];
+        load_chunk(sXX, r, 4 * ch + qd, xv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          xu += xv[e] * u[8 * qd + e];
+          dxc[8 * qd + e] += wgt * u[8 * qd + e];
+        }
+      }
+      s_xu[ch * 128 + r] = xu;
+      __nv_bfloat16* dst = (r < 64) ? p.dx + b * p.dxsb + (int64_t)(t0 + s) * p.dxst + h * p.dxsh
+                                    : p.dxp + b * p.dxpsb + (int64_t)(t0 + s) * p.dxpst + h * p.dxpsh;
+      store_row32(dst + 32 * ch, dxc);
+    }
+    // (3) dk / dkp rows (R0)
+    {
+      const int r = 32 * sp + lane;
+      const int s = r & 63;
+      __nv_bfloat16* dst = (r < 64) ? p.dk + b * p.dksb + (int64_t)(t0 + s) * p.dkst + g * p.dksh
+                                    : p.dkp + b * p.dkpsb + (int64_t)(t0 + s) * p.dkpst + g * p.dkpsh;
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        if (64 * ch + 32 * cc < NS) {
+          float v[32];
+          umma::tmem_ld32(R0 + ((uint32_t)(32 * sp) << 16) + 64 * ch + 32 * cc, v);
+          store_row32(dst + 64 * ch + 32 * cc, v);
+        }
+      }
+    }
+    __syncthreads();
+    // per-token scalars: warps 0-1 own tokens 0-63
+    if (tid < 64) {
+      const int s = tid;
+      float da = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) da += s_da[i];
+      const float xu = s_xu[s] + s_xu[128 + s];
+      const float xpu = s_xu[64 + s] + s_xu[192 + s];
+      float colZ = 0.f, colEg = 0.f, colEb = 0.f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        colZ += s_colZ[q * 128 + s] + s_colZ[q * 128 + 64 + s];
+        colEg += s_colE[q * 128 + s];
+        colEb += s_colE[q * 128 + 64 + s];
+      }
+      const float w = s_w[s];
+      const float dw = s_g[s] * xu + s_b[s] * xpu;
+      const float dg = colEg + w * xu;
+      const float db = colEb + w * xpu;
+      float dc = s_rowZ[s] + s_rowZ[64 + s] - colZ + s_dcint[s] - w * dw;
+      // dc_{L-1} += e^{c_L} da + sum_s w_s dw_s   (two warps: combine through shared memory)
+      const float wdw = warp_sum(w * dw);
+      if (lane == 0) s_tmp[warp] = wdw;
+      asm volatile("bar.sync 1, 64;" ::: "memory");
+      if (s == 63) dc += a_chunk * da + s_tmp[0] + s_tmp[1];
+      // dadt_u = sum_{t >= u} dc_t  (reverse cumulative sum over 64 tokens in two warps)
+      const float total = warp_sum(dc);
+      const float incl = warp_incl_scan(dc, lane);
+      float suffix = total - incl + dc;
+      if (lane == 0 && warp == 1) s_tmp[2] = total;
+      asm volatile("bar.sync 1, 64;" ::: "memory");
+      if (warp == 0) suffix += s_tmp[2];
+      const int tt = t0 + s;
+      p.dadt[b * p.dasb + (int64_t)tt * p.dast + h * p.dash] = suffix;
+      p.dgamma[b * p.dgsb + (int64_t)tt * p.dgst + h * p.dgsh] = dg;
+      p.dbeta[b * p.dbsb + (int64_t)tt * p.dbst + h * p.dbsh] = db;
+    }
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tmem, 512);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -397,6 +899,55 @@ int launch_fwd(const zb_ssd_args* a, ChainSync sync, void* states, void* ring, c
   return cudaPeekAtLastError() == cudaSuccess ? ZB_OK : ZB_ERR_CUDA;
 }
 
+bool row_out_ok(const zb_view& v) {
+  return v.ptr && reinterpret_cast<uintptr_t>(v.ptr) % 16 == 0 && (v.sh * 2) % 16 == 0 && (v.st * 2) % 16 == 0 &&
+         (v.sb * 2) % 16 == 0;
+}
+
+template <int NS>
+int launch_bwd(const zb_ssd_args* a, ChainSync sync, void* ring, cudaStream_t stream) {
+  TcBwdParams p;
+  memset(&p, 0, sizeof(p));
+  if (!view_tma_ok(a->dy)) return ZB_ERR_LAYOUT;
+  const zb_view* outs[] = {&a->dx, &a->dxp, &a->dq, &a->dk, &a->dkp};
+  for (auto v : outs)
+    if (!row_out_ok(*v)) return ZB_ERR_LAYOUT;
+  if (!make_map(&p.tq, a->q, a->B, a->T, a->G, NS) || !make_map(&p.tk, a->k, a->B, a->T, a->G, NS) ||
+      !make_map(&p.tkp, a->kp, a->B, a->T, a->G, NS) || !make_map(&p.tx, a->x, a->B, a->T, a->H, kP) ||
+      !make_map(&p.txp, a->xp, a->B, a->T, a->H, kP) || !make_map(&p.tdy, a->dy, a->B, a->T, a->H, kP))
+    return ZB_ERR_LAYOUT;
+  p.B = a->B; p.T = a->T; p.H = a->H; p.G = a->G;
+  p.nc = (int)(a->T / kL);
+  p.adt = static_cast<const float*>(a->adt.ptr);
+  p.gamma = static_cast<const float*>(a->gamma.ptr);
+  p.beta = static_cast<const float*>(a->beta.ptr);
+  p.asb = a->adt.sb; p.ast = a->adt.st; p.ash = a->adt.sh;
+  p.gsb = a->gamma.sb; p.gst = a->gamma.st; p.gsh = a->gamma.sh;
+  p.bsb = a->beta.sb; p.bst = a->beta.st; p.bsh = a->beta.sh;
+  p.states = static_cast<const __nv_bfloat16*>(a->states);
+  p.dfin = static_cast<const float*>(a->dfinal_state);
+  p.dinit = static_cast<float*>(a->dinitial_state);
+  p.ring = static_cast<float*>(ring);
+  p.dx = static_cast<__nv_bfloat16*>(a->dx.ptr); p.dxsb = a->dx.sb; p.dxst = a->dx.st; p.dxsh = a->dx.sh;
+  p.dxp = static_cast<__nv_bfloat16*>(a->dxp.ptr); p.dxpsb = a->dxp.sb; p.dxpst = a->dxp.st; p.dxpsh = a->dxp.sh;
+  p.dq = static_cast<__nv_bfloat16*>(a->dq.ptr); p.dqsb = a->dq.sb; p.dqst = a->dq.st; p.dqsh = a->dq.sh;
+  p.dk = static_cast<__nv_bfloat16*>(a->dk.ptr); p.dksb = a->dk.sb; p.dkst = a->dk.st; p.dksh = a->dk.sh;
+  p.dkp = static_cast<__nv_bfloat16*>(a->dkp.ptr); p.dkpsb = a->dkp.sb; p.dkpst = a->dkp.st; p.dkpsh = a->dkp.sh;
+  p.dadt = static_cast<float*>(a->dadt.ptr); p.dasb = a->dadt.sb; p.dast = a->dadt.st; p.dash = a->dadt.sh;
+  p.dgamma = static_cast<float*>(a->dgamma.ptr); p.dgsb = a->dgamma.sb; p.dgst = a->dgamma.st; p.dgsh = a->dgamma.sh;
+  p.dbeta = static_cast<float*>(a->dbeta.ptr); p.dbsb = a->dbeta.sb; p.dbst = a->dbeta.st; p.dbsh = a->dbeta.sh;
+  p.ticket = sync.ticket;
+  p.flags = sync.flags;
+  p.status = a->status;
+  auto k = ssd_bwd_tc_kernel<NS>;
+  const int smem = (int)BwdSmem<NS>::ALLOC;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return ZB_ERR_CUDA;
+  const dim3 grid((unsigned)(a->B * a->H * p.nc));
+  k<<<grid, kTcThreads, smem, stream>>>(p);
+  note_launches(1);
+  return cudaPeekAtLastError() == cudaSuccess ? ZB_OK : ZB_ERR_CUDA;
+}
+
 }  // namespace
 
 bool tc_supported(const zb_ssd_args* a) {
@@ -414,7 +965,9 @@ bool tc_supported(const zb_ssd_args* a) {
   return encode_fn() != nullptr;
 }
 
-bool tc_has_backward(const zb_ssd_args*) { return false; }
+// The tensor-core backward handles one q/k group per head (G == H, the reference's layout);
+// grouped q/k (G < H) differentiate on the SIMT path.
+bool tc_has_backward(const zb_ssd_args* a) { return a->G == a->H; }
 
 int tc_chunk() { return kL; }
 
@@ -422,9 +975,9 @@ size_t tc_states_bytes(const zb_ssd_args* a) {
   return align_up((size_t)a->B * a->H * (a->T / kL) * a->N * kP * 2, 256);
 }
 
-size_t tc_workspace_bytes(const zb_ssd_args* a, bool backward) {
-  if (!backward) return align_up((size_t)a->B * a->H * 2 * kP * a->N * sizeof(float), 256);
-  return 0;
+// forward and backward both need the two-slot fp32 hand-off ring per (batch, head)
+size_t tc_workspace_bytes(const zb_ssd_args* a, bool) {
+  return align_up((size_t)a->B * a->H * 2 * kP * a->N * sizeof(float), 256);
 }
 
 int tc_fwd(const zb_ssd_args* a, ChainSync sync, void* states, void* ws, cudaStream_t stream) {
@@ -433,6 +986,11 @@ int tc_fwd(const zb_ssd_args* a, ChainSync sync, void* states, void* ws, cudaStr
   return ZB_ERR_UNSUPPORTED;
 }
 
-int tc_bwd(const zb_ssd_args*, ChainSync, void*, cudaStream_t) { return ZB_ERR_UNSUPPORTED; }
+int tc_bwd(const zb_ssd_args* a, ChainSync sync, void* ws, cudaStream_t stream) {
+  if (a->G != a->H || (a->flags & ZB_FLAG_STATE_ONLY)) return ZB_ERR_UNSUPPORTED;
+  if (a->N == 128) return launch_bwd<128>(a, sync, ws, stream);
+  if (a->N == 64) return launch_bwd<64>(a, sync, ws, stream);
+  return ZB_ERR_UNSUPPORTED;
+}
 
 }  // namespace zb
