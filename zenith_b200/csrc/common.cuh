@@ -106,7 +106,7 @@ static __device__ __noinline__ int wait_flag(const int* flag, int32_t* status) {
       if (globaltimer() - t0 > kWaitTimeoutNs) break;
     }
     __nanosleep(sleep_ns);
-    if (sleep_ns < 1024) sleep_ns <<= 1;
+    if (sleep_ns < 256) sleep_ns <<= 1;
   }
   atomicCAS(status, 0, (int32_t)ZB_ERR_TIMEOUT);
   return kFlagAbort;

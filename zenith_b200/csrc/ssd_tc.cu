@@ -195,30 +195,32 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
   }
   if (ok) {
     umma::fence_after_sync();
-    // scores -> Ps (bf16, K-major [2][64 t][64 s]) over the K/Kp tiles
+    // scores -> Ps (bf16, K-major [2][64 t][64 s]) over the K/Kp tiles.  TMEM gives lanes 0-15
+    // the S row; lanes 16-31 take over columns 16-31 of each 32-column block by one shuffle each.
     const int sp = warp & 3, half = warp >> 2;
     const int t = 16 * sp + (lane & 15);
+    const bool hiL = lane >= 16;
     const float* coef = half ? s_b : s_g;
     const float ct = s_c[t];
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {
       float v[32];
       umma::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + half * 64 + cc * 32, v);
-      if (lane < 16) {
+      uint32_t w8[8];
 #pragma unroll
-        for (int qd = 0; qd < 4; ++qd) {
-          uint32_t w4[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i0 = qd * 8 + 2 * e, s0 = cc * 32 + i0;
-            const float v0 = (s0 <= t) ? v[i0] * coef[s0] * expf(ct - s_c[s0]) : 0.f;
-            const float v1 = (s0 + 1 <= t) ? v[i0 + 1] * coef[s0 + 1] * expf(ct - s_c[s0 + 1]) : 0.f;
-            w4[e] = pack_bf16(v0, v1);
-          }
-          *reinterpret_cast<uint4*>(sPs + half * 8192 + umma::sw128_offset(t, cc * 4 + qd)) =
-              make_uint4(w4[0], w4[1], w4[2], w4[3]);
-        }
+      for (int i = 0; i < 16; i += 2) {
+        const float r0 = __shfl_xor_sync(0xffffffffu, v[16 + i], 16);
+        const float r1 = __shfl_xor_sync(0xffffffffu, v[17 + i], 16);
+        const int s0 = cc * 32 + (hiL ? 16 : 0) + i;
+        const float a0 = hiL ? r0 : v[i], a1 = hiL ? r1 : v[i + 1];
+        const float v0 = (s0 <= t) ? a0 * coef[s0] * __expf(ct - s_c[s0]) : 0.f;
+        const float v1 = (s0 + 1 <= t) ? a1 * coef[s0 + 1] * __expf(ct - s_c[s0 + 1]) : 0.f;
+        w8[i >> 1] = pack_bf16(v0, v1);
       }
+      const int c0 = cc * 4 + (hiL ? 2 : 0);
+      *reinterpret_cast<uint4*>(sPs + half * 8192 + umma::sw128_offset(t, c0)) = make_uint4(w8[0], w8[1], w8[2], w8[3]);
+      *reinterpret_cast<uint4*>(sPs + half * 8192 + umma::sw128_offset(t, c0 + 1)) =
+          make_uint4(w8[4], w8[5], w8[6], w8[7]);
     }
     umma::fence_proxy_async_smem();
     umma::fence_before_sync();
@@ -246,23 +248,39 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
     const bool rows128 = (NS == 128);
     const int n = rows128 ? 32 * sp + lane : 16 * sp + (lane & 15);
     const bool active = rows128 || lane < 16;
-    float sl[32];
+    float sl[32], sin[32];
     umma::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + 192 + 32 * ph, sl);
     if (active) {
-      const float* src = nullptr;
-      if (j == 0) src = p.init ? p.init + bh * (int64_t)kP * NS : nullptr;
-      else src = p.ring + (bh * 2 + (j & 1)) * (int64_t)kP * NS;
-      float* dst = p.ring + (bh * 2 + ((j + 1) & 1)) * (int64_t)kP * NS;
-      float* fin = (j == p.nc - 1 && p.fin) ? p.fin + bh * (int64_t)kP * NS : nullptr;
-      float sin[32];
+      // ring slots are [p/4][n][4] (a warp's float4 access covers 512 contiguous bytes); the
+      // caller's initial and final states are [p][n]
+      const int64_t PN = (int64_t)kP * NS;
+      if (j == 0) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) sin[i] = src ? __ldcg(src + (32 * ph + i) * NS + n) : 0.f;
+        for (int i = 0; i < 32; ++i) sin[i] = p.init ? __ldcg(p.init + bh * PN + (32 * ph + i) * NS + n) : 0.f;
+      } else {
+        const float4* s4 = reinterpret_cast<const float4*>(p.ring + (bh * 2 + (j & 1)) * PN) + 8 * ph * NS + n;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float o = a_chunk * sin[i] + sl[i];
-        dst[(32 * ph + i) * NS + n] = o;
-        if (fin) fin[(32 * ph + i) * NS + n] = o;
+        for (int q = 0; q < 8; ++q) {
+          const float4 v = __ldcg(s4 + q * NS);
+          sin[4 * q] = v.x; sin[4 * q + 1] = v.y; sin[4 * q + 2] = v.z; sin[4 * q + 3] = v.w;
+        }
       }
+      float* fin = (j == p.nc - 1 && p.fin) ? p.fin + bh * PN : nullptr;
+      float4* d4 = reinterpret_cast<float4*>(p.ring + (bh * 2 + ((j + 1) & 1)) * PN) + 8 * ph * NS + n;
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        d4[q * NS] = make_float4(a_chunk * sin[4 * q] + sl[4 * q], a_chunk * sin[4 * q + 1] + sl[4 * q + 1],
+                                 a_chunk * sin[4 * q + 2] + sl[4 * q + 2], a_chunk * sin[4 * q + 3] + sl[4 * q + 3]);
+      if (fin) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) fin[(32 * ph + i) * NS + n] = a_chunk * sin[i] + sl[i];
+      }
+    }
+    // publish the outgoing state first; the bf16 copies below are off the chain's critical path
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) st_release(&flags[j + 1], kFlagReady);
+    if (active) {
       // S_in[j] in bf16: B operand of MMA4 ([n][p], p contiguous) and the saved state
       uint4 pk[4];
 #pragma unroll
@@ -278,12 +296,10 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
         for (int qd = 0; qd < 4; ++qd) *reinterpret_cast<uint4*>(gs + umma::sw128_offset(n, 4 * ph + qd)) = pk[qd];
       }
     }
-    __threadfence();
     umma::fence_proxy_async_smem();
     umma::fence_before_sync();
     __syncthreads();
     if (tid == 0) {
-      st_release(&flags[j + 1], kFlagReady);
       umma::fence_after_sync();
       const uint32_t q0 = umma::smem_u32(sQ), sin0 = umma::smem_u32(sSin);
       constexpr uint32_t id4 = umma::idesc_bf16(64, 64, false, true);
@@ -402,6 +418,22 @@ __device__ __forceinline__ void scale_rows(const unsigned char* src, unsigned ch
     e = unpack_bf16(v.w); o.w = pack_bf16(e.x * s, e.y * s);
     *reinterpret_cast<uint4*>(dst + off) = o;
   }
+}
+
+// v[i] (i < 16) is this lane's value in column i; the 16 lanes of each half-warp hold 16 rows.
+// Returns the sum over those 16 rows of column (lane % 16) (reduce-scatter: 15 shuffles).
+__device__ __forceinline__ float colsum16(float (&v)[16], int lane) {
+#pragma unroll
+  for (int w = 8; w >= 1; w >>= 1) {
+    const bool hi = (lane & w) != 0;
+#pragma unroll
+    for (int i = 0; i < w; ++i) {
+      const float send = hi ? v[i] : v[i + w];
+      const float keep = hi ? v[i + w] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+    }
+  }
+  return v[0];
 }
 
 // 8 consecutive bf16 of row r (16-byte chunk c) of a swizzled tile, as floats
@@ -565,9 +597,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
   if (ok) {
     umma::fence_after_sync();
     // score-gradient epilogue.  Warp w: sub-partition sp = w % 4 (rows t = 16 sp + lane % 16),
-    // half = w / 4 (0: K part with gamma, 1: Kp part with beta).  Lanes 0-15 hold S, 16-31 hold dA.
+    // half = w / 4 (0: K part with gamma, 1: Kp part with beta).  TMEM gives lanes 0-15 the S row
+    // and lanes 16-31 the dA row; one swap per column pair hands lanes 0-15 columns 0-15 and
+    // lanes 16-31 columns 16-31 of each 32-column block, so every lane works.
     const int sp = warp & 3, half = warp >> 2;
     const int t = 16 * sp + (lane & 15);
+    const bool hiL = lane >= 16;
     const float* coef = half ? s_b : s_g;
     const float ct = s_c[t];
     float rowZ = 0.f;
@@ -575,49 +610,47 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
     for (int cc = 0; cc < 2; ++cc) {
       float v[32];
       umma::tmem_ld32(R0 + ((uint32_t)(32 * sp) << 16) + half * 64 + cc * 32, v);
-      uint32_t wa[16], we[16];
+      float zc[16], ecs[16];
+      uint32_t wa[8], we[8];
+      float pa = 0.f, pe = 0.f;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float other = __shfl_xor_sync(0xffffffffu, v[i], 16);
-        const float sv = (lane < 16) ? v[i] : 0.f;   // S_ts
-        const float dav = (lane < 16) ? other : 0.f; // dA_ts
-        const int s = cc * 32 + i;
-        const float m = (s <= t && lane < 16) ? expf(ct - s_c[s]) : 0.f;
-        const float A = sv * coef[s] * m;
+      for (int i = 0; i < 16; ++i) {
+        const float recv = __shfl_xor_sync(0xffffffffu, hiL ? v[i] : v[16 + i], 16);
+        const float sv = hiL ? recv : v[i];          // S_ts
+        const float dav = hiL ? v[16 + i] : recv;    // dA_ts
+        const int s = cc * 32 + (hiL ? 16 : 0) + i;
+        const float m = (s <= t) ? __expf(ct - s_c[s]) : 0.f;
+        const float cf = coef[s];
+        const float A = sv * cf * m;
         const float E = dav * m;
         const float z = dav * A;
-        const float es = E * sv;
         rowZ += z;
-        // column sums over the 16 rows of this warp
-        float cz = z, ce = es;
-#pragma unroll
-        for (int o = 1; o < 16; o <<= 1) {
-          cz += __shfl_xor_sync(0xffffffffu, cz, o);
-          ce += __shfl_xor_sync(0xffffffffu, ce, o);
-        }
-        if (lane == 0) {
-          s_colZ[sp * 128 + half * 64 + s] = cz;
-          s_colE[sp * 128 + half * 64 + s] = ce;
-        }
-        // pack A and E*coef in pairs of bf16
-        if ((i & 1) == 0) {
-          wa[i >> 1] = __float_as_uint(A);
-          we[i >> 1] = __float_as_uint(E * coef[s]);
+        zc[i] = z;
+        ecs[i] = E * sv;
+        const float eg = E * cf;
+        if (i & 1) {
+          wa[i >> 1] = pack_bf16(pa, A);
+          we[i >> 1] = pack_bf16(pe, eg);
         } else {
-          wa[i >> 1] = pack_bf16(__uint_as_float(wa[i >> 1]), A);
-          we[i >> 1] = pack_bf16(__uint_as_float(we[i >> 1]), E * coef[s]);
+          pa = A;
+          pe = eg;
         }
       }
-      if (lane < 16) {
+      // column sums over the 16 rows of this half-warp; lane keeps column (lane % 16)
+      const float cz = colsum16(zc, lane), ce = colsum16(ecs, lane);
+      const int col = half * 64 + cc * 32 + (hiL ? 16 : 0) + (lane & 15);
+      s_colZ[sp * 128 + col] = cz;
+      s_colE[sp * 128 + col] = ce;
+      const int c0 = cc * 4 + (hiL ? 2 : 0);
 #pragma unroll
-        for (int qd = 0; qd < 4; ++qd) {
-          *reinterpret_cast<uint4*>(sPS + half * 8192 + umma::sw128_offset(t, cc * 4 + qd)) =
-              make_uint4(wa[4 * qd], wa[4 * qd + 1], wa[4 * qd + 2], wa[4 * qd + 3]);
-          *reinterpret_cast<uint4*>(sEG + half * 8192 + umma::sw128_offset(t, cc * 4 + qd)) =
-              make_uint4(we[4 * qd], we[4 * qd + 1], we[4 * qd + 2], we[4 * qd + 3]);
-        }
+      for (int q = 0; q < 2; ++q) {
+        *reinterpret_cast<uint4*>(sPS + half * 8192 + umma::sw128_offset(t, c0 + q)) =
+            make_uint4(wa[4 * q], wa[4 * q + 1], wa[4 * q + 2], wa[4 * q + 3]);
+        *reinterpret_cast<uint4*>(sEG + half * 8192 + umma::sw128_offset(t, c0 + q)) =
+            make_uint4(we[4 * q], we[4 * q + 1], we[4 * q + 2], we[4 * q + 3]);
       }
     }
+    rowZ += __shfl_xor_sync(0xffffffffu, rowZ, 16);
     if (lane < 16) s_rowZ[half * 64 + t] = rowZ;
     umma::fence_proxy_async_smem();
     umma::fence_before_sync();
@@ -659,23 +692,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
     const bool rows128 = (NS == 128);
     const int n = rows128 ? 32 * sp + lane : 16 * sp + (lane & 15);
     const bool active = rows128 || lane < 16;
-    float ds[32];
+    float ds[32], gn[32];
     umma::tmem_ld32(R4 + ((uint32_t)(32 * sp) << 16) + 32 * ph, ds);
     float da_part = 0.f;
     if (active) {
-      const float* src = (j == p.nc - 1) ? (p.dfin ? p.dfin + bh * (int64_t)kP * NS : nullptr)
-                                         : p.ring + (bh * 2 + ((j + 1) & 1)) * (int64_t)kP * NS;
-      float* dst = p.ring + (bh * 2 + (j & 1)) * (int64_t)kP * NS;
-      float* dinit = (j == 0 && p.dinit) ? p.dinit + bh * (int64_t)kP * NS : nullptr;
-      float gn[32];
+      // ring slots are [p/4][n][4]; the caller's dfinal / dinitial states are [p][n]
+      const int64_t PN = (int64_t)kP * NS;
+      if (j == p.nc - 1) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) gn[i] = src ? __ldcg(src + (32 * ph + i) * NS + n) : 0.f;
+        for (int i = 0; i < 32; ++i) gn[i] = p.dfin ? __ldcg(p.dfin + bh * PN + (32 * ph + i) * NS + n) : 0.f;
+      } else {
+        const float4* s4 = reinterpret_cast<const float4*>(p.ring + (bh * 2 + ((j + 1) & 1)) * PN) + 8 * ph * NS + n;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float o = ds[i] + a_chunk * gn[i];
-        dst[(32 * ph + i) * NS + n] = o;
-        if (dinit) dinit[(32 * ph + i) * NS + n] = o;
+        for (int q = 0; q < 8; ++q) {
+          const float4 v = __ldcg(s4 + q * NS);
+          gn[4 * q] = v.x; gn[4 * q + 1] = v.y; gn[4 * q + 2] = v.z; gn[4 * q + 3] = v.w;
+        }
       }
+      float* dinit = (j == 0 && p.dinit) ? p.dinit + bh * PN : nullptr;
+      float4* d4 = reinterpret_cast<float4*>(p.ring + (bh * 2 + (j & 1)) * PN) + 8 * ph * NS + n;
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        d4[q * NS] = make_float4(ds[4 * q] + a_chunk * gn[4 * q], ds[4 * q + 1] + a_chunk * gn[4 * q + 1],
+                                 ds[4 * q + 2] + a_chunk * gn[4 * q + 2], ds[4 * q + 3] + a_chunk * gn[4 * q + 3]);
+      if (dinit) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) dinit[(32 * ph + i) * NS + n] = ds[i] + a_chunk * gn[i];
+      }
+    }
+    // publish G[j] first; Gn in bf16 and <Gn, S_in> are off the chain's critical path
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) st_release(&flags[j], kFlagReady);
+    if (active) {
 #pragma unroll
       for (int qd = 0; qd < 4; ++qd) {
         float sv[8];
@@ -689,12 +738,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
     }
     da_part = warp_sum(da_part);
     if (lane == 0) s_da[warp] = da_part;
-    __threadfence();
     umma::fence_proxy_async_smem();
     umma::fence_before_sync();
     __syncthreads();
     if (tid == 0) {
-      st_release(&flags[j], kFlagReady);
       umma::fence_after_sync();
       const uint32_t kk0 = umma::smem_u32(sKK), xw0 = umma::smem_u32(sXW), gn0 = umma::smem_u32(sGN);
       // e (state part): dK += [wgX;wbXp] Gn
@@ -722,25 +769,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
     // (1) dQ rows (R1 lanes +0) and, for warps 0-3, Ye rows (R1 lanes +16) for the dc inter term
     {
       const int t = 16 * sp + (lane & 15);
+      const uint32_t base = R1 + ((uint32_t)(32 * sp) << 16) + 64 * ch;
+      float v0[32], v1[32];
+      umma::tmem_ld32x2(base, base + 32, v0, v1);
+      if (lane < 16 && 64 * ch < NS) {
+        __nv_bfloat16* dst = p.dq + b * p.dqsb + (int64_t)(t0 + t) * p.dqst + g * p.dqsh + 64 * ch;
+        store_row32(dst, v0);
+        store_row32(dst + 32, v1);
+      }
+      if (lane >= 16 && ch == 0) {
+        float acc = 0.f;
 #pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        float v[32];
-        umma::tmem_ld32(R1 + ((uint32_t)(32 * sp) << 16) + 64 * ch + 32 * cc, v);
-        if (lane < 16 && 64 * ch + 32 * cc < NS)
-          store_row32(p.dq + b * p.dqsb + (int64_t)(t0 + t) * p.dqst + g * p.dqsh + 64 * ch + 32 * cc, v);
-        if (lane >= 16 && ch == 0) {
-          float acc = 0.f;
+        for (int qd = 0; qd < 4; ++qd) {
+          float d0[8], d1[8];
+          load_chunk(sDY, t, qd, d0);
+          load_chunk(sDY, t, 4 + qd, d1);
 #pragma unroll
-          for (int qd = 0; qd < 4; ++qd) {
-            float dyv[8];
-            load_chunk(sDY, t, 4 * cc + qd, dyv);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc += dyv[e] * v[8 * qd + e];
-          }
-          // cc = 0 writes, cc = 1 adds (same thread)
-          if (cc == 0) s_dcint[t] = acc;
-          else s_dcint[t] = s_ec[t] * (s_dcint[t] + acc);
+          for (int e = 0; e < 8; ++e) acc += d0[e] * v0[8 * qd + e] + d1[e] * v1[8 * qd + e];
         }
+        s_dcint[t] = s_ec[t] * acc;
       }
     }
     // (2) dx / dxp rows: dXc (R2) + w g U (R3); x.U partial sums for dgamma / dbeta
@@ -748,8 +795,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
       const int r = 32 * sp + lane;  // 0-63: s of X, 64-127: s of Xp
       const int s = r & 63;
       float dxc[32], u[32];
-      umma::tmem_ld32(R2 + ((uint32_t)(32 * sp) << 16) + 32 * ch, dxc);
-      umma::tmem_ld32(R3 + ((uint32_t)(32 * sp) << 16) + 32 * ch, u);
+      umma::tmem_ld32x2(R2 + ((uint32_t)(32 * sp) << 16) + 32 * ch, R3 + ((uint32_t)(32 * sp) << 16) + 32 * ch, dxc, u);
       const float wgt = s_wgb[r];  // wg for X rows, wb for Xp rows
       float xu = 0.f;
 #pragma unroll
@@ -768,19 +814,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
       store_row32(dst + 32 * ch, dxc);
     }
     // (3) dk / dkp rows (R0)
-    {
+    if (64 * ch < NS) {
       const int r = 32 * sp + lane;
       const int s = r & 63;
       __nv_bfloat16* dst = (r < 64) ? p.dk + b * p.dksb + (int64_t)(t0 + s) * p.dkst + g * p.dksh
                                     : p.dkp + b * p.dkpsb + (int64_t)(t0 + s) * p.dkpst + g * p.dkpsh;
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        if (64 * ch + 32 * cc < NS) {
-          float v[32];
-          umma::tmem_ld32(R0 + ((uint32_t)(32 * sp) << 16) + 64 * ch + 32 * cc, v);
-          store_row32(dst + 64 * ch + 32 * cc, v);
-        }
-      }
+      const uint32_t base = R0 + ((uint32_t)(32 * sp) << 16) + 64 * ch;
+      float v0[32], v1[32];
+      umma::tmem_ld32x2(base, base + 32, v0, v1);
+      store_row32(dst + 64 * ch, v0);
+      store_row32(dst + 64 * ch + 32, v1);
     }
     __syncthreads();
     // per-token scalars: warps 0-1 own tokens 0-63
