@@ -49,6 +49,7 @@ struct FwdSmem {
 
 struct TcFwdParams {
   CUtensorMap tq, tk, tkp, tx, txp;
+  CUtensorMap ty;  // output, written by a TMA store from the staged tile
   int64_t B, T, H, G;
   int nc;
   const float* adt;
@@ -289,17 +290,18 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
                             pack_bf16(sin[qd * 8 + 4], sin[qd * 8 + 5]), pack_bf16(sin[qd * 8 + 6], sin[qd * 8 + 7]));
 #pragma unroll
       for (int qd = 0; qd < 4; ++qd) *reinterpret_cast<uint4*>(sSin + umma::sw128_offset(n, 4 * ph + qd)) = pk[qd];
-      if (p.states) {
-        // saved in the shared-memory image (128-byte swizzle) so the backward can bulk-copy it
-        unsigned char* gs = reinterpret_cast<unsigned char*>(p.states) + (bh * p.nc + j) * (int64_t)NS * 128;
-#pragma unroll
-        for (int qd = 0; qd < 4; ++qd) *reinterpret_cast<uint4*>(gs + umma::sw128_offset(n, 4 * ph + qd)) = pk[qd];
-      }
     }
     umma::fence_proxy_async_smem();
     umma::fence_before_sync();
     __syncthreads();
     if (tid == 0) {
+      if (p.states) {
+        // the saved state is the shared-memory image itself (bf16, 128-byte swizzle), so the
+        // backward can bulk-copy it back into place
+        umma::bulk_store(reinterpret_cast<unsigned char*>(p.states) + (bh * p.nc + j) * (int64_t)NS * 128, sSin,
+                         NS * 128);
+        umma::bulk_commit();
+      }
       umma::fence_after_sync();
       const uint32_t q0 = umma::smem_u32(sQ), sin0 = umma::smem_u32(sSin);
       constexpr uint32_t id4 = umma::idesc_bf16(64, 64, false, true);
@@ -317,25 +319,29 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
   }
   if (ok) {
     umma::fence_after_sync();
-    // y = Yi + e^{c_t} Ye  (mamba3.py:55)
+    // y = Yi + e^{c_t} Ye  (mamba3.py:55), staged as a bf16 tile over [wgX | wbXp] and TMA-stored
     const int sp = warp & 3, ph = warp >> 2;
     const int t = 16 * sp + (lane & 15);
     float v[32];
     umma::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + 128 + 32 * ph, v);
     const float ect = s_ec[t];
-    uint32_t w[16];
 #pragma unroll
-    for (int i = 0; i < 32; i += 2) {
-      const float o0 = __shfl_xor_sync(0xffffffffu, v[i], 16);
-      const float o1 = __shfl_xor_sync(0xffffffffu, v[i + 1], 16);
-      w[i / 2] = pack_bf16(v[i] + ect * o0, v[i + 1] + ect * o1);
-    }
+    for (int i = 0; i < 32; ++i) v[i] += ect * __shfl_xor_sync(0xffffffffu, v[i], 16);
     if (lane < 16) {
-      uint4* dst = reinterpret_cast<uint4*>(p.y + b * p.ysb + (int64_t)(t0 + t) * p.yst + h * p.ysh + 32 * ph);
 #pragma unroll
-      for (int qd = 0; qd < 4; ++qd) dst[qd] = make_uint4(w[4 * qd], w[4 * qd + 1], w[4 * qd + 2], w[4 * qd + 3]);
+      for (int qd = 0; qd < 4; ++qd)
+        *reinterpret_cast<uint4*>(sXs + umma::sw128_offset(t, 4 * ph + qd)) =
+            make_uint4(pack_bf16(v[8 * qd], v[8 * qd + 1]), pack_bf16(v[8 * qd + 2], v[8 * qd + 3]),
+                       pack_bf16(v[8 * qd + 4], v[8 * qd + 5]), pack_bf16(v[8 * qd + 6], v[8 * qd + 7]));
+    }
+    umma::fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      umma::tma_store_4d(&p.ty, sXs, 0, h, t0, b);
+      umma::bulk_commit();
     }
   }
+  if (tid == 0) umma::bulk_wait_all();  // staged tiles must be read out before exit
   umma::fence_before_sync();
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tmem, 256);
@@ -385,6 +391,7 @@ struct BwdSmem {
 
 struct TcBwdParams {
   CUtensorMap tq, tk, tkp, tx, txp, tdy;
+  CUtensorMap tdq, tdk, tdkp, tdx, tdxp;  // outputs, written by TMA stores from staged tiles
   int64_t B, T, H, G;
   int nc;
   const float* adt;
@@ -446,13 +453,15 @@ __device__ __forceinline__ void load_chunk(const unsigned char* tile, int r, int
   e = unpack_bf16(v.w); o[6] = e.x; o[7] = e.y;
 }
 
-__device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float* v) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
+// 32 floats -> bf16 into chunks [c0, c0 + 4) of row r of a 128-byte-swizzled staging tile
+__device__ __forceinline__ void stage_row32(unsigned char* tile, int r, int c0, const float* v) {
 #pragma unroll
   for (int qd = 0; qd < 4; ++qd)
-    d[qd] = make_uint4(pack_bf16(v[8 * qd], v[8 * qd + 1]), pack_bf16(v[8 * qd + 2], v[8 * qd + 3]),
-                       pack_bf16(v[8 * qd + 4], v[8 * qd + 5]), pack_bf16(v[8 * qd + 6], v[8 * qd + 7]));
+    *reinterpret_cast<uint4*>(tile + umma::sw128_offset(r, c0 + qd)) =
+        make_uint4(pack_bf16(v[8 * qd], v[8 * qd + 1]), pack_bf16(v[8 * qd + 2], v[8 * qd + 3]),
+                   pack_bf16(v[8 * qd + 4], v[8 * qd + 5]), pack_bf16(v[8 * qd + 6], v[8 * qd + 7]));
 }
+
 
 template <int NS>
 __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_constant__ TcBwdParams p) {
@@ -548,15 +557,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
   bool ok = __syncthreads_and(load_ok);
 
   if (ok) {
-    scale_rows(sXX, sXW, 16384, s_wgb, tid);  // [wgX | wbXp]
-    scale_rows(sDY, sDYE, 8192, s_ec, tid);   // e^{c_t} dY
-    umma::fence_proxy_async_smem();
-    umma::fence_before_sync();
-    __syncthreads();
+    // the products that need no rescaled operand start right away
     if (tid == 0) {
       umma::fence_after_sync();
       const uint32_t q0 = umma::smem_u32(sQ), kk0 = umma::smem_u32(sKK), xx0 = umma::smem_u32(sXX);
-      const uint32_t dy0 = umma::smem_u32(sDY), dye0 = umma::smem_u32(sDYE), sin0 = umma::smem_u32(sSin);
+      const uint32_t dy0 = umma::smem_u32(sDY), sin0 = umma::smem_u32(sSin);
       // b: S = Q [K;Kp]^T
       constexpr uint32_t idb = umma::idesc_bf16(64, 128, false, false);
 #pragma unroll
@@ -570,12 +575,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
       for (int ks = 0; ks < 4; ++ks)
         umma::mma_bf16(R0 + (16u << 16), umma::desc_sw128(dy0 + ks * 32, 16, 1024),
                        umma::desc_sw128(xx0 + ks * 32, 16, 1024), idb, ks > 0);
-      // g: dSl' = Q^T dYe   (M = n)
-      constexpr uint32_t idg = umma::idesc_bf16(NS, 64, true, true);
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        umma::mma_bf16(R4, umma::desc_sw128(q0 + ks * 2048, 8192, 1024), umma::desc_sw128(dye0 + ks * 2048, 8192, 1024),
-                       idg, ks > 0);
       // h: Ye = Q S_in^T
       constexpr uint32_t idh = umma::idesc_bf16(64, 64, false, true);
 #pragma unroll
@@ -584,6 +583,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
         umma::mma_bf16(R1 + (16u << 16), umma::desc_sw128(q0 + qb * 8192 + kin * 32, 16, 1024),
                        umma::desc_sw128(sin0 + ks * 2048, 8192, 1024), idh, ks > 0);
       }
+    }
+    scale_rows(sXX, sXW, 16384, s_wgb, tid);  // [wgX | wbXp]
+    scale_rows(sDY, sDYE, 8192, s_ec, tid);   // e^{c_t} dY
+    umma::fence_proxy_async_smem();
+    umma::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+      umma::fence_after_sync();
+      const uint32_t q0 = umma::smem_u32(sQ);
+      const uint32_t dye0 = umma::smem_u32(sDYE), sin0 = umma::smem_u32(sSin);
+      // g: dSl' = Q^T dYe   (M = n)
+      constexpr uint32_t idg = umma::idesc_bf16(NS, 64, true, true);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma::mma_bf16(R4, umma::desc_sw128(q0 + ks * 2048, 8192, 1024), umma::desc_sw128(dye0 + ks * 2048, 8192, 1024),
+                       idg, ks > 0);
       // d (inter part): dQ = dYe S_in
       constexpr uint32_t idd1 = umma::idesc_bf16(64, NS, false, false);
 #pragma unroll
@@ -766,6 +781,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
   if (ok) {
     umma::fence_after_sync();
     const int sp = warp & 3, ch = warp >> 2;
+    // Output tiles are staged (bf16, 128-byte swizzle) in shared memory that is dead by now and
+    // leave through TMA stores: dq -> Q tile, dk | dkp -> K/Kp tiles, dx | dxp -> [A|Ap] tile.
+    unsigned char* st_dq = sQ;
+    unsigned char* st_dk = sKK;
+    unsigned char* st_dkp = sKK + S::QB * 8192;
+    unsigned char* st_dx = sPS;
+    unsigned char* st_dxp = sPS + 8192;
     // (1) dQ rows (R1 lanes +0) and, for warps 0-3, Ye rows (R1 lanes +16) for the dc inter term
     {
       const int t = 16 * sp + (lane & 15);
@@ -773,9 +795,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
       float v0[32], v1[32];
       umma::tmem_ld32x2(base, base + 32, v0, v1);
       if (lane < 16 && 64 * ch < NS) {
-        __nv_bfloat16* dst = p.dq + b * p.dqsb + (int64_t)(t0 + t) * p.dqst + g * p.dqsh + 64 * ch;
-        store_row32(dst, v0);
-        store_row32(dst + 32, v1);
+        stage_row32(st_dq + ch * 8192, t, 0, v0);
+        stage_row32(st_dq + ch * 8192, t, 4, v1);
       }
       if (lane >= 16 && ch == 0) {
         float acc = 0.f;
@@ -793,7 +814,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
     // (2) dx / dxp rows: dXc (R2) + w g U (R3); x.U partial sums for dgamma / dbeta
     {
       const int r = 32 * sp + lane;  // 0-63: s of X, 64-127: s of Xp
-      const int s = r & 63;
       float dxc[32], u[32];
       umma::tmem_ld32x2(R2 + ((uint32_t)(32 * sp) << 16) + 32 * ch, R3 + ((uint32_t)(32 * sp) << 16) + 32 * ch, dxc, u);
       const float wgt = s_wgb[r];  // wg for X rows, wb for Xp rows
@@ -809,21 +829,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
         }
       }
       s_xu[ch * 128 + r] = xu;
-      __nv_bfloat16* dst = (r < 64) ? p.dx + b * p.dxsb + (int64_t)(t0 + s) * p.dxst + h * p.dxsh
-                                    : p.dxp + b * p.dxpsb + (int64_t)(t0 + s) * p.dxpst + h * p.dxpsh;
-      store_row32(dst + 32 * ch, dxc);
+      stage_row32(r < 64 ? st_dx : st_dxp, r & 63, 4 * ch, dxc);
     }
     // (3) dk / dkp rows (R0)
     if (64 * ch < NS) {
       const int r = 32 * sp + lane;
-      const int s = r & 63;
-      __nv_bfloat16* dst = (r < 64) ? p.dk + b * p.dksb + (int64_t)(t0 + s) * p.dkst + g * p.dksh
-                                    : p.dkp + b * p.dkpsb + (int64_t)(t0 + s) * p.dkpst + g * p.dkpsh;
       const uint32_t base = R0 + ((uint32_t)(32 * sp) << 16) + 64 * ch;
       float v0[32], v1[32];
       umma::tmem_ld32x2(base, base + 32, v0, v1);
-      store_row32(dst + 64 * ch, v0);
-      store_row32(dst + 64 * ch + 32, v1);
+      unsigned char* tile = (r < 64 ? st_dk : st_dkp) + ch * 8192;
+      stage_row32(tile, r & 63, 0, v0);
+      stage_row32(tile, r & 63, 4, v1);
+    }
+    umma::fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+#pragma unroll
+      for (int qb = 0; qb < S::QB; ++qb) {
+        umma::tma_store_4d(&p.tdq, st_dq + qb * 8192, qb * 64, g, t0, b);
+        umma::tma_store_4d(&p.tdk, st_dk + qb * 8192, qb * 64, g, t0, b);
+        umma::tma_store_4d(&p.tdkp, st_dkp + qb * 8192, qb * 64, g, t0, b);
+      }
+      umma::tma_store_4d(&p.tdx, st_dx, 0, h, t0, b);
+      umma::tma_store_4d(&p.tdxp, st_dxp, 0, h, t0, b);
+      umma::bulk_commit();
     }
     __syncthreads();
     // per-token scalars: warps 0-1 own tokens 0-63
@@ -864,6 +893,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
       p.dbeta[b * p.dbsb + (int64_t)tt * p.dbst + h * p.dbsh] = db;
     }
   }
+  if (tid == 0) umma::bulk_wait_all();  // staged output tiles must be read out before exit
   umma::fence_before_sync();
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tmem, 512);
@@ -914,7 +944,7 @@ int launch_fwd(const zb_ssd_args* a, ChainSync sync, void* states, void* ring, c
   memset(&p, 0, sizeof(p));
   if (!make_map(&p.tq, a->q, a->B, a->T, a->G, NS) || !make_map(&p.tk, a->k, a->B, a->T, a->G, NS) ||
       !make_map(&p.tkp, a->kp, a->B, a->T, a->G, NS) || !make_map(&p.tx, a->x, a->B, a->T, a->H, kP) ||
-      !make_map(&p.txp, a->xp, a->B, a->T, a->H, kP))
+      !make_map(&p.txp, a->xp, a->B, a->T, a->H, kP) || !make_map(&p.ty, a->y, a->B, a->T, a->H, kP))
     return ZB_ERR_LAYOUT;
   p.B = a->B; p.T = a->T; p.H = a->H; p.G = a->G;
   p.nc = (int)(a->T / kL);
@@ -942,10 +972,6 @@ int launch_fwd(const zb_ssd_args* a, ChainSync sync, void* states, void* ring, c
   return cudaPeekAtLastError() == cudaSuccess ? ZB_OK : ZB_ERR_CUDA;
 }
 
-bool row_out_ok(const zb_view& v) {
-  return v.ptr && reinterpret_cast<uintptr_t>(v.ptr) % 16 == 0 && (v.sh * 2) % 16 == 0 && (v.st * 2) % 16 == 0 &&
-         (v.sb * 2) % 16 == 0;
-}
 
 template <int NS>
 int launch_bwd(const zb_ssd_args* a, ChainSync sync, void* ring, cudaStream_t stream) {
@@ -954,7 +980,11 @@ int launch_bwd(const zb_ssd_args* a, ChainSync sync, void* ring, cudaStream_t st
   if (!view_tma_ok(a->dy)) return ZB_ERR_LAYOUT;
   const zb_view* outs[] = {&a->dx, &a->dxp, &a->dq, &a->dk, &a->dkp};
   for (auto v : outs)
-    if (!row_out_ok(*v)) return ZB_ERR_LAYOUT;
+    if (!view_tma_ok(*v)) return ZB_ERR_LAYOUT;
+  if (!make_map(&p.tdq, a->dq, a->B, a->T, a->G, NS) || !make_map(&p.tdk, a->dk, a->B, a->T, a->G, NS) ||
+      !make_map(&p.tdkp, a->dkp, a->B, a->T, a->G, NS) || !make_map(&p.tdx, a->dx, a->B, a->T, a->H, kP) ||
+      !make_map(&p.tdxp, a->dxp, a->B, a->T, a->H, kP))
+    return ZB_ERR_LAYOUT;
   if (!make_map(&p.tq, a->q, a->B, a->T, a->G, NS) || !make_map(&p.tk, a->k, a->B, a->T, a->G, NS) ||
       !make_map(&p.tkp, a->kp, a->B, a->T, a->G, NS) || !make_map(&p.tx, a->x, a->B, a->T, a->H, kP) ||
       !make_map(&p.txp, a->xp, a->B, a->T, a->H, kP) || !make_map(&p.tdy, a->dy, a->B, a->T, a->H, kP))
