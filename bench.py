@@ -170,7 +170,9 @@ def cpu_reference_sample(shape, seconds: float, max_reps: int | None = None):
 
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
-    sl = SsdShape(1, shape.T, shape.H, shape.P, shape.N, shape.G, shape.chunk)
+    # one sequence of the workload; for long contexts an 8192-token slice (the scan is linear in T,
+    # so tokens/s of a slice stands for the whole sequence)
+    sl = SsdShape(1, min(shape.T, 8192), shape.H, shape.P, shape.N, shape.G, shape.chunk)
     inp = make_inputs(sl, seed=0)
     leaves = [(inp[n].to(torch.bfloat16).float() if n in VEC else inp[n]).requires_grad_() for n in NAMES]
     dy = inp["dy"].to(torch.bfloat16).float()
@@ -228,7 +230,7 @@ def run_ours(args):
     import zenith_b200
     from zenith_b200 import _lib
     from zenith_b200.ssd import ssd_bwd_op, ssd_fwd_op
-    from zenith_b200.synthetic import SHAPES
+    from zenith_b200.synthetic import SHAPES, SsdShape
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -238,23 +240,46 @@ def run_ours(args):
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     shape = SHAPES[args.workload]
-    inp = make_device_inputs(shape, rank, dev)
+    # long-context workload on N > 1 GPUs: context parallelism (each rank owns T/N tokens of the
+    # sequence; boundary states move between ranks with NCCL send/recv).  Otherwise every rank
+    # runs its own batch of the workload (batch x heads sharding: weak scaling, no collective).
+    cp = args.workload == "long" and world > 1
+    local_shape = SsdShape(shape.B, shape.T // world, shape.H, shape.P, shape.N, shape.G, shape.chunk) if cp else shape
+    inp = make_device_inputs(local_shape, rank, dev)
     a = [inp[n] for n in NAMES]
     dy = inp["dy"]
     chunk = shape.chunk
     fwd_b, bwd_b = algorithmic_bytes(shape)
-    th = shape.B * shape.T * shape.H
+    th = local_shape.B * local_shape.T * local_shape.H
 
-    def step(ev=None):
-        if ev is not None:
-            ev[0].record()
-        y, fin, states = ssd_fwd_op(*a, chunk, None, True, False)
-        if ev is not None:
-            ev[1].record()
-        g = ssd_bwd_op(dy, *a, states, chunk, None, None, False)
-        if ev is not None:
-            ev[2].record()
-        return y, g
+    if cp:
+        from zenith_b200.parallel import cp_ssd
+
+        leaves = [t.clone().requires_grad_() for t in a]
+
+        def step(ev=None):
+            if ev is not None:
+                ev[0].record()
+            y = cp_ssd(*leaves, chunk)
+            if ev is not None:
+                ev[1].record()
+            y.backward(dy)
+            if ev is not None:
+                ev[2].record()
+            for t in leaves:
+                t.grad = None
+            return y
+    else:
+        def step(ev=None):
+            if ev is not None:
+                ev[0].record()
+            y, fin, states = ssd_fwd_op(*a, chunk, None, True, False)
+            if ev is not None:
+                ev[1].record()
+            g = ssd_bwd_op(dy, *a, states, chunk, None, None, False)
+            if ev is not None:
+                ev[2].record()
+            return y, g
 
     def barrier():
         if world > 1:
@@ -289,7 +314,7 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     elapsed_ms = float(t.item())
     ms_per_step = elapsed_ms / args.steps
-    tokens_per_step = shape.B * shape.T * world
+    tokens_per_step = shape.B * shape.T if cp else shape.B * shape.T * world
     value = tokens_per_step / (ms_per_step / 1e3)
 
     # end-to-end through the public API with host buffers (pinned), copies inside the timed region
@@ -301,7 +326,7 @@ def run_ours(args):
     def e2e_step():
         leaves = [host[n].to(dev, non_blocking=True).requires_grad_() for n in NAMES]
         d = host["dy"].to(dev, non_blocking=True)
-        y = zenith_b200.ssd(*leaves, chunk)
+        y = zenith_b200.parallel.cp_ssd(*leaves, chunk) if cp else zenith_b200.ssd(*leaves, chunk)
         y.backward(d)
         outs["x"].copy_(y.detach(), non_blocking=True)  # y shares x's shape/dtype
         for n, lf in zip(NAMES, leaves):
@@ -346,7 +371,10 @@ def run_ours(args):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": shape.name, "B_per_gpu": shape.B, "T": shape.T, "H": shape.H, "P": shape.P,
                    "N": shape.N, "chunk": shape.chunk, "vector_dtype": "bf16", "scalar_dtype": "fp32",
-                   "parallelism": f"batch-sharded x{world}", "l2": "inputs larger than L2 (1.3 GB/step)"},
+                   "parallelism": (f"context-parallel x{world} (T/{world} per rank, NCCL send/recv of boundary states)"
+                                   if cp else f"batch-sharded x{world}"),
+                   "tokens_per_rank": local_shape.B * local_shape.T,
+                   "l2": f"inputs larger than L2 ({(fwd_b + bwd_b) * th / 1e9:.2f} GB/step per rank)"},
         "roofline": {"bound": "hbm", "kernel": dname, "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic_from_profile(dname),
                      "algorithmic_bytes_per_launch": dbytes, "launch_ms": dms},

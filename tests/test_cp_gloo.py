@@ -1,0 +1,50 @@
+"""Context parallelism on CPU ranks (gloo): the exchange logic of zenith_b200.parallel with the
+oracle as the per-rank scan, against the oracle on the whole sequence."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from oracle.ssd_oracle import max_rel_err, ssd_backward, ssd_forward
+from tests.cp_workers import NAMES, cp_failure_worker, cp_parity_worker, shape_for
+from zenith_b200.synthetic import make_inputs
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_context_parallel_matches_whole_sequence(world, tmp_path):
+    mp.start_processes(cp_parity_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    s = shape_for(world)
+    inp = make_inputs(s, seed=11)
+    args = [inp[n].double() for n in NAMES]
+    y, _, _ = ssd_forward(*args, s.chunk)
+    g = ssd_backward(inp["dy"].double(), *args, s.chunk)
+    parts = [torch.load(tmp_path / f"rank{r}.pt") for r in range(world)]
+    assert max_rel_err(torch.cat([p["y"] for p in parts], 1), y) < 1e-12
+    for n in NAMES:
+        got = torch.cat([p["d" + n] for p in parts], 1)
+        assert max_rel_err(got, g["d" + n]) < 1e-11, n
+
+
+def test_context_parallel_rank_failure_ends_in_an_error_not_a_hang(tmp_path):
+    ctx = mp.start_processes(cp_failure_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=False,
+                             start_method="spawn")
+    try:
+        while not ctx.join(timeout=90):
+            pass
+    except mp.ProcessRaisedException as e:
+        assert "injected failure on rank 1" in str(e)
+    for p in ctx.processes:
+        if p.is_alive():
+            p.join(timeout=60)
+        assert not p.is_alive(), "a rank hung"
+    msg = (tmp_path / "rank0.txt").read_text() if (tmp_path / "rank0.txt").exists() else "rank 0 died"
+    assert msg.startswith("error") or msg == "rank 0 died", msg

@@ -1,0 +1,71 @@
+"""Context parallelism on 2 GPUs over NCCL: cp_ssd on two halves of a sequence against the
+single-GPU scan on the whole sequence (same kernels, bf16)."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+NAMES = ("x", "q", "k", "kp", "xp", "adt", "gamma", "beta")
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, outdir):
+    import datetime
+
+    import torch.distributed as dist
+
+    import zenith_b200
+    from zenith_b200.parallel import cp_ssd
+    from zenith_b200.synthetic import SsdShape, make_inputs
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    s = SsdShape(2, 1024, 4, 64, 128, 4, 64)
+    inp = make_inputs(s, seed=2)
+    Tl = s.T // world
+    sl = slice(rank * Tl, (rank + 1) * Tl)
+    leaves = [(inp[n].to(torch.bfloat16) if n in ("x", "q", "k", "kp", "xp") else inp[n])[:, sl].to(dev).contiguous()
+              .requires_grad_() for n in NAMES]
+    y = cp_ssd(*leaves, s.chunk)
+    y.backward(inp["dy"][:, sl].to(torch.bfloat16).to(dev))
+    zenith_b200.check_status(dev)
+    out = {"y": y.detach().float().cpu()}
+    for n, t in zip(NAMES, leaves):
+        out["d" + n] = t.grad.detach().float().cpu()
+    torch.save(out, os.path.join(outdir, f"rank{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_context_parallel_two_gpus_matches_single_gpu(tmp_path):
+    import zenith_b200
+    from oracle.ssd_oracle import max_rel_err
+    from zenith_b200.synthetic import SsdShape, make_inputs
+
+    world = 2
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    s = SsdShape(2, 1024, 4, 64, 128, 4, 64)
+    inp = make_inputs(s, seed=2)
+    leaves = [(inp[n].to(torch.bfloat16) if n in ("x", "q", "k", "kp", "xp") else inp[n]).cuda().requires_grad_()
+              for n in NAMES]
+    y = zenith_b200.ssd(*leaves, s.chunk)
+    y.backward(inp["dy"].to(torch.bfloat16).cuda())
+    parts = [torch.load(tmp_path / f"rank{r}.pt") for r in range(world)]
+    assert max_rel_err(torch.cat([p["y"] for p in parts], 1), y.float()) < 1e-2
+    for n, t in zip(NAMES, leaves):
+        got = torch.cat([p["d" + n] for p in parts], 1)
+        assert max_rel_err(got, t.grad.float()) < 1e-2, n

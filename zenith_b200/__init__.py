@@ -6,3 +6,7 @@ from .ssd import prepare_inputs, ssd, ssd_dinitial_state, ssd_final_state, use_b
 
 __all__ = ["ssd", "ssd_final_state", "ssd_dinitial_state", "use_b200_scan", "prepare_inputs", "check_status", "SsdError"]
 __version__ = "0.1.0"
+
+from .parallel import cp_ssd  # noqa: E402  (context parallelism over torch.distributed)
+
+__all__.append("cp_ssd")

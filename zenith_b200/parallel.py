@@ -1,0 +1,184 @@
+"""Context parallelism for long sequences: each rank owns a contiguous range of the sequence.
+
+The reference runs one sequence on one device (zenith/mamba3.py:30-56).  Because the SSD state
+recurrence is linear, S_out = D S_in + F with D = exp(sum adt) over a range and F that range's final
+state from a zero start, a sequence split over ranks needs only the boundary states:
+
+forward
+  1. every rank: F_r = final state of its range from zero, D_r = exp(sum_t adt) per (b, h)
+     (state-only pass: reads x, xp, k, kp and the scalars, writes nothing else)
+  2. chain over ranks with NCCL send/recv: S_0 = initial state (zero), S_{r+1} = D_r S_r + F_r;
+     rank r receives S_r from rank r-1 and sends S_{r+1} to rank r+1  ([B, H, P, N] fp32)
+  3. every rank: the full local scan with initial_state = S_r (saving chunk states)
+backward
+  1. every rank: G_r = gradient w.r.t. its initial state from its own dy alone (state-only pass)
+  2. reverse chain: E_{R-1} = 0, E_{r-1} = D_r E_r + G_r  (E_r = gradient w.r.t. the state
+     leaving rank r, i.e. the incoming dfinal of rank r)
+  3. every rank: the full local backward with dfinal = E_r.
+
+Ranks hold data in the caller's layout ([B, T_local, H, ...]).  The exchange is collective: every
+rank of the group must call with equally shaped local ranges.
+"""
+
+from __future__ import annotations
+
+import datetime
+from dataclasses import dataclass
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+from . import _lib as L
+from .ssd import _stream, prepare_inputs, ssd_bwd_op, ssd_fwd_op
+
+NAMES = ("x", "q", "k", "kp", "xp", "adt", "gamma", "beta")
+
+
+# ------------------------------------------------------------------------------------------------
+# local scan implementation (injectable: the default is the CUDA library)
+
+
+@dataclass
+class LocalScan:
+    """The per-rank operations context parallelism needs."""
+
+    final_state: Callable    # (inputs, chunk, init) -> F [B,H,P,N]
+    forward: Callable        # (inputs, chunk, init) -> (y, saved)
+    dinitial: Callable       # (dy, inputs, chunk) -> G [B,H,P,N]   (dfinal = 0)
+    backward: Callable       # (dy, inputs, saved, chunk, init, dfinal) -> 8 grads
+    total_decay: Callable    # (adt) -> D [B,H] fp32
+    combine: Callable        # (s_prev, d, f) -> d * s_prev + f
+
+
+def _cuda_final_state(inp, chunk, init):
+    return ssd_fwd_op(*inp, int(chunk), init, False, True)[1]
+
+
+def _cuda_forward(inp, chunk, init):
+    y, fin, states = ssd_fwd_op(*inp, int(chunk), init, True, False)
+    return y, (states, fin)
+
+
+def _cuda_dinitial(dy, inp, chunk):
+    empty = torch.empty(0, dtype=torch.uint8, device=dy.device)
+    out = ssd_bwd_op(dy, *inp, empty, int(chunk), None, None, True)
+    return out[-1]
+
+
+def _cuda_backward(dy, inp, saved, chunk, init, dfinal):
+    states, _ = saved
+    out = ssd_bwd_op(dy, *inp, states, int(chunk), init, dfinal, False)
+    return out[:8]
+
+
+def _cuda_total_decay(adt):
+    B, T, H = adt.shape
+    out = torch.empty(B * H, dtype=torch.float32, device=adt.device)
+    a = L.Args()
+    a.B, a.T, a.H = B, T, H
+    a.scalar_dtype = L.DTYPE_CODE[adt.dtype]
+    a.adt = L.view(adt)
+    L.check(L.lib().zb_ssd_total_decay(ctypes_byref(a), out.data_ptr(), _stream(adt.device)), "zb_ssd_total_decay")
+    return out.view(B, H)
+
+
+def _cuda_combine(s_prev, d, f):
+    out = torch.empty_like(f)
+    BH = d.numel()
+    L.check(L.lib().zb_ssd_state_combine(s_prev.data_ptr(), d.data_ptr(), f.data_ptr(), out.data_ptr(), BH,
+                                         f.numel() // BH, _stream(f.device)), "zb_ssd_state_combine")
+    return out
+
+
+def ctypes_byref(a):
+    import ctypes
+
+    return ctypes.byref(a)
+
+
+CUDA_SCAN = LocalScan(_cuda_final_state, _cuda_forward, _cuda_dinitial, _cuda_backward, _cuda_total_decay, _cuda_combine)
+
+
+# ------------------------------------------------------------------------------------------------
+# the exchange
+
+
+def _chain_forward(F, D, group, init, impl: LocalScan):
+    """S_r for this rank: receive from rank-1, send D_r S_r + F_r to rank+1."""
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    if rank == 0:
+        S = torch.zeros_like(F) if init is None else init.to(F.dtype).contiguous()
+    else:
+        S = torch.empty_like(F)
+        dist.recv(S, src=dist.get_global_rank(group, rank - 1) if group is not None else rank - 1, group=group)
+    if rank < world - 1:
+        nxt = impl.combine(S, D, F).contiguous()
+        dist.send(nxt, dst=dist.get_global_rank(group, rank + 1) if group is not None else rank + 1, group=group)
+    return S
+
+
+def _chain_backward(G, D, group, dfinal, impl: LocalScan):
+    """E_r (gradient w.r.t. the state leaving this rank): receive from rank+1, send
+    D_r E_r + G_r to rank-1."""
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    if rank == world - 1:
+        E = torch.zeros_like(G) if dfinal is None else dfinal.to(G.dtype).contiguous()
+    else:
+        E = torch.empty_like(G)
+        dist.recv(E, src=dist.get_global_rank(group, rank + 1) if group is not None else rank + 1, group=group)
+    if rank > 0:
+        prv = impl.combine(E, D, G).contiguous()
+        dist.send(prv, dst=dist.get_global_rank(group, rank - 1) if group is not None else rank - 1, group=group)
+    return E
+
+
+class _CpScan(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, chunk, group, impl, init, x, q, k, kp, xp, adt, gamma, beta):
+        inp = (x, q, k, kp, xp, adt, gamma, beta)
+        F = impl.final_state(inp, chunk, None)
+        D = impl.total_decay(adt)
+        S = _chain_forward(F, D, group, init, impl)
+        y, saved = impl.forward(inp, chunk, S)
+        ctx.chunk, ctx.group, ctx.impl = chunk, group, impl
+        ctx.saved = saved
+        ctx.save_for_backward(S, D, *inp)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        S, D, *inp = ctx.saved_tensors
+        dy = dy.to(inp[0].dtype).contiguous()
+        G = ctx.impl.dinitial(dy, tuple(inp), ctx.chunk)
+        E = _chain_backward(G, D, ctx.group, None, ctx.impl)
+        grads = ctx.impl.backward(dy, tuple(inp), ctx.saved, ctx.chunk, S, E)
+        return (None, None, None, None, *grads)
+
+
+def cp_ssd(x, q, k, kp, xp, adt, gamma, beta, chunk_size, *, group=None, initial_state=None,
+           impl: Optional[LocalScan] = None):
+    """Context-parallel SSD scan over the ranks of ``group`` (default: the world).
+
+    Each rank passes its contiguous range of the sequence ([B, T_local, H, ...], rank r holding
+    tokens [r T_local, (r+1) T_local)); returns this rank's y.  Same arithmetic as
+    ``zenith_b200.ssd`` on the whole sequence, differentiable w.r.t. all eight inputs.
+    ``initial_state`` (rank 0 only) starts the sequence from a given state.
+    """
+    assert x.shape[1] % chunk_size == 0, "sequence length must be a multiple of chunk_size"
+    impl = impl or CUDA_SCAN
+    if impl is CUDA_SCAN:
+        args = prepare_inputs(x, q, k, kp, xp, adt, gamma, beta)
+    else:
+        args = (x, q, k, kp, xp, adt, gamma, beta)
+    y = _CpScan.apply(int(chunk_size), group, impl, initial_state, *args)
+    return y.to(x.dtype) if y.dtype != x.dtype else y
+
+
+def init_process_group_from_env(backend: str, timeout_s: float = 120.0, device_id=None):
+    """Initialise torch.distributed from RANK / WORLD_SIZE / MASTER_ADDR / MASTER_PORT with a
+    short timeout, so that ranks waiting for a failed peer end with an error instead of hanging."""
+    kw = {"timeout": datetime.timedelta(seconds=timeout_s)}
+    if device_id is not None:
+        kw["device_id"] = device_id
+    dist.init_process_group(backend, **kw)
