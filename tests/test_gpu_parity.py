@@ -179,6 +179,21 @@ def test_tensor_core_forward_matches_oracle(shape):
     assert max_rel_err(fin, ref["final_state"]) < TOL[torch.bfloat16]
 
 
+@pytest.mark.parametrize("shape", [SsdShape(1, 8192, 2, 64, 128, 2, 128), SsdShape(2, 4096, 3, 64, 64, 3, 64)],
+                         ids=["B1-T8192-H2", "B2-T4096-H3-N64"])
+def test_long_sequences_with_few_heads_match_oracle(shape):
+    """Few (batch, head) chains and many chunks: the library splits each sequence into segments
+    joined by a state-only pass and a combine step; all outputs, gradients and the boundary
+    states must still match the oracle."""
+    inp = _cast(make_inputs(shape, seed=31), torch.bfloat16, torch.float32)
+    g = torch.Generator().manual_seed(13)
+    init = torch.randn(shape.B, shape.H, shape.P, shape.N, generator=g)
+    dfinal = torch.randn(shape.B, shape.H, shape.P, shape.N, generator=g)
+    got = run_cuda(inp, shape.chunk, init=init, dfinal=dfinal)
+    ref = oracle(inp, shape.chunk, init=init.double(), dfinal=dfinal.double())
+    compare(got, ref, TOL[torch.bfloat16])
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_runs_are_bitwise_deterministic(dtype):
     inp = _cast(make_inputs(SsdShape(2, 256, 4, 64, 128, 4, 64), seed=9), dtype, torch.float32)

@@ -202,6 +202,191 @@ size_t plan_workspace(const Plan& pl, bool backward) {
   if (!backward) return pl.sync_bytes + pl.states_bytes;  // the chain lives here when no states buffer is given
   return pl.sync_bytes + pl.gchain_bytes + pl.grp_bytes;
 }
+
+// ---------------------------------------------------------------------------------------------
+// Segmented long sequences.  With fewer (batch, head) chains than SMs, a long sequence would be
+// handed chunk to chunk through one long chain per (batch, head).  Instead each sequence is viewed
+// as M consecutive segments (M sequences of T/M tokens: a pure stride change when the batch
+// dimension is contiguous), and the same linear algebra as context parallelism joins them:
+//   forward : F_m, D_m = final state from zero and exp(sum adt) of segment m (state-only pass);
+//             S_m = D_{m-1} S_{m-1} + F_{m-1} (combine kernel); full pass with initial states S_m.
+//   backward: G_m = d(initial state of m) from segment m's own dy (state-only pass);
+//             E_{m-1} = D_m E_m + G_m (combine kernel); full pass with final-state gradients E_m.
+// The decision depends only on sizes and the input views, so forward and backward agree.
+constexpr int64_t kSegMinChains = 296;  // aim for two chains per SM
+constexpr int kSegMinChunks = 4;         // and at least four chunks per chain
+
+bool batch_contiguous(const zb_view& v, int64_t T) { return v.sb == T * v.st; }
+
+int segments_for(const zb_ssd_args* a, const Plan& pl) {
+  if (pl.kind != kTc || (a->flags & ZB_FLAG_STATE_ONLY)) return 1;
+  const int64_t chains = a->B * a->H;
+  if (chains >= 148) return 1;
+  const zb_view* v[] = {&a->x, &a->q, &a->k, &a->kp, &a->xp, &a->adt, &a->gamma, &a->beta};
+  for (auto x : v)
+    if (!batch_contiguous(*x, a->T)) return 1;
+  int M = 1;
+  while (chains * M < kSegMinChains && pl.nc % (2 * M) == 0 && pl.nc / (2 * M) >= kSegMinChunks) M *= 2;
+  return M;
+}
+
+zb_view seg_view(const zb_view& v, int64_t T, int M) {
+  zb_view o = v;
+  o.sb = (T / M) * v.st;
+  return o;
+}
+
+// the arguments seen as B*M sequences of T/M tokens (views must be batch-contiguous)
+bool seg_args(const zb_ssd_args* a, int M, bool backward, zb_ssd_args* s) {
+  *s = *a;
+  s->B = a->B * M;
+  s->T = a->T / M;
+  s->chunk_size = tc_chunk();
+  zb_view* v[] = {&s->x, &s->q, &s->k, &s->kp, &s->xp, &s->adt, &s->gamma, &s->beta};
+  for (auto x : v) *x = seg_view(*x, a->T, M);
+  if (!backward) {
+    if (!batch_contiguous(a->y, a->T)) return false;
+    s->y = seg_view(a->y, a->T, M);
+  } else {
+    const zb_view* src[] = {&a->dy, &a->dx, &a->dq, &a->dk, &a->dkp, &a->dxp, &a->dadt, &a->dgamma, &a->dbeta};
+    zb_view* dst[] = {&s->dy, &s->dx, &s->dq, &s->dk, &s->dkp, &s->dxp, &s->dadt, &s->dgamma, &s->dbeta};
+    for (int i = 0; i < 9; ++i) {
+      if (!batch_contiguous(*src[i], a->T)) return false;
+      *dst[i] = seg_view(*src[i], a->T, M);
+    }
+  }
+  return true;
+}
+
+struct SegLayout {
+  size_t sync, ring, fg, d, se, total;  // byte offsets of each part, and the total
+};
+
+SegLayout seg_layout(const zb_ssd_args* a, int M) {
+  const int64_t BHs = a->B * M * a->H, nc = a->T / M / tc_chunk();
+  const size_t pn = (size_t)a->P * a->N * sizeof(float);
+  SegLayout L;
+  L.sync = 0;
+  L.ring = chain_sync_bytes(BHs * (nc + 1));
+  L.fg = L.ring + align_up((size_t)BHs * 2 * pn, 256);
+  L.d = L.fg + align_up((size_t)BHs * pn, 256);
+  L.se = L.d + align_up((size_t)BHs * sizeof(float), 256);
+  L.total = L.se + align_up((size_t)BHs * pn, 256);
+  return L;
+}
+
+// forward combine: segment initial states from `init` (or zero), F and D; writes the final state
+__global__ void seg_combine_fwd_kernel(const float* init, const float* F, const float* D, float* S, float* fin, int64_t B,
+                                       int64_t H, int M, int64_t PN) {
+  const int64_t total = B * H * PN;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = i % PN, bh = i / PN, b = bh / H, h = bh % H;
+    float s = init ? init[i] : 0.f;
+    for (int m = 0; m < M; ++m) {
+      const int64_t idx = (b * M + m) * H + h;
+      S[idx * PN + e] = s;
+      s = D[idx] * s + F[idx * PN + e];
+    }
+    if (fin) fin[i] = s;
+  }
+}
+
+// backward combine: gradient w.r.t. each segment's final state, from `dfinal` (or zero), the
+// segments' own initial-state gradients G and D; writes the gradient w.r.t. the initial state
+__global__ void seg_combine_bwd_kernel(const float* dfinal, const float* G, const float* D, float* E, float* dinit,
+                                       int64_t B, int64_t H, int M, int64_t PN) {
+  const int64_t total = B * H * PN;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = i % PN, bh = i / PN, b = bh / H, h = bh % H;
+    float g = dfinal ? dfinal[i] : 0.f;
+    for (int m = M - 1; m >= 0; --m) {
+      const int64_t idx = (b * M + m) * H + h;
+      E[idx * PN + e] = g;
+      g = D[idx] * g + G[idx * PN + e];
+    }
+    if (dinit) dinit[i] = g;
+  }
+}
+
+int launch_total_decay(const zb_ssd_args* a, float* out, cudaStream_t s);
+
+// segmented forward / backward (see above); `ws` holds SegLayout
+int seg_fwd(const zb_ssd_args* a, int M, char* ws, cudaStream_t stream) {
+  const SegLayout L = seg_layout(a, M);
+  zb_ssd_args sa;
+  if (!seg_args(a, M, false, &sa)) return ZB_ERR_LAYOUT;
+  const int64_t BHs = sa.B * sa.H;
+  const size_t sync_bytes = chain_sync_bytes(BHs * (sa.T / tc_chunk() + 1));
+  float* F = reinterpret_cast<float*>(ws + L.fg);
+  float* D = reinterpret_cast<float*>(ws + L.d);
+  float* Sg = reinterpret_cast<float*>(ws + L.se);
+  ChainSync sync{reinterpret_cast<unsigned int*>(ws), reinterpret_cast<int*>(ws + 256)};
+  cudaError_t e = cudaMemsetAsync(ws, 0, sync_bytes, stream);
+  if (e != cudaSuccess) return ZB_ERR_CUDA;
+  zb_ssd_args st = sa;
+  st.flags |= ZB_FLAG_STATE_ONLY;
+  st.initial_state = nullptr;
+  st.final_state = F;
+  st.states = nullptr;
+  int rc = tc_fwd(&st, sync, nullptr, ws + L.ring, stream);
+  if (rc) return rc;
+  if ((rc = launch_total_decay(&sa, D, stream))) return rc;
+  const int64_t PN = a->P * a->N, total = a->B * a->H * PN;
+  seg_combine_fwd_kernel<<<(unsigned)std::min<int64_t>((total + 255) / 256, 148 * 8), 256, 0, stream>>>(
+      static_cast<const float*>(a->initial_state), F, D, Sg, static_cast<float*>(a->final_state), a->B, a->H, M, PN);
+  note_launches(1);
+  if ((e = cudaMemsetAsync(ws, 0, sync_bytes, stream)) != cudaSuccess) return ZB_ERR_CUDA;
+  zb_ssd_args full = sa;
+  full.initial_state = Sg;
+  full.final_state = nullptr;
+  return tc_fwd(&full, sync, a->states, ws + L.ring, stream);
+}
+
+int seg_bwd(const zb_ssd_args* a, int M, char* ws, cudaStream_t stream) {
+  const SegLayout L = seg_layout(a, M);
+  zb_ssd_args sa;
+  if (!seg_args(a, M, true, &sa)) return ZB_ERR_LAYOUT;
+  const int64_t BHs = sa.B * sa.H;
+  const size_t sync_bytes = chain_sync_bytes(BHs * (sa.T / tc_chunk() + 1));
+  float* G = reinterpret_cast<float*>(ws + L.fg);
+  float* D = reinterpret_cast<float*>(ws + L.d);
+  float* E = reinterpret_cast<float*>(ws + L.se);
+  ChainSync sync{reinterpret_cast<unsigned int*>(ws), reinterpret_cast<int*>(ws + 256)};
+  cudaError_t e = cudaMemsetAsync(ws, 0, sync_bytes, stream);
+  if (e != cudaSuccess) return ZB_ERR_CUDA;
+  zb_ssd_args st = sa;
+  st.flags |= ZB_FLAG_STATE_ONLY;
+  st.dfinal_state = nullptr;
+  st.dinitial_state = G;
+  int rc = tc_bwd(&st, sync, ws + L.ring, stream);
+  if (rc) return rc;
+  if ((rc = launch_total_decay(&sa, D, stream))) return rc;
+  const int64_t PN = a->P * a->N, total = a->B * a->H * PN;
+  seg_combine_bwd_kernel<<<(unsigned)std::min<int64_t>((total + 255) / 256, 148 * 8), 256, 0, stream>>>(
+      static_cast<const float*>(a->dfinal_state), G, D, E, static_cast<float*>(a->dinitial_state), a->B, a->H, M, PN);
+  note_launches(1);
+  if ((e = cudaMemsetAsync(ws, 0, sync_bytes, stream)) != cudaSuccess) return ZB_ERR_CUDA;
+  zb_ssd_args full = sa;
+  full.dfinal_state = E;
+  full.dinitial_state = nullptr;
+  return tc_bwd(&full, sync, ws + L.ring, stream);
+}
+}  // namespace
+
+namespace {
+int launch_total_decay(const zb_ssd_args* a, float* out, cudaStream_t s) {
+  const unsigned nb = (unsigned)(a->B * a->H);
+  const View v = to_view(a->adt);
+  switch (a->scalar_dtype) {
+    case ZB_F32: total_decay_kernel<float><<<nb, 256, 0, s>>>(v, a->T, a->H, out); break;
+    case ZB_BF16: total_decay_kernel<__nv_bfloat16><<<nb, 256, 0, s>>>(v, a->T, a->H, out); break;
+    case ZB_F16: total_decay_kernel<__half><<<nb, 256, 0, s>>>(v, a->T, a->H, out); break;
+    case ZB_F64: total_decay_kernel<double><<<nb, 256, 0, s>>>(v, a->T, a->H, out); break;
+    default: return ZB_ERR_DTYPE;
+  }
+  note_launches(1);
+  return cudaPeekAtLastError() == cudaSuccess ? ZB_OK : ZB_ERR_CUDA;
+}
 }  // namespace
 
 size_t zb_ssd_workspace_bytes(const zb_ssd_args* a, int backward) {
@@ -211,10 +396,15 @@ size_t zb_ssd_workspace_bytes(const zb_ssd_args* a, int backward) {
   Plan pl;
   if (make_plan(a, &pl, false) != ZB_OK) return 0;
   size_t need = plan_workspace(pl, backward != 0);
+  int M = segments_for(a, pl);
   if (!backward) {  // a forward may run with or without a states buffer: cover both plans
     Plan p2;
-    if (make_plan(a, &p2, true) == ZB_OK) need = std::max(need, plan_workspace(p2, false));
+    if (make_plan(a, &p2, true) == ZB_OK) {
+      need = std::max(need, plan_workspace(p2, false));
+      M = std::max(M, segments_for(a, p2));
+    }
   }
+  if (M > 1) need = std::max(need, seg_layout(a, M).total);
   return need;
 }
 
@@ -224,10 +414,16 @@ int zb_ssd_fwd(const zb_ssd_args* a, void* stream_) {
   if (rc) return rc;
   Plan pl;
   if ((rc = make_plan(a, &pl, a->states == nullptr))) return rc;
-  const size_t need = plan_workspace(pl, false);
+  const int M = segments_for(a, pl);
+  const size_t need = M > 1 ? seg_layout(a, M).total : plan_workspace(pl, false);
   if (!a->workspace || a->workspace_bytes < need || reinterpret_cast<uintptr_t>(a->workspace) % 256) return ZB_ERR_WORKSPACE;
   if (a->states && reinterpret_cast<uintptr_t>(a->states) % 256) return ZB_ERR_WORKSPACE;
   char* ws = static_cast<char*>(a->workspace);
+  if (M > 1) {
+    rc = seg_fwd(a, M, ws, stream);
+    if (rc == ZB_ERR_CUDA) return cuda_fail(cudaGetLastError());
+    return rc;
+  }
   cudaError_t e = cudaMemsetAsync(ws, 0, pl.sync_bytes, stream);
   if (e != cudaSuccess) return cuda_fail(e);
   ChainSync sync{reinterpret_cast<unsigned int*>(ws), reinterpret_cast<int*>(ws + 256)};
@@ -250,10 +446,16 @@ int zb_ssd_bwd(const zb_ssd_args* a, void* stream_) {
   if (rc) return rc;
   Plan pl;
   if ((rc = make_plan(a, &pl, false))) return rc;
-  const size_t need = plan_workspace(pl, true);
+  const int M = segments_for(a, pl);
+  const size_t need = M > 1 ? seg_layout(a, M).total : plan_workspace(pl, true);
   if (!a->workspace || a->workspace_bytes < need || reinterpret_cast<uintptr_t>(a->workspace) % 256) return ZB_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(a->states) % 256) return ZB_ERR_WORKSPACE;
   char* ws = static_cast<char*>(a->workspace);
+  if (M > 1) {
+    rc = seg_bwd(a, M, ws, stream);
+    if (rc == ZB_ERR_CUDA) return cuda_fail(cudaGetLastError());
+    return rc;
+  }
   cudaError_t e = cudaMemsetAsync(ws, 0, pl.sync_bytes, stream);
   if (e != cudaSuccess) return cuda_fail(e);
   ChainSync sync{reinterpret_cast<unsigned int*>(ws), reinterpret_cast<int*>(ws + 256)};

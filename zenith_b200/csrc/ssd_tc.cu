@@ -900,6 +900,222 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
 }
 
 // ---------------------------------------------------------------------------------------------
+// state-only passes (context parallelism, segmented long sequences): no per-token outputs.
+//   forward : S_in[j+1] = e^{c_L} S_in[j] + [K;Kp]^T [wgX; wbXp]   (MMA M=N, N=64, K=128)
+//   backward: G[j] = Q^T (e^{c} dY) + e^{c_L} G[j+1]                 (MMA M=N, N=64, K=64)
+// 128 threads, 64 TMEM columns, <= 65 KB shared memory: several CTAs per SM hide the hand-off.
+
+constexpr int kStThreads = 128;
+
+template <int NS>
+struct StateSmem {
+  static constexpr int QB = NS / 64;
+  static constexpr uint32_t A0 = 0;                    // fwd: [QB][K | Kp]   bwd: Q [QB][64][64]
+  static constexpr uint32_t B0 = A0 + QB * 16384;      // fwd: [X | Xp]       bwd: dY
+  static constexpr uint32_t B1 = B0 + 16384;           // fwd: [wgX | wbXp]   bwd: e^c dY
+  static constexpr uint32_t SCAL = B1 + 16384;         // c, w*g, w*b (or e^c) : 3 x 64 floats
+  static constexpr uint32_t BAR = SCAL + 3 * 256;
+  static constexpr uint32_t MISC = BAR + 2 * 8;
+  static constexpr uint32_t TOTAL = MISC + 16;
+  static constexpr uint32_t ALLOC = TOTAL + 1024;
+};
+
+struct TcStateParams {
+  CUtensorMap t0, t1, t2, t3;  // fwd: k, kp, x, xp   bwd: q, dy
+  int64_t B, T, H, G;
+  int nc;
+  const float* adt;
+  const float* gamma;
+  const float* beta;
+  int64_t asb, ast, ash, gsb, gst, gsh, bsb, bst, bsh;
+  const float* init;   // fwd: initial state [B*H][P][N] or null;  bwd: dfinal or null
+  float* out;          // fwd: final state;  bwd: dinitial state (both [B*H][P][N], may be null)
+  float* ring;         // [B*H][2] slots, [p/4][n][4]
+  unsigned int* ticket;
+  int* flags;
+  int32_t* status;
+};
+
+template <int NS, bool BACKWARD>
+__global__ void __launch_bounds__(kStThreads) ssd_state_tc_kernel(const __grid_constant__ TcStateParams p) {
+  using S = StateSmem<NS>;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sA = sm + S::A0;
+  unsigned char* sB0 = sm + S::B0;
+  unsigned char* sB1 = sm + S::B1;
+  float* s_c = reinterpret_cast<float*>(sm + S::SCAL);
+  float* s_f0 = s_c + 64;   // fwd: w*g   bwd: e^{c}
+  float* s_f1 = s_c + 128;  // fwd: w*b
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::BAR);
+  uint32_t* misc = reinterpret_cast<uint32_t*>(sm + S::MISC);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    misc[1] = atomicAdd(p.ticket, 1u);
+    umma::mbar_init(&bars[0], 1);
+    umma::mbar_init(&bars[1], 1);
+    umma::mbar_fence_init();
+  }
+  if (warp == 0) {
+    umma::tmem_alloc(&misc[0], 64);
+    umma::tmem_relinquish();
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = misc[0];
+  const int64_t BH = p.B * p.H;
+  const int64_t tk = misc[1];
+  const int j = BACKWARD ? p.nc - 1 - (int)(tk / BH) : (int)(tk / BH);
+  const int64_t bh = tk % BH;
+  const int b = (int)(bh / p.H), h = (int)(bh % p.H);
+  const int g = (int)(h / (p.H / p.G));
+  const int t0 = j * kL;
+  int* flags = p.flags + bh * (p.nc + 1);
+  const int64_t PN = (int64_t)kP * NS;
+
+  if (tid == 0) {
+    if (BACKWARD) {
+      umma::mbar_arrive_expect_tx(&bars[0], S::QB * 8192 + 8192);
+#pragma unroll
+      for (int qb = 0; qb < S::QB; ++qb) umma::tma_load_4d(sA + qb * 8192, &p.t0, &bars[0], qb * 64, g, t0, b);
+      umma::tma_load_4d(sB0, &p.t1, &bars[0], 0, h, t0, b);
+    } else {
+      umma::mbar_arrive_expect_tx(&bars[0], S::QB * 16384 + 16384);
+#pragma unroll
+      for (int qb = 0; qb < S::QB; ++qb) {
+        umma::tma_load_4d(sA + qb * 16384, &p.t0, &bars[0], qb * 64, g, t0, b);
+        umma::tma_load_4d(sA + qb * 16384 + 8192, &p.t1, &bars[0], qb * 64, g, t0, b);
+      }
+      umma::tma_load_4d(sB0, &p.t2, &bars[0], 0, h, t0, b);
+      umma::tma_load_4d(sB0 + 8192, &p.t3, &bars[0], 0, h, t0, b);
+    }
+  }
+  if (tid < 64) {
+    const int t = t0 + tid;
+    const float a = p.adt[b * p.asb + t * p.ast + h * p.ash];
+    if (!BACKWARD) {
+      s_f0[tid] = p.gamma[b * p.gsb + t * p.gst + h * p.gsh];
+      s_f1[tid] = p.beta[b * p.bsb + t * p.bst + h * p.bsh];
+    }
+    s_c[tid] = warp_incl_scan(a, lane);
+  }
+  __syncthreads();
+  if (tid >= 32 && tid < 64) s_c[tid] += s_c[31];
+  __syncthreads();
+  if (tid < 64) {
+    const float c = s_c[tid];
+    if (BACKWARD) {
+      s_f0[tid] = expf(c);
+    } else {
+      const float w = expf(s_c[63] - c);
+      s_f0[tid] *= w;
+      s_f1[tid] *= w;
+    }
+  }
+  const bool load_ok = umma::mbar_wait(&bars[0], 0, p.status);
+  __syncthreads();
+  const float a_chunk = expf(s_c[63]);
+  bool ok = __syncthreads_and(load_ok);
+  if (ok) {
+    // rescale the rows of the x (fwd) or dy (bwd) tile(s) into B1
+    const uint32_t bytes = BACKWARD ? 8192u : 16384u;
+    for (uint32_t off = (uint32_t)tid * 16u; off < bytes; off += kStThreads * 16u) {
+      const int r = off >> 7;
+      const float f = BACKWARD ? s_f0[r] : (r < 64 ? s_f0[r] : s_f1[r - 64]);
+      const uint4 v = *reinterpret_cast<const uint4*>(sB0 + off);
+      uint4 o;
+      float2 e;
+      e = unpack_bf16(v.x); o.x = pack_bf16(e.x * f, e.y * f);
+      e = unpack_bf16(v.y); o.y = pack_bf16(e.x * f, e.y * f);
+      e = unpack_bf16(v.z); o.z = pack_bf16(e.x * f, e.y * f);
+      e = unpack_bf16(v.w); o.w = pack_bf16(e.x * f, e.y * f);
+      *reinterpret_cast<uint4*>(sB1 + off) = o;
+    }
+    umma::fence_proxy_async_smem();
+    umma::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+      umma::fence_after_sync();
+      const uint32_t a0 = umma::smem_u32(sA), b1 = umma::smem_u32(sB1);
+      constexpr uint32_t id = umma::idesc_bf16(NS, 64, true, true);
+      if (BACKWARD) {
+        // G_loc^T[n][p] = sum_t q_t[n] e^{c_t} dy_t[p]   (A = Q^T, B = e^c dY, both MN-major)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma::mma_bf16(tmem, umma::desc_sw128(a0 + ks * 2048, 8192, 1024), umma::desc_sw128(b1 + ks * 2048, 8192, 1024),
+                         id, ks > 0);
+      } else {
+        // S_loc^T[n][p] = sum_s k_s[n] wg_s x_s[p] + kp_s[n] wb_s xp_s[p]
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t part = ks >> 2, kin = ks & 3;
+          umma::mma_bf16(tmem, umma::desc_sw128(a0 + part * 8192 + kin * 2048, 16384, 1024),
+                         umma::desc_sw128(b1 + part * 8192 + kin * 2048, 8192, 1024), id, ks > 0);
+        }
+      }
+      umma::mma_commit(&bars[1]);
+    }
+    ok = __syncthreads_and(umma::mbar_wait(&bars[1], 0, p.status));
+  }
+  if (ok) {
+    umma::fence_after_sync();
+    // this thread's n (lane of the MMA's D layout) and all 64 p
+    const int sp = warp;
+    const bool rows128 = (NS == 128);
+    const int n = rows128 ? 32 * sp + lane : 16 * sp + (lane & 15);
+    const bool active = rows128 || lane < 16;
+    float v0[32], v1[32];
+    umma::tmem_ld32x2(tmem + ((uint32_t)(32 * sp) << 16), tmem + ((uint32_t)(32 * sp) << 16) + 32, v0, v1);
+    if (tid == 0) {
+      const bool first = BACKWARD ? (j == p.nc - 1) : (j == 0);
+      misc[2] = first ? kFlagReady : wait_flag(&flags[BACKWARD ? j + 1 : j], p.status);
+    }
+    __syncthreads();
+    ok = misc[2] == kFlagReady;
+    if (ok && active) {
+      const bool first = BACKWARD ? (j == p.nc - 1) : (j == 0);
+      const bool last = BACKWARD ? (j == 0) : (j == p.nc - 1);
+      const int in_slot = BACKWARD ? ((j + 1) & 1) : (j & 1);
+      const int out_slot = BACKWARD ? (j & 1) : ((j + 1) & 1);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const float* loc = half ? v1 : v0;
+        float prev[32];
+        if (first) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) prev[i] = p.init ? __ldcg(p.init + bh * PN + (32 * half + i) * NS + n) : 0.f;
+        } else {
+          const float4* s4 = reinterpret_cast<const float4*>(p.ring + (bh * 2 + in_slot) * PN) + 8 * half * NS + n;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 v = __ldcg(s4 + q * NS);
+            prev[4 * q] = v.x; prev[4 * q + 1] = v.y; prev[4 * q + 2] = v.z; prev[4 * q + 3] = v.w;
+          }
+        }
+        float4* d4 = reinterpret_cast<float4*>(p.ring + (bh * 2 + out_slot) * PN) + 8 * half * NS + n;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          d4[q * NS] = make_float4(a_chunk * prev[4 * q] + loc[4 * q], a_chunk * prev[4 * q + 1] + loc[4 * q + 1],
+                                   a_chunk * prev[4 * q + 2] + loc[4 * q + 2], a_chunk * prev[4 * q + 3] + loc[4 * q + 3]);
+        if (last && p.out) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) p.out[bh * PN + (32 * half + i) * NS + n] = a_chunk * prev[i] + loc[i];
+        }
+      }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) st_release(&flags[BACKWARD ? j : j + 1], ok ? kFlagReady : kFlagAbort);
+  } else if (tid == 0) {
+    st_release(&flags[BACKWARD ? j : j + 1], kFlagAbort);
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tmem, 64);
+}
+
+// ---------------------------------------------------------------------------------------------
 // host side
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -1021,11 +1237,45 @@ int launch_bwd(const zb_ssd_args* a, ChainSync sync, void* ring, cudaStream_t st
   return cudaPeekAtLastError() == cudaSuccess ? ZB_OK : ZB_ERR_CUDA;
 }
 
+template <int NS, bool BACKWARD>
+int launch_state(const zb_ssd_args* a, ChainSync sync, void* ring, cudaStream_t stream) {
+  TcStateParams p;
+  memset(&p, 0, sizeof(p));
+  bool maps_ok;
+  if (BACKWARD) {
+    maps_ok = view_tma_ok(a->dy) && make_map(&p.t0, a->q, a->B, a->T, a->G, NS) &&
+              make_map(&p.t1, a->dy, a->B, a->T, a->H, kP);
+  } else {
+    maps_ok = make_map(&p.t0, a->k, a->B, a->T, a->G, NS) && make_map(&p.t1, a->kp, a->B, a->T, a->G, NS) &&
+              make_map(&p.t2, a->x, a->B, a->T, a->H, kP) && make_map(&p.t3, a->xp, a->B, a->T, a->H, kP);
+  }
+  if (!maps_ok) return ZB_ERR_LAYOUT;
+  p.B = a->B; p.T = a->T; p.H = a->H; p.G = a->G;
+  p.nc = (int)(a->T / kL);
+  p.adt = static_cast<const float*>(a->adt.ptr);
+  p.gamma = static_cast<const float*>(a->gamma.ptr);
+  p.beta = static_cast<const float*>(a->beta.ptr);
+  p.asb = a->adt.sb; p.ast = a->adt.st; p.ash = a->adt.sh;
+  p.gsb = a->gamma.sb; p.gst = a->gamma.st; p.gsh = a->gamma.sh;
+  p.bsb = a->beta.sb; p.bst = a->beta.st; p.bsh = a->beta.sh;
+  p.init = static_cast<const float*>(BACKWARD ? a->dfinal_state : a->initial_state);
+  p.out = static_cast<float*>(BACKWARD ? a->dinitial_state : a->final_state);
+  p.ring = static_cast<float*>(ring);
+  p.ticket = sync.ticket;
+  p.flags = sync.flags;
+  p.status = a->status;
+  auto k = ssd_state_tc_kernel<NS, BACKWARD>;
+  const int smem = (int)StateSmem<NS>::ALLOC;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return ZB_ERR_CUDA;
+  k<<<(unsigned)(a->B * a->H * p.nc), kStThreads, smem, stream>>>(p);
+  note_launches(1);
+  return cudaPeekAtLastError() == cudaSuccess ? ZB_OK : ZB_ERR_CUDA;
+}
+
 }  // namespace
 
 bool tc_supported(const zb_ssd_args* a) {
   if (a->dtype != ZB_BF16 || a->scalar_dtype != ZB_F32) return false;
-  if (a->flags & ZB_FLAG_STATE_ONLY) return false;
   if (a->P != kP || (a->N != 64 && a->N != 128)) return false;
   if (a->T % kL != 0) return false;
   if (a->T / kL >= (1 << 30) || a->B * a->H * (a->T / kL) >= (1ll << 31)) return false;
@@ -1054,13 +1304,23 @@ size_t tc_workspace_bytes(const zb_ssd_args* a, bool) {
 }
 
 int tc_fwd(const zb_ssd_args* a, ChainSync sync, void* states, void* ws, cudaStream_t stream) {
+  if (a->flags & ZB_FLAG_STATE_ONLY) {
+    if (a->N == 128) return launch_state<128, false>(a, sync, ws, stream);
+    if (a->N == 64) return launch_state<64, false>(a, sync, ws, stream);
+    return ZB_ERR_UNSUPPORTED;
+  }
   if (a->N == 128) return launch_fwd<128>(a, sync, states, ws, stream);
   if (a->N == 64) return launch_fwd<64>(a, sync, states, ws, stream);
   return ZB_ERR_UNSUPPORTED;
 }
 
 int tc_bwd(const zb_ssd_args* a, ChainSync sync, void* ws, cudaStream_t stream) {
-  if (a->G != a->H || (a->flags & ZB_FLAG_STATE_ONLY)) return ZB_ERR_UNSUPPORTED;
+  if (a->flags & ZB_FLAG_STATE_ONLY) {
+    if (a->N == 128) return launch_state<128, true>(a, sync, ws, stream);
+    if (a->N == 64) return launch_state<64, true>(a, sync, ws, stream);
+    return ZB_ERR_UNSUPPORTED;
+  }
+  if (a->G != a->H) return ZB_ERR_UNSUPPORTED;
   if (a->N == 128) return launch_bwd<128>(a, sync, ws, stream);
   if (a->N == 64) return launch_bwd<64>(a, sync, ws, stream);
   return ZB_ERR_UNSUPPORTED;
