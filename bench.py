@@ -367,7 +367,7 @@ def run_ours(args):
     step_gbs = (fwd_b + bwd_b) * th / (ms_per_step / 1e3) / 1e9
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong" if cp else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": shape.name, "B_per_gpu": shape.B, "T": shape.T, "H": shape.H, "P": shape.P,
                    "N": shape.N, "chunk": shape.chunk, "vector_dtype": "bf16", "scalar_dtype": "fp32",

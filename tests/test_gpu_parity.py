@@ -192,6 +192,14 @@ def test_long_sequences_with_few_heads_match_oracle(shape):
     got = run_cuda(inp, shape.chunk, init=init, dfinal=dfinal)
     ref = oracle(inp, shape.chunk, init=init.double(), dfinal=dfinal.double())
     compare(got, ref, TOL[torch.bfloat16])
+    # the state-only passes (context-parallel pre-passes) take the same segmented route
+    dev = "cuda"
+    args = [inp[n].to(dev) for n in NAMES]
+    fin = zenith_b200.ssd_final_state(*args, shape.chunk, initial_state=init.to(dev))
+    dinit = zenith_b200.ssd_dinitial_state(inp["dy"].to(dev), *args, shape.chunk, dfinal=dfinal.to(dev))
+    zenith_b200.check_status()
+    assert max_rel_err(fin, ref["final_state"]) < TOL[torch.bfloat16]
+    assert max_rel_err(dinit, ref["dinitial_state"]) < TOL[torch.bfloat16]
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])

@@ -219,7 +219,7 @@ constexpr int kSegMinChunks = 4;         // and at least four chunks per chain
 bool batch_contiguous(const zb_view& v, int64_t T) { return v.sb == T * v.st; }
 
 int segments_for(const zb_ssd_args* a, const Plan& pl) {
-  if (pl.kind != kTc || (a->flags & ZB_FLAG_STATE_ONLY)) return 1;
+  if (pl.kind != kTc) return 1;
   const int64_t chains = a->B * a->H;
   if (chains >= 148) return 1;
   const zb_view* v[] = {&a->x, &a->q, &a->k, &a->kp, &a->xp, &a->adt, &a->gamma, &a->beta};
@@ -244,7 +244,9 @@ bool seg_args(const zb_ssd_args* a, int M, bool backward, zb_ssd_args* s) {
   s->chunk_size = tc_chunk();
   zb_view* v[] = {&s->x, &s->q, &s->k, &s->kp, &s->xp, &s->adt, &s->gamma, &s->beta};
   for (auto x : v) *x = seg_view(*x, a->T, M);
+  const bool state_only = (a->flags & ZB_FLAG_STATE_ONLY) != 0;
   if (!backward) {
+    if (state_only) return true;
     if (!batch_contiguous(a->y, a->T)) return false;
     s->y = seg_view(a->y, a->T, M);
   } else {
@@ -335,6 +337,7 @@ int seg_fwd(const zb_ssd_args* a, int M, char* ws, cudaStream_t stream) {
   seg_combine_fwd_kernel<<<(unsigned)std::min<int64_t>((total + 255) / 256, 148 * 8), 256, 0, stream>>>(
       static_cast<const float*>(a->initial_state), F, D, Sg, static_cast<float*>(a->final_state), a->B, a->H, M, PN);
   note_launches(1);
+  if (a->flags & ZB_FLAG_STATE_ONLY) return cudaPeekAtLastError() == cudaSuccess ? ZB_OK : ZB_ERR_CUDA;
   if ((e = cudaMemsetAsync(ws, 0, sync_bytes, stream)) != cudaSuccess) return ZB_ERR_CUDA;
   zb_ssd_args full = sa;
   full.initial_state = Sg;
@@ -365,6 +368,7 @@ int seg_bwd(const zb_ssd_args* a, int M, char* ws, cudaStream_t stream) {
   seg_combine_bwd_kernel<<<(unsigned)std::min<int64_t>((total + 255) / 256, 148 * 8), 256, 0, stream>>>(
       static_cast<const float*>(a->dfinal_state), G, D, E, static_cast<float*>(a->dinitial_state), a->B, a->H, M, PN);
   note_launches(1);
+  if (a->flags & ZB_FLAG_STATE_ONLY) return cudaPeekAtLastError() == cudaSuccess ? ZB_OK : ZB_ERR_CUDA;
   if ((e = cudaMemsetAsync(ws, 0, sync_bytes, stream)) != cudaSuccess) return ZB_ERR_CUDA;
   zb_ssd_args full = sa;
   full.dfinal_state = E;
