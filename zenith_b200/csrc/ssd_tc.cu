@@ -39,10 +39,11 @@ struct FwdSmem {
   static constexpr uint32_t X = KK + QB * 16384;          // [64 s][64 p]
   static constexpr uint32_t XP = X + 8192;
   static constexpr uint32_t XS = XP + 8192;               // [wgX | wbXp]
-  static constexpr uint32_t SIN = XS + 16384;             // [NS n][64 p]
-  static constexpr uint32_t SCAL = SIN + NS * 128;        // c, ec, wg, wb, g, b (64 floats each)
-  static constexpr uint32_t BAR = SCAL + 6 * 64 * 4;      // 4 mbarriers
-  static constexpr uint32_t MISC = BAR + 4 * 8;           // tmem base, ticket, ready
+  static constexpr uint32_t SIN = XS + 16384;             // [NS n][64 p]; before that the scores Ps [2][64][64]
+  static constexpr uint32_t SIN_BYTES = NS * 128 > 16384 ? NS * 128 : 16384;
+  static constexpr uint32_t SCAL = SIN + SIN_BYTES;       // c, ec, wg, wb, g, b (64 floats each)
+  static constexpr uint32_t BAR = SCAL + 6 * 64 * 4;      // 5 mbarriers (load, MMA1, MMA2, MMA4, MMA3)
+  static constexpr uint32_t MISC = BAR + 6 * 8;           // tmem base, ticket, ready
   static constexpr uint32_t TOTAL = MISC + 16;
   static constexpr uint32_t ALLOC = TOTAL + 1024;         // slack to align the base to 1024
 };
@@ -84,7 +85,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* sQ = sm + S::Q;
   unsigned char* sKK = sm + S::KK;
-  unsigned char* sPs = sKK;  // reused once MMA1 and MMA3 have read K/Kp
+  unsigned char* sPs = sm + S::SIN;  // scores live in the S_in tile until MMA2 has read them
   unsigned char* sX = sm + S::X;
   unsigned char* sXp = sm + S::XP;
   unsigned char* sXs = sm + S::XS;
@@ -101,7 +102,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     misc[1] = atomicAdd(p.ticket, 1u);
-    for (int i = 0; i < 4; ++i) umma::mbar_init(&bars[i], 1);
+    for (int i = 0; i < 5; ++i) umma::mbar_init(&bars[i], 1);
     umma::mbar_fence_init();
   }
   if (warp == 0) {
@@ -156,6 +157,19 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
   bool ok = __syncthreads_and(load_ok);
 
   if (ok) {
+    // MMA1 (scores) needs no rescaled operand: start it before scaling X
+    if (tid == 0) {
+      umma::fence_after_sync();
+      const uint32_t q0 = umma::smem_u32(sQ), kk0 = umma::smem_u32(sKK);
+      constexpr uint32_t id1 = umma::idesc_bf16(64, 128, false, false);
+#pragma unroll
+      for (int ks = 0; ks < NS / 16; ++ks) {
+        const uint32_t qb = ks >> 2, kin = ks & 3;
+        umma::mma_bf16(tmem, umma::desc_sw128(q0 + qb * 8192 + kin * 32, 16, 1024),
+                       umma::desc_sw128(kk0 + qb * 16384 + kin * 32, 16, 1024), id1, ks > 0);
+      }
+      umma::mma_commit(&bars[1]);
+    }
     // [wgX | wbXp]: scale each row s of X / Xp (a 16-byte chunk at byte offset o lies in row o / 128)
     for (int i = tid; i < 1024; i += kTcThreads) {
       const int tile = i >> 9;
@@ -175,14 +189,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
     __syncthreads();
     if (tid == 0) {
       umma::fence_after_sync();
-      const uint32_t q0 = umma::smem_u32(sQ), kk0 = umma::smem_u32(sKK), xs0 = umma::smem_u32(sXs);
-      constexpr uint32_t id1 = umma::idesc_bf16(64, 128, false, false);
-#pragma unroll
-      for (int ks = 0; ks < NS / 16; ++ks) {
-        const uint32_t qb = ks >> 2, kin = ks & 3;
-        umma::mma_bf16(tmem, umma::desc_sw128(q0 + qb * 8192 + kin * 32, 16, 1024),
-                       umma::desc_sw128(kk0 + qb * 16384 + kin * 32, 16, 1024), id1, ks > 0);
-      }
+      const uint32_t kk0 = umma::smem_u32(sKK), xs0 = umma::smem_u32(sXs);
       constexpr uint32_t id3 = umma::idesc_bf16(NS, 64, true, true);
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
@@ -190,8 +197,9 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
         umma::mma_bf16(tmem + 192, umma::desc_sw128(kk0 + part * 8192 + kin * 2048, 16384, 1024),
                        umma::desc_sw128(xs0 + part * 8192 + kin * 2048, 8192, 1024), id3, ks > 0);
       }
-      umma::mma_commit(&bars[1]);
+      umma::mma_commit(&bars[4]);
     }
+    // the score epilogue needs only MMA1; MMA3 (chunk state) finishes meanwhile
     ok = __syncthreads_and(umma::mbar_wait(&bars[1], 0, p.status));
   }
   if (ok) {
@@ -241,9 +249,14 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
     }
     __syncthreads();
     ok = misc[2] == kFlagReady;
-    if (!ok) umma::mbar_wait(&bars[2], 0, p.status);  // let MMA2 finish before TMEM is freed
+    if (!ok) {  // let the MMAs finish before TMEM is freed
+      umma::mbar_wait(&bars[2], 0, p.status);
+      umma::mbar_wait(&bars[4], 0, p.status);
+    }
   }
+  if (ok) ok = __syncthreads_and(umma::mbar_wait(&bars[4], 0, p.status));  // S_loc ready
   if (ok) {
+    umma::fence_after_sync();
     // state hand-off: S_in[j+1] = e^{c_L} S_in[j] + S_loc (mamba3.py:52)
     const int sp = warp & 3, ph = warp >> 2;
     const bool rows128 = (NS == 128);
@@ -281,6 +294,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
     __threadfence();
     __syncthreads();
     if (tid == 0) st_release(&flags[j + 1], kFlagReady);
+    umma::mbar_wait(&bars[2], 0, p.status);  // MMA2 has read the scores that share the S_in tile
     if (active) {
       // S_in[j] in bf16: B operand of MMA4 ([n][p], p contiguous) and the saved state
       uint4 pk[4];
@@ -584,7 +598,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
                        umma::desc_sw128(sin0 + ks * 2048, 8192, 1024), idh, ks > 0);
       }
     }
-    scale_rows(sXX, sXW, 16384, s_wgb, tid);  // [wgX | wbXp]
     scale_rows(sDY, sDYE, 8192, s_ec, tid);   // e^{c_t} dY
     umma::fence_proxy_async_smem();
     umma::fence_before_sync();
@@ -697,6 +710,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
       umma::mma_commit(&bars[2]);
       misc[2] = (j == p.nc - 1) ? kFlagReady : wait_flag(&flags[j + 1], p.status);
     }
+    // [wgX | wbXp] is needed only after the hand-off: build it while thread 0 waits for it
+    scale_rows(sXX, sXW, 16384, s_wgb, tid);
     __syncthreads();
     ok = misc[2] == kFlagReady;
     if (!ok) umma::mbar_wait(&bars[2], 0, p.status);
