@@ -317,31 +317,65 @@ def run_ours(args):
     tokens_per_step = shape.B * shape.T if cp else shape.B * shape.T * world
     value = tokens_per_step / (ms_per_step / 1e3)
 
-    # end-to-end through the public API with host buffers (pinned), copies inside the timed region
+    # End-to-end through the public API with host buffers (pinned).  Every step copies its inputs and
+    # dy in (host -> device) and y plus all eight gradients out (device -> host) inside the timed
+    # region.  Copies run on their own streams with two device buffer sets, so step i+1's inputs
+    # and step i-1's outputs cross PCIe while step i computes, as a data pipeline would.
     host = {n: inp[n].cpu().pin_memory() for n in NAMES + ("dy",)}
-    outs = {n: torch.empty(host[n].shape, dtype=host[n].dtype).pin_memory() for n in ("x",) + NAMES}
+    outs = [{n: torch.empty(host["x" if n == "y" else n].shape, dtype=host["x" if n == "y" else n].dtype).pin_memory()
+             for n in ("y",) + NAMES} for _ in range(2)]
     h2d = sum(v.numel() * v.element_size() for v in host.values())
-    d2h = sum(v.numel() * v.element_size() for v in outs.values())
+    d2h = sum(v.numel() * v.element_size() for v in outs[0].values())
+    cur = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    dbuf = [{n: torch.empty_like(inp[n]) for n in NAMES + ("dy",)} for _ in range(2)]
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_free = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+    for e in ev_free:
+        e.record(cur)
 
-    def e2e_step():
-        leaves = [host[n].to(dev, non_blocking=True).requires_grad_() for n in NAMES]
-        d = host["dy"].to(dev, non_blocking=True)
+    def issue_h2d(i):
+        k = i % 2
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_free[k])  # step i-2 has finished with buffer set k
+            for n in NAMES + ("dy",):
+                dbuf[k][n].copy_(host[n], non_blocking=True)
+            ev_in[k].record(s_in)
+
+    def compute_and_d2h(i):
+        k = i % 2
+        cur.wait_event(ev_in[k])
+        leaves = [dbuf[k][n].detach().requires_grad_() for n in NAMES]
         y = zenith_b200.parallel.cp_ssd(*leaves, chunk) if cp else zenith_b200.ssd(*leaves, chunk)
-        y.backward(d)
-        outs["x"].copy_(y.detach(), non_blocking=True)  # y shares x's shape/dtype
-        for n, lf in zip(NAMES, leaves):
-            outs[n].copy_(lf.grad, non_blocking=True)
+        y.backward(dbuf[k]["dy"])
+        ev_free[k].record(cur)
+        ev_done[k].record(cur)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_done[k])
+            outs[k]["y"].copy_(y.detach(), non_blocking=True)
+            y.record_stream(s_out)
+            for n, lf in zip(NAMES, leaves):
+                outs[k][n].copy_(lf.grad, non_blocking=True)
+                lf.grad.record_stream(s_out)
+
+    def e2e_run(steps):
+        issue_h2d(0)
+        for i in range(steps):
+            if i + 1 < steps:
+                issue_h2d(i + 1)
+            compute_and_d2h(i)
+        cur.wait_stream(s_out)
 
     e2e_steps = max(3, min(args.steps, 10))
-    for _ in range(2):
-        e2e_step()
+    e2e_run(2)
     torch.cuda.synchronize()
     barrier()
     s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    e2.record()
+    s2.record(cur)
+    s_in.wait_event(s2)
+    e2e_run(e2e_steps)
+    e2.record(cur)
     torch.cuda.synchronize()
     zenith_b200.check_status(dev)
     t2 = torch.tensor([s2.elapsed_time(e2)], device=dev)
