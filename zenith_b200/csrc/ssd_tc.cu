@@ -395,8 +395,8 @@ struct BwdSmem {
   static constexpr uint32_t GN = XW + 16384;        // [NS n][64 p]
   static constexpr uint32_t SCAL = GN + NS * 128;   // c ec w wg wb g b (64 floats each)
   static constexpr uint32_t RED = SCAL + 7 * 256;
-  // RED: rowZ[2][64] | colZ[4][128] | colE[4][128] | xu[2][128] | dcint[64] | da[8] | tmp[8]
-  static constexpr uint32_t RED_FLOATS = 128 + 512 + 512 + 256 + 64 + 8 + 8;
+  // RED: rowZ[4][64] | colZ[4][128] | colE[4][128] | xu[4][128] | dcint[2][64] | da[16] | tmp[8]
+  static constexpr uint32_t RED_FLOATS = 256 + 512 + 512 + 512 + 128 + 16 + 8;
   static constexpr uint32_t BAR = RED + RED_FLOATS * 4;
   static constexpr uint32_t MISC = BAR + 4 * 8;
   static constexpr uint32_t TOTAL = MISC + 16;
@@ -425,10 +425,12 @@ struct TcBwdParams {
   int32_t* status;
 };
 
+constexpr int kBwdThreads = 512;
+
 // scale each 128-byte row r of a bf16 tile by f[r] (rows = bytes / 128), src -> dst
 __device__ __forceinline__ void scale_rows(const unsigned char* src, unsigned char* dst, uint32_t bytes, const float* f,
                                            int tid) {
-  for (uint32_t off = (uint32_t)tid * 16u; off < bytes; off += kTcThreads * 16u) {
+  for (uint32_t off = (uint32_t)tid * 16u; off < bytes; off += kBwdThreads * 16u) {
     const float s = f[off >> 7];
     const uint4 v = *reinterpret_cast<const uint4*>(src + off);
     uint4 o;
@@ -476,9 +478,19 @@ __device__ __forceinline__ void stage_row32(unsigned char* tile, int r, int c0, 
                    pack_bf16(v[8 * qd + 4], v[8 * qd + 5]), pack_bf16(v[8 * qd + 6], v[8 * qd + 7]));
 }
 
+// 16 floats -> bf16 into chunks c0, c0 + 1 of row r of a 128-byte-swizzled staging tile
+__device__ __forceinline__ void stage_row16(unsigned char* tile, int r, int c0, const float* v) {
+#pragma unroll
+  for (int qd = 0; qd < 2; ++qd)
+    *reinterpret_cast<uint4*>(tile + umma::sw128_offset(r, c0 + qd)) =
+        make_uint4(pack_bf16(v[8 * qd], v[8 * qd + 1]), pack_bf16(v[8 * qd + 2], v[8 * qd + 3]),
+                   pack_bf16(v[8 * qd + 4], v[8 * qd + 5]), pack_bf16(v[8 * qd + 6], v[8 * qd + 7]));
+}
 
+// 512 threads: the lane-parallel epilogues split four ways per TMEM sub-partition (warp w reads
+// the lanes of sub-partition w % 4; w / 4 picks a column quarter).
 template <int NS>
-__global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_constant__ TcBwdParams p) {
+__global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid_constant__ TcBwdParams p) {
   using S = BwdSmem<NS>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -498,13 +510,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
   float* s_wgb = s_c + 192;  // [wg (64) | wb (64)]
   float* s_g = s_c + 320;
   float* s_b = s_c + 384;
-  float* s_rowZ = reinterpret_cast<float*>(sm + S::RED);  // [2][64]
-  float* s_colZ = s_rowZ + 128;                           // [4][128]
+  float* s_rowZ = reinterpret_cast<float*>(sm + S::RED);  // [2 column block][2 half][64]
+  float* s_colZ = s_rowZ + 256;                           // [4][128]
   float* s_colE = s_colZ + 512;                           // [4][128]
-  float* s_xu = s_colE + 512;                             // [2][128]
-  float* s_dcint = s_xu + 256;                            // [64]
-  float* s_da = s_dcint + 64;                             // [8]
-  float* s_tmp = s_da + 8;                                // [8]
+  float* s_xu = s_colE + 512;                             // [4][128]
+  float* s_dcint = s_xu + 512;                            // [2][64]
+  float* s_da = s_dcint + 128;                            // [16]
+  float* s_tmp = s_da + 16;                               // [8]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::BAR);
   uint32_t* misc = reinterpret_cast<uint32_t*>(sm + S::MISC);
 
@@ -554,7 +566,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
     s_b[tid] = p.beta[b * p.bsb + t * p.bst + h * p.bsh];
     s_c[tid] = warp_incl_scan(a, lane);
   }
-  for (int i = tid; i < S::RED_FLOATS; i += kTcThreads) s_rowZ[i] = 0.f;
+  for (int i = tid; i < S::RED_FLOATS; i += kBwdThreads) s_rowZ[i] = 0.f;
   __syncthreads();
   if (tid >= 32 && tid < 64) s_c[tid] += s_c[31];
   __syncthreads();
@@ -625,17 +637,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
   if (ok) {
     umma::fence_after_sync();
     // score-gradient epilogue.  Warp w: sub-partition sp = w % 4 (rows t = 16 sp + lane % 16),
-    // half = w / 4 (0: K part with gamma, 1: Kp part with beta).  TMEM gives lanes 0-15 the S row
-    // and lanes 16-31 the dA row; one swap per column pair hands lanes 0-15 columns 0-15 and
-    // lanes 16-31 columns 16-31 of each 32-column block, so every lane works.
-    const int sp = warp & 3, half = warp >> 2;
+    // half = (w / 4) % 2 (0: K part with gamma, 1: Kp part with beta), 32-column block cc = w / 8.
+    // TMEM gives lanes 0-15 the S row and lanes 16-31 the dA row; one swap per column pair hands
+    // lanes 0-15 columns 0-15 and lanes 16-31 columns 16-31 of the block, so every lane works.
+    const int sp = warp & 3, half = (warp >> 2) & 1, cc = warp >> 3;
     const int t = 16 * sp + (lane & 15);
     const bool hiL = lane >= 16;
     const float* coef = half ? s_b : s_g;
     const float ct = s_c[t];
     float rowZ = 0.f;
-#pragma unroll
-    for (int cc = 0; cc < 2; ++cc) {
+    {
       float v[32];
       umma::tmem_ld32(R0 + ((uint32_t)(32 * sp) << 16) + half * 64 + cc * 32, v);
       float zc[16], ecs[16];
@@ -679,7 +690,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
       }
     }
     rowZ += __shfl_xor_sync(0xffffffffu, rowZ, 16);
-    if (lane < 16) s_rowZ[half * 64 + t] = rowZ;
+    if (lane < 16) s_rowZ[(cc * 2 + half) * 64 + t] = rowZ;
     umma::fence_proxy_async_smem();
     umma::fence_before_sync();
     __syncthreads();
@@ -718,36 +729,37 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
   }
   if (ok) {
     // reverse state hand-off: G[j] = dSl'^T + e^{c_L} G[j+1];  da = <G[j+1], S_in[j]>
-    const int sp = warp & 3, ph = warp >> 2;
+    // warp w: sub-partition sp = w % 4 (state rows n), p-quarter pq = w / 4 (16 columns)
+    const int sp = warp & 3, pq = warp >> 2;
     const bool rows128 = (NS == 128);
     const int n = rows128 ? 32 * sp + lane : 16 * sp + (lane & 15);
     const bool active = rows128 || lane < 16;
-    float ds[32], gn[32];
-    umma::tmem_ld32(R4 + ((uint32_t)(32 * sp) << 16) + 32 * ph, ds);
+    float ds[16], gn[16];
+    umma::tmem_ld16(R4 + ((uint32_t)(32 * sp) << 16) + 16 * pq, ds);
     float da_part = 0.f;
     if (active) {
       // ring slots are [p/4][n][4]; the caller's dfinal / dinitial states are [p][n]
       const int64_t PN = (int64_t)kP * NS;
       if (j == p.nc - 1) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) gn[i] = p.dfin ? __ldcg(p.dfin + bh * PN + (32 * ph + i) * NS + n) : 0.f;
+        for (int i = 0; i < 16; ++i) gn[i] = p.dfin ? __ldcg(p.dfin + bh * PN + (16 * pq + i) * NS + n) : 0.f;
       } else {
-        const float4* s4 = reinterpret_cast<const float4*>(p.ring + (bh * 2 + ((j + 1) & 1)) * PN) + 8 * ph * NS + n;
+        const float4* s4 = reinterpret_cast<const float4*>(p.ring + (bh * 2 + ((j + 1) & 1)) * PN) + 4 * pq * NS + n;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < 4; ++q) {
           const float4 v = __ldcg(s4 + q * NS);
           gn[4 * q] = v.x; gn[4 * q + 1] = v.y; gn[4 * q + 2] = v.z; gn[4 * q + 3] = v.w;
         }
       }
       float* dinit = (j == 0 && p.dinit) ? p.dinit + bh * PN : nullptr;
-      float4* d4 = reinterpret_cast<float4*>(p.ring + (bh * 2 + (j & 1)) * PN) + 8 * ph * NS + n;
+      float4* d4 = reinterpret_cast<float4*>(p.ring + (bh * 2 + (j & 1)) * PN) + 4 * pq * NS + n;
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
+      for (int q = 0; q < 4; ++q)
         d4[q * NS] = make_float4(ds[4 * q] + a_chunk * gn[4 * q], ds[4 * q + 1] + a_chunk * gn[4 * q + 1],
                                  ds[4 * q + 2] + a_chunk * gn[4 * q + 2], ds[4 * q + 3] + a_chunk * gn[4 * q + 3]);
       if (dinit) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) dinit[(32 * ph + i) * NS + n] = ds[i] + a_chunk * gn[i];
+        for (int i = 0; i < 16; ++i) dinit[(16 * pq + i) * NS + n] = ds[i] + a_chunk * gn[i];
       }
     }
     // publish G[j] first; Gn in bf16 and <Gn, S_in> are off the chain's critical path
@@ -756,12 +768,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
     if (tid == 0) st_release(&flags[j], kFlagReady);
     if (active) {
 #pragma unroll
-      for (int qd = 0; qd < 4; ++qd) {
+      for (int qd = 0; qd < 2; ++qd) {
         float sv[8];
-        load_chunk(sSin, n, 4 * ph + qd, sv);
+        load_chunk(sSin, n, 2 * pq + qd, sv);
 #pragma unroll
         for (int e = 0; e < 8; ++e) da_part += gn[8 * qd + e] * sv[e];
-        *reinterpret_cast<uint4*>(sGN + umma::sw128_offset(n, 4 * ph + qd)) =
+        *reinterpret_cast<uint4*>(sGN + umma::sw128_offset(n, 2 * pq + qd)) =
             make_uint4(pack_bf16(gn[8 * qd], gn[8 * qd + 1]), pack_bf16(gn[8 * qd + 2], gn[8 * qd + 3]),
                        pack_bf16(gn[8 * qd + 4], gn[8 * qd + 5]), pack_bf16(gn[8 * qd + 6], gn[8 * qd + 7]));
       }
@@ -795,7 +807,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
   }
   if (ok) {
     umma::fence_after_sync();
-    const int sp = warp & 3, ch = warp >> 2;
+    // warp w: sub-partition sp = w % 4, column quarter cq = w / 4
+    const int sp = warp & 3, cq = warp >> 2;
     // Output tiles are staged (bf16, 128-byte swizzle) in shared memory that is dead by now and
     // leave through TMA stores: dq -> Q tile, dk | dkp -> K/Kp tiles, dx | dxp -> [A|Ap] tile.
     unsigned char* st_dq = sQ;
@@ -803,58 +816,52 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
     unsigned char* st_dkp = sKK + S::QB * 8192;
     unsigned char* st_dx = sPS;
     unsigned char* st_dxp = sPS + 8192;
-    // (1) dQ rows (R1 lanes +0) and, for warps 0-3, Ye rows (R1 lanes +16) for the dc inter term
-    {
+    // (1) dQ rows (R1 lanes +0, columns [32 cq, 32 cq + 32)) and, for cq < 2, Ye rows (R1 lanes
+    // +16, same columns) for the dc inter term
+    if (32 * cq < NS) {
       const int t = 16 * sp + (lane & 15);
-      const uint32_t base = R1 + ((uint32_t)(32 * sp) << 16) + 64 * ch;
-      float v0[32], v1[32];
-      umma::tmem_ld32x2(base, base + 32, v0, v1);
-      if (lane < 16 && 64 * ch < NS) {
-        stage_row32(st_dq + ch * 8192, t, 0, v0);
-        stage_row32(st_dq + ch * 8192, t, 4, v1);
-      }
-      if (lane >= 16 && ch == 0) {
+      float v[32];
+      umma::tmem_ld32(R1 + ((uint32_t)(32 * sp) << 16) + 32 * cq, v);
+      if (lane < 16) stage_row32(st_dq + (cq >> 1) * 8192, t, 4 * (cq & 1), v);
+      if (lane >= 16 && cq < 2) {
         float acc = 0.f;
 #pragma unroll
         for (int qd = 0; qd < 4; ++qd) {
-          float d0[8], d1[8];
-          load_chunk(sDY, t, qd, d0);
-          load_chunk(sDY, t, 4 + qd, d1);
+          float d[8];
+          load_chunk(sDY, t, 4 * cq + qd, d);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc += d0[e] * v0[8 * qd + e] + d1[e] * v1[8 * qd + e];
+          for (int e = 0; e < 8; ++e) acc += d[e] * v[8 * qd + e];
         }
-        s_dcint[t] = s_ec[t] * acc;
+        s_dcint[cq * 64 + t] = s_ec[t] * acc;
       }
     }
-    // (2) dx / dxp rows: dXc (R2) + w g U (R3); x.U partial sums for dgamma / dbeta
+    // (2) dx / dxp rows: dXc (R2) + w g U (R3), columns [16 cq, 16 cq + 16); x.U partial sums for
+    // dgamma / dbeta
     {
       const int r = 32 * sp + lane;  // 0-63: s of X, 64-127: s of Xp
-      float dxc[32], u[32];
-      umma::tmem_ld32x2(R2 + ((uint32_t)(32 * sp) << 16) + 32 * ch, R3 + ((uint32_t)(32 * sp) << 16) + 32 * ch, dxc, u);
+      float dxc[16], u[16];
+      umma::tmem_ld16x2(R2 + ((uint32_t)(32 * sp) << 16) + 16 * cq, R3 + ((uint32_t)(32 * sp) << 16) + 16 * cq, dxc, u);
       const float wgt = s_wgb[r];  // wg for X rows, wb for Xp rows
       float xu = 0.f;
 #pragma unroll
-      for (int qd = 0; qd < 4; ++qd) {
+      for (int qd = 0; qd < 2; ++qd) {
         float xv[8];
-        load_chunk(sXX, r, 4 * ch + qd, xv);
+        load_chunk(sXX, r, 2 * cq + qd, xv);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           xu += xv[e] * u[8 * qd + e];
           dxc[8 * qd + e] += wgt * u[8 * qd + e];
         }
       }
-      s_xu[ch * 128 + r] = xu;
-      stage_row32(r < 64 ? st_dx : st_dxp, r & 63, 4 * ch, dxc);
+      s_xu[cq * 128 + r] = xu;
+      stage_row16(r < 64 ? st_dx : st_dxp, r & 63, 2 * cq, dxc);
     }
-    // (3) dk / dkp rows (R0)
-    if (64 * ch < NS) {
+    // (3) dk / dkp rows (R0), columns [32 cq, 32 cq + 32)
+    if (32 * cq < NS) {
       const int r = 32 * sp + lane;
-      const uint32_t base = R0 + ((uint32_t)(32 * sp) << 16) + 64 * ch;
-      float v0[32], v1[32];
-      umma::tmem_ld32x2(base, base + 32, v0, v1);
-      unsigned char* tile = (r < 64 ? st_dk : st_dkp) + ch * 8192;
-      stage_row32(tile, r & 63, 0, v0);
-      stage_row32(tile, r & 63, 4, v1);
+      float v[32];
+      umma::tmem_ld32(R0 + ((uint32_t)(32 * sp) << 16) + 32 * cq, v);
+      stage_row32((r < 64 ? st_dk : st_dkp) + (cq >> 1) * 8192, r & 63, 4 * (cq & 1), v);
     }
     umma::fence_proxy_async_smem();
     __syncthreads();
@@ -875,21 +882,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) ssd_bwd_tc_kernel(const __grid_
       const int s = tid;
       float da = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) da += s_da[i];
-      const float xu = s_xu[s] + s_xu[128 + s];
-      const float xpu = s_xu[64 + s] + s_xu[192 + s];
-      float colZ = 0.f, colEg = 0.f, colEb = 0.f;
+      for (int i = 0; i < 16; ++i) da += s_da[i];
+      float xu = 0.f, xpu = 0.f, colZ = 0.f, colEg = 0.f, colEb = 0.f, rowZ = 0.f;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
+        xu += s_xu[q * 128 + s];
+        xpu += s_xu[q * 128 + 64 + s];
         colZ += s_colZ[q * 128 + s] + s_colZ[q * 128 + 64 + s];
         colEg += s_colE[q * 128 + s];
         colEb += s_colE[q * 128 + 64 + s];
+        rowZ += s_rowZ[q * 64 + s];
       }
       const float w = s_w[s];
       const float dw = s_g[s] * xu + s_b[s] * xpu;
       const float dg = colEg + w * xu;
       const float db = colEb + w * xpu;
-      float dc = s_rowZ[s] + s_rowZ[64 + s] - colZ + s_dcint[s] - w * dw;
+      float dc = rowZ - colZ + s_dcint[s] + s_dcint[64 + s] - w * dw;
       // dc_{L-1} += e^{c_L} da + sum_s w_s dw_s   (two warps: combine through shared memory)
       const float wdw = warp_sum(w * dw);
       if (lane == 0) s_tmp[warp] = wdw;
@@ -1247,7 +1255,7 @@ int launch_bwd(const zb_ssd_args* a, ChainSync sync, void* ring, cudaStream_t st
   const int smem = (int)BwdSmem<NS>::ALLOC;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return ZB_ERR_CUDA;
   const dim3 grid((unsigned)(a->B * a->H * p.nc));
-  k<<<grid, kTcThreads, smem, stream>>>(p);
+  k<<<grid, kBwdThreads, smem, stream>>>(p);
   note_launches(1);
   return cudaPeekAtLastError() == cudaSuccess ? ZB_OK : ZB_ERR_CUDA;
 }
