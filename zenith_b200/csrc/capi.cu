@@ -56,6 +56,8 @@ int validate(const zb_ssd_args* a, bool backward) {
     return ZB_ERR_SHAPE;
   if (a->T % a->chunk_size != 0) return ZB_ERR_SHAPE;  // mamba3.py:33
   if (a->H % a->G != 0) return ZB_ERR_SHAPE;
+  // work units are numbered in 32 bits on the device
+  if ((double)a->B * (double)a->H * (double)a->T > 2147483647.0) return ZB_ERR_SHAPE;
   const size_t e = dtype_size(a->dtype), es = dtype_size(a->scalar_dtype);
   if (!e || !es) return ZB_ERR_DTYPE;
   if ((a->dtype == ZB_F64) != (a->scalar_dtype == ZB_F64)) return ZB_ERR_DTYPE;

@@ -119,6 +119,26 @@ struct ChainSync {
 };
 
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// The (batch, head, chunk) unit of ticket tk, tickets in chunk-major order:
+// tk = chunk * (B*H) + b * H + h.  32-bit arithmetic (64-bit division is a long software
+// routine); the argument checks bound B*H*T below 2^31.
+struct UnitIdx {
+  int chunk, b, h, g;
+  uint32_t bh;
+};
+__device__ __forceinline__ UnitIdx decode_ticket(uint32_t tk, int64_t B, int64_t H, int64_t G) {
+  const uint32_t h32 = (uint32_t)H, bh32 = (uint32_t)B * h32;
+  UnitIdx u;
+  const uint32_t c = tk / bh32;
+  u.chunk = (int)c;
+  u.bh = tk - c * bh32;
+  const uint32_t b = u.bh / h32;
+  u.b = (int)b;
+  u.h = (int)(u.bh - b * h32);
+  u.g = (int)((uint32_t)u.h / (h32 / (uint32_t)G));
+  return u;
+}
 inline size_t chain_sync_bytes(int64_t n_flags) { return align_up(256 + (size_t)n_flags * sizeof(int), 256); }
 
 // ---------------------------------------------------------------------------------------------

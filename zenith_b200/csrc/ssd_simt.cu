@@ -60,11 +60,9 @@ __global__ void __launch_bounds__(kThreads) ssd_fwd_simt_kernel(const SimtParams
   const bool state_only = (p.flags & ZB_FLAG_STATE_ONLY) != 0;
   if (tid == 0) s_ticket = (int)atomicAdd(p.sync.ticket, 1u);
   __syncthreads();
-  const int64_t BH = p.B * p.H;
-  const int64_t tk = s_ticket;
-  const int j = (int)(tk / BH);
-  const int64_t bh = tk % BH;
-  const int64_t b = bh / p.H, h = bh % p.H, g = h / (p.H / p.G);
+  const UnitIdx u = decode_ticket((uint32_t)s_ticket, p.B, p.H, p.G);
+  const int j = u.chunk;
+  const int64_t bh = u.bh, b = u.b, h = u.h, g = u.g;
   const int64_t t0 = (int64_t)j * L;
   const int Lc = (int)min((int64_t)L, p.T - t0);
   int* flags = p.sync.flags + bh * (p.nc + 1);
@@ -221,11 +219,9 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
   const bool state_only = (p.flags & ZB_FLAG_STATE_ONLY) != 0;
   if (tid == 0) s_ticket = (int)atomicAdd(p.sync.ticket, 1u);
   __syncthreads();
-  const int64_t BH = p.B * p.H;
-  const int64_t tk = s_ticket;
-  const int j = p.nc - 1 - (int)(tk / BH);
-  const int64_t bh = tk % BH;
-  const int64_t b = bh / p.H, h = bh % p.H, g = h / (p.H / p.G);
+  const UnitIdx u = decode_ticket((uint32_t)s_ticket, p.B, p.H, p.G);
+  const int j = p.nc - 1 - u.chunk;
+  const int64_t bh = u.bh, b = u.b, h = u.h, g = u.g;
   const int64_t t0 = (int64_t)j * L;
   const int Lc = (int)min((int64_t)L, p.T - t0);
   int* flags = p.sync.flags + bh * (p.nc + 1);

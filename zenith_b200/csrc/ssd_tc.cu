@@ -17,6 +17,7 @@
 // states the backward needs are saved in bf16 [B*H][nc][N][P].
 #include <cuda.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "ssd_tc.h"
@@ -113,12 +114,10 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tmem = misc[0];
-  const int64_t BH = p.B * p.H;
-  const int64_t tk = misc[1];
-  const int j = (int)(tk / BH);
-  const int64_t bh = tk % BH;
-  const int b = (int)(bh / p.H), h = (int)(bh % p.H);
-  const int g = (int)(h / (p.H / p.G));
+  const UnitIdx u = decode_ticket(misc[1], p.B, p.H, p.G);
+  const int j = u.chunk;
+  const int64_t bh = u.bh;
+  const int b = u.b, h = u.h, g = u.g;
   const int t0 = j * kL;
   int* flags = p.flags + bh * (p.nc + 1);
 
@@ -364,7 +363,8 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
 // ---------------------------------------------------------------------------------------------
 // backward
 //
-// One CTA per (batch, head, chunk), chunks taken in reverse order, 256 threads, 512 TMEM columns.
+// Persistent CTAs (one per SM) take the (batch, head, chunk) units in reverse chunk order, 512
+// threads, 512 TMEM columns.
 //   MMA b  S      = Q [K;Kp]^T          M=64  N=128 K=N   -> R0 lanes +0
 //   MMA a  dA     = dY [X;Xp]^T         M=64  N=128 K=64  -> R0 lanes +16
 //   MMA g  dSl'   = Q^T dYe             M=N   N=64  K=64  -> R4     (dYe = e^{c_t} dY)
@@ -383,24 +383,25 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
 template <int NS>
 struct BwdSmem {
   static constexpr int QB = NS / 64;
-  static constexpr uint32_t Q = 0;                  // [QB][64 t][64 n]
-  static constexpr uint32_t KK = Q + QB * 8192;     // [QB][K | Kp]
-  static constexpr uint32_t XX = KK + QB * 16384;   // [X | Xp]  (128 rows)
+  // one input stage (two of them: the next chunk's operands land while this one is worked on)
+  static constexpr uint32_t Q = 0;                  // [QB][64 t][64 n]; at the end the dq staging tile
+  static constexpr uint32_t KK = Q + QB * 8192;     // [QB][K | Kp]; at the end the dk | dkp staging tiles
+  static constexpr uint32_t XX = KK + QB * 16384;   // [X | Xp]  (128 rows); at the end dx | dxp
   static constexpr uint32_t DY = XX + 16384;
   static constexpr uint32_t SIN = DY + 8192;        // [NS n][64 p]
-  static constexpr uint32_t PS = SIN + NS * 128;    // [A | Ap]   [2][64 t][64 s]
-  static constexpr uint32_t EG = PS + 16384;        // [Eg | Epb] [2][64 t][64 s]
-  static constexpr uint32_t DYE = EG + 16384;
-  static constexpr uint32_t XW = DYE + 8192;        // [wgX | wbXp] (128 rows)
-  static constexpr uint32_t GN = XW + 16384;        // [NS n][64 p]
-  static constexpr uint32_t SCAL = GN + NS * 128;   // c ec w wg wb g b (64 floats each)
-  static constexpr uint32_t RED = SCAL + 7 * 256;
+  static constexpr uint32_t STAGE = SIN + NS * 128;
+  // shared work tiles, reused phase by phase
+  static constexpr uint32_t W = 2 * STAGE;          // dYe -> [A | Ap] -> [wgX | wbXp]
+  static constexpr uint32_t E = W + 16384;          // [Eg | Epb] -> Gn [NS n][64 p]
+  static constexpr uint32_t SCAL = E + 16384;       // c ec w wg wb g b, next chunk's adt g b (64 floats each)
+  static constexpr uint32_t RED = SCAL + 10 * 256;
   // RED: rowZ[4][64] | colZ[4][128] | colE[4][128] | xu[4][128] | dcint[2][64] | da[16] | tmp[8]
   static constexpr uint32_t RED_FLOATS = 256 + 512 + 512 + 512 + 128 + 16 + 8;
-  static constexpr uint32_t BAR = RED + RED_FLOATS * 4;
-  static constexpr uint32_t MISC = BAR + 4 * 8;
+  static constexpr uint32_t BAR = RED + RED_FLOATS * 4;  // stage loads [2], MMA groups 1-3
+  static constexpr uint32_t MISC = BAR + 5 * 8;          // tmem base, ticket, chain result, next ticket
   static constexpr uint32_t TOTAL = MISC + 16;
   static constexpr uint32_t ALLOC = TOTAL + 1024;
+  static_assert(STAGE % 1024 == 0, "swizzled tiles need 1024-byte alignment");
 };
 
 struct TcBwdParams {
@@ -487,29 +488,77 @@ __device__ __forceinline__ void stage_row16(unsigned char* tile, int r, int c0, 
                    pack_bf16(v[8 * qd + 4], v[8 * qd + 5]), pack_bf16(v[8 * qd + 6], v[8 * qd + 7]));
 }
 
-// 512 threads: the lane-parallel epilogues split four ways per TMEM sub-partition (warp w reads
-// the lanes of sub-partition w % 4; w / 4 picks a column quarter).
+// Persistent: one CTA per SM walks the chunks in ticket order (reverse chunk order), 512 threads.
+// While a chunk is worked on, the next ticket's operands load into the other input stage.  Each
+// CTA takes its tickets in increasing order and a chunk only waits on a lower ticket, so the
+// lowest unfinished ticket always belongs to a CTA that can run it: no deadlock.
+// The lane-parallel epilogues split four ways per TMEM sub-partition (warp w reads the lanes of
+// sub-partition w % 4; w / 4 picks a column quarter).
+struct BwdChunk {
+  int j, b, h, g, t0;
+  int64_t bh;
+};
+
+__device__ __forceinline__ BwdChunk bwd_chunk(const TcBwdParams& p, uint32_t tk) {
+  const UnitIdx u = decode_ticket(tk, p.B, p.H, p.G);
+  BwdChunk c;
+  c.j = p.nc - 1 - u.chunk;
+  c.bh = u.bh;
+  c.b = u.b;
+  c.h = u.h;
+  c.g = u.g;
+  c.t0 = c.j * kL;
+  return c;
+}
+
+// one chunk's operands -> an input stage: Q, [K | Kp], [X | Xp], dY (TMA) and the saved S_in image
+// (bulk copy), all completing on the stage's mbarrier
+template <int NS>
+__device__ __forceinline__ void bwd_issue_loads(const TcBwdParams& p, unsigned char* st, uint64_t* bar,
+                                                const BwdChunk& c) {
+  using S = BwdSmem<NS>;
+  constexpr uint32_t kLoadBytes = S::QB * 8192 * 3 + 3 * 8192 + NS * 128;
+  umma::mbar_arrive_expect_tx(bar, kLoadBytes);
+#pragma unroll
+  for (int qb = 0; qb < S::QB; ++qb) {
+    umma::tma_load_4d(st + S::Q + qb * 8192, &p.tq, bar, qb * 64, c.g, c.t0, c.b);
+    umma::tma_load_4d(st + S::KK + qb * 16384, &p.tk, bar, qb * 64, c.g, c.t0, c.b);
+    umma::tma_load_4d(st + S::KK + qb * 16384 + 8192, &p.tkp, bar, qb * 64, c.g, c.t0, c.b);
+  }
+  umma::tma_load_4d(st + S::XX, &p.tx, bar, 0, c.h, c.t0, c.b);
+  umma::tma_load_4d(st + S::XX + 8192, &p.txp, bar, 0, c.h, c.t0, c.b);
+  umma::tma_load_4d(st + S::DY, &p.tdy, bar, 0, c.h, c.t0, c.b);
+  umma::bulk_load(st + S::SIN, reinterpret_cast<const unsigned char*>(p.states) + (c.bh * p.nc + c.j) * (int64_t)NS * 128,
+                  NS * 128, bar);
+}
+
+// token s of a chunk: adt, gamma, beta -> dst[s], dst[64 + s], dst[128 + s] (asynchronous copies)
+__device__ __forceinline__ void bwd_prefetch_scalars(const TcBwdParams& p, const BwdChunk& c, int s, float* dst) {
+  const int t = c.t0 + s;
+  umma::cp_async4(dst + s, p.adt + (c.b * p.asb + t * p.ast + c.h * p.ash));
+  umma::cp_async4(dst + 64 + s, p.gamma + (c.b * p.gsb + t * p.gst + c.h * p.gsh));
+  umma::cp_async4(dst + 128 + s, p.beta + (c.b * p.bsb + t * p.bst + c.h * p.bsh));
+  umma::cp_async_commit();
+}
+
 template <int NS>
 __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid_constant__ TcBwdParams p) {
   using S = BwdSmem<NS>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char* sQ = sm + S::Q;
-  unsigned char* sKK = sm + S::KK;
-  unsigned char* sXX = sm + S::XX;
-  unsigned char* sDY = sm + S::DY;
-  unsigned char* sSin = sm + S::SIN;
-  unsigned char* sPS = sm + S::PS;
-  unsigned char* sEG = sm + S::EG;
-  unsigned char* sDYE = sm + S::DYE;
-  unsigned char* sXW = sm + S::XW;
-  unsigned char* sGN = sm + S::GN;
+  unsigned char* sW = sm + S::W;
+  unsigned char* sDYE = sW;  // e^{c_t} dY
+  unsigned char* sPS = sW;   // [A | Ap]   [2][64 t][64 s]
+  unsigned char* sXW = sW;   // [wgX | wbXp] (128 rows)
+  unsigned char* sEG = sm + S::E;  // [Eg | Epb] [2][64 t][64 s]
+  unsigned char* sGN = sm + S::E;  // Gn [NS n][64 p]
   float* s_c = reinterpret_cast<float*>(sm + S::SCAL);
   float* s_ec = s_c + 64;
   float* s_w = s_c + 128;
   float* s_wgb = s_c + 192;  // [wg (64) | wb (64)]
   float* s_g = s_c + 320;
   float* s_b = s_c + 384;
+  float* s_nx = s_c + 448;   // next chunk's [adt | gamma | beta]
   float* s_rowZ = reinterpret_cast<float*>(sm + S::RED);  // [2 column block][2 half][64]
   float* s_colZ = s_rowZ + 256;                           // [4][128]
   float* s_colE = s_colZ + 512;                           // [4][128]
@@ -521,9 +570,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
   uint32_t* misc = reinterpret_cast<uint32_t*>(sm + S::MISC);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t total = p.B * p.H * p.nc;
   if (tid == 0) {
     misc[1] = atomicAdd(p.ticket, 1u);
-    for (int i = 0; i < 4; ++i) umma::mbar_init(&bars[i], 1);
+    for (int i = 0; i < 5; ++i) umma::mbar_init(&bars[i], 1);
     umma::mbar_fence_init();
   }
   if (warp == 0) {
@@ -535,388 +585,409 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
   umma::fence_after_sync();
   const uint32_t tmem = misc[0];
   const uint32_t R0 = tmem, R1 = tmem + 128, R2 = tmem + 256, R3 = tmem + 320, R4 = tmem + 384;
-  const int64_t BH = p.B * p.H;
-  const int64_t tk = misc[1];
-  const int j = p.nc - 1 - (int)(tk / BH);
-  const int64_t bh = tk % BH;
-  const int b = (int)(bh / p.H), h = (int)(bh % p.H);
-  const int g = (int)(h / (p.H / p.G));
-  const int t0 = j * kL;
-  int* flags = p.flags + bh * (p.nc + 1);
+  uint32_t cur = misc[1];
+  if (tid == 0 && cur < total) bwd_issue_loads<NS>(p, sm, &bars[0], bwd_chunk(p, cur));
+  if (tid < 64 && cur < total) bwd_prefetch_scalars(p, bwd_chunk(p, cur), tid, s_nx);
 
-  constexpr uint32_t kLoadBytes = S::QB * 8192 * 3 + 3 * 8192 + NS * 128;
-  if (tid == 0) {
-    umma::mbar_arrive_expect_tx(&bars[0], kLoadBytes);
-#pragma unroll
-    for (int qb = 0; qb < S::QB; ++qb) {
-      umma::tma_load_4d(sQ + qb * 8192, &p.tq, &bars[0], qb * 64, g, t0, b);
-      umma::tma_load_4d(sKK + qb * 16384, &p.tk, &bars[0], qb * 64, g, t0, b);
-      umma::tma_load_4d(sKK + qb * 16384 + 8192, &p.tkp, &bars[0], qb * 64, g, t0, b);
+  for (uint32_t it = 0; cur < total; ++it) {
+    const int stage = it & 1;
+    const uint32_t ph = it & 1;  // parity of this chunk's MMA-group barriers
+    unsigned char* sQ = sm + stage * S::STAGE + S::Q;
+    unsigned char* sKK = sm + stage * S::STAGE + S::KK;
+    unsigned char* sXX = sm + stage * S::STAGE + S::XX;
+    unsigned char* sDY = sm + stage * S::STAGE + S::DY;
+    unsigned char* sSin = sm + stage * S::STAGE + S::SIN;
+    const BwdChunk ck = bwd_chunk(p, cur);
+    const int j = ck.j, b = ck.b, h = ck.h, g = ck.g, t0 = ck.t0;
+    const int64_t bh = ck.bh;
+    int* flags = p.flags + bh * (p.nc + 1);
+    // Thread 32 is the producer: it takes the next ticket now, and while thread 0 waits for the
+    // hand-off it drains the previous chunk's output tiles (its own TMA stores) and loads the next
+    // chunk's operands into the other stage.
+    uint32_t nx = 0, nxt = 0;
+    bool prefetched = false;
+    if (tid == 32) nx = atomicAdd(p.ticket, 1u);
+    if (tid < 64) {
+      umma::cp_async_wait_all();  // this thread's own copies
+      s_g[tid] = s_nx[64 + tid];
+      s_b[tid] = s_nx[128 + tid];
+      s_c[tid] = warp_incl_scan(s_nx[tid], lane);
     }
-    umma::tma_load_4d(sXX, &p.tx, &bars[0], 0, h, t0, b);
-    umma::tma_load_4d(sXX + 8192, &p.txp, &bars[0], 0, h, t0, b);
-    umma::tma_load_4d(sDY, &p.tdy, &bars[0], 0, h, t0, b);
-    umma::bulk_load(sSin, reinterpret_cast<const unsigned char*>(p.states) + (bh * p.nc + j) * (int64_t)NS * 128,
-                    NS * 128, &bars[0]);
-  }
-  if (tid < 64) {
-    const int t = t0 + tid;
-    const float a = p.adt[b * p.asb + t * p.ast + h * p.ash];
-    s_g[tid] = p.gamma[b * p.gsb + t * p.gst + h * p.gsh];
-    s_b[tid] = p.beta[b * p.bsb + t * p.bst + h * p.bsh];
-    s_c[tid] = warp_incl_scan(a, lane);
-  }
-  for (int i = tid; i < S::RED_FLOATS; i += kBwdThreads) s_rowZ[i] = 0.f;
-  __syncthreads();
-  if (tid >= 32 && tid < 64) s_c[tid] += s_c[31];
-  __syncthreads();
-  if (tid < 64) {
-    const float c = s_c[tid], w = expf(s_c[63] - c);
-    s_ec[tid] = expf(c);
-    s_w[tid] = w;
-    s_wgb[tid] = w * s_g[tid];
-    s_wgb[64 + tid] = w * s_b[tid];
-  }
-  const bool load_ok = umma::mbar_wait(&bars[0], 0, p.status);
-  __syncthreads();
-  const float a_chunk = expf(s_c[63]);
-  bool ok = __syncthreads_and(load_ok);
-
-  if (ok) {
-    // the products that need no rescaled operand start right away
-    if (tid == 0) {
-      umma::fence_after_sync();
-      const uint32_t q0 = umma::smem_u32(sQ), kk0 = umma::smem_u32(sKK), xx0 = umma::smem_u32(sXX);
-      const uint32_t dy0 = umma::smem_u32(sDY), sin0 = umma::smem_u32(sSin);
-      // b: S = Q [K;Kp]^T
-      constexpr uint32_t idb = umma::idesc_bf16(64, 128, false, false);
-#pragma unroll
-      for (int ks = 0; ks < NS / 16; ++ks) {
-        const uint32_t qb = ks >> 2, kin = ks & 3;
-        umma::mma_bf16(R0, umma::desc_sw128(q0 + qb * 8192 + kin * 32, 16, 1024),
-                       umma::desc_sw128(kk0 + qb * 16384 + kin * 32, 16, 1024), idb, ks > 0);
-      }
-      // a: dA = dY [X;Xp]^T
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        umma::mma_bf16(R0 + (16u << 16), umma::desc_sw128(dy0 + ks * 32, 16, 1024),
-                       umma::desc_sw128(xx0 + ks * 32, 16, 1024), idb, ks > 0);
-      // h: Ye = Q S_in^T
-      constexpr uint32_t idh = umma::idesc_bf16(64, 64, false, true);
-#pragma unroll
-      for (int ks = 0; ks < NS / 16; ++ks) {
-        const uint32_t qb = ks >> 2, kin = ks & 3;
-        umma::mma_bf16(R1 + (16u << 16), umma::desc_sw128(q0 + qb * 8192 + kin * 32, 16, 1024),
-                       umma::desc_sw128(sin0 + ks * 2048, 8192, 1024), idh, ks > 0);
-      }
-    }
-    scale_rows(sDY, sDYE, 8192, s_ec, tid);   // e^{c_t} dY
-    umma::fence_proxy_async_smem();
-    umma::fence_before_sync();
+    for (int i = tid; i < S::RED_FLOATS; i += kBwdThreads) s_rowZ[i] = 0.f;
     __syncthreads();
-    if (tid == 0) {
-      umma::fence_after_sync();
-      const uint32_t q0 = umma::smem_u32(sQ);
-      const uint32_t dye0 = umma::smem_u32(sDYE), sin0 = umma::smem_u32(sSin);
-      // g: dSl' = Q^T dYe   (M = n)
-      constexpr uint32_t idg = umma::idesc_bf16(NS, 64, true, true);
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        umma::mma_bf16(R4, umma::desc_sw128(q0 + ks * 2048, 8192, 1024), umma::desc_sw128(dye0 + ks * 2048, 8192, 1024),
-                       idg, ks > 0);
-      // d (inter part): dQ = dYe S_in
-      constexpr uint32_t idd1 = umma::idesc_bf16(64, NS, false, false);
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        umma::mma_bf16(R1, umma::desc_sw128(dye0 + ks * 32, 16, 1024), umma::desc_sw128(sin0 + ks * 32, 16, 1024), idd1,
-                       ks > 0);
-      umma::mma_commit(&bars[1]);
+    if (tid >= 32 && tid < 64) s_c[tid] += s_c[31];
+    __syncthreads();
+    if (tid < 64) {
+      const float c = s_c[tid], w = expf(s_c[63] - c);
+      s_ec[tid] = expf(c);
+      s_w[tid] = w;
+      s_wgb[tid] = w * s_g[tid];
+      s_wgb[64 + tid] = w * s_b[tid];
     }
-    ok = __syncthreads_and(umma::mbar_wait(&bars[1], 0, p.status));
-  }
-  if (ok) {
-    umma::fence_after_sync();
-    // score-gradient epilogue.  Warp w: sub-partition sp = w % 4 (rows t = 16 sp + lane % 16),
-    // half = (w / 4) % 2 (0: K part with gamma, 1: Kp part with beta), 32-column block cc = w / 8.
-    // TMEM gives lanes 0-15 the S row and lanes 16-31 the dA row; one swap per column pair hands
-    // lanes 0-15 columns 0-15 and lanes 16-31 columns 16-31 of the block, so every lane works.
-    const int sp = warp & 3, half = (warp >> 2) & 1, cc = warp >> 3;
-    const int t = 16 * sp + (lane & 15);
-    const bool hiL = lane >= 16;
-    const float* coef = half ? s_b : s_g;
-    const float ct = s_c[t];
-    float rowZ = 0.f;
-    {
-      float v[32];
-      umma::tmem_ld32(R0 + ((uint32_t)(32 * sp) << 16) + half * 64 + cc * 32, v);
-      float zc[16], ecs[16];
-      uint32_t wa[8], we[8];
-      float pa = 0.f, pe = 0.f;
+    const bool load_ok = umma::mbar_wait(&bars[stage], (it >> 1) & 1, p.status);
+    const float a_chunk = expf(s_c[63]);
+    bool ok = __syncthreads_and(load_ok);
+
+    if (ok) {
+      // the products that need no rescaled operand start right away
+      if (tid == 0) {
+        umma::fence_after_sync();
+        const uint32_t q0 = umma::smem_u32(sQ), kk0 = umma::smem_u32(sKK), xx0 = umma::smem_u32(sXX);
+        const uint32_t dy0 = umma::smem_u32(sDY), sin0 = umma::smem_u32(sSin);
+        // b: S = Q [K;Kp]^T
+        constexpr uint32_t idb = umma::idesc_bf16(64, 128, false, false);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float recv = __shfl_xor_sync(0xffffffffu, hiL ? v[i] : v[16 + i], 16);
-        const float sv = hiL ? recv : v[i];          // S_ts
-        const float dav = hiL ? v[16 + i] : recv;    // dA_ts
-        const int s = cc * 32 + (hiL ? 16 : 0) + i;
-        const float m = (s <= t) ? __expf(ct - s_c[s]) : 0.f;
-        const float cf = coef[s];
-        const float A = sv * cf * m;
-        const float E = dav * m;
-        const float z = dav * A;
-        rowZ += z;
-        zc[i] = z;
-        ecs[i] = E * sv;
-        const float eg = E * cf;
-        if (i & 1) {
-          wa[i >> 1] = pack_bf16(pa, A);
-          we[i >> 1] = pack_bf16(pe, eg);
-        } else {
-          pa = A;
-          pe = eg;
+        for (int ks = 0; ks < NS / 16; ++ks) {
+          const uint32_t qb = ks >> 2, kin = ks & 3;
+          umma::mma_bf16(R0, umma::desc_sw128(q0 + qb * 8192 + kin * 32, 16, 1024),
+                         umma::desc_sw128(kk0 + qb * 16384 + kin * 32, 16, 1024), idb, ks > 0);
+        }
+        // a: dA = dY [X;Xp]^T
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma::mma_bf16(R0 + (16u << 16), umma::desc_sw128(dy0 + ks * 32, 16, 1024),
+                         umma::desc_sw128(xx0 + ks * 32, 16, 1024), idb, ks > 0);
+        // h: Ye = Q S_in^T
+        constexpr uint32_t idh = umma::idesc_bf16(64, 64, false, true);
+#pragma unroll
+        for (int ks = 0; ks < NS / 16; ++ks) {
+          const uint32_t qb = ks >> 2, kin = ks & 3;
+          umma::mma_bf16(R1 + (16u << 16), umma::desc_sw128(q0 + qb * 8192 + kin * 32, 16, 1024),
+                         umma::desc_sw128(sin0 + ks * 2048, 8192, 1024), idh, ks > 0);
         }
       }
-      // column sums over the 16 rows of this half-warp; lane keeps column (lane % 16)
-      const float cz = colsum16(zc, lane), ce = colsum16(ecs, lane);
-      const int col = half * 64 + cc * 32 + (hiL ? 16 : 0) + (lane & 15);
-      s_colZ[sp * 128 + col] = cz;
-      s_colE[sp * 128 + col] = ce;
-      const int c0 = cc * 4 + (hiL ? 2 : 0);
+      scale_rows(sDY, sDYE, 8192, s_ec, tid);   // e^{c_t} dY
+      umma::fence_proxy_async_smem();
+      umma::fence_before_sync();
+      __syncthreads();
+      if (tid == 0) {
+        umma::fence_after_sync();
+        const uint32_t q0 = umma::smem_u32(sQ);
+        const uint32_t dye0 = umma::smem_u32(sDYE), sin0 = umma::smem_u32(sSin);
+        // g: dSl' = Q^T dYe   (M = n)
+        constexpr uint32_t idg = umma::idesc_bf16(NS, 64, true, true);
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        *reinterpret_cast<uint4*>(sPS + half * 8192 + umma::sw128_offset(t, c0 + q)) =
-            make_uint4(wa[4 * q], wa[4 * q + 1], wa[4 * q + 2], wa[4 * q + 3]);
-        *reinterpret_cast<uint4*>(sEG + half * 8192 + umma::sw128_offset(t, c0 + q)) =
-            make_uint4(we[4 * q], we[4 * q + 1], we[4 * q + 2], we[4 * q + 3]);
+        for (int ks = 0; ks < 4; ++ks)
+          umma::mma_bf16(R4, umma::desc_sw128(q0 + ks * 2048, 8192, 1024), umma::desc_sw128(dye0 + ks * 2048, 8192, 1024),
+                         idg, ks > 0);
+        // d (inter part): dQ = dYe S_in
+        constexpr uint32_t idd1 = umma::idesc_bf16(64, NS, false, false);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma::mma_bf16(R1, umma::desc_sw128(dye0 + ks * 32, 16, 1024), umma::desc_sw128(sin0 + ks * 32, 16, 1024), idd1,
+                         ks > 0);
+        umma::mma_commit(&bars[2]);
       }
+      ok = __syncthreads_and(umma::mbar_wait(&bars[2], ph, p.status));
     }
-    rowZ += __shfl_xor_sync(0xffffffffu, rowZ, 16);
-    if (lane < 16) s_rowZ[(cc * 2 + half) * 64 + t] = rowZ;
-    umma::fence_proxy_async_smem();
-    umma::fence_before_sync();
-    __syncthreads();
-    if (tid == 0) {
+    if (ok) {
       umma::fence_after_sync();
-      const uint32_t q0 = umma::smem_u32(sQ), kk0 = umma::smem_u32(sKK), dy0 = umma::smem_u32(sDY);
-      const uint32_t ps0 = umma::smem_u32(sPS), eg0 = umma::smem_u32(sEG);
-      // c: dXc = [A|Ap]^T dY   (M = s|s')
-      constexpr uint32_t idc = umma::idesc_bf16(128, 64, true, true);
+      // score-gradient epilogue.  Warp w: sub-partition sp = w % 4 (rows t = 16 sp + lane % 16),
+      // half = (w / 4) % 2 (0: K part with gamma, 1: Kp part with beta), 32-column block cc = w / 8.
+      // TMEM gives lanes 0-15 the S row and lanes 16-31 the dA row; one swap per column pair hands
+      // lanes 0-15 columns 0-15 and lanes 16-31 columns 16-31 of the block, so every lane works.
+      const int sp = warp & 3, half = (warp >> 2) & 1, cc = warp >> 3;
+      const int t = 16 * sp + (lane & 15);
+      const bool hiL = lane >= 16;
+      const float* coef = half ? s_b : s_g;
+      const float ct = s_c[t];
+      float rowZ = 0.f;
+      {
+        float v[32];
+        umma::tmem_ld32(R0 + ((uint32_t)(32 * sp) << 16) + half * 64 + cc * 32, v);
+        float zc[16], ecs[16];
+        uint32_t wa[8], we[8];
+        float pa = 0.f, pe = 0.f;
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        umma::mma_bf16(R2, umma::desc_sw128(ps0 + ks * 2048, 8192, 1024), umma::desc_sw128(dy0 + ks * 2048, 8192, 1024),
-                       idc, ks > 0);
-      // d (intra part): dQ += [Eg|Epb] [K;Kp]
-      constexpr uint32_t idd2 = umma::idesc_bf16(64, NS, false, true);
+        for (int i = 0; i < 16; ++i) {
+          const float recv = __shfl_xor_sync(0xffffffffu, hiL ? v[i] : v[16 + i], 16);
+          const float sv = hiL ? recv : v[i];          // S_ts
+          const float dav = hiL ? v[16 + i] : recv;    // dA_ts
+          const int s = cc * 32 + (hiL ? 16 : 0) + i;
+          const float m = (s <= t) ? __expf(ct - s_c[s]) : 0.f;
+          const float cf = coef[s];
+          const float A = sv * cf * m;
+          const float E = dav * m;
+          const float z = dav * A;
+          rowZ += z;
+          zc[i] = z;
+          ecs[i] = E * sv;
+          const float eg = E * cf;
+          if (i & 1) {
+            wa[i >> 1] = pack_bf16(pa, A);
+            we[i >> 1] = pack_bf16(pe, eg);
+          } else {
+            pa = A;
+            pe = eg;
+          }
+        }
+        // column sums over the 16 rows of this half-warp; lane keeps column (lane % 16)
+        const float cz = colsum16(zc, lane), ce = colsum16(ecs, lane);
+        const int col = half * 64 + cc * 32 + (hiL ? 16 : 0) + (lane & 15);
+        s_colZ[sp * 128 + col] = cz;
+        s_colE[sp * 128 + col] = ce;
+        const int c0 = cc * 4 + (hiL ? 2 : 0);
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t part = ks >> 2, kin = ks & 3;
-        umma::mma_bf16(R1, umma::desc_sw128(eg0 + part * 8192 + kin * 32, 16, 1024),
-                       umma::desc_sw128(kk0 + part * 8192 + kin * 2048, 16384, 1024), idd2, 1);
+        for (int q = 0; q < 2; ++q) {
+          *reinterpret_cast<uint4*>(sPS + half * 8192 + umma::sw128_offset(t, c0 + q)) =
+              make_uint4(wa[4 * q], wa[4 * q + 1], wa[4 * q + 2], wa[4 * q + 3]);
+          *reinterpret_cast<uint4*>(sEG + half * 8192 + umma::sw128_offset(t, c0 + q)) =
+              make_uint4(we[4 * q], we[4 * q + 1], we[4 * q + 2], we[4 * q + 3]);
+        }
       }
-      // e: dK = [Eg|Epb]^T Q   (M = s|s')
-      constexpr uint32_t ide = umma::idesc_bf16(128, NS, true, true);
+      rowZ += __shfl_xor_sync(0xffffffffu, rowZ, 16);
+      if (lane < 16) s_rowZ[(cc * 2 + half) * 64 + t] = rowZ;
+      umma::fence_proxy_async_smem();
+      umma::fence_before_sync();
+      __syncthreads();
+      if (tid == 0) {
+        umma::fence_after_sync();
+        const uint32_t q0 = umma::smem_u32(sQ), kk0 = umma::smem_u32(sKK), dy0 = umma::smem_u32(sDY);
+        const uint32_t ps0 = umma::smem_u32(sPS), eg0 = umma::smem_u32(sEG);
+        // c: dXc = [A|Ap]^T dY   (M = s|s')
+        constexpr uint32_t idc = umma::idesc_bf16(128, 64, true, true);
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        umma::mma_bf16(R0, umma::desc_sw128(eg0 + ks * 2048, 8192, 1024), umma::desc_sw128(q0 + ks * 2048, 8192, 1024),
-                       ide, ks > 0);
-      umma::mma_commit(&bars[2]);
-      misc[2] = (j == p.nc - 1) ? kFlagReady : wait_flag(&flags[j + 1], p.status);
+        for (int ks = 0; ks < 4; ++ks)
+          umma::mma_bf16(R2, umma::desc_sw128(ps0 + ks * 2048, 8192, 1024), umma::desc_sw128(dy0 + ks * 2048, 8192, 1024),
+                         idc, ks > 0);
+        // d (intra part): dQ += [Eg|Epb] [K;Kp]
+        constexpr uint32_t idd2 = umma::idesc_bf16(64, NS, false, true);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t part = ks >> 2, kin = ks & 3;
+          umma::mma_bf16(R1, umma::desc_sw128(eg0 + part * 8192 + kin * 32, 16, 1024),
+                         umma::desc_sw128(kk0 + part * 8192 + kin * 2048, 16384, 1024), idd2, 1);
+        }
+        // e: dK = [Eg|Epb]^T Q   (M = s|s')
+        constexpr uint32_t ide = umma::idesc_bf16(128, NS, true, true);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma::mma_bf16(R0, umma::desc_sw128(eg0 + ks * 2048, 8192, 1024), umma::desc_sw128(q0 + ks * 2048, 8192, 1024),
+                         ide, ks > 0);
+        umma::mma_commit(&bars[3]);
+        misc[2] = (j == p.nc - 1) ? kFlagReady : wait_flag(&flags[j + 1], p.status);
+      }
+      // [wgX | wbXp] takes the place of [A | Ap] once the second group has read it; it is built
+      // while thread 0 waits for the hand-off
+      if (tid == 32) {
+        misc[3] = nx;
+        umma::bulk_wait_read();  // the previous chunk's output tiles (in the other stage) are out
+        if (nx < total) {
+          bwd_issue_loads<NS>(p, sm + (stage ^ 1) * S::STAGE, &bars[stage ^ 1], bwd_chunk(p, nx));
+          prefetched = true;
+        }
+      }
+      const bool g2 = umma::mbar_wait(&bars[3], ph, p.status);
+      if (g2) scale_rows(sXX, sXW, 16384, s_wgb, tid);
+      ok = __syncthreads_and(g2) && misc[2] == kFlagReady;
+      nxt = misc[3];
+      if (tid < 64 && nxt < total) bwd_prefetch_scalars(p, bwd_chunk(p, nxt), tid, s_nx);  // for the next chunk
     }
-    // [wgX | wbXp] is needed only after the hand-off: build it while thread 0 waits for it
-    scale_rows(sXX, sXW, 16384, s_wgb, tid);
-    __syncthreads();
-    ok = misc[2] == kFlagReady;
-    if (!ok) umma::mbar_wait(&bars[2], 0, p.status);
-  }
-  if (ok) {
-    // reverse state hand-off: G[j] = dSl'^T + e^{c_L} G[j+1];  da = <G[j+1], S_in[j]>
-    // warp w: sub-partition sp = w % 4 (state rows n), p-quarter pq = w / 4 (16 columns)
-    const int sp = warp & 3, pq = warp >> 2;
-    const bool rows128 = (NS == 128);
-    const int n = rows128 ? 32 * sp + lane : 16 * sp + (lane & 15);
-    const bool active = rows128 || lane < 16;
-    float ds[16], gn[16];
-    umma::tmem_ld16(R4 + ((uint32_t)(32 * sp) << 16) + 16 * pq, ds);
-    float da_part = 0.f;
-    if (active) {
-      // ring slots are [p/4][n][4]; the caller's dfinal / dinitial states are [p][n]
-      const int64_t PN = (int64_t)kP * NS;
-      if (j == p.nc - 1) {
+    if (ok) {
+      // reverse state hand-off: G[j] = dSl'^T + e^{c_L} G[j+1];  da = <G[j+1], S_in[j]>
+      // warp w: sub-partition sp = w % 4 (state rows n), p-quarter pq = w / 4 (16 columns)
+      const int sp = warp & 3, pq = warp >> 2;
+      const bool rows128 = (NS == 128);
+      const int n = rows128 ? 32 * sp + lane : 16 * sp + (lane & 15);
+      const bool active = rows128 || lane < 16;
+      float ds[16], gn[16];
+      umma::tmem_ld16(R4 + ((uint32_t)(32 * sp) << 16) + 16 * pq, ds);
+      float da_part = 0.f;
+      if (active) {
+        // ring slots are [p/4][n][4]; the caller's dfinal / dinitial states are [p][n]
+        const int64_t PN = (int64_t)kP * NS;
+        if (j == p.nc - 1) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) gn[i] = p.dfin ? __ldcg(p.dfin + bh * PN + (16 * pq + i) * NS + n) : 0.f;
-      } else {
-        const float4* s4 = reinterpret_cast<const float4*>(p.ring + (bh * 2 + ((j + 1) & 1)) * PN) + 4 * pq * NS + n;
+          for (int i = 0; i < 16; ++i) gn[i] = p.dfin ? __ldcg(p.dfin + bh * PN + (16 * pq + i) * NS + n) : 0.f;
+        } else {
+          const float4* s4 = reinterpret_cast<const float4*>(p.ring + (bh * 2 + ((j + 1) & 1)) * PN) + 4 * pq * NS + n;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 v = __ldcg(s4 + q * NS);
+            gn[4 * q] = v.x; gn[4 * q + 1] = v.y; gn[4 * q + 2] = v.z; gn[4 * q + 3] = v.w;
+          }
+        }
+        float* dinit = (j == 0 && p.dinit) ? p.dinit + bh * PN : nullptr;
+        float4* d4 = reinterpret_cast<float4*>(p.ring + (bh * 2 + (j & 1)) * PN) + 4 * pq * NS + n;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          d4[q * NS] = make_float4(ds[4 * q] + a_chunk * gn[4 * q], ds[4 * q + 1] + a_chunk * gn[4 * q + 1],
+                                   ds[4 * q + 2] + a_chunk * gn[4 * q + 2], ds[4 * q + 3] + a_chunk * gn[4 * q + 3]);
+        if (dinit) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) dinit[(16 * pq + i) * NS + n] = ds[i] + a_chunk * gn[i];
+        }
+      }
+      // publish G[j] first; Gn in bf16 and <Gn, S_in> are off the chain's critical path
+      __threadfence();
+      __syncthreads();
+      if (tid == 0) st_release(&flags[j], kFlagReady);
+      if (active) {
+#pragma unroll
+        for (int qd = 0; qd < 2; ++qd) {
+          float sv[8];
+          load_chunk(sSin, n, 2 * pq + qd, sv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) da_part += gn[8 * qd + e] * sv[e];
+          *reinterpret_cast<uint4*>(sGN + umma::sw128_offset(n, 2 * pq + qd)) =
+              make_uint4(pack_bf16(gn[8 * qd], gn[8 * qd + 1]), pack_bf16(gn[8 * qd + 2], gn[8 * qd + 3]),
+                         pack_bf16(gn[8 * qd + 4], gn[8 * qd + 5]), pack_bf16(gn[8 * qd + 6], gn[8 * qd + 7]));
+        }
+      }
+      da_part = warp_sum(da_part);
+      if (lane == 0) s_da[warp] = da_part;
+      umma::fence_proxy_async_smem();
+      umma::fence_before_sync();
+      __syncthreads();
+      if (tid == 0) {
+        umma::fence_after_sync();
+        const uint32_t kk0 = umma::smem_u32(sKK), xw0 = umma::smem_u32(sXW), gn0 = umma::smem_u32(sGN);
+        // e (state part): dK += [wgX;wbXp] Gn
+        constexpr uint32_t ide2 = umma::idesc_bf16(128, NS, false, false);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma::mma_bf16(R0, umma::desc_sw128(xw0 + ks * 32, 16, 1024), umma::desc_sw128(gn0 + ks * 32, 16, 1024), ide2, 1);
+        // f: U = [K;Kp] Gn^T
+        constexpr uint32_t idf = umma::idesc_bf16(128, 64, false, true);
+#pragma unroll
+        for (int ks = 0; ks < NS / 16; ++ks) {
+          const uint32_t qb = ks >> 2, kin = ks & 3;
+          umma::mma_bf16(R3, umma::desc_sw128(kk0 + qb * 16384 + kin * 32, 16, 1024),
+                         umma::desc_sw128(gn0 + ks * 2048, 8192, 1024), idf, ks > 0);
+        }
+        umma::mma_commit(&bars[4]);
+      }
+      ok = __syncthreads_and(umma::mbar_wait(&bars[4], ph, p.status));
+    } else if (tid == 0) {
+      st_release(&flags[j], kFlagAbort);
+    }
+    if (ok) {
+      umma::fence_after_sync();
+      // warp w: sub-partition sp = w % 4, column quarter cq = w / 4
+      const int sp = warp & 3, cq = warp >> 2;
+      // Output tiles are staged (bf16, 128-byte swizzle) in shared memory that is dead by now and
+      // leave through TMA stores: dq -> Q tile, dk | dkp -> K/Kp tiles, dx | dxp -> X/Xp tiles (each
+      // thread overwrites exactly the X elements it has just read).
+      unsigned char* st_dq = sQ;
+      unsigned char* st_dk = sKK;
+      unsigned char* st_dkp = sKK + S::QB * 8192;
+      unsigned char* st_dx = sXX;
+      unsigned char* st_dxp = sXX + 8192;
+      // (1) dQ rows (R1 lanes +0, columns [32 cq, 32 cq + 32)) and, for cq < 2, Ye rows (R1 lanes
+      // +16, same columns) for the dc inter term
+      if (32 * cq < NS) {
+        const int t = 16 * sp + (lane & 15);
+        float v[32];
+        umma::tmem_ld32(R1 + ((uint32_t)(32 * sp) << 16) + 32 * cq, v);
+        if (lane < 16) stage_row32(st_dq + (cq >> 1) * 8192, t, 4 * (cq & 1), v);
+        if (lane >= 16 && cq < 2) {
+          float acc = 0.f;
+#pragma unroll
+          for (int qd = 0; qd < 4; ++qd) {
+            float d[8];
+            load_chunk(sDY, t, 4 * cq + qd, d);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc += d[e] * v[8 * qd + e];
+          }
+          s_dcint[cq * 64 + t] = s_ec[t] * acc;
+        }
+      }
+      // (2) dx / dxp rows: dXc (R2) + w g U (R3), columns [16 cq, 16 cq + 16); x.U partial sums for
+      // dgamma / dbeta
+      {
+        const int r = 32 * sp + lane;  // 0-63: s of X, 64-127: s of Xp
+        float dxc[16], u[16];
+        umma::tmem_ld16x2(R2 + ((uint32_t)(32 * sp) << 16) + 16 * cq, R3 + ((uint32_t)(32 * sp) << 16) + 16 * cq, dxc, u);
+        const float wgt = s_wgb[r];  // wg for X rows, wb for Xp rows
+        float xu = 0.f;
+#pragma unroll
+        for (int qd = 0; qd < 2; ++qd) {
+          float xv[8];
+          load_chunk(sXX, r, 2 * cq + qd, xv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            xu += xv[e] * u[8 * qd + e];
+            dxc[8 * qd + e] += wgt * u[8 * qd + e];
+          }
+        }
+        s_xu[cq * 128 + r] = xu;
+        stage_row16(r < 64 ? st_dx : st_dxp, r & 63, 2 * cq, dxc);
+      }
+      // (3) dk / dkp rows (R0), columns [32 cq, 32 cq + 32)
+      if (32 * cq < NS) {
+        const int r = 32 * sp + lane;
+        float v[32];
+        umma::tmem_ld32(R0 + ((uint32_t)(32 * sp) << 16) + 32 * cq, v);
+        stage_row32((r < 64 ? st_dk : st_dkp) + (cq >> 1) * 8192, r & 63, 4 * (cq & 1), v);
+      }
+      umma::fence_proxy_async_smem();
+      umma::fence_before_sync();
+      __syncthreads();
+      if (tid == 32) {  // the producer waits for these before reusing the stage
+#pragma unroll
+        for (int qb = 0; qb < S::QB; ++qb) {
+          umma::tma_store_4d(&p.tdq, st_dq + qb * 8192, qb * 64, g, t0, b);
+          umma::tma_store_4d(&p.tdk, st_dk + qb * 8192, qb * 64, g, t0, b);
+          umma::tma_store_4d(&p.tdkp, st_dkp + qb * 8192, qb * 64, g, t0, b);
+        }
+        umma::tma_store_4d(&p.tdx, st_dx, 0, h, t0, b);
+        umma::tma_store_4d(&p.tdxp, st_dxp, 0, h, t0, b);
+        umma::bulk_commit();
+      }
+      __syncthreads();
+      // per-token scalars: warps 0-1 own tokens 0-63
+      if (tid < 64) {
+        const int s = tid;
+        float da = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) da += s_da[i];
+        float xu = 0.f, xpu = 0.f, colZ = 0.f, colEg = 0.f, colEb = 0.f, rowZ = 0.f;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const float4 v = __ldcg(s4 + q * NS);
-          gn[4 * q] = v.x; gn[4 * q + 1] = v.y; gn[4 * q + 2] = v.z; gn[4 * q + 3] = v.w;
+          xu += s_xu[q * 128 + s];
+          xpu += s_xu[q * 128 + 64 + s];
+          colZ += s_colZ[q * 128 + s] + s_colZ[q * 128 + 64 + s];
+          colEg += s_colE[q * 128 + s];
+          colEb += s_colE[q * 128 + 64 + s];
+          rowZ += s_rowZ[q * 64 + s];
         }
-      }
-      float* dinit = (j == 0 && p.dinit) ? p.dinit + bh * PN : nullptr;
-      float4* d4 = reinterpret_cast<float4*>(p.ring + (bh * 2 + (j & 1)) * PN) + 4 * pq * NS + n;
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        d4[q * NS] = make_float4(ds[4 * q] + a_chunk * gn[4 * q], ds[4 * q + 1] + a_chunk * gn[4 * q + 1],
-                                 ds[4 * q + 2] + a_chunk * gn[4 * q + 2], ds[4 * q + 3] + a_chunk * gn[4 * q + 3]);
-      if (dinit) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) dinit[(16 * pq + i) * NS + n] = ds[i] + a_chunk * gn[i];
-      }
-    }
-    // publish G[j] first; Gn in bf16 and <Gn, S_in> are off the chain's critical path
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) st_release(&flags[j], kFlagReady);
-    if (active) {
-#pragma unroll
-      for (int qd = 0; qd < 2; ++qd) {
-        float sv[8];
-        load_chunk(sSin, n, 2 * pq + qd, sv);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) da_part += gn[8 * qd + e] * sv[e];
-        *reinterpret_cast<uint4*>(sGN + umma::sw128_offset(n, 2 * pq + qd)) =
-            make_uint4(pack_bf16(gn[8 * qd], gn[8 * qd + 1]), pack_bf16(gn[8 * qd + 2], gn[8 * qd + 3]),
-                       pack_bf16(gn[8 * qd + 4], gn[8 * qd + 5]), pack_bf16(gn[8 * qd + 6], gn[8 * qd + 7]));
+        const float w = s_w[s];
+        const float dw = s_g[s] * xu + s_b[s] * xpu;
+        const float dg = colEg + w * xu;
+        const float db = colEb + w * xpu;
+        float dc = rowZ - colZ + s_dcint[s] + s_dcint[64 + s] - w * dw;
+        // dc_{L-1} += e^{c_L} da + sum_s w_s dw_s   (two warps: combine through shared memory)
+        const float wdw = warp_sum(w * dw);
+        if (lane == 0) s_tmp[warp] = wdw;
+        asm volatile("bar.sync 1, 64;" ::: "memory");
+        if (s == 63) dc += a_chunk * da + s_tmp[0] + s_tmp[1];
+        // dadt_u = sum_{t >= u} dc_t  (reverse cumulative sum over 64 tokens in two warps)
+        const float total = warp_sum(dc);
+        const float incl = warp_incl_scan(dc, lane);
+        float suffix = total - incl + dc;
+        if (lane == 0 && warp == 1) s_tmp[2] = total;
+        asm volatile("bar.sync 1, 64;" ::: "memory");
+        if (warp == 0) suffix += s_tmp[2];
+        const int tt = t0 + s;
+        p.dadt[b * p.dasb + (int64_t)tt * p.dast + h * p.dash] = suffix;
+        p.dgamma[b * p.dgsb + (int64_t)tt * p.dgst + h * p.dgsh] = dg;
+        p.dbeta[b * p.dbsb + (int64_t)tt * p.dbst + h * p.dbsh] = db;
       }
     }
-    da_part = warp_sum(da_part);
-    if (lane == 0) s_da[warp] = da_part;
-    umma::fence_proxy_async_smem();
-    umma::fence_before_sync();
-    __syncthreads();
-    if (tid == 0) {
-      umma::fence_after_sync();
-      const uint32_t kk0 = umma::smem_u32(sKK), xw0 = umma::smem_u32(sXW), gn0 = umma::smem_u32(sGN);
-      // e (state part): dK += [wgX;wbXp] Gn
-      constexpr uint32_t ide2 = umma::idesc_bf16(128, NS, false, false);
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        umma::mma_bf16(R0, umma::desc_sw128(xw0 + ks * 32, 16, 1024), umma::desc_sw128(gn0 + ks * 32, 16, 1024), ide2, 1);
-      // f: U = [K;Kp] Gn^T
-      constexpr uint32_t idf = umma::idesc_bf16(128, 64, false, true);
-#pragma unroll
-      for (int ks = 0; ks < NS / 16; ++ks) {
-        const uint32_t qb = ks >> 2, kin = ks & 3;
-        umma::mma_bf16(R3, umma::desc_sw128(kk0 + qb * 16384 + kin * 32, 16, 1024),
-                       umma::desc_sw128(gn0 + ks * 2048, 8192, 1024), idf, ks > 0);
+    __syncthreads();  // every read of this stage and of the work tiles is done
+    if (!ok) {
+      // leave after an error; the ticket already taken is aborted and its loads land first
+      if (tid == 32 && nx < total) {
+        const BwdChunk cn = bwd_chunk(p, nx);
+        st_release(&p.flags[cn.bh * (p.nc + 1) + cn.j], kFlagAbort);
+        if (prefetched) umma::mbar_wait(&bars[stage ^ 1], ((it + 1) >> 1) & 1, p.status);
       }
-      umma::mma_commit(&bars[3]);
+      break;
     }
-    ok = __syncthreads_and(umma::mbar_wait(&bars[3], 0, p.status));
-  } else if (tid == 0) {
-    st_release(&flags[j], kFlagAbort);
+    cur = nxt;
   }
-  if (ok) {
-    umma::fence_after_sync();
-    // warp w: sub-partition sp = w % 4, column quarter cq = w / 4
-    const int sp = warp & 3, cq = warp >> 2;
-    // Output tiles are staged (bf16, 128-byte swizzle) in shared memory that is dead by now and
-    // leave through TMA stores: dq -> Q tile, dk | dkp -> K/Kp tiles, dx | dxp -> [A|Ap] tile.
-    unsigned char* st_dq = sQ;
-    unsigned char* st_dk = sKK;
-    unsigned char* st_dkp = sKK + S::QB * 8192;
-    unsigned char* st_dx = sPS;
-    unsigned char* st_dxp = sPS + 8192;
-    // (1) dQ rows (R1 lanes +0, columns [32 cq, 32 cq + 32)) and, for cq < 2, Ye rows (R1 lanes
-    // +16, same columns) for the dc inter term
-    if (32 * cq < NS) {
-      const int t = 16 * sp + (lane & 15);
-      float v[32];
-      umma::tmem_ld32(R1 + ((uint32_t)(32 * sp) << 16) + 32 * cq, v);
-      if (lane < 16) stage_row32(st_dq + (cq >> 1) * 8192, t, 4 * (cq & 1), v);
-      if (lane >= 16 && cq < 2) {
-        float acc = 0.f;
-#pragma unroll
-        for (int qd = 0; qd < 4; ++qd) {
-          float d[8];
-          load_chunk(sDY, t, 4 * cq + qd, d);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc += d[e] * v[8 * qd + e];
-        }
-        s_dcint[cq * 64 + t] = s_ec[t] * acc;
-      }
-    }
-    // (2) dx / dxp rows: dXc (R2) + w g U (R3), columns [16 cq, 16 cq + 16); x.U partial sums for
-    // dgamma / dbeta
-    {
-      const int r = 32 * sp + lane;  // 0-63: s of X, 64-127: s of Xp
-      float dxc[16], u[16];
-      umma::tmem_ld16x2(R2 + ((uint32_t)(32 * sp) << 16) + 16 * cq, R3 + ((uint32_t)(32 * sp) << 16) + 16 * cq, dxc, u);
-      const float wgt = s_wgb[r];  // wg for X rows, wb for Xp rows
-      float xu = 0.f;
-#pragma unroll
-      for (int qd = 0; qd < 2; ++qd) {
-        float xv[8];
-        load_chunk(sXX, r, 2 * cq + qd, xv);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          xu += xv[e] * u[8 * qd + e];
-          dxc[8 * qd + e] += wgt * u[8 * qd + e];
-        }
-      }
-      s_xu[cq * 128 + r] = xu;
-      stage_row16(r < 64 ? st_dx : st_dxp, r & 63, 2 * cq, dxc);
-    }
-    // (3) dk / dkp rows (R0), columns [32 cq, 32 cq + 32)
-    if (32 * cq < NS) {
-      const int r = 32 * sp + lane;
-      float v[32];
-      umma::tmem_ld32(R0 + ((uint32_t)(32 * sp) << 16) + 32 * cq, v);
-      stage_row32((r < 64 ? st_dk : st_dkp) + (cq >> 1) * 8192, r & 63, 4 * (cq & 1), v);
-    }
-    umma::fence_proxy_async_smem();
-    __syncthreads();
-    if (tid == 0) {
-#pragma unroll
-      for (int qb = 0; qb < S::QB; ++qb) {
-        umma::tma_store_4d(&p.tdq, st_dq + qb * 8192, qb * 64, g, t0, b);
-        umma::tma_store_4d(&p.tdk, st_dk + qb * 8192, qb * 64, g, t0, b);
-        umma::tma_store_4d(&p.tdkp, st_dkp + qb * 8192, qb * 64, g, t0, b);
-      }
-      umma::tma_store_4d(&p.tdx, st_dx, 0, h, t0, b);
-      umma::tma_store_4d(&p.tdxp, st_dxp, 0, h, t0, b);
-      umma::bulk_commit();
-    }
-    __syncthreads();
-    // per-token scalars: warps 0-1 own tokens 0-63
-    if (tid < 64) {
-      const int s = tid;
-      float da = 0.f;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) da += s_da[i];
-      float xu = 0.f, xpu = 0.f, colZ = 0.f, colEg = 0.f, colEb = 0.f, rowZ = 0.f;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        xu += s_xu[q * 128 + s];
-        xpu += s_xu[q * 128 + 64 + s];
-        colZ += s_colZ[q * 128 + s] + s_colZ[q * 128 + 64 + s];
-        colEg += s_colE[q * 128 + s];
-        colEb += s_colE[q * 128 + 64 + s];
-        rowZ += s_rowZ[q * 64 + s];
-      }
-      const float w = s_w[s];
-      const float dw = s_g[s] * xu + s_b[s] * xpu;
-      const float dg = colEg + w * xu;
-      const float db = colEb + w * xpu;
-      float dc = rowZ - colZ + s_dcint[s] + s_dcint[64 + s] - w * dw;
-      // dc_{L-1} += e^{c_L} da + sum_s w_s dw_s   (two warps: combine through shared memory)
-      const float wdw = warp_sum(w * dw);
-      if (lane == 0) s_tmp[warp] = wdw;
-      asm volatile("bar.sync 1, 64;" ::: "memory");
-      if (s == 63) dc += a_chunk * da + s_tmp[0] + s_tmp[1];
-      // dadt_u = sum_{t >= u} dc_t  (reverse cumulative sum over 64 tokens in two warps)
-      const float total = warp_sum(dc);
-      const float incl = warp_incl_scan(dc, lane);
-      float suffix = total - incl + dc;
-      if (lane == 0 && warp == 1) s_tmp[2] = total;
-      asm volatile("bar.sync 1, 64;" ::: "memory");
-      if (warp == 0) suffix += s_tmp[2];
-      const int tt = t0 + s;
-      p.dadt[b * p.dasb + (int64_t)tt * p.dast + h * p.dash] = suffix;
-      p.dgamma[b * p.dgsb + (int64_t)tt * p.dgst + h * p.dgsh] = dg;
-      p.dbeta[b * p.dbsb + (int64_t)tt * p.dbst + h * p.dbsh] = db;
-    }
-  }
-  if (tid == 0) umma::bulk_wait_all();  // staged output tiles must be read out before exit
+  if (tid == 32) umma::bulk_wait_all();  // staged output tiles must be read out before exit
+  if (tid < 64) umma::cp_async_wait_all();
   umma::fence_before_sync();
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tmem, 512);
@@ -987,12 +1058,10 @@ __global__ void __launch_bounds__(kStThreads) ssd_state_tc_kernel(const __grid_c
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tmem = misc[0];
-  const int64_t BH = p.B * p.H;
-  const int64_t tk = misc[1];
-  const int j = BACKWARD ? p.nc - 1 - (int)(tk / BH) : (int)(tk / BH);
-  const int64_t bh = tk % BH;
-  const int b = (int)(bh / p.H), h = (int)(bh % p.H);
-  const int g = (int)(h / (p.H / p.G));
+  const UnitIdx u = decode_ticket(misc[1], p.B, p.H, p.G);
+  const int j = BACKWARD ? p.nc - 1 - u.chunk : u.chunk;
+  const int64_t bh = u.bh;
+  const int b = u.b, h = u.h, g = u.g;
   const int t0 = j * kL;
   int* flags = p.flags + bh * (p.nc + 1);
   const int64_t PN = (int64_t)kP * NS;
@@ -1177,6 +1246,19 @@ bool view_tma_ok(const zb_view& v) {
   return v.ptr && reinterpret_cast<uintptr_t>(v.ptr) % 16 == 0 && a16(v.sh) && a16(v.st) && a16(v.sb);
 }
 
+// streaming multiprocessors of the current device (cached per device)
+int sm_count() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
 template <int NS>
 int launch_fwd(const zb_ssd_args* a, ChainSync sync, void* states, void* ring, cudaStream_t stream) {
   TcFwdParams p;
@@ -1254,7 +1336,8 @@ int launch_bwd(const zb_ssd_args* a, ChainSync sync, void* ring, cudaStream_t st
   auto k = ssd_bwd_tc_kernel<NS>;
   const int smem = (int)BwdSmem<NS>::ALLOC;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return ZB_ERR_CUDA;
-  const dim3 grid((unsigned)(a->B * a->H * p.nc));
+  const int64_t units = a->B * a->H * p.nc;
+  const dim3 grid((unsigned)(units < sm_count() ? units : sm_count()));  // persistent: one CTA per SM
   k<<<grid, kBwdThreads, smem, stream>>>(p);
   note_launches(1);
   return cudaPeekAtLastError() == cudaSuccess ? ZB_OK : ZB_ERR_CUDA;
