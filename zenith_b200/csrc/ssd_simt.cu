@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(kThreads) ssd_fwd_simt_kernel(const SimtParams
     slot_out[i] = v;
     if (last && p.fin) reinterpret_cast<TA*>(p.fin)[bh * PN + i] = v;
   }
-  __threadfence();
+  // the barrier orders every thread's ring writes before thread 0's release (cumulative)
   __syncthreads();
   if (tid == 0) st_release(&flags[j + 1], kFlagReady);
   if (state_only) return;
@@ -365,7 +365,7 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
     if (j == 0 && p.dinit) reinterpret_cast<TA*>(p.dinit)[bh * PN + i] = v;
     if (!state_only) da_part += gn * s_S[(i / N) * N1 + i % N];
   }
-  __threadfence();
+  // the barrier orders every thread's ring writes before thread 0's release (cumulative)
   __syncthreads();
   if (tid == 0) st_release(&flags[j], kFlagReady);
   if (state_only) return;

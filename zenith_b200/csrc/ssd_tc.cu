@@ -42,9 +42,9 @@ struct FwdSmem {
   static constexpr uint32_t XS = XP + 8192;               // [wgX | wbXp]
   static constexpr uint32_t SIN = XS + 16384;             // [NS n][64 p]; before that the scores Ps [2][64][64]
   static constexpr uint32_t SIN_BYTES = NS * 128 > 16384 ? NS * 128 : 16384;
-  static constexpr uint32_t SCAL = SIN + SIN_BYTES;       // c, ec, wg, wb, g, b (64 floats each)
-  static constexpr uint32_t BAR = SCAL + 6 * 64 * 4;      // 5 mbarriers (load, MMA1, MMA2, MMA4, MMA3)
-  static constexpr uint32_t MISC = BAR + 6 * 8;           // tmem base, ticket, ready
+  static constexpr uint32_t SCAL = SIN + SIN_BYTES;       // c, ec, wg, wb, g, b, next chunk's adt g b (64 floats each)
+  static constexpr uint32_t BAR = SCAL + 9 * 64 * 4;      // 5 mbarriers (load, MMA1, MMA2, MMA4, MMA3)
+  static constexpr uint32_t MISC = BAR + 6 * 8;           // tmem base, ticket, chain result, next ticket
   static constexpr uint32_t TOTAL = MISC + 16;
   static constexpr uint32_t ALLOC = TOTAL + 1024;         // slack to align the base to 1024
 };
@@ -79,6 +79,39 @@ __device__ __forceinline__ float2 unpack_bf16(uint32_t u) {
   return __bfloat1622float2(v);
 }
 
+// Loads of one chunk's operands, issued in three parts as the previous chunk frees the tiles.
+template <int NS>
+__device__ __forceinline__ void fwd_load_kk(const TcFwdParams& p, unsigned char* sKK, uint64_t* bar, const UnitIdx& u) {
+  const int t0 = u.chunk * kL;
+#pragma unroll
+  for (int qb = 0; qb < NS / 64; ++qb) {
+    umma::tma_load_4d(sKK + qb * 16384, &p.tk, bar, qb * 64, u.g, t0, u.b);
+    umma::tma_load_4d(sKK + qb * 16384 + 8192, &p.tkp, bar, qb * 64, u.g, t0, u.b);
+  }
+}
+__device__ __forceinline__ void fwd_load_x(const TcFwdParams& p, unsigned char* sX, unsigned char* sXp, uint64_t* bar,
+                                           const UnitIdx& u) {
+  umma::tma_load_4d(sX, &p.tx, bar, 0, u.h, u.chunk * kL, u.b);
+  umma::tma_load_4d(sXp, &p.txp, bar, 0, u.h, u.chunk * kL, u.b);
+}
+template <int NS>
+__device__ __forceinline__ void fwd_load_q(const TcFwdParams& p, unsigned char* sQ, uint64_t* bar, const UnitIdx& u) {
+#pragma unroll
+  for (int qb = 0; qb < NS / 64; ++qb) umma::tma_load_4d(sQ + qb * 8192, &p.tq, bar, qb * 64, u.g, u.chunk * kL, u.b);
+}
+// token s of a chunk: adt, gamma, beta -> dst[s], dst[64 + s], dst[128 + s] (asynchronous copies)
+__device__ __forceinline__ void fwd_prefetch_scalars(const TcFwdParams& p, const UnitIdx& u, int s, float* dst) {
+  const int t = u.chunk * kL + s;
+  umma::cp_async4(dst + s, p.adt + (u.b * p.asb + t * p.ast + u.h * p.ash));
+  umma::cp_async4(dst + 64 + s, p.gamma + (u.b * p.gsb + t * p.gst + u.h * p.gsh));
+  umma::cp_async4(dst + 128 + s, p.beta + (u.b * p.bsb + t * p.bst + u.h * p.bsh));
+  umma::cp_async_commit();
+}
+
+// Persistent: two CTAs per SM walk the chunks in ticket order (chunk-major).  Each CTA takes its
+// tickets in increasing order and a chunk only waits on a lower ticket, so the lowest unfinished
+// ticket always belongs to a CTA that can run it.  The next ticket's operands load into the
+// tiles of the current one as soon as its MMAs are done with them.
 template <int NS>
 __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_constant__ TcFwdParams p) {
   using S = FwdSmem<NS>;
@@ -97,10 +130,13 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
   float* s_wb = s_c + 192;
   float* s_g = s_c + 256;
   float* s_b = s_c + 320;
+  float* s_nx = s_c + 384;  // next chunk's [adt | gamma | beta]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::BAR);
   uint32_t* misc = reinterpret_cast<uint32_t*>(sm + S::MISC);
+  constexpr uint32_t kLoadBytes = S::QB * 8192 * 3 + 2 * 8192;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t total = p.B * p.H * p.nc;
   if (tid == 0) {
     misc[1] = atomicAdd(p.ticket, 1u);
     for (int i = 0; i < 5; ++i) umma::mbar_init(&bars[i], 1);
@@ -114,247 +150,295 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tmem = misc[0];
-  const UnitIdx u = decode_ticket(misc[1], p.B, p.H, p.G);
-  const int j = u.chunk;
-  const int64_t bh = u.bh;
-  const int b = u.b, h = u.h, g = u.g;
-  const int t0 = j * kL;
-  int* flags = p.flags + bh * (p.nc + 1);
+  uint32_t cur = misc[1];
+  if (cur < total) {
+    const UnitIdx u0 = decode_ticket(cur, p.B, p.H, p.G);
+    if (tid == 0) {
+      umma::mbar_arrive_expect_tx(&bars[0], kLoadBytes);
+      fwd_load_q<NS>(p, sQ, &bars[0], u0);
+      fwd_load_kk<NS>(p, sKK, &bars[0], u0);
+      fwd_load_x(p, sX, sXp, &bars[0], u0);
+    }
+    if (tid < 64) fwd_prefetch_scalars(p, u0, tid, s_nx);
+  }
 
-  constexpr uint32_t kLoadBytes = S::QB * 8192 * 3 + 2 * 8192;
-  if (tid == 0) {
-    umma::mbar_arrive_expect_tx(&bars[0], kLoadBytes);
-#pragma unroll
-    for (int qb = 0; qb < S::QB; ++qb) {
-      umma::tma_load_4d(sQ + qb * 8192, &p.tq, &bars[0], qb * 64, g, t0, b);
-      umma::tma_load_4d(sKK + qb * 16384, &p.tk, &bars[0], qb * 64, g, t0, b);
-      umma::tma_load_4d(sKK + qb * 16384 + 8192, &p.tkp, &bars[0], qb * 64, g, t0, b);
-    }
-    umma::tma_load_4d(sX, &p.tx, &bars[0], 0, h, t0, b);
-    umma::tma_load_4d(sXp, &p.txp, &bars[0], 0, h, t0, b);
-  }
-  // per-token scalars and the in-chunk cumulative sum c (mamba3.py:40)
-  if (tid < 64) {
-    const int t = t0 + tid;
-    const float a = p.adt[b * p.asb + t * p.ast + h * p.ash];
-    s_g[tid] = p.gamma[b * p.gsb + t * p.gst + h * p.gsh];
-    s_b[tid] = p.beta[b * p.bsb + t * p.bst + h * p.bsh];
-    s_c[tid] = warp_incl_scan(a, lane);
-  }
-  __syncthreads();
-  if (tid >= 32 && tid < 64) s_c[tid] += s_c[31];
-  __syncthreads();
-  if (tid < 64) {
-    const float c = s_c[tid], w = expf(s_c[63] - c);
-    s_ec[tid] = expf(c);
-    s_wg[tid] = w * s_g[tid];
-    s_wb[tid] = w * s_b[tid];
-  }
-  const bool load_ok = umma::mbar_wait(&bars[0], 0, p.status);
-  __syncthreads();
-  const float a_chunk = expf(s_c[63]);
-  bool ok = __syncthreads_and(load_ok);
+  for (uint32_t it = 0; cur < total; ++it) {
+    const uint32_t par = it & 1;  // parity of this chunk's barriers (each completes once per chunk)
+    const UnitIdx u = decode_ticket(cur, p.B, p.H, p.G);
+    const int j = u.chunk;
+    const int64_t bh = u.bh;
+    const int b = u.b, h = u.h;
+    const int t0 = j * kL;
+    int* flags = p.flags + bh * (p.nc + 1);
+    // thread 0 takes the next ticket now and uses it once [K | Kp] is free
+    uint32_t nx = 0, nxt = 0;
+    UnitIdx nu = u;
+    int pf = 0;  // parts of the next chunk's operands issued (K/Kp, X/Xp, Q)
+    if (tid == 0) nx = atomicAdd(p.ticket, 1u);
 
-  if (ok) {
-    // MMA1 (scores) needs no rescaled operand: start it before scaling X
-    if (tid == 0) {
-      umma::fence_after_sync();
-      const uint32_t q0 = umma::smem_u32(sQ), kk0 = umma::smem_u32(sKK);
-      constexpr uint32_t id1 = umma::idesc_bf16(64, 128, false, false);
-#pragma unroll
-      for (int ks = 0; ks < NS / 16; ++ks) {
-        const uint32_t qb = ks >> 2, kin = ks & 3;
-        umma::mma_bf16(tmem, umma::desc_sw128(q0 + qb * 8192 + kin * 32, 16, 1024),
-                       umma::desc_sw128(kk0 + qb * 16384 + kin * 32, 16, 1024), id1, ks > 0);
-      }
-      umma::mma_commit(&bars[1]);
-    }
-    // [wgX | wbXp]: scale each row s of X / Xp (a 16-byte chunk at byte offset o lies in row o / 128)
-    for (int i = tid; i < 1024; i += kTcThreads) {
-      const int tile = i >> 9;
-      const uint32_t off = (uint32_t)(i & 511) * 16u;
-      const float f = tile ? s_wb[off >> 7] : s_wg[off >> 7];
-      const uint4 v = *reinterpret_cast<const uint4*>((tile ? sXp : sX) + off);
-      uint4 o;
-      float2 e;
-      e = unpack_bf16(v.x); o.x = pack_bf16(e.x * f, e.y * f);
-      e = unpack_bf16(v.y); o.y = pack_bf16(e.x * f, e.y * f);
-      e = unpack_bf16(v.z); o.z = pack_bf16(e.x * f, e.y * f);
-      e = unpack_bf16(v.w); o.w = pack_bf16(e.x * f, e.y * f);
-      *reinterpret_cast<uint4*>(sXs + tile * 8192 + off) = o;
-    }
-    umma::fence_proxy_async_smem();
-    umma::fence_before_sync();
-    __syncthreads();
-    if (tid == 0) {
-      umma::fence_after_sync();
-      const uint32_t kk0 = umma::smem_u32(sKK), xs0 = umma::smem_u32(sXs);
-      constexpr uint32_t id3 = umma::idesc_bf16(NS, 64, true, true);
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t part = ks >> 2, kin = ks & 3;
-        umma::mma_bf16(tmem + 192, umma::desc_sw128(kk0 + part * 8192 + kin * 2048, 16384, 1024),
-                       umma::desc_sw128(xs0 + part * 8192 + kin * 2048, 8192, 1024), id3, ks > 0);
-      }
-      umma::mma_commit(&bars[4]);
-    }
-    // the score epilogue needs only MMA1; MMA3 (chunk state) finishes meanwhile
-    ok = __syncthreads_and(umma::mbar_wait(&bars[1], 0, p.status));
-  }
-  if (ok) {
-    umma::fence_after_sync();
-    // scores -> Ps (bf16, K-major [2][64 t][64 s]) over the K/Kp tiles.  TMEM gives lanes 0-15
-    // the S row; lanes 16-31 take over columns 16-31 of each 32-column block by one shuffle each.
-    const int sp = warp & 3, half = warp >> 2;
-    const int t = 16 * sp + (lane & 15);
-    const bool hiL = lane >= 16;
-    const float* coef = half ? s_b : s_g;
-    const float ct = s_c[t];
-#pragma unroll
-    for (int cc = 0; cc < 2; ++cc) {
-      float v[32];
-      umma::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + half * 64 + cc * 32, v);
-      uint32_t w8[8];
-#pragma unroll
-      for (int i = 0; i < 16; i += 2) {
-        const float r0 = __shfl_xor_sync(0xffffffffu, v[16 + i], 16);
-        const float r1 = __shfl_xor_sync(0xffffffffu, v[17 + i], 16);
-        const int s0 = cc * 32 + (hiL ? 16 : 0) + i;
-        const float a0 = hiL ? r0 : v[i], a1 = hiL ? r1 : v[i + 1];
-        const float v0 = (s0 <= t) ? a0 * coef[s0] * __expf(ct - s_c[s0]) : 0.f;
-        const float v1 = (s0 + 1 <= t) ? a1 * coef[s0 + 1] * __expf(ct - s_c[s0 + 1]) : 0.f;
-        w8[i >> 1] = pack_bf16(v0, v1);
-      }
-      const int c0 = cc * 4 + (hiL ? 2 : 0);
-      *reinterpret_cast<uint4*>(sPs + half * 8192 + umma::sw128_offset(t, c0)) = make_uint4(w8[0], w8[1], w8[2], w8[3]);
-      *reinterpret_cast<uint4*>(sPs + half * 8192 + umma::sw128_offset(t, c0 + 1)) =
-          make_uint4(w8[4], w8[5], w8[6], w8[7]);
-    }
-    umma::fence_proxy_async_smem();
-    umma::fence_before_sync();
-    __syncthreads();
-    if (tid == 0) {
-      umma::fence_after_sync();
-      const uint32_t ps0 = umma::smem_u32(sPs), x0 = umma::smem_u32(sX), xp0 = umma::smem_u32(sXp);
-      constexpr uint32_t id2 = umma::idesc_bf16(64, 64, false, true);
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t part = ks >> 2, kin = ks & 3;
-        umma::mma_bf16(tmem + 128, umma::desc_sw128(ps0 + part * 8192 + kin * 32, 16, 1024),
-                       umma::desc_sw128((part ? xp0 : x0) + kin * 2048, 8192, 1024), id2, ks > 0);
-      }
-      umma::mma_commit(&bars[2]);
-      misc[2] = (j == 0) ? kFlagReady : wait_flag(&flags[j], p.status);
+    // per-token scalars and the in-chunk cumulative sum c (mamba3.py:40)
+    if (tid < 64) {
+      umma::cp_async_wait_all();  // this thread's own copies
+      s_g[tid] = s_nx[64 + tid];
+      s_b[tid] = s_nx[128 + tid];
+      s_c[tid] = warp_incl_scan(s_nx[tid], lane);
     }
     __syncthreads();
-    ok = misc[2] == kFlagReady;
-    if (!ok) {  // let the MMAs finish before TMEM is freed
-      umma::mbar_wait(&bars[2], 0, p.status);
-      umma::mbar_wait(&bars[4], 0, p.status);
+    if (tid >= 32 && tid < 64) s_c[tid] += s_c[31];
+    __syncthreads();
+    if (tid < 64) {
+      const float c = s_c[tid], w = expf(s_c[63] - c);
+      s_ec[tid] = expf(c);
+      s_wg[tid] = w * s_g[tid];
+      s_wb[tid] = w * s_b[tid];
     }
-  }
-  if (ok) ok = __syncthreads_and(umma::mbar_wait(&bars[4], 0, p.status));  // S_loc ready
-  if (ok) {
-    umma::fence_after_sync();
-    // state hand-off: S_in[j+1] = e^{c_L} S_in[j] + S_loc (mamba3.py:52)
-    const int sp = warp & 3, ph = warp >> 2;
-    const bool rows128 = (NS == 128);
-    const int n = rows128 ? 32 * sp + lane : 16 * sp + (lane & 15);
-    const bool active = rows128 || lane < 16;
-    float sl[32], sin[32];
-    umma::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + 192 + 32 * ph, sl);
-    if (active) {
-      // ring slots are [p/4][n][4] (a warp's float4 access covers 512 contiguous bytes); the
-      // caller's initial and final states are [p][n]
-      const int64_t PN = (int64_t)kP * NS;
-      if (j == 0) {
+    // the previous chunk's y tile and saved state leave shared memory before [wgX | wbXp] and the
+    // scores overwrite them
+    if (tid == 0) umma::bulk_wait_read();
+    const bool load_ok = umma::mbar_wait(&bars[0], par, p.status);
+    const float a_chunk = expf(s_c[63]);
+    bool ok = __syncthreads_and(load_ok);
+
+    if (ok) {
+      // MMA1 (scores) needs no rescaled operand: start it before scaling X
+      if (tid == 0) {
+        umma::fence_after_sync();
+        const uint32_t q0 = umma::smem_u32(sQ), kk0 = umma::smem_u32(sKK);
+        constexpr uint32_t id1 = umma::idesc_bf16(64, 128, false, false);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) sin[i] = p.init ? __ldcg(p.init + bh * PN + (32 * ph + i) * NS + n) : 0.f;
-      } else {
-        const float4* s4 = reinterpret_cast<const float4*>(p.ring + (bh * 2 + (j & 1)) * PN) + 8 * ph * NS + n;
+        for (int ks = 0; ks < NS / 16; ++ks) {
+          const uint32_t qb = ks >> 2, kin = ks & 3;
+          umma::mma_bf16(tmem, umma::desc_sw128(q0 + qb * 8192 + kin * 32, 16, 1024),
+                         umma::desc_sw128(kk0 + qb * 16384 + kin * 32, 16, 1024), id1, ks > 0);
+        }
+        umma::mma_commit(&bars[1]);
+      }
+      // [wgX | wbXp]: scale each row s of X / Xp (a 16-byte chunk at byte offset o lies in row o / 128)
+      for (int i = tid; i < 1024; i += kTcThreads) {
+        const int tile = i >> 9;
+        const uint32_t off = (uint32_t)(i & 511) * 16u;
+        const float f = tile ? s_wb[off >> 7] : s_wg[off >> 7];
+        const uint4 v = *reinterpret_cast<const uint4*>((tile ? sXp : sX) + off);
+        uint4 o;
+        float2 e;
+        e = unpack_bf16(v.x); o.x = pack_bf16(e.x * f, e.y * f);
+        e = unpack_bf16(v.y); o.y = pack_bf16(e.x * f, e.y * f);
+        e = unpack_bf16(v.z); o.z = pack_bf16(e.x * f, e.y * f);
+        e = unpack_bf16(v.w); o.w = pack_bf16(e.x * f, e.y * f);
+        *reinterpret_cast<uint4*>(sXs + tile * 8192 + off) = o;
+      }
+      umma::fence_proxy_async_smem();
+      umma::fence_before_sync();
+      __syncthreads();
+      if (tid == 0) {
+        umma::fence_after_sync();
+        const uint32_t kk0 = umma::smem_u32(sKK), xs0 = umma::smem_u32(sXs);
+        constexpr uint32_t id3 = umma::idesc_bf16(NS, 64, true, true);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float4 v = __ldcg(s4 + q * NS);
-          sin[4 * q] = v.x; sin[4 * q + 1] = v.y; sin[4 * q + 2] = v.z; sin[4 * q + 3] = v.w;
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t part = ks >> 2, kin = ks & 3;
+          umma::mma_bf16(tmem + 192, umma::desc_sw128(kk0 + part * 8192 + kin * 2048, 16384, 1024),
+                         umma::desc_sw128(xs0 + part * 8192 + kin * 2048, 8192, 1024), id3, ks > 0);
+        }
+        umma::mma_commit(&bars[4]);
+      }
+      // the score epilogue needs only MMA1; MMA3 (chunk state) finishes meanwhile
+      ok = __syncthreads_and(umma::mbar_wait(&bars[1], par, p.status));
+    }
+    if (ok) {
+      umma::fence_after_sync();
+      // scores -> Ps (bf16, K-major [2][64 t][64 s]) over the K/Kp tiles.  TMEM gives lanes 0-15
+      // the S row; lanes 16-31 take over columns 16-31 of each 32-column block by one shuffle each.
+      const int sp = warp & 3, half = warp >> 2;
+      const int t = 16 * sp + (lane & 15);
+      const bool hiL = lane >= 16;
+      const float* coef = half ? s_b : s_g;
+      const float ct = s_c[t];
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        float v[32];
+        umma::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + half * 64 + cc * 32, v);
+        uint32_t w8[8];
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          const float r0 = __shfl_xor_sync(0xffffffffu, v[16 + i], 16);
+          const float r1 = __shfl_xor_sync(0xffffffffu, v[17 + i], 16);
+          const int s0 = cc * 32 + (hiL ? 16 : 0) + i;
+          const float a0 = hiL ? r0 : v[i], a1 = hiL ? r1 : v[i + 1];
+          const float v0 = (s0 <= t) ? a0 * coef[s0] * __expf(ct - s_c[s0]) : 0.f;
+          const float v1 = (s0 + 1 <= t) ? a1 * coef[s0 + 1] * __expf(ct - s_c[s0 + 1]) : 0.f;
+          w8[i >> 1] = pack_bf16(v0, v1);
+        }
+        const int c0 = cc * 4 + (hiL ? 2 : 0);
+        *reinterpret_cast<uint4*>(sPs + half * 8192 + umma::sw128_offset(t, c0)) = make_uint4(w8[0], w8[1], w8[2], w8[3]);
+        *reinterpret_cast<uint4*>(sPs + half * 8192 + umma::sw128_offset(t, c0 + 1)) =
+            make_uint4(w8[4], w8[5], w8[6], w8[7]);
+      }
+      umma::fence_proxy_async_smem();
+      umma::fence_before_sync();
+      __syncthreads();
+      if (tid == 0) {
+        umma::fence_after_sync();
+        const uint32_t ps0 = umma::smem_u32(sPs), x0 = umma::smem_u32(sX), xp0 = umma::smem_u32(sXp);
+        constexpr uint32_t id2 = umma::idesc_bf16(64, 64, false, true);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t part = ks >> 2, kin = ks & 3;
+          umma::mma_bf16(tmem + 128, umma::desc_sw128(ps0 + part * 8192 + kin * 32, 16, 1024),
+                         umma::desc_sw128((part ? xp0 : x0) + kin * 2048, 8192, 1024), id2, ks > 0);
+        }
+        umma::mma_commit(&bars[2]);
+        misc[2] = (j == 0) ? kFlagReady : wait_flag(&flags[j], p.status);
+      }
+      __syncthreads();
+      ok = misc[2] == kFlagReady;
+      if (!ok) {  // let the MMAs finish before TMEM is freed
+        umma::mbar_wait(&bars[2], par, p.status);
+        umma::mbar_wait(&bars[4], par, p.status);
+      }
+    }
+    if (ok) ok = __syncthreads_and(umma::mbar_wait(&bars[4], par, p.status));  // S_loc ready
+    if (ok) {
+      umma::fence_after_sync();
+      // MMA1 and MMA3 are done with [K | Kp]: the next chunk's tiles start loading over them
+      if (tid == 0) {
+        misc[3] = nx;
+        if (nx < total) {
+          nu = decode_ticket(nx, p.B, p.H, p.G);
+          umma::mbar_arrive_expect_tx(&bars[0], kLoadBytes);
+          fwd_load_kk<NS>(p, sKK, &bars[0], nu);
+          pf = 1;
         }
       }
-      float* fin = (j == p.nc - 1 && p.fin) ? p.fin + bh * PN : nullptr;
-      float4* d4 = reinterpret_cast<float4*>(p.ring + (bh * 2 + ((j + 1) & 1)) * PN) + 8 * ph * NS + n;
+      // state hand-off: S_in[j+1] = e^{c_L} S_in[j] + S_loc (mamba3.py:52)
+      const int sp = warp & 3, ph = warp >> 2;
+      const bool rows128 = (NS == 128);
+      const int n = rows128 ? 32 * sp + lane : 16 * sp + (lane & 15);
+      const bool active = rows128 || lane < 16;
+      float sl[32], sin[32];
+      umma::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + 192 + 32 * ph, sl);
+      if (active) {
+        // ring slots are [p/4][n][4] (a warp's float4 access covers 512 contiguous bytes); the
+        // caller's initial and final states are [p][n]
+        const int64_t PN = (int64_t)kP * NS;
+        if (j == 0) {
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
-        d4[q * NS] = make_float4(a_chunk * sin[4 * q] + sl[4 * q], a_chunk * sin[4 * q + 1] + sl[4 * q + 1],
-                                 a_chunk * sin[4 * q + 2] + sl[4 * q + 2], a_chunk * sin[4 * q + 3] + sl[4 * q + 3]);
-      if (fin) {
+          for (int i = 0; i < 32; ++i) sin[i] = p.init ? __ldcg(p.init + bh * PN + (32 * ph + i) * NS + n) : 0.f;
+        } else {
+          const float4* s4 = reinterpret_cast<const float4*>(p.ring + (bh * 2 + (j & 1)) * PN) + 8 * ph * NS + n;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) fin[(32 * ph + i) * NS + n] = a_chunk * sin[i] + sl[i];
+          for (int q = 0; q < 8; ++q) {
+            const float4 v = __ldcg(s4 + q * NS);
+            sin[4 * q] = v.x; sin[4 * q + 1] = v.y; sin[4 * q + 2] = v.z; sin[4 * q + 3] = v.w;
+          }
+        }
+        float* fin = (j == p.nc - 1 && p.fin) ? p.fin + bh * PN : nullptr;
+        float4* d4 = reinterpret_cast<float4*>(p.ring + (bh * 2 + ((j + 1) & 1)) * PN) + 8 * ph * NS + n;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          d4[q * NS] = make_float4(a_chunk * sin[4 * q] + sl[4 * q], a_chunk * sin[4 * q + 1] + sl[4 * q + 1],
+                                   a_chunk * sin[4 * q + 2] + sl[4 * q + 2], a_chunk * sin[4 * q + 3] + sl[4 * q + 3]);
+        if (fin) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) fin[(32 * ph + i) * NS + n] = a_chunk * sin[i] + sl[i];
+        }
       }
-    }
-    // publish the outgoing state first; the bf16 copies below are off the chain's critical path
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) st_release(&flags[j + 1], kFlagReady);
-    umma::mbar_wait(&bars[2], 0, p.status);  // MMA2 has read the scores that share the S_in tile
-    if (active) {
-      // S_in[j] in bf16: B operand of MMA4 ([n][p], p contiguous) and the saved state
-      uint4 pk[4];
+      // publish the outgoing state first; the bf16 copies below are off the chain's critical path
+      // the barrier orders every thread's ring writes before thread 0's release (cumulative)
+      __syncthreads();
+      if (tid == 0) st_release(&flags[j + 1], kFlagReady);
+      umma::mbar_wait(&bars[2], par, p.status);  // MMA2 has read the scores (S_in tile) and X / Xp
+      if (tid == 0 && pf == 1) {
+        fwd_load_x(p, sX, sXp, &bars[0], nu);
+        pf = 2;
+      }
+      if (active) {
+        // S_in[j] in bf16: B operand of MMA4 ([n][p], p contiguous) and the saved state
+        uint4 pk[4];
 #pragma unroll
-      for (int qd = 0; qd < 4; ++qd)
-        pk[qd] = make_uint4(pack_bf16(sin[qd * 8 + 0], sin[qd * 8 + 1]), pack_bf16(sin[qd * 8 + 2], sin[qd * 8 + 3]),
-                            pack_bf16(sin[qd * 8 + 4], sin[qd * 8 + 5]), pack_bf16(sin[qd * 8 + 6], sin[qd * 8 + 7]));
+        for (int qd = 0; qd < 4; ++qd)
+          pk[qd] = make_uint4(pack_bf16(sin[qd * 8 + 0], sin[qd * 8 + 1]), pack_bf16(sin[qd * 8 + 2], sin[qd * 8 + 3]),
+                              pack_bf16(sin[qd * 8 + 4], sin[qd * 8 + 5]), pack_bf16(sin[qd * 8 + 6], sin[qd * 8 + 7]));
 #pragma unroll
-      for (int qd = 0; qd < 4; ++qd) *reinterpret_cast<uint4*>(sSin + umma::sw128_offset(n, 4 * ph + qd)) = pk[qd];
+        for (int qd = 0; qd < 4; ++qd) *reinterpret_cast<uint4*>(sSin + umma::sw128_offset(n, 4 * ph + qd)) = pk[qd];
+      }
+      umma::fence_proxy_async_smem();
+      umma::fence_before_sync();
+      __syncthreads();
+      if (tid == 0) {
+        if (p.states) {
+          // the saved state is the shared-memory image itself (bf16, 128-byte swizzle), so the
+          // backward can bulk-copy it back into place
+          umma::bulk_store(reinterpret_cast<unsigned char*>(p.states) + (bh * p.nc + j) * (int64_t)NS * 128, sSin,
+                           NS * 128);
+          umma::bulk_commit();
+        }
+        umma::fence_after_sync();
+        const uint32_t q0 = umma::smem_u32(sQ), sin0 = umma::smem_u32(sSin);
+        constexpr uint32_t id4 = umma::idesc_bf16(64, 64, false, true);
+#pragma unroll
+        for (int ks = 0; ks < NS / 16; ++ks) {
+          const uint32_t qb = ks >> 2, kin = ks & 3;
+          umma::mma_bf16(tmem + 128 + (16u << 16), umma::desc_sw128(q0 + qb * 8192 + kin * 32, 16, 1024),
+                         umma::desc_sw128(sin0 + ks * 2048, 8192, 1024), id4, ks > 0);
+        }
+        umma::mma_commit(&bars[3]);
+      }
+      ok = __syncthreads_and(umma::mbar_wait(&bars[3], par, p.status));
+      nxt = misc[3];
+      if (tid < 64 && nxt < total) fwd_prefetch_scalars(p, decode_ticket(nxt, p.B, p.H, p.G), tid, s_nx);
+    } else if (tid == 0) {
+      st_release(&flags[j + 1], kFlagAbort);
     }
-    umma::fence_proxy_async_smem();
-    umma::fence_before_sync();
-    __syncthreads();
-    if (tid == 0) {
-      if (p.states) {
-        // the saved state is the shared-memory image itself (bf16, 128-byte swizzle), so the
-        // backward can bulk-copy it back into place
-        umma::bulk_store(reinterpret_cast<unsigned char*>(p.states) + (bh * p.nc + j) * (int64_t)NS * 128, sSin,
-                         NS * 128);
+    if (ok) {
+      umma::fence_after_sync();
+      // MMA4 is done with Q: the next chunk's Q tiles complete its operand set
+      if (tid == 0 && pf == 2) {
+        fwd_load_q<NS>(p, sQ, &bars[0], nu);
+        pf = 3;
+      }
+      // y = Yi + e^{c_t} Ye  (mamba3.py:55), staged as a bf16 tile over [wgX | wbXp] and TMA-stored
+      const int sp = warp & 3, ph = warp >> 2;
+      const int t = 16 * sp + (lane & 15);
+      float v[32];
+      umma::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + 128 + 32 * ph, v);
+      const float ect = s_ec[t];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += ect * __shfl_xor_sync(0xffffffffu, v[i], 16);
+      if (lane < 16) {
+#pragma unroll
+        for (int qd = 0; qd < 4; ++qd)
+          *reinterpret_cast<uint4*>(sXs + umma::sw128_offset(t, 4 * ph + qd)) =
+              make_uint4(pack_bf16(v[8 * qd], v[8 * qd + 1]), pack_bf16(v[8 * qd + 2], v[8 * qd + 3]),
+                         pack_bf16(v[8 * qd + 4], v[8 * qd + 5]), pack_bf16(v[8 * qd + 6], v[8 * qd + 7]));
+      }
+      umma::fence_proxy_async_smem();
+      umma::fence_before_sync();
+      __syncthreads();
+      if (tid == 0) {
+        umma::tma_store_4d(&p.ty, sXs, 0, h, t0, b);
         umma::bulk_commit();
       }
-      umma::fence_after_sync();
-      const uint32_t q0 = umma::smem_u32(sQ), sin0 = umma::smem_u32(sSin);
-      constexpr uint32_t id4 = umma::idesc_bf16(64, 64, false, true);
-#pragma unroll
-      for (int ks = 0; ks < NS / 16; ++ks) {
-        const uint32_t qb = ks >> 2, kin = ks & 3;
-        umma::mma_bf16(tmem + 128 + (16u << 16), umma::desc_sw128(q0 + qb * 8192 + kin * 32, 16, 1024),
-                       umma::desc_sw128(sin0 + ks * 2048, 8192, 1024), id4, ks > 0);
+    }
+    __syncthreads();  // every read of this chunk's tiles is done
+    if (!ok) {
+      // leave after an error: the ticket already taken is aborted, and any of its loads that were
+      // issued are completed (the rest issued too) so that none is in flight at exit
+      if (tid == 0 && nx < total) {
+        const UnitIdx cn = decode_ticket(nx, p.B, p.H, p.G);
+        st_release(&p.flags[cn.bh * (p.nc + 1) + cn.chunk + 1], kFlagAbort);
+        if (pf > 0) {
+          if (pf < 2) fwd_load_x(p, sX, sXp, &bars[0], cn);
+          if (pf < 3) fwd_load_q<NS>(p, sQ, &bars[0], cn);
+          umma::mbar_wait(&bars[0], par ^ 1, p.status);
+        }
       }
-      umma::mma_commit(&bars[3]);
+      break;
     }
-    ok = __syncthreads_and(umma::mbar_wait(&bars[3], 0, p.status));
-  } else if (tid == 0) {
-    st_release(&flags[j + 1], kFlagAbort);
-  }
-  if (ok) {
-    umma::fence_after_sync();
-    // y = Yi + e^{c_t} Ye  (mamba3.py:55), staged as a bf16 tile over [wgX | wbXp] and TMA-stored
-    const int sp = warp & 3, ph = warp >> 2;
-    const int t = 16 * sp + (lane & 15);
-    float v[32];
-    umma::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + 128 + 32 * ph, v);
-    const float ect = s_ec[t];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] += ect * __shfl_xor_sync(0xffffffffu, v[i], 16);
-    if (lane < 16) {
-#pragma unroll
-      for (int qd = 0; qd < 4; ++qd)
-        *reinterpret_cast<uint4*>(sXs + umma::sw128_offset(t, 4 * ph + qd)) =
-            make_uint4(pack_bf16(v[8 * qd], v[8 * qd + 1]), pack_bf16(v[8 * qd + 2], v[8 * qd + 3]),
-                       pack_bf16(v[8 * qd + 4], v[8 * qd + 5]), pack_bf16(v[8 * qd + 6], v[8 * qd + 7]));
-    }
-    umma::fence_proxy_async_smem();
-    __syncthreads();
-    if (tid == 0) {
-      umma::tma_store_4d(&p.ty, sXs, 0, h, t0, b);
-      umma::bulk_commit();
-    }
+    cur = nxt;
   }
   if (tid == 0) umma::bulk_wait_all();  // staged tiles must be read out before exit
+  if (tid < 64) umma::cp_async_wait_all();
   umma::fence_before_sync();
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tmem, 256);
@@ -591,7 +675,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
 
   for (uint32_t it = 0; cur < total; ++it) {
     const int stage = it & 1;
-    const uint32_t ph = it & 1;  // parity of this chunk's MMA-group barriers
+    const uint32_t par = it & 1;  // parity of this chunk's MMA-group barriers
     unsigned char* sQ = sm + stage * S::STAGE + S::Q;
     unsigned char* sKK = sm + stage * S::STAGE + S::KK;
     unsigned char* sXX = sm + stage * S::STAGE + S::XX;
@@ -678,7 +762,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
                          ks > 0);
         umma::mma_commit(&bars[2]);
       }
-      ok = __syncthreads_and(umma::mbar_wait(&bars[2], ph, p.status));
+      ok = __syncthreads_and(umma::mbar_wait(&bars[2], par, p.status));
     }
     if (ok) {
       umma::fence_after_sync();
@@ -777,7 +861,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
           prefetched = true;
         }
       }
-      const bool g2 = umma::mbar_wait(&bars[3], ph, p.status);
+      const bool g2 = umma::mbar_wait(&bars[3], par, p.status);
       if (g2) scale_rows(sXX, sXW, 16384, s_wgb, tid);
       ok = __syncthreads_and(g2) && misc[2] == kFlagReady;
       nxt = misc[3];
@@ -819,7 +903,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
         }
       }
       // publish G[j] first; Gn in bf16 and <Gn, S_in> are off the chain's critical path
-      __threadfence();
+      // the barrier orders every thread's ring writes before thread 0's release (cumulative)
       __syncthreads();
       if (tid == 0) st_release(&flags[j], kFlagReady);
       if (active) {
@@ -857,7 +941,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
         }
         umma::mma_commit(&bars[4]);
       }
-      ok = __syncthreads_and(umma::mbar_wait(&bars[4], ph, p.status));
+      ok = __syncthreads_and(umma::mbar_wait(&bars[4], par, p.status));
     } else if (tid == 0) {
       st_release(&flags[j], kFlagAbort);
     }
@@ -1196,7 +1280,7 @@ __global__ void __launch_bounds__(kStThreads) ssd_state_tc_kernel(const __grid_c
         }
       }
     }
-    __threadfence();
+    // the barrier orders every thread's ring writes before thread 0's release (cumulative)
     __syncthreads();
     if (tid == 0) st_release(&flags[BACKWARD ? j : j + 1], ok ? kFlagReady : kFlagAbort);
   } else if (tid == 0) {
@@ -1287,7 +1371,8 @@ int launch_fwd(const zb_ssd_args* a, ChainSync sync, void* states, void* ring, c
   auto k = ssd_fwd_tc_kernel<NS>;
   const int smem = (int)FwdSmem<NS>::ALLOC;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return ZB_ERR_CUDA;
-  const dim3 grid((unsigned)(a->B * a->H * p.nc));
+  const int64_t units = a->B * a->H * p.nc, slots = 2 * (int64_t)sm_count();  // persistent: two CTAs per SM
+  const dim3 grid((unsigned)(units < slots ? units : slots));
   k<<<grid, kTcThreads, smem, stream>>>(p);
   note_launches(1);
   return cudaPeekAtLastError() == cudaSuccess ? ZB_OK : ZB_ERR_CUDA;
