@@ -142,6 +142,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
     for (int i = 0; i < 5; ++i) umma::mbar_init(&bars[i], 1);
     umma::mbar_fence_init();
   }
+  __syncwarp();  // lane 0 of warp 0 rejoins before the warp-collective allocation
   if (warp == 0) {
     umma::tmem_alloc(&misc[0], 256);
     umma::tmem_relinquish();
@@ -477,10 +478,12 @@ struct BwdSmem {
   // shared work tiles, reused phase by phase
   static constexpr uint32_t W = 2 * STAGE;          // dYe -> [A | Ap] -> [wgX | wbXp]
   static constexpr uint32_t E = W + 16384;          // [Eg | Epb] -> Gn [NS n][64 p]
-  static constexpr uint32_t SCAL = E + 16384;       // c ec w wg wb g b, next chunk's adt g b (64 floats each)
-  static constexpr uint32_t RED = SCAL + 10 * 256;
-  // RED: rowZ[4][64] | colZ[4][128] | colE[4][128] | xu[4][128] | dcint[2][64] | da[16] | tmp[8]
-  static constexpr uint32_t RED_FLOATS = 256 + 512 + 512 + 512 + 128 + 16 + 8;
+  // per-chunk scalars [c | ec | w | wg wb | g | b] (64 floats each), one block per chunk parity,
+  // then the next chunk's staged [adt | gamma | beta]
+  static constexpr uint32_t SCAL = E + 16384;
+  static constexpr uint32_t RED = SCAL + (2 * 448 + 192) * 4;
+  // RED: rowZ[4][64] | colZ[4][128] | colE[4][128] | xu[4][128] | dcint[2][64] | da[16] | tmp[8] | pre[3][64]
+  static constexpr uint32_t RED_FLOATS = 256 + 512 + 512 + 512 + 128 + 16 + 8 + 192;
   static constexpr uint32_t BAR = RED + RED_FLOATS * 4;  // stage loads [2], MMA groups 1-3
   static constexpr uint32_t MISC = BAR + 5 * 8;          // tmem base, ticket, chain result, next ticket
   static constexpr uint32_t TOTAL = MISC + 16;
@@ -625,6 +628,26 @@ __device__ __forceinline__ void bwd_prefetch_scalars(const TcBwdParams& p, const
   umma::cp_async_commit();
 }
 
+// Two warps (token s = 0-63 per thread): the in-chunk cumulative sum c of adt and the per-token
+// weights of one chunk, from its staged [adt | gamma | beta], into sc = [c | ec | w | wg wb | g | b]
+// (mamba3.py:40).  The two warps meet at named barrier 2.
+__device__ __forceinline__ void bwd_chunk_scalars(float* sc, const float* nx, int s, int lane) {
+  const float gm = nx[64 + s], bt = nx[128 + s];
+  float c = warp_incl_scan(nx[s], lane);
+  if (s == 31) sc[31] = c;
+  asm volatile("bar.sync 2, 64;" ::: "memory");
+  if (s >= 32) c += sc[31];
+  if (s != 31) sc[s] = c;
+  asm volatile("bar.sync 2, 64;" ::: "memory");
+  const float w = expf(sc[63] - c);
+  sc[64 + s] = expf(c);
+  sc[128 + s] = w;
+  sc[192 + s] = w * gm;
+  sc[256 + s] = w * bt;
+  sc[320 + s] = gm;
+  sc[384 + s] = bt;
+}
+
 template <int NS>
 __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid_constant__ TcBwdParams p) {
   using S = BwdSmem<NS>;
@@ -636,13 +659,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
   unsigned char* sXW = sW;   // [wgX | wbXp] (128 rows)
   unsigned char* sEG = sm + S::E;  // [Eg | Epb] [2][64 t][64 s]
   unsigned char* sGN = sm + S::E;  // Gn [NS n][64 p]
-  float* s_c = reinterpret_cast<float*>(sm + S::SCAL);
-  float* s_ec = s_c + 64;
-  float* s_w = s_c + 128;
-  float* s_wgb = s_c + 192;  // [wg (64) | wb (64)]
-  float* s_g = s_c + 320;
-  float* s_b = s_c + 384;
-  float* s_nx = s_c + 448;   // next chunk's [adt | gamma | beta]
+  float* s_scal = reinterpret_cast<float*>(sm + S::SCAL);  // [2 parity][c | ec | w | wg wb | g | b]
+  float* s_nx = s_scal + 2 * 448;                            // next chunk's [adt | gamma | beta]
   float* s_rowZ = reinterpret_cast<float*>(sm + S::RED);  // [2 column block][2 half][64]
   float* s_colZ = s_rowZ + 256;                           // [4][128]
   float* s_colE = s_colZ + 512;                           // [4][128]
@@ -650,16 +668,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
   float* s_dcint = s_xu + 512;                            // [2][64]
   float* s_da = s_dcint + 128;                            // [16]
   float* s_tmp = s_da + 16;                               // [8]
+  float* s_pre = s_tmp + 8;                               // [rowZ - colZ | colE g | colE b] per token
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::BAR);
   uint32_t* misc = reinterpret_cast<uint32_t*>(sm + S::MISC);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool scal_warp = (warp == 2 || warp == 3);  // stage and prepare the next chunk's scalars
   const int64_t total = p.B * p.H * p.nc;
   if (tid == 0) {
     misc[1] = atomicAdd(p.ticket, 1u);
     for (int i = 0; i < 5; ++i) umma::mbar_init(&bars[i], 1);
     umma::mbar_fence_init();
   }
+  __syncwarp();  // lane 0 of warp 0 rejoins before the warp-collective allocation
   if (warp == 0) {
     umma::tmem_alloc(&misc[0], 512);
     umma::tmem_relinquish();
@@ -670,8 +691,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
   const uint32_t tmem = misc[0];
   const uint32_t R0 = tmem, R1 = tmem + 128, R2 = tmem + 256, R3 = tmem + 320, R4 = tmem + 384;
   uint32_t cur = misc[1];
-  if (tid == 0 && cur < total) bwd_issue_loads<NS>(p, sm, &bars[0], bwd_chunk(p, cur));
-  if (tid < 64 && cur < total) bwd_prefetch_scalars(p, bwd_chunk(p, cur), tid, s_nx);
+  if (cur < total) {
+    if (tid == 0) bwd_issue_loads<NS>(p, sm, &bars[0], bwd_chunk(p, cur));
+    if (scal_warp) {
+      bwd_prefetch_scalars(p, bwd_chunk(p, cur), tid - 64, s_nx);
+      umma::cp_async_wait_all();
+      bwd_chunk_scalars(s_scal, s_nx, tid - 64, lane);
+    }
+  }
 
   for (uint32_t it = 0; cur < total; ++it) {
     const int stage = it & 1;
@@ -691,26 +718,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
     uint32_t nx = 0, nxt = 0;
     bool prefetched = false;
     if (tid == 32) nx = atomicAdd(p.ticket, 1u);
-    if (tid < 64) {
-      umma::cp_async_wait_all();  // this thread's own copies
-      s_g[tid] = s_nx[64 + tid];
-      s_b[tid] = s_nx[128 + tid];
-      s_c[tid] = warp_incl_scan(s_nx[tid], lane);
-    }
-    for (int i = tid; i < S::RED_FLOATS; i += kBwdThreads) s_rowZ[i] = 0.f;
-    __syncthreads();
-    if (tid >= 32 && tid < 64) s_c[tid] += s_c[31];
-    __syncthreads();
-    if (tid < 64) {
-      const float c = s_c[tid], w = expf(s_c[63] - c);
-      s_ec[tid] = expf(c);
-      s_w[tid] = w;
-      s_wgb[tid] = w * s_g[tid];
-      s_wgb[64 + tid] = w * s_b[tid];
-    }
+    // this chunk's scalars were prepared by the end of the previous one (or before the loop)
+    const float* s_c = s_scal + (it & 1) * 448;
+    const float* s_ec = s_c + 64;
+    const float* s_w = s_c + 128;
+    const float* s_wgb = s_c + 192;  // [wg (64) | wb (64)]
+    const float* s_g = s_c + 320;
+    const float* s_b = s_c + 384;
     const bool load_ok = umma::mbar_wait(&bars[stage], (it >> 1) & 1, p.status);
-    const float a_chunk = expf(s_c[63]);
     bool ok = __syncthreads_and(load_ok);
+    const float a_chunk = expf(s_c[63]);
 
     if (ok) {
       // the products that need no rescaled operand start right away
@@ -862,12 +879,63 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
         }
       }
       const bool g2 = umma::mbar_wait(&bars[3], par, p.status);
-      if (g2) scale_rows(sXX, sXW, 16384, s_wgb, tid);
+      if (g2) {
+        scale_rows(sXX, sXW, 16384, s_wgb, tid);
+        // dQ is final after the second group: it leaves TMEM for the dq staging tile over Q (dead
+        // now) while the hand-off is awaited, with the dc inter term from Ye (R1 lanes +16).
+        // Warps 0 and 1 carry the wait and the producer; warps 4 and 5 take their share.
+        if (warp >= 2) {
+          umma::fence_after_sync();
+          const int sp = warp & 3;
+#pragma unroll 1
+          for (int cq = (warp == 4 || warp == 5) ? 0 : (warp >> 2); cq <= (warp >> 2); ++cq) {
+            if (32 * cq < NS) {
+              const int t = 16 * sp + (lane & 15);
+              float v[32];
+              umma::tmem_ld32(R1 + ((uint32_t)(32 * sp) << 16) + 32 * cq, v);
+              if (lane < 16) stage_row32(sQ + (cq >> 1) * 8192, t, 4 * (cq & 1), v);
+              if (lane >= 16 && cq < 2) {
+                float acc = 0.f;
+#pragma unroll
+                for (int qd = 0; qd < 4; ++qd) {
+                  float d[8];
+                  load_chunk(sDY, t, 4 * cq + qd, d);
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) acc += d[e] * v[8 * qd + e];
+                }
+                s_dcint[cq * 64 + t] = s_ec[t] * acc;
+              }
+            }
+          }
+          umma::fence_proxy_async_smem();
+        }
+        // per-token sums of the score epilogue, reduced off the final phase
+        if (scal_warp) {
+          const int s = tid - 64;
+          float colZ = 0.f, colEg = 0.f, colEb = 0.f, rowZ = 0.f;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            colZ += s_colZ[q * 128 + s] + s_colZ[q * 128 + 64 + s];
+            colEg += s_colE[q * 128 + s];
+            colEb += s_colE[q * 128 + 64 + s];
+            rowZ += s_rowZ[q * 64 + s];
+          }
+          s_pre[s] = rowZ - colZ;
+          s_pre[64 + s] = colEg;
+          s_pre[128 + s] = colEb;
+        }
+      }
+      umma::fence_before_sync();
       ok = __syncthreads_and(g2) && misc[2] == kFlagReady;
       nxt = misc[3];
-      if (tid < 64 && nxt < total) bwd_prefetch_scalars(p, bwd_chunk(p, nxt), tid, s_nx);  // for the next chunk
+      if (scal_warp && nxt < total) bwd_prefetch_scalars(p, bwd_chunk(p, nxt), tid - 64, s_nx);  // next chunk
     }
     if (ok) {
+      if (tid == 32) {  // dq leaves from its staging tile over Q
+#pragma unroll
+        for (int qb = 0; qb < S::QB; ++qb) umma::tma_store_4d(&p.tdq, sQ + qb * 8192, qb * 64, g, t0, b);
+        umma::bulk_commit();
+      }
       // reverse state hand-off: G[j] = dSl'^T + e^{c_L} G[j+1];  da = <G[j+1], S_in[j]>
       // warp w: sub-partition sp = w % 4 (state rows n), p-quarter pq = w / 4 (16 columns)
       const int sp = warp & 3, pq = warp >> 2;
@@ -950,32 +1018,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
       // warp w: sub-partition sp = w % 4, column quarter cq = w / 4
       const int sp = warp & 3, cq = warp >> 2;
       // Output tiles are staged (bf16, 128-byte swizzle) in shared memory that is dead by now and
-      // leave through TMA stores: dq -> Q tile, dk | dkp -> K/Kp tiles, dx | dxp -> X/Xp tiles (each
-      // thread overwrites exactly the X elements it has just read).
-      unsigned char* st_dq = sQ;
+      // leave through TMA stores: dk | dkp -> K/Kp tiles, dx | dxp -> X/Xp tiles (each thread
+      // overwrites exactly the X elements it has just read).  dq left during the hand-off.
       unsigned char* st_dk = sKK;
       unsigned char* st_dkp = sKK + S::QB * 8192;
       unsigned char* st_dx = sXX;
       unsigned char* st_dxp = sXX + 8192;
-      // (1) dQ rows (R1 lanes +0, columns [32 cq, 32 cq + 32)) and, for cq < 2, Ye rows (R1 lanes
-      // +16, same columns) for the dc inter term
-      if (32 * cq < NS) {
-        const int t = 16 * sp + (lane & 15);
-        float v[32];
-        umma::tmem_ld32(R1 + ((uint32_t)(32 * sp) << 16) + 32 * cq, v);
-        if (lane < 16) stage_row32(st_dq + (cq >> 1) * 8192, t, 4 * (cq & 1), v);
-        if (lane >= 16 && cq < 2) {
-          float acc = 0.f;
-#pragma unroll
-          for (int qd = 0; qd < 4; ++qd) {
-            float d[8];
-            load_chunk(sDY, t, 4 * cq + qd, d);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc += d[e] * v[8 * qd + e];
-          }
-          s_dcint[cq * 64 + t] = s_ec[t] * acc;
-        }
-      }
       // (2) dx / dxp rows: dXc (R2) + w g U (R3), columns [16 cq, 16 cq + 16); x.U partial sums for
       // dgamma / dbeta
       {
@@ -1010,7 +1058,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
       if (tid == 32) {  // the producer waits for these before reusing the stage
 #pragma unroll
         for (int qb = 0; qb < S::QB; ++qb) {
-          umma::tma_store_4d(&p.tdq, st_dq + qb * 8192, qb * 64, g, t0, b);
           umma::tma_store_4d(&p.tdk, st_dk + qb * 8192, qb * 64, g, t0, b);
           umma::tma_store_4d(&p.tdkp, st_dkp + qb * 8192, qb * 64, g, t0, b);
         }
@@ -1018,28 +1065,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
         umma::tma_store_4d(&p.tdxp, st_dxp, 0, h, t0, b);
         umma::bulk_commit();
       }
-      __syncthreads();
-      // per-token scalars: warps 0-1 own tokens 0-63
+      // per-token scalars: warps 0-1 own tokens 0-63; warps 2-3 prepare the next chunk's scalars
       if (tid < 64) {
         const int s = tid;
         float da = 0.f;
 #pragma unroll
         for (int i = 0; i < 16; ++i) da += s_da[i];
-        float xu = 0.f, xpu = 0.f, colZ = 0.f, colEg = 0.f, colEb = 0.f, rowZ = 0.f;
+        float xu = 0.f, xpu = 0.f;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           xu += s_xu[q * 128 + s];
           xpu += s_xu[q * 128 + 64 + s];
-          colZ += s_colZ[q * 128 + s] + s_colZ[q * 128 + 64 + s];
-          colEg += s_colE[q * 128 + s];
-          colEb += s_colE[q * 128 + 64 + s];
-          rowZ += s_rowZ[q * 64 + s];
         }
         const float w = s_w[s];
         const float dw = s_g[s] * xu + s_b[s] * xpu;
-        const float dg = colEg + w * xu;
-        const float db = colEb + w * xpu;
-        float dc = rowZ - colZ + s_dcint[s] + s_dcint[64 + s] - w * dw;
+        const float dg = s_pre[64 + s] + w * xu;
+        const float db = s_pre[128 + s] + w * xpu;
+        float dc = s_pre[s] + s_dcint[s] + s_dcint[64 + s] - w * dw;
         // dc_{L-1} += e^{c_L} da + sum_s w_s dw_s   (two warps: combine through shared memory)
         const float wdw = warp_sum(w * dw);
         if (lane == 0) s_tmp[warp] = wdw;
@@ -1056,6 +1098,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
         p.dadt[b * p.dasb + (int64_t)tt * p.dast + h * p.dash] = suffix;
         p.dgamma[b * p.dgsb + (int64_t)tt * p.dgst + h * p.dgsh] = dg;
         p.dbeta[b * p.dbsb + (int64_t)tt * p.dbst + h * p.dbsh] = db;
+      } else if (scal_warp && nxt < total) {
+        umma::cp_async_wait_all();  // this thread's own copies
+        bwd_chunk_scalars(s_scal + ((it + 1) & 1) * 448, s_nx, tid - 64, lane);
       }
     }
     __syncthreads();  // every read of this stage and of the work tiles is done
@@ -1071,7 +1116,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
     cur = nxt;
   }
   if (tid == 32) umma::bulk_wait_all();  // staged output tiles must be read out before exit
-  if (tid < 64) umma::cp_async_wait_all();
+  if (scal_warp) umma::cp_async_wait_all();
   umma::fence_before_sync();
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tmem, 512);
@@ -1134,6 +1179,7 @@ __global__ void __launch_bounds__(kStThreads) ssd_state_tc_kernel(const __grid_c
     umma::mbar_init(&bars[1], 1);
     umma::mbar_fence_init();
   }
+  __syncwarp();  // lane 0 of warp 0 rejoins before the warp-collective allocation
   if (warp == 0) {
     umma::tmem_alloc(&misc[0], 64);
     umma::tmem_relinquish();
