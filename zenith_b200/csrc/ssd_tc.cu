@@ -879,63 +879,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
         }
       }
       const bool g2 = umma::mbar_wait(&bars[3], par, p.status);
-      if (g2) {
-        scale_rows(sXX, sXW, 16384, s_wgb, tid);
-        // dQ is final after the second group: it leaves TMEM for the dq staging tile over Q (dead
-        // now) while the hand-off is awaited, with the dc inter term from Ye (R1 lanes +16).
-        // Warps 0 and 1 carry the wait and the producer; warps 4 and 5 take their share.
-        if (warp >= 2) {
-          umma::fence_after_sync();
-          const int sp = warp & 3;
-#pragma unroll 1
-          for (int cq = (warp == 4 || warp == 5) ? 0 : (warp >> 2); cq <= (warp >> 2); ++cq) {
-            if (32 * cq < NS) {
-              const int t = 16 * sp + (lane & 15);
-              float v[32];
-              umma::tmem_ld32(R1 + ((uint32_t)(32 * sp) << 16) + 32 * cq, v);
-              if (lane < 16) stage_row32(sQ + (cq >> 1) * 8192, t, 4 * (cq & 1), v);
-              if (lane >= 16 && cq < 2) {
-                float acc = 0.f;
-#pragma unroll
-                for (int qd = 0; qd < 4; ++qd) {
-                  float d[8];
-                  load_chunk(sDY, t, 4 * cq + qd, d);
-#pragma unroll
-                  for (int e = 0; e < 8; ++e) acc += d[e] * v[8 * qd + e];
-                }
-                s_dcint[cq * 64 + t] = s_ec[t] * acc;
-              }
-            }
-          }
-          umma::fence_proxy_async_smem();
-        }
-        // per-token sums of the score epilogue, reduced off the final phase
-        if (scal_warp) {
-          const int s = tid - 64;
-          float colZ = 0.f, colEg = 0.f, colEb = 0.f, rowZ = 0.f;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            colZ += s_colZ[q * 128 + s] + s_colZ[q * 128 + 64 + s];
-            colEg += s_colE[q * 128 + s];
-            colEb += s_colE[q * 128 + 64 + s];
-            rowZ += s_rowZ[q * 64 + s];
-          }
-          s_pre[s] = rowZ - colZ;
-          s_pre[64 + s] = colEg;
-          s_pre[128 + s] = colEb;
-        }
-      }
-      umma::fence_before_sync();
+      if (g2) scale_rows(sXX, sXW, 16384, s_wgb, tid);
       ok = __syncthreads_and(g2) && misc[2] == kFlagReady;
       nxt = misc[3];
       if (scal_warp && nxt < total) bwd_prefetch_scalars(p, bwd_chunk(p, nxt), tid - 64, s_nx);  // next chunk
     }
     if (ok) {
-      if (tid == 32) {  // dq leaves from its staging tile over Q
-#pragma unroll
-        for (int qb = 0; qb < S::QB; ++qb) umma::tma_store_4d(&p.tdq, sQ + qb * 8192, qb * 64, g, t0, b);
-        umma::bulk_commit();
-      }
       // reverse state hand-off: G[j] = dSl'^T + e^{c_L} G[j+1];  da = <G[j+1], S_in[j]>
       // warp w: sub-partition sp = w % 4 (state rows n), p-quarter pq = w / 4 (16 columns)
       const int sp = warp & 3, pq = warp >> 2;
@@ -1009,6 +958,45 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
         }
         umma::mma_commit(&bars[4]);
       }
+      // While the third group runs: dQ (final since the second group) leaves TMEM for the dq staging
+      // tile over Q (dead now), with the dc inter term from Ye (R1 lanes +16); warps 2-3 reduce the
+      // per-token sums of the score epilogue.
+      {
+        __syncwarp();  // lane 0 rejoins warp 0 before the warp-collective TMEM load
+        umma::fence_after_sync();
+        const int sp = warp & 3, cq = warp >> 2;
+        if (32 * cq < NS) {
+          const int t = 16 * sp + (lane & 15);
+          float v[32];
+          umma::tmem_ld32(R1 + ((uint32_t)(32 * sp) << 16) + 32 * cq, v);
+          if (lane < 16) stage_row32(sQ + (cq >> 1) * 8192, t, 4 * (cq & 1), v);
+          if (lane >= 16 && cq < 2) {
+            float acc = 0.f;
+#pragma unroll
+            for (int qd = 0; qd < 4; ++qd) {
+              float d[8];
+              load_chunk(sDY, t, 4 * cq + qd, d);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) acc += d[e] * v[8 * qd + e];
+            }
+            s_dcint[cq * 64 + t] = s_ec[t] * acc;
+          }
+        }
+        if (scal_warp) {
+          const int s = tid - 64;
+          float colZ = 0.f, colEg = 0.f, colEb = 0.f, rowZ = 0.f;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            colZ += s_colZ[q * 128 + s] + s_colZ[q * 128 + 64 + s];
+            colEg += s_colE[q * 128 + s];
+            colEb += s_colE[q * 128 + 64 + s];
+            rowZ += s_rowZ[q * 64 + s];
+          }
+          s_pre[s] = rowZ - colZ;
+          s_pre[64 + s] = colEg;
+          s_pre[128 + s] = colEb;
+        }
+      }
       ok = __syncthreads_and(umma::mbar_wait(&bars[4], par, p.status));
     } else if (tid == 0) {
       st_release(&flags[j], kFlagAbort);
@@ -1018,8 +1006,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
       // warp w: sub-partition sp = w % 4, column quarter cq = w / 4
       const int sp = warp & 3, cq = warp >> 2;
       // Output tiles are staged (bf16, 128-byte swizzle) in shared memory that is dead by now and
-      // leave through TMA stores: dk | dkp -> K/Kp tiles, dx | dxp -> X/Xp tiles (each thread
-      // overwrites exactly the X elements it has just read).  dq left during the hand-off.
+      // leave through TMA stores: dq -> Q tile (staged while the third group ran), dk | dkp -> K/Kp
+      // tiles, dx | dxp -> X/Xp tiles (each thread overwrites exactly the X elements it has just read).
+      unsigned char* st_dq = sQ;
       unsigned char* st_dk = sKK;
       unsigned char* st_dkp = sKK + S::QB * 8192;
       unsigned char* st_dx = sXX;
@@ -1058,6 +1047,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
       if (tid == 32) {  // the producer waits for these before reusing the stage
 #pragma unroll
         for (int qb = 0; qb < S::QB; ++qb) {
+          umma::tma_store_4d(&p.tdq, st_dq + qb * 8192, qb * 64, g, t0, b);
           umma::tma_store_4d(&p.tdk, st_dk + qb * 8192, qb * 64, g, t0, b);
           umma::tma_store_4d(&p.tdkp, st_dkp + qb * 8192, qb * 64, g, t0, b);
         }
