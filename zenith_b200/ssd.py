@@ -149,6 +149,9 @@ def _setup_context(ctx, inputs, output):
     ctx.chunk_size = chunk_size
     ctx.has_init = initial_state is not None
     ctx.state_only = state_only
+    # gradients of unused outputs (the final state, the saved-state bytes) arrive as None rather
+    # than as zero-filled tensors; the backward treats None as zero
+    ctx.set_materialize_grads(False)
     saved = [x, q, k, kp, xp, adt, gamma, beta, states]
     if initial_state is not None:
         saved.append(initial_state)
