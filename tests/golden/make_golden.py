@@ -11,6 +11,10 @@ reference ``repeat_interleave``d q/k/kp (the reference has no groups), so autogr
 per-head gradients over each group.  The final state comes from the reference test's
 per-token recurrence (tests/test_mamba3.py:10-21), imported from the reference's tests.
 
+It also runs the reference ``Mamba3`` module (zenith/mamba3.py:58-119) with its input and
+output projections replaced by identities, for the fused layer body (prologue, scan, D skip,
+silu gate): the split tensors, the parameters, the output and every gradient.
+
 The fixtures are consumed by tests/test_oracle.py (CPU) and the GPU parity tests; nothing at
 run time reads the reference.
 """
@@ -84,6 +88,47 @@ def naive_final_state(naive, x, q, k, kp, xp, adt, gamma, beta):
     return y[:, -1].reshape(N, B, H, P).permute(1, 2, 3, 0).contiguous()   # [B,H,P,N]
 
 
+def mamba3_case(Mamba3, B, T, H, P, N, chunk, A_floor, seed):
+    """The layer body of the reference ``Mamba3`` module (zenith/mamba3.py:96-119) between the
+    ``in_proj`` split and ``out_proj``: both projections are replaced by identities, so the
+    module's input is the concatenation of the split tensors and its output is the gated y.
+    autograd; parameters are perturbed away from their initial values so that every
+    parameter gradient is generic.  The reference forward upcasts to float32 (``x.float()``,
+    mamba3.py:102), so the module runs in float32: the fixtures carry float32 precision."""
+    torch.manual_seed(seed)
+    m = Mamba3(d_model=H * P // 2, d_state=N, expand=2, headdim=P, chunk_size=chunk, A_floor=A_floor)
+    m.in_proj = torch.nn.Identity()
+    m.out_proj = torch.nn.Identity()
+    g = torch.Generator().manual_seed(seed + 100)
+    with torch.no_grad():
+        m.B_bias.add_(0.3 * torch.randn(m.B_bias.shape, generator=g))
+        m.C_bias.add_(0.3 * torch.randn(m.C_bias.shape, generator=g))
+        m.B_norm.weight.add_(0.2 * torch.randn(N, generator=g))
+        m.C_norm.weight.add_(0.2 * torch.randn(N, generator=g))
+        m.D.add_(0.5 * torch.randn(H, generator=g))
+    NA = N // 4
+    sizes = [H * P, H * P, N, N, H, H, H, NA]
+    names = ("z", "x", "Bm", "Cm", "dd_dt", "dd_A", "trap", "ang")
+    u = torch.randn(B, T, sum(sizes), generator=g).requires_grad_(True)
+    out = m(u)
+    dout = torch.randn(out.shape, generator=g)
+    out.backward(dout)
+    blob = {"chunk_size": np.array(chunk), "A_floor": np.array(A_floor), "eps": np.array(m.B_norm.eps)}
+    shapes = {"z": (B, T, H, P), "x": (B, T, H, P), "Bm": (B, T, N), "Cm": (B, T, N), "dd_dt": (B, T, H),
+              "dd_A": (B, T, H), "trap": (B, T, H), "ang": (B, T, NA)}
+    for n, piece, gpiece in zip(names, torch.split(u.detach(), sizes, dim=-1), torch.split(u.grad, sizes, dim=-1)):
+        blob["in_" + n] = piece.reshape(shapes[n]).numpy()
+        blob["out_d" + n] = gpiece.reshape(shapes[n]).numpy()
+    params = {"dt_bias": m.dt_bias, "B_bias": m.B_bias, "C_bias": m.C_bias, "B_norm_w": m.B_norm.weight,
+              "C_norm_w": m.C_norm.weight, "D": m.D}
+    for n, prm in params.items():
+        blob["in_" + n] = prm.detach().numpy()
+        blob["out_d" + n] = prm.grad.numpy()
+    blob["in_dout"] = dout.reshape(B, T, H, P).numpy()
+    blob["out_out"] = out.detach().reshape(B, T, H, P).numpy()
+    return blob
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -130,6 +175,20 @@ def main():
         path = HERE / f"{name}.npz"
         np.savez_compressed(path, **blob)
         print(f"{name}: chunk {chunk}, naive-vs-chunked {err:.2e}, {path.stat().st_size / 1e3:.0f} kB")
+
+    # 3. the Mamba-3 layer body around the scan (prologue: discretisation, RMSNorm, RoPE, shift;
+    #    epilogue: D skip and silu gate), from the reference module itself (float32, as it runs).
+    from zenith.mamba3 import Mamba3
+    m3 = {
+        "mamba3_small_f32": (2, 128, 4, 16, 16, 32, 1e-4, 11),
+        "mamba3_wide_f32": (1, 96, 3, 8, 32, 16, 1e-4, 12),
+        "mamba3_floor_f32": (2, 64, 2, 8, 16, 16, -0.5, 13),   # negative floor: the clamp lets A vary
+    }
+    for name, (B, T, H, P, N, chunk, A_floor, seed) in m3.items():
+        blob = mamba3_case(Mamba3, B, T, H, P, N, chunk, A_floor, seed)
+        path = HERE / f"{name}.npz"
+        np.savez_compressed(path, **blob)
+        print(f"{name}: B{B} T{T} H{H} P{P} N{N} chunk {chunk}, {path.stat().st_size / 1e3:.0f} kB")
 
 
 if __name__ == "__main__":

@@ -6,7 +6,7 @@ import torch
 
 GOLDEN = pathlib.Path(__file__).resolve().parent / "golden"
 NAMES = ("x", "q", "k", "kp", "xp", "adt", "gamma", "beta")
-CASES = sorted(p.stem for p in GOLDEN.glob("*.npz"))
+CASES = sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith("mamba3_"))  # scan-boundary cases
 
 
 def load(name):
@@ -14,3 +14,16 @@ def load(name):
     inp = {n: torch.from_numpy(z["in_" + n]) for n in NAMES + ("dy",)}
     out = {k[4:]: torch.from_numpy(z[k]) for k in z.files if k.startswith("out_")}
     return inp, out, int(z["chunk_size"])
+
+
+MAMBA3_CASES = ("mamba3_small_f32", "mamba3_wide_f32", "mamba3_floor_f32")
+
+
+def load_mamba3(name):
+    """Inputs and parameters, upstream gradient, output and all gradients of one layer-body case
+    (written from the reference ``Mamba3`` module by make_golden.py)."""
+    z = np.load(GOLDEN / f"{name}.npz")
+    tensors = {k[3:]: torch.from_numpy(z[k]) for k in z.files if k.startswith("in_") and k != "in_dout"}
+    ref = {k[4:]: torch.from_numpy(z[k]) for k in z.files if k.startswith("out_")}
+    meta = {"A_floor": float(z["A_floor"]), "chunk": int(z["chunk_size"]), "eps": float(z["eps"])}
+    return tensors, torch.from_numpy(z["in_dout"]), ref, meta

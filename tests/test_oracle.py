@@ -3,7 +3,8 @@ import pytest
 import torch
 
 from oracle.ssd_oracle import max_rel_err, naive_recurrence, ssd_backward, ssd_forward
-from tests.golden_io import CASES, NAMES, load
+from oracle import mamba3_oracle
+from tests.golden_io import CASES, MAMBA3_CASES, NAMES, load, load_mamba3
 
 
 @pytest.mark.parametrize("case", CASES)
@@ -68,3 +69,18 @@ def test_oracle_rejects_length_not_multiple_of_chunk():
     a = torch.zeros(1, 10, 1, dtype=torch.float64)
     with pytest.raises(AssertionError, match="multiple of chunk_size"):
         ssd_forward(t, n, n, n, t, a, a, a, 4)
+
+
+@pytest.mark.parametrize("case", MAMBA3_CASES)
+def test_mamba3_oracle_matches_reference_module(case):
+    """The layer-body oracle (prologue, scan, D skip, silu gate) against the reference Mamba3
+    module run in float32 with autograd: the output and every input / parameter gradient."""
+    tensors, dout, ref, meta = load_mamba3(case)
+    out, grads = mamba3_oracle.forward_backward(tensors, dout, meta["A_floor"], meta["chunk"], meta["eps"])
+    assert max_rel_err(out, ref["out"].double()) < 2e-6
+    for n in mamba3_oracle.INPUTS + mamba3_oracle.PARAMS:
+        r = ref["d" + n].double()
+        if r.abs().max() == 0:   # dd_A: the A_floor clamp is saturated (mamba3.py:105)
+            assert grads["d" + n].abs().max() == 0, n
+        else:
+            assert max_rel_err(grads["d" + n], r) < 2e-6, n
