@@ -89,12 +89,20 @@ class _Scan(torch.autograd.Function):
         return (None, *(g[n] for n in ("dx", "dq", "dk", "dkp", "dxp", "dadt", "dgamma", "dbeta")))
 
 
+def _round(t: torch.Tensor, dtype) -> torch.Tensor:
+    """Round to ``dtype`` and back; the gradient passes through unchanged."""
+    return t if dtype is None else t + (t.to(dtype).to(t.dtype) - t).detach()
+
+
 def forward(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D, A_floor, chunk,
-            eps=1e-5):
-    """(ssd(...) + D x) * silu(z): the layer body between the in_proj split and out_proj."""
+            eps=1e-5, scan_operand_dtype=None):
+    """(ssd(...) + D x) * silu(z): the layer body between the in_proj split and out_proj.
+    ``scan_operand_dtype`` rounds the scan's vector operands (x, q, k, kp, xp) to that dtype, as a
+    16-bit scan reads them; the D skip keeps the unrounded x."""
     q, k, kp, xp, adt, gamma, beta = prologue(x, Bm, Cm, dd_dt, dd_A, trap, ang, dt_bias, B_bias, C_bias, B_norm_w,
                                               C_norm_w, A_floor, eps)
-    y = _Scan.apply(chunk, x, q, k, kp, xp, adt, gamma, beta)
+    r = scan_operand_dtype
+    y = _Scan.apply(chunk, _round(x, r), _round(q, r), _round(k, r), _round(kp, r), _round(xp, r), adt, gamma, beta)
     y = y + D[:, None] * x
     return y if z is None else y * torch.nn.functional.silu(z)
 
@@ -103,11 +111,12 @@ INPUTS = ("x", "z", "Bm", "Cm", "dd_dt", "dd_A", "trap", "ang")
 PARAMS = ("dt_bias", "B_bias", "C_bias", "B_norm_w", "C_norm_w", "D")
 
 
-def forward_backward(tensors: dict, dout: torch.Tensor, A_floor: float, chunk: int, eps: float = 1e-5):
+def forward_backward(tensors: dict, dout: torch.Tensor, A_floor: float, chunk: int, eps: float = 1e-5,
+                     scan_operand_dtype=None):
     """Output and the gradients of every input and parameter (float64, autograd)."""
     leaves = {n: tensors[n].detach().to(F64).clone().requires_grad_(True) for n in INPUTS + PARAMS
               if tensors.get(n) is not None}
-    out = forward(*(leaves.get(n) for n in INPUTS + PARAMS), A_floor, chunk, eps)
+    out = forward(*(leaves.get(n) for n in INPUTS + PARAMS), A_floor, chunk, eps, scan_operand_dtype)
     out.backward(dout.to(F64))
     grads = {"d" + n: leaves[n].grad for n in leaves}
     return out.detach(), grads

@@ -10,3 +10,7 @@ __version__ = "0.1.0"
 from .parallel import cp_ssd  # noqa: E402  (context parallelism over torch.distributed)
 
 __all__.append("cp_ssd")
+
+from .mamba3 import mamba3_ssd_fused, use_b200_layer  # noqa: E402  (fused Mamba-3 layer body)
+
+__all__ += ["mamba3_ssd_fused", "use_b200_layer"]
