@@ -136,3 +136,39 @@ def test_fused_layer_rejects_length_not_multiple_of_chunk():
     dev = torch.device("cuda")
     with pytest.raises(AssertionError, match="sequence length must be a multiple of chunk_size"):
         zenith_b200.mamba3_ssd_fused(*(tensors[n].to(dev) for n in ALL), chunk_size=64)
+
+
+def test_fused_layer_reads_the_in_proj_split_in_place():
+    """Layer inputs as views into one [B, T, n_in] projection, as Mamba3.forward's torch.split makes
+    them (mamba3.py:98-100), including an odd column offset that rules out vector accesses."""
+    import zenith_b200
+
+    B, T, H, P, N = 2, 128, 3, 16, 32
+    tensors, dout, meta = _synthetic(B, T, H, P, N, seed=25)
+    sizes = [H * P, H * P, N, N, H, H, H, N // 4]
+    names = ("z", "x", "Bm", "Cm", "dd_dt", "dd_A", "trap", "ang")
+    dev = torch.device("cuda")
+    for pad in (0, 1):
+        u = torch.zeros(B, T, pad + sum(sizes), device=dev)
+        off = pad
+        views = {}
+        for n, sz in zip(names, sizes):
+            u[..., off:off + sz] = tensors[n].to(dev).reshape(B, T, sz)
+            views[n] = u[..., off:off + sz]
+            off += sz
+        u.requires_grad_(True)
+        pieces = torch.split(u[..., pad:], sizes, dim=-1)
+        v = dict(zip(names, pieces))
+        v["x"] = v["x"].view(B, T, H, P)
+        v["z"] = v["z"].view(B, T, H, P)
+        params = {n: tensors[n].to(dev).requires_grad_(True) for n in M.PARAMS}
+        out = zenith_b200.mamba3_ssd_fused(*(v[n] for n in M.INPUTS), *(params[n] for n in M.PARAMS),
+                                           A_floor=meta["A_floor"], chunk_size=64, scan_dtype=torch.float32)
+        out.backward(dout.to(dev))
+        ref_out, ref = M.forward_backward(tensors, dout, meta["A_floor"], 64, meta["eps"])
+        assert max_rel_err(out.detach().double().cpu(), ref_out) < 1e-4, pad
+        g = u.grad[..., pad:]
+        for n, piece in zip(names, torch.split(g, sizes, dim=-1)):
+            assert max_rel_err(piece.reshape(ref["d" + n].shape).double().cpu(), ref["d" + n]) < 1e-4, (pad, n)
+        for n in M.PARAMS:
+            assert max_rel_err(params[n].grad.double().cpu(), ref["d" + n]) < 1e-4, (pad, n)

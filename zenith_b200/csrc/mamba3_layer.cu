@@ -2,7 +2,7 @@
 // the prologue that turns the in_proj split into the scan operands (discretisation, RMSNorm,
 // RoPE, one-token shift) and the epilogue (D skip, silu gate).
 //
-// One CTA per (batch, 64-token segment), one warp per head (H <= 32).  Per-token RMSNorm and
+// One CTA per (batch, 64-token segment), one warp per head (H <= 31).  Per-token RMSNorm and
 // RoPE run lane-parallel over the state features: lane i owns RoPE pair i (features 2i, 2i+1)
 // and the pass-through pair (2A+2i, 2A+2i+1), A = N/4 angles.  theta = cumsum_t(DT ang) spans
 // the whole sequence; it crosses segments through per-segment sums (forward) and per-segment
@@ -26,6 +26,8 @@ constexpr int kSeg = 64;  // tokens per segment
 struct M3 {
   int64_t B, T, H, P, N;
   int NA, nseg;
+  bool pairs;  // B / C rows and their gradients allow 2-element accesses (checked on the host)
+  bool vec8;   // x, z, out, dout, dx, dz allow 16-byte accesses of 8 elements (checked on the host)
   float A_floor, eps;
   View x, z, Bm, Cm, dd_dt, dd_A, trap, ang;
   const float *dt_bias, *B_bias, *C_bias, *B_norm_w, *C_norm_w, *D;
@@ -78,18 +80,76 @@ struct Feat {
 };
 __device__ __forceinline__ Feat feat(int lane, int NA) { return {2 * lane, 2 * NA + 2 * lane, lane < NA}; }
 
-template <typename T> __device__ __forceinline__ void ld4(const T* row, Feat f, float (&v)[4]) {
-  v[0] = ldv<float>(row + f.f0);
-  v[1] = ldv<float>(row + f.f0 + 1);
-  v[2] = ldv<float>(row + f.f2);
-  v[3] = ldv<float>(row + f.f2 + 1);
+// two adjacent elements (an even feature index) as one access
+template <typename T> struct Pair;
+template <> struct Pair<float> {
+  static __device__ __forceinline__ float2 ld(const float* p) { return *reinterpret_cast<const float2*>(p); }
+  static __device__ __forceinline__ void st(float* p, float a, float b) { *reinterpret_cast<float2*>(p) = make_float2(a, b); }
+};
+template <> struct Pair<__nv_bfloat16> {
+  static __device__ __forceinline__ float2 ld(const __nv_bfloat16* p) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+  }
+  static __device__ __forceinline__ void st(__nv_bfloat16* p, float a, float b) {
+    *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(a, b);
+  }
+};
+
+// the lane's four features of a row; pairs = the row allows 2-element accesses
+template <typename T> __device__ __forceinline__ void ld4(const T* row, Feat f, float (&v)[4], bool pairs = true) {
+  if (pairs) {
+    const float2 a = Pair<T>::ld(row + f.f0), c = Pair<T>::ld(row + f.f2);
+    v[0] = a.x; v[1] = a.y; v[2] = c.x; v[3] = c.y;
+  } else {
+    v[0] = ldv<float>(row + f.f0);
+    v[1] = ldv<float>(row + f.f0 + 1);
+    v[2] = ldv<float>(row + f.f2);
+    v[3] = ldv<float>(row + f.f2 + 1);
+  }
 }
-template <typename T> __device__ __forceinline__ void st4(T* row, Feat f, const float (&v)[4]) {
-  stv<float>(row + f.f0, v[0]);
-  stv<float>(row + f.f0 + 1, v[1]);
-  stv<float>(row + f.f2, v[2]);
-  stv<float>(row + f.f2 + 1, v[3]);
+template <typename T> __device__ __forceinline__ void st4(T* row, Feat f, const float (&v)[4], bool pairs = true) {
+  if (pairs) {
+    Pair<T>::st(row + f.f0, v[0], v[1]);
+    Pair<T>::st(row + f.f2, v[2], v[3]);
+  } else {
+    stv<float>(row + f.f0, v[0]);
+    stv<float>(row + f.f0 + 1, v[1]);
+    stv<float>(row + f.f2, v[2]);
+    stv<float>(row + f.f2 + 1, v[3]);
+  }
 }
+
+// eight consecutive elements (16-byte aligned) as 16-byte accesses
+template <typename T> struct Vec8;
+template <> struct Vec8<float> {
+  static __device__ __forceinline__ void ld(const float* p, float (&v)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+  static __device__ __forceinline__ void st(float* p, const float (&v)[8]) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+  }
+};
+template <> struct Vec8<__nv_bfloat16> {
+  static __device__ __forceinline__ void ld(const __nv_bfloat16* p, float (&v)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+  static __device__ __forceinline__ void st(__nv_bfloat16* p, const float (&v)[8]) {
+    uint4 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4*>(p) = u;
+  }
+};
 __device__ __forceinline__ void ldp4(const float* row, Feat f, float (&v)[4]) {
   v[0] = row[f.f0];
   v[1] = row[f.f0 + 1];
@@ -110,134 +170,256 @@ __device__ __forceinline__ void norm_bias_rope(const float (&c)[4], float r, con
 
 // ---------------------------------------------------------------------------------------------
 // forward
+//
+// Every row kernel stages its segment's per-token inputs (B / C rows, angles, scalars) in shared
+// memory with coalesced loads first, so the per-head walks over the segment read shared memory
+// only; theta's running sum is the one serial dependency.
+
+// shared layout of a forward segment: C rows, B rows (both scaled by their RMSNorm factor),
+// angles, DT per head
+struct FwdSeg {
+  float *c, *bm, *ang, *dt;
+  __device__ FwdSeg(float* s, int N, int NA, int H)
+      : c(s), bm(s + kSeg * N), ang(s + 2 * kSeg * N), dt(s + 2 * kSeg * N + kSeg * NA) {}
+};
+
+// stage the segment's C / B rows and angles; optionally scale the rows by their RMSNorm factor
+template <typename TI>
+__device__ __forceinline__ void stage_rows(const M3& p, int b, int64_t t0, int nt, float* c, float* bm, float* ang,
+                                           float* rfac) {
+  const int N = (int)p.N, NA = p.NA;
+  for (int idx = threadIdx.x; idx < nt * N; idx += blockDim.x) {
+    const int t = idx / N, n = idx % N;
+    c[t * N + n] = ldv<float>(p.Cm.row<TI>(b, t0 + t, 0) + n);
+    bm[t * N + n] = ldv<float>(p.Bm.row<TI>(b, t0 + t, 0) + n);  // (coalesced across the block)
+  }
+  for (int idx = threadIdx.x; idx < nt * NA; idx += blockDim.x) {
+    const int t = idx / NA, i = idx % NA;
+    ang[t * NA + i] = ldv<float>(p.ang.row<TI>(b, t0 + t, 0) + i);
+  }
+  __syncthreads();
+  // RMSNorm factors r = rsqrt(mean(x^2) + eps), one warp per token
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  for (int t = warp; t < nt; t += nwarps) {
+    float sc = 0.f, sb = 0.f;
+    for (int n = lane; n < N; n += 32) {
+      sc += c[t * N + n] * c[t * N + n];
+      sb += bm[t * N + n] * bm[t * N + n];
+    }
+    sc = warp_sum(sc);
+    sb = warp_sum(sb);
+    const float rc = rsqrtf(sc / N + p.eps), rb = rsqrtf(sb / N + p.eps);
+    if (rfac) {
+      if (lane == 0) {
+        rfac[2 * t] = rc;
+        rfac[2 * t + 1] = rb;
+      }
+    } else {
+      for (int n = lane; n < N; n += 32) {
+        c[t * N + n] *= rc;
+        bm[t * N + n] *= rb;
+      }
+    }
+  }
+  __syncthreads();
+}
 
 // theta segment sums: segsum[b][h][seg][i] = sum over the segment's tokens of DT * ang_i
 template <typename TI>
 __global__ void __launch_bounds__(1024) m3_segsum_kernel(const M3 p) {
+  extern __shared__ float smem[];
   const int b = blockIdx.x / p.nseg, seg = blockIdx.x % p.nseg;
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t t0 = (int64_t)seg * kSeg, t1 = min(p.T, t0 + kSeg);
-  const float dtb = p.dt_bias[h];
-  float acc = 0.f;
-  for (int64_t t = t0; t < t1; ++t) {
-    const float DT = softplus20(ldv<float>(p.dd_dt.row<TI>(b, t, h)) + dtb);
-    if (lane < p.NA) acc += DT * ldv<float>(p.ang.row<TI>(b, t, 0) + lane);
+  const int H = (int)p.H, NA = p.NA;
+  const int64_t t0 = (int64_t)seg * kSeg;
+  const int nt = (int)min((int64_t)kSeg, p.T - t0);
+  float* sA = smem;              // [kSeg][NA]
+  float* sDT = smem + kSeg * NA;  // [kSeg][H]
+  for (int idx = threadIdx.x; idx < nt * NA; idx += blockDim.x)
+    sA[idx] = ldv<float>(p.ang.row<TI>(b, t0 + idx / NA, 0) + idx % NA);
+  for (int idx = threadIdx.x; idx < nt * H; idx += blockDim.x) {
+    const int t = idx / H, hh = idx % H;
+    sDT[idx] = softplus20(ldv<float>(p.dd_dt.row<TI>(b, t0 + t, hh)) + p.dt_bias[hh]);
   }
-  if (lane < p.NA) p.segsum[((b * p.H + h) * p.nseg + seg) * p.NA + lane] = acc;
+  __syncthreads();
+  if (lane < NA) {
+    float acc = 0.f;
+    for (int t = 0; t < nt; ++t) acc += sDT[t * H + h] * sA[t * NA + lane];
+    p.segsum[((b * H + h) * p.nseg + seg) * NA + lane] = acc;
+  }
 }
 
 // q, k (into k_ext rows t+1), xp, adt, gamma, beta and theta for one segment of one batch
 template <typename TI, typename TO>
 __global__ void __launch_bounds__(1024) m3_prologue_fwd_kernel(const M3 p) {
+  extern __shared__ float smem[];
   const int b = blockIdx.x / p.nseg, seg = blockIdx.x % p.nseg;
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int NA = p.NA, N = (int)p.N, P = (int)p.P, H = (int)p.H;
+  const int64_t t0 = (int64_t)seg * kSeg;
+  const int nt = (int)min((int64_t)kSeg, p.T - t0);
+  FwdSeg S(smem, N, NA, H);
+  // per (token, head) discretisation: scan scalars out, DT kept for theta
+  for (int idx = threadIdx.x; idx < nt * H; idx += blockDim.x) {
+    const int t = idx / H, hh = idx % H;
+    const Disc d = discretise(ldv<float>(p.dd_dt.row<TI>(b, t0 + t, hh)), ldv<float>(p.dd_A.row<TI>(b, t0 + t, hh)),
+                              ldv<float>(p.trap.row<TI>(b, t0 + t, hh)), p.dt_bias[hh], p.A_floor);
+    const int64_t bth = (b * p.T + t0 + t) * H + hh;
+    p.adt[bth] = d.adt;
+    p.gamma[bth] = d.gamma;
+    p.beta[bth] = d.beta;
+    S.dt[t * H + hh] = d.DT;
+  }
+  stage_rows<TI>(p, b, t0, nt, S.c, S.bm, S.ang, nullptr);  // rows scaled by their RMSNorm factor
+  TO* __restrict__ q = static_cast<TO*>(p.q);
+  TO* __restrict__ kx = static_cast<TO*>(p.k_ext);
+  const int64_t HN = (int64_t)H * N;
   const Feat f = feat(lane, NA);
-  float th = 0.f;  // theta at the end of the previous segment
-  if (f.on)
-    for (int s = 0; s < seg; ++s) th += p.segsum[((b * H + h) * p.nseg + s) * NA + lane];
-  float wc[4] = {}, wb[4] = {}, cb[4] = {}, bb[4] = {};
   if (f.on) {
+    float th = 0.f;  // theta at the end of the previous segment
+    for (int s = 0; s < seg; ++s) th += p.segsum[((b * H + h) * p.nseg + s) * NA + lane];
+    float wc[4], wb[4], cb[4], bb[4];
     ldp4(p.C_norm_w, f, wc);
     ldp4(p.B_norm_w, f, wb);
     ldp4(p.C_bias + h * N, f, cb);
     ldp4(p.B_bias + h * N, f, bb);
-  }
-  const float dtb = p.dt_bias[h];
-  const int64_t t0 = (int64_t)seg * kSeg, t1 = min(p.T, t0 + kSeg);
-  TO* q = static_cast<TO*>(p.q);
-  TO* kx = static_cast<TO*>(p.k_ext);
-  TO* xp = static_cast<TO*>(p.xp);
-  const int64_t HN = (int64_t)H * N, HP = (int64_t)H * P;
-  if (seg == 0 && f.on) {  // k_ext row 0 = kp of token 0 = 0
-    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-    st4(kx + (int64_t)b * (p.T + 1) * HN + h * N, f, zero);
-  }
-  for (int64_t t = t0; t < t1; ++t) {
-    const Disc d = discretise(ldv<float>(p.dd_dt.row<TI>(b, t, h)), ldv<float>(p.dd_A.row<TI>(b, t, h)),
-                              ldv<float>(p.trap.row<TI>(b, t, h)), dtb, p.A_floor);
-    const int64_t bth = (b * p.T + t) * H + h;
-    if (lane == 0) {
-      p.adt[bth] = d.adt;
-      p.gamma[bth] = d.gamma;
-      p.beta[bth] = d.beta;
+    if (seg == 0) {  // k_ext row 0 = kp of token 0 = 0
+      const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+      st4(kx + (int64_t)b * (p.T + 1) * HN + h * N, f, zero);
     }
-    float c[4] = {}, bm[4] = {};
-    if (f.on) {
-      th += d.DT * ldv<float>(p.ang.row<TI>(b, t, 0) + lane);  // theta = cumsum_t(DT ang) (mamba3.py:111)
+    for (int t = 0; t < nt; ++t) {
+      th += S.dt[t * H + h] * S.ang[t * NA + lane];  // theta = cumsum_t(DT ang) (mamba3.py:111)
+      const int64_t bth = (b * p.T + t0 + t) * H + h;
       p.theta[bth * NA + lane] = th;
-      ld4(p.Cm.row<TI>(b, t, 0), f, c);
-      ld4(p.Bm.row<TI>(b, t, 0), f, bm);
-    }
-    const float sc = warp_sum(c[0] * c[0] + c[1] * c[1] + c[2] * c[2] + c[3] * c[3]);
-    const float sb = warp_sum(bm[0] * bm[0] + bm[1] * bm[1] + bm[2] * bm[2] + bm[3] * bm[3]);
-    if (f.on) {
-      const float rc = rsqrtf(sc / N + p.eps), rb = rsqrtf(sb / N + p.eps);
       float sn, cs;
       sincosf(th, &sn, &cs);
-      float u[4], o[4];
-      norm_bias_rope(c, rc, wc, cb, sn, cs, u, o);
-      st4(q + (b * p.T + t) * HN + h * N, f, o);
-      norm_bias_rope(bm, rb, wb, bb, sn, cs, u, o);
-      st4(kx + (b * (p.T + 1) + t + 1) * HN + h * N, f, o);
+      float c[4], bm[4], u[4], o[4];
+      ldp4(S.c + t * N, f, c);
+      ldp4(S.bm + t * N, f, bm);
+      const float one = 1.f;
+      norm_bias_rope(c, one, wc, cb, sn, cs, u, o);
+      st4(q + bth * N, f, o);
+      norm_bias_rope(bm, one, wb, bb, sn, cs, u, o);
+      st4(kx + (b * (p.T + 1) + t0 + t + 1) * HN + h * N, f, o);
     }
-    for (int pp = lane; pp < P; pp += 32)  // xp = x one token later (mamba3.py:115)
-      stv<float>(xp + (b * p.T + t) * HP + h * P + pp, t > 0 ? ldv<float>(p.x.row<TI>(b, t - 1, h) + pp) : 0.f);
+  }
+  // xp = x one token later (mamba3.py:115), all threads over (token, head, feature)
+  TO* __restrict__ xp = static_cast<TO*>(p.xp);
+  const int HP = H * P;
+  if (p.vec8) {
+    const int HP8 = HP / 8, P8 = P / 8;
+    for (int idx = threadIdx.x; idx < nt * HP8; idx += blockDim.x) {
+      const int t = idx / HP8, r8 = idx % HP8, hh = r8 / P8, pp = (r8 % P8) * 8;
+      const int64_t tt = t0 + t;
+      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (tt > 0) Vec8<TI>::ld(p.x.row<TI>(b, tt - 1, hh) + pp, v);
+      Vec8<TO>::st(xp + (b * p.T + tt) * HP + hh * P + pp, v);
+    }
+  } else {
+    for (int idx = threadIdx.x; idx < nt * HP; idx += blockDim.x) {
+      const int t = idx / HP, r = idx % HP, hh = r / P, pp = r % P;
+      const int64_t tt = t0 + t;
+      stv<float>(xp + (b * p.T + tt) * HP + r, tt > 0 ? ldv<float>(p.x.row<TI>(b, tt - 1, hh) + pp) : 0.f);
+    }
   }
 }
 
-// out = (y + D x) * silu(z)   (mamba3.py:119)
+// out = (y + D x) * silu(z)   (mamba3.py:119); 256 threads over (token, head, feature)
 template <typename TI, typename TO>
-__global__ void __launch_bounds__(1024) m3_epilogue_fwd_kernel(const M3 p) {
+__global__ void __launch_bounds__(256) m3_epilogue_fwd_kernel(const M3 p) {
   const int b = blockIdx.x / p.nseg, seg = blockIdx.x % p.nseg;
-  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int P = (int)p.P;
-  const int64_t HP = p.H * P;
-  const float Dh = p.D[h];
-  const TO* y = static_cast<const TO*>(p.y);
-  const int64_t t0 = (int64_t)seg * kSeg, t1 = min(p.T, t0 + kSeg);
-  for (int64_t t = t0; t < t1; ++t)
-    for (int pp = lane; pp < P; pp += 32) {
-      float v = ldv<float>(y + (b * p.T + t) * HP + h * P + pp) + Dh * ldv<float>(p.x.row<TI>(b, t, h) + pp);
-      if (p.z.ptr) {
-        const float zz = ldv<float>(p.z.row<TI>(b, t, h) + pp);
-        v *= zz * sigmoidf_(zz);
-      }
-      stv<float>(p.out.wrow<TI>(b, t, h) + pp, v);
+  const int P = (int)p.P, HP = (int)(p.H * P);
+  const int64_t t0 = (int64_t)seg * kSeg;
+  const int nt = (int)min((int64_t)kSeg, p.T - t0);
+  const TO* __restrict__ y = static_cast<const TO*>(p.y);
+#pragma unroll 4
+  for (int idx = threadIdx.x; idx < nt * HP; idx += blockDim.x) {
+    const int t = idx / HP, r = idx % HP, hh = r / P, pp = r % P;
+    const int64_t tt = t0 + t;
+    float v = ldv<float>(y + (b * p.T + tt) * HP + r) + p.D[hh] * ldv<float>(p.x.row<TI>(b, tt, hh) + pp);
+    if (p.z.ptr) {
+      const float zz = ldv<float>(p.z.row<TI>(b, tt, hh) + pp);
+      v *= zz * sigmoidf_(zz);
     }
+    stv<float>(p.out.wrow<TI>(b, tt, hh) + pp, v);
+  }
 }
 
 // ---------------------------------------------------------------------------------------------
 // backward
 
-// dy = dout silu(z) for the scan; dz = dout (y + D x) silu'(z); D partial sums of dy . x
+// dy = dout silu(z) for the scan; dz = dout (y + D x) silu'(z); D partial sums of dy . x.
+// 256 threads; thread tid keeps features r = tid + 256 k of every token, so its sums have a fixed head.
 template <typename TI, typename TO>
-__global__ void __launch_bounds__(1024) m3_epilogue_bwd_kernel(const M3 p) {
+__global__ void __launch_bounds__(256) m3_epilogue_bwd_kernel(const M3 p) {
+  extern __shared__ float sacc[];  // [H * P] per-feature sums
   const int b = blockIdx.x / p.nseg, seg = blockIdx.x % p.nseg;
-  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int P = (int)p.P;
-  const int64_t HP = p.H * P;
-  const float Dh = p.D[h];
-  const TO* y = static_cast<const TO*>(p.y);
-  TO* dy = static_cast<TO*>(p.dy);
-  const int64_t t0 = (int64_t)seg * kSeg, t1 = min(p.T, t0 + kSeg);
-  float acc = 0.f;
-  for (int64_t t = t0; t < t1; ++t)
-    for (int pp = lane; pp < P; pp += 32) {
-      const float go = ldv<float>(p.dout.row<TI>(b, t, h) + pp);
-      const float xv = ldv<float>(p.x.row<TI>(b, t, h) + pp);
+  const int P = (int)p.P, H = (int)p.H, HP = H * P;
+  const int64_t t0 = (int64_t)seg * kSeg;
+  const int nt = (int)min((int64_t)kSeg, p.T - t0);
+  const TO* __restrict__ y = static_cast<const TO*>(p.y);
+  TO* __restrict__ dy = static_cast<TO*>(p.dy);
+  constexpr int kSlots = 32;  // HP <= 32 * 256 features per token
+  float acc[kSlots];
+#pragma unroll
+  for (int s = 0; s < kSlots; ++s) acc[s] = 0.f;
+  for (int t = 0; t < nt; ++t) {
+    const int64_t tt = t0 + t;
+#pragma unroll
+    for (int s = 0; s < kSlots; ++s) {
+      const int r = threadIdx.x + 256 * s;
+      if (r >= HP) break;
+      const int hh = r / P, pp = r % P;
+      const float go = ldv<float>(p.dout.row<TI>(b, tt, hh) + pp);
+      const float xv = ldv<float>(p.x.row<TI>(b, tt, hh) + pp);
       float g = go;
       if (p.z.ptr) {
-        const float zz = ldv<float>(p.z.row<TI>(b, t, h) + pp), s = sigmoidf_(zz);
-        g = go * zz * s;
-        const float v = ldv<float>(y + (b * p.T + t) * HP + h * P + pp) + Dh * xv;
-        stv<float>(p.dz.wrow<TI>(b, t, h) + pp, go * v * s * (1.f + zz * (1.f - s)));
+        const float zz = ldv<float>(p.z.row<TI>(b, tt, hh) + pp), sg = sigmoidf_(zz);
+        g = go * zz * sg;
+        const float v = ldv<float>(y + (b * p.T + tt) * HP + r) + p.D[hh] * xv;
+        stv<float>(p.dz.wrow<TI>(b, tt, hh) + pp, go * v * sg * (1.f + zz * (1.f - sg)));
       }
-      stv<float>(dy + (b * p.T + t) * HP + h * P + pp, g);
-      acc += g * xv;
+      stv<float>(dy + (b * p.T + tt) * HP + r, g);
+      acc[s] += g * xv;
     }
-  acc = warp_sum(acc);
-  if (lane == 0) p.pD[(b * p.nseg + seg) * p.H + h] = acc;
+  }
+  // per head: features h*P .. h*P+P-1 summed in feature order
+#pragma unroll
+  for (int s = 0; s < kSlots; ++s) {
+    const int r = threadIdx.x + 256 * s;
+    if (r >= HP) break;
+    sacc[r] = acc[s];
+  }
+  __syncthreads();
+  for (int hh = threadIdx.x; hh < H; hh += blockDim.x) {
+    float s = 0.f;
+    for (int pp = 0; pp < P; ++pp) s += sacc[hh * P + pp];
+    p.pD[(b * p.nseg + seg) * H + hh] = s;
+  }
+}
+
+// dx = scan dx + dxp of the next token (xp[t+1] = x[t]) + D dout silu(z)   (mamba3.py:115,119)
+template <typename TI, typename TO>
+__global__ void __launch_bounds__(256) m3_dx_kernel(const M3 p) {
+  const int b = blockIdx.x / p.nseg, seg = blockIdx.x % p.nseg;
+  const int P = (int)p.P, HP = (int)(p.H * P);
+  const int64_t t0 = (int64_t)seg * kSeg;
+  const int nt = (int)min((int64_t)kSeg, p.T - t0);
+  const TO* __restrict__ dxs = static_cast<const TO*>(p.dxs);
+  const TO* __restrict__ dxp = static_cast<const TO*>(p.dxp);
+#pragma unroll 4
+  for (int idx = threadIdx.x; idx < nt * HP; idx += blockDim.x) {
+    const int t = idx / HP, r = idx % HP, hh = r / P, pp = r % P;
+    const int64_t tt = t0 + t;
+    float g = ldv<float>(dxs + (b * p.T + tt) * HP + r);
+    if (tt + 1 < p.T) g += ldv<float>(dxp + (b * p.T + tt + 1) * HP + r);
+    float go = ldv<float>(p.dout.row<TI>(b, tt, hh) + pp);
+    if (p.z.ptr) {
+      const float zz = ldv<float>(p.z.row<TI>(b, tt, hh) + pp);
+      go *= zz * sigmoidf_(zz);
+    }
+    stv<float>(p.dx.wrow<TI>(b, tt, hh) + pp, g + p.D[hh] * go);
+  }
 }
 
 // RMSNorm backward of one token (mamba3.py:13-15), given the per-head gradients of its
@@ -266,67 +448,101 @@ __device__ __forceinline__ void rms_bwd_token(const float* src, int H, int N, Fe
   }
 }
 
+// per-head rows of one token the reverse walk needs from global memory
+struct BwdRow {
+  float th, gq[4], gk[4];
+};
+template <typename TO>
+__device__ __forceinline__ void load_bwd_row(const M3& p, const TO* dq, const TO* dk, const TO* dkp, int b, int64_t t,
+                                             int h, Feat f, BwdRow& r) {
+  const int64_t HN = p.H * p.N, bth = (b * p.T + t) * p.H + h;
+  r.th = p.theta[bth * p.NA + (f.f0 >> 1)];
+  ld4(dq + bth * p.N, f, r.gq);
+  ld4(dk + bth * p.N, f, r.gk);
+  if (t + 1 < p.T) {  // kp[t+1] = k[t]
+    float g[4];
+    ld4(dkp + (b * p.T + t + 1) * HN + h * p.N, f, g);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) r.gk[j] += g[j];
+  }
+}
+
 // Reverse walk over one segment: RoPE and RMSNorm backward, bias / norm-weight partial sums,
-// dx (scan dx + shifted dxp + D skip), the within-segment suffix of the theta gradient, and the
-// per-token sums over heads (dCm, dBm, ang gradient part) through shared memory.
+// the within-segment suffix of the theta gradient, and the per-token sums over heads (dCm, dBm,
+// ang gradient part) through shared memory.  Warps 0..H-1 own a head each and load their next
+// token's rows one step ahead; warps H, H+1, H+2 only reduce over heads (C rows, B rows, angles),
+// one token behind the head warps, so the two kinds of work overlap.
 template <typename TI, typename TO>
 __global__ void __launch_bounds__(1024) m3_prologue_bwd_kernel(const M3 p) {
-  extern __shared__ float smem[];  // [2 buffers][dvq H*N | dvk H*N | DT*sfx H*NA]
+  extern __shared__ float smem[];
   const int b = blockIdx.x / p.nseg, seg = blockIdx.x % p.nseg;
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int NA = p.NA, N = (int)p.N, P = (int)p.P, H = (int)p.H;
+  const int NA = p.NA, N = (int)p.N, H = (int)p.H;
+  const int64_t t0 = (int64_t)seg * kSeg;
+  const int nt = (int)min((int64_t)kSeg, p.T - t0);
+  // shared: C rows, B rows, angles, RMSNorm factors [kSeg][2], DT [kSeg][H], then two staging
+  // buffers of (dvq, dvk: H x N; DT * theta-gradient: H x NA)
+  float* sC = smem;
+  float* sB = sC + kSeg * N;
+  float* sA = sB + kSeg * N;
+  float* sR = sA + kSeg * NA;
+  float* sDT = sR + 2 * kSeg;
+  float* stage = sDT + kSeg * H;
   const int buf_floats = H * (2 * N + NA);
+  for (int idx = threadIdx.x; idx < nt * H; idx += blockDim.x) {
+    const int t = idx / H, hh = idx % H;
+    sDT[idx] = softplus20(ldv<float>(p.dd_dt.row<TI>(b, t0 + t, hh)) + p.dt_bias[hh]);
+  }
+  stage_rows<TI>(p, b, t0, nt, sC, sB, sA, sR);
   const Feat f = feat(lane, NA);
   float wc[4] = {}, wb[4] = {}, cb[4] = {}, bb[4] = {};
   if (f.on) {
     ldp4(p.C_norm_w, f, wc);
     ldp4(p.B_norm_w, f, wb);
-    ldp4(p.C_bias + h * N, f, cb);
-    ldp4(p.B_bias + h * N, f, bb);
+    if (h < H) {
+      ldp4(p.C_bias + h * N, f, cb);
+      ldp4(p.B_bias + h * N, f, bb);
+    }
   }
-  const float dtb = p.dt_bias[h], Dh = p.D[h];
-  const int64_t t0 = (int64_t)seg * kSeg, t1 = min(p.T, t0 + kSeg);
-  const int64_t HN = (int64_t)H * N, HP = (int64_t)H * P;
-  const TO* dq = static_cast<const TO*>(p.dq);
-  const TO* dk = static_cast<const TO*>(p.dk);
-  const TO* dkp = static_cast<const TO*>(p.dkp);
-  const TO* dxs = static_cast<const TO*>(p.dxs);
-  const TO* dxp = static_cast<const TO*>(p.dxp);
-  const bool wC = (h == 0), wB = (h == 1 % H), wA = (h == 2 % H);
+  const int64_t HN = (int64_t)H * N;
+  const TO* __restrict__ dq = static_cast<const TO*>(p.dq);
+  const TO* __restrict__ dk = static_cast<const TO*>(p.dk);
+  const TO* __restrict__ dkp = static_cast<const TO*>(p.dkp);
+  // reduction roles on the R = min(3, 32 - H) warps after the heads (H <= 31)
+  const int R = (int)(blockDim.x >> 5) - H;
+  const bool head = h < H;
+  const bool wC = (h == H), wB = (h == H + (R >= 2 ? 1 : 0)), wA = (h == H + (R >= 3 ? 2 : R - 1));
   float gcb[4] = {}, gbb[4] = {}, gwc[4] = {}, gwb[4] = {};
   float sfx = 0.f;  // theta gradient summed over this segment's tokens >= t
-  int step = 0;
-  for (int64_t t = t1 - 1; t >= t0; --t, ++step) {
-    float* buf = smem + (step & 1) * buf_floats;
-    const int64_t bth = (b * p.T + t) * H + h;
-    const float DT = softplus20(ldv<float>(p.dd_dt.row<TI>(b, t, h)) + dtb);
+  BwdRow nxt;
+  if (head && f.on) load_bwd_row(p, dq, dk, dkp, b, t0 + nt - 1, h, f, nxt);
+  // head warps compute token nt-1-step at step `step`; reduction warps reduce the token staged
+  // at the previous step (one extra step at the end)
+  for (int step = 0; step <= nt; ++step) {
+    if (head && step < nt) {
+    const int t = nt - 1 - step;
+    const BwdRow cur = nxt;
+    if (f.on && t > 0) load_bwd_row(p, dq, dk, dkp, b, t0 + t - 1, h, f, nxt);  // one token ahead
+    float* buf = stage + (step & 1) * buf_floats;
+    const int64_t bth = (b * p.T + t0 + t) * H + h;
     float c[4] = {}, bm[4] = {};
-    if (f.on) {
-      ld4(p.Cm.row<TI>(b, t, 0), f, c);
-      ld4(p.Bm.row<TI>(b, t, 0), f, bm);
-    }
-    const float sc = warp_sum(c[0] * c[0] + c[1] * c[1] + c[2] * c[2] + c[3] * c[3]);
-    const float sb = warp_sum(bm[0] * bm[0] + bm[1] * bm[1] + bm[2] * bm[2] + bm[3] * bm[3]);
-    const float rc = rsqrtf(sc / N + p.eps), rb = rsqrtf(sb / N + p.eps);
+    const float rc = sR[2 * t], rb = sR[2 * t + 1];
     float part = 0.f;
     if (f.on) {
-      const float th = p.theta[bth * NA + lane];
+      ldp4(sC + t * N, f, c);
+      ldp4(sB + t * N, f, bm);
       float sn, cs;
-      sincosf(th, &sn, &cs);
+      sincosf(cur.th, &sn, &cs);
       float uq[4], oq[4], uk[4], ok[4];
       norm_bias_rope(c, rc, wc, cb, sn, cs, uq, oq);
       norm_bias_rope(bm, rb, wb, bb, sn, cs, uk, ok);
-      float gq[4], gk[4], gkp[4] = {};
-      ld4(dq + (b * p.T + t) * HN + h * N, f, gq);
-      ld4(dk + (b * p.T + t) * HN + h * N, f, gk);
-      if (t + 1 < p.T) ld4(dkp + (b * p.T + t + 1) * HN + h * N, f, gkp);  // kp[t+1] = k[t]
-#pragma unroll
-      for (int j = 0; j < 4; ++j) gk[j] += gkp[j];
+      const float* gq = cur.gq;
+      const float* gk = cur.gk;
       // rope backward: rotate the gradient back; d theta from the rotated outputs
       const float dvq[4] = {gq[0] * cs + gq[1] * sn, -gq[0] * sn + gq[1] * cs, gq[2], gq[3]};
       const float dvk[4] = {gk[0] * cs + gk[1] * sn, -gk[0] * sn + gk[1] * cs, gk[2], gk[3]};
       sfx += (gq[1] * oq[0] - gq[0] * oq[1]) + (gk[1] * ok[0] - gk[0] * ok[1]);
-      part = sfx * ldv<float>(p.ang.row<TI>(b, t, 0) + lane);
+      part = sfx * sA[t * NA + lane];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         gcb[j] += dvq[j];
@@ -336,40 +552,35 @@ __global__ void __launch_bounds__(1024) m3_prologue_bwd_kernel(const M3 p) {
       float* bk = buf + HN + h * N;
       bq[f.f0] = dvq[0]; bq[f.f0 + 1] = dvq[1]; bq[f.f2] = dvq[2]; bq[f.f2 + 1] = dvq[3];
       bk[f.f0] = dvk[0]; bk[f.f0 + 1] = dvk[1]; bk[f.f2] = dvk[2]; bk[f.f2 + 1] = dvk[3];
-      buf[2 * HN + h * NA + lane] = DT * sfx;
+      buf[2 * HN + h * NA + lane] = sDT[t * H + h] * sfx;
     }
     part = warp_sum(part);
     if (lane == 0) p.dDTl[bth] = part;
-    // dx = scan dx + dxp of the next token (xp[t+1] = x[t]) + D dout silu(z)
-    for (int pp = lane; pp < P; pp += 32) {
-      float g = ldv<float>(dxs + (b * p.T + t) * HP + h * P + pp);
-      if (t + 1 < p.T) g += ldv<float>(dxp + (b * p.T + t + 1) * HP + h * P + pp);
-      float go = ldv<float>(p.dout.row<TI>(b, t, h) + pp);
-      if (p.z.ptr) {
-        const float zz = ldv<float>(p.z.row<TI>(b, t, h) + pp);
-        go *= zz * sigmoidf_(zz);
+    } else if (!head && step > 0) {
+      // per-token sums over heads in head order, then the RMSNorm backward of Cm / Bm
+      const int t = nt - step;  // the token the head warps staged at step - 1
+      const float* buf = stage + ((step - 1) & 1) * buf_floats;
+      if (wC) {
+        float x4[4] = {}, gx[4];
+        if (f.on) ldp4(sC + t * N, f, x4);
+        rms_bwd_token(buf, H, N, f, x4, wc, sR[2 * t], gwc, gx);
+        if (f.on) st4(p.dCm.wrow<TI>(b, t0 + t, 0), f, gx, p.pairs);
       }
-      stv<float>(p.dx.wrow<TI>(b, t, h) + pp, g + Dh * go);
+      if (wB) {
+        float x4[4] = {}, gx[4];
+        if (f.on) ldp4(sB + t * N, f, x4);
+        rms_bwd_token(buf + HN, H, N, f, x4, wb, sR[2 * t + 1], gwb, gx);
+        if (f.on) st4(p.dBm.wrow<TI>(b, t0 + t, 0), f, gx, p.pairs);
+      }
+      if (wA && lane < NA) {
+        float s = 0.f;
+        for (int hh = 0; hh < H; ++hh) s += buf[2 * HN + hh * NA + lane];
+        p.dangl[(b * p.T + t0 + t) * NA + lane] = s;
+      }
     }
     __syncthreads();
-    // per-token sums over heads in head order, then the RMSNorm backward of Cm / Bm
-    if (wC) {
-      float gx[4];
-      rms_bwd_token(buf, H, N, f, c, wc, rc, gwc, gx);
-      if (f.on) st4(p.dCm.wrow<TI>(b, t, 0), f, gx);
-    }
-    if (wB) {
-      float gx[4];
-      rms_bwd_token(buf + HN, H, N, f, bm, wb, rb, gwb, gx);
-      if (f.on) st4(p.dBm.wrow<TI>(b, t, 0), f, gx);
-    }
-    if (wA && lane < NA) {
-      float s = 0.f;
-      for (int hh = 0; hh < H; ++hh) s += buf[2 * HN + hh * NA + lane];
-      p.dangl[(b * p.T + t) * NA + lane] = s;
-    }
   }
-  if (f.on) {
+  if (head && f.on) {
     p.segsum[((b * H + h) * p.nseg + seg) * NA + lane] = sfx;
     const int64_t pb = ((int64_t)(b * p.nseg + seg) * H + h) * N;
     const int64_t part1 = (int64_t)p.B * p.nseg * HN;
@@ -377,69 +588,195 @@ __global__ void __launch_bounds__(1024) m3_prologue_bwd_kernel(const M3 p) {
     float* pC = p.pbias + part1 + pb;
     pB[f.f0] = gbb[0]; pB[f.f0 + 1] = gbb[1]; pB[f.f2] = gbb[2]; pB[f.f2 + 1] = gbb[3];
     pC[f.f0] = gcb[0]; pC[f.f0 + 1] = gcb[1]; pC[f.f2] = gcb[2]; pC[f.f2 + 1] = gcb[3];
-    const int64_t pn = (int64_t)(b * p.nseg + seg) * N;
-    if (wB) {
-      float* o = p.pnorm + pn;
-      o[f.f0] = gwb[0]; o[f.f0 + 1] = gwb[1]; o[f.f2] = gwb[2]; o[f.f2 + 1] = gwb[3];
-    }
-    if (wC) {
-      float* o = p.pnorm + (int64_t)p.B * p.nseg * N + pn;
-      o[f.f0] = gwc[0]; o[f.f0 + 1] = gwc[1]; o[f.f2] = gwc[2]; o[f.f2 + 1] = gwc[3];
-    }
+  }
+  const int64_t pn = (int64_t)(b * p.nseg + seg) * N;
+  if (wB && f.on) {
+    float* o = p.pnorm + pn;
+    o[f.f0] = gwb[0]; o[f.f0 + 1] = gwb[1]; o[f.f2] = gwb[2]; o[f.f2 + 1] = gwb[3];
+  }
+  if (wC && f.on) {
+    float* o = p.pnorm + (int64_t)p.B * p.nseg * N + pn;
+    o[f.f0] = gwc[0]; o[f.f0 + 1] = gwc[1]; o[f.f2] = gwc[2]; o[f.f2 + 1] = gwc[3];
   }
 }
 
-// The theta-gradient carry from later segments, then the discretisation backward per token
-// (mamba3.py:105-111) and the ang gradient.
+// The theta-gradient carry from later segments, then the discretisation backward per (token,
+// head) (mamba3.py:105-111) and the ang gradient.  Thread tid keeps head tid % H (blockDim is a
+// multiple of H), so its dt_bias partial sum has a fixed head.
 template <typename TI>
 __global__ void __launch_bounds__(1024) m3_scalars_bwd_kernel(const M3 p) {
-  extern __shared__ float smem[];  // sDT [kSeg][H] | sC [H][NA]
+  extern __shared__ float smem[];  // sA [kSeg][NA] | sC [H][NA] | sDT [kSeg][H] | sacc [blockDim]
   const int b = blockIdx.x / p.nseg, seg = blockIdx.x % p.nseg;
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int NA = p.NA, H = (int)p.H;
-  float* sDT = smem;
-  float* sC = smem + kSeg * H;
-  float C = 0.f;  // theta gradient summed over all later tokens (later segments)
-  if (lane < NA) {
+  const int64_t t0 = (int64_t)seg * kSeg;
+  const int nt = (int)min((int64_t)kSeg, p.T - t0);
+  float* sA = smem;
+  float* sC = sA + kSeg * NA;
+  float* sDT = sC + H * NA;
+  float* sacc = sDT + kSeg * H;
+  if (lane < NA) {  // theta gradient summed over all later tokens (later segments)
+    float C = 0.f;
     for (int s = seg + 1; s < p.nseg; ++s) C += p.segsum[((b * H + h) * p.nseg + s) * NA + lane];
     sC[h * NA + lane] = C;
   }
-  const float dtb = p.dt_bias[h];
-  const int64_t t0 = (int64_t)seg * kSeg, t1 = min(p.T, t0 + kSeg);
-  float acc_dt = 0.f;
-  for (int64_t t = t0; t < t1; ++t) {
-    const int64_t bth = (b * p.T + t) * H + h;
-    const Disc d = discretise(ldv<float>(p.dd_dt.row<TI>(b, t, h)), ldv<float>(p.dd_A.row<TI>(b, t, h)),
-                              ldv<float>(p.trap.row<TI>(b, t, h)), dtb, p.A_floor);
-    const float carry = warp_sum(lane < NA ? C * ldv<float>(p.ang.row<TI>(b, t, 0) + lane) : 0.f);
-    if (lane == 0) {
-      sDT[(t - t0) * H + h] = d.DT;
-      const float ga = p.dadt[bth], gg = p.dgamma[bth], gb = p.dbeta[bth];
-      const float g_adt = ga + gb * d.beta;  // beta = (1 - tr) DT e^{adt}
-      const float g_DT = g_adt * d.A + gg * d.tr + gb * (1.f - d.tr) * d.ea + p.dDTl[bth] + carry;
-      const float g_A = g_adt * d.DT;
-      const float g_tr = gg * d.DT - gb * d.DT * d.ea;
-      const float g_xs = g_DT * (d.xs > 20.f ? 1.f : sigmoidf_(d.xs));  // softplus'
-      const float ddA = ldv<float>(p.dd_A.row<TI>(b, t, h));
-      // clamp(max=-A_floor) passes the gradient where heavy_tail <= -A_floor; heavy_tail's two
-      // clamps pass it at x >= 0 and x <= 0 respectively (torch.clamp's masks)
-      const float dht = (ddA >= 0.f ? 1.f : 0.f) + (ddA <= 0.f ? 1.f / ((1.f - ddA) * (1.f - ddA)) : 0.f);
-      const float g_ddA = d.ht <= -p.A_floor ? -g_A * dht : 0.f;
-      stv<float>(p.ddd_dt.wrow<TI>(b, t, h), g_xs);
-      stv<float>(p.ddd_A.wrow<TI>(b, t, h), g_ddA);
-      stv<float>(p.dtrap.wrow<TI>(b, t, h), g_tr * d.tr * (1.f - d.tr));
-      acc_dt += g_xs;
-    }
-  }
-  if (lane == 0) p.pdt[(b * p.nseg + seg) * H + h] = acc_dt;
+  for (int idx = threadIdx.x; idx < nt * NA; idx += blockDim.x)
+    sA[idx] = ldv<float>(p.ang.row<TI>(b, t0 + idx / NA, 0) + idx % NA);
   __syncthreads();
+  float acc_dt = 0.f;
+  for (int idx = threadIdx.x; idx < nt * H; idx += blockDim.x) {
+    const int t = idx / H, hh = idx % H;
+    const int64_t tt = t0 + t, bth = (b * p.T + tt) * H + hh;
+    const float ddA = ldv<float>(p.dd_A.row<TI>(b, tt, hh));
+    const Disc d = discretise(ldv<float>(p.dd_dt.row<TI>(b, tt, hh)), ddA, ldv<float>(p.trap.row<TI>(b, tt, hh)),
+                              p.dt_bias[hh], p.A_floor);
+    float carry = 0.f;
+    for (int i = 0; i < NA; ++i) carry += sC[hh * NA + i] * sA[t * NA + i];
+    sDT[t * H + hh] = d.DT;
+    const float ga = p.dadt[bth], gg = p.dgamma[bth], gb = p.dbeta[bth];
+    const float g_adt = ga + gb * d.beta;  // beta = (1 - tr) DT e^{adt}
+    const float g_DT = g_adt * d.A + gg * d.tr + gb * (1.f - d.tr) * d.ea + p.dDTl[bth] + carry;
+    const float g_A = g_adt * d.DT;
+    const float g_tr = gg * d.DT - gb * d.DT * d.ea;
+    const float g_xs = g_DT * (d.xs > 20.f ? 1.f : sigmoidf_(d.xs));  // softplus'
+    // clamp(max=-A_floor) passes the gradient where heavy_tail <= -A_floor; heavy_tail's two
+    // clamps pass it at x >= 0 and x <= 0 respectively (torch.clamp's masks)
+    const float dht = (ddA >= 0.f ? 1.f : 0.f) + (ddA <= 0.f ? 1.f / ((1.f - ddA) * (1.f - ddA)) : 0.f);
+    const float g_ddA = d.ht <= -p.A_floor ? -g_A * dht : 0.f;
+    stv<float>(p.ddd_dt.wrow<TI>(b, tt, hh), g_xs);
+    stv<float>(p.ddd_A.wrow<TI>(b, tt, hh), g_ddA);
+    stv<float>(p.dtrap.wrow<TI>(b, tt, hh), g_tr * d.tr * (1.f - d.tr));
+    acc_dt += g_xs;
+  }
+  sacc[threadIdx.x] = acc_dt;
+  __syncthreads();
+  for (int hh = threadIdx.x; hh < H; hh += blockDim.x) {  // dt_bias partial: threads of head hh in order
+    float s = 0.f;
+    for (int k = hh; k < (int)blockDim.x; k += H) s += sacc[k];
+    p.pdt[(b * p.nseg + seg) * H + hh] = s;
+  }
   // ang gradient: the within-segment part plus sum_h DT[t][h] * carry[h][i]
-  const int n = (int)(t1 - t0) * NA;
-  for (int idx = threadIdx.x; idx < n; idx += blockDim.x) {
-    const int tt = idx / NA, i = idx % NA;
-    float s = p.dangl[(b * p.T + t0 + tt) * NA + i];
-    for (int hh = 0; hh < H; ++hh) s += sDT[tt * H + hh] * sC[hh * NA + i];
-    stv<float>(p.dang.wrow<TI>(b, t0 + tt, 0) + i, s);
+  for (int idx = threadIdx.x; idx < nt * NA; idx += blockDim.x) {
+    const int t = idx / NA, i = idx % NA;
+    float s = p.dangl[(b * p.T + t0 + t) * NA + i];
+    for (int hh = 0; hh < H; ++hh) s += sDT[t * H + hh] * sC[hh * NA + i];
+    stv<float>(p.dang.wrow<TI>(b, t0 + t, 0) + i, s);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// elementwise kernels, 16-byte vectors: blockDim = slots x groups, slots = H P / 8 (head,
+// 8-feature slot) and up to 4 groups; group g walks the segment's tokens g, g + groups, ...
+// (P % 8 == 0 and 16-byte-aligned views; the kernels above are the fallback)
+
+template <typename TI, typename TO>
+__global__ void __launch_bounds__(1024) m3_epilogue_fwd_vec_kernel(const M3 p) {
+  const int b = blockIdx.x / p.nseg, seg = blockIdx.x % p.nseg;
+  const int P = (int)p.P, P8 = P / 8, HP = (int)p.H * P;
+  const int slots = (int)p.H * P8, grp = threadIdx.x / slots, ngrp = blockDim.x / slots, sl = threadIdx.x % slots;
+  const int hh = sl / P8, pp = (sl % P8) * 8, r = hh * P + pp;
+  const int64_t t0 = (int64_t)seg * kSeg;
+  const int nt = (int)min((int64_t)kSeg, p.T - t0);
+  const float Dh = p.D[hh];
+  const TO* __restrict__ y = static_cast<const TO*>(p.y) + (int64_t)b * p.T * HP + r;
+#pragma unroll 2
+  for (int t = grp; t < nt; t += ngrp) {
+    const int64_t tt = t0 + t;
+    float yv[8], xv[8], o[8];
+    Vec8<TO>::ld(y + tt * HP, yv);
+    Vec8<TI>::ld(p.x.row<TI>(b, tt, hh) + pp, xv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = yv[e] + Dh * xv[e];
+    if (p.z.ptr) {
+      float zv[8];
+      Vec8<TI>::ld(p.z.row<TI>(b, tt, hh) + pp, zv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] *= zv[e] * sigmoidf_(zv[e]);
+    }
+    Vec8<TI>::st(p.out.wrow<TI>(b, tt, hh) + pp, o);
+  }
+}
+
+template <typename TI, typename TO>
+__global__ void __launch_bounds__(1024) m3_epilogue_bwd_vec_kernel(const M3 p) {
+  extern __shared__ float sacc[];  // [H * P / 8] per-slot sums
+  const int b = blockIdx.x / p.nseg, seg = blockIdx.x % p.nseg;
+  const int P = (int)p.P, P8 = P / 8, H = (int)p.H, HP = H * P;
+  const int slots = (int)p.H * P8, grp = threadIdx.x / slots, ngrp = blockDim.x / slots, sl = threadIdx.x % slots;
+  const int hh = sl / P8, pp = (sl % P8) * 8, r = hh * P + pp;
+  const int64_t t0 = (int64_t)seg * kSeg;
+  const int nt = (int)min((int64_t)kSeg, p.T - t0);
+  const float Dh = p.D[hh];
+  const TO* __restrict__ y = static_cast<const TO*>(p.y) + (int64_t)b * p.T * HP + r;
+  TO* __restrict__ dy = static_cast<TO*>(p.dy) + (int64_t)b * p.T * HP + r;
+  float acc = 0.f;
+#pragma unroll 2
+  for (int t = grp; t < nt; t += ngrp) {
+    const int64_t tt = t0 + t;
+    float go[8], xv[8], g[8];
+    Vec8<TI>::ld(p.dout.row<TI>(b, tt, hh) + pp, go);
+    Vec8<TI>::ld(p.x.row<TI>(b, tt, hh) + pp, xv);
+    if (p.z.ptr) {
+      float zv[8], yv[8], dz[8];
+      Vec8<TI>::ld(p.z.row<TI>(b, tt, hh) + pp, zv);
+      Vec8<TO>::ld(y + tt * HP, yv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float sg = sigmoidf_(zv[e]);
+        g[e] = go[e] * zv[e] * sg;
+        dz[e] = go[e] * (yv[e] + Dh * xv[e]) * sg * (1.f + zv[e] * (1.f - sg));
+      }
+      Vec8<TI>::st(p.dz.wrow<TI>(b, tt, hh) + pp, dz);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) g[e] = go[e];
+    }
+    Vec8<TO>::st(dy + tt * HP, g);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc += g[e] * xv[e];
+  }
+  sacc[threadIdx.x] = acc;
+  __syncthreads();
+  for (int h2 = threadIdx.x; h2 < H; h2 += blockDim.x) {  // per head: groups, then slots in feature order
+    float s = 0.f;
+    for (int g = 0; g < ngrp; ++g)
+      for (int k = 0; k < P8; ++k) s += sacc[g * slots + h2 * P8 + k];
+    p.pD[(b * p.nseg + seg) * H + h2] = s;
+  }
+}
+
+template <typename TI, typename TO>
+__global__ void __launch_bounds__(1024) m3_dx_vec_kernel(const M3 p) {
+  const int b = blockIdx.x / p.nseg, seg = blockIdx.x % p.nseg;
+  const int P = (int)p.P, P8 = P / 8, HP = (int)p.H * P;
+  const int slots = (int)p.H * P8, grp = threadIdx.x / slots, ngrp = blockDim.x / slots, sl = threadIdx.x % slots;
+  const int hh = sl / P8, pp = (sl % P8) * 8, r = hh * P + pp;
+  const int64_t t0 = (int64_t)seg * kSeg;
+  const int nt = (int)min((int64_t)kSeg, p.T - t0);
+  const float Dh = p.D[hh];
+  const TO* __restrict__ dxs = static_cast<const TO*>(p.dxs) + (int64_t)b * p.T * HP + r;
+  const TO* __restrict__ dxp = static_cast<const TO*>(p.dxp) + (int64_t)b * p.T * HP + r;
+#pragma unroll 2
+  for (int t = grp; t < nt; t += ngrp) {
+    const int64_t tt = t0 + t;
+    float g[8], go[8];
+    Vec8<TO>::ld(dxs + tt * HP, g);
+    if (tt + 1 < p.T) {  // xp[t+1] = x[t]
+      float gp[8];
+      Vec8<TO>::ld(dxp + (tt + 1) * HP, gp);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) g[e] += gp[e];
+    }
+    Vec8<TI>::ld(p.dout.row<TI>(b, tt, hh) + pp, go);
+    if (p.z.ptr) {
+      float zv[8];
+      Vec8<TI>::ld(p.z.row<TI>(b, tt, hh) + pp, zv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) go[e] *= zv[e] * sigmoidf_(zv[e]);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) g[e] += Dh * go[e];
+    Vec8<TI>::st(p.dx.wrow<TI>(b, tt, hh) + pp, g);
   }
 }
 
@@ -500,7 +837,7 @@ WsLayout ws_layout(const zb_m3_args* a) {
 int check(const zb_m3_args* a) {
   if (!a) return ZB_ERR_LAYOUT;
   if (a->B <= 0 || a->T <= 0 || a->H <= 0 || a->P <= 0 || a->N <= 0) return ZB_ERR_SHAPE;
-  if (a->H > 32 || a->N % 4 != 0 || a->N > 128) return ZB_ERR_UNSUPPORTED;
+  if (a->H > 31 || a->N % 4 != 0 || a->N > 128 || a->P > 256) return ZB_ERR_UNSUPPORTED;
   if ((double)a->B * (double)(a->T + 1) * (double)a->H * (double)(a->N > a->P ? a->N : a->P) > 9.0e15)
     return ZB_ERR_SHAPE;
   if ((a->io_dtype != ZB_F32 && a->io_dtype != ZB_BF16) || (a->op_dtype != ZB_F32 && a->op_dtype != ZB_BF16))
@@ -509,12 +846,28 @@ int check(const zb_m3_args* a) {
     return ZB_ERR_LAYOUT;
   if (!a->workspace || a->workspace_bytes < ws_layout(a).total || (reinterpret_cast<uintptr_t>(a->workspace) & 255))
     return ZB_ERR_WORKSPACE;
+  const void* contiguous[] = {a->q, a->k_ext, a->xp, a->y, a->dy, a->dxs, a->dxp, a->dq, a->dk, a->dkp};
+  for (const void* c : contiguous)
+    if (reinterpret_cast<uintptr_t>(c) & 15) return ZB_ERR_LAYOUT;
   return ZB_OK;
+}
+
+// a view allows aligned accesses of `elems` elements: base and (b, t, h) strides all multiples
+bool view_aligned(const zb_view& v, int64_t elems, size_t esize) {
+  if (!v.ptr) return true;
+  const uint64_t bytes = (uint64_t)elems * esize;
+  return reinterpret_cast<uintptr_t>(v.ptr) % bytes == 0 && (v.sb * (int64_t)esize) % bytes == 0 &&
+         (v.st * (int64_t)esize) % bytes == 0 && (v.sh * (int64_t)esize) % bytes == 0;
 }
 
 M3 make_m3(const zb_m3_args* a) {
   M3 p;
   memset(&p, 0, sizeof(p));
+  const size_t es = a->io_dtype == ZB_F32 ? 4 : 2;
+  p.pairs = view_aligned(a->Bm, 2, es) && view_aligned(a->Cm, 2, es) && view_aligned(a->dBm, 2, es) &&
+            view_aligned(a->dCm, 2, es);
+  p.vec8 = a->P % 8 == 0 && view_aligned(a->x, 8, es) && view_aligned(a->z, 8, es) && view_aligned(a->out, 8, es) &&
+           view_aligned(a->dout, 8, es) && view_aligned(a->dx, 8, es) && view_aligned(a->dz, 8, es);
   p.B = a->B; p.T = a->T; p.H = a->H; p.P = a->P; p.N = a->N;
   p.NA = (int)(a->N / 4);
   p.nseg = (int)((a->T + kSeg - 1) / kSeg);
@@ -574,9 +927,13 @@ extern "C" ZB_API int zb_m3_prologue_fwd(const zb_m3_args* a, void* stream) {
   const M3 p = make_m3(a);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const dim3 grid((unsigned)(p.B * p.nseg)), block((unsigned)(32 * p.H));
+  const int smem0 = (int)(kSeg * (p.NA + p.H) * sizeof(float));
+  const int smem1 = (int)(kSeg * (2 * p.N + p.NA + p.H) * sizeof(float));
   ZB_M3_DISPATCH(a->io_dtype, a->op_dtype, {
-    m3_segsum_kernel<TI><<<grid, block, 0, s>>>(p);
-    m3_prologue_fwd_kernel<TI, TO><<<grid, block, 0, s>>>(p);
+    auto k1 = m3_prologue_fwd_kernel<TI, TO>;
+    if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1) != cudaSuccess) return ZB_ERR_CUDA;
+    m3_segsum_kernel<TI><<<grid, block, smem0, s>>>(p);
+    k1<<<grid, block, smem1, s>>>(p);
   });
   return finish(2);
 }
@@ -587,8 +944,12 @@ extern "C" ZB_API int zb_m3_epilogue_fwd(const zb_m3_args* a, void* stream) {
   if (!a->y || !a->out.ptr) return ZB_ERR_LAYOUT;
   const M3 p = make_m3(a);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const dim3 grid((unsigned)(p.B * p.nseg)), block((unsigned)(32 * p.H));
-  ZB_M3_DISPATCH(a->io_dtype, a->op_dtype, { m3_epilogue_fwd_kernel<TI, TO><<<grid, block, 0, s>>>(p); });
+  const dim3 grid((unsigned)(p.B * p.nseg));
+  const unsigned slots = (unsigned)(p.H * p.P / 8), vthreads = slots * (slots >= 256 ? 1024 / slots : 4);
+  ZB_M3_DISPATCH(a->io_dtype, a->op_dtype, {
+    if (p.vec8) m3_epilogue_fwd_vec_kernel<TI, TO><<<grid, vthreads, 0, s>>>(p);
+    else m3_epilogue_fwd_kernel<TI, TO><<<grid, 256, 0, s>>>(p);
+  });
   return finish(1);
 }
 
@@ -598,8 +959,13 @@ extern "C" ZB_API int zb_m3_epilogue_bwd(const zb_m3_args* a, void* stream) {
   if (!a->y || !a->dout.ptr || !a->dy || (a->z.ptr && !a->dz.ptr)) return ZB_ERR_LAYOUT;
   const M3 p = make_m3(a);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const dim3 grid((unsigned)(p.B * p.nseg)), block((unsigned)(32 * p.H));
-  ZB_M3_DISPATCH(a->io_dtype, a->op_dtype, { m3_epilogue_bwd_kernel<TI, TO><<<grid, block, 0, s>>>(p); });
+  const dim3 grid((unsigned)(p.B * p.nseg));
+  const int smem = (int)(p.H * p.P * sizeof(float));
+  const unsigned slots = (unsigned)(p.H * p.P / 8), vthreads = slots * (slots >= 256 ? 1024 / slots : 4);
+  ZB_M3_DISPATCH(a->io_dtype, a->op_dtype, {
+    if (p.vec8) m3_epilogue_bwd_vec_kernel<TI, TO><<<grid, vthreads, vthreads * sizeof(float), s>>>(p);
+    else m3_epilogue_bwd_kernel<TI, TO><<<grid, 256, smem, s>>>(p);
+  });
   return finish(1);
 }
 
@@ -613,15 +979,21 @@ extern "C" ZB_API int zb_m3_prologue_bwd(const zb_m3_args* a, void* stream) {
   const M3 p = make_m3(a);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const dim3 grid((unsigned)(p.B * p.nseg)), block((unsigned)(32 * p.H));
-  // two staging buffers of (dvq, dvk: H x N; DT * theta-gradient: H x NA)
-  const int smem1 = (int)(2 * (p.H * (2 * p.N + p.NA)) * sizeof(float));
-  const int smem2 = (int)((kSeg * p.H + p.H * p.NA) * sizeof(float));
+  // staged rows (C, B: N each; angles; RMSNorm factors; DT per head) for kSeg tokens, then two
+  // staging buffers of (dvq, dvk: H x N; DT * theta-gradient: H x NA)
+  const int smem1 = (int)((kSeg * (2 * p.N + p.NA + 2 + p.H) + 2 * (p.H * (2 * p.N + p.NA))) * sizeof(float));
+  const int smem2 = (int)((kSeg * p.NA + p.H * p.NA + kSeg * p.H + 32 * p.H) * sizeof(float));
   ZB_M3_DISPATCH(a->io_dtype, a->op_dtype, {
     auto k1 = m3_prologue_bwd_kernel<TI, TO>;
     if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1) != cudaSuccess) return ZB_ERR_CUDA;
-    k1<<<grid, block, smem1, s>>>(p);
+    if (p.vec8) {
+      const unsigned slots = (unsigned)(p.H * p.P / 8), vthreads = slots * (slots >= 256 ? 1024 / slots : 4);
+      m3_dx_vec_kernel<TI, TO><<<grid, vthreads, 0, s>>>(p);
+    }
+    else m3_dx_kernel<TI, TO><<<grid, 256, 0, s>>>(p);
+    k1<<<grid, (unsigned)(32 * (p.H + (p.H <= 29 ? 3 : 32 - p.H))), smem1, s>>>(p);  // heads + reduction warps
     m3_scalars_bwd_kernel<TI><<<grid, block, smem2, s>>>(p);
   });
   m3_param_reduce_kernel<<<64, 256, 0, s>>>(p);
-  return finish(3);
+  return finish(4);
 }
