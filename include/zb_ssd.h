@@ -112,6 +112,14 @@ ZB_API int zb_ssd_fwd(const zb_ssd_args* args, void* stream);
  * zb_ssd_fwd with the same arguments.  dq/dk/dkp are summed over the heads of a group. */
 ZB_API int zb_ssd_bwd(const zb_ssd_args* args, void* stream);
 
+/* Recurrent form for decode: advance a state through args->T tokens in order,
+ *     h = e^{adt} h + gamma x k^T + beta xp kp^T ,   y = h q      (tests/test_mamba3.py:10-21)
+ * from initial_state (NULL = zero) to final_state (required; may be the same buffer, updated in
+ * place), writing y.  Uses x, q, k, kp, xp, adt, gamma, beta, y, initial_state, final_state of
+ * args (chunk_size, states and workspace are ignored).  fp32 / bf16 / fp16 vectors with fp32
+ * scalars, P <= 128, N <= 128; states fp32.  Not differentiated. */
+ZB_API int zb_ssd_decode(const zb_ssd_args* args, void* stream);
+
 /* Context-parallel combine of per-rank boundary states (no reference counterpart; the
  * reference is single-device): given the state entering this rank's range `s_prev`,
  * the total decay exp(sum adt) of the previous rank's range `decay_prev` [B*H], and that

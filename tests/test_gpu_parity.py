@@ -250,3 +250,58 @@ def test_full_size_layer_workload_slice_parity_and_state_split():
     zenith_b200.check_status()
     assert max_rel_err(torch.cat([y1, y2], 1), got["y"]) < 1e-2
     assert max_rel_err(f2, got["final_state"]) < 1e-3
+
+
+# ------------------------------------------------------------------------------------------------
+# recurrent (decode) form
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-5), (torch.bfloat16, 2e-2)])
+def test_decode_matches_per_token_recurrence(dtype, tol):
+    """zb_ssd_decode against the reference test's per-token recurrence (float64 oracle), from a
+    random initial state, several tokens in one call and one token per call."""
+    import zenith_b200
+    from oracle.ssd_oracle import naive_recurrence
+
+    g = torch.Generator().manual_seed(7)
+    B, T, H, G, P, N = 2, 6, 4, 2, 64, 128
+    x, xp = torch.randn(2, B, T, H, P, generator=g)
+    q, k, kp = torch.randn(3, B, T, G, N, generator=g) / N ** 0.5
+    adt = -torch.rand(B, T, H, generator=g)
+    gamma, beta = torch.rand(2, B, T, H, generator=g)
+    s0 = torch.randn(B, H, P, N, generator=g)
+    vec = [t.to(dtype) for t in (x, q, k, kp, xp)]
+    ref_y, ref_s = naive_recurrence(*[t.double() for t in vec], adt, gamma, beta, initial_state=s0)
+    dev = torch.device("cuda")
+    dvec = [t.to(dev) for t in vec]
+    dsc = [t.to(dev) for t in (adt, gamma, beta)]
+    state = s0.to(dev).contiguous()
+    y = zenith_b200.ssd_decode(*dvec, *dsc, state)
+    zenith_b200.check_status(dev)
+    assert max_rel_err(y, ref_y) < tol
+    assert max_rel_err(state, ref_s) < (1e-6 if dtype == torch.float32 else 1e-5)
+    state = s0.to(dev).contiguous()  # one token per call (decode)
+    ys = [zenith_b200.ssd_decode(*[t[:, i:i + 1] for t in dvec], *[t[:, i:i + 1] for t in dsc], state) for i in range(T)]
+    assert max_rel_err(torch.cat(ys, 1), ref_y) < tol
+    assert max_rel_err(state, ref_s) < (1e-6 if dtype == torch.float32 else 1e-5)
+
+
+@pytest.mark.gpu
+def test_decode_continues_a_chunked_prefill():
+    """Prefill with the chunked tensor-core scan (final state out), then decode the next tokens
+    one by one from that state: the decode outputs equal the chunked scan over the whole sequence."""
+    import zenith_b200
+    from zenith_b200.synthetic import SsdShape, make_inputs
+
+    s = SsdShape(2, 256, 4, 64, 128, 4, 64)
+    inp = make_inputs(s, seed=3)
+    dev = torch.device("cuda")
+    t = {n: (inp[n].to(torch.bfloat16) if n in ("x", "q", "k", "kp", "xp") else inp[n]).to(dev) for n in NAMES}
+    y_full = zenith_b200.ssd(*(t[n] for n in NAMES), s.chunk)
+    pre = 192
+    _, state = zenith_b200.ssd(*(t[n][:, :pre] for n in NAMES), s.chunk, return_final_state=True)
+    state = state.contiguous()
+    ys = [zenith_b200.ssd_decode(*(t[n][:, i:i + 1] for n in NAMES), state) for i in range(pre, s.T)]
+    zenith_b200.check_status(dev)
+    assert max_rel_err(torch.cat(ys, 1).float(), y_full[:, pre:].float()) < 2e-2

@@ -2,9 +2,9 @@
 reference's ``zenith.mamba3.ssd`` behind ``Mamba3.scan``."""
 
 from ._lib import SsdError, check_status
-from .ssd import prepare_inputs, ssd, ssd_dinitial_state, ssd_final_state, use_b200_scan
+from .ssd import prepare_inputs, ssd, ssd_decode, ssd_dinitial_state, ssd_final_state, use_b200_scan
 
-__all__ = ["ssd", "ssd_final_state", "ssd_dinitial_state", "use_b200_scan", "prepare_inputs", "check_status", "SsdError"]
+__all__ = ["ssd", "ssd_decode", "ssd_final_state", "ssd_dinitial_state", "use_b200_scan", "prepare_inputs", "check_status", "SsdError"]
 __version__ = "0.1.0"
 
 from .parallel import cp_ssd  # noqa: E402  (context parallelism over torch.distributed)

@@ -46,7 +46,7 @@ class Args(ctypes.Structure):
 EXPORTS = (
     "zb_version", "zb_strerror", "zb_last_cuda_error", "zb_ssd_states_bytes", "zb_ssd_workspace_bytes",
     "zb_ssd_fwd", "zb_ssd_bwd", "zb_ssd_state_combine", "zb_ssd_total_decay", "zb_ssd_check_status",
-    "zb_launch_count",
+    "zb_launch_count", "zb_ssd_decode",
 )
 
 _lib = None
@@ -78,7 +78,7 @@ def lib() -> ctypes.CDLL:
             getattr(L, fn).restype = ctypes.c_size_t
         L.zb_ssd_states_bytes.argtypes = [ctypes.POINTER(Args)]
         L.zb_ssd_workspace_bytes.argtypes = [ctypes.POINTER(Args), ctypes.c_int]
-        for fn in ("zb_ssd_fwd", "zb_ssd_bwd"):
+        for fn in ("zb_ssd_fwd", "zb_ssd_bwd", "zb_ssd_decode"):
             getattr(L, fn).restype = ctypes.c_int
             getattr(L, fn).argtypes = [ctypes.POINTER(Args), ctypes.c_void_p]
         L.zb_ssd_state_combine.restype = ctypes.c_int

@@ -265,6 +265,31 @@ def ssd_dinitial_state(dy, x, q, k, kp, xp, adt, gamma, beta, chunk_size, *, dfi
     return out[-1]
 
 
+def ssd_decode(x, q, k, kp, xp, adt, gamma, beta, state: Tensor) -> Tensor:
+    """Recurrent (decode) form: for each of the T tokens in order,
+    ``h = e^{adt} h + gamma x k^T + beta xp kp^T``, ``y = h q`` (the reference test's per-token
+    recurrence, tests/test_mamba3.py:10-21), starting from ``state`` and updating it in place.
+
+    Shapes as ``ssd`` (x, xp ``[B,T,H,P]``, q, k, kp ``[B,T,G,N]``, scalars ``[B,T,H]``; T is
+    typically 1); ``state`` is a contiguous fp32 ``[B,H,P,N]`` tensor, e.g. the final state of
+    a chunked forward over the prompt (``ssd(..., return_final_state=True)``).  Returns y
+    ``[B,T,H,P]`` in x's dtype.  Inference only (no autograd)."""
+    B, T, H, P = x.shape
+    N = q.shape[3]
+    if state.dtype != torch.float32 or tuple(state.shape) != (B, H, P, N) or not state.is_contiguous():
+        raise ValueError("ssd_decode: state must be a contiguous float32 [B, H, P, N] tensor")
+    dev = x.device
+    scal = [t if t.dtype == torch.float32 else t.float() for t in (adt, gamma, beta)]
+    vec = [t if t.stride(-1) == 1 else t.contiguous() for t in (x, q, k, kp, xp)]
+    a = _build_args(*vec, *scal, 1)
+    y = torch.empty(B, T, H, P, dtype=x.dtype, device=dev)
+    a.y = L.view(y)
+    a.initial_state = state.data_ptr()
+    a.final_state = state.data_ptr()
+    L.check(L.lib().zb_ssd_decode(ctypes.byref(a), _stream(dev)), "zb_ssd_decode")
+    return y
+
+
 def use_b200_scan(model: torch.nn.Module) -> int:
     """Install :func:`ssd` as the scan of every Mamba-3 block (``module.scan``, the reference's
     injection point, zenith/mamba3.py:77).  Returns the number of blocks patched."""
