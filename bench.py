@@ -35,6 +35,7 @@ sys.path.insert(0, str(ROOT))
 import torch  # noqa: E402
 
 METRIC = "SSD fwd+bwd tokens/s"
+METRIC_FWD = "SSD fwd tokens/s"  # --workload infer: forward with the final state, no saved states
 UNIT = "tokens/s"
 NAMES = ("x", "q", "k", "kp", "xp", "adt", "gamma", "beta")
 VEC = ("x", "q", "k", "kp", "xp")
@@ -162,7 +163,7 @@ def make_device_inputs(shape, rank, dev):
 # CPU baseline / reference arm
 
 
-def cpu_reference_sample(shape, seconds: float, max_reps: int | None = None):
+def cpu_reference_sample(shape, seconds: float, max_reps: int | None = None, fwd_only: bool = False):
     """Time the reference algorithm (CPU restatement of zenith/mamba3.py:30-56, fp32, autograd)
     on a one-sequence slice of the workload; returns (tokens/s, cores, reps, sample string)."""
     from oracle.ssd_oracle import ssd_forward
@@ -178,6 +179,10 @@ def cpu_reference_sample(shape, seconds: float, max_reps: int | None = None):
     dy = inp["dy"].to(torch.bfloat16).float()
 
     def once():
+        if fwd_only:
+            with torch.no_grad():
+                ssd_forward(*leaves, sl.chunk, dtype=torch.float32)
+            return
         y, _, _ = ssd_forward(*leaves, sl.chunk, dtype=torch.float32)
         y.backward(dy)
         for t in leaves:
@@ -192,7 +197,8 @@ def cpu_reference_sample(shape, seconds: float, max_reps: int | None = None):
         if el >= seconds or (max_reps is not None and reps >= max_reps):
             break
     tok_s = reps * sl.B * sl.T / el
-    sample = (f"reference algorithm fp32 + autograd on host CPU, 1 sequence (T{sl.T} H{sl.H} P{sl.P} N{sl.N} "
+    what = "forward" if fwd_only else "fp32 + autograd"
+    sample = (f"reference algorithm {what} on host CPU, 1 sequence (T{sl.T} H{sl.H} P{sl.P} N{sl.N} G{sl.G} "
               f"chunk {sl.chunk}) of the B{shape.B} workload, {reps} reps in {el:.1f} s, {cores} threads")
     return tok_s, cores, reps, sample
 
@@ -205,10 +211,11 @@ def run_reference(args):
 
     shape = SHAPES[args.workload]
     seconds = max(3.0, min(120.0, 2.0 * (args.steps + args.warmup)))
-    tok_s, cores, reps, sample = cpu_reference_sample(shape, seconds)
+    fwd_only = args.workload == "infer"
+    tok_s, cores, reps, sample = cpu_reference_sample(shape, seconds, fwd_only=fwd_only)
     ms = shape.B * shape.T / tok_s * 1e3
     line = {
-        "impl": "reference", "metric": METRIC, "value": tok_s, "unit": UNIT, "n_gpus": args.gpus,
+        "impl": "reference", "metric": METRIC_FWD if fwd_only else METRIC, "value": tok_s, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
         "config": {"workload": shape.name, "B": shape.B, "T": shape.T, "H": shape.H, "P": shape.P, "N": shape.N,
@@ -244,6 +251,7 @@ def run_ours(args):
     # sequence; boundary states move between ranks with NCCL send/recv).  Otherwise every rank
     # runs its own batch of the workload (batch x heads sharding: weak scaling, no collective).
     cp = args.workload == "long" and world > 1
+    fwd_only = args.workload == "infer"  # C4: inference forward returning the final state (decode hand-off)
     local_shape = SsdShape(shape.B, shape.T // world, shape.H, shape.P, shape.N, shape.G, shape.chunk) if cp else shape
     inp = make_device_inputs(local_shape, rank, dev)
     a = [inp[n] for n in NAMES]
@@ -269,6 +277,15 @@ def run_ours(args):
             for t in leaves:
                 t.grad = None
             return y
+    elif fwd_only:
+        def step(ev=None):
+            if ev is not None:
+                ev[0].record()
+            y, fin, _ = ssd_fwd_op(*a, chunk, None, False, False)
+            if ev is not None:
+                ev[1].record()
+                ev[2].record()
+            return y, fin
     else:
         def step(ev=None):
             if ev is not None:
@@ -321,14 +338,19 @@ def run_ours(args):
     # dy in (host -> device) and y plus all eight gradients out (device -> host) inside the timed
     # region.  Copies run on their own streams with two device buffer sets, so step i+1's inputs
     # and step i-1's outputs cross PCIe while step i computes, as a data pipeline would.
-    host = {n: inp[n].cpu().pin_memory() for n in NAMES + ("dy",)}
-    outs = [{n: torch.empty(host["x" if n == "y" else n].shape, dtype=host["x" if n == "y" else n].dtype).pin_memory()
-             for n in ("y",) + NAMES} for _ in range(2)]
+    # (--workload infer: inputs in, y and the final state out, no backward)
+    in_names = NAMES if fwd_only else NAMES + ("dy",)
+    host = {n: inp[n].cpu().pin_memory() for n in in_names}
+    B_, T_, H_, P_ = inp["x"].shape
+    out_shapes = ({"y": (inp["x"].shape, inp["x"].dtype), "final": ((B_, H_, P_, inp["q"].shape[3]), torch.float32)}
+                  if fwd_only else {n: (host["x" if n == "y" else n].shape, host["x" if n == "y" else n].dtype)
+                                    for n in ("y",) + NAMES})
+    outs = [{n: torch.empty(sh, dtype=dt).pin_memory() for n, (sh, dt) in out_shapes.items()} for _ in range(2)]
     h2d = sum(v.numel() * v.element_size() for v in host.values())
     d2h = sum(v.numel() * v.element_size() for v in outs[0].values())
     cur = torch.cuda.current_stream(dev)
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    dbuf = [{n: torch.empty_like(inp[n]) for n in NAMES + ("dy",)} for _ in range(2)]
+    dbuf = [{n: torch.empty_like(inp[n]) for n in in_names} for _ in range(2)]
     ev_in = [torch.cuda.Event() for _ in range(2)]
     ev_free = [torch.cuda.Event() for _ in range(2)]
     ev_done = [torch.cuda.Event() for _ in range(2)]
@@ -339,13 +361,24 @@ def run_ours(args):
         k = i % 2
         with torch.cuda.stream(s_in):
             s_in.wait_event(ev_free[k])  # step i-2 has finished with buffer set k
-            for n in NAMES + ("dy",):
+            for n in in_names:
                 dbuf[k][n].copy_(host[n], non_blocking=True)
             ev_in[k].record(s_in)
 
     def compute_and_d2h(i):
         k = i % 2
         cur.wait_event(ev_in[k])
+        if fwd_only:
+            with torch.no_grad():
+                y, fin = zenith_b200.ssd(*(dbuf[k][n] for n in NAMES), chunk, return_final_state=True)
+            ev_free[k].record(cur)
+            ev_done[k].record(cur)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_done[k])
+                for n, t in (("y", y), ("final", fin)):
+                    outs[k][n].copy_(t, non_blocking=True)
+                    t.record_stream(s_out)
+            return
         leaves = [dbuf[k][n].detach().requires_grad_() for n in NAMES]
         y = zenith_b200.parallel.cp_ssd(*leaves, chunk) if cp else zenith_b200.ssd(*leaves, chunk)
         y.backward(dbuf[k]["dy"])
@@ -385,7 +418,7 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        tok_s, cores, reps, sample = cpu_reference_sample(shape, args.cpu_seconds)
+        tok_s, cores, reps, sample = cpu_reference_sample(shape, args.cpu_seconds, fwd_only=fwd_only)
         cpu = {"value": tok_s, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
 
     if world > 1:
@@ -394,13 +427,15 @@ def run_ours(args):
     if rank != 0:
         return 0
     peak, peak_kind = peaks()
+    if fwd_only:
+        bwd_b = 0
     kern = {"fwd": (fwd_ms, fwd_b * th, "ssd_fwd"), "bwd": (bwd_ms, bwd_b * th, "ssd_bwd")}
-    dom = max(kern, key=lambda k: kern[k][0])
+    dom = "fwd" if fwd_only else max(kern, key=lambda k: kern[k][0])
     dms, dbytes, dname = kern[dom]
     achieved = dbytes / (dms / 1e3) / 1e9
     step_gbs = (fwd_b + bwd_b) * th / (ms_per_step / 1e3) / 1e9
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "metric": METRIC_FWD if fwd_only else METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong" if cp else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": shape.name, "B_per_gpu": shape.B, "T": shape.T, "H": shape.H, "P": shape.P,
@@ -410,7 +445,8 @@ def run_ours(args):
                    "tokens_per_rank": local_shape.B * local_shape.T,
                    "l2": f"inputs larger than L2 ({(fwd_b + bwd_b) * th / 1e9:.2f} GB/step per rank)"},
         "roofline": {"bound": "hbm", "kernel": dname, "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic_from_profile(dname),
+                     "frac": achieved / peak, "peak_kind": peak_kind,
+                     "traffic": traffic_from_profile(dname) if args.workload == "layer" else None,
                      "algorithmic_bytes_per_launch": dbytes, "launch_ms": dms},
         "step_roofline": {"achieved_gbs": step_gbs, "frac": step_gbs / peak,
                           "algorithmic_bytes_per_token_head": fwd_b + bwd_b, "fwd_ms": fwd_ms, "bwd_ms": bwd_ms},
