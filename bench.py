@@ -459,8 +459,97 @@ def run_ours(args):
     return 0
 
 
+# ------------------------------------------------------------------------------------------------
+# --workload mamba3: the fused Mamba-3 layer body (prologue, scan, epilogue; mamba3.py:96-119)
+
+LAYER_METRIC = "Mamba-3 layer body fwd+bwd tokens/s"
+
+
+def layer_inputs(B, T, H, P, N, dev, dtype, seed=0):
+    """The in_proj split and the layer parameters, with the reference module's scales."""
+    g = torch.Generator().manual_seed(seed)
+    mk = lambda *sh: torch.randn(*sh, generator=g)  # noqa: E731
+    t = {"x": mk(B, T, H, P), "z": mk(B, T, H, P), "Bm": mk(B, T, N), "Cm": mk(B, T, N), "dd_dt": mk(B, T, H),
+         "dd_A": mk(B, T, H), "trap": mk(B, T, H), "ang": mk(B, T, N // 4)}
+    dt = torch.exp(torch.rand(H, generator=g) * (torch.log(torch.tensor(0.1)) - torch.log(torch.tensor(1e-3)))
+                   + torch.log(torch.tensor(1e-3)))
+    prm = {"dt_bias": dt + torch.log(-torch.expm1(-dt)), "B_bias": torch.ones(H, N), "C_bias": torch.ones(H, N),
+           "B_norm_w": torch.ones(N), "C_norm_w": torch.ones(N), "D": torch.ones(H)}
+    dout = mk(B, T, H, P)
+    return ({n: v.to(dev, dtype) for n, v in t.items()}, {n: v.to(dev) for n, v in prm.items()}, dout.to(dev, dtype))
+
+
+def layer_bytes(H, P, N, e=2):
+    """Per token per head: the layer inputs read and outputs written once (B / C / ang rows are per
+    token, shared by the heads).  fwd: x, z, B, C, ang, 3 scalars in; out.  bwd: x, z, dout, B, C,
+    ang, 3 scalars in; dx, dz, dB, dC, dang, 3 scalar gradients out."""
+    rows = e * (2 * N + N // 4) / H
+    fwd = e * 2 * P + rows + 3 * e + e * P
+    bwd = (e * 3 * P + rows + 3 * e) + (e * 2 * P + rows + 3 * e)
+    return fwd, bwd
+
+
+def run_layer(args):
+    import zenith_b200
+    from zenith_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, T, H, P, N = 8, 2048, 24, 64, 128
+    t, prm, dout = layer_inputs(B, T, H, P, N, dev, torch.bfloat16)
+    names = ("x", "z", "Bm", "Cm", "dd_dt", "dd_A", "trap", "ang")
+    leaves = [t[n].requires_grad_() for n in names] + [prm[n].requires_grad_() for n in prm]
+
+    def step():
+        out = zenith_b200.mamba3_ssd_fused(*leaves, chunk_size=64, scan_dtype=torch.bfloat16)
+        out.backward(dout)
+        for lf in leaves:
+            lf.grad = None
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    zenith_b200.check_status(dev)
+    sampler = ClockSampler(0)
+    launches0 = _lib.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    zenith_b200.check_status(dev)
+    ms = e0.elapsed_time(e1) / args.steps
+    fwd_b, bwd_b = layer_bytes(H, P, N)
+    peak, peak_kind = peaks()
+    gbs = (fwd_b + bwd_b) * B * T * H / (ms / 1e3) / 1e9
+    line = {
+        "metric": LAYER_METRIC, "value": B * T / (ms / 1e3), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"Mamba-3 layer body B{B} T{T} H{H} P{P} N{N} chunk 64 (in_proj split -> gated y)",
+                   "io_dtype": "bf16", "scan_dtype": "bf16", "l2": "inputs larger than L2"},
+        "roofline": {"bound": "hbm", "kernel": "layer step", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                     "frac": gbs / peak, "peak_kind": peak_kind, "traffic": None,
+                     "algorithmic_bytes_per_token_head": fwd_b + bwd_b},
+        "gpu_launches": _lib.launch_count() - launches0,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
+    if args.workload == "mamba3":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "metric": LAYER_METRIC,
+                              "unavailable": "the layer-body workload has no separate reference arm; the scan "
+                                             "workloads time the reference algorithm"}), flush=True)
+            return 0
+        return run_layer(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
