@@ -11,7 +11,7 @@
  * A layer step is: zb_m3_prologue_fwd -> zb_ssd_fwd -> zb_m3_epilogue_fwd, and backward
  * zb_m3_epilogue_bwd -> zb_ssd_bwd -> zb_m3_prologue_bwd.
  *
- * Sizes: H <= 31 heads, N % 4 == 0 and N <= 128 (N/4 RoPE angles rotate the first N/2
+ * Sizes: H <= 31 heads, N % 16 == 0 and N <= 128 (N/4 RoPE angles rotate the first N/2
  * features), P <= 256.  Layer inputs may be strided views (the in_proj split); scan operands and
  * scan gradients are contiguous and 16-byte aligned.  All kernels are deterministic (fixed-order reductions).
  */

@@ -28,6 +28,7 @@ struct M3 {
   int NA, nseg;
   bool pairs;  // B / C rows and their gradients allow 2-element accesses (checked on the host)
   bool vec8;   // x, z, out, dout, dx, dz allow 16-byte accesses of 8 elements (checked on the host)
+  bool rows8;  // Bm, Cm rows allow 16-byte accesses of 8 elements (checked on the host)
   float A_floor, eps;
   View x, z, Bm, Cm, dd_dt, dd_A, trap, ang;
   const float *dt_bias, *B_bias, *C_bias, *B_norm_w, *C_norm_w, *D;
@@ -150,11 +151,13 @@ template <> struct Vec8<__nv_bfloat16> {
     *reinterpret_cast<uint4*>(p) = u;
   }
 };
+// the lane's four features of an fp32 row (8-byte aligned pairs: two 2-float loads)
 __device__ __forceinline__ void ldp4(const float* row, Feat f, float (&v)[4]) {
-  v[0] = row[f.f0];
-  v[1] = row[f.f0 + 1];
-  v[2] = row[f.f2];
-  v[3] = row[f.f2 + 1];
+  const float2 a = *reinterpret_cast<const float2*>(row + f.f0), c = *reinterpret_cast<const float2*>(row + f.f2);
+  v[0] = a.x;
+  v[1] = a.y;
+  v[2] = c.x;
+  v[3] = c.y;
 }
 
 // rope(rmsnorm(c) + bias): u = c r w + bias (mamba3.py:13-15,113-114), then rotate the first pair
@@ -183,28 +186,43 @@ struct FwdSeg {
       : c(s), bm(s + kSeg * N), ang(s + 2 * kSeg * N), dt(s + 2 * kSeg * N + kSeg * NA) {}
 };
 
-// stage the segment's C / B rows and angles; optionally scale the rows by their RMSNorm factor
+// stage the segment's C / B rows and angles; optionally scale the rows by their RMSNorm factor.
+// One warp per token: it copies the token's rows (16-byte vectors when the views allow), then sums
+// their squares from its own copy, so no block barrier separates the two.
 template <typename TI>
 __device__ __forceinline__ void stage_rows(const M3& p, int b, int64_t t0, int nt, float* c, float* bm, float* ang,
                                            float* rfac) {
   const int N = (int)p.N, NA = p.NA;
-  for (int idx = threadIdx.x; idx < nt * N; idx += blockDim.x) {
-    const int t = idx / N, n = idx % N;
-    c[t * N + n] = ldv<float>(p.Cm.row<TI>(b, t0 + t, 0) + n);
-    bm[t * N + n] = ldv<float>(p.Bm.row<TI>(b, t0 + t, 0) + n);  // (coalesced across the block)
-  }
-  for (int idx = threadIdx.x; idx < nt * NA; idx += blockDim.x) {
-    const int t = idx / NA, i = idx % NA;
-    ang[t * NA + i] = ldv<float>(p.ang.row<TI>(b, t0 + t, 0) + i);
-  }
-  __syncthreads();
-  // RMSNorm factors r = rsqrt(mean(x^2) + eps), one warp per token
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   for (int t = warp; t < nt; t += nwarps) {
+    const TI* cr = p.Cm.row<TI>(b, t0 + t, 0);
+    const TI* br = p.Bm.row<TI>(b, t0 + t, 0);
+    const TI* ar = p.ang.row<TI>(b, t0 + t, 0);
+    float* cs = c + t * N;
+    float* bs = bm + t * N;
+    if (p.rows8) {
+      for (int n = 8 * lane; n < N; n += 256) {
+        float v[8];
+        Vec8<TI>::ld(cr + n, v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) cs[n + e] = v[e];
+        Vec8<TI>::ld(br + n, v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) bs[n + e] = v[e];
+      }
+    } else {
+      for (int n = lane; n < N; n += 32) {
+        cs[n] = ldv<float>(cr + n);
+        bs[n] = ldv<float>(br + n);
+      }
+    }
+    for (int i = lane; i < NA; i += 32) ang[t * NA + i] = ldv<float>(ar + i);
+    __syncwarp();
+    // RMSNorm factors r = rsqrt(mean(x^2) + eps)
     float sc = 0.f, sb = 0.f;
     for (int n = lane; n < N; n += 32) {
-      sc += c[t * N + n] * c[t * N + n];
-      sb += bm[t * N + n] * bm[t * N + n];
+      sc += cs[n] * cs[n];
+      sb += bs[n] * bs[n];
     }
     sc = warp_sum(sc);
     sb = warp_sum(sb);
@@ -216,8 +234,8 @@ __device__ __forceinline__ void stage_rows(const M3& p, int b, int64_t t0, int n
       }
     } else {
       for (int n = lane; n < N; n += 32) {
-        c[t * N + n] *= rc;
-        bm[t * N + n] *= rb;
+        cs[n] *= rc;
+        bs[n] *= rb;
       }
     }
   }
@@ -430,12 +448,12 @@ __device__ __forceinline__ void rms_bwd_token(const float* src, int H, int N, Fe
                                               const float (&wv)[4], float rr, float (&gw)[4], float (&gx)[4]) {
   float du[4] = {0.f, 0.f, 0.f, 0.f};
   if (f.on)
+#pragma unroll 4
     for (int hh = 0; hh < H; ++hh) {
-      const float* r = src + hh * N;
-      du[0] += r[f.f0];
-      du[1] += r[f.f0 + 1];
-      du[2] += r[f.f2];
-      du[3] += r[f.f2 + 1];
+      float v[4];
+      ldp4(src + hh * N, f, v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) du[j] += v[j];
     }
   float dl = 0.f;
 #pragma unroll
@@ -448,23 +466,42 @@ __device__ __forceinline__ void rms_bwd_token(const float* src, int H, int N, Fe
   }
 }
 
-// per-head rows of one token the reverse walk needs from global memory
-struct BwdRow {
-  float th, gq[4], gk[4];
-};
+// Per-head rows of one token that the reverse walk needs from global memory: dq, dk, dkp of the
+// next token (kp[t+1] = k[t]) and theta, copied into a per-warp ring of `depth` slots by cp.async
+// 16-byte copies, several tokens ahead of their use.  Slot layout (bytes): dq | dk | dkp | theta.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int K> __device__ __forceinline__ void cp_async_wait_() { asm volatile("cp.async.wait_group %0;" ::"n"(K) : "memory"); }
+
 template <typename TO>
-__device__ __forceinline__ void load_bwd_row(const M3& p, const TO* dq, const TO* dk, const TO* dkp, int b, int64_t t,
-                                             int h, Feat f, BwdRow& r) {
-  const int64_t HN = p.H * p.N, bth = (b * p.T + t) * p.H + h;
-  r.th = p.theta[bth * p.NA + (f.f0 >> 1)];
-  ld4(dq + bth * p.N, f, r.gq);
-  ld4(dk + bth * p.N, f, r.gk);
-  if (t + 1 < p.T) {  // kp[t+1] = k[t]
-    float g[4];
-    ld4(dkp + (b * p.T + t + 1) * HN + h * p.N, f, g);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) r.gk[j] += g[j];
+__device__ __forceinline__ void ring_issue(const M3& p, const TO* dq, const TO* dk, const TO* dkp, int b, int64_t t,
+                                           int h, unsigned char* slot, int lane) {
+  const int rowB = (int)p.N * (int)sizeof(TO), nq = rowB / 16, nth = p.NA * 4 / 16;
+  const int64_t bth = (b * p.T + t) * p.H + h;
+  const unsigned char* srcq = reinterpret_cast<const unsigned char*>(dq + bth * p.N);
+  const unsigned char* srck = reinterpret_cast<const unsigned char*>(dk + bth * p.N);
+  const unsigned char* srcth = reinterpret_cast<const unsigned char*>(p.theta + bth * p.NA);
+  const bool has_next = t + 1 < p.T;
+  const unsigned char* srckp = reinterpret_cast<const unsigned char*>(dkp + (bth + p.H) * p.N);
+  for (int c = lane; c < 3 * nq + nth; c += 32) {
+    unsigned char* dst = slot + 16 * c;
+    if (c < nq) cp_async16(dst, srcq + 16 * c);
+    else if (c < 2 * nq) cp_async16(dst, srck + 16 * (c - nq));
+    else if (c < 3 * nq) {
+      if (has_next) cp_async16(dst, srckp + 16 * (c - 2 * nq));
+      else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    } else cp_async16(dst, srcth + 16 * (c - 3 * nq));
   }
+}
+
+// the lane's four features of a row staged in a ring slot
+template <typename TO>
+__device__ __forceinline__ void slot4(const unsigned char* row, Feat f, float (&v)[4]) {
+  ld4(reinterpret_cast<const TO*>(row), f, v);
 }
 
 // Reverse walk over one segment: RoPE and RMSNorm backward, bias / norm-weight partial sums,
@@ -472,7 +509,7 @@ __device__ __forceinline__ void load_bwd_row(const M3& p, const TO* dq, const TO
 // ang gradient part) through shared memory.  Warps 0..H-1 own a head each and load their next
 // token's rows one step ahead; warps H, H+1, H+2 only reduce over heads (C rows, B rows, angles),
 // one token behind the head warps, so the two kinds of work overlap.
-template <typename TI, typename TO>
+template <typename TI, typename TO, int kRing>  // kRing: ring slots (tokens in flight) per head warp
 __global__ void __launch_bounds__(1024) m3_prologue_bwd_kernel(const M3 p) {
   extern __shared__ float smem[];
   const int b = blockIdx.x / p.nseg, seg = blockIdx.x % p.nseg;
@@ -514,15 +551,27 @@ __global__ void __launch_bounds__(1024) m3_prologue_bwd_kernel(const M3 p) {
   const bool wC = (h == H), wB = (h == H + (R >= 2 ? 1 : 0)), wA = (h == H + (R >= 3 ? 2 : R - 1));
   float gcb[4] = {}, gbb[4] = {}, gwc[4] = {}, gwb[4] = {};
   float sfx = 0.f;  // theta gradient summed over this segment's tokens >= t
-  BwdRow nxt;
-  if (head && f.on) load_bwd_row(p, dq, dk, dkp, b, t0 + nt - 1, h, f, nxt);
+  // the per-warp row ring: kRing slots of (3 rows of N elements + NA theta floats)
+  const int slotB = 3 * N * (int)sizeof(TO) + NA * 4;
+  unsigned char* ring = reinterpret_cast<unsigned char*>(stage + 2 * buf_floats) + (size_t)h * kRing * slotB;
+  if (head)  // prefill: tokens nt-1 .. nt-kRing+1
+    for (int k = 0; k < kRing - 1; ++k) {
+      if (nt - 1 - k >= 0) ring_issue(p, dq, dk, dkp, b, t0 + nt - 1 - k, h, ring + (size_t)k * slotB, lane);
+      cp_async_commit_();
+    }
   // head warps compute token nt-1-step at step `step`; reduction warps reduce the token staged
   // at the previous step (one extra step at the end)
   for (int step = 0; step <= nt; ++step) {
     if (head && step < nt) {
     const int t = nt - 1 - step;
-    const BwdRow cur = nxt;
-    if (f.on && t > 0) load_bwd_row(p, dq, dk, dkp, b, t0 + t - 1, h, f, nxt);  // one token ahead
+    {  // keep kRing - 1 tokens in flight: issue token t - (kRing - 1), then wait for token t
+      const int ti = t - (kRing - 1);
+      if (ti >= 0) ring_issue(p, dq, dk, dkp, b, t0 + ti, h, ring + (size_t)((step + kRing - 1) % kRing) * slotB, lane);
+      cp_async_commit_();
+      cp_async_wait_<kRing - 1>();
+      __syncwarp();
+    }
+    const unsigned char* slot = ring + (size_t)(step % kRing) * slotB;
     float* buf = stage + (step & 1) * buf_floats;
     const int64_t bth = (b * p.T + t0 + t) * H + h;
     float c[4] = {}, bm[4] = {};
@@ -531,13 +580,18 @@ __global__ void __launch_bounds__(1024) m3_prologue_bwd_kernel(const M3 p) {
     if (f.on) {
       ldp4(sC + t * N, f, c);
       ldp4(sB + t * N, f, bm);
+      const int rowB = N * (int)sizeof(TO);
       float sn, cs;
-      sincosf(cur.th, &sn, &cs);
+      sincosf(reinterpret_cast<const float*>(slot + 3 * rowB)[lane], &sn, &cs);
       float uq[4], oq[4], uk[4], ok[4];
       norm_bias_rope(c, rc, wc, cb, sn, cs, uq, oq);
       norm_bias_rope(bm, rb, wb, bb, sn, cs, uk, ok);
-      const float* gq = cur.gq;
-      const float* gk = cur.gk;
+      float gq[4], gk[4], gkp[4];
+      slot4<TO>(slot, f, gq);
+      slot4<TO>(slot + rowB, f, gk);
+      slot4<TO>(slot + 2 * rowB, f, gkp);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) gk[j] += gkp[j];
       // rope backward: rotate the gradient back; d theta from the rotated outputs
       const float dvq[4] = {gq[0] * cs + gq[1] * sn, -gq[0] * sn + gq[1] * cs, gq[2], gq[3]};
       const float dvk[4] = {gk[0] * cs + gk[1] * sn, -gk[0] * sn + gk[1] * cs, gk[2], gk[3]};
@@ -550,8 +604,10 @@ __global__ void __launch_bounds__(1024) m3_prologue_bwd_kernel(const M3 p) {
       }
       float* bq = buf + h * N;
       float* bk = buf + HN + h * N;
-      bq[f.f0] = dvq[0]; bq[f.f0 + 1] = dvq[1]; bq[f.f2] = dvq[2]; bq[f.f2 + 1] = dvq[3];
-      bk[f.f0] = dvk[0]; bk[f.f0 + 1] = dvk[1]; bk[f.f2] = dvk[2]; bk[f.f2 + 1] = dvk[3];
+      *reinterpret_cast<float2*>(bq + f.f0) = make_float2(dvq[0], dvq[1]);
+      *reinterpret_cast<float2*>(bq + f.f2) = make_float2(dvq[2], dvq[3]);
+      *reinterpret_cast<float2*>(bk + f.f0) = make_float2(dvk[0], dvk[1]);
+      *reinterpret_cast<float2*>(bk + f.f2) = make_float2(dvk[2], dvk[3]);
       buf[2 * HN + h * NA + lane] = sDT[t * H + h] * sfx;
     }
     part = warp_sum(part);
@@ -837,7 +893,7 @@ WsLayout ws_layout(const zb_m3_args* a) {
 int check(const zb_m3_args* a) {
   if (!a) return ZB_ERR_LAYOUT;
   if (a->B <= 0 || a->T <= 0 || a->H <= 0 || a->P <= 0 || a->N <= 0) return ZB_ERR_SHAPE;
-  if (a->H > 31 || a->N % 4 != 0 || a->N > 128 || a->P > 256) return ZB_ERR_UNSUPPORTED;
+  if (a->H > 31 || a->N % 16 != 0 || a->N > 128 || a->P > 256) return ZB_ERR_UNSUPPORTED;
   if ((double)a->B * (double)(a->T + 1) * (double)a->H * (double)(a->N > a->P ? a->N : a->P) > 9.0e15)
     return ZB_ERR_SHAPE;
   if ((a->io_dtype != ZB_F32 && a->io_dtype != ZB_BF16) || (a->op_dtype != ZB_F32 && a->op_dtype != ZB_BF16))
@@ -866,6 +922,7 @@ M3 make_m3(const zb_m3_args* a) {
   const size_t es = a->io_dtype == ZB_F32 ? 4 : 2;
   p.pairs = view_aligned(a->Bm, 2, es) && view_aligned(a->Cm, 2, es) && view_aligned(a->dBm, 2, es) &&
             view_aligned(a->dCm, 2, es);
+  p.rows8 = a->N % 8 == 0 && view_aligned(a->Bm, 8, es) && view_aligned(a->Cm, 8, es);
   p.vec8 = a->P % 8 == 0 && view_aligned(a->x, 8, es) && view_aligned(a->z, 8, es) && view_aligned(a->out, 8, es) &&
            view_aligned(a->dout, 8, es) && view_aligned(a->dx, 8, es) && view_aligned(a->dz, 8, es);
   p.B = a->B; p.T = a->T; p.H = a->H; p.P = a->P; p.N = a->N;
@@ -981,10 +1038,18 @@ extern "C" ZB_API int zb_m3_prologue_bwd(const zb_m3_args* a, void* stream) {
   const dim3 grid((unsigned)(p.B * p.nseg)), block((unsigned)(32 * p.H));
   // staged rows (C, B: N each; angles; RMSNorm factors; DT per head) for kSeg tokens, then two
   // staging buffers of (dvq, dvk: H x N; DT * theta-gradient: H x NA)
-  const int smem1 = (int)((kSeg * (2 * p.N + p.NA + 2 + p.H) + 2 * (p.H * (2 * p.N + p.NA))) * sizeof(float));
+  // plus the per-warp row rings: as many slots (4, 2 or 1) as shared memory allows
+  const int op_es = a->op_dtype == ZB_F32 ? 4 : 2;
+  const size_t base1 = (kSeg * (2 * p.N + p.NA + 2 + p.H) + 2 * (p.H * (2 * p.N + p.NA))) * sizeof(float);
+  const size_t ring1 = (size_t)p.H * (3 * p.N * op_es + p.NA * 4);
+  const size_t kMaxSmem = 227 * 1024;
+  const int ring = base1 + 4 * ring1 <= kMaxSmem ? 4 : base1 + 2 * ring1 <= kMaxSmem ? 2 : 1;
+  const int smem1 = (int)(base1 + ring * ring1);
+  if ((size_t)smem1 > kMaxSmem) return ZB_ERR_UNSUPPORTED;
   const int smem2 = (int)((kSeg * p.NA + p.H * p.NA + kSeg * p.H + 32 * p.H) * sizeof(float));
   ZB_M3_DISPATCH(a->io_dtype, a->op_dtype, {
-    auto k1 = m3_prologue_bwd_kernel<TI, TO>;
+    auto k1 = ring == 4 ? m3_prologue_bwd_kernel<TI, TO, 4>
+              : ring == 2 ? m3_prologue_bwd_kernel<TI, TO, 2> : m3_prologue_bwd_kernel<TI, TO, 1>;
     if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1) != cudaSuccess) return ZB_ERR_CUDA;
     if (p.vec8) {
       const unsigned slots = (unsigned)(p.H * p.P / 8), vthreads = slots * (slots >= 256 ? 1024 / slots : 4);
