@@ -541,8 +541,195 @@ def run_layer(args):
     return 0
 
 
+# ------------------------------------------------------------------------------------------------
+# --workload lm: one data-parallel training step of the Mamba-3 LM (zenith/model.py:42-99,
+# zenith/train.py:99-111): d_model 1536, expand 2, headdim 64 (48 heads), N 128, 24 layers
+# (4 input, 16 recurrent, 4 output, one loop), vocab 32000 tied, micro-batch 8 x 2048 per GPU.
+
+LM_METRIC = "Mamba-3 LM training step tokens/s"
+LM_CONFIG = dict(vocab_size=32000, d_model=1536, d_state=128, expand=2, headdim=64, chunk_size=64, n_input=4,
+                 n_recurrent=16, n_output=4, max_loops=1, tie_word_embeddings=True)
+LM_BATCH, LM_SEQ = 8, 2048
+
+
+def lm_flops_per_token(cfg):
+    """Algorithmic FLOPs per token of one training step (forward + backward = 3x forward): the
+    in_proj / out_proj / LM-head GEMMs (2 flops per weight per token, forward) and the SSD scan
+    (fwd F = 4 L N + 4 L P + 6 N P per head, chunk L)."""
+    d, V = cfg["d_model"], cfg["vocab_size"]
+    d_inner = cfg["expand"] * d
+    H, P, N, Lc = d_inner // cfg["headdim"], cfg["headdim"], cfg["d_state"], cfg["chunk_size"]
+    n_in = 2 * d_inner + 2 * N + 3 * H + N // 4
+    layers = cfg["n_input"] + cfg["n_recurrent"] * cfg["max_loops"] + cfg["n_output"]
+    gemm = 2 * (d * n_in + d_inner * d) * layers + 2 * d * V
+    scan = (4 * Lc * N + 4 * Lc * P + 6 * N * P) * H * layers
+    return 3 * (gemm + scan)
+
+
+def cpu_lm_sample(cfg, seconds: float, T: int = 128):
+    """The reference LM step (the oracle restatement of zenith/model.py:79-99, float32, autograd)
+    on the host CPU for one sequence of T tokens; returns (tokens/s, cores, sample string)."""
+    from oracle import lm_oracle
+
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    torch.manual_seed(0)
+    with torch.device("cpu"):
+        from zenith_b200.lm import ZenithForCausalLM
+
+        model = ZenithForCausalLM(cfg)          # initialisation only; the step below is the oracle's
+    params = {n: t.detach().clone().requires_grad_(True) for n, t in model.named_parameters()}
+    ids = torch.randint(0, cfg["vocab_size"], (1, T))
+
+    def once():
+        _, loss = lm_oracle.forward(params, cfg, ids, ids, loops=cfg["max_loops"])
+        loss.backward()
+        for t in params.values():
+            t.grad = None
+
+    once()
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        once()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    tok_s = reps * T / el
+    sample = (f"reference LM step (float32 + autograd) on host CPU, 1 sequence of {T} tokens of the full model, "
+              f"{reps} reps in {el:.1f} s, {cores} threads")
+    return tok_s, cores, sample
+
+
+def run_lm_reference(args):
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    seconds = max(5.0, min(120.0, 2.0 * (args.steps + args.warmup)))
+    tok_s, cores, sample = cpu_lm_sample(LM_CONFIG, seconds)
+    line = {
+        "impl": "reference", "metric": LM_METRIC, "value": tok_s, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": LM_BATCH * LM_SEQ / tok_s * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": "Mamba-3 LM training step", **LM_CONFIG, "micro_batch": LM_BATCH, "seq_len": LM_SEQ,
+                   "device": "host cpu"},
+        "cpu_baseline": {"value": tok_s, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": tok_s, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_lm(args):
+    import torch.distributed as dist
+
+    import zenith_b200
+    from zenith_b200 import _lib, lm
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    torch.manual_seed(0)                                  # identical replicas
+    model = lm.ZenithForCausalLM(LM_CONFIG).to(dev)
+    net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local], bucket_cap_mb=100,
+                                                    gradient_as_bucket_view=True) if world > 1 else model
+    opt = lm.make_optimizer(model)
+    g = torch.Generator().manual_seed(1000 + rank)        # every rank its own micro-batch
+    n_batches = 4
+    host_ids = [torch.randint(0, LM_CONFIG["vocab_size"], (LM_BATCH, LM_SEQ), generator=g).pin_memory()
+                for _ in range(n_batches)]
+    dev_ids = [t.to(dev) for t in host_ids]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for i in range(max(args.warmup, 3)):
+        lm.train_step(net, opt, dev_ids[i % n_batches], loops=1)
+    torch.cuda.synchronize()
+    zenith_b200.check_status(dev)
+
+    sampler = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    launches0 = _lib.launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(args.steps):
+        lm.train_step(net, opt, dev_ids[i % n_batches], loops=1)
+    end.record()
+    torch.cuda.synchronize()
+    launches = _lib.launch_count() - launches0
+    barrier()
+    clocks = sampler.stop()
+    zenith_b200.check_status(dev)
+    t = torch.tensor([start.elapsed_time(end)], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item()) / args.steps
+    tokens = LM_BATCH * LM_SEQ * world
+    value = tokens / (ms / 1e3)
+
+    # end to end: token ids from pinned host memory every step, the loss read back every step
+    e2e_steps = max(3, args.steps)
+    ids_buf = torch.empty(LM_BATCH, LM_SEQ, dtype=torch.int64, device=dev)
+    barrier()
+    torch.cuda.synchronize()
+    start.record()
+    for i in range(e2e_steps):
+        ids_buf.copy_(host_ids[i % n_batches], non_blocking=True)
+        loss = lm.train_step(net, opt, ids_buf, loops=1)
+        loss.item()
+    end.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([start.elapsed_time(end)], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item()) / e2e_steps
+    zenith_b200.check_status(dev)
+
+    line = None
+    if rank == 0:
+        flops = lm_flops_per_token(LM_CONFIG) * LM_BATCH * LM_SEQ
+        pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+        peak, kind = (float(pk["bf16_tflops_sustained"]), "measured sustained") if pk else (1400.0, "fallback")
+        achieved = flops / (ms / 1e3) / 1e12
+        cpu = None
+        if not args.no_cpu_baseline:
+            tok_s, cores, sample = cpu_lm_sample(LM_CONFIG, args.cpu_seconds)
+            cpu = {"value": tok_s, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+        line = {
+            "metric": LM_METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "Mamba-3 LM training step (AdamW, grad clip, DDP all-reduce over NCCL)",
+                       **LM_CONFIG, "micro_batch": LM_BATCH, "seq_len": LM_SEQ, "global_batch": LM_BATCH * world,
+                       "parallelism": f"dp{world}", "params": sum(p.numel() for p in model.parameters()),
+                       "l2": "activations far larger than L2"},
+            "roofline": {"bound": "tensor", "kernel": "training step (GEMMs + SSD scan), model FLOPs",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                         "peak_kind": kind, "traffic": None, "flops_per_step": flops},
+            "cpu_baseline": cpu,
+            "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": LM_BATCH * LM_SEQ * 8,
+                    "d2h_bytes_per_step": 4},
+            "gpu_launches": launches,
+            "clocks": clocks,
+        }
+    if world > 1:
+        del net
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
+    if args.workload == "lm":
+        return run_lm_reference(args) if args.impl == "reference" else run_lm(args)
     if args.workload == "mamba3":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "metric": LAYER_METRIC,

@@ -44,7 +44,8 @@ typedef enum {
   ZB_ERR_TIMEOUT = 5,      /* a kernel gave up waiting for the preceding chunk's state */
   ZB_ERR_WORKSPACE = 6,    /* workspace or saved-states buffer too small / misaligned */
   ZB_ERR_UNSUPPORTED = 7,  /* sizes beyond what the kernels handle (e.g. P > 256) */
-  ZB_ERR_SCRATCH_LIMIT = 8 /* zb_ssd_fwd_noalloc: the call needs more scratch than ZB_NOALLOC_SCRATCH_BYTES */
+  ZB_ERR_SCRATCH_LIMIT = 8, /* zb_ssd_fwd_noalloc: the call needs more scratch than ZB_NOALLOC_SCRATCH_BYTES */
+  ZB_ERR_INDEX = 9          /* zb_xent: a label outside [0, V) that is not ignore_index */
 } zb_status;
 
 typedef enum { ZB_F32 = 0, ZB_BF16 = 1, ZB_F16 = 2, ZB_F64 = 3 } zb_dtype;

@@ -13,7 +13,9 @@ per-token recurrence (tests/test_mamba3.py:10-21), imported from the reference's
 
 It also runs the reference ``Mamba3`` module (zenith/mamba3.py:58-119) with its input and
 output projections replaced by identities, for the fused layer body (prologue, scan, D skip,
-silu gate): the split tensors, the parameters, the output and every gradient.
+silu gate): the split tensors, the parameters, the output and every gradient; and the reference
+language model ``ZenithForCausalLM`` (zenith/model.py:42-99) at a small configuration: token
+ids, parameters, logits, loss and every parameter gradient (``--only lm`` writes just that).
 
 The fixtures are consumed by tests/test_oracle.py (CPU) and the GPU parity tests; nothing at
 run time reads the reference.
@@ -129,12 +131,48 @@ def mamba3_case(Mamba3, B, T, H, P, N, chunk, A_floor, seed):
     return blob
 
 
+LM_CONFIG = dict(vocab_size=256, d_model=64, d_state=16, expand=2, headdim=16, chunk_size=32, n_input=1,
+                 n_recurrent=1, n_output=1, max_loops=2, tie_word_embeddings=True)  # as configs/*/config.json
+
+
+def lm_case(cfg, B, T, loops, seed):
+    """The reference language model (zenith/model.py:42-99) at a small configuration: one training
+    forward (``model(ids, labels=ids, loops=loops)``, loops > 1 so the no-autograd loops run
+    too) and its backward, in float32.  Norm weights, biases and D are perturbed away from their
+    initial values so every parameter gradient is generic.  Stores the configuration, the token
+    ids, every parameter (``lm_head.weight`` is ``embed.weight``), the logits, the loss and every
+    parameter gradient."""
+    from zenith import ZenithConfig, ZenithForCausalLM
+
+    torch.manual_seed(seed)
+    model = ZenithForCausalLM(ZenithConfig(**cfg))
+    g = torch.Generator().manual_seed(seed + 100)
+    with torch.no_grad():
+        for n, prm in model.named_parameters():
+            if n.endswith(("norm.weight", "B_bias", "C_bias", ".D")):
+                prm.add_(0.2 * torch.randn(prm.shape, generator=g))
+    ids = torch.randint(0, cfg["vocab_size"], (B, T), generator=g)
+    out = model(ids, labels=ids, loops=loops)
+    out.loss.backward()
+    blob = {"config_keys": np.array(list(cfg)), "config_vals": np.array(list(cfg.values())),
+            "ids": ids.numpy(), "loops": np.array(loops), "out_logits": out.logits.detach().numpy(),
+            "out_loss": out.loss.detach().numpy()}
+    for n, prm in model.named_parameters():   # tied lm_head.weight is listed once, as embed.weight
+        blob["in_" + n] = prm.detach().numpy()
+        blob["grad_" + n] = prm.grad.numpy()
+    return blob
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", choices=("ssd", "mamba3", "lm"), help="write one group of fixtures")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from zenith.mamba3 import ssd  # the reference's own chunked scan
+
+    if args.only == "lm":
+        return write_lm()
 
     spec = importlib.util.spec_from_file_location("ref_test_mamba3", pathlib.Path(args.reference) / "tests" / "test_mamba3.py")
     mod = importlib.util.module_from_spec(spec)
@@ -189,6 +227,14 @@ def main():
         path = HERE / f"{name}.npz"
         np.savez_compressed(path, **blob)
         print(f"{name}: B{B} T{T} H{H} P{P} N{N} chunk {chunk}, {path.stat().st_size / 1e3:.0f} kB")
+    # 4. the language model around the layers
+    write_lm()
+
+
+def write_lm():
+    path = HERE / "lm_small_f32.npz"
+    np.savez_compressed(path, **lm_case(LM_CONFIG, 2, 64, 2, 21))
+    print(f"lm_small_f32: {LM_CONFIG}, {path.stat().st_size / 1e3:.0f} kB")
 
 
 if __name__ == "__main__":

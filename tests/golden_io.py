@@ -6,7 +6,7 @@ import torch
 
 GOLDEN = pathlib.Path(__file__).resolve().parent / "golden"
 NAMES = ("x", "q", "k", "kp", "xp", "adt", "gamma", "beta")
-CASES = sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith("mamba3_"))  # scan-boundary cases
+CASES = sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith(("mamba3_", "lm_")))  # scan-boundary cases
 
 
 def load(name):
@@ -27,3 +27,18 @@ def load_mamba3(name):
     ref = {k[4:]: torch.from_numpy(z[k]) for k in z.files if k.startswith("out_")}
     meta = {"A_floor": float(z["A_floor"]), "chunk": int(z["chunk_size"]), "eps": float(z["eps"])}
     return tensors, torch.from_numpy(z["in_dout"]), ref, meta
+
+
+LM_CASES = ("lm_small_f32",)
+
+
+def load_lm(name):
+    """Configuration, token ids, loop count, parameters (state_dict names, lm_head tied to embed),
+    logits, loss and parameter gradients of one language-model case (from the reference
+    ``ZenithForCausalLM`` by make_golden.py)."""
+    z = np.load(GOLDEN / f"{name}.npz")
+    cfg = {str(k): int(v) for k, v in zip(z["config_keys"], z["config_vals"])}
+    params = {k[3:]: torch.from_numpy(z[k]) for k in z.files if k.startswith("in_")}
+    grads = {k[5:]: torch.from_numpy(z[k]) for k in z.files if k.startswith("grad_")}
+    return (cfg, torch.from_numpy(z["ids"]), int(z["loops"]), params, torch.from_numpy(z["out_logits"]),
+            torch.from_numpy(z["out_loss"]), grads)

@@ -1,0 +1,157 @@
+"""GPU parity of the language-model kernels and model (zenith_b200.lm): the fused residual-add +
+RMSNorm and the one-pass cross-entropy against plain float64 PyTorch restatements, and the whole
+looped LM (forward logits, loss, every parameter gradient) against golden vectors from the
+reference ZenithForCausalLM (float32) and against the float64 oracle under bf16 autocast.
+Error metric: max |out - ref| / max |ref| per tensor."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import lm_oracle
+from oracle.ssd_oracle import max_rel_err
+from tests.golden_io import LM_CASES, load_lm
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda")
+
+
+def _rmsnorm_ref(s, w, eps):
+    return s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + eps) * w
+
+
+@pytest.mark.parametrize("x_dtype,b_dtype,u_dtype,D", [
+    (torch.float32, torch.float32, torch.float32, 256),
+    (torch.float32, torch.bfloat16, torch.bfloat16, 1536),
+    (torch.bfloat16, torch.bfloat16, torch.bfloat16, 640),
+    (torch.float32, None, torch.float32, 100),           # D % 8 != 0: the scalar path
+    (torch.float32, torch.float32, torch.bfloat16, 36),
+])
+def test_add_rmsnorm_matches_torch(x_dtype, b_dtype, u_dtype, D):
+    from zenith_b200 import lm
+
+    g = torch.Generator().manual_seed(D)
+    M = 3 * 333
+    a = torch.randn(M, D, generator=g).to(x_dtype)
+    b = torch.randn(M, D, generator=g).to(b_dtype) if b_dtype else None
+    w = 1 + 0.3 * torch.randn(D, generator=g)
+    ds = torch.randn(M, D, generator=g)
+    du = torch.randn(M, D, generator=g)
+    la, lw = a.to(DEV).requires_grad_(), w.to(DEV).requires_grad_()
+    lb = b.to(DEV).requires_grad_() if b is not None else None
+    out = lm.add_rmsnorm(la, lb, lw, 1e-5, u_dtype)
+    s, u = out if b is not None else (la, out)
+    tot = (u.float() * du.to(DEV)).sum() + ((s.float() * ds.to(DEV)).sum() if b is not None else 0)
+    tot.backward()
+    # reference: float64 on the stored sum (rounded to the residual dtype), as the kernel computes
+    ra, rw = a.double().requires_grad_(), w.double().requires_grad_()
+    rb = b.double().requires_grad_() if b is not None else None
+    rs = (ra + rb) if rb is not None else ra
+    rs_st = rs + (rs.to(x_dtype).double() - rs).detach()
+    ru = _rmsnorm_ref(rs_st, rw, 1e-5)
+    rtot = (ru * du.double()).sum() + ((rs_st * ds.double()).sum() if rb is not None else 0)
+    rtot.backward()
+    tol_u = 1e-5 if u_dtype == torch.float32 else 8e-3
+    tol_g = 1e-5 if (x_dtype == torch.float32 and u_dtype == torch.float32) else 2e-2
+    assert max_rel_err(u.double().cpu(), ru.to(u_dtype).double()) < tol_u
+    if b is not None:
+        assert max_rel_err(s.double().cpu(), rs_st) < 1e-6
+        assert max_rel_err(lb.grad.double().cpu(), rb.grad) < tol_g
+    assert max_rel_err(la.grad.double().cpu(), ra.grad) < tol_g
+    assert max_rel_err(lw.grad.double().cpu(), rw.grad) < tol_g
+
+
+@pytest.mark.parametrize("dtype,V", [(torch.float32, 1000), (torch.float32, 999), (torch.bfloat16, 32000),
+                                     (torch.bfloat16, 50001), (torch.float32, 8)])
+def test_linear_cross_entropy_matches_torch(dtype, V):
+    from zenith_b200 import lm
+
+    g = torch.Generator().manual_seed(V)
+    M, d = 300, 64
+    h = torch.randn(M, d, generator=g)
+    W = 0.3 * torch.randn(V, d, generator=g)
+    labels = torch.randint(0, V, (M,), generator=g)
+    labels[::7] = -100                                   # ignored rows
+    lh, lW = h.to(DEV).requires_grad_(), W.to(DEV).requires_grad_()
+    loss = lm.linear_cross_entropy(lh, lW, labels.to(DEV), compute_dtype=dtype)
+    loss.backward()
+    # float64 reference on the operands and logits as the kernel sees them (rounded to dtype)
+    rh, rW = h.double().requires_grad_(), W.double().requires_grad_()
+    rnd = lambda t: t + (t.to(dtype).double() - t).detach()
+    logits = rnd(rnd(rh) @ rnd(rW).T)
+    ref = F.cross_entropy(logits, labels)
+    ref.backward()
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    assert abs(loss.item() - ref.item()) < tol * abs(ref.item())
+    assert max_rel_err(lh.grad.double().cpu(), rh.grad) < tol
+    assert max_rel_err(lW.grad.double().cpu(), rW.grad) < tol
+
+
+def test_cross_entropy_rejects_out_of_range_labels():
+    """A label outside [0, V) sets the device status word (the row is skipped, nothing faults)."""
+    import zenith_b200
+    from zenith_b200 import lm
+
+    h = torch.randn(4, 16, device=DEV)
+    W = torch.randn(32, 16, device=DEV)
+    labels = torch.tensor([1, 2, 40, 3], device=DEV)
+    lm.linear_cross_entropy(h, W, labels)
+    with pytest.raises(zenith_b200.SsdError, match="status 9"):
+        zenith_b200.check_status()
+    zenith_b200.check_status()   # reset by the failed check
+
+
+def _model(case):
+    from zenith_b200 import lm
+
+    cfg, ids, loops, params, logits, loss, grads = load_lm(case)
+    model = lm.ZenithForCausalLM(cfg).to(DEV)
+    lm.load_reference_state_dict(model, {n: t.to(DEV) for n, t in params.items()})
+    return model, cfg, ids, loops, params, logits, loss, grads
+
+
+@pytest.mark.parametrize("case", LM_CASES)
+def test_lm_fp32_matches_reference_model(case):
+    """float32 throughout (exact scan): logits, loss and every parameter gradient of the reference
+    ZenithForCausalLM to 1e-4, including the no-autograd recurrent loops."""
+    model, cfg, ids, loops, params, logits, loss, grads = _model(case)
+    out = model(ids.to(DEV), labels=ids.to(DEV), loops=loops, return_logits=True)
+    out.loss.backward()
+    torch.cuda.synchronize()
+    assert max_rel_err(out.logits.double().cpu(), logits.double()) < 1e-4
+    assert abs(out.loss.item() - loss.item()) < 1e-4 * abs(loss.item())
+    named = dict(model.named_parameters())
+    for n, g in grads.items():
+        assert max_rel_err(named[n].grad.double().cpu(), g.double()) < 1e-4, (n, max_rel_err(named[n].grad.double().cpu(), g.double()))
+
+
+@pytest.mark.parametrize("case", LM_CASES)
+def test_lm_bf16_autocast_matches_oracle(case):
+    """bf16 autocast (bf16 GEMMs, bf16 in_proj output into the layer kernels, tensor-core scan)
+    against the float64 oracle: loss to 1e-2, logits and parameter gradients to 5e-2 (bf16
+    rounding of the GEMM operands through five layers)."""
+    model, cfg, ids, loops, params, logits, loss, grads = _model(case)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        out = model(ids.to(DEV), labels=ids.to(DEV), loops=loops, return_logits=True)
+    out.loss.backward()
+    o_logits, o_loss, o_grads = lm_oracle.forward_backward(params, cfg, ids, loops)
+    assert abs(out.loss.item() - o_loss.item()) < 1e-2 * abs(o_loss.item())
+    assert max_rel_err(out.logits.double().cpu(), o_logits) < 5e-2
+    named = dict(model.named_parameters())
+    errs = {n: max_rel_err(named[n].grad.double().cpu(), g) for n, g in o_grads.items() if g.abs().max() > 0}
+    bad = {n: e for n, e in errs.items() if not e < 5e-2}
+    assert not bad, bad
+
+
+def test_train_step_reduces_loss():
+    """A few AdamW steps on one fixed batch of the small configuration lower its loss."""
+    from zenith_b200 import lm
+
+    cfg = dict(vocab_size=256, d_model=64, d_state=16, expand=2, headdim=16, chunk_size=32, n_input=1,
+               n_recurrent=1, n_output=1, max_loops=2)
+    torch.manual_seed(0)
+    model = lm.ZenithForCausalLM(cfg).to(DEV)
+    opt = lm.make_optimizer(model, lr=3e-3)
+    ids = torch.randint(0, 256, (2, 64), device=DEV)
+    losses = [lm.train_step(model, opt, ids, loops=2).item() for _ in range(8)]
+    assert losses[-1] < losses[0] - 0.1, losses

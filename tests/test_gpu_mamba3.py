@@ -188,3 +188,20 @@ def test_fused_layer_many_heads(H, scan_dtype):
     for n in ALL:
         if ref["d" + n].abs().max() > 0:
             assert max_rel_err(grads["d" + n], ref["d" + n]) < tol, (n, max_rel_err(grads["d" + n], ref["d" + n]))
+
+
+@pytest.mark.parametrize("H,P,scan_dtype", [(48, 64, torch.bfloat16), (40, 16, torch.float32), (32, 32, torch.float32)])
+def test_fused_layer_head_groups(H, P, scan_dtype):
+    """More than 31 heads: the row kernels split the heads into groups (48 -> 2 x 24, 40 -> 2 x 20,
+    32 -> 2 x 16); the backward sums the B / C row gradients over the groups before the RMSNorm.
+    Results match the oracle."""
+    tensors, dout, meta = _synthetic(2, 192, H, P, 128, seed=27)
+    out, grads = _run(tensors, dout, meta, scan_dtype=scan_dtype)
+    rnd = torch.bfloat16 if scan_dtype == torch.bfloat16 else None
+    ref_out, ref = M.forward_backward(tensors, dout, meta["A_floor"], meta["chunk"], meta["eps"],
+                                      scan_operand_dtype=rnd)
+    tol = 2e-2 if rnd is not None else 1e-4
+    assert max_rel_err(out, ref_out) < tol
+    for n in ALL:
+        if ref["d" + n].abs().max() > 0:
+            assert max_rel_err(grads["d" + n], ref["d" + n]) < tol, (n, max_rel_err(grads["d" + n], ref["d" + n]))

@@ -3,8 +3,8 @@ import pytest
 import torch
 
 from oracle.ssd_oracle import max_rel_err, naive_recurrence, ssd_backward, ssd_forward
-from oracle import mamba3_oracle
-from tests.golden_io import CASES, MAMBA3_CASES, NAMES, load, load_mamba3
+from oracle import lm_oracle, mamba3_oracle
+from tests.golden_io import CASES, LM_CASES, MAMBA3_CASES, NAMES, load, load_lm, load_mamba3
 
 
 @pytest.mark.parametrize("case", CASES)
@@ -84,3 +84,21 @@ def test_mamba3_oracle_matches_reference_module(case):
             assert grads["d" + n].abs().max() == 0, n
         else:
             assert max_rel_err(grads["d" + n], r) < 2e-6, n
+
+
+@pytest.mark.parametrize("case", LM_CASES)
+def test_lm_oracle_matches_reference_model(case):
+    """The language-model oracle (embedding, input / looped recurrent / output layers, tied LM
+    head, next-token cross-entropy) against the reference ZenithForCausalLM run in float32:
+    logits, loss and the gradient of every parameter."""
+    cfg, ids, loops, params, logits, loss, grads = load_lm(case)
+    o_logits, o_loss, o_grads = lm_oracle.forward_backward(params, cfg, ids, loops)
+    assert max_rel_err(o_logits, logits.double()) < 2e-5
+    assert abs(o_loss.item() - loss.item()) < 2e-5 * abs(loss.item())
+    assert set(o_grads) == set(grads)
+    for n, g in grads.items():
+        if g.abs().max() == 0:   # dd_A rows of in_proj can be saturated by the A_floor clamp
+            assert o_grads[n].abs().max() < 1e-12, n
+        else:
+            assert max_rel_err(o_grads[n], g.double()) < 5e-5, (n, max_rel_err(o_grads[n], g.double()))
+

@@ -11,6 +11,10 @@ from .parallel import cp_ssd  # noqa: E402  (context parallelism over torch.dist
 
 __all__.append("cp_ssd")
 
-from .mamba3 import mamba3_ssd_fused, use_b200_layer  # noqa: E402  (fused Mamba-3 layer body)
+from .mamba3 import mamba3_layer_packed, mamba3_ssd_fused, use_b200_layer  # noqa: E402  (fused Mamba-3 layer body)
 
-__all__ += ["mamba3_ssd_fused", "use_b200_layer"]
+__all__ += ["mamba3_layer_packed", "mamba3_ssd_fused", "use_b200_layer"]
+
+from .lm import ZenithConfig, ZenithForCausalLM, add_rmsnorm, linear_cross_entropy, train_step  # noqa: E402  (LM)
+
+__all__ += ["ZenithConfig", "ZenithForCausalLM", "add_rmsnorm", "linear_cross_entropy", "train_step"]

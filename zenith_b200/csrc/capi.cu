@@ -179,6 +179,7 @@ const char* zb_strerror(int s) {
     case ZB_ERR_WORKSPACE: return "workspace or saved-states buffer missing, too small or misaligned";
     case ZB_ERR_UNSUPPORTED: return "sizes not supported by the kernels";
     case ZB_ERR_SCRATCH_LIMIT: return "call needs more scratch than the fixed no-alloc array (ZB_NOALLOC_SCRATCH_BYTES)";
+    case ZB_ERR_INDEX: return "label outside [0, vocabulary size)";
     default: return "unknown status";
   }
 }

@@ -1,0 +1,407 @@
+// Language-model kernels around the Mamba-3 layers (zenith/model.py:42-99): the residual add
+// fused with the RMSNorm that reads it, and the next-token cross-entropy with its logit gradient
+// in one pass over the logits.  Both are HBM-bound row kernels: 16-byte accesses, one warp per
+// row (RMSNorm) or one CTA per row (cross-entropy), fixed-order reductions.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+
+#include "common.cuh"
+#include "ssd_kernels.h"
+#include "zb_lm.h"
+
+namespace zb {
+namespace {
+
+// ---------------------------------------------------------------------------------------------
+// residual add + RMSNorm (mamba3.py:8-15; model.py:48-49,87,93)
+
+constexpr int kNormWarps = 8;     // rows in flight per CTA, one warp each
+constexpr int kNormGrid = 1024;   // CTAs at most: a fixed grid fixes the order of the dw sums
+constexpr int kNormMaxD = 8192;
+
+struct NormP {
+  int64_t M, D;
+  float eps;
+  bool vec;  // D % 8 == 0 and every row pointer 16-byte aligned: 8-element accesses
+  const void *a, *b;
+  void* s;
+  const float* w;
+  void* u;
+  float* r;
+  const void *du, *ds;
+  void *dsum, *dsum_b;
+  float* dw;
+  float* part;  // [grid][D] per-CTA dw sums
+};
+
+// v rounded to the storage type T
+template <typename T> __device__ __forceinline__ float round_to(float v);
+template <> __device__ __forceinline__ float round_to<__nv_bfloat16>(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+template <> __device__ __forceinline__ float round_to<float>(float v) { return v; }
+
+// s = a + b (stored, then read back as stored), r = rsqrt(mean(s^2) + eps), u = (s r) w
+template <typename TX, typename TB, typename TU>
+__global__ void __launch_bounds__(32 * kNormWarps) rmsnorm_fwd_kernel(const NormP p) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, D = (int)p.D;
+  const TX* __restrict__ A = static_cast<const TX*>(p.a);
+  const TB* __restrict__ Bv = static_cast<const TB*>(p.b);
+  TX* __restrict__ S = static_cast<TX*>(p.s);
+  TU* __restrict__ U = static_cast<TU*>(p.u);
+  for (int64_t row = (int64_t)blockIdx.x * kNormWarps + warp; row < p.M; row += (int64_t)gridDim.x * kNormWarps) {
+    const int64_t o = row * D;
+    float ss = 0.f;
+    if (p.vec) {
+      for (int n = 8 * lane; n < D; n += 256) {
+        float v[8];
+        Vec8<TX>::ld(A + o + n, v);
+        if (Bv) {
+          float c[8];
+          Vec8<TB>::ld(Bv + o + n, c);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = round_to<TX>(v[e] + c[e]);
+          Vec8<TX>::st(S + o + n, v);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+      }
+    } else {
+      for (int n = lane; n < D; n += 32) {
+        float v = ldv<float>(A + o + n);
+        if (Bv) {
+          v = round_to<TX>(v + ldv<float>(Bv + o + n));
+          stv<float>(S + o + n, v);
+        }
+        ss += v * v;
+      }
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / D + p.eps);
+    if (p.r && lane == 0) p.r[row] = r;
+    const TX* __restrict__ src = Bv ? S : A;  // the lane re-reads only what it wrote itself
+    if (p.vec) {
+      for (int n = 8 * lane; n < D; n += 256) {
+        float v[8], w[8];
+        Vec8<TX>::ld(src + o + n, v);
+        Vec8<float>::ld(p.w + n, w);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = v[e] * r * w[e];
+        Vec8<TU>::st(U + o + n, v);
+      }
+    } else {
+      for (int n = lane; n < D; n += 32) stv<float>(U + o + n, ldv<float>(src + o + n) * r * p.w[n]);
+    }
+  }
+}
+
+// dsum = ds + r w du - s r^3 / D sum(du w s) (also as TB in dsum_b); per-CTA dw sums of du s r
+// (per warp in shared memory, then over the warps in order)
+template <typename TX, typename TB, typename TU>
+__global__ void __launch_bounds__(32 * kNormWarps) rmsnorm_bwd_kernel(const NormP p) {
+  extern __shared__ float sdw[];  // [kNormWarps][D]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, D = (int)p.D;
+  float* myw = sdw + warp * D;
+  for (int n = lane; n < D; n += 32) myw[n] = 0.f;
+  const TX* __restrict__ S = static_cast<const TX*>(p.b ? p.s : p.a);
+  const TU* __restrict__ dU = static_cast<const TU*>(p.du);
+  const TX* __restrict__ dS = static_cast<const TX*>(p.ds);
+  TX* __restrict__ G = static_cast<TX*>(p.dsum);
+  TB* __restrict__ GB = static_cast<TB*>(p.dsum_b);
+  for (int64_t row = (int64_t)blockIdx.x * kNormWarps + warp; row < p.M; row += (int64_t)gridDim.x * kNormWarps) {
+    const int64_t o = row * D;
+    const float r = p.r[row];
+    float dot = 0.f;
+    if (p.vec) {
+      for (int n = 8 * lane; n < D; n += 256) {
+        float g[8], x[8], w[8];
+        Vec8<TU>::ld(dU + o + n, g);
+        Vec8<TX>::ld(S + o + n, x);
+        Vec8<float>::ld(p.w + n, w);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dot += g[e] * w[e] * x[e];
+      }
+    } else {
+      for (int n = lane; n < D; n += 32) dot += ldv<float>(dU + o + n) * p.w[n] * ldv<float>(S + o + n);
+    }
+    const float k3 = r * r * r / D * warp_sum(dot);
+    if (p.vec) {
+      for (int n = 8 * lane; n < D; n += 256) {
+        float g[8], x[8], w[8], out[8];
+        Vec8<TU>::ld(dU + o + n, g);
+        Vec8<TX>::ld(S + o + n, x);
+        Vec8<float>::ld(p.w + n, w);
+        if (dS) Vec8<TX>::ld(dS + o + n, out);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          out[e] = (dS ? out[e] : 0.f) + r * w[e] * g[e] - x[e] * k3;
+          myw[n + e] += g[e] * x[e] * r;
+        }
+        Vec8<TX>::st(G + o + n, out);
+        if (GB) Vec8<TB>::st(GB + o + n, out);
+      }
+    } else {
+      for (int n = lane; n < D; n += 32) {
+        const float g = ldv<float>(dU + o + n), x = ldv<float>(S + o + n);
+        const float v = (dS ? ldv<float>(dS + o + n) : 0.f) + r * p.w[n] * g - x * k3;
+        stv<float>(G + o + n, v);
+        if (GB) stv<float>(GB + o + n, v);
+        myw[n] += g * x * r;
+      }
+    }
+  }
+  __syncthreads();
+  for (int n = threadIdx.x; n < D; n += blockDim.x) {
+    float s = 0.f;
+    for (int k = 0; k < kNormWarps; ++k) s += sdw[k * D + n];
+    p.part[(int64_t)blockIdx.x * D + n] = s;
+  }
+}
+
+__global__ void rmsnorm_dw_kernel(const NormP p, int nblocks) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= p.D) return;
+  float s = 0.f;
+  for (int k = 0; k < nblocks; ++k) s += p.part[(int64_t)k * p.D + n];
+  p.dw[n] = s;
+}
+
+int norm_grid(int64_t M) { return (int)((M + kNormWarps - 1) / kNormWarps < kNormGrid ? (M + kNormWarps - 1) / kNormWarps : kNormGrid); }
+
+bool aligned16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; }
+
+int norm_check(const zb_rmsnorm_args* a) {
+  if (!a) return ZB_ERR_LAYOUT;
+  if (a->M <= 0 || a->D <= 0) return ZB_ERR_SHAPE;
+  if (a->D > kNormMaxD) return ZB_ERR_UNSUPPORTED;
+  for (int32_t d : {a->x_dtype, a->b_dtype, a->u_dtype})
+    if (d != ZB_F32 && d != ZB_BF16) return ZB_ERR_DTYPE;
+  if (!a->a || !a->w) return ZB_ERR_LAYOUT;
+  return ZB_OK;
+}
+
+NormP make_norm(const zb_rmsnorm_args* a, bool bwd) {
+  NormP p;
+  p.M = a->M; p.D = a->D; p.eps = a->eps;
+  p.a = a->a; p.b = a->b; p.s = a->s; p.w = a->w; p.u = a->u; p.r = a->r;
+  p.du = a->du; p.ds = a->ds; p.dsum = a->dsum; p.dsum_b = a->dsum_b; p.dw = a->dw;
+  p.part = static_cast<float*>(a->workspace);
+  const void* ptrs_f[] = {a->a, a->b, a->s, a->w, a->u};
+  const void* ptrs_b[] = {a->a, a->b, a->s, a->w, a->du, a->ds, a->dsum, a->dsum_b};
+  bool ok = a->D % 8 == 0;
+  if (bwd) { for (const void* q : ptrs_b) ok = ok && aligned16(q); }
+  else { for (const void* q : ptrs_f) ok = ok && aligned16(q); }
+  p.vec = ok;
+  return p;
+}
+
+// call f with a value of the element type that a zb_dtype code names (float or bf16)
+template <typename F> int with_type(int32_t code, F&& f) {
+  switch (code) {
+    case ZB_F32: return f(float{});
+    case ZB_BF16: return f(__nv_bfloat16{});
+    default: return ZB_ERR_DTYPE;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// cross-entropy (model.py:95-97): one CTA per row
+
+constexpr int kXentThreads = 512;
+
+struct XentP {
+  int64_t M, V, ld, ignore;
+  bool write_grad;
+  void* logits;
+  const int64_t* labels;
+  float* loss;
+  float* lse;
+  int32_t* status;
+};
+
+// max and sum of exp over the CTA: warp shuffles, then the warps' pairs in order
+__device__ __forceinline__ void block_max_sum(float& m, float& s, float* sm, float* ss) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    const float M = fmaxf(m, m2);
+    s = (M == -INFINITY) ? 0.f : s * expf(m - M) + s2 * expf(m2 - M);
+    m = M;
+  }
+  if (lane == 0) {
+    sm[warp] = m;
+    ss[warp] = s;
+  }
+  __syncthreads();
+  float M = -INFINITY;
+  for (int k = 0; k < nw; ++k) M = fmaxf(M, sm[k]);
+  float S = 0.f;
+  if (M != -INFINITY)
+    for (int k = 0; k < nw; ++k) S += ss[k] * expf(sm[k] - M);
+  m = M;
+  s = S;
+}
+
+// kPer > 0: the row is held in registers, kPer 8-element units per thread (V % 8 == 0, aligned
+// rows); kPer == 0: any V, the row is read twice
+template <typename T, int kPer>
+__global__ void __launch_bounds__(kXentThreads) xent_kernel(const XentP p) {
+  __shared__ float sm[kXentThreads / 32], ss[kXentThreads / 32];
+  const int64_t row = blockIdx.x;
+  T* __restrict__ L = static_cast<T*>(p.logits) + row * p.ld;
+  const int V = (int)p.V;
+  const int64_t lab = p.labels[row];
+  bool valid = lab != p.ignore;
+  if (valid && (lab < 0 || lab >= p.V)) {
+    if (threadIdx.x == 0) atomicCAS(p.status, 0, (int32_t)ZB_ERR_INDEX);
+    valid = false;
+  }
+  const float xl = (valid && threadIdx.x == 0) ? ldv<float>(L + lab) : 0.f;  // before any thread writes
+  float m = -INFINITY, s = 0.f;
+  float v[kPer > 0 ? kPer : 1][8];
+  if constexpr (kPer > 0) {
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int n = (i * kXentThreads + threadIdx.x) * 8;
+      if (n < V) {
+        Vec8<T>::ld(L + n, v[i]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m = fmaxf(m, v[i][e]);
+      }
+    }
+    if (m != -INFINITY)
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int n = (i * kXentThreads + threadIdx.x) * 8;
+        if (n < V)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) s += expf(v[i][e] - m);
+      }
+  } else {
+    for (int n = threadIdx.x; n < V; n += kXentThreads) {
+      const float x = ldv<float>(L + n);
+      if (x > m) {
+        s = s * expf(m - x) + 1.f;
+        m = x;
+      } else {
+        s += expf(x - m);
+      }
+    }
+  }
+  block_max_sum(m, s, sm, ss);
+  const float lse = m + logf(s);
+  if (threadIdx.x == 0) {
+    p.loss[row] = valid ? lse - xl : 0.f;
+    if (p.lse) p.lse[row] = lse;
+  }
+  if (!p.write_grad) return;
+  if constexpr (kPer > 0) {
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int n = (i * kXentThreads + threadIdx.x) * 8;
+      if (n < V) {
+        float g[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) g[e] = valid ? expf(v[i][e] - lse) - (n + e == lab ? 1.f : 0.f) : 0.f;
+        Vec8<T>::st(L + n, g);
+      }
+    }
+  } else {
+    for (int n = threadIdx.x; n < V; n += kXentThreads) {
+      const float x = ldv<float>(L + n);
+      stv<float>(L + n, valid ? expf(x - lse) - (n == lab ? 1.f : 0.f) : 0.f);
+    }
+  }
+}
+
+template <typename T> int launch_xent(const XentP& p, bool vec, cudaStream_t st) {
+  const dim3 grid((unsigned)p.M);
+  const int64_t unit = (int64_t)kXentThreads * 8;
+  if (vec && p.V <= unit) xent_kernel<T, 1><<<grid, kXentThreads, 0, st>>>(p);
+  else if (vec && p.V <= 2 * unit) xent_kernel<T, 2><<<grid, kXentThreads, 0, st>>>(p);
+  else if (vec && p.V <= 4 * unit) xent_kernel<T, 4><<<grid, kXentThreads, 0, st>>>(p);
+  else if (vec && p.V <= 8 * unit) xent_kernel<T, 8><<<grid, kXentThreads, 0, st>>>(p);
+  else xent_kernel<T, 0><<<grid, kXentThreads, 0, st>>>(p);
+  return ZB_OK;
+}
+
+int finish_lm(int n) {
+  note_launches(n);
+  return cudaPeekAtLastError() == cudaSuccess ? ZB_OK : ZB_ERR_CUDA;
+}
+
+}  // namespace
+}  // namespace zb
+
+using namespace zb;
+
+extern "C" ZB_API uint64_t zb_rmsnorm_workspace_bytes(const zb_rmsnorm_args* a) {
+  if (!a || a->M <= 0 || a->D <= 0) return 0;
+  return align_up((size_t)norm_grid(a->M) * a->D * sizeof(float), 256);
+}
+
+extern "C" ZB_API int zb_rmsnorm_fwd(const zb_rmsnorm_args* a, void* stream) {
+  int rc = norm_check(a);
+  if (rc) return rc;
+  if (!a->u || (a->b && !a->s)) return ZB_ERR_LAYOUT;
+  const NormP p = make_norm(a, false);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = with_type(a->x_dtype, [&](auto tx) {
+    return with_type(a->b_dtype, [&](auto tb) {
+      return with_type(a->u_dtype, [&](auto tu) {
+        rmsnorm_fwd_kernel<decltype(tx), decltype(tb), decltype(tu)><<<norm_grid(a->M), 32 * kNormWarps, 0, st>>>(p);
+        return (int)ZB_OK;
+      });
+    });
+  });
+  return rc ? rc : finish_lm(1);
+}
+
+extern "C" ZB_API int zb_rmsnorm_bwd(const zb_rmsnorm_args* a, void* stream) {
+  int rc = norm_check(a);
+  if (rc) return rc;
+  if (!a->du || !a->dsum || !a->dw || !a->r || (a->b && !a->s)) return ZB_ERR_LAYOUT;
+  if (!a->workspace || a->workspace_bytes < zb_rmsnorm_workspace_bytes(a) ||
+      (reinterpret_cast<uintptr_t>(a->workspace) & 255))
+    return ZB_ERR_WORKSPACE;
+  const NormP p = make_norm(a, true);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int grid = norm_grid(a->M);
+  const int smem = (int)(kNormWarps * a->D * sizeof(float));
+  rc = with_type(a->x_dtype, [&](auto tx) {
+    return with_type(a->b_dtype, [&](auto tb) {
+      return with_type(a->u_dtype, [&](auto tu) {
+        auto k = rmsnorm_bwd_kernel<decltype(tx), decltype(tb), decltype(tu)>;
+        if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+          return (int)ZB_ERR_CUDA;
+        k<<<grid, 32 * kNormWarps, smem, st>>>(p);
+        return (int)ZB_OK;
+      });
+    });
+  });
+  if (rc) return rc;
+  rmsnorm_dw_kernel<<<(unsigned)((a->D + 255) / 256), 256, 0, st>>>(p, grid);
+  return finish_lm(2);
+}
+
+extern "C" ZB_API int zb_xent(const zb_xent_args* a, void* stream) {
+  if (!a) return ZB_ERR_LAYOUT;
+  if (a->M <= 0 || a->V <= 0 || a->ld < a->V || a->M > 0x7fffffff || a->V > 0x7fffffff) return ZB_ERR_SHAPE;
+  if (!a->logits || !a->labels || !a->loss || !a->status) return ZB_ERR_LAYOUT;
+  XentP p;
+  p.M = a->M; p.V = a->V; p.ld = a->ld; p.ignore = a->ignore_index;
+  p.write_grad = a->write_grad != 0;
+  p.logits = a->logits; p.labels = a->labels; p.loss = a->loss; p.lse = a->lse; p.status = a->status;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t es = a->dtype == ZB_F32 ? 4 : 2;
+  const bool vec = a->V % 8 == 0 && (a->ld * es) % 16 == 0 && aligned16(a->logits);
+  switch (a->dtype) {
+    case ZB_F32: launch_xent<float>(p, vec, st); break;
+    case ZB_BF16: launch_xent<__nv_bfloat16>(p, vec, st); break;
+    default: return ZB_ERR_DTYPE;
+  }
+  return finish_lm(1);
+}

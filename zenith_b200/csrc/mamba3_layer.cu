@@ -2,12 +2,14 @@
 // the prologue that turns the in_proj split into the scan operands (discretisation, RMSNorm,
 // RoPE, one-token shift) and the epilogue (D skip, silu gate).
 //
-// One CTA per (batch, 64-token segment), one warp per head (H <= 31).  Per-token RMSNorm and
+// One CTA per (batch, 64-token segment, head group), one warp per head of the group (at most 29
+// heads a group; H <= 31 is one group).  Per-token RMSNorm and
 // RoPE run lane-parallel over the state features: lane i owns RoPE pair i (features 2i, 2i+1)
 // and the pass-through pair (2A+2i, 2A+2i+1), A = N/4 angles.  theta = cumsum_t(DT ang) spans
 // the whole sequence; it crosses segments through per-segment sums (forward) and per-segment
 // totals of its gradient (backward).  Reductions over heads and over (batch, token) run in a
-// fixed order, so results are bitwise reproducible.
+// fixed order, so results are bitwise reproducible.  With several head groups the backward's sums
+// over heads are summed per group, then over the groups by a per-token kernel.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -26,6 +28,7 @@ constexpr int kSeg = 64;  // tokens per segment
 struct M3 {
   int64_t B, T, H, P, N;
   int NA, nseg;
+  int hg, nhg;  // heads per group, head groups: CTA (b, seg, g) owns heads g hg .. min(H, (g + 1) hg) - 1
   bool pairs;  // B / C rows and their gradients allow 2-element accesses (checked on the host)
   bool vec8;   // x, z, out, dout, dx, dz allow 16-byte accesses of 8 elements (checked on the host)
   bool rows8;  // Bm, Cm rows allow 16-byte accesses of 8 elements (checked on the host)
@@ -44,7 +47,9 @@ struct M3 {
   // scratch
   float* segsum;  // [B][H][nseg][NA]   theta segment sums (forward) / theta-gradient segment totals (backward)
   float* dDTl;    // [B][T][H]          backward: DT gradient through theta, within-segment part
-  float* dangl;   // [B][T][NA]         backward: ang gradient, within-segment part
+  float* dangl;   // [nhg][B][T][NA]    backward: ang gradient, within-segment part (per head group)
+  float* duC;     // [nhg][B][T][N]     backward, nhg > 1: C row gradient before the RMSNorm, per head group
+  float* duB;     // [nhg][B][T][N]     backward, nhg > 1: B row gradient before the RMSNorm, per head group
   float* pbias;   // [2][B][nseg][H][N] backward: B_bias, C_bias partial sums
   float* pnorm;   // [2][B][nseg][N]    backward: B_norm_w, C_norm_w partial sums
   float* pdt;     // [B][nseg][H]       backward: dt_bias partial sums
@@ -120,37 +125,6 @@ template <typename T> __device__ __forceinline__ void st4(T* row, Feat f, const 
   }
 }
 
-// eight consecutive elements (16-byte aligned) as 16-byte accesses
-template <typename T> struct Vec8;
-template <> struct Vec8<float> {
-  static __device__ __forceinline__ void ld(const float* p, float (&v)[8]) {
-    const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-  }
-  static __device__ __forceinline__ void st(float* p, const float (&v)[8]) {
-    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
-    *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
-  }
-};
-template <> struct Vec8<__nv_bfloat16> {
-  static __device__ __forceinline__ void ld(const __nv_bfloat16* p, float (&v)[8]) {
-    const uint4 u = *reinterpret_cast<const uint4*>(p);
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __bfloat1622float2(h[i]);
-      v[2 * i] = f.x;
-      v[2 * i + 1] = f.y;
-    }
-  }
-  static __device__ __forceinline__ void st(__nv_bfloat16* p, const float (&v)[8]) {
-    uint4 u;
-    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-    *reinterpret_cast<uint4*>(p) = u;
-  }
-};
 // the lane's four features of an fp32 row (8-byte aligned pairs: two 2-float loads)
 __device__ __forceinline__ void ldp4(const float* row, Feat f, float (&v)[4]) {
   const float2 a = *reinterpret_cast<const float2*>(row + f.f0), c = *reinterpret_cast<const float2*>(row + f.f2);
@@ -171,6 +145,21 @@ __device__ __forceinline__ void norm_bias_rope(const float (&c)[4], float r, con
   o[3] = u[3];
 }
 
+// the CTA's (batch, segment, head group): blockIdx.x = (b nseg + seg) nhg + g, heads h0 .. h0 + hc - 1
+struct Blk {
+  int b, seg, g, h0, hc;
+};
+__device__ __forceinline__ Blk blk(const M3& p) {
+  Blk k;
+  k.g = blockIdx.x % p.nhg;
+  const int bs = blockIdx.x / p.nhg;
+  k.b = bs / p.nseg;
+  k.seg = bs % p.nseg;
+  k.h0 = k.g * p.hg;
+  k.hc = min(p.hg, (int)p.H - k.h0);
+  return k;
+}
+
 // ---------------------------------------------------------------------------------------------
 // forward
 //
@@ -179,10 +168,10 @@ __device__ __forceinline__ void norm_bias_rope(const float (&c)[4], float r, con
 // only; theta's running sum is the one serial dependency.
 
 // shared layout of a forward segment: C rows, B rows (both scaled by their RMSNorm factor),
-// angles, DT per head
+// angles, DT per head of the group
 struct FwdSeg {
   float *c, *bm, *ang, *dt;
-  __device__ FwdSeg(float* s, int N, int NA, int H)
+  __device__ FwdSeg(float* s, int N, int NA)
       : c(s), bm(s + kSeg * N), ang(s + 2 * kSeg * N), dt(s + 2 * kSeg * N + kSeg * NA) {}
 };
 
@@ -246,54 +235,57 @@ __device__ __forceinline__ void stage_rows(const M3& p, int b, int64_t t0, int n
 template <typename TI>
 __global__ void __launch_bounds__(1024) m3_segsum_kernel(const M3 p) {
   extern __shared__ float smem[];
-  const int b = blockIdx.x / p.nseg, seg = blockIdx.x % p.nseg;
-  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const Blk k = blk(p);
+  const int b = k.b, seg = k.seg, hc = k.hc;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int H = (int)p.H, NA = p.NA;
   const int64_t t0 = (int64_t)seg * kSeg;
   const int nt = (int)min((int64_t)kSeg, p.T - t0);
   float* sA = smem;              // [kSeg][NA]
-  float* sDT = smem + kSeg * NA;  // [kSeg][H]
+  float* sDT = smem + kSeg * NA;  // [kSeg][hc]
   for (int idx = threadIdx.x; idx < nt * NA; idx += blockDim.x)
     sA[idx] = ldv<float>(p.ang.row<TI>(b, t0 + idx / NA, 0) + idx % NA);
-  for (int idx = threadIdx.x; idx < nt * H; idx += blockDim.x) {
-    const int t = idx / H, hh = idx % H;
+  for (int idx = threadIdx.x; idx < nt * hc; idx += blockDim.x) {
+    const int t = idx / hc, hh = k.h0 + idx % hc;
     sDT[idx] = softplus20(ldv<float>(p.dd_dt.row<TI>(b, t0 + t, hh)) + p.dt_bias[hh]);
   }
   __syncthreads();
-  if (lane < NA) {
+  if (w < hc && lane < NA) {
     float acc = 0.f;
-    for (int t = 0; t < nt; ++t) acc += sDT[t * H + h] * sA[t * NA + lane];
-    p.segsum[((b * H + h) * p.nseg + seg) * NA + lane] = acc;
+    for (int t = 0; t < nt; ++t) acc += sDT[t * hc + w] * sA[t * NA + lane];
+    p.segsum[((b * H + k.h0 + w) * p.nseg + seg) * NA + lane] = acc;
   }
 }
 
-// q, k (into k_ext rows t+1), xp, adt, gamma, beta and theta for one segment of one batch
+// q, k (into k_ext rows t+1), xp, adt, gamma, beta and theta for one segment of one batch, the
+// heads of one group
 template <typename TI, typename TO>
 __global__ void __launch_bounds__(1024) m3_prologue_fwd_kernel(const M3 p) {
   extern __shared__ float smem[];
-  const int b = blockIdx.x / p.nseg, seg = blockIdx.x % p.nseg;
-  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const Blk k = blk(p);
+  const int b = k.b, seg = k.seg, hc = k.hc;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, h = k.h0 + w;
   const int NA = p.NA, N = (int)p.N, P = (int)p.P, H = (int)p.H;
   const int64_t t0 = (int64_t)seg * kSeg;
   const int nt = (int)min((int64_t)kSeg, p.T - t0);
-  FwdSeg S(smem, N, NA, H);
+  FwdSeg S(smem, N, NA);
   // per (token, head) discretisation: scan scalars out, DT kept for theta
-  for (int idx = threadIdx.x; idx < nt * H; idx += blockDim.x) {
-    const int t = idx / H, hh = idx % H;
+  for (int idx = threadIdx.x; idx < nt * hc; idx += blockDim.x) {
+    const int t = idx / hc, hl = idx % hc, hh = k.h0 + hl;
     const Disc d = discretise(ldv<float>(p.dd_dt.row<TI>(b, t0 + t, hh)), ldv<float>(p.dd_A.row<TI>(b, t0 + t, hh)),
                               ldv<float>(p.trap.row<TI>(b, t0 + t, hh)), p.dt_bias[hh], p.A_floor);
     const int64_t bth = (b * p.T + t0 + t) * H + hh;
     p.adt[bth] = d.adt;
     p.gamma[bth] = d.gamma;
     p.beta[bth] = d.beta;
-    S.dt[t * H + hh] = d.DT;
+    S.dt[t * hc + hl] = d.DT;
   }
   stage_rows<TI>(p, b, t0, nt, S.c, S.bm, S.ang, nullptr);  // rows scaled by their RMSNorm factor
   TO* __restrict__ q = static_cast<TO*>(p.q);
   TO* __restrict__ kx = static_cast<TO*>(p.k_ext);
   const int64_t HN = (int64_t)H * N;
   const Feat f = feat(lane, NA);
-  if (f.on) {
+  if (w < hc && f.on) {
     float th = 0.f;  // theta at the end of the previous segment
     for (int s = 0; s < seg; ++s) th += p.segsum[((b * H + h) * p.nseg + s) * NA + lane];
     float wc[4], wb[4], cb[4], bb[4];
@@ -306,7 +298,7 @@ __global__ void __launch_bounds__(1024) m3_prologue_fwd_kernel(const M3 p) {
       st4(kx + (int64_t)b * (p.T + 1) * HN + h * N, f, zero);
     }
     for (int t = 0; t < nt; ++t) {
-      th += S.dt[t * H + h] * S.ang[t * NA + lane];  // theta = cumsum_t(DT ang) (mamba3.py:111)
+      th += S.dt[t * hc + w] * S.ang[t * NA + lane];  // theta = cumsum_t(DT ang) (mamba3.py:111)
       const int64_t bth = (b * p.T + t0 + t) * H + h;
       p.theta[bth * NA + lane] = th;
       float sn, cs;
@@ -321,21 +313,21 @@ __global__ void __launch_bounds__(1024) m3_prologue_fwd_kernel(const M3 p) {
       st4(kx + (b * (p.T + 1) + t0 + t + 1) * HN + h * N, f, o);
     }
   }
-  // xp = x one token later (mamba3.py:115), all threads over (token, head, feature)
+  // xp = x one token later (mamba3.py:115), all threads over (token, group head, feature)
   TO* __restrict__ xp = static_cast<TO*>(p.xp);
-  const int HP = H * P;
+  const int HP = H * P, GP = hc * P;
   if (p.vec8) {
-    const int HP8 = HP / 8, P8 = P / 8;
-    for (int idx = threadIdx.x; idx < nt * HP8; idx += blockDim.x) {
-      const int t = idx / HP8, r8 = idx % HP8, hh = r8 / P8, pp = (r8 % P8) * 8;
+    const int GP8 = GP / 8, P8 = P / 8;
+    for (int idx = threadIdx.x; idx < nt * GP8; idx += blockDim.x) {
+      const int t = idx / GP8, r8 = idx % GP8, hh = k.h0 + r8 / P8, pp = (r8 % P8) * 8;
       const int64_t tt = t0 + t;
       float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       if (tt > 0) Vec8<TI>::ld(p.x.row<TI>(b, tt - 1, hh) + pp, v);
       Vec8<TO>::st(xp + (b * p.T + tt) * HP + hh * P + pp, v);
     }
   } else {
-    for (int idx = threadIdx.x; idx < nt * HP; idx += blockDim.x) {
-      const int t = idx / HP, r = idx % HP, hh = r / P, pp = r % P;
+    for (int idx = threadIdx.x; idx < nt * GP; idx += blockDim.x) {
+      const int t = idx / GP, r = k.h0 * P + idx % GP, hh = r / P, pp = r % P;
       const int64_t tt = t0 + t;
       stv<float>(xp + (b * p.T + tt) * HP + r, tt > 0 ? ldv<float>(p.x.row<TI>(b, tt - 1, hh) + pp) : 0.f);
     }
@@ -440,13 +432,10 @@ __global__ void __launch_bounds__(256) m3_dx_kernel(const M3 p) {
   }
 }
 
-// RMSNorm backward of one token (mamba3.py:13-15), given the per-head gradients of its
-// normalised output staged in src [H][N]: they are summed in head order (u = x r w + bias_h for
-// every head h), then dx = r w du - x r^3 / N sum(du w x); dw accumulates du x r.  Lanes past
-// the RoPE angles hold zeros, so the warp-wide sum sees every lane.
-__device__ __forceinline__ void rms_bwd_token(const float* src, int H, int N, Feat f, const float (&xv)[4],
-                                              const float (&wv)[4], float rr, float (&gw)[4], float (&gx)[4]) {
-  float du[4] = {0.f, 0.f, 0.f, 0.f};
+// the lane's four features of the per-head rows src [H][N], summed in head order
+__device__ __forceinline__ void sum_heads(const float* src, int H, int N, Feat f, float (&du)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) du[j] = 0.f;
   if (f.on)
 #pragma unroll 4
     for (int hh = 0; hh < H; ++hh) {
@@ -455,6 +444,14 @@ __device__ __forceinline__ void rms_bwd_token(const float* src, int H, int N, Fe
 #pragma unroll
       for (int j = 0; j < 4; ++j) du[j] += v[j];
     }
+}
+
+// RMSNorm backward of one token (mamba3.py:13-15), given du, the gradient of its normalised
+// output summed over heads (u = x r w + bias_h for every head h): dx = r w du - x r^3 / N
+// sum(du w x); dw accumulates du x r.  Lanes past the RoPE angles hold zeros, so the warp-wide sum
+// sees every lane.
+__device__ __forceinline__ void rms_bwd_du(const float (&du)[4], int N, const float (&xv)[4], const float (&wv)[4],
+                                           float rr, float (&gw)[4], float (&gx)[4]) {
   float dl = 0.f;
 #pragma unroll
   for (int j = 0; j < 4; ++j) dl += du[j] * wv[j] * xv[j];
@@ -509,25 +506,36 @@ __device__ __forceinline__ void slot4(const unsigned char* row, Feat f, float (&
 // ang gradient part) through shared memory.  Warps 0..H-1 own a head each and load their next
 // token's rows one step ahead; warps H, H+1, H+2 only reduce over heads (C rows, B rows, angles),
 // one token behind the head warps, so the two kinds of work overlap.
-template <typename TI, typename TO, int kRing>  // kRing: ring slots (tokens in flight) per head warp
+// kRing: ring slots (tokens in flight) per head warp; kGrouped: several head groups (p.nhg > 1)
+template <typename TI, typename TO, int kRing, bool kGrouped>
 __global__ void __launch_bounds__(1024) m3_prologue_bwd_kernel(const M3 p) {
   extern __shared__ float smem[];
-  const int b = blockIdx.x / p.nseg, seg = blockIdx.x % p.nseg;
-  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int NA = p.NA, N = (int)p.N, H = (int)p.H;
+  Blk k;
+  if (kGrouped) {
+    k = blk(p);
+  } else {  // one group: blockIdx.x = b nseg + seg
+    k.b = blockIdx.x / p.nseg;
+    k.seg = blockIdx.x % p.nseg;
+    k.g = 0;
+    k.h0 = 0;
+    k.hc = H;
+  }
+  const int b = k.b, seg = k.seg, hc = k.hc;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, h = k.h0 + w;  // h: global head of a head warp
   const int64_t t0 = (int64_t)seg * kSeg;
   const int nt = (int)min((int64_t)kSeg, p.T - t0);
-  // shared: C rows, B rows, angles, RMSNorm factors [kSeg][2], DT [kSeg][H], then two staging
-  // buffers of (dvq, dvk: H x N; DT * theta-gradient: H x NA)
+  // shared: C rows, B rows, angles, RMSNorm factors [kSeg][2], DT [kSeg][hc], then two staging
+  // buffers of (dvq, dvk: hc x N; DT * theta-gradient: hc x NA)
   float* sC = smem;
   float* sB = sC + kSeg * N;
   float* sA = sB + kSeg * N;
   float* sR = sA + kSeg * NA;
   float* sDT = sR + 2 * kSeg;
-  float* stage = sDT + kSeg * H;
-  const int buf_floats = H * (2 * N + NA);
-  for (int idx = threadIdx.x; idx < nt * H; idx += blockDim.x) {
-    const int t = idx / H, hh = idx % H;
+  float* stage = sDT + kSeg * hc;
+  const int buf_floats = hc * (2 * N + NA);
+  for (int idx = threadIdx.x; idx < nt * hc; idx += blockDim.x) {
+    const int t = idx / hc, hh = k.h0 + idx % hc;
     sDT[idx] = softplus20(ldv<float>(p.dd_dt.row<TI>(b, t0 + t, hh)) + p.dt_bias[hh]);
   }
   stage_rows<TI>(p, b, t0, nt, sC, sB, sA, sR);
@@ -536,24 +544,25 @@ __global__ void __launch_bounds__(1024) m3_prologue_bwd_kernel(const M3 p) {
   if (f.on) {
     ldp4(p.C_norm_w, f, wc);
     ldp4(p.B_norm_w, f, wb);
-    if (h < H) {
+    if (w < hc) {
       ldp4(p.C_bias + h * N, f, cb);
       ldp4(p.B_bias + h * N, f, bb);
     }
   }
-  const int64_t HN = (int64_t)H * N;
+  const int64_t HN = (int64_t)H * N, GN = (int64_t)hc * N;
   const TO* __restrict__ dq = static_cast<const TO*>(p.dq);
   const TO* __restrict__ dk = static_cast<const TO*>(p.dk);
   const TO* __restrict__ dkp = static_cast<const TO*>(p.dkp);
-  // reduction roles on the R = min(3, 32 - H) warps after the heads (H <= 31)
-  const int R = (int)(blockDim.x >> 5) - H;
-  const bool head = h < H;
-  const bool wC = (h == H), wB = (h == H + (R >= 2 ? 1 : 0)), wA = (h == H + (R >= 3 ? 2 : R - 1));
+  // reduction roles on the R = min(3, 32 - hc) warps after the group's heads
+  const int R = (int)(blockDim.x >> 5) - hc;
+  const bool head = w < hc;
+  const bool wC = (w == hc), wB = (w == hc + (R >= 2 ? 1 : 0)), wA = (w == hc + (R >= 3 ? 2 : R - 1));
+  // several groups: the sums over the group's heads go to global memory, m3_rms_bwd_kernel finishes
   float gcb[4] = {}, gbb[4] = {}, gwc[4] = {}, gwb[4] = {};
   float sfx = 0.f;  // theta gradient summed over this segment's tokens >= t
   // the per-warp row ring: kRing slots of (3 rows of N elements + NA theta floats)
   const int slotB = 3 * N * (int)sizeof(TO) + NA * 4;
-  unsigned char* ring = reinterpret_cast<unsigned char*>(stage + 2 * buf_floats) + (size_t)h * kRing * slotB;
+  unsigned char* ring = reinterpret_cast<unsigned char*>(stage + 2 * buf_floats) + (size_t)w * kRing * slotB;
   if (head)  // prefill: tokens nt-1 .. nt-kRing+1
     for (int k = 0; k < kRing - 1; ++k) {
       if (nt - 1 - k >= 0) ring_issue(p, dq, dk, dkp, b, t0 + nt - 1 - k, h, ring + (size_t)k * slotB, lane);
@@ -602,13 +611,13 @@ __global__ void __launch_bounds__(1024) m3_prologue_bwd_kernel(const M3 p) {
         gcb[j] += dvq[j];
         gbb[j] += dvk[j];
       }
-      float* bq = buf + h * N;
-      float* bk = buf + HN + h * N;
+      float* bq = buf + w * N;
+      float* bk = buf + GN + w * N;
       *reinterpret_cast<float2*>(bq + f.f0) = make_float2(dvq[0], dvq[1]);
       *reinterpret_cast<float2*>(bq + f.f2) = make_float2(dvq[2], dvq[3]);
       *reinterpret_cast<float2*>(bk + f.f0) = make_float2(dvk[0], dvk[1]);
       *reinterpret_cast<float2*>(bk + f.f2) = make_float2(dvk[2], dvk[3]);
-      buf[2 * HN + h * NA + lane] = sDT[t * H + h] * sfx;
+      buf[2 * GN + w * NA + lane] = sDT[t * hc + w] * sfx;
     }
     part = warp_sum(part);
     if (lane == 0) p.dDTl[bth] = part;
@@ -616,22 +625,33 @@ __global__ void __launch_bounds__(1024) m3_prologue_bwd_kernel(const M3 p) {
       // per-token sums over heads in head order, then the RMSNorm backward of Cm / Bm
       const int t = nt - step;  // the token the head warps staged at step - 1
       const float* buf = stage + ((step - 1) & 1) * buf_floats;
+      const int64_t gbt = ((int64_t)k.g * p.B + b) * p.T + t0 + t;  // (group, batch, token) row
       if (wC) {
-        float x4[4] = {}, gx[4];
-        if (f.on) ldp4(sC + t * N, f, x4);
-        rms_bwd_token(buf, H, N, f, x4, wc, sR[2 * t], gwc, gx);
-        if (f.on) st4(p.dCm.wrow<TI>(b, t0 + t, 0), f, gx, p.pairs);
+        float du[4], x4[4] = {}, gx[4];
+        sum_heads(buf, hc, N, f, du);
+        if (kGrouped) {
+          if (f.on) st4(p.duC + gbt * N, f, du);
+        } else {
+          if (f.on) ldp4(sC + t * N, f, x4);
+          rms_bwd_du(du, N, x4, wc, sR[2 * t], gwc, gx);
+          if (f.on) st4(p.dCm.wrow<TI>(b, t0 + t, 0), f, gx, p.pairs);
+        }
       }
       if (wB) {
-        float x4[4] = {}, gx[4];
-        if (f.on) ldp4(sB + t * N, f, x4);
-        rms_bwd_token(buf + HN, H, N, f, x4, wb, sR[2 * t + 1], gwb, gx);
-        if (f.on) st4(p.dBm.wrow<TI>(b, t0 + t, 0), f, gx, p.pairs);
+        float du[4], x4[4] = {}, gx[4];
+        sum_heads(buf + GN, hc, N, f, du);
+        if (kGrouped) {
+          if (f.on) st4(p.duB + gbt * N, f, du);
+        } else {
+          if (f.on) ldp4(sB + t * N, f, x4);
+          rms_bwd_du(du, N, x4, wb, sR[2 * t + 1], gwb, gx);
+          if (f.on) st4(p.dBm.wrow<TI>(b, t0 + t, 0), f, gx, p.pairs);
+        }
       }
       if (wA && lane < NA) {
         float s = 0.f;
-        for (int hh = 0; hh < H; ++hh) s += buf[2 * HN + hh * NA + lane];
-        p.dangl[(b * p.T + t0 + t) * NA + lane] = s;
+        for (int hh = 0; hh < hc; ++hh) s += buf[2 * GN + hh * NA + lane];
+        p.dangl[gbt * NA + lane] = s;
       }
     }
     __syncthreads();
@@ -646,6 +666,7 @@ __global__ void __launch_bounds__(1024) m3_prologue_bwd_kernel(const M3 p) {
     pC[f.f0] = gcb[0]; pC[f.f0 + 1] = gcb[1]; pC[f.f2] = gcb[2]; pC[f.f2 + 1] = gcb[3];
   }
   const int64_t pn = (int64_t)(b * p.nseg + seg) * N;
+  if (kGrouped) return;  // the norm-weight partials come from m3_rms_bwd_kernel
   if (wB && f.on) {
     float* o = p.pnorm + pn;
     o[f.f0] = gwb[0]; o[f.f0 + 1] = gwb[1]; o[f.f2] = gwb[2]; o[f.f2 + 1] = gwb[3];
@@ -656,6 +677,70 @@ __global__ void __launch_bounds__(1024) m3_prologue_bwd_kernel(const M3 p) {
   }
 }
 
+// Several head groups: the C / B row gradients summed over the groups in group order, then the
+// RMSNorm backward per token (one warp per token) and the norm-weight partial sums of the segment
+// (per warp, then over the warps in order).
+template <typename TI>
+__global__ void __launch_bounds__(256) m3_rms_bwd_kernel(const M3 p) {
+  __shared__ float sw[2][8][128];  // [B, C][warp][feature]
+  const int b = blockIdx.x / p.nseg, seg = blockIdx.x % p.nseg;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int N = (int)p.N, NA = p.NA;
+  const int64_t t0 = (int64_t)seg * kSeg;
+  const int nt = (int)min((int64_t)kSeg, p.T - t0);
+  const int64_t gstride = p.B * p.T * N;
+  const Feat f = feat(lane, NA);
+  float wc[4] = {}, wb[4] = {};
+  if (f.on) {
+    ldp4(p.C_norm_w, f, wc);
+    ldp4(p.B_norm_w, f, wb);
+  }
+  float gwc[4] = {}, gwb[4] = {};
+  for (int t = w; t < nt; t += 8) {
+    const int64_t tt = t0 + t, row = (b * p.T + tt) * N;
+    float c4[4] = {}, b4[4] = {}, duc[4] = {}, dub[4] = {};
+    if (f.on) {
+      ld4(p.Cm.row<TI>(b, tt, 0), f, c4, p.pairs);
+      ld4(p.Bm.row<TI>(b, tt, 0), f, b4, p.pairs);
+      for (int g = 0; g < p.nhg; ++g) {
+        float v[4];
+        ldp4(p.duC + g * gstride + row, f, v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) duc[j] += v[j];
+        ldp4(p.duB + g * gstride + row, f, v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) dub[j] += v[j];
+      }
+    }
+    float sc = 0.f, sb = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      sc += c4[j] * c4[j];
+      sb += b4[j] * b4[j];
+    }
+    sc = warp_sum(sc);
+    sb = warp_sum(sb);
+    const float rc = rsqrtf(sc / N + p.eps), rb = rsqrtf(sb / N + p.eps);
+    float gx[4];
+    rms_bwd_du(duc, N, c4, wc, rc, gwc, gx);
+    if (f.on) st4(p.dCm.wrow<TI>(b, tt, 0), f, gx, p.pairs);
+    rms_bwd_du(dub, N, b4, wb, rb, gwb, gx);
+    if (f.on) st4(p.dBm.wrow<TI>(b, tt, 0), f, gx, p.pairs);
+  }
+  if (f.on) {
+    st4(&sw[0][w][0], f, gwb);
+    st4(&sw[1][w][0], f, gwc);
+  }
+  __syncthreads();
+  const int64_t pn = (int64_t)(b * p.nseg + seg) * N;
+  for (int i = threadIdx.x; i < 2 * N; i += blockDim.x) {
+    const int part = i / N, n = i % N;
+    float s = 0.f;
+    for (int k = 0; k < 8; ++k) s += sw[part][k][n];
+    p.pnorm[part * p.B * p.nseg * N + pn + n] = s;
+  }
+}
+
 // The theta-gradient carry from later segments, then the discretisation backward per (token,
 // head) (mamba3.py:105-111) and the ang gradient.  Thread tid keeps head tid % H (blockDim is a
 // multiple of H), so its dt_bias partial sum has a fixed head.
@@ -663,7 +748,6 @@ template <typename TI>
 __global__ void __launch_bounds__(1024) m3_scalars_bwd_kernel(const M3 p) {
   extern __shared__ float smem[];  // sA [kSeg][NA] | sC [H][NA] | sDT [kSeg][H] | sacc [blockDim]
   const int b = blockIdx.x / p.nseg, seg = blockIdx.x % p.nseg;
-  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int NA = p.NA, H = (int)p.H;
   const int64_t t0 = (int64_t)seg * kSeg;
   const int nt = (int)min((int64_t)kSeg, p.T - t0);
@@ -671,10 +755,11 @@ __global__ void __launch_bounds__(1024) m3_scalars_bwd_kernel(const M3 p) {
   float* sC = sA + kSeg * NA;
   float* sDT = sC + H * NA;
   float* sacc = sDT + kSeg * H;
-  if (lane < NA) {  // theta gradient summed over all later tokens (later segments)
+  for (int idx = threadIdx.x; idx < H * NA; idx += blockDim.x) {  // theta gradient over all later segments
+    const int hh = idx / NA, i = idx % NA;
     float C = 0.f;
-    for (int s = seg + 1; s < p.nseg; ++s) C += p.segsum[((b * H + h) * p.nseg + s) * NA + lane];
-    sC[h * NA + lane] = C;
+    for (int s = seg + 1; s < p.nseg; ++s) C += p.segsum[((b * H + hh) * p.nseg + s) * NA + i];
+    sC[idx] = C;
   }
   for (int idx = threadIdx.x; idx < nt * NA; idx += blockDim.x)
     sA[idx] = ldv<float>(p.ang.row<TI>(b, t0 + idx / NA, 0) + idx % NA);
@@ -711,10 +796,12 @@ __global__ void __launch_bounds__(1024) m3_scalars_bwd_kernel(const M3 p) {
     for (int k = hh; k < (int)blockDim.x; k += H) s += sacc[k];
     p.pdt[(b * p.nseg + seg) * H + hh] = s;
   }
-  // ang gradient: the within-segment part plus sum_h DT[t][h] * carry[h][i]
+  // ang gradient: the within-segment part (per head group) plus sum_h DT[t][h] * carry[h][i]
+  const int64_t gstride = p.B * p.T * NA;
   for (int idx = threadIdx.x; idx < nt * NA; idx += blockDim.x) {
     const int t = idx / NA, i = idx % NA;
     float s = p.dangl[(b * p.T + t0 + t) * NA + i];
+    for (int g = 1; g < p.nhg; ++g) s += p.dangl[g * gstride + (b * p.T + t0 + t) * NA + i];
     for (int hh = 0; hh < H; ++hh) s += sDT[t * H + hh] * sC[hh * NA + i];
     stv<float>(p.dang.wrow<TI>(b, t0 + t, 0) + i, s);
   }
@@ -867,11 +954,20 @@ __global__ void m3_param_reduce_kernel(const M3 p) {
 
 View view_of(const zb_view& v) { return View{v.ptr, v.sb, v.st, v.sh}; }
 
+// head groups: up to 31 heads in one group; more heads split evenly into groups of at most 28
+void head_groups(int64_t H, int* hg, int* nhg) {
+  *nhg = H <= 31 ? 1 : (int)((H + 27) / 28);
+  *hg = (int)((H + *nhg - 1) / *nhg);
+}
+
 struct WsLayout {
-  size_t segsum, dDTl, dangl, pbias, pnorm, pdt, pD, total;
+  size_t segsum, dDTl, dangl, duC, duB, pbias, pnorm, pdt, pD, total;
 };
 WsLayout ws_layout(const zb_m3_args* a) {
   const int64_t nseg = (a->T + kSeg - 1) / kSeg, NA = a->N / 4;
+  int hg, nhg;
+  head_groups(a->H, &hg, &nhg);
+  const size_t ng = nhg > 1 ? (size_t)nhg : 0;
   WsLayout L;
   size_t off = 0;
   auto take = [&](size_t floats) {
@@ -881,7 +977,9 @@ WsLayout ws_layout(const zb_m3_args* a) {
   };
   L.segsum = take((size_t)a->B * a->H * nseg * NA);
   L.dDTl = take((size_t)a->B * a->T * a->H);
-  L.dangl = take((size_t)a->B * a->T * NA);
+  L.dangl = take((size_t)nhg * a->B * a->T * NA);
+  L.duC = take(ng * a->B * a->T * a->N);
+  L.duB = take(ng * a->B * a->T * a->N);
   L.pbias = take((size_t)2 * a->B * nseg * a->H * a->N);
   L.pnorm = take((size_t)2 * a->B * nseg * a->N);
   L.pdt = take((size_t)a->B * nseg * a->H);
@@ -893,7 +991,7 @@ WsLayout ws_layout(const zb_m3_args* a) {
 int check(const zb_m3_args* a) {
   if (!a) return ZB_ERR_LAYOUT;
   if (a->B <= 0 || a->T <= 0 || a->H <= 0 || a->P <= 0 || a->N <= 0) return ZB_ERR_SHAPE;
-  if (a->H > 31 || a->N % 16 != 0 || a->N > 128 || a->P > 256) return ZB_ERR_UNSUPPORTED;
+  if (a->H > 128 || a->H * a->P > 8192 || a->N % 16 != 0 || a->N > 128 || a->P > 256) return ZB_ERR_UNSUPPORTED;
   if ((double)a->B * (double)(a->T + 1) * (double)a->H * (double)(a->N > a->P ? a->N : a->P) > 9.0e15)
     return ZB_ERR_SHAPE;
   if ((a->io_dtype != ZB_F32 && a->io_dtype != ZB_BF16) || (a->op_dtype != ZB_F32 && a->op_dtype != ZB_BF16))
@@ -928,6 +1026,7 @@ M3 make_m3(const zb_m3_args* a) {
   p.B = a->B; p.T = a->T; p.H = a->H; p.P = a->P; p.N = a->N;
   p.NA = (int)(a->N / 4);
   p.nseg = (int)((a->T + kSeg - 1) / kSeg);
+  head_groups(a->H, &p.hg, &p.nhg);
   p.A_floor = a->A_floor; p.eps = a->eps;
   p.x = view_of(a->x); p.z = view_of(a->z); p.Bm = view_of(a->Bm); p.Cm = view_of(a->Cm);
   p.dd_dt = view_of(a->dd_dt); p.dd_A = view_of(a->dd_A); p.trap = view_of(a->trap); p.ang = view_of(a->ang);
@@ -947,6 +1046,8 @@ M3 make_m3(const zb_m3_args* a) {
   p.segsum = reinterpret_cast<float*>(ws + L.segsum);
   p.dDTl = reinterpret_cast<float*>(ws + L.dDTl);
   p.dangl = reinterpret_cast<float*>(ws + L.dangl);
+  p.duC = reinterpret_cast<float*>(ws + L.duC);
+  p.duB = reinterpret_cast<float*>(ws + L.duB);
   p.pbias = reinterpret_cast<float*>(ws + L.pbias);
   p.pnorm = reinterpret_cast<float*>(ws + L.pnorm);
   p.pdt = reinterpret_cast<float*>(ws + L.pdt);
@@ -983,9 +1084,9 @@ extern "C" ZB_API int zb_m3_prologue_fwd(const zb_m3_args* a, void* stream) {
     return ZB_ERR_LAYOUT;
   const M3 p = make_m3(a);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const dim3 grid((unsigned)(p.B * p.nseg)), block((unsigned)(32 * p.H));
-  const int smem0 = (int)(kSeg * (p.NA + p.H) * sizeof(float));
-  const int smem1 = (int)(kSeg * (2 * p.N + p.NA + p.H) * sizeof(float));
+  const dim3 grid((unsigned)(p.B * p.nseg * p.nhg)), block((unsigned)(32 * p.hg));
+  const int smem0 = (int)(kSeg * (p.NA + p.hg) * sizeof(float));
+  const int smem1 = (int)(kSeg * (2 * p.N + p.NA + p.hg) * sizeof(float));
   ZB_M3_DISPATCH(a->io_dtype, a->op_dtype, {
     auto k1 = m3_prologue_fwd_kernel<TI, TO>;
     if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1) != cudaSuccess) return ZB_ERR_CUDA;
@@ -1035,30 +1136,37 @@ extern "C" ZB_API int zb_m3_prologue_bwd(const zb_m3_args* a, void* stream) {
     return ZB_ERR_LAYOUT;
   const M3 p = make_m3(a);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const dim3 grid((unsigned)(p.B * p.nseg)), block((unsigned)(32 * p.H));
-  // staged rows (C, B: N each; angles; RMSNorm factors; DT per head) for kSeg tokens, then two
-  // staging buffers of (dvq, dvk: H x N; DT * theta-gradient: H x NA)
+  const dim3 grid((unsigned)(p.B * p.nseg)), ggrid((unsigned)(p.B * p.nseg * p.nhg));
+  // staged rows (C, B: N each; angles; RMSNorm factors; DT per group head) for kSeg tokens, then
+  // two staging buffers of (dvq, dvk: hg x N; DT * theta-gradient: hg x NA)
   // plus the per-warp row rings: as many slots (4, 2 or 1) as shared memory allows
   const int op_es = a->op_dtype == ZB_F32 ? 4 : 2;
-  const size_t base1 = (kSeg * (2 * p.N + p.NA + 2 + p.H) + 2 * (p.H * (2 * p.N + p.NA))) * sizeof(float);
-  const size_t ring1 = (size_t)p.H * (3 * p.N * op_es + p.NA * 4);
+  const size_t base1 = (kSeg * (2 * p.N + p.NA + 2 + p.hg) + 2 * (p.hg * (2 * p.N + p.NA))) * sizeof(float);
+  const size_t ring1 = (size_t)p.hg * (3 * p.N * op_es + p.NA * 4);
   const size_t kMaxSmem = 227 * 1024;
   const int ring = base1 + 4 * ring1 <= kMaxSmem ? 4 : base1 + 2 * ring1 <= kMaxSmem ? 2 : 1;
   const int smem1 = (int)(base1 + ring * ring1);
   if ((size_t)smem1 > kMaxSmem) return ZB_ERR_UNSUPPORTED;
-  const int smem2 = (int)((kSeg * p.NA + p.H * p.NA + kSeg * p.H + 32 * p.H) * sizeof(float));
+  // scalars kernel: thread tid keeps head tid % H, so blockDim is a multiple of H
+  const int sthreads = (int)(p.H * (p.H <= 32 ? 32 : 1024 / p.H));
+  const int smem2 = (int)((kSeg * p.NA + p.H * p.NA + kSeg * p.H + sthreads) * sizeof(float));
   ZB_M3_DISPATCH(a->io_dtype, a->op_dtype, {
-    auto k1 = ring == 4 ? m3_prologue_bwd_kernel<TI, TO, 4>
-              : ring == 2 ? m3_prologue_bwd_kernel<TI, TO, 2> : m3_prologue_bwd_kernel<TI, TO, 1>;
+    auto k1 = p.nhg > 1 ? (ring == 4   ? m3_prologue_bwd_kernel<TI, TO, 4, true>
+                           : ring == 2 ? m3_prologue_bwd_kernel<TI, TO, 2, true>
+                                       : m3_prologue_bwd_kernel<TI, TO, 1, true>)
+                        : (ring == 4   ? m3_prologue_bwd_kernel<TI, TO, 4, false>
+                           : ring == 2 ? m3_prologue_bwd_kernel<TI, TO, 2, false>
+                                       : m3_prologue_bwd_kernel<TI, TO, 1, false>);
     if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1) != cudaSuccess) return ZB_ERR_CUDA;
     if (p.vec8) {
       const unsigned slots = (unsigned)(p.H * p.P / 8), vthreads = slots * (slots >= 256 ? 1024 / slots : 4);
       m3_dx_vec_kernel<TI, TO><<<grid, vthreads, 0, s>>>(p);
     }
     else m3_dx_kernel<TI, TO><<<grid, 256, 0, s>>>(p);
-    k1<<<grid, (unsigned)(32 * (p.H + (p.H <= 29 ? 3 : 32 - p.H))), smem1, s>>>(p);  // heads + reduction warps
-    m3_scalars_bwd_kernel<TI><<<grid, block, smem2, s>>>(p);
+    k1<<<ggrid, (unsigned)(32 * (p.hg + (p.hg <= 29 ? 3 : 32 - p.hg))), smem1, s>>>(p);  // heads + reduction warps
+    if (p.nhg > 1) m3_rms_bwd_kernel<TI><<<grid, 256, 0, s>>>(p);
+    m3_scalars_bwd_kernel<TI><<<grid, (unsigned)sthreads, smem2, s>>>(p);
   });
   m3_param_reduce_kernel<<<64, 256, 0, s>>>(p);
-  return finish(4);
+  return finish(p.nhg > 1 ? 5 : 4);
 }

@@ -1,0 +1,414 @@
+"""The Mamba-3 language model on the B200 kernels: a drop-in for the reference's looped causal LM
+``ZenithForCausalLM`` (zenith/model.py:42-99) and its training step (zenith/train.py:99-111).
+
+Same modules, parameter names and shapes as the reference (a reference ``state_dict`` loads as
+it is), same forward semantics: embedding, input layers, ``loops`` passes of the shared
+recurrent block of which only the last is tracked by autograd, output layers, final norm, tied
+LM head, next-token cross-entropy.  What runs where:
+
+- the residual add and the RMSNorm that reads it, forward and backward: ``zb_rmsnorm_fwd`` /
+  ``zb_rmsnorm_bwd`` (one pass each; the layer output is added into the residual stream as it is
+  normalised for the next layer);
+- the Mamba-3 layer body between in_proj and out_proj: ``mamba3_layer_packed`` (prologue, the
+  tcgen05 SSD scan, epilogue), reading the packed in_proj output and writing its gradient as one
+  tensor;
+- in_proj / out_proj / LM head GEMMs: cuBLAS through torch (bf16 under autocast, as the
+  reference's ``train.py`` runs them);
+- the next-token cross-entropy: ``zb_xent`` computes each row's loss and overwrites the logits
+  with their gradient in the same pass, so no float32 logits or softmax are ever stored.
+
+``train_step`` is one optimiser step (autocast forward, backward, gradient clipping, AdamW),
+with the gradient all-reduce of ``DistributedDataParallel`` over NCCL when the model is wrapped.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import dataclasses
+import math
+from contextlib import nullcontext
+from typing import NamedTuple, Optional
+
+import torch
+import torch.nn as nn
+from torch import Tensor
+
+from . import _lib as L
+from .mamba3 import mamba3_layer_packed
+
+
+# ---------------------------------------------------------------------------------------------
+# C ABI (include/zb_lm.h)
+
+class NormArgs(ctypes.Structure):
+    """ctypes mirror of ``zb_rmsnorm_args``."""
+
+    _fields_ = (
+        [("M", ctypes.c_int64), ("D", ctypes.c_int64), ("eps", ctypes.c_float)]
+        + [(n, ctypes.c_int32) for n in ("x_dtype", "b_dtype", "u_dtype")]
+        + [(n, ctypes.c_void_p) for n in ("a", "b", "s", "w", "u", "r", "du", "ds", "dsum", "dsum_b", "dw",
+                                          "workspace")]
+        + [("workspace_bytes", ctypes.c_uint64)]
+    )
+
+
+class XentArgs(ctypes.Structure):
+    """ctypes mirror of ``zb_xent_args``."""
+
+    _fields_ = [("M", ctypes.c_int64), ("V", ctypes.c_int64), ("ld", ctypes.c_int64), ("dtype", ctypes.c_int32),
+                ("write_grad", ctypes.c_int32), ("ignore_index", ctypes.c_int64), ("logits", ctypes.c_void_p),
+                ("labels", ctypes.c_void_p), ("loss", ctypes.c_void_p), ("lse", ctypes.c_void_p),
+                ("status", ctypes.c_void_p)]
+
+
+def _lib():
+    lib = L.lib()
+    if not getattr(lib, "_lm_typed", False):
+        lib.zb_rmsnorm_workspace_bytes.restype = ctypes.c_uint64
+        lib.zb_rmsnorm_workspace_bytes.argtypes = [ctypes.POINTER(NormArgs)]
+        for fn in ("zb_rmsnorm_fwd", "zb_rmsnorm_bwd"):
+            getattr(lib, fn).restype = ctypes.c_int
+            getattr(lib, fn).argtypes = [ctypes.POINTER(NormArgs), ctypes.c_void_p]
+        lib.zb_xent.restype = ctypes.c_int
+        lib.zb_xent.argtypes = [ctypes.POINTER(XentArgs), ctypes.c_void_p]
+        lib._lm_typed = True
+    return lib
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _code(dt: torch.dtype) -> int:
+    if dt not in (torch.float32, torch.bfloat16):
+        raise TypeError(f"zenith_b200.lm: float32 or bfloat16 tensors, not {dt}")
+    return L.DTYPE_CODE[dt]
+
+
+# ---------------------------------------------------------------------------------------------
+# residual add + RMSNorm
+
+class _AddRMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a, b, weight, eps, u_dtype):
+        D = a.shape[-1]
+        M = a.numel() // D
+        dev = a.device
+        w = weight.detach().float().contiguous()
+        s = torch.empty_like(a) if b is not None else None
+        u = torch.empty(a.shape, dtype=u_dtype, device=dev)
+        r = torch.empty(M, dtype=torch.float32, device=dev)
+        args = NormArgs(M=M, D=D, eps=float(eps), x_dtype=_code(a.dtype),
+                        b_dtype=_code(b.dtype if b is not None else a.dtype), u_dtype=_code(u_dtype))
+        args.a, args.b, args.s = a.data_ptr(), L.ptr(b), L.ptr(s)
+        args.w, args.u, args.r = w.data_ptr(), u.data_ptr(), r.data_ptr()
+        L.check(_lib().zb_rmsnorm_fwd(ctypes.byref(args), _stream(dev)), "zb_rmsnorm_fwd")
+        ctx.save_for_backward(s if b is not None else a, w, r)
+        ctx.meta = (float(eps), b.dtype if b is not None else None, weight.dtype)
+        ctx.set_materialize_grads(False)
+        return (s, u) if b is not None else u
+
+    @staticmethod
+    def backward(ctx, *grads):
+        s, w, r = ctx.saved_tensors
+        eps, b_dtype, w_dtype = ctx.meta
+        ds, du = grads if b_dtype is not None else (None, grads[0])
+        D = s.shape[-1]
+        M = s.numel() // D
+        dev = s.device
+        if du is None:
+            du = torch.zeros(s.shape, dtype=s.dtype, device=dev)
+        du = du.contiguous()
+        ds = ds.contiguous() if ds is not None else None
+        dsum = torch.empty_like(s)
+        dsum_b = torch.empty(s.shape, dtype=b_dtype, device=dev) if b_dtype not in (None, s.dtype) else None
+        dw = torch.empty(D, dtype=torch.float32, device=dev)
+        args = NormArgs(M=M, D=D, eps=eps, x_dtype=_code(s.dtype), b_dtype=_code(b_dtype or s.dtype),
+                        u_dtype=_code(du.dtype))
+        args.a, args.w, args.r = s.data_ptr(), w.data_ptr(), r.data_ptr()
+        args.du, args.ds, args.dsum, args.dsum_b, args.dw = du.data_ptr(), L.ptr(ds), dsum.data_ptr(), L.ptr(dsum_b), dw.data_ptr()
+        lib = _lib()
+        nbytes = int(lib.zb_rmsnorm_workspace_bytes(ctypes.byref(args)))
+        ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+        args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
+        L.check(lib.zb_rmsnorm_bwd(ctypes.byref(args), _stream(dev)), "zb_rmsnorm_bwd")
+        if b_dtype is None:
+            return dsum, None, dw.to(w_dtype), None, None
+        return dsum, dsum_b if dsum_b is not None else dsum, dw.to(w_dtype), None, None
+
+
+def add_rmsnorm(a: Tensor, b: Optional[Tensor], weight: Tensor, eps: float = 1e-5,
+                out_dtype: Optional[torch.dtype] = None):
+    """``s = a + b`` and ``u = RMSNorm(s) = s rsqrt(mean(s^2) + eps) w`` (zenith/mamba3.py:8-15)
+    in one pass; returns ``(s, u)``, or ``u`` alone when ``b`` is None.  ``a``: float32 or
+    bfloat16 ``[..., D]``; ``b`` may be the other of the two; ``u`` in ``out_dtype`` (default
+    ``a``'s).  The backward is one pass too and gives ``a`` and ``b`` the same gradient."""
+    a = a.contiguous()
+    b = b.contiguous() if b is not None else None
+    return _AddRMSNorm.apply(a, b, weight, eps, out_dtype or a.dtype)
+
+
+# ---------------------------------------------------------------------------------------------
+# LM head + next-token cross-entropy
+
+class _fp32_reductions:
+    """cuBLAS may reduce split-K partial sums of a bf16 GEMM in bf16 (torch's default); the LM
+    head's GEMMs sum over the vocabulary, so they keep those reductions in fp32."""
+
+    def __enter__(self):
+        self.prev = torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction
+        torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
+
+    def __exit__(self, *exc):
+        torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = self.prev
+
+
+class _LinearCrossEntropy(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, h, weight, labels, ignore_index, compute_dtype):
+        dev = h.device
+        hc = h.to(compute_dtype)
+        wc = weight.to(compute_dtype)
+        with _fp32_reductions():
+            logits = hc @ wc.t()                                 # [M, V] (cuBLAS)
+        M, V = logits.shape
+        loss_rows = torch.empty(M, dtype=torch.float32, device=dev)
+        args = XentArgs(M=M, V=V, ld=logits.stride(0), dtype=_code(logits.dtype), write_grad=1,
+                        ignore_index=int(ignore_index), logits=logits.data_ptr(), labels=labels.data_ptr(),
+                        loss=loss_rows.data_ptr(), lse=None, status=L.status_word(dev).data_ptr())
+        L.check(_lib().zb_xent(ctypes.byref(args), _stream(dev)), "zb_xent")
+        n_valid = (labels != ignore_index).sum().clamp_(min=1).to(torch.float32)
+        ctx.save_for_backward(hc, wc, logits, n_valid)          # logits now hold softmax - onehot
+        ctx.dtypes = (h.dtype, weight.dtype)
+        return loss_rows.sum() / n_valid
+
+    @staticmethod
+    def backward(ctx, gl):
+        hc, wc, g, n_valid = ctx.saved_tensors
+        scale = gl / n_valid
+        with _fp32_reductions():
+            dh = (g @ wc).mul_(scale.to(g.dtype))
+            dw = (g.t() @ hc).mul_(scale.to(g.dtype))
+        return dh.to(ctx.dtypes[0]), dw.to(ctx.dtypes[1]), None, None, None
+
+
+def linear_cross_entropy(h: Tensor, weight: Tensor, labels: Tensor, ignore_index: int = -100,
+                         compute_dtype: Optional[torch.dtype] = None) -> Tensor:
+    """``F.cross_entropy(h @ weight.T, labels)`` (mean over rows whose label is not
+    ``ignore_index``) without storing float32 logits: the logits GEMM runs in ``compute_dtype``
+    (bf16 under CUDA autocast, else h's dtype), then ``zb_xent`` turns each row into its loss and
+    its gradient ``softmax - onehot`` in place; the backward is two GEMMs on that gradient.
+    ``h``: ``[M, d]``; ``weight``: ``[V, d]``; ``labels``: ``[M]`` int64."""
+    if compute_dtype is None:
+        ac = torch.is_autocast_enabled("cuda")
+        compute_dtype = torch.get_autocast_dtype("cuda") if ac else h.dtype
+    labels = labels.contiguous().to(torch.int64)
+    with torch.autocast("cuda", enabled=False):
+        return _LinearCrossEntropy.apply(h.contiguous(), weight, labels, ignore_index, compute_dtype)
+
+
+# ---------------------------------------------------------------------------------------------
+# modules (parameter names and shapes of zenith/mamba3.py:58-93 and zenith/model.py:12-77)
+
+@dataclasses.dataclass
+class ZenithConfig:
+    """The reference's ``ZenithConfig`` fields (zenith/model.py:12-39)."""
+
+    vocab_size: int = 32000
+    d_model: int = 640
+    d_state: int = 128
+    expand: int = 2
+    headdim: int = 64
+    chunk_size: int = 64
+    n_input: int = 4
+    n_recurrent: int = 16
+    n_output: int = 4
+    max_loops: int = 4
+    tie_word_embeddings: bool = True
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "ZenithConfig":
+        names = {f.name for f in dataclasses.fields(cls)}
+        return cls(**{k: v for k, v in d.items() if k in names})
+
+
+class RMSNorm(nn.Module):
+    """zenith/mamba3.py:8-15 (weight ``[dim]``, eps 1e-5)."""
+
+    def __init__(self, dim: int, eps: float = 1e-5):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x: Tensor) -> Tensor:
+        return add_rmsnorm(x, None, self.weight, self.eps)
+
+
+class Mamba3(nn.Module):
+    """The reference ``Mamba3`` mixer (zenith/mamba3.py:58-120) on the fused layer body."""
+
+    def __init__(self, d_model, d_state=128, expand=2, headdim=64, chunk_size=64, dt_min=1e-3, dt_max=1e-1,
+                 dt_init_floor=1e-4, A_floor=1e-4):
+        super().__init__()
+        self.d_state, self.headdim, self.chunk_size, self.A_floor = d_state, headdim, chunk_size, A_floor
+        self.d_inner = expand * d_model
+        self.nheads = self.d_inner // headdim
+        self.num_angles = d_state // 4
+        n_in = 2 * self.d_inner + 2 * d_state + 3 * self.nheads + self.num_angles
+        self.in_proj = nn.Linear(d_model, n_in, bias=False)
+        self.out_proj = nn.Linear(self.d_inner, d_model, bias=False)
+        dt = torch.exp(torch.rand(self.nheads) * (math.log(dt_max) - math.log(dt_min)) + math.log(dt_min))
+        dt = dt.clamp(min=dt_init_floor)
+        self.dt_bias = nn.Parameter(dt + torch.log(-torch.expm1(-dt)))   # inverse softplus (mamba3.py:87-89)
+        self.B_bias = nn.Parameter(torch.ones(self.nheads, d_state))
+        self.C_bias = nn.Parameter(torch.ones(self.nheads, d_state))
+        self.B_norm = RMSNorm(d_state)
+        self.C_norm = RMSNorm(d_state)
+        self.D = nn.Parameter(torch.ones(self.nheads))
+
+    def forward(self, u: Tensor) -> Tensor:
+        Bsz, T, _ = u.shape
+        zxbc = self.in_proj(u)
+        if zxbc.dtype not in (torch.float32, torch.bfloat16):
+            zxbc = zxbc.float()
+        y = mamba3_layer_packed(zxbc, self.dt_bias, self.B_bias, self.C_bias, self.B_norm.weight,
+                                self.C_norm.weight, self.D, self.nheads, self.headdim, self.d_state, self.A_floor,
+                                self.chunk_size, self.B_norm.eps)
+        return self.out_proj(y.reshape(Bsz, T, self.d_inner))
+
+
+class Layer(nn.Module):
+    """``x + mixer(norm(x))`` (zenith/model.py:42-49)."""
+
+    def __init__(self, cfg: ZenithConfig):
+        super().__init__()
+        self.norm = RMSNorm(cfg.d_model)
+        self.mixer = Mamba3(cfg.d_model, cfg.d_state, cfg.expand, cfg.headdim, cfg.chunk_size)
+
+    def forward(self, x: Tensor) -> Tensor:
+        s, delta = run_layers([self], x)
+        return s + delta
+
+
+def _u_dtype(x: Tensor) -> torch.dtype:
+    """The in_proj input dtype: the autocast dtype when CUDA autocast is on (in_proj would cast
+    to it), else the residual stream's."""
+    return torch.get_autocast_dtype("cuda") if torch.is_autocast_enabled("cuda") else x.dtype
+
+
+def run_layers(layers, x: Tensor, delta: Optional[Tensor] = None):
+    """``x = x + layer.mixer(layer.norm(x))`` for each layer, with every residual add fused into
+    the RMSNorm of the next layer.  Returns ``(s, delta)`` with the stack's output ``s + delta``
+    (the last add is left to the caller, to fuse it with whatever reads it)."""
+    for layer in layers:
+        if delta is None:
+            u = add_rmsnorm(x, None, layer.norm.weight, layer.norm.eps, _u_dtype(x))
+        else:
+            x, u = add_rmsnorm(x, delta, layer.norm.weight, layer.norm.eps, _u_dtype(x))
+        delta = layer.mixer(u)
+    return x, delta
+
+
+class LMOutput(NamedTuple):
+    loss: Optional[Tensor]
+    logits: Optional[Tensor]
+
+
+class ZenithForCausalLM(nn.Module):
+    """The reference's looped Mamba-3 LM (zenith/model.py:52-99) on the B200 kernels.  With
+    labels the loss comes from ``linear_cross_entropy`` and ``logits`` is None unless
+    ``return_logits`` (the fused loss never stores them); without labels the logits are
+    returned."""
+
+    def __init__(self, config):
+        super().__init__()
+        cfg = config if isinstance(config, ZenithConfig) else ZenithConfig.from_dict(
+            config if isinstance(config, dict) else vars(config))
+        self.config = cfg
+        self.embed = nn.Embedding(cfg.vocab_size, cfg.d_model)
+        self.input_layers = nn.ModuleList(Layer(cfg) for _ in range(cfg.n_input))
+        self.recurrent_layers = nn.ModuleList(Layer(cfg) for _ in range(cfg.n_recurrent))
+        self.output_layers = nn.ModuleList(Layer(cfg) for _ in range(cfg.n_output))
+        self.recurrent_norm = RMSNorm(cfg.d_model)
+        self.norm = RMSNorm(cfg.d_model)
+        self.lm_head = nn.Linear(cfg.d_model, cfg.vocab_size, bias=False)
+        if cfg.tie_word_embeddings:
+            self.lm_head.weight = self.embed.weight
+        self.reset_parameters()
+
+    def reset_parameters(self, std: float = 0.02):
+        """Linear and embedding weights N(0, 0.02), as the reference's post_init leaves them."""
+        with torch.no_grad():
+            for m in self.modules():
+                if isinstance(m, (nn.Linear, nn.Embedding)):
+                    m.weight.normal_(0.0, std)
+
+    def get_input_embeddings(self):
+        return self.embed
+
+    def get_output_embeddings(self):
+        return self.lm_head
+
+    def forward(self, input_ids: Tensor, labels: Optional[Tensor] = None, loops: Optional[int] = None,
+                return_logits: bool = False) -> LMOutput:
+        cfg = self.config
+        loops = loops or cfg.max_loops
+        x = self.embed(input_ids)
+        x, d = run_layers(self.input_layers, x)
+        x = x + d if d is not None else x
+        s = x
+        for t in range(loops):
+            with torch.no_grad() if t < loops - 1 else nullcontext():
+                h = add_rmsnorm(s, x, self.recurrent_norm.weight, self.recurrent_norm.eps)[1]   # norm(s + x)
+                h, d = run_layers(self.recurrent_layers, h)
+                s = h + d if d is not None else h
+        s, d = run_layers(self.output_layers, s)
+        if d is None:
+            u = add_rmsnorm(s, None, self.norm.weight, self.norm.eps, _u_dtype(s))
+        else:
+            u = add_rmsnorm(s, d, self.norm.weight, self.norm.eps, _u_dtype(s))[1]
+        loss = logits = None
+        if labels is not None:
+            Bsz, T = labels.shape
+            # next-token targets: position t predicts labels[t + 1]; the last position is ignored
+            tgt = torch.cat((labels[:, 1:], torch.full_like(labels[:, :1], -100)), dim=1)
+            loss = linear_cross_entropy(u.reshape(Bsz * T, -1), self.lm_head.weight, tgt.reshape(-1))
+        if labels is None or return_logits:
+            logits = self.lm_head(u)
+        return LMOutput(loss, logits)
+
+
+def load_reference_state_dict(model: ZenithForCausalLM, state_dict: dict):
+    """Load a reference ``ZenithForCausalLM`` state_dict (same names; the tied ``lm_head.weight``
+    may be present or not)."""
+    sd = dict(state_dict)
+    if model.config.tie_word_embeddings:
+        sd.pop("lm_head.weight", None)
+    missing, unexpected = model.load_state_dict(sd, strict=False)
+    missing = [m for m in missing if not (m == "lm_head.weight" and model.config.tie_word_embeddings)]
+    if missing or unexpected:
+        raise KeyError(f"state_dict mismatch: missing {missing}, unexpected {unexpected}")
+
+
+# ---------------------------------------------------------------------------------------------
+# training step (zenith/train.py:99-111)
+
+def train_step(model: nn.Module, opt: torch.optim.Optimizer, ids: Tensor, loops: int = 1, grad_clip: float = 1.0,
+               amp: bool = True) -> Tensor:
+    """One optimiser step on a batch of token ids: bf16-autocast forward with ``labels=ids``,
+    backward (under ``DistributedDataParallel`` the gradient all-reduce runs during it), global
+    gradient-norm clipping, the optimiser step.  Returns the loss (a device scalar, no sync)."""
+    ctx = torch.autocast("cuda", dtype=torch.bfloat16) if amp else nullcontext()
+    with ctx:
+        loss = model(ids, labels=ids, loops=loops).loss
+    loss.backward()
+    torch.nn.utils.clip_grad_norm_(model.parameters(), grad_clip, foreach=True)
+    opt.step()
+    opt.zero_grad(set_to_none=True)
+    return loss.detach()
+
+
+def make_optimizer(model: nn.Module, lr: float = 5e-4, weight_decay: float = 0.1) -> torch.optim.Optimizer:
+    """AdamW with the reference's settings (train.py:89: betas (0.9, 0.95), eps 1e-8), fused CUDA."""
+    return torch.optim.AdamW(model.parameters(), lr=lr, betas=(0.9, 0.95), eps=1e-8, weight_decay=weight_decay,
+                             fused=True)

@@ -97,89 +97,167 @@ def _check(rc: int, what: str):
     L.check(rc, what)
 
 
+def _layer_fwd(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, params, A_floor, chunk_size, eps, op_dtype, save_states=True):
+    """Prologue -> scan -> epilogue.  Returns the output and the tensors the backward needs."""
+    B, T, H, P = x.shape
+    N = Bm.shape[-1]
+    if T % chunk_size != 0:
+        raise AssertionError("sequence length must be a multiple of chunk_size")  # mamba3.py:33
+    dev = x.device
+    lib = _lib()
+    a = _base_args(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, params, A_floor, eps, op_dtype)
+    ws = torch.empty(max(int(lib.zb_m3_workspace_bytes(ctypes.byref(a))), 256), dtype=torch.uint8, device=dev)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    q = torch.empty(B, T, H, N, dtype=op_dtype, device=dev)
+    k_ext = torch.empty(B, T + 1, H, N, dtype=op_dtype, device=dev)
+    xp = torch.empty(B, T, H, P, dtype=op_dtype, device=dev)
+    adt, gamma, beta = (torch.empty(B, T, H, dtype=torch.float32, device=dev) for _ in range(3))
+    theta = torch.empty(B, T, H, N // 4, dtype=torch.float32, device=dev)
+    for n, t in (("q", q), ("k_ext", k_ext), ("xp", xp), ("adt", adt), ("gamma", gamma), ("beta", beta),
+                 ("theta", theta)):
+        setattr(a, n, t.data_ptr())
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    _check(lib.zb_m3_prologue_fwd(ctypes.byref(a), stream), "zb_m3_prologue_fwd")
+    xs = x if x.dtype == op_dtype else x.to(op_dtype)
+    k, kp = k_ext[:, 1:], k_ext[:, :-1]
+    y, _, states = ssd_fwd_op(xs, q, k, kp, xp, adt, gamma, beta, chunk_size, None, save_states, False)
+    out = torch.empty(B, T, H, P, dtype=x.dtype, device=dev)
+    a.y, a.out = y.data_ptr(), _v(out)
+    _check(lib.zb_m3_epilogue_fwd(ctypes.byref(a), stream), "zb_m3_epilogue_fwd")
+    return out, (xs, q, k_ext, xp, adt, gamma, beta, theta, y, states)
+
+
+def _layer_bwd(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, params, scan_saved, A_floor, chunk_size, eps, op_dtype, dout,
+               grads_in):
+    """Epilogue backward -> scan backward -> prologue backward.  ``grads_in`` maps dx, dz, dBm,
+    dCm, ddd_dt, ddd_A, dtrap, dang to the tensors (or views) to write; returns the parameter
+    gradients (fp32, in the order of ``params``)."""
+    xs, q, k_ext, xp, adt, gamma, beta, theta, y, states = scan_saved
+    B, T, H, P = x.shape
+    dev = x.device
+    dout = dout.to(x.dtype)
+    if dout.stride(-1) != 1:
+        dout = dout.contiguous()
+    lib = _lib()
+    a = _base_args(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, params, A_floor, eps, op_dtype)
+    ws = torch.empty(max(int(lib.zb_m3_workspace_bytes(ctypes.byref(a))), 256), dtype=torch.uint8, device=dev)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    for n, t in (("q", q), ("k_ext", k_ext), ("xp", xp), ("adt", adt), ("gamma", gamma), ("beta", beta),
+                 ("theta", theta), ("y", y)):
+        setattr(a, n, t.data_ptr())
+    a.dout = _v(dout)
+    dy = torch.empty(B, T, H, P, dtype=op_dtype, device=dev)
+    a.dy, a.dz = dy.data_ptr(), _v(grads_in["dz"] if z is not None else None)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    _check(lib.zb_m3_epilogue_bwd(ctypes.byref(a), stream), "zb_m3_epilogue_bwd")
+    k, kp = k_ext[:, 1:], k_ext[:, :-1]
+    dxs, dq, dk, dkp, dxp, dadt, dgamma, dbeta, _ = ssd_bwd_op(dy, xs, q, k, kp, xp, adt, gamma, beta, states,
+                                                              chunk_size, None, None, False)
+    for n, t in (("dxs", dxs), ("dxp", dxp), ("dq", dq), ("dk", dk), ("dkp", dkp), ("dadt", dadt),
+                 ("dgamma", dgamma), ("dbeta", dbeta)):
+        setattr(a, n, t.data_ptr())
+    a.dx = _v(grads_in["dx"])
+    a.dBm, a.dCm, a.dang = (_row_view(grads_in[n]) for n in ("dBm", "dCm", "dang"))
+    a.ddd_dt, a.ddd_A, a.dtrap = (_scalar_view(grads_in[n]) for n in ("ddd_dt", "ddd_A", "dtrap"))
+    gp = [torch.empty(prm.shape, dtype=torch.float32, device=dev) for prm in params]
+    for n, t in zip(("ddt_bias", "dB_bias", "dC_bias", "dB_norm_w", "dC_norm_w", "dD"), gp):
+        setattr(a, n, t.data_ptr())
+    _check(lib.zb_m3_prologue_bwd(ctypes.byref(a), stream), "zb_m3_prologue_bwd")
+    return gp
+
+
+def _fp32_params(ps):
+    return [prm.detach().float().contiguous() for prm in ps]
+
+
 class _Mamba3Fused(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, z, Bm, Cm, dd_dt, dd_A, trap, ang, dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D, A_floor,
                 chunk_size, eps, op_dtype):
-        B, T, H, P = x.shape
-        N = Bm.shape[-1]
-        if T % chunk_size != 0:
-            raise AssertionError("sequence length must be a multiple of chunk_size")  # mamba3.py:33
-        dev = x.device
-        params = [p.detach().float().contiguous() for p in (dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D)]
-        lib = _lib()
-        a = _base_args(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, params, A_floor, eps, op_dtype)
-        ws = torch.empty(max(int(lib.zb_m3_workspace_bytes(ctypes.byref(a))), 256), dtype=torch.uint8, device=dev)
-        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
-        q = torch.empty(B, T, H, N, dtype=op_dtype, device=dev)
-        k_ext = torch.empty(B, T + 1, H, N, dtype=op_dtype, device=dev)
-        xp = torch.empty(B, T, H, P, dtype=op_dtype, device=dev)
-        adt, gamma, beta = (torch.empty(B, T, H, dtype=torch.float32, device=dev) for _ in range(3))
-        theta = torch.empty(B, T, H, N // 4, dtype=torch.float32, device=dev)
-        for n, t in (("q", q), ("k_ext", k_ext), ("xp", xp), ("adt", adt), ("gamma", gamma), ("beta", beta),
-                     ("theta", theta)):
-            setattr(a, n, t.data_ptr())
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        _check(lib.zb_m3_prologue_fwd(ctypes.byref(a), stream), "zb_m3_prologue_fwd")
-        xs = x if x.dtype == op_dtype else x.to(op_dtype)
-        k, kp = k_ext[:, 1:], k_ext[:, :-1]
-        y, _, states = ssd_fwd_op(xs, q, k, kp, xp, adt, gamma, beta, chunk_size, None, True, False)
-        out = torch.empty(B, T, H, P, dtype=x.dtype, device=dev)
-        a.y, a.out = y.data_ptr(), _v(out)
-        _check(lib.zb_m3_epilogue_fwd(ctypes.byref(a), stream), "zb_m3_epilogue_fwd")
-        ctx.save_for_backward(x, z if z is not None else torch.empty(0, device=dev), Bm, Cm, dd_dt, dd_A, trap, ang,
-                              *params, xs, q, k_ext, xp, adt, gamma, beta, theta, y, states)
+        params = _fp32_params((dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D))
+        out, saved = _layer_fwd(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, params, A_floor, chunk_size, eps, op_dtype)
+        ctx.save_for_backward(x, z if z is not None else torch.empty(0, device=x.device), Bm, Cm, dd_dt, dd_A, trap,
+                              ang, *params, *saved)
         ctx.has_z = z is not None
         ctx.meta = (float(A_floor), int(chunk_size), float(eps), op_dtype)
-        ctx.param_dtypes = [p.dtype for p in (dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D)]
+        ctx.param_dtypes = [prm.dtype for prm in (dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D)]
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        (x, z, Bm, Cm, dd_dt, dd_A, trap, ang, dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D, xs, q, k_ext, xp, adt,
-         gamma, beta, theta, y, states) = ctx.saved_tensors
+        t = ctx.saved_tensors
+        x, z, Bm, Cm, dd_dt, dd_A, trap, ang = t[:8]
+        params, saved = t[8:14], t[14:]
         z = z if ctx.has_z else None
         A_floor, chunk_size, eps, op_dtype = ctx.meta
-        B, T, H, P = x.shape
-        N = Bm.shape[-1]
-        dev = x.device
-        dout = dout.to(x.dtype)
-        if dout.stride(-1) != 1:
-            dout = dout.contiguous()
-        lib = _lib()
-        params = (dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D)
-        a = _base_args(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, params, A_floor, eps, op_dtype)
-        ws = torch.empty(max(int(lib.zb_m3_workspace_bytes(ctypes.byref(a))), 256), dtype=torch.uint8, device=dev)
-        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
-        for n, t in (("q", q), ("k_ext", k_ext), ("xp", xp), ("adt", adt), ("gamma", gamma), ("beta", beta),
-                     ("theta", theta), ("y", y)):
-            setattr(a, n, t.data_ptr())
-        a.dout = _v(dout)
-        dy = torch.empty(B, T, H, P, dtype=op_dtype, device=dev)
-        dz = torch.empty_like(z, memory_format=torch.contiguous_format) if z is not None else None
-        a.dy, a.dz = dy.data_ptr(), _v(dz)
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        _check(lib.zb_m3_epilogue_bwd(ctypes.byref(a), stream), "zb_m3_epilogue_bwd")
-        k, kp = k_ext[:, 1:], k_ext[:, :-1]
-        dxs, dq, dk, dkp, dxp, dadt, dgamma, dbeta, _ = ssd_bwd_op(dy, xs, q, k, kp, xp, adt, gamma, beta, states,
-                                                                  chunk_size, None, None, False)
-        for n, t in (("dxs", dxs), ("dxp", dxp), ("dq", dq), ("dk", dk), ("dkp", dkp), ("dadt", dadt),
-                     ("dgamma", dgamma), ("dbeta", dbeta)):
-            setattr(a, n, t.data_ptr())
-        grads_in = {n: torch.empty(t.shape, dtype=t.dtype, device=dev)
-                    for n, t in (("dx", x), ("dBm", Bm), ("dCm", Cm), ("ddd_dt", dd_dt), ("ddd_A", dd_A),
+        grads_in = {n: torch.empty(v.shape, dtype=v.dtype, device=x.device)
+                    for n, v in (("dx", x), ("dBm", Bm), ("dCm", Cm), ("ddd_dt", dd_dt), ("ddd_A", dd_A),
                                  ("dtrap", trap), ("dang", ang))}
-        for n in ("dx",):
-            setattr(a, n, _v(grads_in[n]))
-        a.dBm, a.dCm, a.dang = _row_view(grads_in["dBm"]), _row_view(grads_in["dCm"]), _row_view(grads_in["dang"])
-        a.ddd_dt, a.ddd_A, a.dtrap = (_scalar_view(grads_in[n]) for n in ("ddd_dt", "ddd_A", "dtrap"))
-        gp = [torch.empty_like(p) for p in params]
-        for n, t in zip(("ddt_bias", "dB_bias", "dC_bias", "dB_norm_w", "dC_norm_w", "dD"), gp):
-            setattr(a, n, t.data_ptr())
-        _check(lib.zb_m3_prologue_bwd(ctypes.byref(a), stream), "zb_m3_prologue_bwd")
+        grads_in["dz"] = torch.empty(z.shape, dtype=z.dtype, device=x.device) if z is not None else None
+        gp = _layer_bwd(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, params, saved, A_floor, chunk_size, eps, op_dtype, dout,
+                        grads_in)
         gp = [g.to(dt) for g, dt in zip(gp, ctx.param_dtypes)]
-        return (grads_in["dx"], dz, grads_in["dBm"], grads_in["dCm"], grads_in["ddd_dt"], grads_in["ddd_A"],
-                grads_in["dtrap"], grads_in["dang"], *gp, None, None, None, None)
+        return (grads_in["dx"], grads_in["dz"], grads_in["dBm"], grads_in["dCm"], grads_in["ddd_dt"],
+                grads_in["ddd_A"], grads_in["dtrap"], grads_in["dang"], *gp, None, None, None, None)
+
+
+def split_in_proj(zxbc: Tensor, H: int, P: int, N: int):
+    """The in_proj output [B, T, 2 H P + 2 N + 3 H + N/4] split as Mamba3.forward does
+    (mamba3.py:98-103), as views: z, x [B,T,H,P]; Bm, Cm [B,T,N]; dd_dt, dd_A, trap [B,T,H]; ang [B,T,N/4]."""
+    Bsz, T, _ = zxbc.shape
+    z, x, Bm, Cm, dd_dt, dd_A, trap, ang = torch.split(zxbc, [H * P, H * P, N, N, H, H, H, N // 4], dim=-1)
+    return x.view(Bsz, T, H, P), z.view(Bsz, T, H, P), Bm, Cm, dd_dt, dd_A, trap, ang
+
+
+class _Mamba3Packed(torch.autograd.Function):
+    """The layer body on the packed in_proj output: the split pieces are views, and the backward
+    writes every piece's gradient straight into one packed gradient tensor (no concatenation)."""
+
+    @staticmethod
+    def forward(ctx, zxbc, dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D, H, P, N, A_floor, chunk_size, eps,
+                op_dtype, grad):
+        params = _fp32_params((dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D))
+        x, z, *rest = split_in_proj(zxbc, H, P, N)
+        out, saved = _layer_fwd(x, z, *rest, params, A_floor, chunk_size, eps, op_dtype, save_states=grad)
+        if grad:
+            ctx.save_for_backward(zxbc, *params, *saved)
+        ctx.meta = (H, P, N, float(A_floor), int(chunk_size), float(eps), op_dtype)
+        ctx.param_dtypes = [prm.dtype for prm in (dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D)]
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        t = ctx.saved_tensors
+        zxbc, params, saved = t[0], t[1:7], t[7:]
+        H, P, N, A_floor, chunk_size, eps, op_dtype = ctx.meta
+        x, z, Bm, Cm, dd_dt, dd_A, trap, ang = split_in_proj(zxbc, H, P, N)
+        dzxbc = torch.empty_like(zxbc, memory_format=torch.contiguous_format)
+        gx, gz, gBm, gCm, gdt, gdA, gtr, gang = split_in_proj(dzxbc, H, P, N)
+        grads_in = {"dx": gx, "dz": gz, "dBm": gBm, "dCm": gCm, "ddd_dt": gdt, "ddd_A": gdA, "dtrap": gtr,
+                    "dang": gang}
+        gp = _layer_bwd(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, params, saved, A_floor, chunk_size, eps, op_dtype, dout,
+                        grads_in)
+        gp = [g.to(dt) for g, dt in zip(gp, ctx.param_dtypes)]
+        return (dzxbc, *gp, None, None, None, None, None, None, None, None)
+
+
+def mamba3_layer_packed(zxbc: Tensor, dt_bias: Tensor, B_bias: Tensor, C_bias: Tensor, B_norm_w: Tensor,
+                        C_norm_w: Tensor, D: Tensor, H: int, P: int, N: int, A_floor: float = 1e-4,
+                        chunk_size: int = 64, eps: float = 1e-5, scan_dtype: Optional[torch.dtype] = None) -> Tensor:
+    """``mamba3_ssd_fused`` on the packed in_proj output ``zxbc`` ``[B, T, 2HP + 2N + 3H + N/4]``
+    (float32 or bfloat16, innermost dimension contiguous), split as Mamba3.forward splits it
+    (mamba3.py:98-100).  Returns ``[B, T, H, P]`` in zxbc's dtype; the gradient of zxbc is
+    written as one tensor."""
+    if zxbc.dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError("mamba3_layer_packed: float32 or bfloat16 input")
+    if zxbc.stride(-1) != 1:
+        zxbc = zxbc.contiguous()
+    op_dtype = _scan_dtype(zxbc, scan_dtype)
+    # no backward (the reference's non-final loops run under no_grad): no saved states
+    grad = torch.is_grad_enabled() and any(t.requires_grad for t in (zxbc, dt_bias, B_bias, C_bias, B_norm_w,
+                                                                      C_norm_w, D))
+    return _Mamba3Packed.apply(zxbc, dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D, H, P, N, A_floor, chunk_size,
+                               eps, op_dtype, grad)
 
 
 def _scan_dtype(x: Tensor, scan_dtype: Optional[torch.dtype]) -> torch.dtype:
@@ -217,17 +295,17 @@ def mamba3_ssd_fused(x: Tensor, z: Optional[Tensor], Bm: Tensor, Cm: Tensor, dd_
 
 
 def layer_forward(module, u: Tensor, scan_dtype: Optional[torch.dtype] = None) -> Tensor:
-    """``Mamba3.forward`` (zenith/mamba3.py:96-119) with the layer body fused: in_proj, the split,
-    ``mamba3_ssd_fused``, out_proj.  ``module`` has the reference's attributes."""
+    """``Mamba3.forward`` (zenith/mamba3.py:96-120) with the layer body fused: in_proj, the
+    packed layer body (``mamba3_layer_packed``), out_proj.  ``module`` has the reference's
+    attributes.  A bfloat16 in_proj output (autocast) feeds the kernels as it is; they compute in
+    float32, as the reference's ``.float()`` upcasts do."""
     Bsz, T, _ = u.shape
-    H, P, N = module.nheads, module.headdim, module.d_state
-    z, x, Bm, Cm, dd_dt, dd_A, trap, ang = torch.split(
-        module.in_proj(u), [module.d_inner, module.d_inner, N, N, H, H, H, module.num_angles], dim=-1)
-    x = x.float().view(Bsz, T, H, P) if x.dtype != torch.bfloat16 else x.reshape(Bsz, T, H, P)
-    z = z.float().view(Bsz, T, H, P) if z.dtype != torch.bfloat16 else z.reshape(Bsz, T, H, P)
-    y = mamba3_ssd_fused(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, module.dt_bias, module.B_bias, module.C_bias,
-                         module.B_norm.weight, module.C_norm.weight, module.D, module.A_floor, module.chunk_size,
-                         module.B_norm.eps, scan_dtype)
+    zxbc = module.in_proj(u)
+    if zxbc.dtype not in (torch.float32, torch.bfloat16):
+        zxbc = zxbc.float()
+    y = mamba3_layer_packed(zxbc, module.dt_bias, module.B_bias, module.C_bias, module.B_norm.weight,
+                            module.C_norm.weight, module.D, module.nheads, module.headdim, module.d_state,
+                            module.A_floor, module.chunk_size, module.B_norm.eps, scan_dtype)
     return module.out_proj(y.reshape(Bsz, T, module.d_inner).to(u.dtype))
 
 
