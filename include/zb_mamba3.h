@@ -11,8 +11,8 @@
  * A layer step is: zb_m3_prologue_fwd -> zb_ssd_fwd -> zb_m3_epilogue_fwd, and backward
  * zb_m3_epilogue_bwd -> zb_ssd_bwd -> zb_m3_prologue_bwd.
  *
- * Sizes: H <= 31 heads, N % 16 == 0 and N <= 128 (N/4 RoPE angles rotate the first N/2
- * features), P <= 256.  Layer inputs may be strided views (the in_proj split); scan operands and
+ * Sizes: H <= 128 heads with H P <= 8192 (more than 31 heads run in groups of at most 28),
+ * N % 16 == 0 and N <= 128 (N/4 RoPE angles rotate the first N/2 features), P <= 256.  Layer inputs may be strided views (the in_proj split); scan operands and
  * scan gradients are contiguous and 16-byte aligned.  All kernels are deterministic (fixed-order reductions).
  */
 #ifndef ZB_MAMBA3_H
@@ -67,7 +67,8 @@ ZB_API int zb_m3_prologue_fwd(const zb_m3_args* args, void* stream);
 ZB_API int zb_m3_epilogue_fwd(const zb_m3_args* args, void* stream);
 /* from dout: dy for the scan backward, dz, and the D gradient's partial sums (in workspace)   */
 ZB_API int zb_m3_epilogue_bwd(const zb_m3_args* args, void* stream);
-/* from the scan's gradients: dx, dBm, dCm, ddd_dt, ddd_A, dtrap, dang and all parameter grads */
+/* from the scan's gradients and dy (as zb_m3_epilogue_bwd wrote it): dx, dBm, dCm, ddd_dt,
+   ddd_A, dtrap, dang and all parameter grads */
 ZB_API int zb_m3_prologue_bwd(const zb_m3_args* args, void* stream);
 
 #ifdef __cplusplus

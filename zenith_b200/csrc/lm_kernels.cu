@@ -160,15 +160,119 @@ __global__ void __launch_bounds__(32 * kNormWarps) rmsnorm_bwd_kernel(const Norm
   }
 }
 
-__global__ void rmsnorm_dw_kernel(const NormP p, int nblocks) {
-  const int n = blockIdx.x * blockDim.x + threadIdx.x;
-  if (n >= p.D) return;
-  float s = 0.f;
-  for (int k = 0; k < nblocks; ++k) s += p.part[(int64_t)k * p.D + n];
-  p.dw[n] = s;
+// ---- one CTA per row, the row in registers (D % 8 == 0, 16-byte aligned rows): thread i owns
+// features 8i .. 8i+7, so every element is read once and the dw sums stay in registers
+
+// sum over the CTA, every thread gets the total (warp sums, then the warps' sums in order)
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int k = 0; k < nw; ++k) t += red[k];
+  __syncthreads();  // red is reused by the next row
+  return t;
 }
 
-int norm_grid(int64_t M) { return (int)((M + kNormWarps - 1) / kNormWarps < kNormGrid ? (M + kNormWarps - 1) / kNormWarps : kNormGrid); }
+template <typename TX, typename TB, typename TU>
+__global__ void __launch_bounds__(1024) rmsnorm_fwd_row_kernel(const NormP p) {
+  __shared__ float red[32];
+  const int D = (int)p.D, n = 8 * threadIdx.x;
+  const bool on = n < D;
+  const TX* __restrict__ A = static_cast<const TX*>(p.a);
+  const TB* __restrict__ Bv = static_cast<const TB*>(p.b);
+  TX* __restrict__ S = static_cast<TX*>(p.s);
+  TU* __restrict__ U = static_cast<TU*>(p.u);
+  float w[8];
+  if (on) Vec8<float>::ld(p.w + n, w);
+  for (int64_t row = blockIdx.x; row < p.M; row += gridDim.x) {
+    const int64_t o = row * D + n;
+    float v[8], ss = 0.f;
+    if (on) {
+      Vec8<TX>::ld(A + o, v);
+      if (Bv) {
+        float c[8];
+        Vec8<TB>::ld(Bv + o, c);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = round_to<TX>(v[e] + c[e]);
+        Vec8<TX>::st(S + o, v);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+    }
+    const float r = rsqrtf(block_sum(ss, red) / D + p.eps);
+    if (p.r && threadIdx.x == 0) p.r[row] = r;
+    if (on) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = v[e] * r * w[e];
+      Vec8<TU>::st(U + o, v);
+    }
+  }
+}
+
+template <typename TX, typename TB, typename TU>
+__global__ void __launch_bounds__(1024) rmsnorm_bwd_row_kernel(const NormP p) {
+  __shared__ float red[32];
+  const int D = (int)p.D, n = 8 * threadIdx.x;
+  const bool on = n < D;
+  const TX* __restrict__ S = static_cast<const TX*>(p.b ? p.s : p.a);
+  const TU* __restrict__ dU = static_cast<const TU*>(p.du);
+  const TX* __restrict__ dS = static_cast<const TX*>(p.ds);
+  TX* __restrict__ G = static_cast<TX*>(p.dsum);
+  TB* __restrict__ GB = static_cast<TB*>(p.dsum_b);
+  float w[8], dw[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (on) Vec8<float>::ld(p.w + n, w);
+  for (int64_t row = blockIdx.x; row < p.M; row += gridDim.x) {
+    const int64_t o = row * D + n;
+    const float r = p.r[row];
+    float g[8], x[8], dot = 0.f;
+    if (on) {
+      Vec8<TU>::ld(dU + o, g);
+      Vec8<TX>::ld(S + o, x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) dot += g[e] * w[e] * x[e];
+    }
+    const float k3 = r * r * r / D * block_sum(dot, red);
+    if (on) {
+      float out[8];
+      if (dS) Vec8<TX>::ld(dS + o, out);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        out[e] = (dS ? out[e] : 0.f) + r * w[e] * g[e] - x[e] * k3;
+        dw[e] += g[e] * x[e] * r;
+      }
+      Vec8<TX>::st(G + o, out);
+      if (GB) Vec8<TB>::st(GB + o, out);
+    }
+  }
+  if (on) Vec8<float>::st(p.part + (int64_t)blockIdx.x * D + n, dw);
+}
+
+// dw[n] = sum over the CTAs' partials in CTA order: 32 features per CTA, the partials split over
+// 8 warps (coalesced rows), then the warps' sums in order
+__global__ void __launch_bounds__(256) rmsnorm_dw_kernel(const NormP p, int nblocks) {
+  __shared__ float sm[8][33];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * 32 + lane;
+  float s = 0.f;
+  if (n < p.D)
+    for (int k = warp; k < nblocks; k += 8) s += p.part[(int64_t)k * p.D + n];
+  sm[warp][lane] = s;
+  __syncthreads();
+  if (warp == 0 && n < p.D) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += sm[k][lane];
+    p.dw[n] = t;
+  }
+}
+
+// warp-per-row kernels: M / 8 CTAs up to kNormGrid; row kernels: M CTAs up to kNormGrid
+int norm_grid_warp(int64_t M) { return (int)((M + kNormWarps - 1) / kNormWarps < kNormGrid ? (M + kNormWarps - 1) / kNormWarps : kNormGrid); }
+int row_grid(int64_t M) { return (int)(M < kNormGrid ? M : kNormGrid); }
+int row_threads(int64_t D) { return (int)((D / 8 + 31) / 32 * 32); }
+
 
 bool aligned16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; }
 
@@ -245,8 +349,31 @@ __device__ __forceinline__ void block_max_sum(float& m, float& s, float* sm, flo
   s = S;
 }
 
-// kPer > 0: the row is held in registers, kPer 8-element units per thread (V % 8 == 0, aligned
-// rows); kPer == 0: any V, the row is read twice
+// eight consecutive elements held packed in registers (bf16: one 16-byte word)
+template <typename T> struct Pack8;
+template <> struct Pack8<__nv_bfloat16> {
+  uint4 u;
+  __device__ __forceinline__ void ld(const __nv_bfloat16* p) { u = *reinterpret_cast<const uint4*>(p); }
+  __device__ __forceinline__ float get(int e) const {
+    const uint32_t w = e < 2 ? u.x : e < 4 ? u.y : e < 6 ? u.z : u.w;
+    return __uint_as_float((e & 1) ? (w & 0xffff0000u) : (w << 16));
+  }
+};
+template <> struct Pack8<float> {
+  float4 a, b;
+  __device__ __forceinline__ void ld(const float* p) {
+    a = *reinterpret_cast<const float4*>(p);
+    b = *reinterpret_cast<const float4*>(p + 4);
+  }
+  __device__ __forceinline__ float get(int e) const {
+    const float4& q = e < 4 ? a : b;
+    const int k = e & 3;
+    return k == 0 ? q.x : k == 1 ? q.y : k == 2 ? q.z : q.w;
+  }
+};
+
+// kPer > 0: the row is held in registers (packed), kPer 8-element units per thread (V % 8 == 0,
+// aligned rows); kPer == 0: any V, the row is read twice
 template <typename T, int kPer>
 __global__ void __launch_bounds__(kXentThreads) xent_kernel(const XentP p) {
   __shared__ float sm[kXentThreads / 32], ss[kXentThreads / 32];
@@ -261,16 +388,19 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const XentP p) {
   }
   const float xl = (valid && threadIdx.x == 0) ? ldv<float>(L + lab) : 0.f;  // before any thread writes
   float m = -INFINITY, s = 0.f;
-  float v[kPer > 0 ? kPer : 1][8];
+  Pack8<T> v[kPer > 0 ? kPer : 1];
   if constexpr (kPer > 0) {
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
       const int n = (i * kXentThreads + threadIdx.x) * 8;
-      if (n < V) {
-        Vec8<T>::ld(L + n, v[i]);
+      if (n < V) v[i].ld(L + n);
+    }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) m = fmaxf(m, v[i][e]);
-      }
+    for (int i = 0; i < kPer; ++i) {
+      const int n = (i * kXentThreads + threadIdx.x) * 8;
+      if (n < V)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m = fmaxf(m, v[i].get(e));
     }
     if (m != -INFINITY)
 #pragma unroll
@@ -278,7 +408,7 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const XentP p) {
         const int n = (i * kXentThreads + threadIdx.x) * 8;
         if (n < V)
 #pragma unroll
-          for (int e = 0; e < 8; ++e) s += expf(v[i][e] - m);
+          for (int e = 0; e < 8; ++e) s += expf(v[i].get(e) - m);
       }
   } else {
     for (int n = threadIdx.x; n < V; n += kXentThreads) {
@@ -305,7 +435,7 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const XentP p) {
       if (n < V) {
         float g[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) g[e] = valid ? expf(v[i][e] - lse) - (n + e == lab ? 1.f : 0.f) : 0.f;
+        for (int e = 0; e < 8; ++e) g[e] = valid ? expf(v[i].get(e) - lse) - (n + e == lab ? 1.f : 0.f) : 0.f;
         Vec8<T>::st(L + n, g);
       }
     }
@@ -340,7 +470,7 @@ using namespace zb;
 
 extern "C" ZB_API uint64_t zb_rmsnorm_workspace_bytes(const zb_rmsnorm_args* a) {
   if (!a || a->M <= 0 || a->D <= 0) return 0;
-  return align_up((size_t)norm_grid(a->M) * a->D * sizeof(float), 256);
+  return align_up((size_t)row_grid(a->M) * a->D * sizeof(float), 256);  // row_grid >= norm_grid_warp
 }
 
 extern "C" ZB_API int zb_rmsnorm_fwd(const zb_rmsnorm_args* a, void* stream) {
@@ -352,7 +482,11 @@ extern "C" ZB_API int zb_rmsnorm_fwd(const zb_rmsnorm_args* a, void* stream) {
   rc = with_type(a->x_dtype, [&](auto tx) {
     return with_type(a->b_dtype, [&](auto tb) {
       return with_type(a->u_dtype, [&](auto tu) {
-        rmsnorm_fwd_kernel<decltype(tx), decltype(tb), decltype(tu)><<<norm_grid(a->M), 32 * kNormWarps, 0, st>>>(p);
+        using TX = decltype(tx);
+        using TB = decltype(tb);
+        using TU = decltype(tu);
+        if (p.vec) rmsnorm_fwd_row_kernel<TX, TB, TU><<<row_grid(a->M), row_threads(a->D), 0, st>>>(p);
+        else rmsnorm_fwd_kernel<TX, TB, TU><<<norm_grid_warp(a->M), 32 * kNormWarps, 0, st>>>(p);
         return (int)ZB_OK;
       });
     });
@@ -369,12 +503,19 @@ extern "C" ZB_API int zb_rmsnorm_bwd(const zb_rmsnorm_args* a, void* stream) {
     return ZB_ERR_WORKSPACE;
   const NormP p = make_norm(a, true);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int grid = norm_grid(a->M);
+  const int grid = p.vec ? row_grid(a->M) : norm_grid_warp(a->M);
   const int smem = (int)(kNormWarps * a->D * sizeof(float));
   rc = with_type(a->x_dtype, [&](auto tx) {
     return with_type(a->b_dtype, [&](auto tb) {
       return with_type(a->u_dtype, [&](auto tu) {
-        auto k = rmsnorm_bwd_kernel<decltype(tx), decltype(tb), decltype(tu)>;
+        using TX = decltype(tx);
+        using TB = decltype(tb);
+        using TU = decltype(tu);
+        if (p.vec) {
+          rmsnorm_bwd_row_kernel<TX, TB, TU><<<grid, row_threads(a->D), 0, st>>>(p);
+          return (int)ZB_OK;
+        }
+        auto k = rmsnorm_bwd_kernel<TX, TB, TU>;
         if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
           return (int)ZB_ERR_CUDA;
         k<<<grid, 32 * kNormWarps, smem, st>>>(p);
@@ -383,7 +524,7 @@ extern "C" ZB_API int zb_rmsnorm_bwd(const zb_rmsnorm_args* a, void* stream) {
     });
   });
   if (rc) return rc;
-  rmsnorm_dw_kernel<<<(unsigned)((a->D + 255) / 256), 256, 0, st>>>(p, grid);
+  rmsnorm_dw_kernel<<<(unsigned)((a->D + 31) / 32), 256, 0, st>>>(p, grid);
   return finish_lm(2);
 }
 

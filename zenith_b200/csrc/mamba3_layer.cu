@@ -408,7 +408,8 @@ __global__ void __launch_bounds__(256) m3_epilogue_bwd_kernel(const M3 p) {
   }
 }
 
-// dx = scan dx + dxp of the next token (xp[t+1] = x[t]) + D dout silu(z)   (mamba3.py:115,119)
+// dx = scan dx + dxp of the next token (xp[t+1] = x[t]) + D dy, with dy = dout silu(z) as the
+// epilogue backward stored it for the scan   (mamba3.py:115,119)
 template <typename TI, typename TO>
 __global__ void __launch_bounds__(256) m3_dx_kernel(const M3 p) {
   const int b = blockIdx.x / p.nseg, seg = blockIdx.x % p.nseg;
@@ -417,18 +418,14 @@ __global__ void __launch_bounds__(256) m3_dx_kernel(const M3 p) {
   const int nt = (int)min((int64_t)kSeg, p.T - t0);
   const TO* __restrict__ dxs = static_cast<const TO*>(p.dxs);
   const TO* __restrict__ dxp = static_cast<const TO*>(p.dxp);
+  const TO* __restrict__ dy = static_cast<const TO*>(p.dy);
 #pragma unroll 4
   for (int idx = threadIdx.x; idx < nt * HP; idx += blockDim.x) {
     const int t = idx / HP, r = idx % HP, hh = r / P, pp = r % P;
-    const int64_t tt = t0 + t;
-    float g = ldv<float>(dxs + (b * p.T + tt) * HP + r);
-    if (tt + 1 < p.T) g += ldv<float>(dxp + (b * p.T + tt + 1) * HP + r);
-    float go = ldv<float>(p.dout.row<TI>(b, tt, hh) + pp);
-    if (p.z.ptr) {
-      const float zz = ldv<float>(p.z.row<TI>(b, tt, hh) + pp);
-      go *= zz * sigmoidf_(zz);
-    }
-    stv<float>(p.dx.wrow<TI>(b, tt, hh) + pp, g + p.D[hh] * go);
+    const int64_t tt = t0 + t, o = (b * p.T + tt) * HP + r;
+    float g = ldv<float>(dxs + o);
+    if (tt + 1 < p.T) g += ldv<float>(dxp + o + HP);
+    stv<float>(p.dx.wrow<TI>(b, tt, hh) + pp, g + p.D[hh] * ldv<float>(dy + o));
   }
 }
 
@@ -757,8 +754,10 @@ __global__ void __launch_bounds__(1024) m3_scalars_bwd_kernel(const M3 p) {
   float* sacc = sDT + kSeg * H;
   for (int idx = threadIdx.x; idx < H * NA; idx += blockDim.x) {  // theta gradient over all later segments
     const int hh = idx / NA, i = idx % NA;
+    const float* __restrict__ src = p.segsum + (int64_t)(b * H + hh) * p.nseg * NA + i;
     float C = 0.f;
-    for (int s = seg + 1; s < p.nseg; ++s) C += p.segsum[((b * H + hh) * p.nseg + s) * NA + i];
+#pragma unroll 8
+    for (int s = seg + 1; s < p.nseg; ++s) C += __ldg(src + (int64_t)s * NA);
     sC[idx] = C;
   }
   for (int idx = threadIdx.x; idx < nt * NA; idx += blockDim.x)
@@ -899,53 +898,64 @@ __global__ void __launch_bounds__(1024) m3_dx_vec_kernel(const M3 p) {
   const float Dh = p.D[hh];
   const TO* __restrict__ dxs = static_cast<const TO*>(p.dxs) + (int64_t)b * p.T * HP + r;
   const TO* __restrict__ dxp = static_cast<const TO*>(p.dxp) + (int64_t)b * p.T * HP + r;
+  const TO* __restrict__ dy = static_cast<const TO*>(p.dy) + (int64_t)b * p.T * HP + r;
 #pragma unroll 2
   for (int t = grp; t < nt; t += ngrp) {
     const int64_t tt = t0 + t;
-    float g[8], go[8];
+    float g[8], gy[8];
     Vec8<TO>::ld(dxs + tt * HP, g);
+    Vec8<TO>::ld(dy + tt * HP, gy);  // dout silu(z), as stored for the scan
     if (tt + 1 < p.T) {  // xp[t+1] = x[t]
       float gp[8];
       Vec8<TO>::ld(dxp + (tt + 1) * HP, gp);
 #pragma unroll
       for (int e = 0; e < 8; ++e) g[e] += gp[e];
     }
-    Vec8<TI>::ld(p.dout.row<TI>(b, tt, hh) + pp, go);
-    if (p.z.ptr) {
-      float zv[8];
-      Vec8<TI>::ld(p.z.row<TI>(b, tt, hh) + pp, zv);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) go[e] *= zv[e] * sigmoidf_(zv[e]);
-    }
-#pragma unroll
-    for (int e = 0; e < 8; ++e) g[e] += Dh * go[e];
+    for (int e = 0; e < 8; ++e) g[e] += Dh * gy[e];
     Vec8<TI>::st(p.dx.wrow<TI>(b, tt, hh) + pp, g);
   }
 }
 
-// parameter gradients: fixed-order sums of the per-(batch, segment) partials
-__global__ void m3_param_reduce_kernel(const M3 p) {
+// parameter gradients: fixed-order sums of the per-(batch, segment) partials.  One warp lane per
+// output over 32 consecutive outputs, the partials split over the 8 warps of the CTA (coalesced
+// rows), then the warps' sums in order.
+__global__ void __launch_bounds__(256) m3_param_reduce_kernel(const M3 p) {
+  __shared__ float sm[8][33];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t H = p.H, N = p.N, BS = p.B * p.nseg;
   const int64_t n_bias = H * N;
   const int64_t total = 2 * n_bias + 2 * N + 2 * H;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    float s = 0.f;
-    if (i < 2 * n_bias) {  // B_bias then C_bias
-      const int64_t part = i / n_bias, j = i % n_bias;
-      const float* src = p.pbias + part * BS * n_bias + j;
-      for (int64_t k = 0; k < BS; ++k) s += src[k * n_bias];
-      (part ? p.dC_bias : p.dB_bias)[j] = s;
-    } else if (i < 2 * n_bias + 2 * N) {  // B_norm_w then C_norm_w
-      const int64_t r = i - 2 * n_bias, part = r / N, j = r % N;
-      const float* src = p.pnorm + part * BS * N + j;
-      for (int64_t k = 0; k < BS; ++k) s += src[k * N];
-      (part ? p.dC_norm_w : p.dB_norm_w)[j] = s;
-    } else {  // dt_bias then D
-      const int64_t r = i - 2 * n_bias - 2 * N, part = r / H, j = r % H;
-      const float* src = (part ? p.pD : p.pdt) + j;
-      for (int64_t k = 0; k < BS; ++k) s += src[k * H];
-      (part ? p.dD : p.ddt_bias)[j] = s;
-    }
+  const int64_t i = (int64_t)blockIdx.x * 32 + lane;
+  const float* src = nullptr;
+  int64_t stride = 0;
+  float* dst = nullptr;
+  if (i < 2 * n_bias) {  // B_bias then C_bias
+    const int64_t part = i / n_bias, j = i % n_bias;
+    src = p.pbias + part * BS * n_bias + j;
+    stride = n_bias;
+    dst = (part ? p.dC_bias : p.dB_bias) + j;
+  } else if (i < 2 * n_bias + 2 * N) {  // B_norm_w then C_norm_w
+    const int64_t r = i - 2 * n_bias, part = r / N, j = r % N;
+    src = p.pnorm + part * BS * N + j;
+    stride = N;
+    dst = (part ? p.dC_norm_w : p.dB_norm_w) + j;
+  } else if (i < total) {  // dt_bias then D
+    const int64_t r = i - 2 * n_bias - 2 * N, part = r / H, j = r % H;
+    src = (part ? p.pD : p.pdt) + j;
+    stride = H;
+    dst = (part ? p.dD : p.ddt_bias) + j;
+  }
+  float s = 0.f;
+  if (src)
+    for (int64_t k = warp; k < BS; k += 8) s += src[k * stride];
+  sm[warp][lane] = s;
+  __syncthreads();
+  if (warp == 0 && dst) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += sm[k][lane];
+    *dst = t;
   }
 }
 
@@ -1130,7 +1140,7 @@ extern "C" ZB_API int zb_m3_epilogue_bwd(const zb_m3_args* a, void* stream) {
 extern "C" ZB_API int zb_m3_prologue_bwd(const zb_m3_args* a, void* stream) {
   int rc = check(a);
   if (rc) return rc;
-  if (!a->theta || !a->dout.ptr || !a->dxs || !a->dxp || !a->dq || !a->dk || !a->dkp || !a->dadt || !a->dgamma ||
+  if (!a->theta || !a->dout.ptr || !a->dy || !a->dxs || !a->dxp || !a->dq || !a->dk || !a->dkp || !a->dadt || !a->dgamma ||
       !a->dbeta || !a->dx.ptr || !a->dBm.ptr || !a->dCm.ptr || !a->ddd_dt.ptr || !a->ddd_A.ptr || !a->dtrap.ptr ||
       !a->dang.ptr || !a->ddt_bias || !a->dB_bias || !a->dC_bias || !a->dB_norm_w || !a->dC_norm_w || !a->dD)
     return ZB_ERR_LAYOUT;
@@ -1167,6 +1177,7 @@ extern "C" ZB_API int zb_m3_prologue_bwd(const zb_m3_args* a, void* stream) {
     if (p.nhg > 1) m3_rms_bwd_kernel<TI><<<grid, 256, 0, s>>>(p);
     m3_scalars_bwd_kernel<TI><<<grid, (unsigned)sthreads, smem2, s>>>(p);
   });
-  m3_param_reduce_kernel<<<64, 256, 0, s>>>(p);
+  const int64_t n_params = 2 * p.H * p.N + 2 * p.N + 2 * p.H;
+  m3_param_reduce_kernel<<<(unsigned)((n_params + 31) / 32), 256, 0, s>>>(p);
   return finish(p.nhg > 1 ? 5 : 4);
 }
