@@ -57,6 +57,9 @@ typedef struct {
      zb_m3_epilogue_bwd and the zb_m3_prologue_bwd that follows it */
   void* workspace;
   uint64_t workspace_bytes;
+  /* device int32 status word (zb_m3_prologue_bwd): a bounded wait on its row copies that gives up
+     after about a second records ZB_ERR_TIMEOUT there and the kernel returns */
+  int32_t* status;
 } zb_m3_args;
 
 /* scratch bytes the four calls need (the maximum over them) */

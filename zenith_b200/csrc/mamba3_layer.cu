@@ -17,6 +17,7 @@
 
 #include "common.cuh"
 #include "ssd_kernels.h"
+#include "umma.cuh"
 #include "zb_mamba3.h"
 
 namespace zb {
@@ -44,6 +45,7 @@ struct M3 {
   const float *dadt, *dgamma, *dbeta;
   View dx, dz, dBm, dCm, ddd_dt, ddd_A, dtrap, dang;
   float *ddt_bias, *dB_bias, *dC_bias, *dB_norm_w, *dC_norm_w, *dD;
+  int32_t* status;  // device word: a bounded wait that gave up records ZB_ERR_TIMEOUT
   // scratch
   float* segsum;  // [B][H][nseg][NA]   theta segment sums (forward) / theta-gradient segment totals (backward)
   float* dDTl;    // [B][T][H]          backward: DT gradient through theta, within-segment part
@@ -460,53 +462,45 @@ __device__ __forceinline__ void rms_bwd_du(const float (&du)[4], int N, const fl
   }
 }
 
-// Per-head rows of one token that the reverse walk needs from global memory: dq, dk, dkp of the
-// next token (kp[t+1] = k[t]) and theta, copied into a per-warp ring of `depth` slots by cp.async
-// 16-byte copies, several tokens ahead of their use.  Slot layout (bytes): dq | dk | dkp | theta.
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
-               "l"(src)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit_() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int K> __device__ __forceinline__ void cp_async_wait_() { asm volatile("cp.async.wait_group %0;" ::"n"(K) : "memory"); }
+// Per-token rows that the reverse walk needs from global memory, for all heads of the group at
+// once: dq, dk, dkp of the next token (kp[t+1] = k[t]) and theta.  For one token and a run of
+// consecutive heads each is one contiguous block ([B, T, H, N] layout), so one thread moves a
+// token with four bulk copies (cp.async.bulk, completion on the slot's mbarrier) into a ring of
+// kRing slots, kRing - 1 tokens ahead of their use.  Slot layout: dq [hc][N] | dk [hc][N] |
+// dkp [hc][N] (op dtype) | theta [hc][NA] (fp32).
+template <int kRing> constexpr int kRingBars = (kRing + 1) / 2 * 2;  // barriers, padded to 16 bytes
+
+struct RowRing {
+  unsigned char* base;
+  uint64_t* bars;
+  int slot_bytes, row_bytes;  // row_bytes: one [hc][N] block
+};
 
 template <typename TO>
-__device__ __forceinline__ void ring_issue(const M3& p, const TO* dq, const TO* dk, const TO* dkp, int b, int64_t t,
-                                           int h, unsigned char* slot, int lane) {
-  const int rowB = (int)p.N * (int)sizeof(TO), nq = rowB / 16, nth = p.NA * 4 / 16;
-  const int64_t bth = (b * p.T + t) * p.H + h;
-  const unsigned char* srcq = reinterpret_cast<const unsigned char*>(dq + bth * p.N);
-  const unsigned char* srck = reinterpret_cast<const unsigned char*>(dk + bth * p.N);
-  const unsigned char* srcth = reinterpret_cast<const unsigned char*>(p.theta + bth * p.NA);
-  const bool has_next = t + 1 < p.T;
-  const unsigned char* srckp = reinterpret_cast<const unsigned char*>(dkp + (bth + p.H) * p.N);
-  for (int c = lane; c < 3 * nq + nth; c += 32) {
-    unsigned char* dst = slot + 16 * c;
-    if (c < nq) cp_async16(dst, srcq + 16 * c);
-    else if (c < 2 * nq) cp_async16(dst, srck + 16 * (c - nq));
-    else if (c < 3 * nq) {
-      if (has_next) cp_async16(dst, srckp + 16 * (c - 2 * nq));
-      else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
-    } else cp_async16(dst, srcth + 16 * (c - 3 * nq));
-  }
-}
-
-// the lane's four features of a row staged in a ring slot
-template <typename TO>
-__device__ __forceinline__ void slot4(const unsigned char* row, Feat f, float (&v)[4]) {
-  ld4(reinterpret_cast<const TO*>(row), f, v);
+__device__ __forceinline__ void ring_issue_token(const M3& p, const RowRing& R, int slot, int b, int64_t tt, int h0, int hc) {
+  const int64_t bth = (b * p.T + tt) * p.H + h0;
+  const bool has_next = tt + 1 < p.T;
+  const uint32_t th_bytes = (uint32_t)(hc * p.NA * 4);
+  const uint32_t bytes = (uint32_t)R.row_bytes * (has_next ? 3u : 2u) + th_bytes;
+  unsigned char* dst = R.base + (size_t)slot * R.slot_bytes;
+  uint64_t* bar = R.bars + slot;
+  umma::fence_proxy_async_smem();  // the slot's previous contents were read through the generic proxy
+  umma::mbar_arrive_expect_tx(bar, bytes);
+  umma::bulk_load(dst, static_cast<const TO*>(p.dq) + bth * p.N, R.row_bytes, bar);
+  umma::bulk_load(dst + R.row_bytes, static_cast<const TO*>(p.dk) + bth * p.N, R.row_bytes, bar);
+  if (has_next) umma::bulk_load(dst + 2 * R.row_bytes, static_cast<const TO*>(p.dkp) + (bth + p.H) * p.N, R.row_bytes, bar);
+  umma::bulk_load(dst + 3 * R.row_bytes, p.theta + bth * p.NA, th_bytes, bar);
 }
 
 // Reverse walk over one segment: RoPE and RMSNorm backward, bias / norm-weight partial sums,
 // the within-segment suffix of the theta gradient, and the per-token sums over heads (dCm, dBm,
-// ang gradient part) through shared memory.  Warps 0..H-1 own a head each and load their next
-// token's rows one step ahead; warps H, H+1, H+2 only reduce over heads (C rows, B rows, angles),
-// one token behind the head warps, so the two kinds of work overlap.
-// kRing: ring slots (tokens in flight) per head warp; kGrouped: several head groups (p.nhg > 1)
+// the ang and DT gradients' within-segment parts) through shared memory.  Warps 0..hc-1 own a
+// head each; warps hc, hc+1, hc+2 only reduce over heads (C rows, B rows, angles), one token
+// behind the head warps, so the two kinds of work overlap.  Thread 0 feeds the row ring.
+// kRing: ring slots (tokens in flight); kGrouped: several head groups (p.nhg > 1)
 template <typename TI, typename TO, int kRing, bool kGrouped>
 __global__ void __launch_bounds__(1024) m3_prologue_bwd_kernel(const M3 p) {
-  extern __shared__ float smem[];
+  extern __shared__ __align__(16) float smem[];
   const int NA = p.NA, N = (int)p.N, H = (int)p.H;
   Blk k;
   if (kGrouped) {
@@ -522,20 +516,39 @@ __global__ void __launch_bounds__(1024) m3_prologue_bwd_kernel(const M3 p) {
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, h = k.h0 + w;  // h: global head of a head warp
   const int64_t t0 = (int64_t)seg * kSeg;
   const int nt = (int)min((int64_t)kSeg, p.T - t0);
-  // shared: C rows, B rows, angles, RMSNorm factors [kSeg][2], DT [kSeg][hc], then two staging
-  // buffers of (dvq, dvk: hc x N; DT * theta-gradient: hc x NA)
-  float* sC = smem;
+  // shared: ring slots and their mbarriers, then C rows, B rows, angles, RMSNorm factors
+  // [kSeg][2], DT [kSeg][hc], then two staging buffers of (dvq, dvk: hc x N; theta-gradient
+  // suffix sums: hc x (NA + 1))
+  const int es = (int)sizeof(TO);
+  RowRing R;
+  R.row_bytes = hc * N * es;
+  R.slot_bytes = 3 * R.row_bytes + hc * NA * 4;
+  R.base = reinterpret_cast<unsigned char*>(smem);
+  R.bars = reinterpret_cast<uint64_t*>(R.base + (size_t)kRing * R.slot_bytes);
+  float* sC = reinterpret_cast<float*>(R.bars + kRingBars<kRing>);
   float* sB = sC + kSeg * N;
   float* sA = sB + kSeg * N;
   float* sR = sA + kSeg * NA;
   float* sDT = sR + 2 * kSeg;
   float* stage = sDT + kSeg * hc;
-  const int buf_floats = hc * (2 * N + NA);
+  const int NA1 = NA + 1;  // padded: lane h reads head h's row without bank conflicts
+  const int buf_floats = (hc * (2 * N + NA1) + 3) & ~3;  // keeps both buffers 16-byte aligned
+  int uses[kRing] = {};  // thread 0: copies issued into each slot so far
+  if (threadIdx.x == 0) {  // ring barriers, then the first kRing - 1 tokens (nt-1, nt-2, ...)
+    for (int i = 0; i < kRing; ++i) umma::mbar_init(R.bars + i, 1);
+    umma::mbar_fence_init();
+#pragma unroll
+    for (int i = 0; i < kRing - 1; ++i)
+      if (nt - 1 - i >= 0) {
+        ring_issue_token<TO>(p, R, i, b, t0 + nt - 1 - i, k.h0, hc);
+        ++uses[i];
+      }
+  }
   for (int idx = threadIdx.x; idx < nt * hc; idx += blockDim.x) {
     const int t = idx / hc, hh = k.h0 + idx % hc;
     sDT[idx] = softplus20(ldv<float>(p.dd_dt.row<TI>(b, t0 + t, hh)) + p.dt_bias[hh]);
   }
-  stage_rows<TI>(p, b, t0, nt, sC, sB, sA, sR);
+  stage_rows<TI>(p, b, t0, nt, sC, sB, sA, sR);  // ends with a block barrier
   const Feat f = feat(lane, NA);
   float wc[4] = {}, wb[4] = {}, cb[4] = {}, bb[4] = {};
   if (f.on) {
@@ -546,78 +559,65 @@ __global__ void __launch_bounds__(1024) m3_prologue_bwd_kernel(const M3 p) {
       ldp4(p.B_bias + h * N, f, bb);
     }
   }
-  const int64_t HN = (int64_t)H * N, GN = (int64_t)hc * N;
-  const TO* __restrict__ dq = static_cast<const TO*>(p.dq);
-  const TO* __restrict__ dk = static_cast<const TO*>(p.dk);
-  const TO* __restrict__ dkp = static_cast<const TO*>(p.dkp);
+  const int64_t GN = (int64_t)hc * N;
   // reduction roles on the R = min(3, 32 - hc) warps after the group's heads
-  const int R = (int)(blockDim.x >> 5) - hc;
+  const int Rw = (int)(blockDim.x >> 5) - hc;
   const bool head = w < hc;
-  const bool wC = (w == hc), wB = (w == hc + (R >= 2 ? 1 : 0)), wA = (w == hc + (R >= 3 ? 2 : R - 1));
+  const bool wC = (w == hc), wB = (w == hc + (Rw >= 2 ? 1 : 0)), wA = (w == hc + (Rw >= 3 ? 2 : Rw - 1));
   // several groups: the sums over the group's heads go to global memory, m3_rms_bwd_kernel finishes
   float gcb[4] = {}, gbb[4] = {}, gwc[4] = {}, gwb[4] = {};
   float sfx = 0.f;  // theta gradient summed over this segment's tokens >= t
-  // the per-warp row ring: kRing slots of (3 rows of N elements + NA theta floats)
-  const int slotB = 3 * N * (int)sizeof(TO) + NA * 4;
-  unsigned char* ring = reinterpret_cast<unsigned char*>(stage + 2 * buf_floats) + (size_t)w * kRing * slotB;
-  if (head)  // prefill: tokens nt-1 .. nt-kRing+1
-    for (int k = 0; k < kRing - 1; ++k) {
-      if (nt - 1 - k >= 0) ring_issue(p, dq, dk, dkp, b, t0 + nt - 1 - k, h, ring + (size_t)k * slotB, lane);
-      cp_async_commit_();
-    }
+  bool ok = true, aborted = false;
   // head warps compute token nt-1-step at step `step`; reduction warps reduce the token staged
   // at the previous step (one extra step at the end)
   for (int step = 0; step <= nt; ++step) {
-    if (head && step < nt) {
-    const int t = nt - 1 - step;
-    {  // keep kRing - 1 tokens in flight: issue token t - (kRing - 1), then wait for token t
-      const int ti = t - (kRing - 1);
-      if (ti >= 0) ring_issue(p, dq, dk, dkp, b, t0 + ti, h, ring + (size_t)((step + kRing - 1) % kRing) * slotB, lane);
-      cp_async_commit_();
-      cp_async_wait_<kRing - 1>();
-      __syncwarp();
-    }
-    const unsigned char* slot = ring + (size_t)(step % kRing) * slotB;
-    float* buf = stage + (step & 1) * buf_floats;
-    const int64_t bth = (b * p.T + t0 + t) * H + h;
-    float c[4] = {}, bm[4] = {};
-    const float rc = sR[2 * t], rb = sR[2 * t + 1];
-    float part = 0.f;
-    if (f.on) {
-      ldp4(sC + t * N, f, c);
-      ldp4(sB + t * N, f, bm);
-      const int rowB = N * (int)sizeof(TO);
-      float sn, cs;
-      sincosf(reinterpret_cast<const float*>(slot + 3 * rowB)[lane], &sn, &cs);
-      float uq[4], oq[4], uk[4], ok[4];
-      norm_bias_rope(c, rc, wc, cb, sn, cs, uq, oq);
-      norm_bias_rope(bm, rb, wb, bb, sn, cs, uk, ok);
-      float gq[4], gk[4], gkp[4];
-      slot4<TO>(slot, f, gq);
-      slot4<TO>(slot + rowB, f, gk);
-      slot4<TO>(slot + 2 * rowB, f, gkp);
+    if (threadIdx.x == 0 && step < nt) {  // keep kRing - 1 tokens in flight (the slot was freed by the last barrier)
+      const int ti = nt - 1 - step - (kRing - 1);
+      if (ti >= 0) {
+        const int sl = (step + kRing - 1) % kRing;
+        ring_issue_token<TO>(p, R, sl, b, t0 + ti, k.h0, hc);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) gk[j] += gkp[j];
-      // rope backward: rotate the gradient back; d theta from the rotated outputs
-      const float dvq[4] = {gq[0] * cs + gq[1] * sn, -gq[0] * sn + gq[1] * cs, gq[2], gq[3]};
-      const float dvk[4] = {gk[0] * cs + gk[1] * sn, -gk[0] * sn + gk[1] * cs, gk[2], gk[3]};
-      sfx += (gq[1] * oq[0] - gq[0] * oq[1]) + (gk[1] * ok[0] - gk[0] * ok[1]);
-      part = sfx * sA[t * NA + lane];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        gcb[j] += dvq[j];
-        gbb[j] += dvk[j];
+        for (int i = 0; i < kRing; ++i) uses[i] += (i == sl);
       }
-      float* bq = buf + w * N;
-      float* bk = buf + GN + w * N;
-      *reinterpret_cast<float2*>(bq + f.f0) = make_float2(dvq[0], dvq[1]);
-      *reinterpret_cast<float2*>(bq + f.f2) = make_float2(dvq[2], dvq[3]);
-      *reinterpret_cast<float2*>(bk + f.f0) = make_float2(dvk[0], dvk[1]);
-      *reinterpret_cast<float2*>(bk + f.f2) = make_float2(dvk[2], dvk[3]);
-      buf[2 * GN + w * NA + lane] = sDT[t * hc + w] * sfx;
     }
-    part = warp_sum(part);
-    if (lane == 0) p.dDTl[bth] = part;
+    if (head && step < nt) {
+      const int t = nt - 1 - step;
+      ok = umma::mbar_wait(R.bars + step % kRing, (uint32_t)((step / kRing) & 1), p.status);
+      const unsigned char* slot = R.base + (size_t)(step % kRing) * R.slot_bytes;
+      float* buf = stage + (step & 1) * buf_floats;
+      float c[4] = {}, bm[4] = {};
+      const float rc = sR[2 * t], rb = sR[2 * t + 1];
+      if (f.on && ok) {
+        ldp4(sC + t * N, f, c);
+        ldp4(sB + t * N, f, bm);
+        float sn, cs;
+        sincosf(reinterpret_cast<const float*>(slot + 3 * R.row_bytes)[w * NA + lane], &sn, &cs);
+        float uq[4], oq[4], uk[4], ok4[4];
+        norm_bias_rope(c, rc, wc, cb, sn, cs, uq, oq);
+        norm_bias_rope(bm, rb, wb, bb, sn, cs, uk, ok4);
+        float gq[4], gk[4], gkp[4] = {0.f, 0.f, 0.f, 0.f};
+        ld4(reinterpret_cast<const TO*>(slot) + w * N, f, gq);
+        ld4(reinterpret_cast<const TO*>(slot + R.row_bytes) + w * N, f, gk);
+        if (t0 + t + 1 < p.T) ld4(reinterpret_cast<const TO*>(slot + 2 * R.row_bytes) + w * N, f, gkp);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) gk[j] += gkp[j];
+        // rope backward: rotate the gradient back; d theta from the rotated outputs
+        const float dvq[4] = {gq[0] * cs + gq[1] * sn, -gq[0] * sn + gq[1] * cs, gq[2], gq[3]};
+        const float dvk[4] = {gk[0] * cs + gk[1] * sn, -gk[0] * sn + gk[1] * cs, gk[2], gk[3]};
+        sfx += (gq[1] * oq[0] - gq[0] * oq[1]) + (gk[1] * ok4[0] - gk[0] * ok4[1]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          gcb[j] += dvq[j];
+          gbb[j] += dvk[j];
+        }
+        float* bq = buf + w * N;
+        float* bk = buf + GN + w * N;
+        *reinterpret_cast<float2*>(bq + f.f0) = make_float2(dvq[0], dvq[1]);
+        *reinterpret_cast<float2*>(bq + f.f2) = make_float2(dvq[2], dvq[3]);
+        *reinterpret_cast<float2*>(bk + f.f0) = make_float2(dvk[0], dvk[1]);
+        *reinterpret_cast<float2*>(bk + f.f2) = make_float2(dvk[2], dvk[3]);
+        buf[2 * GN + w * NA1 + lane] = sfx;
+      }
     } else if (!head && step > 0) {
       // per-token sums over heads in head order, then the RMSNorm backward of Cm / Bm
       const int t = nt - step;  // the token the head warps staged at step - 1
@@ -645,18 +645,36 @@ __global__ void __launch_bounds__(1024) m3_prologue_bwd_kernel(const M3 p) {
           if (f.on) st4(p.dBm.wrow<TI>(b, t0 + t, 0), f, gx, p.pairs);
         }
       }
-      if (wA && lane < NA) {
-        float s = 0.f;
-        for (int hh = 0; hh < hc; ++hh) s += buf[2 * GN + hh * NA + lane];
-        p.dangl[gbt * NA + lane] = s;
+      if (wA) {
+        const float* sf = buf + 2 * GN;  // [hc][NA1] theta-gradient suffix sums
+        if (lane < NA) {  // ang gradient, within-segment part: sum_h DT[t][h] sfx[h][i]
+          float s = 0.f;
+          for (int hh = 0; hh < hc; ++hh) s += sDT[t * hc + hh] * sf[hh * NA1 + lane];
+          p.dangl[gbt * NA + lane] = s;
+        }
+        if (lane < hc) {  // DT gradient through theta, within-segment part: sum_i sfx[h][i] ang[t][i]
+          float s = 0.f;
+          for (int i = 0; i < NA; ++i) s += sf[lane * NA1 + i] * sA[t * NA + i];
+          p.dDTl[(b * p.T + t0 + t) * H + k.h0 + lane] = s;
+        }
       }
     }
-    __syncthreads();
+    if (__syncthreads_or(!ok)) {  // a ring wait gave up (status recorded): stop every warp
+      aborted = true;
+      break;
+    }
+  }
+  if (aborted) {  // let the copies in flight land (bounded waits on each slot's last use), then leave
+    if (threadIdx.x == 0)
+#pragma unroll
+      for (int i = 0; i < kRing; ++i)
+        if (uses[i] > 0) umma::mbar_wait(R.bars + i, (uint32_t)((uses[i] - 1) & 1), p.status);
+    return;
   }
   if (head && f.on) {
     p.segsum[((b * H + h) * p.nseg + seg) * NA + lane] = sfx;
     const int64_t pb = ((int64_t)(b * p.nseg + seg) * H + h) * N;
-    const int64_t part1 = (int64_t)p.B * p.nseg * HN;
+    const int64_t part1 = (int64_t)p.B * p.nseg * H * N;
     float* pB = p.pbias + pb;
     float* pC = p.pbias + part1 + pb;
     pB[f.f0] = gbb[0]; pB[f.f0 + 1] = gbb[1]; pB[f.f2] = gbb[2]; pB[f.f2 + 1] = gbb[3];
@@ -1010,7 +1028,7 @@ int check(const zb_m3_args* a) {
     return ZB_ERR_LAYOUT;
   if (!a->workspace || a->workspace_bytes < ws_layout(a).total || (reinterpret_cast<uintptr_t>(a->workspace) & 255))
     return ZB_ERR_WORKSPACE;
-  const void* contiguous[] = {a->q, a->k_ext, a->xp, a->y, a->dy, a->dxs, a->dxp, a->dq, a->dk, a->dkp};
+  const void* contiguous[] = {a->q, a->k_ext, a->xp, a->theta, a->y, a->dy, a->dxs, a->dxp, a->dq, a->dk, a->dkp};
   for (const void* c : contiguous)
     if (reinterpret_cast<uintptr_t>(c) & 15) return ZB_ERR_LAYOUT;
   return ZB_OK;
@@ -1051,6 +1069,7 @@ M3 make_m3(const zb_m3_args* a) {
   p.ddd_dt = view_of(a->ddd_dt); p.ddd_A = view_of(a->ddd_A); p.dtrap = view_of(a->dtrap); p.dang = view_of(a->dang);
   p.ddt_bias = a->ddt_bias; p.dB_bias = a->dB_bias; p.dC_bias = a->dC_bias;
   p.dB_norm_w = a->dB_norm_w; p.dC_norm_w = a->dC_norm_w; p.dD = a->dD;
+  p.status = a->status;
   const WsLayout L = ws_layout(a);
   unsigned char* ws = static_cast<unsigned char*>(a->workspace);
   p.segsum = reinterpret_cast<float*>(ws + L.segsum);
@@ -1142,7 +1161,8 @@ extern "C" ZB_API int zb_m3_prologue_bwd(const zb_m3_args* a, void* stream) {
   if (rc) return rc;
   if (!a->theta || !a->dout.ptr || !a->dy || !a->dxs || !a->dxp || !a->dq || !a->dk || !a->dkp || !a->dadt || !a->dgamma ||
       !a->dbeta || !a->dx.ptr || !a->dBm.ptr || !a->dCm.ptr || !a->ddd_dt.ptr || !a->ddd_A.ptr || !a->dtrap.ptr ||
-      !a->dang.ptr || !a->ddt_bias || !a->dB_bias || !a->dC_bias || !a->dB_norm_w || !a->dC_norm_w || !a->dD)
+      !a->dang.ptr || !a->ddt_bias || !a->dB_bias || !a->dC_bias || !a->dB_norm_w || !a->dC_norm_w || !a->dD ||
+      !a->status)
     return ZB_ERR_LAYOUT;
   const M3 p = make_m3(a);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -1150,12 +1170,15 @@ extern "C" ZB_API int zb_m3_prologue_bwd(const zb_m3_args* a, void* stream) {
   // staged rows (C, B: N each; angles; RMSNorm factors; DT per group head) for kSeg tokens, then
   // two staging buffers of (dvq, dvk: hg x N; DT * theta-gradient: hg x NA)
   // plus the per-warp row rings: as many slots (4, 2 or 1) as shared memory allows
+  // ring slots: as many (4, 2 or 1) as shared memory allows
   const int op_es = a->op_dtype == ZB_F32 ? 4 : 2;
-  const size_t base1 = (kSeg * (2 * p.N + p.NA + 2 + p.hg) + 2 * (p.hg * (2 * p.N + p.NA))) * sizeof(float);
+  const size_t buf_floats = (p.hg * (2 * p.N + p.NA + 1) + 3) & ~(size_t)3;
+  const size_t base1 = (kSeg * (2 * p.N + p.NA + 2 + p.hg) + 2 * buf_floats) * sizeof(float);
   const size_t ring1 = (size_t)p.hg * (3 * p.N * op_es + p.NA * 4);
   const size_t kMaxSmem = 227 * 1024;
-  const int ring = base1 + 4 * ring1 <= kMaxSmem ? 4 : base1 + 2 * ring1 <= kMaxSmem ? 2 : 1;
-  const int smem1 = (int)(base1 + ring * ring1);
+  auto need = [&](int r) { return base1 + r * ring1 + 8 * ((r + 1) / 2 * 2); };
+  const int ring = need(4) <= kMaxSmem ? 4 : need(2) <= kMaxSmem ? 2 : 1;
+  const int smem1 = (int)need(ring);
   if ((size_t)smem1 > kMaxSmem) return ZB_ERR_UNSUPPORTED;
   // scalars kernel: thread tid keeps head tid % H, so blockDim is a multiple of H
   const int sthreads = (int)(p.H * (p.H <= 32 ? 32 : 1024 / p.H));

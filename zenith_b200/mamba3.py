@@ -37,7 +37,7 @@ class M3Args(ctypes.Structure):
         + [(n, ctypes.c_void_p) for n in ("dxs", "dxp", "dq", "dk", "dkp", "dadt", "dgamma", "dbeta")]
         + [(n, L.View) for n in ("dx", "dz", "dBm", "dCm", "ddd_dt", "ddd_A", "dtrap", "dang")]
         + [(n, ctypes.c_void_p) for n in ("ddt_bias", "dB_bias", "dC_bias", "dB_norm_w", "dC_norm_w", "dD")]
-        + [("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64)]
+        + [("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64), ("status", ctypes.c_void_p)]
     )
 
 
@@ -90,6 +90,7 @@ def _base_args(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, params, A_floor, eps, op_dt
     a.dd_dt, a.dd_A, a.trap = _scalar_view(dd_dt), _scalar_view(dd_A), _scalar_view(trap)
     for n, t in zip(("dt_bias", "B_bias", "C_bias", "B_norm_w", "C_norm_w", "D"), params):
         setattr(a, n, t.data_ptr())
+    a.status = L.status_word(x.device).data_ptr()
     return a
 
 
