@@ -289,7 +289,9 @@ __global__ void __launch_bounds__(1024) m3_prologue_fwd_kernel(const M3 p) {
   const Feat f = feat(lane, NA);
   if (w < hc && f.on) {
     float th = 0.f;  // theta at the end of the previous segment
-    for (int s = 0; s < seg; ++s) th += p.segsum[((b * H + h) * p.nseg + s) * NA + lane];
+    const float* __restrict__ ss = p.segsum + (int64_t)(b * H + h) * p.nseg * NA + lane;
+#pragma unroll 8
+    for (int s = 0; s < seg; ++s) th += __ldg(ss + (int64_t)s * NA);
     float wc[4], wb[4], cb[4], bb[4];
     ldp4(p.C_norm_w, f, wc);
     ldp4(p.B_norm_w, f, wb);
@@ -761,14 +763,15 @@ __global__ void __launch_bounds__(256) m3_rms_bwd_kernel(const M3 p) {
 // multiple of H), so its dt_bias partial sum has a fixed head.
 template <typename TI>
 __global__ void __launch_bounds__(1024) m3_scalars_bwd_kernel(const M3 p) {
-  extern __shared__ float smem[];  // sA [kSeg][NA] | sC [H][NA] | sDT [kSeg][H] | sacc [blockDim]
+  extern __shared__ float smem[];  // sA [kSeg][NA] | sC [H][NA + 1] | sDT [kSeg][H] | sacc [blockDim]
   const int b = blockIdx.x / p.nseg, seg = blockIdx.x % p.nseg;
   const int NA = p.NA, H = (int)p.H;
   const int64_t t0 = (int64_t)seg * kSeg;
   const int nt = (int)min((int64_t)kSeg, p.T - t0);
+  const int NA1 = NA + 1;  // padded rows: the (token, head) walk below reads them without bank conflicts
   float* sA = smem;
   float* sC = sA + kSeg * NA;
-  float* sDT = sC + H * NA;
+  float* sDT = sC + H * NA1;
   float* sacc = sDT + kSeg * H;
   for (int idx = threadIdx.x; idx < H * NA; idx += blockDim.x) {  // theta gradient over all later segments
     const int hh = idx / NA, i = idx % NA;
@@ -776,7 +779,7 @@ __global__ void __launch_bounds__(1024) m3_scalars_bwd_kernel(const M3 p) {
     float C = 0.f;
 #pragma unroll 8
     for (int s = seg + 1; s < p.nseg; ++s) C += __ldg(src + (int64_t)s * NA);
-    sC[idx] = C;
+    sC[hh * NA1 + i] = C;
   }
   for (int idx = threadIdx.x; idx < nt * NA; idx += blockDim.x)
     sA[idx] = ldv<float>(p.ang.row<TI>(b, t0 + idx / NA, 0) + idx % NA);
@@ -789,7 +792,7 @@ __global__ void __launch_bounds__(1024) m3_scalars_bwd_kernel(const M3 p) {
     const Disc d = discretise(ldv<float>(p.dd_dt.row<TI>(b, tt, hh)), ddA, ldv<float>(p.trap.row<TI>(b, tt, hh)),
                               p.dt_bias[hh], p.A_floor);
     float carry = 0.f;
-    for (int i = 0; i < NA; ++i) carry += sC[hh * NA + i] * sA[t * NA + i];
+    for (int i = 0; i < NA; ++i) carry += sC[hh * NA1 + i] * sA[t * NA + i];
     sDT[t * H + hh] = d.DT;
     const float ga = p.dadt[bth], gg = p.dgamma[bth], gb = p.dbeta[bth];
     const float g_adt = ga + gb * d.beta;  // beta = (1 - tr) DT e^{adt}
@@ -819,7 +822,7 @@ __global__ void __launch_bounds__(1024) m3_scalars_bwd_kernel(const M3 p) {
     const int t = idx / NA, i = idx % NA;
     float s = p.dangl[(b * p.T + t0 + t) * NA + i];
     for (int g = 1; g < p.nhg; ++g) s += p.dangl[g * gstride + (b * p.T + t0 + t) * NA + i];
-    for (int hh = 0; hh < H; ++hh) s += sDT[t * H + hh] * sC[hh * NA + i];
+    for (int hh = 0; hh < H; ++hh) s += sDT[t * H + hh] * sC[hh * NA1 + i];
     stv<float>(p.dang.wrow<TI>(b, t0 + t, 0) + i, s);
   }
 }
@@ -1182,7 +1185,7 @@ extern "C" ZB_API int zb_m3_prologue_bwd(const zb_m3_args* a, void* stream) {
   if ((size_t)smem1 > kMaxSmem) return ZB_ERR_UNSUPPORTED;
   // scalars kernel: thread tid keeps head tid % H, so blockDim is a multiple of H
   const int sthreads = (int)(p.H * (p.H <= 32 ? 32 : 1024 / p.H));
-  const int smem2 = (int)((kSeg * p.NA + p.H * p.NA + kSeg * p.H + sthreads) * sizeof(float));
+  const int smem2 = (int)((kSeg * p.NA + p.H * (p.NA + 1) + kSeg * p.H + sthreads) * sizeof(float));
   ZB_M3_DISPATCH(a->io_dtype, a->op_dtype, {
     auto k1 = p.nhg > 1 ? (ring == 4   ? m3_prologue_bwd_kernel<TI, TO, 4, true>
                            : ring == 2 ? m3_prologue_bwd_kernel<TI, TO, 2, true>
