@@ -36,8 +36,9 @@ typedef struct {
      C_norm_w [N], D [H] */
   const float *dt_bias, *B_bias, *C_bias, *B_norm_w, *C_norm_w, *D;
   /* scan operands written by the prologue, contiguous: q [B,T,H,N]; k_ext [B,T+1,H,N] (rows
-     1..T are k, rows 0..T-1 are kp); xp [B,T,H,P]; adt, gamma, beta fp32 [B,T,H]; theta fp32
-     [B,T,H,N/4] (kept for the backward) */
+     1..T are k, rows 0..T-1 are kp); xp [B,T,H,P], or NULL when the scan reads x one token
+     earlier itself (ZB_FLAG_SHIFTED); adt, gamma, beta fp32 [B,T,H]; theta fp32 [B,T,H,N/4]
+     (kept for the backward) */
   void *q, *k_ext, *xp;
   float *adt, *gamma, *beta, *theta;
   /* scan output y (contiguous [B,T,H,P]) and the layer output out [B,T,H,P] (view) */

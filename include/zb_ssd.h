@@ -58,6 +58,9 @@ typedef struct {
 
 /* flags */
 #define ZB_FLAG_STATE_ONLY 1  /* forward: only the final state (no y);  backward: only dinitial_state */
+#define ZB_FLAG_SHIFTED 2     /* xp and kp are x and k one token later (xp[t] = x[t-1], zero at t = 0), as
+                                 Mamba3.forward builds them (zenith/mamba3.py:115-116): the kernels read x and k
+                                 at t - 1 and the xp / kp views are ignored.  No segmentation. */
 
 typedef struct {
   int64_t B, T, H, G, P, N;

@@ -205,3 +205,38 @@ def test_fused_layer_head_groups(H, P, scan_dtype):
     for n in ALL:
         if ref["d" + n].abs().max() > 0:
             assert max_rel_err(grads["d" + n], ref["d" + n]) < tol, (n, max_rel_err(grads["d" + n], ref["d" + n]))
+
+
+@pytest.mark.parametrize("dtype,P,N", [(torch.bfloat16, 64, 128), (torch.float32, 16, 32)])
+def test_shifted_flag_matches_explicit_shifted_operands(dtype, P, N):
+    """ZB_FLAG_SHIFTED (xp / kp read as x / k one token earlier, what the layer body uses) gives
+    bitwise the same y and gradients as passing the shifted tensors explicitly, on the tensor-core
+    (bf16) and SIMT (fp32) paths."""
+    from zenith_b200 import mamba3 as m3
+    from zenith_b200.ssd import ssd_bwd_op, ssd_fwd_op
+
+    g = torch.Generator().manual_seed(31)
+    B, T, H = 2, 256, 4
+    dev = torch.device("cuda")
+    x = torch.randn(B, T, H, P, generator=g).to(dev, dtype)
+    q = (torch.randn(B, T, H, N, generator=g) / N ** 0.5).to(dev, dtype)
+    k = (torch.randn(B, T, H, N, generator=g) / N ** 0.5).to(dev, dtype)
+    adt = (-0.1 * torch.rand(B, T, H, generator=g)).to(dev)
+    gamma, beta = (0.1 * torch.rand(2, B, T, H, generator=g)).to(dev)
+    dy = torch.randn(B, T, H, P, generator=g).to(dev, dtype)
+    shift = lambda t: torch.cat((torch.zeros_like(t[:, :1]), t[:, :-1]), dim=1)  # noqa: E731
+    y1, st1 = m3._scan_fwd(x, q, k, adt, gamma, beta, 64, True)
+    y0, _, st0 = ssd_fwd_op(x, q, k, shift(k), shift(x), adt, gamma, beta, 64, None, True, False)
+    g1 = m3._scan_bwd(dy, x, q, k, adt, gamma, beta, st1, 64)
+    g0 = ssd_bwd_op(dy, x, q, k, shift(k), shift(x), adt, gamma, beta, st0, 64, None, None, False)[:8]
+    torch.cuda.synchronize()
+    zenith_b200_check()
+    assert torch.equal(y1, y0)
+    for a, b in zip(g1, g0):
+        assert torch.equal(a, b)
+
+
+def zenith_b200_check():
+    import zenith_b200
+
+    zenith_b200.check_status()

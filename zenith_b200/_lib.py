@@ -16,6 +16,7 @@ LIB_PATH = pathlib.Path(__file__).resolve().parent / "libzenith_ssd.so"
 
 ZB_F32, ZB_BF16, ZB_F16, ZB_F64 = 0, 1, 2, 3
 ZB_FLAG_STATE_ONLY = 1
+ZB_FLAG_SHIFTED = 2  # xp / kp are x / k one token later: the kernels read x / k at t - 1
 ZB_ERR_SHAPE, ZB_ERR_TIMEOUT, ZB_ERR_SCRATCH_LIMIT = 1, 5, 8
 ZB_NOALLOC_SCRATCH_BYTES = 32 << 20
 

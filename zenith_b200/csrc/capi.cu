@@ -122,6 +122,15 @@ int make_plan(const zb_ssd_args* a, Plan* pl, bool stateless_forward) {
 
 View to_view(const zb_view& v) { return View{v.ptr, v.sb, v.st, v.sh}; }
 
+// ZB_FLAG_SHIFTED: xp / kp are read from x / k one token earlier; give them x's and k's views
+const zb_ssd_args* unshift(const zb_ssd_args* a, zb_ssd_args* tmp) {
+  if (!a || !(a->flags & ZB_FLAG_SHIFTED)) return a;
+  *tmp = *a;
+  tmp->kp = tmp->k;
+  tmp->xp = tmp->x;
+  return tmp;
+}
+
 SimtParams simt_params(const zb_ssd_args* a, const Plan& pl) {
   SimtParams p;
   memset(&p, 0, sizeof(p));
@@ -186,7 +195,9 @@ const char* zb_strerror(int s) {
 
 const char* zb_last_cuda_error(void) { return g_cuda_err; }
 
-size_t zb_ssd_states_bytes(const zb_ssd_args* a) {
+size_t zb_ssd_states_bytes(const zb_ssd_args* a_) {
+  zb_ssd_args tmp_;
+  const zb_ssd_args* a = unshift(a_, &tmp_);
   if (validate(a, false) != ZB_OK && validate(a, true) != ZB_OK) {
     // shape/dtype check only: pointers may be unset when sizing
     if (!a || a->B <= 0 || a->T <= 0 || a->H <= 0 || a->G <= 0 || a->P <= 0 || a->N <= 0) return 0;
@@ -222,7 +233,7 @@ constexpr int kSegMinChunks = 4;         // and at least four chunks per chain
 bool batch_contiguous(const zb_view& v, int64_t T) { return v.sb == T * v.st; }
 
 int segments_for(const zb_ssd_args* a, const Plan& pl) {
-  if (pl.kind != kTc) return 1;
+  if (pl.kind != kTc || (a->flags & ZB_FLAG_SHIFTED)) return 1;  // a segment's row -1 is not zero
   const int64_t chains = a->B * a->H;
   if (chains >= 148) return 1;
   const zb_view* v[] = {&a->x, &a->q, &a->k, &a->kp, &a->xp, &a->adt, &a->gamma, &a->beta};
@@ -396,7 +407,9 @@ int launch_total_decay(const zb_ssd_args* a, float* out, cudaStream_t s) {
 }
 }  // namespace
 
-size_t zb_ssd_workspace_bytes(const zb_ssd_args* a, int backward) {
+size_t zb_ssd_workspace_bytes(const zb_ssd_args* a_, int backward) {
+  zb_ssd_args tmp_;
+  const zb_ssd_args* a = unshift(a_, &tmp_);
   if (!a || a->B <= 0 || a->T <= 0 || a->H <= 0 || a->G <= 0 || a->P <= 0 || a->N <= 0) return 0;
   if (a->chunk_size <= 0 || a->T % a->chunk_size || a->H % a->G) return 0;
   if (!dtype_size(a->dtype) || !dtype_size(a->scalar_dtype)) return 0;
@@ -415,7 +428,9 @@ size_t zb_ssd_workspace_bytes(const zb_ssd_args* a, int backward) {
   return need;
 }
 
-int zb_ssd_fwd(const zb_ssd_args* a, void* stream_) {
+int zb_ssd_fwd(const zb_ssd_args* a_, void* stream_) {
+  zb_ssd_args tmp_;
+  const zb_ssd_args* a = unshift(a_, &tmp_);
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   int rc = validate(a, false);
   if (rc) return rc;
@@ -447,7 +462,9 @@ int zb_ssd_fwd(const zb_ssd_args* a, void* stream_) {
   return rc;
 }
 
-int zb_ssd_bwd(const zb_ssd_args* a, void* stream_) {
+int zb_ssd_bwd(const zb_ssd_args* a_, void* stream_) {
+  zb_ssd_args tmp_;
+  const zb_ssd_args* a = unshift(a_, &tmp_);
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   int rc = validate(a, true);
   if (rc) return rc;
@@ -521,7 +538,9 @@ int zb_ssd_check_status(const int32_t* status, void* stream) {
 
 uint64_t zb_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
-int zb_ssd_kernel_family(const zb_ssd_args* a, int states_saved) {
+int zb_ssd_kernel_family(const zb_ssd_args* a_, int states_saved) {
+  zb_ssd_args tmp_;
+  const zb_ssd_args* a = unshift(a_, &tmp_);
   if (!a || a->B <= 0 || a->T <= 0 || a->H <= 0 || a->G <= 0 || a->P <= 0 || a->N <= 0) return -1;
   if (a->chunk_size <= 0 || a->T % a->chunk_size || a->H % a->G) return -1;
   if (!dtype_size(a->dtype) || !dtype_size(a->scalar_dtype)) return -1;

@@ -317,9 +317,11 @@ __global__ void __launch_bounds__(1024) m3_prologue_fwd_kernel(const M3 p) {
       st4(kx + (b * (p.T + 1) + t0 + t + 1) * HN + h * N, f, o);
     }
   }
-  // xp = x one token later (mamba3.py:115), all threads over (token, group head, feature)
+  // xp = x one token later (mamba3.py:115), all threads over (token, group head, feature); not
+  // needed (NULL) when the scan reads x one token earlier itself (ZB_FLAG_SHIFTED)
   TO* __restrict__ xp = static_cast<TO*>(p.xp);
   const int HP = H * P, GP = hc * P;
+  if (!xp) return;
   if (p.vec8) {
     const int GP8 = GP / 8, P8 = P / 8;
     for (int idx = threadIdx.x; idx < nt * GP8; idx += blockDim.x) {
@@ -1111,7 +1113,7 @@ extern "C" ZB_API uint64_t zb_m3_workspace_bytes(const zb_m3_args* a) { return a
 extern "C" ZB_API int zb_m3_prologue_fwd(const zb_m3_args* a, void* stream) {
   int rc = check(a);
   if (rc) return rc;
-  if (!a->q || !a->k_ext || !a->xp || !a->adt || !a->gamma || !a->beta || !a->theta || !a->Bm.ptr || !a->Cm.ptr ||
+  if (!a->q || !a->k_ext || !a->adt || !a->gamma || !a->beta || !a->theta || !a->Bm.ptr || !a->Cm.ptr ||
       !a->dd_dt.ptr || !a->dd_A.ptr || !a->trap.ptr || !a->ang.ptr)
     return ZB_ERR_LAYOUT;
   const M3 p = make_m3(a);

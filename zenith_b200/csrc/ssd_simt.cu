@@ -64,6 +64,7 @@ __global__ void __launch_bounds__(kThreads) ssd_fwd_simt_kernel(const SimtParams
   const int j = u.chunk;
   const int64_t bh = u.bh, b = u.b, h = u.h, g = u.g;
   const int64_t t0 = (int64_t)j * L;
+  const int sh = (p.flags & ZB_FLAG_SHIFTED) ? 1 : 0;  // xp / kp = x / k one token later
   const int Lc = (int)min((int64_t)L, p.T - t0);
   int* flags = p.sync.flags + bh * (p.nc + 1);
 
@@ -85,14 +86,14 @@ __global__ void __launch_bounds__(kThreads) ssd_fwd_simt_kernel(const SimtParams
     const int t = i / N, n = i % N;
     const bool v = t < Lc;
     s_k[t * N1 + n] = v ? ldv<TA>(p.k.row<TI>(b, t0 + t, g) + n) : TA(0);
-    s_kp[t * N1 + n] = v ? ldv<TA>(p.kp.row<TI>(b, t0 + t, g) + n) : TA(0);
+    s_kp[t * N1 + n] = v && t0 + t >= sh ? ldv<TA>(p.kp.row<TI>(b, t0 + t - sh, g) + n) : TA(0);
     if (!state_only) s_q[t * N1 + n] = v ? ldv<TA>(p.q.row<TI>(b, t0 + t, g) + n) : TA(0);
   }
   for (int i = tid; i < L * P; i += kThreads) {
     const int t = i / P, pp = i % P;
     const bool v = t < Lc;
     s_x[t * P1 + pp] = v ? ldv<TA>(p.x.row<TI>(b, t0 + t, h) + pp) : TA(0);
-    s_xp[t * P1 + pp] = v ? ldv<TA>(p.xp.row<TI>(b, t0 + t, h) + pp) : TA(0);
+    s_xp[t * P1 + pp] = v && t0 + t >= sh ? ldv<TA>(p.xp.row<TI>(b, t0 + t - sh, h) + pp) : TA(0);
   }
   __syncthreads();
   const TA cl = s_c[Lc - 1];
@@ -223,6 +224,7 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
   const int j = p.nc - 1 - u.chunk;
   const int64_t bh = u.bh, b = u.b, h = u.h, g = u.g;
   const int64_t t0 = (int64_t)j * L;
+  const int sh = (p.flags & ZB_FLAG_SHIFTED) ? 1 : 0;  // xp / kp = x / k one token later
   const int Lc = (int)min((int64_t)L, p.T - t0);
   int* flags = p.sync.flags + bh * (p.nc + 1);
   const int64_t PN = (int64_t)P * N;
@@ -252,7 +254,7 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
     s_q[t * N1 + n] = v ? ldv<TA>(p.q.row<TI>(b, t0 + t, g) + n) : TA(0);
     if (!state_only) {
       s_k[t * N1 + n] = v ? ldv<TA>(p.k.row<TI>(b, t0 + t, g) + n) : TA(0);
-      s_kp[t * N1 + n] = v ? ldv<TA>(p.kp.row<TI>(b, t0 + t, g) + n) : TA(0);
+      s_kp[t * N1 + n] = v && t0 + t >= sh ? ldv<TA>(p.kp.row<TI>(b, t0 + t - sh, g) + n) : TA(0);
     }
   }
   for (int i = tid; i < L * P; i += kThreads) {
@@ -261,7 +263,7 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
     s_dy[t * P1 + pp] = v ? ldv<TA>(p.dy.row<TI>(b, t0 + t, h) + pp) : TA(0);
     if (!state_only) {
       s_x[t * P1 + pp] = v ? ldv<TA>(p.x.row<TI>(b, t0 + t, h) + pp) : TA(0);
-      s_xp[t * P1 + pp] = v ? ldv<TA>(p.xp.row<TI>(b, t0 + t, h) + pp) : TA(0);
+      s_xp[t * P1 + pp] = v && t0 + t >= sh ? ldv<TA>(p.xp.row<TI>(b, t0 + t - sh, h) + pp) : TA(0);
     }
   }
   const TA* states_bh = reinterpret_cast<const TA*>(p.chain) + bh * (int64_t)(p.nc + 1) * PN;

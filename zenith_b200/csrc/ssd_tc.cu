@@ -68,6 +68,7 @@ struct TcFwdParams {
   unsigned int* ticket;
   int* flags;             // [B*H][nc+1]
   int32_t* status;
+  int shift;              // 1: tkp / txp map k / x, read one token earlier (row -1 is out of range: zeros)
 };
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
@@ -86,13 +87,13 @@ __device__ __forceinline__ void fwd_load_kk(const TcFwdParams& p, unsigned char*
 #pragma unroll
   for (int qb = 0; qb < NS / 64; ++qb) {
     umma::tma_load_4d(sKK + qb * 16384, &p.tk, bar, qb * 64, u.g, t0, u.b);
-    umma::tma_load_4d(sKK + qb * 16384 + 8192, &p.tkp, bar, qb * 64, u.g, t0, u.b);
+    umma::tma_load_4d(sKK + qb * 16384 + 8192, &p.tkp, bar, qb * 64, u.g, t0 - p.shift, u.b);
   }
 }
 __device__ __forceinline__ void fwd_load_x(const TcFwdParams& p, unsigned char* sX, unsigned char* sXp, uint64_t* bar,
                                            const UnitIdx& u) {
   umma::tma_load_4d(sX, &p.tx, bar, 0, u.h, u.chunk * kL, u.b);
-  umma::tma_load_4d(sXp, &p.txp, bar, 0, u.h, u.chunk * kL, u.b);
+  umma::tma_load_4d(sXp, &p.txp, bar, 0, u.h, u.chunk * kL - p.shift, u.b);
 }
 template <int NS>
 __device__ __forceinline__ void fwd_load_q(const TcFwdParams& p, unsigned char* sQ, uint64_t* bar, const UnitIdx& u) {
@@ -511,6 +512,7 @@ struct TcBwdParams {
   unsigned int* ticket;
   int* flags;
   int32_t* status;
+  int shift;  // as in TcFwdParams
 };
 
 constexpr int kBwdThreads = 512;
@@ -610,10 +612,10 @@ __device__ __forceinline__ void bwd_issue_loads(const TcBwdParams& p, unsigned c
   for (int qb = 0; qb < S::QB; ++qb) {
     umma::tma_load_4d(st + S::Q + qb * 8192, &p.tq, bar, qb * 64, c.g, c.t0, c.b);
     umma::tma_load_4d(st + S::KK + qb * 16384, &p.tk, bar, qb * 64, c.g, c.t0, c.b);
-    umma::tma_load_4d(st + S::KK + qb * 16384 + 8192, &p.tkp, bar, qb * 64, c.g, c.t0, c.b);
+    umma::tma_load_4d(st + S::KK + qb * 16384 + 8192, &p.tkp, bar, qb * 64, c.g, c.t0 - p.shift, c.b);
   }
   umma::tma_load_4d(st + S::XX, &p.tx, bar, 0, c.h, c.t0, c.b);
-  umma::tma_load_4d(st + S::XX + 8192, &p.txp, bar, 0, c.h, c.t0, c.b);
+  umma::tma_load_4d(st + S::XX + 8192, &p.txp, bar, 0, c.h, c.t0 - p.shift, c.b);
   umma::tma_load_4d(st + S::DY, &p.tdy, bar, 0, c.h, c.t0, c.b);
   umma::bulk_load(st + S::SIN, reinterpret_cast<const unsigned char*>(p.states) + (c.bh * p.nc + c.j) * (int64_t)NS * 128,
                   NS * 128, bar);
@@ -1147,6 +1149,7 @@ struct TcStateParams {
   unsigned int* ticket;
   int* flags;
   int32_t* status;
+  int shift;           // as in TcFwdParams (t1 / t3 of the forward read one token earlier)
 };
 
 template <int NS, bool BACKWARD>
@@ -1197,10 +1200,10 @@ __global__ void __launch_bounds__(kStThreads) ssd_state_tc_kernel(const __grid_c
 #pragma unroll
       for (int qb = 0; qb < S::QB; ++qb) {
         umma::tma_load_4d(sA + qb * 16384, &p.t0, &bars[0], qb * 64, g, t0, b);
-        umma::tma_load_4d(sA + qb * 16384 + 8192, &p.t1, &bars[0], qb * 64, g, t0, b);
+        umma::tma_load_4d(sA + qb * 16384 + 8192, &p.t1, &bars[0], qb * 64, g, t0 - p.shift, b);
       }
       umma::tma_load_4d(sB0, &p.t2, &bars[0], 0, h, t0, b);
-      umma::tma_load_4d(sB0 + 8192, &p.t3, &bars[0], 0, h, t0, b);
+      umma::tma_load_4d(sB0 + 8192, &p.t3, &bars[0], 0, h, t0 - p.shift, b);
     }
   }
   if (tid < 64) {
@@ -1404,6 +1407,7 @@ int launch_fwd(const zb_ssd_args* a, ChainSync sync, void* states, void* ring, c
   p.ticket = sync.ticket;
   p.flags = sync.flags;
   p.status = a->status;
+  p.shift = (a->flags & ZB_FLAG_SHIFTED) ? 1 : 0;
   auto k = ssd_fwd_tc_kernel<NS>;
   const int smem = (int)FwdSmem<NS>::ALLOC;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return ZB_ERR_CUDA;
@@ -1454,6 +1458,7 @@ int launch_bwd(const zb_ssd_args* a, ChainSync sync, void* ring, cudaStream_t st
   p.ticket = sync.ticket;
   p.flags = sync.flags;
   p.status = a->status;
+  p.shift = (a->flags & ZB_FLAG_SHIFTED) ? 1 : 0;
   auto k = ssd_bwd_tc_kernel<NS>;
   const int smem = (int)BwdSmem<NS>::ALLOC;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return ZB_ERR_CUDA;
@@ -1491,6 +1496,7 @@ int launch_state(const zb_ssd_args* a, ChainSync sync, void* ring, cudaStream_t 
   p.ticket = sync.ticket;
   p.flags = sync.flags;
   p.status = a->status;
+  p.shift = (a->flags & ZB_FLAG_SHIFTED) ? 1 : 0;
   auto k = ssd_state_tc_kernel<NS, BACKWARD>;
   const int smem = (int)StateSmem<NS>::ALLOC;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return ZB_ERR_CUDA;

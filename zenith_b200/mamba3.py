@@ -21,7 +21,7 @@ import torch
 from torch import Tensor
 
 from . import _lib as L
-from .ssd import ssd_bwd_op, ssd_fwd_op
+from .ssd import _build_args
 
 
 class M3Args(ctypes.Structure):
@@ -98,6 +98,45 @@ def _check(rc: int, what: str):
     L.check(rc, what)
 
 
+def _scan_fwd(xs, q, k, adt, gamma, beta, chunk_size, save_states):
+    """The scan with kp / xp read as k / x one token earlier (ZB_FLAG_SHIFTED): no xp tensor."""
+    B, T, H, P = xs.shape
+    N = q.shape[3]
+    dev = xs.device
+    lib = L.lib()
+    a = _build_args(xs, q, k, k, xs, adt, gamma, beta, chunk_size, L.ZB_FLAG_SHIFTED)
+    y = torch.empty(B, T, H, P, dtype=xs.dtype, device=dev)
+    final = torch.empty(B, H, P, N, dtype=torch.float32, device=dev)
+    states = torch.empty(lib.zb_ssd_states_bytes(ctypes.byref(a)) if save_states else 0, dtype=torch.uint8, device=dev)
+    ws = torch.empty(max(int(lib.zb_ssd_workspace_bytes(ctypes.byref(a), 0)), 256), dtype=torch.uint8, device=dev)
+    a.y = L.view(y)
+    a.final_state = final.data_ptr()
+    a.states = L.ptr(states)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    a.status = L.status_word(dev).data_ptr()
+    _check(lib.zb_ssd_fwd(ctypes.byref(a), torch.cuda.current_stream(dev).cuda_stream), "zb_ssd_fwd")
+    return y, states
+
+
+def _scan_bwd(dy, xs, q, k, adt, gamma, beta, states, chunk_size):
+    """Backward of ``_scan_fwd``: dx, dq, dk, dkp, dxp, dadt, dgamma, dbeta (kp / xp gradients per token)."""
+    dev = xs.device
+    lib = L.lib()
+    a = _build_args(xs, q, k, k, xs, adt, gamma, beta, chunk_size, L.ZB_FLAG_SHIFTED)
+    grads = [torch.empty(t.shape, dtype=t.dtype, device=dev) for t in (xs, q, k, k, xs, adt, gamma, beta)]
+    for n, g in zip(L._VIEWS_BWD, grads):
+        setattr(a, n, L.view(g))
+    dinit = torch.empty(xs.shape[0], xs.shape[2], xs.shape[3], q.shape[3], dtype=torch.float32, device=dev)
+    ws = torch.empty(max(int(lib.zb_ssd_workspace_bytes(ctypes.byref(a), 1)), 256), dtype=torch.uint8, device=dev)
+    a.dy = L.view(dy)
+    a.states = L.ptr(states)
+    a.dinitial_state = dinit.data_ptr()
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    a.status = L.status_word(dev).data_ptr()
+    _check(lib.zb_ssd_bwd(ctypes.byref(a), torch.cuda.current_stream(dev).cuda_stream), "zb_ssd_bwd")
+    return grads
+
+
 def _layer_fwd(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, params, A_floor, chunk_size, eps, op_dtype, save_states=True):
     """Prologue -> scan -> epilogue.  Returns the output and the tensors the backward needs."""
     B, T, H, P = x.shape
@@ -111,21 +150,18 @@ def _layer_fwd(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, params, A_floor, chunk_size
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     q = torch.empty(B, T, H, N, dtype=op_dtype, device=dev)
     k_ext = torch.empty(B, T + 1, H, N, dtype=op_dtype, device=dev)
-    xp = torch.empty(B, T, H, P, dtype=op_dtype, device=dev)
     adt, gamma, beta = (torch.empty(B, T, H, dtype=torch.float32, device=dev) for _ in range(3))
     theta = torch.empty(B, T, H, N // 4, dtype=torch.float32, device=dev)
-    for n, t in (("q", q), ("k_ext", k_ext), ("xp", xp), ("adt", adt), ("gamma", gamma), ("beta", beta),
-                 ("theta", theta)):
+    for n, t in (("q", q), ("k_ext", k_ext), ("adt", adt), ("gamma", gamma), ("beta", beta), ("theta", theta)):
         setattr(a, n, t.data_ptr())
     stream = torch.cuda.current_stream(dev).cuda_stream
     _check(lib.zb_m3_prologue_fwd(ctypes.byref(a), stream), "zb_m3_prologue_fwd")
     xs = x if x.dtype == op_dtype else x.to(op_dtype)
-    k, kp = k_ext[:, 1:], k_ext[:, :-1]
-    y, _, states = ssd_fwd_op(xs, q, k, kp, xp, adt, gamma, beta, chunk_size, None, save_states, False)
+    y, states = _scan_fwd(xs, q, k_ext[:, 1:], adt, gamma, beta, chunk_size, save_states)
     out = torch.empty(B, T, H, P, dtype=x.dtype, device=dev)
     a.y, a.out = y.data_ptr(), _v(out)
     _check(lib.zb_m3_epilogue_fwd(ctypes.byref(a), stream), "zb_m3_epilogue_fwd")
-    return out, (xs, q, k_ext, xp, adt, gamma, beta, theta, y, states)
+    return out, (xs, q, k_ext, adt, gamma, beta, theta, y, states)
 
 
 def _layer_bwd(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, params, scan_saved, A_floor, chunk_size, eps, op_dtype, dout,
@@ -133,7 +169,7 @@ def _layer_bwd(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, params, scan_saved, A_floor
     """Epilogue backward -> scan backward -> prologue backward.  ``grads_in`` maps dx, dz, dBm,
     dCm, ddd_dt, ddd_A, dtrap, dang to the tensors (or views) to write; returns the parameter
     gradients (fp32, in the order of ``params``)."""
-    xs, q, k_ext, xp, adt, gamma, beta, theta, y, states = scan_saved
+    xs, q, k_ext, adt, gamma, beta, theta, y, states = scan_saved
     B, T, H, P = x.shape
     dev = x.device
     dout = dout.to(x.dtype)
@@ -143,17 +179,16 @@ def _layer_bwd(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, params, scan_saved, A_floor
     a = _base_args(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, params, A_floor, eps, op_dtype)
     ws = torch.empty(max(int(lib.zb_m3_workspace_bytes(ctypes.byref(a))), 256), dtype=torch.uint8, device=dev)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
-    for n, t in (("q", q), ("k_ext", k_ext), ("xp", xp), ("adt", adt), ("gamma", gamma), ("beta", beta),
-                 ("theta", theta), ("y", y)):
+    for n, t in (("q", q), ("k_ext", k_ext), ("adt", adt), ("gamma", gamma), ("beta", beta), ("theta", theta),
+                 ("y", y)):
         setattr(a, n, t.data_ptr())
     a.dout = _v(dout)
     dy = torch.empty(B, T, H, P, dtype=op_dtype, device=dev)
     a.dy, a.dz = dy.data_ptr(), _v(grads_in["dz"] if z is not None else None)
     stream = torch.cuda.current_stream(dev).cuda_stream
     _check(lib.zb_m3_epilogue_bwd(ctypes.byref(a), stream), "zb_m3_epilogue_bwd")
-    k, kp = k_ext[:, 1:], k_ext[:, :-1]
-    dxs, dq, dk, dkp, dxp, dadt, dgamma, dbeta, _ = ssd_bwd_op(dy, xs, q, k, kp, xp, adt, gamma, beta, states,
-                                                              chunk_size, None, None, False)
+    dxs, dq, dk, dkp, dxp, dadt, dgamma, dbeta = _scan_bwd(dy, xs, q, k_ext[:, 1:], adt, gamma, beta, states,
+                                                           chunk_size)
     for n, t in (("dxs", dxs), ("dxp", dxp), ("dq", dq), ("dk", dk), ("dkp", dkp), ("dadt", dadt),
                  ("dgamma", dgamma), ("dbeta", dbeta)):
         setattr(a, n, t.data_ptr())
