@@ -1,7 +1,12 @@
-"""Small fixed workload for profiler captures (ncu): a few forward (saving states) + backward
-calls of the bf16 scan on B sequences of the layer shape (T2048 H24 P64 N128, chunk 64).
+"""Small fixed workloads for profiler captures (ncu).
 
     python -m zenith_b200.profile_case [--batch 2] [--iters 3]
+        a few forward (saving states) + backward calls of the bf16 scan on B sequences of the layer
+        shape (T2048 H24 P64 N128, chunk 64)
+    python -m zenith_b200.profile_case --workload rows [--batch 2] [--heads 48] [--iters 2]
+        the row kernels around it, once per iteration each: the fused Mamba-3 layer body (fwd + bwd,
+        bf16, P64 N128) on B sequences of 2048 tokens, the residual add + RMSNorm (d_model 1536) and
+        the LM head's cross-entropy (vocabulary 32000) on the same B x 2048 tokens
 """
 from __future__ import annotations
 
@@ -21,7 +26,11 @@ def main():
     ap.add_argument("--batch", type=int, default=2)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--seqlen", type=int, default=2048)
+    ap.add_argument("--workload", choices=("scan", "rows"), default="scan")
+    ap.add_argument("--heads", type=int, default=48)
     args = ap.parse_args()
+    if args.workload == "rows":
+        return rows(args)
     s = SsdShape(args.batch, args.seqlen, 24, 64, 128, 24, 64)
     inp = make_inputs(s, seed=0)
     dev = torch.device("cuda")
@@ -31,6 +40,36 @@ def main():
     for _ in range(args.iters):
         _, _, st = ssd_fwd_op(*a, s.chunk, None, True, False)
         ssd_bwd_op(dy, *a, st, s.chunk, None, None, False)
+    torch.cuda.synchronize()
+    zenith_b200.check_status()
+    print("ok")
+
+
+def rows(args):
+    from zenith_b200 import lm
+
+    dev = torch.device("cuda")
+    B, T, H, P, N, D, V = args.batch, args.seqlen, args.heads, 64, 128, 1536, 32000
+    g = torch.Generator().manual_seed(0)
+    mk = lambda *sh: torch.randn(*sh, generator=g)  # noqa: E731
+    n_in = 2 * H * P + 2 * N + 3 * H + N // 4
+    zxbc = mk(B, T, n_in).to(dev, torch.bfloat16).requires_grad_()
+    prm = [(torch.rand(H, generator=g) * -4.0 - 3.0), torch.ones(H, N), torch.ones(H, N), torch.ones(N), torch.ones(N),
+           torch.ones(H)]
+    prm = [t.to(dev).requires_grad_() for t in prm]
+    dout = mk(B, T, H, P).to(dev, torch.bfloat16)
+    resid = mk(B * T, D).to(dev).requires_grad_()
+    delta = mk(B * T, D).to(dev, torch.bfloat16).requires_grad_()
+    w = torch.ones(D, device=dev, requires_grad=True)
+    h = mk(B * T, D).to(dev, torch.bfloat16).requires_grad_()
+    W = (0.02 * mk(V, D)).to(dev, torch.bfloat16).requires_grad_()
+    labels = torch.randint(0, V, (B * T,), generator=g).to(dev)
+    for _ in range(args.iters):
+        out = zenith_b200.mamba3_layer_packed(zxbc, *prm, H, P, N, 1e-4, 64, 1e-5, torch.bfloat16)
+        out.backward(dout)
+        s_, u = lm.add_rmsnorm(resid, delta, w, 1e-5, torch.bfloat16)
+        (u.float().sum() + s_.sum()).backward()
+        lm.linear_cross_entropy(h, W, labels, compute_dtype=torch.bfloat16).backward()
     torch.cuda.synchronize()
     zenith_b200.check_status()
     print("ok")
