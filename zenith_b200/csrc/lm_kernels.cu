@@ -255,10 +255,19 @@ __global__ void __launch_bounds__(256) rmsnorm_dw_kernel(const NormP p, int nblo
   __shared__ float sm[8][33];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = blockIdx.x * 32 + lane;
-  float s = 0.f;
-  if (n < p.D)
-    for (int k = warp; k < nblocks; k += 8) s += p.part[(int64_t)k * p.D + n];
-  sm[warp][lane] = s;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;  // four loads in flight; summed in a fixed order
+  if (n < p.D) {
+    const float* src = p.part + n;
+    int k = warp;
+    for (; k + 24 < nblocks; k += 32) {
+      s0 += src[(int64_t)k * p.D];
+      s1 += src[(int64_t)(k + 8) * p.D];
+      s2 += src[(int64_t)(k + 16) * p.D];
+      s3 += src[(int64_t)(k + 24) * p.D];
+    }
+    for (; k < nblocks; k += 8) s0 += src[(int64_t)k * p.D];
+  }
+  sm[warp][lane] = (s0 + s1) + (s2 + s3);
   __syncthreads();
   if (warp == 0 && n < p.D) {
     float t = 0.f;
@@ -372,8 +381,11 @@ template <> struct Pack8<float> {
   }
 };
 
+constexpr float kLog2e = 1.4426950408889634f;
+
 // kPer > 0: the row is held in registers (packed), kPer 8-element units per thread (V % 8 == 0,
-// aligned rows); kPer == 0: any V, the row is read twice
+// aligned rows); kPer == 0: any V, the row is read twice.  Exponentials are base 2 of the logits
+// scaled by log2(e) (one multiply-add and exp2f per element).
 template <typename T, int kPer>
 __global__ void __launch_bounds__(kXentThreads) xent_kernel(const XentP p) {
   __shared__ float sm[kXentThreads / 32], ss[kXentThreads / 32];
@@ -402,14 +414,16 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const XentP p) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) m = fmaxf(m, v[i].get(e));
     }
-    if (m != -INFINITY)
+    if (m != -INFINITY) {
+      const float ml = m * kLog2e;
 #pragma unroll
       for (int i = 0; i < kPer; ++i) {
         const int n = (i * kXentThreads + threadIdx.x) * 8;
         if (n < V)
 #pragma unroll
-          for (int e = 0; e < 8; ++e) s += expf(v[i].get(e) - m);
+          for (int e = 0; e < 8; ++e) s += exp2f(fmaf(v[i].get(e), kLog2e, -ml));
       }
+    }
   } else {
     for (int n = threadIdx.x; n < V; n += kXentThreads) {
       const float x = ldv<float>(L + n);
@@ -429,13 +443,15 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const XentP p) {
   }
   if (!p.write_grad) return;
   if constexpr (kPer > 0) {
+    const float ll = lse * kLog2e;
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
       const int n = (i * kXentThreads + threadIdx.x) * 8;
       if (n < V) {
         float g[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) g[e] = valid ? expf(v[i].get(e) - lse) - (n + e == lab ? 1.f : 0.f) : 0.f;
+        for (int e = 0; e < 8; ++e)
+          g[e] = valid ? exp2f(fmaf(v[i].get(e), kLog2e, -ll)) - (n + e == lab ? 1.f : 0.f) : 0.f;
         Vec8<T>::st(L + n, g);
       }
     }
