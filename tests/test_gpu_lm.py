@@ -155,3 +155,64 @@ def test_train_step_reduces_loss():
     ids = torch.randint(0, 256, (2, 64), device=DEV)
     losses = [lm.train_step(model, opt, ids, loops=2).item() for _ in range(8)]
     assert losses[-1] < losses[0] - 0.1, losses
+
+
+# behaviour of the model, as the reference's own model tests check it (tests/test_model.py)
+
+TINY = dict(vocab_size=1024, d_model=128, d_state=32, expand=2, headdim=32, chunk_size=32, n_input=1, n_recurrent=2,
+            n_output=1, max_loops=4)
+
+
+def _tiny():
+    from zenith_b200 import lm
+
+    torch.manual_seed(0)
+    return lm.ZenithForCausalLM(TINY).to(DEV)
+
+
+def test_loss_is_finite_for_each_loop_count_and_none_without_labels():
+    model = _tiny()
+    ids = torch.randint(0, 1024, (2, 64), device=DEV)
+    for k in range(1, 5):
+        out = model(ids, labels=ids, loops=k, return_logits=True)
+        assert out.logits.shape == (2, 64, 1024)
+        assert torch.isfinite(out.loss)
+    assert model(ids[:1, :32]).loss is None
+
+
+def test_more_loops_change_output_and_default_is_max_loops():
+    model = _tiny()
+    ids = torch.randint(0, 1024, (1, 64), device=DEV)
+    with torch.no_grad():
+        l1, l2 = model(ids, loops=1).logits, model(ids, loops=2).logits
+        assert not torch.allclose(l1, l2)
+        assert torch.equal(model(ids).logits, model(ids, loops=TINY["max_loops"]).logits)
+
+
+def test_only_last_loop_is_tracked_by_autograd():
+    model = _tiny()
+    seen = {}
+    for i, layer in enumerate(model.recurrent_layers):
+        layer.mixer.register_forward_hook(lambda m, inp, out, i=i: seen.setdefault(i, []).append(out.requires_grad))
+    ids = torch.randint(0, 1024, (1, 64), device=DEV)
+    model(ids, labels=ids, loops=3).loss.backward()
+    assert all(flags == [False, False, True] for flags in seen.values())
+
+
+def test_loss_matches_manual_next_token_cross_entropy():
+    model = _tiny()
+    ids = torch.randint(0, 1024, (2, 64), device=DEV)
+    out = model(ids, labels=ids, loops=2, return_logits=True)
+    expected = F.cross_entropy(out.logits[:, :-1].reshape(-1, 1024).double(), ids[:, 1:].reshape(-1))
+    assert abs(out.loss.item() - expected.item()) < 1e-5 * abs(expected.item())
+
+
+def test_lm_head_is_tied_and_layer_is_identity_when_mixer_output_is_zero():
+    from zenith_b200 import lm
+
+    model = _tiny()
+    assert model.lm_head.weight is model.embed.weight
+    layer = lm.Layer(lm.ZenithConfig.from_dict(TINY)).to(DEV)
+    torch.nn.init.zeros_(layer.mixer.out_proj.weight)
+    x = torch.randn(1, 64, 128, device=DEV)
+    assert torch.allclose(layer(x), x)
