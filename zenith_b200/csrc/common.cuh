@@ -82,6 +82,29 @@ template <> struct Vec8<__nv_bfloat16> {
     *reinterpret_cast<uint4*>(p) = u;
   }
 };
+// eight consecutive elements held packed in registers (bf16: one 16-byte word)
+template <typename T> struct Pack8;
+template <> struct Pack8<__nv_bfloat16> {
+  uint4 u;
+  __device__ __forceinline__ void ld(const __nv_bfloat16* p) { u = *reinterpret_cast<const uint4*>(p); }
+  __device__ __forceinline__ float get(int e) const {
+    const uint32_t w = e < 2 ? u.x : e < 4 ? u.y : e < 6 ? u.z : u.w;
+    return __uint_as_float((e & 1) ? (w & 0xffff0000u) : (w << 16));
+  }
+};
+template <> struct Pack8<float> {
+  float4 a, b;
+  __device__ __forceinline__ void ld(const float* p) {
+    a = *reinterpret_cast<const float4*>(p);
+    b = *reinterpret_cast<const float4*>(p + 4);
+  }
+  __device__ __forceinline__ float get(int e) const {
+    const float4& q = e < 4 ? a : b;
+    const int k = e & 3;
+    return k == 0 ? q.x : k == 1 ? q.y : k == 2 ? q.z : q.w;
+  }
+};
+
 // A [B, T, H, D] view with element strides; the innermost dimension is contiguous.
 struct View {
   const void* ptr;

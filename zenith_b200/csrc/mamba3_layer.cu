@@ -844,21 +844,35 @@ __global__ void __launch_bounds__(1024) m3_epilogue_fwd_vec_kernel(const M3 p) {
   const int nt = (int)min((int64_t)kSeg, p.T - t0);
   const float Dh = p.D[hh];
   const TO* __restrict__ y = static_cast<const TO*>(p.y) + (int64_t)b * p.T * HP + r;
-#pragma unroll 2
-  for (int t = grp; t < nt; t += ngrp) {
-    const int64_t tt = t0 + t;
-    float yv[8], xv[8], o[8];
-    Vec8<TO>::ld(y + tt * HP, yv);
-    Vec8<TI>::ld(p.x.row<TI>(b, tt, hh) + pp, xv);
+  // two tokens per pass, all loads before either store (as in m3_dx_vec_kernel)
+  for (int t = grp; t < nt; t += 2 * ngrp) {
+    Pack8<TO> yv[2];
+    Pack8<TI> xv[2], zv[2];
+    bool on[2];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) o[e] = yv[e] + Dh * xv[e];
-    if (p.z.ptr) {
-      float zv[8];
-      Vec8<TI>::ld(p.z.row<TI>(b, tt, hh) + pp, zv);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] *= zv[e] * sigmoidf_(zv[e]);
+    for (int u = 0; u < 2; ++u) {
+      const int64_t tt = t0 + t + u * ngrp;
+      on[u] = t + u * ngrp < nt;
+      if (on[u]) {
+        yv[u].ld(y + tt * HP);
+        xv[u].ld(p.x.row<TI>(b, tt, hh) + pp);
+        if (p.z.ptr) zv[u].ld(p.z.row<TI>(b, tt, hh) + pp);
+      }
     }
-    Vec8<TI>::st(p.out.wrow<TI>(b, tt, hh) + pp, o);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (!on[u]) continue;
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        o[e] = yv[u].get(e) + Dh * xv[u].get(e);
+        if (p.z.ptr) {
+          const float zz = zv[u].get(e);
+          o[e] *= zz * sigmoidf_(zz);
+        }
+      }
+      Vec8<TI>::st(p.out.wrow<TI>(b, t0 + t + u * ngrp, hh) + pp, o);
+    }
   }
 }
 
@@ -875,30 +889,46 @@ __global__ void __launch_bounds__(1024) m3_epilogue_bwd_vec_kernel(const M3 p) {
   const TO* __restrict__ y = static_cast<const TO*>(p.y) + (int64_t)b * p.T * HP + r;
   TO* __restrict__ dy = static_cast<TO*>(p.dy) + (int64_t)b * p.T * HP + r;
   float acc = 0.f;
-#pragma unroll 2
-  for (int t = grp; t < nt; t += ngrp) {
-    const int64_t tt = t0 + t;
-    float go[8], xv[8], g[8];
-    Vec8<TI>::ld(p.dout.row<TI>(b, tt, hh) + pp, go);
-    Vec8<TI>::ld(p.x.row<TI>(b, tt, hh) + pp, xv);
-    if (p.z.ptr) {
-      float zv[8], yv[8], dz[8];
-      Vec8<TI>::ld(p.z.row<TI>(b, tt, hh) + pp, zv);
-      Vec8<TO>::ld(y + tt * HP, yv);
+  // two tokens per pass, all loads before any store (as in m3_dx_vec_kernel)
+  for (int t = grp; t < nt; t += 2 * ngrp) {
+    Pack8<TI> go[2], xv[2], zv[2];
+    Pack8<TO> yv[2];
+    bool on[2];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float sg = sigmoidf_(zv[e]);
-        g[e] = go[e] * zv[e] * sg;
-        dz[e] = go[e] * (yv[e] + Dh * xv[e]) * sg * (1.f + zv[e] * (1.f - sg));
+    for (int u = 0; u < 2; ++u) {
+      const int64_t tt = t0 + t + u * ngrp;
+      on[u] = t + u * ngrp < nt;
+      if (on[u]) {
+        go[u].ld(p.dout.row<TI>(b, tt, hh) + pp);
+        xv[u].ld(p.x.row<TI>(b, tt, hh) + pp);
+        if (p.z.ptr) {
+          zv[u].ld(p.z.row<TI>(b, tt, hh) + pp);
+          yv[u].ld(y + tt * HP);
+        }
       }
-      Vec8<TI>::st(p.dz.wrow<TI>(b, tt, hh) + pp, dz);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) g[e] = go[e];
     }
-    Vec8<TO>::st(dy + tt * HP, g);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc += g[e] * xv[e];
+    for (int u = 0; u < 2; ++u) {
+      if (!on[u]) continue;
+      const int64_t tt = t0 + t + u * ngrp;
+      float g[8];
+      if (p.z.ptr) {
+        float dz[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float zz = zv[u].get(e), o = go[u].get(e), sg = sigmoidf_(zz);
+          g[e] = o * zz * sg;
+          dz[e] = o * (yv[u].get(e) + Dh * xv[u].get(e)) * sg * (1.f + zz * (1.f - sg));
+        }
+        Vec8<TI>::st(p.dz.wrow<TI>(b, tt, hh) + pp, dz);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) g[e] = go[u].get(e);
+      }
+      Vec8<TO>::st(dy + tt * HP, g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc += g[e] * xv[u].get(e);
+    }
   }
   sacc[threadIdx.x] = acc;
   __syncthreads();
@@ -922,21 +952,30 @@ __global__ void __launch_bounds__(1024) m3_dx_vec_kernel(const M3 p) {
   const TO* __restrict__ dxs = static_cast<const TO*>(p.dxs) + (int64_t)b * p.T * HP + r;
   const TO* __restrict__ dxp = static_cast<const TO*>(p.dxp) + (int64_t)b * p.T * HP + r;
   const TO* __restrict__ dy = static_cast<const TO*>(p.dy) + (int64_t)b * p.T * HP + r;
-#pragma unroll 2
-  for (int t = grp; t < nt; t += ngrp) {
-    const int64_t tt = t0 + t;
-    float g[8], gy[8];
-    Vec8<TO>::ld(dxs + tt * HP, g);
-    Vec8<TO>::ld(dy + tt * HP, gy);  // dout silu(z), as stored for the scan
-    if (tt + 1 < p.T) {  // xp[t+1] = x[t]
-      float gp[8];
-      Vec8<TO>::ld(dxp + (tt + 1) * HP, gp);
+  // two tokens per pass, all their loads issued before either store (the store through a view may
+  // alias the loads as far as the compiler knows, so it would not hoist them itself)
+  for (int t = grp; t < nt; t += 2 * ngrp) {
+    Pack8<TO> ga[2], gy[2], gp[2];  // dout silu(z) is dy, as stored for the scan
+    bool on[2], nx[2];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) g[e] += gp[e];
+    for (int u = 0; u < 2; ++u) {
+      const int64_t tt = t0 + t + u * ngrp;
+      on[u] = t + u * ngrp < nt;
+      nx[u] = on[u] && tt + 1 < p.T;  // xp[t+1] = x[t]
+      if (on[u]) {
+        ga[u].ld(dxs + tt * HP);
+        gy[u].ld(dy + tt * HP);
+      }
+      if (nx[u]) gp[u].ld(dxp + (tt + 1) * HP);
     }
 #pragma unroll
-    for (int e = 0; e < 8; ++e) g[e] += Dh * gy[e];
-    Vec8<TI>::st(p.dx.wrow<TI>(b, tt, hh) + pp, g);
+    for (int u = 0; u < 2; ++u) {
+      if (!on[u]) continue;
+      float g[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) g[e] = ga[u].get(e) + (nx[u] ? gp[u].get(e) : 0.f) + Dh * gy[u].get(e);
+      Vec8<TI>::st(p.dx.wrow<TI>(b, t0 + t + u * ngrp, hh) + pp, g);
+    }
   }
 }
 
