@@ -26,6 +26,7 @@ def _rmsnorm_ref(s, w, eps):
     (torch.bfloat16, torch.bfloat16, torch.bfloat16, 640),
     (torch.float32, None, torch.float32, 100),           # D % 8 != 0: the scalar path
     (torch.float32, torch.float32, torch.bfloat16, 36),
+    (torch.float32, torch.bfloat16, torch.bfloat16, 4096),  # D > 2048: one warp per row, 16-byte accesses
 ])
 def test_add_rmsnorm_matches_torch(x_dtype, b_dtype, u_dtype, D):
     from zenith_b200 import lm

@@ -20,11 +20,13 @@ namespace {
 constexpr int kNormWarps = 8;     // rows in flight per CTA, one warp each
 constexpr int kNormGrid = 1024;   // CTAs at most: a fixed grid fixes the order of the dw sums
 constexpr int kNormMaxD = 8192;
+constexpr int kRowMaxThreads = 256;  // row kernels: D <= 8 x 256 (the registers of a row pair fit)
 
 struct NormP {
   int64_t M, D;
   float eps;
-  bool vec;  // D % 8 == 0 and every row pointer 16-byte aligned: 8-element accesses
+  bool vec;   // D % 8 == 0 and every row pointer 16-byte aligned: 8-element accesses
+  bool rows;  // vec and D <= 8 kRowMaxThreads: one CTA per row (the row kernels)
   const void *a, *b;
   void* s;
   const float* w;
@@ -176,7 +178,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 template <typename TX, typename TB, typename TU>
-__global__ void __launch_bounds__(1024) rmsnorm_fwd_row_kernel(const NormP p) {
+__global__ void __launch_bounds__(kRowMaxThreads) rmsnorm_fwd_row_kernel(const NormP p) {
   __shared__ float red[32];
   const int D = (int)p.D, n = 8 * threadIdx.x;
   const bool on = n < D;
@@ -186,16 +188,29 @@ __global__ void __launch_bounds__(1024) rmsnorm_fwd_row_kernel(const NormP p) {
   TU* __restrict__ U = static_cast<TU*>(p.u);
   float w[8];
   if (on) Vec8<float>::ld(p.w + n, w);
-  for (int64_t row = blockIdx.x; row < p.M; row += gridDim.x) {
+  // the next row's loads are issued before this row's reduction and stores
+  Pack8<TX> an;
+  Pack8<TB> bn;
+  int64_t row = blockIdx.x;
+  if (on && row < p.M) {
+    an.ld(A + row * D + n);
+    if (Bv) bn.ld(Bv + row * D + n);
+  }
+  for (; row < p.M; row += gridDim.x) {
     const int64_t o = row * D + n;
+    const Pack8<TX> ac = an;
+    const Pack8<TB> bc = bn;
+    if (on && row + gridDim.x < p.M) {
+      an.ld(A + o + (int64_t)gridDim.x * D);
+      if (Bv) bn.ld(Bv + o + (int64_t)gridDim.x * D);
+    }
     float v[8], ss = 0.f;
     if (on) {
-      Vec8<TX>::ld(A + o, v);
-      if (Bv) {
-        float c[8];
-        Vec8<TB>::ld(Bv + o, c);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = round_to<TX>(v[e] + c[e]);
+      for (int e = 0; e < 8; ++e) v[e] = ac.get(e);
+      if (Bv) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = round_to<TX>(v[e] + bc.get(e));
         Vec8<TX>::st(S + o, v);
       }
 #pragma unroll
@@ -212,7 +227,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_fwd_row_kernel(const NormP p) {
 }
 
 template <typename TX, typename TB, typename TU>
-__global__ void __launch_bounds__(1024) rmsnorm_bwd_row_kernel(const NormP p) {
+__global__ void __launch_bounds__(kRowMaxThreads) rmsnorm_bwd_row_kernel(const NormP p) {
   __shared__ float red[32];
   const int D = (int)p.D, n = 8 * threadIdx.x;
   const bool on = n < D;
@@ -223,23 +238,48 @@ __global__ void __launch_bounds__(1024) rmsnorm_bwd_row_kernel(const NormP p) {
   TB* __restrict__ GB = static_cast<TB*>(p.dsum_b);
   float w[8], dw[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   if (on) Vec8<float>::ld(p.w + n, w);
-  for (int64_t row = blockIdx.x; row < p.M; row += gridDim.x) {
+  // the next row's loads are issued before this row's reduction and stores
+  Pack8<TU> gn;
+  Pack8<TX> xn, dn;
+  float rn = 0.f;
+  int64_t row = blockIdx.x;
+  if (row < p.M) {
+    rn = p.r[row];
+    if (on) {
+      gn.ld(dU + row * D + n);
+      xn.ld(S + row * D + n);
+      if (dS) dn.ld(dS + row * D + n);
+    }
+  }
+  for (; row < p.M; row += gridDim.x) {
     const int64_t o = row * D + n;
-    const float r = p.r[row];
+    const float r = rn;
+    const Pack8<TU> gc = gn;
+    const Pack8<TX> xc = xn, dc = dn;
+    if (row + gridDim.x < p.M) {
+      const int64_t o2 = o + (int64_t)gridDim.x * D;
+      rn = p.r[row + gridDim.x];
+      if (on) {
+        gn.ld(dU + o2);
+        xn.ld(S + o2);
+        if (dS) dn.ld(dS + o2);
+      }
+    }
     float g[8], x[8], dot = 0.f;
     if (on) {
-      Vec8<TU>::ld(dU + o, g);
-      Vec8<TX>::ld(S + o, x);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) dot += g[e] * w[e] * x[e];
+      for (int e = 0; e < 8; ++e) {
+        g[e] = gc.get(e);
+        x[e] = xc.get(e);
+        dot += g[e] * w[e] * x[e];
+      }
     }
     const float k3 = r * r * r / D * block_sum(dot, red);
     if (on) {
       float out[8];
-      if (dS) Vec8<TX>::ld(dS + o, out);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        out[e] = (dS ? out[e] : 0.f) + r * w[e] * g[e] - x[e] * k3;
+        out[e] = (dS ? dc.get(e) : 0.f) + r * w[e] * g[e] - x[e] * k3;
         dw[e] += g[e] * x[e] * r;
       }
       Vec8<TX>::st(G + o, out);
@@ -307,6 +347,7 @@ NormP make_norm(const zb_rmsnorm_args* a, bool bwd) {
   if (bwd) { for (const void* q : ptrs_b) ok = ok && aligned16(q); }
   else { for (const void* q : ptrs_f) ok = ok && aligned16(q); }
   p.vec = ok;
+  p.rows = ok && a->D <= 8 * kRowMaxThreads;
   return p;
 }
 
@@ -478,7 +519,7 @@ extern "C" ZB_API int zb_rmsnorm_fwd(const zb_rmsnorm_args* a, void* stream) {
         using TX = decltype(tx);
         using TB = decltype(tb);
         using TU = decltype(tu);
-        if (p.vec) rmsnorm_fwd_row_kernel<TX, TB, TU><<<row_grid(a->M), row_threads(a->D), 0, st>>>(p);
+        if (p.rows) rmsnorm_fwd_row_kernel<TX, TB, TU><<<row_grid(a->M), row_threads(a->D), 0, st>>>(p);
         else rmsnorm_fwd_kernel<TX, TB, TU><<<norm_grid_warp(a->M), 32 * kNormWarps, 0, st>>>(p);
         return (int)ZB_OK;
       });
@@ -496,7 +537,7 @@ extern "C" ZB_API int zb_rmsnorm_bwd(const zb_rmsnorm_args* a, void* stream) {
     return ZB_ERR_WORKSPACE;
   const NormP p = make_norm(a, true);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int grid = p.vec ? row_grid(a->M) : norm_grid_warp(a->M);
+  const int grid = p.rows ? row_grid(a->M) : norm_grid_warp(a->M);
   const int smem = (int)(kNormWarps * a->D * sizeof(float));
   rc = with_type(a->x_dtype, [&](auto tx) {
     return with_type(a->b_dtype, [&](auto tb) {
@@ -504,7 +545,7 @@ extern "C" ZB_API int zb_rmsnorm_bwd(const zb_rmsnorm_args* a, void* stream) {
         using TX = decltype(tx);
         using TB = decltype(tb);
         using TU = decltype(tu);
-        if (p.vec) {
+        if (p.rows) {
           rmsnorm_bwd_row_kernel<TX, TB, TU><<<grid, row_threads(a->D), 0, st>>>(p);
           return (int)ZB_OK;
         }

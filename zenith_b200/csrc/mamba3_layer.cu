@@ -301,20 +301,33 @@ __global__ void __launch_bounds__(1024) m3_prologue_fwd_kernel(const M3 p) {
       const float zero[4] = {0.f, 0.f, 0.f, 0.f};
       st4(kx + (int64_t)b * (p.T + 1) * HN + h * N, f, zero);
     }
-    for (int t = 0; t < nt; ++t) {
-      th += S.dt[t * hc + w] * S.ang[t * NA + lane];  // theta = cumsum_t(DT ang) (mamba3.py:111)
-      const int64_t bth = (b * p.T + t0 + t) * H + h;
-      p.theta[bth * NA + lane] = th;
-      float sn, cs;
-      sincosf(th, &sn, &cs);
-      float c[4], bm[4], u[4], o[4];
-      ldp4(S.c + t * N, f, c);
-      ldp4(S.bm + t * N, f, bm);
-      const float one = 1.f;
-      norm_bias_rope(c, one, wc, cb, sn, cs, u, o);
-      st4(q + bth * N, f, o);
-      norm_bias_rope(bm, one, wb, bb, sn, cs, u, o);
-      st4(kx + (b * (p.T + 1) + t0 + t + 1) * HN + h * N, f, o);
+    // two tokens per pass: their shared-memory reads come before the global stores (which may
+    // alias them for the compiler), so the two sincos / RoPE chains overlap
+    for (int t = 0; t < nt; t += 2) {
+      const int nu = t + 1 < nt ? 2 : 1;
+      float th2[2], c[2][4], bm[2][4];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (u < nu) {
+          th += S.dt[(t + u) * hc + w] * S.ang[(t + u) * NA + lane];  // theta = cumsum_t(DT ang) (mamba3.py:111)
+          ldp4(S.c + (t + u) * N, f, c[u]);
+          ldp4(S.bm + (t + u) * N, f, bm[u]);
+        }
+        th2[u] = th;
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (u >= nu) continue;
+        const int64_t bth = (b * p.T + t0 + t + u) * H + h;
+        p.theta[bth * NA + lane] = th2[u];
+        float sn, cs, uu[4], o[4];
+        sincosf(th2[u], &sn, &cs);
+        const float one = 1.f;
+        norm_bias_rope(c[u], one, wc, cb, sn, cs, uu, o);
+        st4(q + bth * N, f, o);
+        norm_bias_rope(bm[u], one, wb, bb, sn, cs, uu, o);
+        st4(kx + (b * (p.T + 1) + t0 + t + u + 1) * HN + h * N, f, o);
+      }
     }
   }
   // xp = x one token later (mamba3.py:115), all threads over (token, group head, feature); not
