@@ -71,6 +71,20 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def flop_roofline(shape, th, dom, dms, fwd_only):
+    """The flop side of the dominant kernel: algorithmic flops per token-head (forward
+    4 L N / r + 4 L P + 6 N P, backward twice that) over its time, against the measured
+    burst bf16 tensor peak."""
+    L, r = 64, shape.H // shape.G
+    f = 4 * L * shape.N // r + 4 * L * shape.P + 6 * shape.N * shape.P
+    flops = (f if dom == "fwd" else 2 * f) * th
+    p = ROOT / "MEASURED_PEAKS.json"
+    peak = float(json.loads(p.read_text())["bf16_tflops"]) if p.exists() else 1590.0
+    achieved = flops / (dms / 1e3) / 1e12
+    return {"kernel": "ssd_" + dom, "achieved_tflops": achieved, "peak_tflops": peak, "frac": achieved / peak,
+            "flops_per_launch": flops, "internal_chunk": 64}
+
+
 def traffic_from_profile(kernel: str):
     """DRAM bytes per launch from the committed ncu summary (profiles/traffic.json), if any."""
     p = ROOT / "profiles" / "traffic.json"
@@ -450,6 +464,7 @@ def run_ours(args):
                      "algorithmic_bytes_per_launch": dbytes, "launch_ms": dms},
         "step_roofline": {"achieved_gbs": step_gbs, "frac": step_gbs / peak,
                           "algorithmic_bytes_per_token_head": fwd_b + bwd_b, "fwd_ms": fwd_ms, "bwd_ms": bwd_ms},
+        "flop_roofline": flop_roofline(shape, th, dom, dms, fwd_only),
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
         "clocks": clocks,

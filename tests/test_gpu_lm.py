@@ -217,3 +217,31 @@ def test_lm_head_is_tied_and_layer_is_identity_when_mixer_output_is_zero():
     torch.nn.init.zeros_(layer.mixer.out_proj.weight)
     x = torch.randn(1, 64, 128, device=DEV)
     assert torch.allclose(layer(x), x)
+
+
+def test_use_b200_layer_matches_oracle_mixer():
+    """``use_b200_layer`` on a module with the reference Mamba3's attributes (in_proj, the packed
+    layer body, out_proj), float32: output and the gradients of both projections and every layer
+    parameter against the oracle's ``Mamba3.forward`` restatement, to 1e-4."""
+    import zenith_b200
+    from zenith_b200 import lm
+
+    torch.manual_seed(5)
+    cfg = dict(d_model=64, d_state=32, expand=2, headdim=16, chunk_size=32)
+    m = lm.Mamba3(64, 32, 2, 16, 32).to(DEV)
+    with torch.no_grad():
+        for prm in (m.B_bias, m.C_bias, m.B_norm.weight, m.C_norm.weight, m.D):
+            prm.add_(0.2 * torch.randn_like(prm))
+    zenith_b200.use_b200_layer(m, scan_dtype=torch.float32)
+    u = torch.randn(2, 96, 64, device=DEV)
+    dout = torch.randn(2, 96, 64, device=DEV)
+    out = m(u)
+    out.backward(dout)
+    params = {"mixer." + n: t.detach().cpu() for n, t in m.named_parameters()}
+    leaves = {n: t.double().requires_grad_(True) for n, t in params.items()}
+    ref = lm_oracle.mixer(leaves, "mixer.", u.cpu().double(), dict(cfg, vocab_size=0))
+    ref.backward(dout.cpu().double())
+    assert max_rel_err(out.double().cpu(), ref.detach()) < 1e-4
+    for n, prm in m.named_parameters():
+        g = leaves["mixer." + n].grad
+        assert max_rel_err(prm.grad.double().cpu(), g) < 1e-4, n
