@@ -245,3 +245,24 @@ def test_use_b200_layer_matches_oracle_mixer():
     for n, prm in m.named_parameters():
         g = leaves["mixer." + n].grad
         assert max_rel_err(prm.grad.double().cpu(), g) < 1e-4, n
+
+
+def test_train_step_folds_clipping_into_fused_adamw():
+    """The fused path (the clip scale passed to the fused AdamW kernel as its gradient divisor) makes
+    the same update as clip_grad_norm_ followed by a plain AdamW step, with clipping active."""
+    from zenith_b200 import lm
+
+    cfg = dict(vocab_size=256, d_model=64, d_state=16, expand=2, headdim=16, chunk_size=32, n_input=1,
+               n_recurrent=1, n_output=1, max_loops=1)
+    torch.manual_seed(0)
+    a = lm.ZenithForCausalLM(cfg).to(DEV)
+    b = lm.ZenithForCausalLM(cfg).to(DEV)
+    b.load_state_dict(a.state_dict())
+    opt_a = lm.make_optimizer(a, lr=1e-3)
+    opt_b = torch.optim.AdamW(b.parameters(), lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, foreach=False)
+    ids = torch.randint(0, 256, (2, 64), device=DEV)
+    for _ in range(2):
+        lm.train_step(a, opt_a, ids, loops=1, grad_clip=0.05, amp=False)
+        lm.train_step(b, opt_b, ids, loops=1, grad_clip=0.05, amp=False)
+    for (n, pa), (_, pb) in zip(a.named_parameters(), b.named_parameters()):
+        assert torch.allclose(pa, pb, rtol=1e-5, atol=1e-7), n

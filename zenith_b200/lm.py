@@ -402,8 +402,21 @@ def train_step(model: nn.Module, opt: torch.optim.Optimizer, ids: Tensor, loops:
     with ctx:
         loss = model(ids, labels=ids, loops=loops).loss
     loss.backward()
-    torch.nn.utils.clip_grad_norm_(model.parameters(), grad_clip, foreach=True)
-    opt.step()
+    fused = all(g.get("fused") for g in opt.param_groups) and isinstance(opt, torch.optim.Adam)
+    if fused:
+        # clip_grad_norm_'s scale (max_norm / (norm + 1e-6), at most 1) applied inside the fused
+        # AdamW kernel, which divides each gradient by `grad_scale` as it reads it: one pass over
+        # the gradients fewer than scaling them in place first
+        grads = [q.grad for g in opt.param_groups for q in g["params"] if q.grad is not None]
+        norm = torch.nn.utils.get_total_norm(grads, 2.0, foreach=True)
+        opt.grad_scale = ((norm + 1e-6) / grad_clip).clamp_(min=1.0).to(torch.float32)
+        try:
+            opt.step()
+        finally:
+            del opt.grad_scale
+    else:
+        torch.nn.utils.clip_grad_norm_(model.parameters(), grad_clip, foreach=True)
+        opt.step()
     opt.zero_grad(set_to_none=True)
     return loss.detach()
 
