@@ -61,6 +61,11 @@ typedef struct {
   /* device int32 status word (zb_m3_prologue_bwd): a bounded wait on its row copies that gives up
      after about a second records ZB_ERR_TIMEOUT there and the kernel returns */
   int32_t* status;
+  /* continuing a sequence (zb_m3_prologue_fwd; decode): theta0 [B,H,N/4] fp32, theta after the
+     tokens before this call (NULL: zero); kp0 [B,H,N] op dtype, k of the token before this call,
+     written to k_ext row 0 (NULL: zeros, the sequence start) */
+  const float* theta0;
+  const void* kp0;
 } zb_m3_args;
 
 /* scratch bytes the four calls need (the maximum over them) */

@@ -266,3 +266,32 @@ def test_train_step_folds_clipping_into_fused_adamw():
         lm.train_step(b, opt_b, ids, loops=1, grad_clip=0.05, amp=False)
     for (n, pa), (_, pb) in zip(a.named_parameters(), b.named_parameters()):
         assert torch.allclose(pa, pb, rtol=1e-5, atol=1e-7), n
+
+
+# token-by-token inference from the layer caches (prefill + recurrent scan)
+
+def test_stream_logits_match_the_full_forward():
+    """A chunked prefill of 64 tokens then 32 tokens one at a time (layer caches: scan state,
+    theta, previous k and x, per recurrent loop pass) reproduce the full forward's logits at
+    every position, float32, to 1e-4; likewise with no prefill at all."""
+    model = _tiny()
+    ids = torch.randint(0, 1024, (2, 96), device=DEV)
+    with torch.no_grad():
+        full = model(ids, loops=2).logits
+    stream = model.stream_logits(ids, prefill_len=64, loops=2)
+    assert max_rel_err(stream.double().cpu(), full.double().cpu()) < 1e-4
+    short = model.stream_logits(ids[:, :5], prefill_len=0, loops=2)
+    assert max_rel_err(short.double().cpu(), full[:, :5].double().cpu()) < 1e-4
+
+
+def test_generate_is_greedy_on_the_full_forward():
+    """Each generated token is the argmax of the full forward's logits at the previous position
+    (the prompt is 40 tokens: a 32-token prefill, then 8 prompt tokens one at a time)."""
+    model = _tiny()
+    prompt = torch.randint(0, 1024, (2, 40), device=DEV)
+    out = model.generate(prompt, 12, loops=2)
+    assert out.shape == (2, 52) and torch.equal(out[:, :40], prompt)
+    padded = torch.cat((out, torch.zeros(2, 12, dtype=out.dtype, device=DEV)), dim=1)   # 64 tokens
+    with torch.no_grad():
+        logits = model(padded, loops=2).logits
+    assert torch.equal(logits[:, 39:51].argmax(-1), out[:, 40:52])

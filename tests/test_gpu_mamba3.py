@@ -225,7 +225,7 @@ def test_shifted_flag_matches_explicit_shifted_operands(dtype, P, N):
     gamma, beta = (0.1 * torch.rand(2, B, T, H, generator=g)).to(dev)
     dy = torch.randn(B, T, H, P, generator=g).to(dev, dtype)
     shift = lambda t: torch.cat((torch.zeros_like(t[:, :1]), t[:, :-1]), dim=1)  # noqa: E731
-    y1, st1 = m3._scan_fwd(x, q, k, adt, gamma, beta, 64, True)
+    y1, st1, _ = m3._scan_fwd(x, q, k, adt, gamma, beta, 64, True)
     y0, _, st0 = ssd_fwd_op(x, q, k, shift(k), shift(x), adt, gamma, beta, 64, None, True, False)
     g1 = m3._scan_bwd(dy, x, q, k, adt, gamma, beta, st1, 64)
     g0 = ssd_bwd_op(dy, x, q, k, shift(k), shift(x), adt, gamma, beta, st0, 64, None, None, False)[:8]

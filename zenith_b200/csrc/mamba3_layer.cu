@@ -46,6 +46,8 @@ struct M3 {
   View dx, dz, dBm, dCm, ddd_dt, ddd_A, dtrap, dang;
   float *ddt_bias, *dB_bias, *dC_bias, *dB_norm_w, *dC_norm_w, *dD;
   int32_t* status;  // device word: a bounded wait that gave up records ZB_ERR_TIMEOUT
+  const float* theta0;  // [B][H][NA] theta before the first token, or null (0)
+  const void* kp0;      // [B][H][N] k of the token before the first (k_ext row 0), or null (0)
   // scratch
   float* segsum;  // [B][H][nseg][NA]   theta segment sums (forward) / theta-gradient segment totals (backward)
   float* dDTl;    // [B][T][H]          backward: DT gradient through theta, within-segment part
@@ -288,7 +290,7 @@ __global__ void __launch_bounds__(1024) m3_prologue_fwd_kernel(const M3 p) {
   const int64_t HN = (int64_t)H * N;
   const Feat f = feat(lane, NA);
   if (w < hc && f.on) {
-    float th = 0.f;  // theta at the end of the previous segment
+    float th = p.theta0 ? p.theta0[(int64_t)(b * H + h) * NA + lane] : 0.f;  // theta at the end of the previous segment
     const float* __restrict__ ss = p.segsum + (int64_t)(b * H + h) * p.nseg * NA + lane;
 #pragma unroll 8
     for (int s = 0; s < seg; ++s) th += __ldg(ss + (int64_t)s * NA);
@@ -297,9 +299,10 @@ __global__ void __launch_bounds__(1024) m3_prologue_fwd_kernel(const M3 p) {
     ldp4(p.B_norm_w, f, wb);
     ldp4(p.C_bias + h * N, f, cb);
     ldp4(p.B_bias + h * N, f, bb);
-    if (seg == 0) {  // k_ext row 0 = kp of token 0 = 0
-      const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-      st4(kx + (int64_t)b * (p.T + 1) * HN + h * N, f, zero);
+    if (seg == 0) {  // k_ext row 0 = kp of token 0: the previous token's k, or 0 at the sequence start
+      float k0[4] = {0.f, 0.f, 0.f, 0.f};
+      if (p.kp0) ld4(static_cast<const TO*>(p.kp0) + (int64_t)(b * H + h) * N, f, k0);
+      st4(kx + (int64_t)b * (p.T + 1) * HN + h * N, f, k0);
     }
     // two tokens per pass: their shared-memory reads come before the global stores (which may
     // alias them for the compiler), so the two sincos / RoPE chains overlap
@@ -1135,6 +1138,8 @@ M3 make_m3(const zb_m3_args* a) {
   p.ddt_bias = a->ddt_bias; p.dB_bias = a->dB_bias; p.dC_bias = a->dC_bias;
   p.dB_norm_w = a->dB_norm_w; p.dC_norm_w = a->dC_norm_w; p.dD = a->dD;
   p.status = a->status;
+  p.theta0 = a->theta0;
+  p.kp0 = a->kp0;
   const WsLayout L = ws_layout(a);
   unsigned char* ws = static_cast<unsigned char*>(a->workspace);
   p.segsum = reinterpret_cast<float*>(ws + L.segsum);

@@ -34,7 +34,7 @@ import torch.nn as nn
 from torch import Tensor
 
 from . import _lib as L
-from .mamba3 import mamba3_layer_packed
+from .mamba3 import LayerCache, _scan_dtype, mamba3_layer_packed, mamba3_layer_prefill, mamba3_layer_step
 
 
 # ---------------------------------------------------------------------------------------------
@@ -349,6 +349,46 @@ class ZenithForCausalLM(nn.Module):
     def get_output_embeddings(self):
         return self.lm_head
 
+    @torch.no_grad()
+    def stream_logits(self, input_ids: Tensor, prefill_len: Optional[int] = None,
+                      loops: Optional[int] = None) -> Tensor:
+        """The logits of every position, computed the way ``generate`` computes them: a chunked
+        prefill of the first ``prefill_len`` tokens (a multiple of chunk_size; default the longest
+        such prefix), then the remaining tokens one at a time from the layer caches (the scan in its
+        recurrent form, ``zb_ssd_decode``)."""
+        loops = loops or self.config.max_loops
+        T, L = input_ids.shape[1], self.config.chunk_size
+        prefill_len = T // L * L if prefill_len is None else prefill_len
+        caches: dict = {}
+        outs = [_Generation.forward(self, input_ids[:, :prefill_len], caches, loops)] if prefill_len else []
+        for t in range(prefill_len, T):
+            outs.append(_Generation.forward(self, input_ids[:, t:t + 1], caches, loops))
+        return torch.cat(outs, dim=1)
+
+    @torch.no_grad()
+    def generate(self, input_ids: Tensor, max_new_tokens: int, loops: Optional[int] = None) -> Tensor:
+        """Greedy decoding: the prompt is prefilled (its longest chunk_size-multiple prefix in one
+        chunked pass, the rest token by token), then each new token is the argmax of the last
+        logits and runs through the layers from their caches.  Returns the prompt followed by the
+        new tokens.  The reference has no cache (model.py:79-99); this is the recurrent form of
+        its forward."""
+        loops = loops or self.config.max_loops
+        T, L = input_ids.shape[1], self.config.chunk_size
+        pre = T // L * L
+        caches: dict = {}
+        logits = None
+        if pre:
+            logits = _Generation.forward(self, input_ids[:, :pre], caches, loops)
+        for t in range(pre, T):
+            logits = _Generation.forward(self, input_ids[:, t:t + 1], caches, loops)
+        ids = [input_ids]
+        for i in range(max_new_tokens):
+            nxt = logits[:, -1].argmax(-1, keepdim=True)
+            ids.append(nxt)
+            if i + 1 < max_new_tokens:
+                logits = _Generation.forward(self, nxt, caches, loops)
+        return torch.cat(ids, dim=1)
+
     def forward(self, input_ids: Tensor, labels: Optional[Tensor] = None, loops: Optional[int] = None,
                 return_logits: bool = False) -> LMOutput:
         cfg = self.config
@@ -376,6 +416,51 @@ class ZenithForCausalLM(nn.Module):
         if labels is None or return_logits:
             logits = self.lm_head(u)
         return LMOutput(loss, logits)
+
+
+def _empty_cache(B, H, P, N, dtype, dev) -> LayerCache:
+    """The cache before a sequence's first token: zero state, theta, k and x."""
+    z = lambda *sh, dt=torch.float32: torch.zeros(*sh, dtype=dt, device=dev)  # noqa: E731
+    return LayerCache(z(B, H, P, N), z(B, H, N // 4), z(B, H, N, dt=dtype), z(B, H, P, dt=dtype))
+
+
+class _Generation:
+    """Token-by-token inference for ZenithForCausalLM: the forward (model.py:79-93) on new tokens
+    with one layer cache per (stack, layer, loop pass), since every pass of the shared recurrent
+    block runs over the sequence with its own scan state."""
+
+    @staticmethod
+    def mixer(m: "Mamba3", u: Tensor, caches: dict, key) -> Tensor:
+        Bsz, T, _ = u.shape
+        zxbc = m.in_proj(u)
+        if zxbc.dtype not in (torch.float32, torch.bfloat16):
+            zxbc = zxbc.float()
+        prm = (m.dt_bias, m.B_bias, m.C_bias, m.B_norm.weight, m.C_norm.weight, m.D)
+        H, P, N = m.nheads, m.headdim, m.d_state
+        if key not in caches:
+            if T % m.chunk_size == 0:  # a chunked prefill
+                out, caches[key] = mamba3_layer_prefill(zxbc, *prm, H, P, N, m.A_floor, m.chunk_size, m.B_norm.eps)
+                return m.out_proj(out.reshape(Bsz, T, m.d_inner))
+            caches[key] = _empty_cache(Bsz, H, P, N, _scan_dtype(zxbc, None), zxbc.device)
+        out = mamba3_layer_step(zxbc, *prm, H, P, N, caches[key], m.A_floor, m.B_norm.eps)
+        return m.out_proj(out.reshape(Bsz, T, m.d_inner))
+
+    @staticmethod
+    def forward(model: "ZenithForCausalLM", input_ids: Tensor, caches: dict, loops: int) -> Tensor:
+        """Logits of the new tokens; ``caches`` is advanced."""
+        def stack(name, layers, h, loop):
+            for i, layer in enumerate(layers):
+                u = add_rmsnorm(h, None, layer.norm.weight, layer.norm.eps, _u_dtype(h))
+                h = h + _Generation.mixer(layer.mixer, u, caches, (name, i, loop)).to(h.dtype)
+            return h
+
+        x = stack("in", model.input_layers, model.embed(input_ids), 0)
+        s = x
+        for t in range(loops):
+            h = add_rmsnorm(s, x, model.recurrent_norm.weight, model.recurrent_norm.eps)[1]
+            s = stack("rec", model.recurrent_layers, h, t)
+        s = stack("out", model.output_layers, s, 0)
+        return model.lm_head(add_rmsnorm(s, None, model.norm.weight, model.norm.eps, _u_dtype(s)))
 
 
 def load_reference_state_dict(model: ZenithForCausalLM, state_dict: dict):

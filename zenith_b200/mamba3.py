@@ -38,6 +38,7 @@ class M3Args(ctypes.Structure):
         + [(n, L.View) for n in ("dx", "dz", "dBm", "dCm", "ddd_dt", "ddd_A", "dtrap", "dang")]
         + [(n, ctypes.c_void_p) for n in ("ddt_bias", "dB_bias", "dC_bias", "dB_norm_w", "dC_norm_w", "dD")]
         + [("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64), ("status", ctypes.c_void_p)]
+        + [("theta0", ctypes.c_void_p), ("kp0", ctypes.c_void_p)]
     )
 
 
@@ -99,7 +100,8 @@ def _check(rc: int, what: str):
 
 
 def _scan_fwd(xs, q, k, adt, gamma, beta, chunk_size, save_states):
-    """The scan with kp / xp read as k / x one token earlier (ZB_FLAG_SHIFTED): no xp tensor."""
+    """The scan with kp / xp read as k / x one token earlier (ZB_FLAG_SHIFTED): no xp tensor.
+    Returns y, the saved states (empty without ``save_states``) and the final state."""
     B, T, H, P = xs.shape
     N = q.shape[3]
     dev = xs.device
@@ -115,7 +117,7 @@ def _scan_fwd(xs, q, k, adt, gamma, beta, chunk_size, save_states):
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     a.status = L.status_word(dev).data_ptr()
     _check(lib.zb_ssd_fwd(ctypes.byref(a), torch.cuda.current_stream(dev).cuda_stream), "zb_ssd_fwd")
-    return y, states
+    return y, states, final
 
 
 def _scan_bwd(dy, xs, q, k, adt, gamma, beta, states, chunk_size):
@@ -157,7 +159,7 @@ def _layer_fwd(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, params, A_floor, chunk_size
     stream = torch.cuda.current_stream(dev).cuda_stream
     _check(lib.zb_m3_prologue_fwd(ctypes.byref(a), stream), "zb_m3_prologue_fwd")
     xs = x if x.dtype == op_dtype else x.to(op_dtype)
-    y, states = _scan_fwd(xs, q, k_ext[:, 1:], adt, gamma, beta, chunk_size, save_states)
+    y, states, _ = _scan_fwd(xs, q, k_ext[:, 1:], adt, gamma, beta, chunk_size, save_states)
     out = torch.empty(B, T, H, P, dtype=x.dtype, device=dev)
     a.y, a.out = y.data_ptr(), _v(out)
     _check(lib.zb_m3_epilogue_fwd(ctypes.byref(a), stream), "zb_m3_epilogue_fwd")
@@ -349,3 +351,87 @@ def use_b200_layer(module, scan_dtype: Optional[torch.dtype] = None):
     """Route a reference-style ``Mamba3`` module's forward through the fused layer body."""
     module.forward = lambda u: layer_forward(module, u, scan_dtype)
     return module
+
+
+# ---------------------------------------------------------------------------------------------
+# decode: the layer body one token at a time from a carried cache (inference only)
+
+class LayerCache:
+    """What one Mamba-3 layer carries from token to token: the scan state ``[B,H,P,N]`` fp32,
+    theta ``[B,H,N/4]`` fp32 (the running ``cumsum(DT ang)``, mamba3.py:111) and the previous
+    token's k ``[B,H,N]`` and x ``[B,H,P]`` (kp and xp of the next token, mamba3.py:115-116)."""
+
+    def __init__(self, state: Tensor, theta: Tensor, k_prev: Tensor, x_prev: Tensor):
+        self.state, self.theta, self.k_prev, self.x_prev = state, theta, k_prev, x_prev
+
+
+def _prologue(zxbc, params, H, P, N, A_floor, eps, op_dtype, cache: Optional[LayerCache]):
+    x, z, Bm, Cm, dd_dt, dd_A, trap, ang = split_in_proj(zxbc, H, P, N)
+    B, T = x.shape[:2]
+    dev = x.device
+    lib = _lib()
+    a = _base_args(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, params, A_floor, eps, op_dtype)
+    ws = torch.empty(max(int(lib.zb_m3_workspace_bytes(ctypes.byref(a))), 256), dtype=torch.uint8, device=dev)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    q = torch.empty(B, T, H, N, dtype=op_dtype, device=dev)
+    k_ext = torch.empty(B, T + 1, H, N, dtype=op_dtype, device=dev)
+    adt, gamma, beta = (torch.empty(B, T, H, dtype=torch.float32, device=dev) for _ in range(3))
+    theta = torch.empty(B, T, H, N // 4, dtype=torch.float32, device=dev)
+    for n, t in (("q", q), ("k_ext", k_ext), ("adt", adt), ("gamma", gamma), ("beta", beta), ("theta", theta)):
+        setattr(a, n, t.data_ptr())
+    if cache is not None:
+        a.theta0, a.kp0 = cache.theta.data_ptr(), cache.k_prev.data_ptr()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    _check(lib.zb_m3_prologue_fwd(ctypes.byref(a), stream), "zb_m3_prologue_fwd")
+    return a, (x, z), q, k_ext, adt, gamma, beta, theta, stream
+
+
+@torch.no_grad()
+def mamba3_layer_prefill(zxbc: Tensor, dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D, H: int, P: int, N: int,
+                         A_floor: float = 1e-4, chunk_size: int = 64, eps: float = 1e-5,
+                         scan_dtype: Optional[torch.dtype] = None):
+    """``mamba3_layer_packed`` over a prompt (T a multiple of chunk_size) without autograd, also
+    returning the ``LayerCache`` that continues it with ``mamba3_layer_step``."""
+    if zxbc.stride(-1) != 1:
+        zxbc = zxbc.contiguous()
+    op_dtype = _scan_dtype(zxbc, scan_dtype)
+    params = _fp32_params((dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D))
+    T = zxbc.shape[1]
+    if T % chunk_size != 0:
+        raise AssertionError("sequence length must be a multiple of chunk_size")  # mamba3.py:33
+    a, (x, z), q, k_ext, adt, gamma, beta, theta, stream = _prologue(zxbc, params, H, P, N, A_floor, eps, op_dtype,
+                                                                     None)
+    xs = x if x.dtype == op_dtype else x.to(op_dtype)
+    y, _, final = _scan_fwd(xs, q, k_ext[:, 1:], adt, gamma, beta, chunk_size, False)
+    out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    a.y, a.out = y.data_ptr(), _v(out)
+    _check(_lib().zb_m3_epilogue_fwd(ctypes.byref(a), stream), "zb_m3_epilogue_fwd")
+    cache = LayerCache(final, theta[:, -1].contiguous(), k_ext[:, -1].contiguous(), xs[:, -1].contiguous())
+    return out, cache
+
+
+@torch.no_grad()
+def mamba3_layer_step(zxbc: Tensor, dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D, H: int, P: int, N: int,
+                      cache: LayerCache, A_floor: float = 1e-4, eps: float = 1e-5) -> Tensor:
+    """The layer body for the next token(s) ``zxbc [B, T, n_in]`` (T usually 1) from ``cache``,
+    which it advances in place: the prologue continues theta and the k shift from the cache, the
+    scan runs in its recurrent form from the cached state (``zb_ssd_decode``), then the gate."""
+    if zxbc.stride(-1) != 1:
+        zxbc = zxbc.contiguous()
+    op_dtype = cache.k_prev.dtype
+    params = _fp32_params((dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D))
+    a, (x, z), q, k_ext, adt, gamma, beta, theta, stream = _prologue(zxbc, params, H, P, N, A_floor, eps, op_dtype,
+                                                                     cache)
+    xs = x if x.dtype == op_dtype else x.to(op_dtype)
+    xp = torch.cat((cache.x_prev[:, None], xs[:, :-1]), dim=1)
+    from .ssd import ssd_decode
+
+    y = ssd_decode(xs, q, k_ext[:, 1:], k_ext[:, :-1], xp, adt, gamma, beta, cache.state)
+    out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    a.y, a.out = y.data_ptr(), _v(out)
+    _check(_lib().zb_m3_epilogue_fwd(ctypes.byref(a), stream), "zb_m3_epilogue_fwd")
+    cache.theta.copy_(theta[:, -1])
+    cache.k_prev.copy_(k_ext[:, -1])
+    cache.x_prev.copy_(xs[:, -1])
+    return out
+
