@@ -110,3 +110,30 @@ def test_train_step_keeps_replicas_identical():
         assert p.exitcode == 0
     assert all(same for _, same, _ in res)
     assert res[0][2] == res[1][2]
+
+
+def test_lm_c_abi_rejects_bad_arguments_without_launching():
+    """The LM entry points validate on the host and return a status (no kernel runs): NULL
+    pointers, bad sizes and dtypes, a missing workspace."""
+    import ctypes
+
+    from zenith_b200 import _lib as L
+
+    lib = lm._lib()
+    a = lm.NormArgs(M=0, D=16, eps=1e-5, x_dtype=0, b_dtype=0, u_dtype=0)
+    assert lib.zb_rmsnorm_fwd(ctypes.byref(a), None) == 1          # ZB_ERR_SHAPE
+    a = lm.NormArgs(M=4, D=16, eps=1e-5, x_dtype=3, b_dtype=0, u_dtype=0)
+    assert lib.zb_rmsnorm_fwd(ctypes.byref(a), None) == 2          # ZB_ERR_DTYPE (fp64)
+    a = lm.NormArgs(M=4, D=16, eps=1e-5, x_dtype=0, b_dtype=0, u_dtype=0)
+    assert lib.zb_rmsnorm_fwd(ctypes.byref(a), None) == 3          # ZB_ERR_LAYOUT (no a / w)
+    a = lm.NormArgs(M=4, D=9000, eps=1e-5, x_dtype=0, b_dtype=0, u_dtype=0)
+    assert lib.zb_rmsnorm_fwd(ctypes.byref(a), None) == 7          # ZB_ERR_UNSUPPORTED (D > 8192)
+    a = lm.NormArgs(M=4, D=16, eps=1e-5, x_dtype=0, b_dtype=0, u_dtype=0)
+    a.a, a.w, a.du, a.dsum, a.dw, a.r = 16, 16, 16, 16, 16, 16     # never dereferenced: the workspace check fails first
+    assert lib.zb_rmsnorm_bwd(ctypes.byref(a), None) == 6          # ZB_ERR_WORKSPACE
+    assert lib.zb_rmsnorm_workspace_bytes(ctypes.byref(lm.NormArgs(M=10, D=64))) >= 10 * 64 * 4
+    x = lm.XentArgs(M=4, V=0, ld=0, dtype=1)
+    assert lib.zb_xent(ctypes.byref(x), None) == 1                 # ZB_ERR_SHAPE
+    x = lm.XentArgs(M=4, V=8, ld=8, dtype=1)
+    assert lib.zb_xent(ctypes.byref(x), None) == 3                 # ZB_ERR_LAYOUT (no pointers)
+    assert L.strerror(9).startswith("label outside")
