@@ -295,3 +295,15 @@ def test_generate_is_greedy_on_the_full_forward():
     with torch.no_grad():
         logits = model(padded, loops=2).logits
     assert torch.equal(logits[:, 39:51].argmax(-1), out[:, 40:52])
+
+
+def test_generate_with_a_cuda_graph_matches_eager():
+    """The CUDA-graph single-token step gives the same tokens as the eager steps (fp32 and bf16
+    autocast), with a prompt that leaves tokens to step through after the prefill."""
+    model = _tiny()
+    prompt = torch.randint(0, 1024, (3, 45), device=DEV)
+    for amp in (False, True):
+        with torch.autocast("cuda", dtype=torch.bfloat16, enabled=amp):
+            eager = model.generate(prompt, 10, loops=2, cuda_graph=False)
+            graphed = model.generate(prompt, 10, loops=2, cuda_graph=True)
+        assert torch.equal(eager, graphed), amp

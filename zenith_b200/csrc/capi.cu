@@ -3,6 +3,8 @@
 #include <atomic>
 #include <cstdio>
 #include <cstring>
+#include <map>
+#include <mutex>
 
 #include "ssd_kernels.h"
 #include "ssd_tc.h"
@@ -12,6 +14,21 @@ using namespace zb;
 namespace zb {
 static std::atomic<uint64_t> g_launches{0};
 void note_launches(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device) and size: later calls
+// with a size already granted make no CUDA call, so launches can also be captured in CUDA graphs.
+int dyn_smem(const void* fn, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> granted;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return ZB_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(mu);
+  int& have = granted[{fn, dev}];
+  if (bytes <= have) return ZB_OK;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return ZB_ERR_CUDA;
+  have = bytes;
+  return ZB_OK;
+}
 }  // namespace zb
 
 namespace {

@@ -550,7 +550,7 @@ extern "C" ZB_API int zb_rmsnorm_bwd(const zb_rmsnorm_args* a, void* stream) {
           return (int)ZB_OK;
         }
         auto k = rmsnorm_bwd_kernel<TX, TB, TU>;
-        if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        if (dyn_smem(reinterpret_cast<const void*>(k), smem) != ZB_OK)
           return (int)ZB_ERR_CUDA;
         k<<<grid, 32 * kNormWarps, smem, st>>>(p);
         return (int)ZB_OK;

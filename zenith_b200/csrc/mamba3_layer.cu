@@ -1188,7 +1188,7 @@ extern "C" ZB_API int zb_m3_prologue_fwd(const zb_m3_args* a, void* stream) {
   const int smem1 = (int)(kSeg * (2 * p.N + p.NA + p.hg) * sizeof(float));
   ZB_M3_DISPATCH(a->io_dtype, a->op_dtype, {
     auto k1 = m3_prologue_fwd_kernel<TI, TO>;
-    if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1) != cudaSuccess) return ZB_ERR_CUDA;
+    if (dyn_smem(reinterpret_cast<const void*>(k1), smem1) != ZB_OK) return ZB_ERR_CUDA;
     m3_segsum_kernel<TI><<<grid, block, smem0, s>>>(p);
     k1<<<grid, block, smem1, s>>>(p);
   });
@@ -1260,7 +1260,7 @@ extern "C" ZB_API int zb_m3_prologue_bwd(const zb_m3_args* a, void* stream) {
                         : (ring == 4   ? m3_prologue_bwd_kernel<TI, TO, 4, false>
                            : ring == 2 ? m3_prologue_bwd_kernel<TI, TO, 2, false>
                                        : m3_prologue_bwd_kernel<TI, TO, 1, false>);
-    if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1) != cudaSuccess) return ZB_ERR_CUDA;
+    if (dyn_smem(reinterpret_cast<const void*>(k1), smem1) != ZB_OK) return ZB_ERR_CUDA;
     if (p.vec8) {
       const unsigned slots = (unsigned)(p.H * p.P / 8), vthreads = slots * (slots >= 256 ? 1024 / slots : 4);
       m3_dx_vec_kernel<TI, TO><<<grid, vthreads, 0, s>>>(p);

@@ -37,5 +37,7 @@ int simt_launch(const SimtParams& p, int dtype, int sdtype, bool backward, cudaS
 
 // Count kernel launches for zb_launch_count().
 void note_launches(int n);
+// Raise a kernel's dynamic shared-memory limit to `bytes` (once per kernel, device and size).
+int dyn_smem(const void* fn, int bytes);
 
 }  // namespace zb

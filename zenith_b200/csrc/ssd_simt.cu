@@ -514,12 +514,12 @@ static int launch_simt(const SimtParams& p, bool backward, cudaStream_t stream) 
   const dim3 grid((unsigned)(p.B * p.H * p.nc)), block(kThreads);
   if (!backward) {
     auto k = ssd_fwd_simt_kernel<TI, TS, TA>;
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return ZB_ERR_CUDA;
+    if (dyn_smem(reinterpret_cast<const void*>(k), (int)smem) != ZB_OK) return ZB_ERR_CUDA;
     k<<<grid, block, smem, stream>>>(p);
     note_launches(1);
   } else {
     auto k = ssd_bwd_simt_kernel<TI, TS, TA>;
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return ZB_ERR_CUDA;
+    if (dyn_smem(reinterpret_cast<const void*>(k), (int)smem) != ZB_OK) return ZB_ERR_CUDA;
     k<<<grid, block, smem, stream>>>(p);
     note_launches(1);
     if (p.G != p.H && !(p.flags & ZB_FLAG_STATE_ONLY)) {

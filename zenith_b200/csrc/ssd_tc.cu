@@ -1410,7 +1410,7 @@ int launch_fwd(const zb_ssd_args* a, ChainSync sync, void* states, void* ring, c
   p.shift = (a->flags & ZB_FLAG_SHIFTED) ? 1 : 0;
   auto k = ssd_fwd_tc_kernel<NS>;
   const int smem = (int)FwdSmem<NS>::ALLOC;
-  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return ZB_ERR_CUDA;
+  if (dyn_smem(reinterpret_cast<const void*>(k), smem) != ZB_OK) return ZB_ERR_CUDA;
   const int64_t units = a->B * a->H * p.nc, slots = 2 * (int64_t)sm_count();  // persistent: two CTAs per SM
   const dim3 grid((unsigned)(units < slots ? units : slots));
   k<<<grid, kTcThreads, smem, stream>>>(p);
@@ -1461,7 +1461,7 @@ int launch_bwd(const zb_ssd_args* a, ChainSync sync, void* ring, cudaStream_t st
   p.shift = (a->flags & ZB_FLAG_SHIFTED) ? 1 : 0;
   auto k = ssd_bwd_tc_kernel<NS>;
   const int smem = (int)BwdSmem<NS>::ALLOC;
-  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return ZB_ERR_CUDA;
+  if (dyn_smem(reinterpret_cast<const void*>(k), smem) != ZB_OK) return ZB_ERR_CUDA;
   const int64_t units = a->B * a->H * p.nc;
   const dim3 grid((unsigned)(units < sm_count() ? units : sm_count()));  // persistent: one CTA per SM
   k<<<grid, kBwdThreads, smem, stream>>>(p);
@@ -1499,7 +1499,7 @@ int launch_state(const zb_ssd_args* a, ChainSync sync, void* ring, cudaStream_t 
   p.shift = (a->flags & ZB_FLAG_SHIFTED) ? 1 : 0;
   auto k = ssd_state_tc_kernel<NS, BACKWARD>;
   const int smem = (int)StateSmem<NS>::ALLOC;
-  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return ZB_ERR_CUDA;
+  if (dyn_smem(reinterpret_cast<const void*>(k), smem) != ZB_OK) return ZB_ERR_CUDA;
   k<<<(unsigned)(a->B * a->H * p.nc), kStThreads, smem, stream>>>(p);
   note_launches(1);
   return cudaPeekAtLastError() == cudaSuccess ? ZB_OK : ZB_ERR_CUDA;

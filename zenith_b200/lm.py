@@ -366,12 +366,14 @@ class ZenithForCausalLM(nn.Module):
         return torch.cat(outs, dim=1)
 
     @torch.no_grad()
-    def generate(self, input_ids: Tensor, max_new_tokens: int, loops: Optional[int] = None) -> Tensor:
+    def generate(self, input_ids: Tensor, max_new_tokens: int, loops: Optional[int] = None,
+                 cuda_graph: bool = True) -> Tensor:
         """Greedy decoding: the prompt is prefilled (its longest chunk_size-multiple prefix in one
         chunked pass, the rest token by token), then each new token is the argmax of the last
         logits and runs through the layers from their caches.  Returns the prompt followed by the
         new tokens.  The reference has no cache (model.py:79-99); this is the recurrent form of
-        its forward."""
+        its forward.  With ``cuda_graph`` the single-token step (a few hundred launches) is
+        captured once in a CUDA graph and replayed per token."""
         loops = loops or self.config.max_loops
         T, L = input_ids.shape[1], self.config.chunk_size
         pre = T // L * L
@@ -382,11 +384,15 @@ class ZenithForCausalLM(nn.Module):
         for t in range(pre, T):
             logits = _Generation.forward(self, input_ids[:, t:t + 1], caches, loops)
         ids = [input_ids]
+        step = None
         for i in range(max_new_tokens):
             nxt = logits[:, -1].argmax(-1, keepdim=True)
             ids.append(nxt)
-            if i + 1 < max_new_tokens:
-                logits = _Generation.forward(self, nxt, caches, loops)
+            if i + 1 == max_new_tokens:
+                break
+            if cuda_graph and step is None and caches:
+                step = _GraphStep(self, caches, loops, nxt)
+            logits = step(nxt) if step is not None else _Generation.forward(self, nxt, caches, loops)
         return torch.cat(ids, dim=1)
 
     def forward(self, input_ids: Tensor, labels: Optional[Tensor] = None, loops: Optional[int] = None,
@@ -461,6 +467,34 @@ class _Generation:
             s = stack("rec", model.recurrent_layers, h, t)
         s = stack("out", model.output_layers, s, 0)
         return model.lm_head(add_rmsnorm(s, None, model.norm.weight, model.norm.eps, _u_dtype(s)))
+
+
+class _GraphStep:
+    """One single-token generation step captured in a CUDA graph: the token goes into a static
+    buffer, the replay runs every kernel of the step (advancing the layer caches in place, which
+    the graph reads and writes at fixed addresses) and leaves the logits in a static buffer.  The
+    eager warm-up that capture needs would advance the caches, so they are restored after it."""
+
+    def __init__(self, model, caches: dict, loops: int, tok: Tensor):
+        self.tok = tok.clone()
+        saved = {k: (c.state.clone(), c.theta.clone(), c.k_prev.clone(), c.x_prev.clone()) for k, c in caches.items()}
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                _Generation.forward(model, self.tok, caches, loops)
+        torch.cuda.current_stream().wait_stream(side)
+        for k, c in caches.items():
+            for dst, src in zip((c.state, c.theta, c.k_prev, c.x_prev), saved[k]):
+                dst.copy_(src)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.logits = _Generation.forward(model, self.tok, caches, loops)
+
+    def __call__(self, tok: Tensor) -> Tensor:
+        self.tok.copy_(tok)
+        self.graph.replay()
+        return self.logits
 
 
 def load_reference_state_dict(model: ZenithForCausalLM, state_dict: dict):
