@@ -188,29 +188,16 @@ __global__ void __launch_bounds__(kRowMaxThreads) rmsnorm_fwd_row_kernel(const N
   TU* __restrict__ U = static_cast<TU*>(p.u);
   float w[8];
   if (on) Vec8<float>::ld(p.w + n, w);
-  // the next row's loads are issued before this row's reduction and stores
-  Pack8<TX> an;
-  Pack8<TB> bn;
-  int64_t row = blockIdx.x;
-  if (on && row < p.M) {
-    an.ld(A + row * D + n);
-    if (Bv) bn.ld(Bv + row * D + n);
-  }
-  for (; row < p.M; row += gridDim.x) {
+  for (int64_t row = blockIdx.x; row < p.M; row += gridDim.x) {
     const int64_t o = row * D + n;
-    const Pack8<TX> ac = an;
-    const Pack8<TB> bc = bn;
-    if (on && row + gridDim.x < p.M) {
-      an.ld(A + o + (int64_t)gridDim.x * D);
-      if (Bv) bn.ld(Bv + o + (int64_t)gridDim.x * D);
-    }
     float v[8], ss = 0.f;
     if (on) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = ac.get(e);
+      Vec8<TX>::ld(A + o, v);
       if (Bv) {
+        float c[8];
+        Vec8<TB>::ld(Bv + o, c);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = round_to<TX>(v[e] + bc.get(e));
+        for (int e = 0; e < 8; ++e) v[e] = round_to<TX>(v[e] + c[e]);
         Vec8<TX>::st(S + o, v);
       }
 #pragma unroll
@@ -295,19 +282,10 @@ __global__ void __launch_bounds__(256) rmsnorm_dw_kernel(const NormP p, int nblo
   __shared__ float sm[8][33];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = blockIdx.x * 32 + lane;
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;  // four loads in flight; summed in a fixed order
-  if (n < p.D) {
-    const float* src = p.part + n;
-    int k = warp;
-    for (; k + 24 < nblocks; k += 32) {
-      s0 += src[(int64_t)k * p.D];
-      s1 += src[(int64_t)(k + 8) * p.D];
-      s2 += src[(int64_t)(k + 16) * p.D];
-      s3 += src[(int64_t)(k + 24) * p.D];
-    }
-    for (; k < nblocks; k += 8) s0 += src[(int64_t)k * p.D];
-  }
-  sm[warp][lane] = (s0 + s1) + (s2 + s3);
+  float s = 0.f;
+  if (n < p.D)
+    for (int k = warp; k < nblocks; k += 8) s += p.part[(int64_t)k * p.D + n];
+  sm[warp][lane] = s;
   __syncthreads();
   if (warp == 0 && n < p.D) {
     float t = 0.f;

@@ -1024,18 +1024,10 @@ __global__ void __launch_bounds__(256) m3_param_reduce_kernel(const M3 p) {
     stride = H;
     dst = (part ? p.dD : p.ddt_bias) + j;
   }
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;  // four loads in flight; summed in a fixed order
-  if (src) {
-    int64_t k = warp;
-    for (; k + 24 < BS; k += 32) {
-      s0 += src[k * stride];
-      s1 += src[(k + 8) * stride];
-      s2 += src[(k + 16) * stride];
-      s3 += src[(k + 24) * stride];
-    }
-    for (; k < BS; k += 8) s0 += src[k * stride];
-  }
-  sm[warp][lane] = (s0 + s1) + (s2 + s3);
+  float s = 0.f;
+  if (src)
+    for (int64_t k = warp; k < BS; k += 8) s += src[k * stride];
+  sm[warp][lane] = s;
   __syncthreads();
   if (warp == 0 && dst) {
     float t = 0.f;
