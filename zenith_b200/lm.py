@@ -13,7 +13,7 @@ LM head, next-token cross-entropy.  What runs where:
   tcgen05 SSD scan, epilogue), reading the packed in_proj output and writing its gradient as one
   tensor;
 - in_proj / out_proj / LM head GEMMs: cuBLAS through torch (bf16 under autocast, as the
-  reference's ``train.py`` runs them);
+  reference's ``train.py`` runs them), the weight gradients written in float32 by the GEMM;
 - the next-token cross-entropy: ``zb_xent`` computes each row's loss and overwrites the logits
   with their gradient in the same pass, so no float32 logits or softmax are ever stored.
 
@@ -188,7 +188,10 @@ class _LinearCrossEntropy(torch.autograd.Function):
         scale = gl / n_valid
         with _fp32_reductions():
             dh = (g @ wc).mul_(scale.to(g.dtype))
-            dw = (g.t() @ hc).mul_(scale.to(g.dtype))
+            if g.dtype != torch.float32 and ctx.dtypes[1] == torch.float32:
+                dw = torch.mm(g.t(), hc, out_dtype=torch.float32).mul_(scale)  # fp32 straight from the GEMM
+            else:
+                dw = (g.t() @ hc).mul_(scale.to(g.dtype))
         return dh.to(ctx.dtypes[0]), dw.to(ctx.dtypes[1]), None, None, None
 
 
@@ -244,6 +247,41 @@ class RMSNorm(nn.Module):
         return add_rmsnorm(x, None, self.weight, self.eps)
 
 
+class _AutocastLinear(torch.autograd.Function):
+    """``x @ w.T`` as bf16 autocast runs it (bf16 operands, bf16 output), except that the weight
+    gradient comes out of the GEMM in float32 (cuBLAS with an fp32 output) instead of as a bf16
+    tensor cast up to the float32 parameter's dtype in a separate pass."""
+
+    @staticmethod
+    def forward(ctx, x, w):
+        xb, wb = x.to(torch.bfloat16), w.to(torch.bfloat16)
+        ctx.save_for_backward(xb, wb)
+        ctx.x_dtype = x.dtype
+        return xb @ wb.t()
+
+    @staticmethod
+    def backward(ctx, gy):
+        xb, wb = ctx.saved_tensors
+        g2 = gy.reshape(-1, gy.shape[-1]).to(torch.bfloat16)
+        dx = dw = None
+        if ctx.needs_input_grad[0]:
+            dx = (g2 @ wb).view(xb.shape).to(ctx.x_dtype)
+        if ctx.needs_input_grad[1]:
+            dw = torch.mm(g2.t(), xb.reshape(-1, xb.shape[-1]), out_dtype=torch.float32)
+        return dx, dw
+
+
+def _proj(lin: nn.Linear, x: Tensor) -> Tensor:
+    """A bias-free projection: ``_AutocastLinear`` for a float32 weight under CUDA bf16 autocast
+    with gradients on, else the module itself."""
+    w = lin.weight
+    if (x.is_cuda and w.dtype == torch.float32 and torch.is_grad_enabled() and torch.is_autocast_enabled("cuda")
+            and torch.get_autocast_dtype("cuda") == torch.bfloat16):
+        with torch.autocast("cuda", enabled=False):
+            return _AutocastLinear.apply(x, w)
+    return lin(x)
+
+
 class Mamba3(nn.Module):
     """The reference ``Mamba3`` mixer (zenith/mamba3.py:58-120) on the fused layer body."""
 
@@ -268,13 +306,13 @@ class Mamba3(nn.Module):
 
     def forward(self, u: Tensor) -> Tensor:
         Bsz, T, _ = u.shape
-        zxbc = self.in_proj(u)
+        zxbc = _proj(self.in_proj, u)
         if zxbc.dtype not in (torch.float32, torch.bfloat16):
             zxbc = zxbc.float()
         y = mamba3_layer_packed(zxbc, self.dt_bias, self.B_bias, self.C_bias, self.B_norm.weight,
                                 self.C_norm.weight, self.D, self.nheads, self.headdim, self.d_state, self.A_floor,
                                 self.chunk_size, self.B_norm.eps)
-        return self.out_proj(y.reshape(Bsz, T, self.d_inner))
+        return _proj(self.out_proj, y.reshape(Bsz, T, self.d_inner))
 
 
 class Layer(nn.Module):
