@@ -88,6 +88,33 @@ def test_linear_cross_entropy_matches_torch(dtype, V):
     assert max_rel_err(lW.grad.double().cpu(), rW.grad) < tol
 
 
+@pytest.mark.parametrize("x_dtype", [torch.bfloat16, torch.float32])
+def test_autocast_projection_matches_float64(x_dtype):
+    """The LM's bias-free projection under bf16 autocast: output and input gradient as bf16
+    autocast gives them, the float32 weight gradient straight from the GEMM; all against float64
+    on the bf16-rounded operands (2e-2, and 1e-5 for the weight gradient, which sees no bf16
+    output rounding)."""
+    from zenith_b200 import lm
+
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(2, 300, 96, generator=g).to(x_dtype)
+    lin = torch.nn.Linear(96, 200, bias=False).to(DEV)
+    dy = torch.randn(2, 300, 200, generator=g)
+    lx = x.to(DEV).requires_grad_()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y = lm._proj(lin, lx)
+    assert y.dtype == torch.bfloat16
+    y.backward(dy.to(DEV, torch.bfloat16))
+    assert lx.grad.dtype == x_dtype and lin.weight.grad.dtype == torch.float32
+    rx = x.to(torch.bfloat16).double().requires_grad_()
+    rw = lin.weight.detach().cpu().to(torch.bfloat16).double().requires_grad_()
+    ry = rx @ rw.T
+    ry.backward(dy.to(torch.bfloat16).double())
+    assert max_rel_err(y.double().cpu(), ry) < 2e-2
+    assert max_rel_err(lx.grad.double().cpu(), rx.grad) < 2e-2
+    assert max_rel_err(lin.weight.grad.double().cpu(), rw.grad) < 1e-5
+
+
 def test_cross_entropy_rejects_out_of_range_labels():
     """A label outside [0, V) sets the device status word (the row is skipped, nothing faults)."""
     import zenith_b200
