@@ -147,6 +147,15 @@ ZB_API int zb_ssd_kernel_family(const zb_ssd_args* args, int states_saved);
  * No reference counterpart: lets a benchmark count the GPU launches of a timed region. */
 ZB_API uint64_t zb_launch_count(void);
 
+/* Diagnostic, no reference counterpart: runs one of the library's bounded device-side waits on its
+ * own so that a test can watch it give up.  which = 0: the chained hand-off wait on `*flag` (device
+ * int; it ends when the flag becomes 1, another nonzero value, or *status is nonzero); which = 1:
+ * a wait on a fresh mbarrier that never completes (`flag` unused).  After about one second the
+ * wait records ZB_ERR_TIMEOUT in *status (device int32, left alone if already nonzero) and returns.
+ * result (device int32[2]): [0] what the wait returned (flag: 1 ready, 2 aborted; mbarrier: 1
+ * completed, 0 gave up), [1] microseconds it took.  One thread, one launch; nothing faults. */
+ZB_API int zb_wait_probe(const int* flag, int32_t* status, int32_t* result, int which, void* stream);
+
 /* Size of the fixed device scratch array behind zb_ssd_fwd_noalloc (32 MiB per GPU). */
 #define ZB_NOALLOC_SCRATCH_BYTES (32u << 20)
 

@@ -13,7 +13,7 @@ PKG = pathlib.Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libzenith_ssd.so"
-SOURCES = ["capi.cu", "capi_noalloc.cu", "ssd_simt.cu", "ssd_tc.cu", "mamba3_layer.cu", "ssd_decode.cu", "lm_kernels.cu"]
+SOURCES = ["capi.cu", "capi_noalloc.cu", "ssd_simt.cu", "ssd_tc.cu", "mamba3_layer.cu", "ssd_decode.cu", "lm_kernels.cu", "wait_probe.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
