@@ -3,6 +3,7 @@ the CPU oracle, injected through zenith_b200.parallel.LocalScan, so these tests 
 exchange logic (chain order, state combine, gradient hand-back) without a GPU."""
 import datetime
 import os
+import time
 
 import torch
 import torch.distributed as dist
@@ -38,10 +39,10 @@ def oracle_scan() -> LocalScan:
     return LocalScan(final_state, forward, dinitial, backward, total_decay, combine)
 
 
-def _init(rank, world, port):
+def _init(rank, world, port, timeout_s=20):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
 
 
 def shape_for(world):
@@ -84,3 +85,38 @@ def cp_failure_worker(rank, world, port, outdir):
         result = "error: " + type(e).__name__
     with open(os.path.join(outdir, f"rank{rank}.txt"), "w") as f:
         f.write(result)
+
+
+def _run_and_record(rank, outdir, s, sl):
+    inp = make_inputs(s, seed=11)
+    leaves = [inp[n][:, sl].double().requires_grad_() for n in NAMES]
+    try:
+        y = cp_ssd(*leaves, s.chunk, impl=oracle_scan())
+        y.sum().backward()
+        result = "no error"
+    except Exception as e:  # noqa: BLE001 - the test checks which error
+        result = "error: " + type(e).__name__ + ": " + str(e).splitlines()[0][:200]
+    with open(os.path.join(outdir, f"rank{rank}.txt"), "w") as f:
+        f.write(result)
+
+
+def cp_mismatch_worker(rank, world, port, outdir):
+    """Rank 1 passes a local range with a larger head dimension P (a state of another size): every
+    rank must raise ValueError before any state is sent."""
+    _init(rank, world, port)
+    s = shape_for(world)
+    if rank == 1:
+        s = SsdShape(s.B, s.T, s.H, s.P + 1, s.N, s.G, s.chunk)
+    Tl = s.T // world
+    _run_and_record(rank, outdir, s, slice(rank * Tl, (rank + 1) * Tl))
+
+
+def cp_delay_worker(rank, world, port, outdir):
+    """Rank 1 stalls past the process group's timeout before the exchange: rank 0 must end with an
+    error (the timeout), not wait for it."""
+    _init(rank, world, port, timeout_s=4)
+    s = shape_for(world)
+    if rank == 1:
+        time.sleep(10)
+    Tl = s.T // world
+    _run_and_record(rank, outdir, s, slice(rank * Tl, (rank + 1) * Tl))

@@ -8,7 +8,10 @@ import torch
 import torch.multiprocessing as mp
 
 from oracle.ssd_oracle import max_rel_err, ssd_backward, ssd_forward
-from tests.cp_workers import NAMES, cp_failure_worker, cp_parity_worker, shape_for
+import time
+
+from tests.cp_workers import (NAMES, cp_delay_worker, cp_failure_worker, cp_mismatch_worker, cp_parity_worker,
+                             shape_for)
 from zenith_b200.synthetic import make_inputs
 
 
@@ -48,3 +51,29 @@ def test_context_parallel_rank_failure_ends_in_an_error_not_a_hang(tmp_path):
         assert not p.is_alive(), "a rank hung"
     msg = (tmp_path / "rank0.txt").read_text() if (tmp_path / "rank0.txt").exists() else "rank 0 died"
     assert msg.startswith("error") or msg == "rank 0 died", msg
+
+
+def _run_pair(worker, tmp_path, bound_s):
+    """Start two ranks of `worker`; both must exit within `bound_s` seconds; returns what each
+    recorded."""
+    t0 = time.monotonic()
+    ctx = mp.start_processes(worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=False, start_method="spawn")
+    while not ctx.join(timeout=5):
+        assert time.monotonic() - t0 < bound_s, "a rank hung"
+    return [(tmp_path / f"rank{r}.txt").read_text() for r in range(2)]
+
+
+def test_context_parallel_shape_mismatch_raises_on_every_rank(tmp_path):
+    """A rank whose local range has another state size: ValueError on both ranks, before any
+    send / recv of a state."""
+    res = _run_pair(cp_mismatch_worker, tmp_path, 120)
+    for r in res:
+        assert r.startswith("error: ValueError: cp_ssd: the ranks' local ranges differ"), r
+
+
+def test_context_parallel_stalled_rank_ends_in_a_timeout_not_a_hang(tmp_path):
+    """Rank 1 sleeps past the 4 s process-group timeout before the exchange: rank 0's first
+    collective ends with an error; rank 1, arriving late, ends with one too."""
+    res = _run_pair(cp_delay_worker, tmp_path, 120)
+    assert res[0].startswith("error: ") and "Timed out" in res[0], res[0]
+    assert res[1].startswith("error: "), res[1]

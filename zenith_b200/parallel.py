@@ -17,7 +17,8 @@ backward
   3. every rank: the full local backward with dfinal = E_r.
 
 Ranks hold data in the caller's layout ([B, T_local, H, ...]).  The exchange is collective: every
-rank of the group must call with equally shaped local ranges.
+rank of the group must call with equally shaped local ranges (checked first, by one small all_gather:
+a mismatch raises ValueError on every rank).
 """
 
 from __future__ import annotations
@@ -133,6 +134,20 @@ def _chain_backward(G, D, group, dfinal, impl: LocalScan):
     return E
 
 
+def _check_local_shapes(x, q, group):
+    """Every rank must pass an equally shaped local range: the exchanged state is [B, H, P, N], and
+    a send / recv pair of different sizes is undefined under NCCL.  One all_gather of each rank's
+    (B, T_local, H, P, N, G) makes a mismatch raise the same ValueError on every rank."""
+    sig = torch.tensor([x.shape[0], x.shape[1], x.shape[2], x.shape[3], q.shape[3], q.shape[2]], dtype=torch.int64,
+                       device=x.device)
+    parts = [torch.empty_like(sig) for _ in range(dist.get_world_size(group))]
+    dist.all_gather(parts, sig, group=group)
+    sigs = [tuple(t.tolist()) for t in parts]
+    if any(t != sigs[0] for t in sigs):
+        raise ValueError("cp_ssd: the ranks' local ranges differ in shape (B, T_local, H, P, N, G by rank): "
+                         + str(sigs))
+
+
 class _CpScan(torch.autograd.Function):
     @staticmethod
     def forward(ctx, chunk, group, impl, init, x, q, k, kp, xp, adt, gamma, beta):
@@ -166,6 +181,7 @@ def cp_ssd(x, q, k, kp, xp, adt, gamma, beta, chunk_size, *, group=None, initial
     ``initial_state`` (rank 0 only) starts the sequence from a given state.
     """
     assert x.shape[1] % chunk_size == 0, "sequence length must be a multiple of chunk_size"
+    _check_local_shapes(x, q, group)
     impl = impl or CUDA_SCAN
     if impl is CUDA_SCAN:
         args = prepare_inputs(x, q, k, kp, xp, adt, gamma, beta)
