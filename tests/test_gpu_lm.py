@@ -64,9 +64,14 @@ def test_add_rmsnorm_matches_torch(x_dtype, b_dtype, u_dtype, D):
 
 @pytest.mark.parametrize("dtype,V", [(torch.float32, 1000), (torch.float32, 999), (torch.bfloat16, 32000),
                                      (torch.bfloat16, 50001), (torch.float32, 8)])
-def test_linear_cross_entropy_matches_torch(dtype, V):
+@pytest.mark.parametrize("chunk_rows", [None, 64])
+def test_linear_cross_entropy_matches_torch(dtype, V, chunk_rows, monkeypatch):
+    """One row chunk, or chunks of 64 rows (the last of the 300 ragged) with the weight gradient
+    accumulated over them."""
     from zenith_b200 import lm
 
+    if chunk_rows:
+        monkeypatch.setattr(lm, "_CE_CHUNK_BYTES", chunk_rows * V * (4 if dtype == torch.float32 else 2))
     g = torch.Generator().manual_seed(V)
     M, d = 300, 64
     h = torch.randn(M, d, generator=g)

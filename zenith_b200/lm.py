@@ -14,8 +14,9 @@ LM head, next-token cross-entropy.  What runs where:
   tensor;
 - in_proj / out_proj / LM head GEMMs: cuBLAS through torch (bf16 under autocast, as the
   reference's ``train.py`` runs them), the weight gradients written in float32 by the GEMM;
-- the next-token cross-entropy: ``zb_xent`` computes each row's loss and overwrites the logits
-  with their gradient in the same pass, so no float32 logits or softmax are ever stored.
+- the next-token cross-entropy: row chunk by row chunk, ``zb_xent`` computes each row's loss and
+  overwrites the logits with their gradient in the same pass, and the gradient GEMMs consume the
+  chunk at once, so the logits never exist whole and no float32 logits or softmax are stored.
 
 ``train_step`` is one optimiser step (autocast forward, backward, gradient clipping, AdamW),
 with the gradient all-reduce of ``DistributedDataParallel`` over NCCL when the model is wrapped.
@@ -163,51 +164,76 @@ class _fp32_reductions:
         torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = self.prev
 
 
+_CE_CHUNK_BYTES = 256 << 20  # logits of one row chunk of the fused loss
+
+
 class _LinearCrossEntropy(torch.autograd.Function):
+    """The loss is the graph's last operation, so its gradient with respect to the logits is
+    known in the forward: each row chunk's logits are computed, turned into per-row losses and
+    ``softmax - onehot`` in place by ``zb_xent``, and (when a gradient is wanted) fed straight to
+    the two gradient GEMMs.  Only one chunk of logits exists at a time; the backward scales the
+    stored gradients by ``dloss / n_valid``."""
+
     @staticmethod
-    def forward(ctx, h, weight, labels, ignore_index, compute_dtype):
+    def forward(ctx, h, weight, labels, ignore_index, compute_dtype, need_grad):
         dev = h.device
         hc = h.to(compute_dtype)
         wc = weight.to(compute_dtype)
-        with _fp32_reductions():
-            logits = hc @ wc.t()                                 # [M, V] (cuBLAS)
-        M, V = logits.shape
+        M, V = hc.shape[0], wc.shape[0]
+        rows = max(1, min(M, _CE_CHUNK_BYTES // (V * hc.element_size())))
         loss_rows = torch.empty(M, dtype=torch.float32, device=dev)
-        args = XentArgs(M=M, V=V, ld=logits.stride(0), dtype=_code(logits.dtype), write_grad=1,
-                        ignore_index=int(ignore_index), logits=logits.data_ptr(), labels=labels.data_ptr(),
-                        loss=loss_rows.data_ptr(), lse=None, status=L.status_word(dev).data_ptr())
-        L.check(_lib().zb_xent(ctypes.byref(args), _stream(dev)), "zb_xent")
+        dh = torch.empty_like(hc) if need_grad else None
+        dw = None
+        status = L.status_word(dev).data_ptr()
+        lib = _lib()
+        with _fp32_reductions():
+            for r0 in range(0, M, rows):
+                r1 = min(M, r0 + rows)
+                logits = hc[r0:r1] @ wc.t()                                # [rows, V] (cuBLAS)
+                args = XentArgs(M=r1 - r0, V=V, ld=logits.stride(0), dtype=_code(logits.dtype), write_grad=1,
+                                ignore_index=int(ignore_index), logits=logits.data_ptr(),
+                                labels=labels[r0:r1].data_ptr(), loss=loss_rows[r0:r1].data_ptr(), lse=None,
+                                status=status)
+                L.check(lib.zb_xent(ctypes.byref(args), _stream(dev)), "zb_xent")
+                if not need_grad:
+                    continue
+                # the logits now hold softmax - onehot: this chunk's share of both gradients, unscaled
+                torch.mm(logits, wc, out=dh[r0:r1])
+                gt, hr = logits.t(), hc[r0:r1]
+                if compute_dtype == torch.float32:
+                    dw = gt @ hr if dw is None else dw.addmm_(gt, hr)
+                else:   # accumulated in float32 by the GEMM itself
+                    dw = (torch.mm(gt, hr, out_dtype=torch.float32) if dw is None
+                          else torch.addmm(dw, gt, hr, out_dtype=torch.float32, out=dw))
         n_valid = (labels != ignore_index).sum().clamp_(min=1).to(torch.float32)
-        ctx.save_for_backward(hc, wc, logits, n_valid)          # logits now hold softmax - onehot
+        ctx.save_for_backward(dh, dw, n_valid)
         ctx.dtypes = (h.dtype, weight.dtype)
         return loss_rows.sum() / n_valid
 
     @staticmethod
     def backward(ctx, gl):
-        hc, wc, g, n_valid = ctx.saved_tensors
+        dh, dw, n_valid = ctx.saved_tensors
         scale = gl / n_valid
-        with _fp32_reductions():
-            dh = (g @ wc).mul_(scale.to(g.dtype))
-            if g.dtype != torch.float32 and ctx.dtypes[1] == torch.float32:
-                dw = torch.mm(g.t(), hc, out_dtype=torch.float32).mul_(scale)  # fp32 straight from the GEMM
-            else:
-                dw = (g.t() @ hc).mul_(scale.to(g.dtype))
-        return dh.to(ctx.dtypes[0]), dw.to(ctx.dtypes[1]), None, None, None
+        gh = dh.float().mul_(scale).to(ctx.dtypes[0]) if ctx.needs_input_grad[0] else None
+        gw = (dw * scale).to(ctx.dtypes[1]) if ctx.needs_input_grad[1] else None
+        return gh, gw, None, None, None, None
 
 
 def linear_cross_entropy(h: Tensor, weight: Tensor, labels: Tensor, ignore_index: int = -100,
                          compute_dtype: Optional[torch.dtype] = None) -> Tensor:
     """``F.cross_entropy(h @ weight.T, labels)`` (mean over rows whose label is not
-    ``ignore_index``) without storing float32 logits: the logits GEMM runs in ``compute_dtype``
-    (bf16 under CUDA autocast, else h's dtype), then ``zb_xent`` turns each row into its loss and
-    its gradient ``softmax - onehot`` in place; the backward is two GEMMs on that gradient.
+    ``ignore_index``) without storing the logits: row chunk by row chunk (about 256 MB of logits
+    each), the logits GEMM runs in ``compute_dtype`` (bf16 under CUDA autocast, else h's dtype),
+    ``zb_xent`` turns each row into its loss and its gradient ``softmax - onehot`` in place, and
+    the gradient GEMMs consume the chunk at once (the weight gradient accumulated in float32).
     ``h``: ``[M, d]``; ``weight``: ``[V, d]``; ``labels``: ``[M]`` int64."""
     if compute_dtype is None:
         ac = torch.is_autocast_enabled("cuda")
         compute_dtype = torch.get_autocast_dtype("cuda") if ac else h.dtype
     labels = labels.contiguous().to(torch.int64)
+    need_grad = torch.is_grad_enabled() and (h.requires_grad or weight.requires_grad)
     with torch.autocast("cuda", enabled=False):
-        return _LinearCrossEntropy.apply(h.contiguous(), weight, labels, ignore_index, compute_dtype)
+        return _LinearCrossEntropy.apply(h.contiguous(), weight, labels, ignore_index, compute_dtype, need_grad)
 
 
 # ---------------------------------------------------------------------------------------------
