@@ -79,6 +79,14 @@ def test_entry_points_validate_before_touching_the_gpu():
     a.status = None
     assert lib.zb_ssd_fwd(ctypes.byref(a), None) != 0
     assert lib.zb_strerror(L.ZB_ERR_TIMEOUT).decode().startswith("timed out")
+    # the bounded-wait probe: missing pointers or an unknown wait are refused before any launch
+    probe = lib.zb_wait_probe
+    probe.restype = ctypes.c_int
+    probe.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+    assert probe(None, 16, 16, 0, None) == 3     # ZB_ERR_LAYOUT: the flag wait needs a flag
+    assert probe(16, None, 16, 0, None) == 3     # no status word
+    assert probe(16, 16, None, 1, None) == 3     # no result buffer
+    assert probe(16, 16, 16, 2, None) == 7       # ZB_ERR_UNSUPPORTED: no such wait
 
 
 def test_python_entry_raises_reference_assertion_message():
