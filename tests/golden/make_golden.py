@@ -2,7 +2,8 @@
 
 Run in a container that has the reference checked out (read-only is fine):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <checkout of the reference project>
+    (or set ZENITH_REFERENCE to that directory)
 
 For every case it imports ``zenith.mamba3.ssd`` (zenith/mamba3.py:30-56) from the reference,
 runs it in float64 with PyTorch autograd on seeded inputs, and stores the inputs, the output
@@ -24,6 +25,7 @@ run time reads the reference.
 from __future__ import annotations
 
 import argparse
+import os
 import importlib.util
 import pathlib
 import sys
@@ -165,9 +167,12 @@ def lm_case(cfg, B, T, loops, seed):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("ZENITH_REFERENCE"),
+                    help="directory of the reference project (the one holding zenith/); default $ZENITH_REFERENCE")
     ap.add_argument("--only", choices=("ssd", "mamba3", "lm"), help="write one group of fixtures")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set ZENITH_REFERENCE")
     sys.path.insert(0, args.reference)
     from zenith.mamba3 import ssd  # the reference's own chunked scan
 

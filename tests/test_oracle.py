@@ -102,3 +102,46 @@ def test_lm_oracle_matches_reference_model(case):
         else:
             assert max_rel_err(o_grads[n], g.double()) < 5e-5, (n, max_rel_err(o_grads[n], g.double()))
 
+
+
+# ------------------------------------------------------------------------------------------------
+# the long-sequence C oracle (per-token recurrence and its adjoint, oracle/ssd_recurrence.c)
+
+from oracle.recurrence import recurrence_backward, recurrence_forward  # noqa: E402
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_recurrence_oracle_matches_reference_golden(case):
+    """Forward, final state and all eight gradients of the recurrence oracle against the
+    reference's own ssd and its autograd (goldens)."""
+    inp, out, L = load(case)
+    args = [inp[n] for n in NAMES]
+    y, fin = recurrence_forward(*args)
+    tol = 1e-11 if out["y"].dtype == torch.float64 else 1e-6
+    assert max_rel_err(y, out["y"]) < tol
+    assert max_rel_err(fin, out["final_state"]) < tol
+    g = recurrence_backward(inp["dy"], *args)
+    for n in NAMES:
+        assert max_rel_err(g["d" + n], out["d" + n]) < tol, n
+
+
+def test_recurrence_oracle_matches_chunked_oracle_with_states_and_groups():
+    """Initial state, final-state gradient, grouped q/k and a length that is not a multiple of the
+    checkpoint interval: the recurrence oracle against the chunked oracle."""
+    g = torch.Generator().manual_seed(11)
+    B, T, H, G, P, N = 2, 200, 4, 2, 5, 7
+    x, xp = torch.randn(2, B, T, H, P, generator=g, dtype=torch.float64)
+    q, k, kp = torch.randn(3, B, T, G, N, generator=g, dtype=torch.float64)
+    adt = -0.3 * torch.rand(B, T, H, generator=g, dtype=torch.float64)
+    ga, be = torch.rand(2, B, T, H, generator=g, dtype=torch.float64)
+    s0 = torch.randn(B, H, P, N, generator=g, dtype=torch.float64)
+    dy = torch.randn(B, T, H, P, generator=g, dtype=torch.float64)
+    dfin = torch.randn(B, H, P, N, generator=g, dtype=torch.float64)
+    args = (x, q, k, kp, xp, adt, ga, be)
+    y, fin = recurrence_forward(*args, initial_state=s0)
+    yr, finr, _ = ssd_forward(*args, 8, initial_state=s0)
+    assert max_rel_err(y, yr) < 1e-12 and max_rel_err(fin, finr) < 1e-12
+    got = recurrence_backward(dy, *args, initial_state=s0, dfinal=dfin)
+    ref = ssd_backward(dy, *args, 8, initial_state=s0, dfinal=dfin)
+    for n in NAMES + ("initial_state",):
+        assert max_rel_err(got["d" + n], ref["d" + n]) < 1e-11, n
