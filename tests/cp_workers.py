@@ -28,7 +28,7 @@ def oracle_scan() -> LocalScan:
 
     def backward(dy, inp, saved, chunk, init, dfinal):
         g = ssd_backward(dy, *inp, chunk, initial_state=init, dfinal=dfinal)
-        return tuple(g["d" + n] for n in NAMES)
+        return tuple(g["d" + n] for n in NAMES + ("initial_state",))
 
     def total_decay(adt):
         return torch.exp(adt.sum(1))
@@ -66,6 +66,27 @@ def cp_parity_worker(rank, world, port, outdir):
     dist.destroy_process_group()
 
 
+def cp_initial_state_worker(rank, world, port, outdir):
+    """An initial state on rank 0 (the other ranks pass one too, which they must ignore): outputs,
+    input gradients and rank 0's initial-state gradient."""
+    _init(rank, world, port)
+    s = shape_for(world)
+    inp = make_inputs(s, seed=12)
+    s0 = torch.randn(s.B, s.H, s.P, s.N, generator=torch.Generator().manual_seed(5), dtype=torch.float64)
+    Tl = s.T // world
+    sl = slice(rank * Tl, (rank + 1) * Tl)
+    leaves = [inp[n][:, sl].double().clone().requires_grad_() for n in NAMES]
+    init = (s0 if rank == 0 else torch.zeros_like(s0)).clone().requires_grad_()
+    y = cp_ssd(*leaves, s.chunk, impl=oracle_scan(), initial_state=init)
+    y.backward(inp["dy"][:, sl].double())
+    out = {"y": y.detach(), "dinitial_state": init.grad}
+    for n, t in zip(NAMES, leaves):
+        out["d" + n] = t.grad.detach()
+    torch.save(out, os.path.join(outdir, f"rank{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def cp_failure_worker(rank, world, port, outdir):
     """Rank 1 fails before the exchange; rank 0 must end with an error, not hang."""
     _init(rank, world, port)
@@ -77,7 +98,7 @@ def cp_failure_worker(rank, world, port, outdir):
         raise RuntimeError("injected failure on rank 1")
     leaves = [inp[n][:, sl].double() for n in NAMES]
     try:
-        # rank 0 sends its final state to rank 1, then (backward) would wait for rank 1
+        # rank 0 waits in the exchange's all_gather for rank 1, which never arrives
         y = cp_ssd(*(t.requires_grad_() for t in leaves), s.chunk, impl=oracle_scan())
         y.sum().backward()
         result = "no error"

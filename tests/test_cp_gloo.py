@@ -10,8 +10,8 @@ import torch.multiprocessing as mp
 from oracle.ssd_oracle import max_rel_err, ssd_backward, ssd_forward
 import time
 
-from tests.cp_workers import (NAMES, cp_delay_worker, cp_failure_worker, cp_mismatch_worker, cp_parity_worker,
-                             shape_for)
+from tests.cp_workers import (NAMES, cp_delay_worker, cp_failure_worker, cp_initial_state_worker, cp_mismatch_worker,
+                             cp_parity_worker, shape_for)
 from zenith_b200.synthetic import make_inputs
 
 
@@ -35,6 +35,26 @@ def test_context_parallel_matches_whole_sequence(world, tmp_path):
     for n in NAMES:
         got = torch.cat([p["d" + n] for p in parts], 1)
         assert max_rel_err(got, g["d" + n]) < 1e-11, n
+
+
+def test_context_parallel_initial_state_and_its_gradient_on_rank_zero(tmp_path):
+    """initial_state starts the whole sequence (rank 0's is used, the others' ignored) and rank 0
+    gets its gradient; the other ranks' initial states get none."""
+    world = 3
+    mp.start_processes(cp_initial_state_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    s = shape_for(world)
+    inp = make_inputs(s, seed=12)
+    s0 = torch.randn(s.B, s.H, s.P, s.N, generator=torch.Generator().manual_seed(5), dtype=torch.float64)
+    args = [inp[n].double() for n in NAMES]
+    y, _, _ = ssd_forward(*args, s.chunk, initial_state=s0)
+    g = ssd_backward(inp["dy"].double(), *args, s.chunk, initial_state=s0)
+    parts = [torch.load(tmp_path / f"rank{r}.pt") for r in range(world)]
+    assert max_rel_err(torch.cat([p["y"] for p in parts], 1), y) < 1e-12
+    for n in NAMES:
+        assert max_rel_err(torch.cat([p["d" + n] for p in parts], 1), g["d" + n]) < 1e-11, n
+    assert max_rel_err(parts[0]["dinitial_state"], g["dinitial_state"]) < 1e-11
+    assert all(p["dinitial_state"] is None for p in parts[1:])
 
 
 def test_context_parallel_rank_failure_ends_in_an_error_not_a_hang(tmp_path):

@@ -5,16 +5,19 @@ recurrence is linear, S_out = D S_in + F with D = exp(sum adt) over a range and 
 state from a zero start, a sequence split over ranks needs only the boundary states:
 
 forward
-  1. every rank: F_r = final state of its range from zero, D_r = exp(sum_t adt) per (b, h)
-     (state-only pass: reads x, xp, k, kp and the scalars, writes nothing else)
-  2. chain over ranks with NCCL send/recv: S_0 = initial state (zero), S_{r+1} = D_r S_r + F_r;
-     rank r receives S_r from rank r-1 and sends S_{r+1} to rank r+1  ([B, H, P, N] fp32)
+  1. every rank: F_r = final state of its range from zero (rank 0: from the initial state),
+     D_r = exp(sum_t adt) per (b, h)  (state-only pass: reads x, xp, k, kp and the scalars)
+  2. one all_gather of every rank's [D_r | F_r] (fp32, [B, H] + [B, H, P, N]); each rank forms its
+     own entering state locally, S_0 = 0, S_{i+1} = D_i S_i + F_i for i < r
   3. every rank: the full local scan with initial_state = S_r (saving chunk states)
 backward
   1. every rank: G_r = gradient w.r.t. its initial state from its own dy alone (state-only pass)
-  2. reverse chain: E_{R-1} = 0, E_{r-1} = D_r E_r + G_r  (E_r = gradient w.r.t. the state
-     leaving rank r, i.e. the incoming dfinal of rank r)
-  3. every rank: the full local backward with dfinal = E_r.
+  2. one all_gather of [D_r | G_r]; each rank forms E_r, the gradient w.r.t. the state leaving it:
+     E_{R-1} = 0, E_{i-1} = D_i E_i + G_i for i > r
+  3. every rank: the full local backward with dfinal = E_r; rank 0's initial-state gradient is the
+     one that backward returns.
+One collective per direction, so the exchange costs one all_gather latency at any rank count
+instead of R - 1 dependent send / recv hops.
 
 Ranks hold data in the caller's layout ([B, T_local, H, ...]).  The exchange is collective: every
 rank of the group must call with equally shaped local ranges (checked first, by one small all_gather:
@@ -47,7 +50,7 @@ class LocalScan:
     final_state: Callable    # (inputs, chunk, init) -> F [B,H,P,N]
     forward: Callable        # (inputs, chunk, init) -> (y, saved)
     dinitial: Callable       # (dy, inputs, chunk) -> G [B,H,P,N]   (dfinal = 0)
-    backward: Callable       # (dy, inputs, saved, chunk, init, dfinal) -> 8 grads
+    backward: Callable       # (dy, inputs, saved, chunk, init, dfinal) -> 8 grads + d(initial state)
     total_decay: Callable    # (adt) -> D [B,H] fp32
     combine: Callable        # (s_prev, d, f) -> d * s_prev + f
 
@@ -70,7 +73,7 @@ def _cuda_dinitial(dy, inp, chunk):
 def _cuda_backward(dy, inp, saved, chunk, init, dfinal):
     states, _ = saved
     out = ssd_bwd_op(dy, *inp, states, int(chunk), init, dfinal, False)
-    return out[:8]
+    return out[:9]
 
 
 def _cuda_total_decay(adt):
@@ -105,38 +108,39 @@ CUDA_SCAN = LocalScan(_cuda_final_state, _cuda_forward, _cuda_dinitial, _cuda_ba
 # the exchange
 
 
-def _chain_forward(F, D, group, init, impl: LocalScan):
-    """S_r for this rank: receive from rank-1, send D_r S_r + F_r to rank+1."""
-    rank, world = dist.get_rank(group), dist.get_world_size(group)
-    if rank == 0:
-        S = torch.zeros_like(F) if init is None else init.to(F.dtype).contiguous()
-    else:
-        S = torch.empty_like(F)
-        dist.recv(S, src=dist.get_global_rank(group, rank - 1) if group is not None else rank - 1, group=group)
-    if rank < world - 1:
-        nxt = impl.combine(S, D, F).contiguous()
-        dist.send(nxt, dst=dist.get_global_rank(group, rank + 1) if group is not None else rank + 1, group=group)
+def _gather(X, D, group):
+    """Every rank's (X_r, D_r), in rank order: one all_gather of [D_r | X_r] packed in X's dtype."""
+    world = dist.get_world_size(group)
+    packed = torch.cat([D.reshape(-1).to(X.dtype), X.reshape(-1)]).contiguous()
+    parts = [torch.empty_like(packed) for _ in range(world)]
+    dist.all_gather(parts, packed, group=group)
+    nd = D.numel()
+    return [(p[nd:].view_as(X), p[:nd].view(D.shape).to(D.dtype).contiguous()) for p in parts]
+
+
+def _entering_state(F, D, group, impl: LocalScan):
+    """S_r, the state entering this rank's range: S_0 = 0, S_{i+1} = D_i S_i + F_i (rank 0's F
+    already starts from the initial state)."""
+    rank = dist.get_rank(group)
+    S = torch.zeros_like(F)
+    for Fi, Di in _gather(F, D, group)[:rank]:
+        S = impl.combine(S, Di, Fi)
     return S
 
 
-def _chain_backward(G, D, group, dfinal, impl: LocalScan):
-    """E_r (gradient w.r.t. the state leaving this rank): receive from rank+1, send
-    D_r E_r + G_r to rank-1."""
-    rank, world = dist.get_rank(group), dist.get_world_size(group)
-    if rank == world - 1:
-        E = torch.zeros_like(G) if dfinal is None else dfinal.to(G.dtype).contiguous()
-    else:
-        E = torch.empty_like(G)
-        dist.recv(E, src=dist.get_global_rank(group, rank + 1) if group is not None else rank + 1, group=group)
-    if rank > 0:
-        prv = impl.combine(E, D, G).contiguous()
-        dist.send(prv, dst=dist.get_global_rank(group, rank - 1) if group is not None else rank - 1, group=group)
+def _leaving_gradient(G, D, group, impl: LocalScan):
+    """E_r, the gradient w.r.t. the state leaving this rank's range: E_{R-1} = 0,
+    E_{i-1} = D_i E_i + G_i."""
+    rank = dist.get_rank(group)
+    E = torch.zeros_like(G)
+    for Gi, Di in reversed(_gather(G, D, group)[rank + 1:]):
+        E = impl.combine(E, Di, Gi)
     return E
 
 
 def _check_local_shapes(x, q, group):
     """Every rank must pass an equally shaped local range: the exchanged state is [B, H, P, N], and
-    a send / recv pair of different sizes is undefined under NCCL.  One all_gather of each rank's
+    an all_gather of different sizes is undefined under NCCL.  One all_gather of each rank's
     (B, T_local, H, P, N, G) makes a mismatch raise the same ValueError on every rank."""
     sig = torch.tensor([x.shape[0], x.shape[1], x.shape[2], x.shape[3], q.shape[3], q.shape[2]], dtype=torch.int64,
                        device=x.device)
@@ -152,12 +156,18 @@ class _CpScan(torch.autograd.Function):
     @staticmethod
     def forward(ctx, chunk, group, impl, init, x, q, k, kp, xp, adt, gamma, beta):
         inp = (x, q, k, kp, xp, adt, gamma, beta)
-        F = impl.final_state(inp, chunk, None)
+        rank = dist.get_rank(group)
+        if rank != 0:
+            init = None  # only the first range starts from the caller's initial state
+        F = impl.final_state(inp, chunk, init)
         D = impl.total_decay(adt)
-        S = _chain_forward(F, D, group, init, impl)
+        S = _entering_state(F, D, group, impl)  # every rank takes part in the all_gather
+        if init is not None:
+            S = init.to(F.dtype).contiguous()
         y, saved = impl.forward(inp, chunk, S)
         ctx.chunk, ctx.group, ctx.impl = chunk, group, impl
         ctx.saved = saved
+        ctx.has_init = init is not None
         ctx.save_for_backward(S, D, *inp)
         return y
 
@@ -166,9 +176,10 @@ class _CpScan(torch.autograd.Function):
         S, D, *inp = ctx.saved_tensors
         dy = dy.to(inp[0].dtype).contiguous()
         G = ctx.impl.dinitial(dy, tuple(inp), ctx.chunk)
-        E = _chain_backward(G, D, ctx.group, None, ctx.impl)
-        grads = ctx.impl.backward(dy, tuple(inp), ctx.saved, ctx.chunk, S, E)
-        return (None, None, None, None, *grads)
+        E = _leaving_gradient(G, D, ctx.group, ctx.impl)
+        out = ctx.impl.backward(dy, tuple(inp), ctx.saved, ctx.chunk, S, E)
+        grads, dinit = out[:8], out[8]
+        return (None, None, None, dinit if ctx.has_init else None, *grads)
 
 
 def cp_ssd(x, q, k, kp, xp, adt, gamma, beta, chunk_size, *, group=None, initial_state=None,
@@ -178,7 +189,8 @@ def cp_ssd(x, q, k, kp, xp, adt, gamma, beta, chunk_size, *, group=None, initial
     Each rank passes its contiguous range of the sequence ([B, T_local, H, ...], rank r holding
     tokens [r T_local, (r+1) T_local)); returns this rank's y.  Same arithmetic as
     ``zenith_b200.ssd`` on the whole sequence, differentiable w.r.t. all eight inputs.
-    ``initial_state`` (rank 0 only) starts the sequence from a given state.
+    ``initial_state`` [B, H, P, N] (read on rank 0 only; the other ranks ignore theirs) starts the
+    sequence from a given state and is differentiable on rank 0.
     """
     assert x.shape[1] % chunk_size == 0, "sequence length must be a multiple of chunk_size"
     _check_local_shapes(x, q, group)
