@@ -190,6 +190,31 @@ def test_train_step_reduces_loss():
     assert losses[-1] < losses[0] - 0.1, losses
 
 
+def test_train_step_raises_on_a_token_outside_the_vocabulary():
+    """The reference's F.cross_entropy raises on a label outside the vocabulary.  Here the loss
+    kernel records it in the device status word (nothing faults, the row is skipped) and the
+    training loop raises SsdError from train_step once that is visible, without a sync of its
+    own: at the latest in the step after the faulty one has finished on the GPU."""
+    import zenith_b200
+    from zenith_b200 import lm
+
+    cfg = dict(vocab_size=256, d_model=64, d_state=16, expand=2, headdim=16, chunk_size=32, n_input=1,
+               n_recurrent=1, n_output=1, max_loops=1)
+    torch.manual_seed(0)
+    model = lm.ZenithForCausalLM(cfg).to(DEV)
+    opt = lm.make_optimizer(model)
+    good = torch.randint(0, 256, (2, 64), device=DEV)
+    bad = good.clone()
+    bad[1, 5] = 300                      # outside [0, 256): a target of the next-token loss
+    lm.train_step(model, opt, good)
+    lm.train_step(model, opt, bad)       # queued; the error is recorded on the device
+    torch.cuda.synchronize()             # (the faulty step has finished by the next call)
+    with pytest.raises(zenith_b200.SsdError, match="status 9"):
+        lm.train_step(model, opt, good)
+    lm.train_step(model, opt, good)      # the word was cleared: training goes on
+    zenith_b200.check_status()
+
+
 # behaviour of the model, as the reference's own model tests check it (tests/test_model.py)
 
 TINY = dict(vocab_size=1024, d_model=128, d_state=32, expand=2, headdim=32, chunk_size=32, n_input=1, n_recurrent=2,

@@ -144,6 +144,51 @@ def status_word(device: torch.device) -> torch.Tensor:
     return t
 
 
+class StatusPoll:
+    """Deferred, non-blocking check of one device's status word.
+
+    ``poll()`` first looks at the asynchronous copy of the word that the previous ``poll()``
+    queued (into pinned host memory, behind that call's launches): if the copy has landed and the
+    word was nonzero, the word is cleared and ``SsdError`` is raised.  Then it queues a new copy
+    behind the launches made so far.  It never waits for the GPU, so an error surfaces at the
+    first call after the faulty kernel has finished, usually the next step."""
+
+    def __init__(self, word: torch.Tensor, host: torch.Tensor, make_event):
+        self.word, self.host, self.make_event = word, host, make_event
+        self.event = None
+
+    def poll(self) -> None:
+        if self.event is not None and self.event.query():
+            self.event = None
+            code = int(self.host[0])
+            if code != 0:
+                self.word.zero_()
+                self.host.zero_()
+                check(code, "kernel status (an earlier call)")
+        if self.event is None:
+            self.host.copy_(self.word, non_blocking=True)
+            self.event = self.make_event()
+            self.event.record()
+
+
+_polls: dict[int, StatusPoll] = {}
+
+
+def poll_status(device: torch.device) -> None:
+    """Raise ``SsdError`` if an earlier kernel on ``device`` has recorded an error (a timed-out
+    wait, a label out of range), without synchronising; see ``StatusPoll``.  Does nothing while
+    the current stream is being captured into a CUDA graph, and for tensors that are not on a GPU."""
+    if device.type != "cuda" or torch.cuda.is_current_stream_capturing():
+        return
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    p = _polls.get(idx)
+    if p is None:
+        p = StatusPoll(status_word(torch.device("cuda", idx)), torch.zeros(1, dtype=torch.int32).pin_memory(),
+                       torch.cuda.Event)
+        _polls[idx] = p
+    p.poll()
+
+
 def check_status(device: torch.device | None = None, reset: bool = True) -> None:
     """Synchronise and raise if a kernel on ``device`` recorded an error (e.g. a timed-out wait)."""
     dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())

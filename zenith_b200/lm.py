@@ -580,7 +580,11 @@ def train_step(model: nn.Module, opt: torch.optim.Optimizer, ids: Tensor, loops:
                amp: bool = True) -> Tensor:
     """One optimiser step on a batch of token ids: bf16-autocast forward with ``labels=ids``,
     backward (under ``DistributedDataParallel`` the gradient all-reduce runs during it), global
-    gradient-norm clipping, the optimiser step.  Returns the loss (a device scalar, no sync)."""
+    gradient-norm clipping, the optimiser step.  Returns the loss (a device scalar, no sync).
+    Raises ``SsdError`` when a kernel of an earlier step recorded an error in the device status
+    word (a label outside the vocabulary, a timed-out wait), as soon as that is visible without
+    a synchronisation: at the latest, the step after the faulty one has finished on the GPU."""
+    L.poll_status(ids.device)  # an error an earlier step's kernels recorded (e.g. a label out of range)
     ctx = torch.autocast("cuda", dtype=torch.bfloat16) if amp else nullcontext()
     with ctx:
         loss = model(ids, labels=ids, loops=loops).loss
@@ -601,6 +605,7 @@ def train_step(model: nn.Module, opt: torch.optim.Optimizer, ids: Tensor, loops:
         torch.nn.utils.clip_grad_norm_(model.parameters(), grad_clip, foreach=True)
         opt.step()
     opt.zero_grad(set_to_none=True)
+    L.poll_status(ids.device)
     return loss.detach()
 
 

@@ -172,6 +172,7 @@ def _backward(ctx, dy, dfinal, _dstates):
     if dfinal is not None:
         dfinal = dfinal.to(_acc_dtype(x.dtype)).contiguous()
     out = ssd_bwd_op(dy, x, q, k, kp, xp, adt, gamma, beta, states, ctx.chunk_size, init, dfinal, False)
+    L.poll_status(x.device)
     dx, dq, dk, dkp, dxp, dadt, dgamma, dbeta, dinit = out
     return dx, dq, dk, dkp, dxp, dadt, dgamma, dbeta, None, (dinit if ctx.has_init else None), None, None
 
@@ -219,7 +220,8 @@ def ssd(x, q, k, kp, xp, adt, gamma, beta, chunk_size, *, initial_state=None, re
     group h // (H // G)); adt, gamma, beta: [B, T, H].  Returns y [B, T, H, P] in x's dtype, or
     ``(y, final_state)`` with ``return_final_state=True`` (final_state [B, H, P, N] fp32, fp64
     for fp64 inputs).  Raises AssertionError("sequence length must be a multiple of
-    chunk_size") like the reference.
+    chunk_size") like the reference.  A kernel error recorded on the device by an earlier call
+    (a timed-out wait) raises ``SsdError`` here once it is visible, without a synchronisation.
     """
     Bsz, T, H, P = x.shape
     N = q.shape[-1]
@@ -235,6 +237,7 @@ def ssd(x, q, k, kp, xp, adt, gamma, beta, chunk_size, *, initial_state=None, re
     need_grad = torch.is_grad_enabled() and any(
         t.requires_grad for t in (x, q, k, kp, xp, adt, gamma, beta, initial_state) if t is not None)
     y, final, _ = torch.ops.zenith_b200.ssd_fwd(*args, int(chunk_size), initial_state, need_grad, False)
+    L.poll_status(x.device)
     if y.dtype != out_dtype:
         y = y.to(out_dtype)
     if return_final_state:
@@ -278,6 +281,9 @@ def ssd_decode(x, q, k, kp, xp, adt, gamma, beta, state: Tensor) -> Tensor:
     N = q.shape[3]
     if state.dtype != torch.float32 or tuple(state.shape) != (B, H, P, N) or not state.is_contiguous():
         raise ValueError("ssd_decode: state must be a contiguous float32 [B, H, P, N] tensor")
+    if any(t.dtype != x.dtype for t in (q, k, kp, xp)):
+        raise ValueError("ssd_decode: x, q, k, kp and xp must share one dtype, got "
+                         + ", ".join(str(t.dtype) for t in (x, q, k, kp, xp)))
     dev = x.device
     scal = [t if t.dtype == torch.float32 else t.float() for t in (adt, gamma, beta)]
     vec = [t if t.stride(-1) == 1 else t.contiguous() for t in (x, q, k, kp, xp)]
