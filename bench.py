@@ -48,6 +48,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", default="layer")
+    ap.add_argument("--replicate", action="store_true",
+                    help="N > 1: every rank runs a whole job of its own (weak scaling) instead of 1/N of one job")
+    ap.add_argument("--eager", action="store_true", help="time eager launches instead of CUDA-graph replays")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
     return ap.parse_args()
@@ -245,13 +248,33 @@ def run_reference(args):
 # our arm
 
 
+L2_BYTES = 126 << 20  # B200 L2
+
+
+def shard_of(shape, rank, world):
+    """Rank r's part of one job: contiguous ranges of the B*H independent (batch, head) chains,
+    by batch when the ranks divide B (every rank keeps whole sequences), else by heads (whole
+    q/k groups).  Returns (local shape, batch slice, head slice)."""
+    from zenith_b200.synthetic import SsdShape
+
+    if shape.B % world == 0:
+        bl = shape.B // world
+        return (SsdShape(bl, shape.T, shape.H, shape.P, shape.N, shape.G, shape.chunk, shape.name),
+                slice(rank * bl, (rank + 1) * bl), slice(None))
+    if shape.H % world == 0 and shape.G % world == 0:
+        hl, gl = shape.H // world, shape.G // world
+        return (SsdShape(shape.B, shape.T, hl, shape.P, shape.N, gl, shape.chunk, shape.name),
+                slice(None), slice(rank * hl, (rank + 1) * hl))
+    raise SystemExit(f"{world} ranks do not divide the batch ({shape.B}) or the q/k groups ({shape.G})")
+
+
 def run_ours(args):
     import torch.distributed as dist
 
     import zenith_b200
     from zenith_b200 import _lib
     from zenith_b200.ssd import ssd_bwd_op, ssd_fwd_op
-    from zenith_b200.synthetic import SHAPES, SsdShape
+    from zenith_b200.synthetic import SHAPES, SsdShape, make_inputs
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -261,38 +284,59 @@ def run_ours(args):
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     shape = SHAPES[args.workload]
-    # long-context workload on N > 1 GPUs: context parallelism (each rank owns T/N tokens of the
-    # sequence; boundary states move between ranks with NCCL send/recv).  Otherwise every rank
-    # runs its own batch of the workload (batch x heads sharding: weak scaling, no collective).
+    # Long-context workload on N > 1 GPUs: context parallelism (each rank owns T/N tokens of the
+    # sequence; boundary states move between ranks with NCCL send/recv).  Otherwise the B*H
+    # independent (batch, head) chains of ONE job are split over the ranks (no collective on the
+    # data path), or with --replicate every rank runs a whole job of its own (weak scaling).
     cp = args.workload == "long" and world > 1
     fwd_only = args.workload == "infer"  # C4: inference forward returning the final state (decode hand-off)
-    local_shape = SsdShape(shape.B, shape.T // world, shape.H, shape.P, shape.N, shape.G, shape.chunk) if cp else shape
-    inp = make_device_inputs(local_shape, rank, dev)
-    a = [inp[n] for n in NAMES]
-    dy = inp["dy"]
+    replicate = args.replicate and not cp
+    full = make_inputs(shape, seed=rank if replicate else 0)
+    if cp:
+        local_shape = SsdShape(shape.B, shape.T // world, shape.H, shape.P, shape.N, shape.G, shape.chunk)
+        sl_t = slice(rank * local_shape.T, (rank + 1) * local_shape.T)
+        part = {n: v[:, sl_t] for n, v in full.items() if n != "D"}
+    elif replicate or world == 1:
+        local_shape = shape
+        part = {n: v for n, v in full.items() if n != "D"}
+    else:
+        local_shape, sl_b, sl_h = shard_of(shape, rank, world)
+        r = shape.H // shape.G
+        sl_g = sl_h if sl_h == slice(None) else slice(sl_h.start // r, sl_h.stop // r)
+        part = {n: (v[sl_b, :, sl_g] if n in ("q", "k", "kp") else v[sl_b, :, sl_h]) for n, v in full.items() if n != "D"}
+    inp = {n: (t.to(torch.bfloat16) if (n in VEC or n == "dy") else t).to(dev).contiguous() for n, t in part.items()}
+    del full, part
     chunk = shape.chunk
     fwd_b, bwd_b = algorithmic_bytes(shape)
+    if fwd_only:
+        bwd_b = 0
     th = local_shape.B * local_shape.T * local_shape.H
+    step_bytes = (fwd_b + bwd_b) * th
+    tokens_per_step = shape.B * shape.T * (world if replicate else 1)
+
+    # Rotating copies of the inputs, so that a step's inputs were last touched at least two steps
+    # earlier and at least twice the L2 has been streamed since (a step reads and writes
+    # step_bytes): each step starts from HBM, not from a warm L2.
+    n_sets = 1 if step_bytes >= 2 * L2_BYTES else -(-2 * L2_BYTES // step_bytes) + 1
+    sets = [inp] + [{n: t.clone() for n, t in inp.items()} for _ in range(n_sets - 1)]
 
     if cp:
         from zenith_b200.parallel import cp_ssd
 
-        leaves = [t.clone().requires_grad_() for t in a]
-
-        def step(ev=None):
+        def step(st, ev=None):
+            leaves = [st[n].detach().requires_grad_() for n in NAMES]
             if ev is not None:
                 ev[0].record()
             y = cp_ssd(*leaves, chunk)
             if ev is not None:
                 ev[1].record()
-            y.backward(dy)
+            y.backward(st["dy"])
             if ev is not None:
                 ev[2].record()
-            for t in leaves:
-                t.grad = None
             return y
     elif fwd_only:
-        def step(ev=None):
+        def step(st, ev=None):
+            a = [st[n] for n in NAMES]
             if ev is not None:
                 ev[0].record()
             y, fin, _ = ssd_fwd_op(*a, chunk, None, False, False)
@@ -301,13 +345,14 @@ def run_ours(args):
                 ev[2].record()
             return y, fin
     else:
-        def step(ev=None):
+        def step(st, ev=None):
+            a = [st[n] for n in NAMES]
             if ev is not None:
                 ev[0].record()
             y, fin, states = ssd_fwd_op(*a, chunk, None, True, False)
             if ev is not None:
                 ev[1].record()
-            g = ssd_bwd_op(dy, *a, states, chunk, None, None, False)
+            g = ssd_bwd_op(st["dy"], *a, states, chunk, None, None, False)
             if ev is not None:
                 ev[2].record()
             return y, g
@@ -316,13 +361,28 @@ def run_ours(args):
         if world > 1:
             dist.barrier()
 
-    for _ in range(max(args.warmup, 3)):
-        step()
+    for i in range(max(args.warmup, 3)):
+        step(sets[i % n_sets])
     torch.cuda.synchronize()
     zenith_b200.check_status(dev)
 
-    # per-kernel durations (events around each op on the launching stream)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    # The step's launches are captured once per buffer set in a CUDA graph and replayed: the
+    # same kernels on the same data each step, without the host's per-launch cost (which
+    # would set the pace once a rank's share of the job takes ~100 us).  Context parallelism
+    # (NCCL send / recv inside the step) runs eagerly.
+    graphs = []
+    if not cp and not args.eager:
+        keep = []
+        for st in sets:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                keep.append(step(st))
+            graphs.append(g)
+        for g in graphs:  # one untimed replay of each
+            g.replay()
+        torch.cuda.synchronize()
+        zenith_b200.check_status(dev)
+
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local)
     barrier()
@@ -330,22 +390,39 @@ def run_ours(args):
     launches0 = _lib.launch_count()
     start.record()
     for i in range(args.steps):
-        step(evs[i])
+        if graphs:
+            graphs[i % n_sets].replay()
+        else:
+            step(sets[i % n_sets])
     end.record()
     torch.cuda.synchronize()
     launches = _lib.launch_count() - launches0
+    if graphs:  # replays launch without the host library: count the captured step's launches
+        c0 = _lib.launch_count()
+        step(sets[0])
+        torch.cuda.synchronize()
+        launches = (_lib.launch_count() - c0) * args.steps
     barrier()
     clocks = sampler.stop()
     zenith_b200.check_status(dev)
     elapsed_ms = start.elapsed_time(end)
+
+    # per-kernel durations of the forward and backward launches (events around each op on the
+    # launching stream, eager, over the same number of steps and the same buffer rotation)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        step(sets[i % n_sets], evs[i])
+    torch.cuda.synchronize()
     fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
     bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    del graphs
     t = torch.tensor([elapsed_ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     elapsed_ms = float(t.item())
     ms_per_step = elapsed_ms / args.steps
-    tokens_per_step = shape.B * shape.T if cp else shape.B * shape.T * world
     value = tokens_per_step / (ms_per_step / 1e3)
 
     # End-to-end through the public API with host buffers (pinned).  Every step copies its inputs and
@@ -448,16 +525,25 @@ def run_ours(args):
     dms, dbytes, dname = kern[dom]
     achieved = dbytes / (dms / 1e3) / 1e9
     step_gbs = (fwd_b + bwd_b) * th / (ms_per_step / 1e3) / 1e9
+    if cp:
+        par = f"context-parallel x{world} (T/{world} per rank, NCCL send/recv of boundary states)"
+    elif replicate:
+        par = f"replicated x{world} (each rank a whole B{shape.B} job of its own)"
+    else:
+        par = (f"batch x heads sharded x{world}: (batch, head) chains {local_shape.B * local_shape.H} of "
+               f"{shape.B * shape.H} per rank, no collective on the data path")
     line = {
         "metric": METRIC_FWD if fwd_only else METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong" if cp else "weak",
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak" if replicate else "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": shape.name, "B_per_gpu": shape.B, "T": shape.T, "H": shape.H, "P": shape.P,
-                   "N": shape.N, "chunk": shape.chunk, "vector_dtype": "bf16", "scalar_dtype": "fp32",
-                   "parallelism": (f"context-parallel x{world} (T/{world} per rank, NCCL send/recv of boundary states)"
-                                   if cp else f"batch-sharded x{world}"),
+        "config": {"workload": shape.name, "B": shape.B, "T": shape.T, "H": shape.H, "P": shape.P,
+                   "N": shape.N, "G": shape.G, "chunk": shape.chunk, "vector_dtype": "bf16", "scalar_dtype": "fp32",
+                   "parallelism": par, "B_per_rank": local_shape.B, "H_per_rank": local_shape.H,
                    "tokens_per_rank": local_shape.B * local_shape.T,
-                   "l2": f"inputs larger than L2 ({(fwd_b + bwd_b) * th / 1e9:.2f} GB/step per rank)"},
+                   "timed_launch": "eager" if (cp or args.eager) else "CUDA graph of one step, replayed",
+                   "l2": (f"inputs larger than L2: {step_bytes / 1e9:.3f} GB read+written per step per rank, "
+                          f"{n_sets} rotating input set(s) so each step starts from HBM")},
         "roofline": {"bound": "hbm", "kernel": dname, "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
                      "traffic": traffic_from_profile(dname) if args.workload == "layer" else None,
