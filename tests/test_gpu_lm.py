@@ -190,7 +190,7 @@ def test_train_step_reduces_loss():
     assert losses[-1] < losses[0] - 0.1, losses
 
 
-def test_train_step_raises_on_a_token_outside_the_vocabulary():
+def test_train_step_raises_on_a_label_outside_the_vocabulary():
     """The reference's F.cross_entropy raises on a label outside the vocabulary.  Here the loss
     kernel records it in the device status word (nothing faults, the row is skipped) and the
     training loop raises SsdError from train_step once that is visible, without a sync of its
@@ -205,9 +205,10 @@ def test_train_step_raises_on_a_token_outside_the_vocabulary():
     opt = lm.make_optimizer(model)
     good = torch.randint(0, 256, (2, 64), device=DEV)
     bad = good.clone()
-    bad[1, 5] = 300                      # outside [0, 256): a target of the next-token loss
+    bad[1, 5] = 300                      # a label outside [0, 256); the input ids stay in range (an
+                                         # id outside the table would fault in the embedding gather)
     lm.train_step(model, opt, good)
-    lm.train_step(model, opt, bad)       # queued; the error is recorded on the device
+    lm.train_step(model, opt, good, labels=bad)  # queued; the error is recorded on the device
     torch.cuda.synchronize()             # (the faulty step has finished by the next call)
     with pytest.raises(zenith_b200.SsdError, match="status 9"):
         lm.train_step(model, opt, good)

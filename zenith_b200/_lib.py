@@ -118,13 +118,14 @@ def check(code: int, what: str) -> None:
         raise err
 
 
-def view(t: torch.Tensor | None) -> View:
-    """[B, T, H, D] (or [B, T, H]) tensor -> View; the innermost dimension must be contiguous."""
+def view(t: torch.Tensor | None, ptr: int | None = None) -> View:
+    """[B, T, H, D] (or [B, T, H]) tensor -> View; the innermost dimension must be contiguous.
+    ``ptr`` replaces the data address (sizing calls that have no data, e.g. fake tensors)."""
     if t is None:
         return View(None, 0, 0, 0)
     if t.dim() == 4:
         assert t.stride(-1) == 1 or t.shape[-1] == 1, "innermost dimension must be contiguous"
-    return View(t.data_ptr(), t.stride(0), t.stride(1), t.stride(2))
+    return View(t.data_ptr() if ptr is None else ptr, t.stride(0), t.stride(1), t.stride(2))
 
 
 def ptr(t: torch.Tensor | None):
@@ -174,12 +175,23 @@ class StatusPoll:
 _polls: dict[int, StatusPoll] = {}
 
 
-def poll_status(device: torch.device) -> None:
-    """Raise ``SsdError`` if an earlier kernel on ``device`` has recorded an error (a timed-out
-    wait, a label out of range), without synchronising; see ``StatusPoll``.  Does nothing while
-    the current stream is being captured into a CUDA graph, and for tensors that are not on a GPU."""
-    if device.type != "cuda" or torch.cuda.is_current_stream_capturing():
+def _tracing(t: torch.Tensor) -> bool:
+    """True while torch.compile / AOT autograd traces the caller with fake tensors."""
+    if torch.compiler.is_compiling():
+        return True
+    from torch._subclasses.fake_tensor import is_fake
+
+    return bool(is_fake(t))
+
+
+def poll_status(t: torch.Tensor) -> None:
+    """Raise ``SsdError`` if an earlier kernel on ``t``'s device has recorded an error (a timed-out
+    wait, a label out of range), without synchronising; see ``StatusPoll``.  Does nothing for
+    tensors that are not on a GPU, while the call is being traced (torch.compile) and while the
+    current stream is being captured into a CUDA graph."""
+    if not t.is_cuda or _tracing(t) or torch.cuda.is_current_stream_capturing():
         return
+    device = t.device
     idx = device.index if device.index is not None else torch.cuda.current_device()
     p = _polls.get(idx)
     if p is None:

@@ -244,15 +244,35 @@ size_t plan_workspace(const Plan& pl, bool backward) {
 //   backward: G_m = d(initial state of m) from segment m's own dy (state-only pass);
 //             E_{m-1} = D_m E_m + G_m (combine kernel); full pass with final-state gradients E_m.
 // The decision depends only on sizes and the input views, so forward and backward agree.
-constexpr int64_t kSegMinChains = 296;  // aim for two chains per SM
+// When to segment: a chain hands its state on once per 64-token chunk, about 3 us per hand-off in
+// each direction, so T / 64 hand-offs bound a call from below; the chunks' own work spreads over
+// the SMs.  Measured on the layer shape (B x 24 heads x T 2048, one B200, fwd + bwd): unsegmented
+// 197 / 220 / 341 us at B = 1 / 2 / 4, segmented into 8 / 4 / 4 segments 175 / 271 / 495 us.  The
+// extra state-only pass and combine step pay only when there are fewer chains than about a
+// quarter of the SMs.
+constexpr int kSegChainsPerSm = 4;       // segment only while chains * 4 < SMs
+constexpr int64_t kSegMinChains = 296;   // then aim for two chains per SM
 constexpr int kSegMinChunks = 4;         // and at least four chunks per chain
 
 bool batch_contiguous(const zb_view& v, int64_t T) { return v.sb == T * v.st; }
 
+// streaming multiprocessors of the current device (cached per device)
+int device_sms() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
 int segments_for(const zb_ssd_args* a, const Plan& pl) {
   if (pl.kind != kTc || (a->flags & ZB_FLAG_SHIFTED)) return 1;  // a segment's row -1 is not zero
   const int64_t chains = a->B * a->H;
-  if (chains >= 148) return 1;
+  if (chains * kSegChainsPerSm >= device_sms()) return 1;
   const zb_view* v[] = {&a->x, &a->q, &a->k, &a->kp, &a->xp, &a->adt, &a->gamma, &a->beta};
   for (auto x : v)
     if (!batch_contiguous(*x, a->T)) return 1;

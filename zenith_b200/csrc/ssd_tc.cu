@@ -2,17 +2,17 @@
 // per-token scalars): tcgen05 MMAs with fp32 accumulators in TMEM, operands staged in shared
 // memory by TMA (128-byte swizzle, no multicast).
 //
-// Forward, one CTA per (batch, head, 64-token chunk), 256 threads, 256 TMEM columns:
-//   MMA1  S   = Q [K;Kp]^T              M=64 (t)   N=128 (s|s')   K=N   A,B K-major
-//   MMA3  Sl' = [K;Kp]^T [wgX ; wbXp]   M=N (n)    N=64 (p)       K=128 A,B MN-major
-//   epilogue: Ps = (S * [g|b]_s * exp(c_t - c_s) masked to s <= t) -> bf16 smem
-//   MMA2  Yi  = Ps [X;Xp]               M=64 (t)   N=64 (p)       K=128 A K-major, B MN-major
-//   chain: wait for S_in[j]; S_in[j+1] = e^{c_L} S_in[j] + Sl'^T -> ring slot; publish
-//   MMA4  Ye  = Q S_in[j]^T             M=64 (t)   N=64 (p)       K=N   A K-major, B MN-major
-//   epilogue: y = Yi + e^{c_t} Ye -> bf16
-// TMEM columns: [0,128) S (M=64 layout: lanes 0-15 of each 32-lane sub-partition);
-// [128,192) Yi at lane offset 0 and Ye at lane offset 16 (two interleaved M=64 tiles);
-// [192,256) Sl' (M=128 layout for N=128: lane = n).
+// Forward, persistent, 128 TMEM columns and 68 KB (N = 128: 256 threads, 3 CTAs per SM) or 52 KB
+// (N = 64: 128 threads, 4 CTAs per SM) of shared memory, so that several CTAs share an SM and run
+// each other's dependent phases in between.  Per (batch, head, 64-token chunk):
+//   MMA1  S    = Q [K;Kp]^T                M=64 (t)  N=128 (s|s')  K=N    lanes 0-15,  cols 0-127
+//   K, Kp rows scaled in place by w g, w b (MMA1 is done with them)
+//   MMA3  Sl_h = [wgK;wbKp]_h^T [X;Xp]     M=64 (n of half h) N=64 (p) K=128  lanes 16-31, cols 64h..
+//   epilogue: Ps = (S * [g|b]_s * exp(c_t - c_s) masked to s <= t) -> registers -> bf16 over K|Kp
+//   MMA2  Yi   = Ps [X;Xp]                 M=64 (t)  N=64 (p)  K=128    lanes 0-15, cols 0-63 (S consumed)
+//   chain: wait for S_in[j]; S_in[j+1] = e^{c_L} S_in[j] + Sl -> ring slot; publish; S_in[j] bf16 -> smem
+//   MMA4  Ye   = Q S_in[j]^T               M=64 (t)  N=64 (p)  K=N      lanes 0-15, cols 64-127
+//   epilogue: y = Yi + e^{c_t} Ye -> bf16 -> TMA store
 // The fp32 state hand-off lives in a two-slot ring per (batch, head) that stays in L2; the
 // states the backward needs are saved in bf16 [B*H][nc][N][P].
 #include <cuda.h>
@@ -28,25 +28,28 @@ namespace zb {
 
 namespace {
 
-constexpr int kTcThreads = 256;
 constexpr int kL = 64;  // internal chunk length
 constexpr int kP = 64;
 
+// Shared memory of the forward.  After MMA3 the K|Kp block 0 holds the scores Ps [2][64 t][64 s]
+// and (N = 128) block 1 the S_in image; after MMA4 the X tile holds the y tile.
 template <int NS>
 struct FwdSmem {
   static constexpr int QB = NS / 64;                      // 64-wide blocks along n
   static constexpr uint32_t Q = 0;                        // [QB][64 t][64 n]
-  static constexpr uint32_t KK = Q + QB * 8192;           // [QB][K | Kp][64 s][64 n]; later Ps [2][64 t][64 s]
-  static constexpr uint32_t X = KK + QB * 16384;          // [64 s][64 p]
-  static constexpr uint32_t XP = X + 8192;
-  static constexpr uint32_t XS = XP + 8192;               // [wgX | wbXp]
-  static constexpr uint32_t SIN = XS + 16384;             // [NS n][64 p]; before that the scores Ps [2][64][64]
-  static constexpr uint32_t SIN_BYTES = NS * 128 > 16384 ? NS * 128 : 16384;
-  static constexpr uint32_t SCAL = SIN + SIN_BYTES;       // c, ec, wg, wb, g, b, next chunk's adt g b (64 floats each)
-  static constexpr uint32_t BAR = SCAL + 9 * 64 * 4;      // 5 mbarriers (load, MMA1, MMA2, MMA4, MMA3)
-  static constexpr uint32_t MISC = BAR + 6 * 8;           // tmem base, ticket, chain result, next ticket
+  static constexpr uint32_t KK = Q + QB * 8192;           // [QB][K | Kp][64 s][64 n]
+  static constexpr uint32_t XX = KK + QB * 16384;         // [X | Xp] [64 s][64 p]
+  static constexpr uint32_t SIN = NS == 128 ? KK + 16384 : XX + 16384;  // S_in image [NS n][64 p]
+  static constexpr uint32_t SCAL = NS == 128 ? XX + 16384 : SIN + NS * 128;
+  // c, ec, wg, wb, g, b, then the next chunk's staged adt, gamma, beta (64 floats each)
+  static constexpr uint32_t BAR = SCAL + 9 * 64 * 4;      // mbarriers: loads, MMA1, MMA3, MMA2 + MMA4
+  static constexpr uint32_t MISC = BAR + 4 * 8;           // tmem base, first ticket, chain result, next ticket
   static constexpr uint32_t TOTAL = MISC + 16;
   static constexpr uint32_t ALLOC = TOTAL + 1024;         // slack to align the base to 1024
+  static constexpr uint32_t LOAD_BYTES = QB * 8192 * 3 + 2 * 8192;
+  static constexpr int CTAS_PER_SM = NS == 128 ? 3 : 4;   // shared memory: 68 KB / 52 KB per CTA
+  static constexpr int THREADS = NS == 128 ? 256 : 128;   // registers: 80 / 128 per thread
+  static constexpr int WPS = THREADS / 128;               // warps per TMEM sub-partition
 };
 
 struct TcFwdParams {
@@ -80,7 +83,25 @@ __device__ __forceinline__ float2 unpack_bf16(uint32_t u) {
   return __bfloat1622float2(v);
 }
 
-// Loads of one chunk's operands, issued in three parts as the previous chunk frees the tiles.
+// 32 floats -> bf16 into chunks [c0, c0 + 4) of row r of a 128-byte-swizzled staging tile
+__device__ __forceinline__ void stage_row32(unsigned char* tile, int r, int c0, const float* v) {
+#pragma unroll
+  for (int qd = 0; qd < 4; ++qd)
+    *reinterpret_cast<uint4*>(tile + umma::sw128_offset(r, c0 + qd)) =
+        make_uint4(pack_bf16(v[8 * qd], v[8 * qd + 1]), pack_bf16(v[8 * qd + 2], v[8 * qd + 3]),
+                   pack_bf16(v[8 * qd + 4], v[8 * qd + 5]), pack_bf16(v[8 * qd + 6], v[8 * qd + 7]));
+}
+
+// 16 floats -> bf16 into chunks c0, c0 + 1 of row r of a 128-byte-swizzled staging tile
+__device__ __forceinline__ void stage_row16(unsigned char* tile, int r, int c0, const float* v) {
+#pragma unroll
+  for (int qd = 0; qd < 2; ++qd)
+    *reinterpret_cast<uint4*>(tile + umma::sw128_offset(r, c0 + qd)) =
+        make_uint4(pack_bf16(v[8 * qd], v[8 * qd + 1]), pack_bf16(v[8 * qd + 2], v[8 * qd + 3]),
+                   pack_bf16(v[8 * qd + 4], v[8 * qd + 5]), pack_bf16(v[8 * qd + 6], v[8 * qd + 7]));
+}
+
+// Loads of one chunk's operands (Q, K | Kp, X | Xp), completing on one mbarrier.
 template <int NS>
 __device__ __forceinline__ void fwd_load_kk(const TcFwdParams& p, unsigned char* sKK, uint64_t* bar, const UnitIdx& u) {
   const int t0 = u.chunk * kL;
@@ -109,21 +130,25 @@ __device__ __forceinline__ void fwd_prefetch_scalars(const TcFwdParams& p, const
   umma::cp_async_commit();
 }
 
-// Persistent: two CTAs per SM walk the chunks in ticket order (chunk-major).  Each CTA takes its
-// tickets in increasing order and a chunk only waits on a lower ticket, so the lowest unfinished
-// ticket always belongs to a CTA that can run it.  The next ticket's operands load into the
-// tiles of the current one as soon as its MMAs are done with them.
+// Persistent: CTAS_PER_SM CTAs per SM walk the chunks in ticket order (chunk-major).  Each CTA
+// takes its tickets in increasing order and a chunk only waits on a lower ticket, so the lowest
+// unfinished ticket always belongs to a CTA that can run it.  A CTA loads the next chunk's operands
+// once the current chunk's tiles have left shared memory; the other CTAs on the SM cover the wait.
+// Warp w reads TMEM sub-partition w % 4; with two warps per sub-partition, w / 4 picks half the
+// columns of each epilogue.
 template <int NS>
-__global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_constant__ TcFwdParams p) {
+__global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM)
+    ssd_fwd_tc_kernel(const __grid_constant__ TcFwdParams p) {
   using S = FwdSmem<NS>;
+  constexpr int QB = S::QB, WPS = S::WPS;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* sQ = sm + S::Q;
   unsigned char* sKK = sm + S::KK;
-  unsigned char* sPs = sm + S::SIN;  // scores live in the S_in tile until MMA2 has read them
-  unsigned char* sX = sm + S::X;
-  unsigned char* sXp = sm + S::XP;
-  unsigned char* sXs = sm + S::XS;
+  unsigned char* sPs = sm + S::KK;   // scores, over K|Kp block 0 once MMA3 is done
+  unsigned char* sX = sm + S::XX;
+  unsigned char* sXp = sm + S::XX + 8192;
+  unsigned char* sY = sm + S::XX;    // y tile, over X once MMA2 and MMA4 are done
   unsigned char* sSin = sm + S::SIN;
   float* s_c = reinterpret_cast<float*>(sm + S::SCAL);
   float* s_ec = s_c + 64;
@@ -134,29 +159,31 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
   float* s_nx = s_c + 384;  // next chunk's [adt | gamma | beta]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::BAR);
   uint32_t* misc = reinterpret_cast<uint32_t*>(sm + S::MISC);
-  constexpr uint32_t kLoadBytes = S::QB * 8192 * 3 + 2 * 8192;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int sp = warp & 3, hw = warp >> 2;  // TMEM sub-partition, column share
+  const bool hiL = lane >= 16;
   const int64_t total = p.B * p.H * p.nc;
   if (tid == 0) {
     misc[1] = atomicAdd(p.ticket, 1u);
-    for (int i = 0; i < 5; ++i) umma::mbar_init(&bars[i], 1);
+    for (int i = 0; i < 4; ++i) umma::mbar_init(&bars[i], 1);
     umma::mbar_fence_init();
   }
   __syncwarp();  // lane 0 of warp 0 rejoins before the warp-collective allocation
   if (warp == 0) {
-    umma::tmem_alloc(&misc[0], 256);
+    umma::tmem_alloc(&misc[0], 128);
     umma::tmem_relinquish();
   }
   umma::fence_before_sync();
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tmem = misc[0];
+  const uint32_t tlane = (uint32_t)(32 * sp) << 16;  // this warp's TMEM sub-partition
   uint32_t cur = misc[1];
   if (cur < total) {
     const UnitIdx u0 = decode_ticket(cur, p.B, p.H, p.G);
     if (tid == 0) {
-      umma::mbar_arrive_expect_tx(&bars[0], kLoadBytes);
+      umma::mbar_arrive_expect_tx(&bars[0], S::LOAD_BYTES);
       fwd_load_q<NS>(p, sQ, &bars[0], u0);
       fwd_load_kk<NS>(p, sKK, &bars[0], u0);
       fwd_load_x(p, sX, sXp, &bars[0], u0);
@@ -169,14 +196,11 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
     const UnitIdx u = decode_ticket(cur, p.B, p.H, p.G);
     const int j = u.chunk;
     const int64_t bh = u.bh;
-    const int b = u.b, h = u.h;
     const int t0 = j * kL;
     int* flags = p.flags + bh * (p.nc + 1);
-    // thread 0 takes the next ticket now and uses it once [K | Kp] is free
-    uint32_t nx = 0, nxt = 0;
-    UnitIdx nu = u;
-    int pf = 0;  // parts of the next chunk's operands issued (K/Kp, X/Xp, Q)
-    if (tid == 0) nx = atomicAdd(p.ticket, 1u);
+    uint32_t nx = 0;
+    bool next_loaded = false;
+    if (tid == 0) nx = atomicAdd(p.ticket, 1u);  // the next ticket, published to the CTA at the chain
 
     // per-token scalars and the in-chunk cumulative sum c (mamba3.py:40)
     if (tid < 64) {
@@ -194,15 +218,12 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
       s_wg[tid] = w * s_g[tid];
       s_wb[tid] = w * s_b[tid];
     }
-    // the previous chunk's y tile and saved state leave shared memory before [wgX | wbXp] and the
-    // scores overwrite them
-    if (tid == 0) umma::bulk_wait_read();
     const bool load_ok = umma::mbar_wait(&bars[0], par, p.status);
-    const float a_chunk = expf(s_c[63]);
     bool ok = __syncthreads_and(load_ok);
+    const float a_chunk = expf(s_c[63]);
 
     if (ok) {
-      // MMA1 (scores) needs no rescaled operand: start it before scaling X
+      // MMA1: S = Q [K;Kp]^T
       if (tid == 0) {
         umma::fence_after_sync();
         const uint32_t q0 = umma::smem_u32(sQ), kk0 = umma::smem_u32(sKK);
@@ -215,52 +236,56 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
         }
         umma::mma_commit(&bars[1]);
       }
-      // [wgX | wbXp]: scale each row s of X / Xp (a 16-byte chunk at byte offset o lies in row o / 128)
-      for (int i = tid; i < 1024; i += kTcThreads) {
-        const int tile = i >> 9;
-        const uint32_t off = (uint32_t)(i & 511) * 16u;
-        const float f = tile ? s_wb[off >> 7] : s_wg[off >> 7];
-        const uint4 v = *reinterpret_cast<const uint4*>((tile ? sXp : sX) + off);
+      ok = __syncthreads_and(umma::mbar_wait(&bars[1], par, p.status));
+    }
+    constexpr int NB = 4 / WPS;  // 32-column blocks of S per warp
+    uint32_t pk[NB][8];          // this thread's scores (bf16 pairs) until K|Kp is free
+    if (ok) {
+      umma::fence_after_sync();
+      // MMA1 is done with K|Kp: scale them in place, K rows s by w_s g_s and Kp rows by w_s b_s (for
+      // MMA3).  A 16-byte chunk at byte offset o of a 64 x 64 tile lies in row (o mod 8192) / 128.
+      for (uint32_t off = (uint32_t)tid * 16u; off < (uint32_t)QB * 16384u; off += S::THREADS * 16u) {
+        const float f = ((off >> 13) & 1u) ? s_wb[(off & 8191u) >> 7] : s_wg[(off & 8191u) >> 7];
+        const uint4 v = *reinterpret_cast<const uint4*>(sKK + off);
         uint4 o;
         float2 e;
         e = unpack_bf16(v.x); o.x = pack_bf16(e.x * f, e.y * f);
         e = unpack_bf16(v.y); o.y = pack_bf16(e.x * f, e.y * f);
         e = unpack_bf16(v.z); o.z = pack_bf16(e.x * f, e.y * f);
         e = unpack_bf16(v.w); o.w = pack_bf16(e.x * f, e.y * f);
-        *reinterpret_cast<uint4*>(sXs + tile * 8192 + off) = o;
+        *reinterpret_cast<uint4*>(sKK + off) = o;
       }
       umma::fence_proxy_async_smem();
       umma::fence_before_sync();
       __syncthreads();
+      // MMA3: the chunk state, one M=64 product per 64-wide half of n, into lanes 16-31
       if (tid == 0) {
         umma::fence_after_sync();
-        const uint32_t kk0 = umma::smem_u32(sKK), xs0 = umma::smem_u32(sXs);
-        constexpr uint32_t id3 = umma::idesc_bf16(NS, 64, true, true);
+        const uint32_t kk0 = umma::smem_u32(sKK), x0 = umma::smem_u32(sX), xp0 = umma::smem_u32(sXp);
+        constexpr uint32_t id3 = umma::idesc_bf16(64, 64, true, true);
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t part = ks >> 2, kin = ks & 3;
-          umma::mma_bf16(tmem + 192, umma::desc_sw128(kk0 + part * 8192 + kin * 2048, 16384, 1024),
-                         umma::desc_sw128(xs0 + part * 8192 + kin * 2048, 8192, 1024), id3, ks > 0);
+        for (int hf = 0; hf < QB; ++hf) {
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t part = ks >> 2, kin = ks & 3;
+            umma::mma_bf16(tmem + (16u << 16) + 64 * hf,
+                           umma::desc_sw128(kk0 + hf * 16384 + part * 8192 + kin * 2048, 16384, 1024),
+                           umma::desc_sw128((part ? xp0 : x0) + kin * 2048, 8192, 1024), id3, ks > 0);
+          }
         }
-        umma::mma_commit(&bars[4]);
+        umma::mma_commit(&bars[2]);
       }
-      // the score epilogue needs only MMA1; MMA3 (chunk state) finishes meanwhile
-      ok = __syncthreads_and(umma::mbar_wait(&bars[1], par, p.status));
-    }
-    if (ok) {
-      umma::fence_after_sync();
-      // scores -> Ps (bf16, K-major [2][64 t][64 s]) over the K/Kp tiles.  TMEM gives lanes 0-15
-      // the S row; lanes 16-31 take over columns 16-31 of each 32-column block by one shuffle each.
-      const int sp = warp & 3, half = warp >> 2;
+      // scores -> registers.  TMEM gives lanes 0-15 of the warp the S row t; lanes 16-31 take over
+      // columns 16-31 of each 32-column block by one shuffle each.  Block k: half k / 2 (0: K with
+      // gamma, 1: Kp with beta), columns 32 (k % 2) of that half.
       const int t = 16 * sp + (lane & 15);
-      const bool hiL = lane >= 16;
-      const float* coef = half ? s_b : s_g;
       const float ct = s_c[t];
 #pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
+      for (int bi = 0; bi < NB; ++bi) {
+        const int blk = hw * NB + bi, half = blk >> 1, cc = blk & 1;
+        const float* coef = half ? s_b : s_g;
         float v[32];
-        umma::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + half * 64 + cc * 32, v);
-        uint32_t w8[8];
+        umma::tmem_ld32(tmem + tlane + blk * 32, v);
 #pragma unroll
         for (int i = 0; i < 16; i += 2) {
           const float r0 = __shfl_xor_sync(0xffffffffu, v[16 + i], 16);
@@ -269,104 +294,96 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
           const float a0 = hiL ? r0 : v[i], a1 = hiL ? r1 : v[i + 1];
           const float v0 = (s0 <= t) ? a0 * coef[s0] * __expf(ct - s_c[s0]) : 0.f;
           const float v1 = (s0 + 1 <= t) ? a1 * coef[s0 + 1] * __expf(ct - s_c[s0 + 1]) : 0.f;
-          w8[i >> 1] = pack_bf16(v0, v1);
+          pk[bi][i >> 1] = pack_bf16(v0, v1);
         }
-        const int c0 = cc * 4 + (hiL ? 2 : 0);
-        *reinterpret_cast<uint4*>(sPs + half * 8192 + umma::sw128_offset(t, c0)) = make_uint4(w8[0], w8[1], w8[2], w8[3]);
-        *reinterpret_cast<uint4*>(sPs + half * 8192 + umma::sw128_offset(t, c0 + 1)) =
-            make_uint4(w8[4], w8[5], w8[6], w8[7]);
+      }
+      ok = __syncthreads_and(umma::mbar_wait(&bars[2], par, p.status));  // MMA3 done: K|Kp free
+    }
+    if (ok) {
+      umma::fence_after_sync();
+      // Ps (bf16, K-major [2][64 t][64 s]) over K|Kp block 0
+      {
+        const int t = 16 * sp + (lane & 15);
+#pragma unroll
+        for (int bi = 0; bi < NB; ++bi) {
+          const int blk = hw * NB + bi, half = blk >> 1, cc = blk & 1;
+          const int c0 = cc * 4 + (hiL ? 2 : 0);
+          *reinterpret_cast<uint4*>(sPs + half * 8192 + umma::sw128_offset(t, c0)) =
+              make_uint4(pk[bi][0], pk[bi][1], pk[bi][2], pk[bi][3]);
+          *reinterpret_cast<uint4*>(sPs + half * 8192 + umma::sw128_offset(t, c0 + 1)) =
+              make_uint4(pk[bi][4], pk[bi][5], pk[bi][6], pk[bi][7]);
+        }
       }
       umma::fence_proxy_async_smem();
       umma::fence_before_sync();
       __syncthreads();
       if (tid == 0) {
         umma::fence_after_sync();
+        // MMA2: Yi = Ps [X;Xp] into lanes 0-15, cols 0-63 (the scores' TMEM has been read)
         const uint32_t ps0 = umma::smem_u32(sPs), x0 = umma::smem_u32(sX), xp0 = umma::smem_u32(sXp);
         constexpr uint32_t id2 = umma::idesc_bf16(64, 64, false, true);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           const uint32_t part = ks >> 2, kin = ks & 3;
-          umma::mma_bf16(tmem + 128, umma::desc_sw128(ps0 + part * 8192 + kin * 32, 16, 1024),
+          umma::mma_bf16(tmem, umma::desc_sw128(ps0 + part * 8192 + kin * 32, 16, 1024),
                          umma::desc_sw128((part ? xp0 : x0) + kin * 2048, 8192, 1024), id2, ks > 0);
         }
-        umma::mma_commit(&bars[2]);
+        misc[3] = nx;
         misc[2] = (j == 0) ? kFlagReady : wait_flag(&flags[j], p.status);
+        if (misc[2] != kFlagReady) umma::mma_commit(&bars[3]);  // MMA2 must finish before TMEM is freed
       }
       __syncthreads();
       ok = misc[2] == kFlagReady;
-      if (!ok) {  // let the MMAs finish before TMEM is freed
-        umma::mbar_wait(&bars[2], par, p.status);
-        umma::mbar_wait(&bars[4], par, p.status);
-      }
+      if (!ok) umma::mbar_wait(&bars[3], par, p.status);
     }
-    if (ok) ok = __syncthreads_and(umma::mbar_wait(&bars[4], par, p.status));  // S_loc ready
     if (ok) {
-      umma::fence_after_sync();
-      // MMA1 and MMA3 are done with [K | Kp]: the next chunk's tiles start loading over them
-      if (tid == 0) {
-        misc[3] = nx;
-        if (nx < total) {
-          nu = decode_ticket(nx, p.B, p.H, p.G);
-          umma::mbar_arrive_expect_tx(&bars[0], kLoadBytes);
-          fwd_load_kk<NS>(p, sKK, &bars[0], nu);
-          pf = 1;
-        }
-      }
-      // state hand-off: S_in[j+1] = e^{c_L} S_in[j] + S_loc (mamba3.py:52)
-      const int sp = warp & 3, ph = warp >> 2;
-      const bool rows128 = (NS == 128);
-      const int n = rows128 ? 32 * sp + lane : 16 * sp + (lane & 15);
-      const bool active = rows128 || lane < 16;
-      float sl[32], sin[32];
-      umma::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + 192 + 32 * ph, sl);
-      if (active) {
-        // ring slots are [p/4][n][4] (a warp's float4 access covers 512 contiguous bytes); the
-        // caller's initial and final states are [p][n]
-        const int64_t PN = (int64_t)kP * NS;
-        if (j == 0) {
+      // state hand-off: S_in[j+1] = e^{c_L} S_in[j] + S_loc (mamba3.py:52).  Lanes 16-31 hold the
+      // rows n = 64 h + 16 sp + lane - 16 of S_loc (half h); a warp takes 16 columns p at a time,
+      // (h, p range) pairs split over the warps of a sub-partition.  Ring slots are [p/4][n][4];
+      // the caller's initial and final states are [p][n].  S_in[j] also goes to shared memory in
+      // bf16 (the B operand of MMA4 and the saved state).
+      const int64_t PN = (int64_t)kP * NS;
+      const float4* ring_in = reinterpret_cast<const float4*>(p.ring + (bh * 2 + (j & 1)) * PN);
+      float4* ring_out = reinterpret_cast<float4*>(p.ring + (bh * 2 + ((j + 1) & 1)) * PN);
+      float* fin = (j == p.nc - 1 && p.fin) ? p.fin + bh * PN : nullptr;
+      constexpr int NP = 4 * QB / WPS;  // (half, 16-column block) pairs per warp
 #pragma unroll
-          for (int i = 0; i < 32; ++i) sin[i] = p.init ? __ldcg(p.init + bh * PN + (32 * ph + i) * NS + n) : 0.f;
-        } else {
-          const float4* s4 = reinterpret_cast<const float4*>(p.ring + (bh * 2 + (j & 1)) * PN) + 8 * ph * NS + n;
+      for (int pi = 0; pi < NP; ++pi) {
+        const int pair = hw * NP + pi, hf = pair >> 2, pc = pair & 3;
+        const int n = 64 * hf + 16 * sp + (lane - 16);
+        float sl[16];
+        umma::tmem_ld16(tmem + tlane + 64 * hf + 16 * pc, sl);
+        if (hiL) {
+          float sin[16];
+          if (j == 0) {
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float4 v = __ldcg(s4 + q * NS);
-            sin[4 * q] = v.x; sin[4 * q + 1] = v.y; sin[4 * q + 2] = v.z; sin[4 * q + 3] = v.w;
+            for (int i = 0; i < 16; ++i) sin[i] = p.init ? __ldcg(p.init + bh * PN + (16 * pc + i) * NS + n) : 0.f;
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float4 v = __ldcg(ring_in + (4 * pc + q) * NS + n);
+              sin[4 * q] = v.x; sin[4 * q + 1] = v.y; sin[4 * q + 2] = v.z; sin[4 * q + 3] = v.w;
+            }
           }
-        }
-        float* fin = (j == p.nc - 1 && p.fin) ? p.fin + bh * PN : nullptr;
-        float4* d4 = reinterpret_cast<float4*>(p.ring + (bh * 2 + ((j + 1) & 1)) * PN) + 8 * ph * NS + n;
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
-          d4[q * NS] = make_float4(a_chunk * sin[4 * q] + sl[4 * q], a_chunk * sin[4 * q + 1] + sl[4 * q + 1],
-                                   a_chunk * sin[4 * q + 2] + sl[4 * q + 2], a_chunk * sin[4 * q + 3] + sl[4 * q + 3]);
-        if (fin) {
+          for (int q = 0; q < 4; ++q)
+            ring_out[(4 * pc + q) * NS + n] =
+                make_float4(a_chunk * sin[4 * q] + sl[4 * q], a_chunk * sin[4 * q + 1] + sl[4 * q + 1],
+                            a_chunk * sin[4 * q + 2] + sl[4 * q + 2], a_chunk * sin[4 * q + 3] + sl[4 * q + 3]);
+          if (fin) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) fin[(32 * ph + i) * NS + n] = a_chunk * sin[i] + sl[i];
+            for (int i = 0; i < 16; ++i) fin[(16 * pc + i) * NS + n] = a_chunk * sin[i] + sl[i];
+          }
+          stage_row16(sSin, n, 2 * pc, sin);
         }
       }
-      // publish the outgoing state first; the bf16 copies below are off the chain's critical path
       // the barrier orders every thread's ring writes before thread 0's release (cumulative)
       __syncthreads();
       if (tid == 0) st_release(&flags[j + 1], kFlagReady);
-      umma::mbar_wait(&bars[2], par, p.status);  // MMA2 has read the scores (S_in tile) and X / Xp
-      if (tid == 0 && pf == 1) {
-        fwd_load_x(p, sX, sXp, &bars[0], nu);
-        pf = 2;
-      }
-      if (active) {
-        // S_in[j] in bf16: B operand of MMA4 ([n][p], p contiguous) and the saved state
-        uint4 pk[4];
-#pragma unroll
-        for (int qd = 0; qd < 4; ++qd)
-          pk[qd] = make_uint4(pack_bf16(sin[qd * 8 + 0], sin[qd * 8 + 1]), pack_bf16(sin[qd * 8 + 2], sin[qd * 8 + 3]),
-                              pack_bf16(sin[qd * 8 + 4], sin[qd * 8 + 5]), pack_bf16(sin[qd * 8 + 6], sin[qd * 8 + 7]));
-#pragma unroll
-        for (int qd = 0; qd < 4; ++qd) *reinterpret_cast<uint4*>(sSin + umma::sw128_offset(n, 4 * ph + qd)) = pk[qd];
-      }
       umma::fence_proxy_async_smem();
       umma::fence_before_sync();
       __syncthreads();
+      const uint32_t nxt = misc[3];
       if (tid == 0) {
         if (p.states) {
           // the saved state is the shared-memory image itself (bf16, 128-byte swizzle), so the
@@ -376,74 +393,75 @@ __global__ void __launch_bounds__(kTcThreads, 2) ssd_fwd_tc_kernel(const __grid_
           umma::bulk_commit();
         }
         umma::fence_after_sync();
+        // MMA4: Ye = Q S_in^T into lanes 0-15, cols 64-127
         const uint32_t q0 = umma::smem_u32(sQ), sin0 = umma::smem_u32(sSin);
         constexpr uint32_t id4 = umma::idesc_bf16(64, 64, false, true);
 #pragma unroll
         for (int ks = 0; ks < NS / 16; ++ks) {
           const uint32_t qb = ks >> 2, kin = ks & 3;
-          umma::mma_bf16(tmem + 128 + (16u << 16), umma::desc_sw128(q0 + qb * 8192 + kin * 32, 16, 1024),
+          umma::mma_bf16(tmem + 64, umma::desc_sw128(q0 + qb * 8192 + kin * 32, 16, 1024),
                          umma::desc_sw128(sin0 + ks * 2048, 8192, 1024), id4, ks > 0);
         }
         umma::mma_commit(&bars[3]);
       }
-      ok = __syncthreads_and(umma::mbar_wait(&bars[3], par, p.status));
-      nxt = misc[3];
       if (tid < 64 && nxt < total) fwd_prefetch_scalars(p, decode_ticket(nxt, p.B, p.H, p.G), tid, s_nx);
+      ok = __syncthreads_and(umma::mbar_wait(&bars[3], par, p.status));
     } else if (tid == 0) {
       st_release(&flags[j + 1], kFlagAbort);
     }
     if (ok) {
       umma::fence_after_sync();
-      // MMA4 is done with Q: the next chunk's Q tiles complete its operand set
-      if (tid == 0 && pf == 2) {
-        fwd_load_q<NS>(p, sQ, &bars[0], nu);
-        pf = 3;
-      }
-      // y = Yi + e^{c_t} Ye  (mamba3.py:55), staged as a bf16 tile over [wgX | wbXp] and TMA-stored
-      const int sp = warp & 3, ph = warp >> 2;
+      // y = Yi + e^{c_t} Ye (mamba3.py:55): lanes 0-15 hold row t = 16 sp + lane; 16 columns at a
+      // time, staged as a bf16 tile over X
       const int t = 16 * sp + (lane & 15);
-      float v[32];
-      umma::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + 128 + 32 * ph, v);
       const float ect = s_ec[t];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] += ect * __shfl_xor_sync(0xffffffffu, v[i], 16);
-      if (lane < 16) {
+      for (int qi = 0; qi < 4 / WPS; ++qi) {
+        const int q = hw * (4 / WPS) + qi;
+        float yi[16], ye[16];
+        umma::tmem_ld16x2(tmem + tlane + 16 * q, tmem + tlane + 64 + 16 * q, yi, ye);
+        if (!hiL) {
 #pragma unroll
-        for (int qd = 0; qd < 4; ++qd)
-          *reinterpret_cast<uint4*>(sXs + umma::sw128_offset(t, 4 * ph + qd)) =
-              make_uint4(pack_bf16(v[8 * qd], v[8 * qd + 1]), pack_bf16(v[8 * qd + 2], v[8 * qd + 3]),
-                         pack_bf16(v[8 * qd + 4], v[8 * qd + 5]), pack_bf16(v[8 * qd + 6], v[8 * qd + 7]));
+          for (int i = 0; i < 16; ++i) yi[i] += ect * ye[i];
+          stage_row16(sY, t, 2 * q, yi);
+        }
       }
       umma::fence_proxy_async_smem();
       umma::fence_before_sync();
       __syncthreads();
       if (tid == 0) {
-        umma::tma_store_4d(&p.ty, sXs, 0, h, t0, b);
+        umma::tma_store_4d(&p.ty, sY, 0, u.h, t0, u.b);
         umma::bulk_commit();
+        // the y tile and the saved state leave shared memory, then the next chunk's operands load
+        umma::bulk_wait_read();
+        if (nx < total) {
+          const UnitIdx nu = decode_ticket(nx, p.B, p.H, p.G);
+          umma::mbar_arrive_expect_tx(&bars[0], S::LOAD_BYTES);
+          fwd_load_q<NS>(p, sQ, &bars[0], nu);
+          fwd_load_kk<NS>(p, sKK, &bars[0], nu);
+          fwd_load_x(p, sX, sXp, &bars[0], nu);
+          next_loaded = true;
+        }
       }
     }
-    __syncthreads();  // every read of this chunk's tiles is done
+    umma::fence_before_sync();
+    __syncthreads();  // every read of this chunk's tiles and TMEM columns is done
     if (!ok) {
-      // leave after an error: the ticket already taken is aborted, and any of its loads that were
-      // issued are completed (the rest issued too) so that none is in flight at exit
-      if (tid == 0 && nx < total) {
+      // leave after an error: the ticket already taken is aborted (its loads were never issued)
+      if (tid == 0 && nx < total && !next_loaded) {
         const UnitIdx cn = decode_ticket(nx, p.B, p.H, p.G);
         st_release(&p.flags[cn.bh * (p.nc + 1) + cn.chunk + 1], kFlagAbort);
-        if (pf > 0) {
-          if (pf < 2) fwd_load_x(p, sX, sXp, &bars[0], cn);
-          if (pf < 3) fwd_load_q<NS>(p, sQ, &bars[0], cn);
-          umma::mbar_wait(&bars[0], par ^ 1, p.status);
-        }
       }
       break;
     }
-    cur = nxt;
+    umma::fence_after_sync();
+    cur = misc[3];
   }
   if (tid == 0) umma::bulk_wait_all();  // staged tiles must be read out before exit
   if (tid < 64) umma::cp_async_wait_all();
   umma::fence_before_sync();
   __syncthreads();
-  if (warp == 0) umma::tmem_dealloc(tmem, 256);
+  if (warp == 0) umma::tmem_dealloc(tmem, 128);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -559,24 +577,6 @@ __device__ __forceinline__ void load_chunk(const unsigned char* tile, int r, int
   e = unpack_bf16(v.w); o[6] = e.x; o[7] = e.y;
 }
 
-// 32 floats -> bf16 into chunks [c0, c0 + 4) of row r of a 128-byte-swizzled staging tile
-__device__ __forceinline__ void stage_row32(unsigned char* tile, int r, int c0, const float* v) {
-#pragma unroll
-  for (int qd = 0; qd < 4; ++qd)
-    *reinterpret_cast<uint4*>(tile + umma::sw128_offset(r, c0 + qd)) =
-        make_uint4(pack_bf16(v[8 * qd], v[8 * qd + 1]), pack_bf16(v[8 * qd + 2], v[8 * qd + 3]),
-                   pack_bf16(v[8 * qd + 4], v[8 * qd + 5]), pack_bf16(v[8 * qd + 6], v[8 * qd + 7]));
-}
-
-// 16 floats -> bf16 into chunks c0, c0 + 1 of row r of a 128-byte-swizzled staging tile
-__device__ __forceinline__ void stage_row16(unsigned char* tile, int r, int c0, const float* v) {
-#pragma unroll
-  for (int qd = 0; qd < 2; ++qd)
-    *reinterpret_cast<uint4*>(tile + umma::sw128_offset(r, c0 + qd)) =
-        make_uint4(pack_bf16(v[8 * qd], v[8 * qd + 1]), pack_bf16(v[8 * qd + 2], v[8 * qd + 3]),
-                   pack_bf16(v[8 * qd + 4], v[8 * qd + 5]), pack_bf16(v[8 * qd + 6], v[8 * qd + 7]));
-}
-
 // Persistent: one CTA per SM walks the chunks in ticket order (reverse chunk order), 512 threads.
 // While a chunk is worked on, the next ticket's operands load into the other input stage.  Each
 // CTA takes its tickets in increasing order and a chunk only waits on a lower ticket, so the
@@ -660,7 +660,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
   unsigned char* sPS = sW;   // [A | Ap]   [2][64 t][64 s]
   unsigned char* sXW = sW;   // [wgX | wbXp] (128 rows)
   unsigned char* sEG = sm + S::E;  // [Eg | Epb] [2][64 t][64 s]
-  unsigned char* sGN = sm + S::E;  // Gn [NS n][64 p]
+  // Gn [NS n][64 p] goes over the current stage's S_in tile (set per chunk below)
   float* s_scal = reinterpret_cast<float*>(sm + S::SCAL);  // [2 parity][c | ec | w | wg wb | g | b]
   float* s_nx = s_scal + 2 * 448;                            // next chunk's [adt | gamma | beta]
   float* s_rowZ = reinterpret_cast<float*>(sm + S::RED);  // [2 column block][2 half][64]
@@ -710,6 +710,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
     unsigned char* sXX = sm + stage * S::STAGE + S::XX;
     unsigned char* sDY = sm + stage * S::STAGE + S::DY;
     unsigned char* sSin = sm + stage * S::STAGE + S::SIN;
+    unsigned char* sGN = sSin;  // Gn [NS n][64 p] replaces S_in once the first group is done
     const BwdChunk ck = bwd_chunk(p, cur);
     const int j = ck.j, b = ck.b, h = ck.h, g = ck.g, t0 = ck.t0;
     const int64_t bh = ck.bh;
@@ -718,7 +719,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
     // hand-off it drains the previous chunk's output tiles (its own TMA stores) and loads the next
     // chunk's operands into the other stage.
     uint32_t nx = 0, nxt = 0;
-    bool prefetched = false;
+    bool prefetched = false, published = false;
     if (tid == 32) nx = atomicAdd(p.ticket, 1u);
     // this chunk's scalars were prepared by the end of the previous one (or before the loop)
     const float* s_c = s_scal + (it & 1) * 448;
@@ -870,8 +871,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
         umma::mma_commit(&bars[3]);
         misc[2] = (j == p.nc - 1) ? kFlagReady : wait_flag(&flags[j + 1], p.status);
       }
-      // [wgX | wbXp] takes the place of [A | Ap] once the second group has read it; it is built
-      // while thread 0 waits for the hand-off
       if (tid == 32) {
         misc[3] = nx;
         umma::bulk_wait_read();  // the previous chunk's output tiles (in the other stage) are out
@@ -880,14 +879,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
           prefetched = true;
         }
       }
-      const bool g2 = umma::mbar_wait(&bars[3], par, p.status);
-      if (g2) scale_rows(sXX, sXW, 16384, s_wgb, tid);
-      ok = __syncthreads_and(g2) && misc[2] == kFlagReady;
+      __syncthreads();
+      ok = misc[2] == kFlagReady;
       nxt = misc[3];
       if (scal_warp && nxt < total) bwd_prefetch_scalars(p, bwd_chunk(p, nxt), tid - 64, s_nx);  // next chunk
+      if (!ok) umma::mbar_wait(&bars[3], par, p.status);  // the second group must finish before TMEM is freed
     }
     if (ok) {
-      // reverse state hand-off: G[j] = dSl'^T + e^{c_L} G[j+1];  da = <G[j+1], S_in[j]>
+      // reverse state hand-off, while the second group runs on the tensor pipe:
+      // G[j] = dSl'^T + e^{c_L} G[j+1];  da = <G[j+1], S_in[j]>
       // warp w: sub-partition sp = w % 4 (state rows n), p-quarter pq = w / 4 (16 columns)
       const int sp = warp & 3, pq = warp >> 2;
       const bool rows128 = (NS == 128);
@@ -925,6 +925,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
       // the barrier orders every thread's ring writes before thread 0's release (cumulative)
       __syncthreads();
       if (tid == 0) st_release(&flags[j], kFlagReady);
+      published = true;
+      // Gn (bf16, [n][p] like S_in) replaces S_in in its tile: the first group, the only reader of
+      // S_in, is done; each thread reads the S_in chunk it then overwrites
       if (active) {
 #pragma unroll
         for (int qd = 0; qd < 2; ++qd) {
@@ -939,9 +942,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
       }
       da_part = warp_sum(da_part);
       if (lane == 0) s_da[warp] = da_part;
+      // [wgX | wbXp] takes the place of [A | Ap] once the second group has read it
+      const bool g2 = umma::mbar_wait(&bars[3], par, p.status);
+      if (g2) scale_rows(sXX, sXW, 16384, s_wgb, tid);
       umma::fence_proxy_async_smem();
       umma::fence_before_sync();
-      __syncthreads();
+      ok = __syncthreads_and(g2);
+    }
+    if (ok) {
       if (tid == 0) {
         umma::fence_after_sync();
         const uint32_t kk0 = umma::smem_u32(sKK), xw0 = umma::smem_u32(sXW), gn0 = umma::smem_u32(sGN);
@@ -1000,7 +1008,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
         }
       }
       ok = __syncthreads_and(umma::mbar_wait(&bars[4], par, p.status));
-    } else if (tid == 0) {
+    } else if (tid == 0 && !published) {
       st_release(&flags[j], kFlagAbort);
     }
     if (ok) {
@@ -1411,9 +1419,10 @@ int launch_fwd(const zb_ssd_args* a, ChainSync sync, void* states, void* ring, c
   auto k = ssd_fwd_tc_kernel<NS>;
   const int smem = (int)FwdSmem<NS>::ALLOC;
   if (dyn_smem(reinterpret_cast<const void*>(k), smem) != ZB_OK) return ZB_ERR_CUDA;
-  const int64_t units = a->B * a->H * p.nc, slots = 2 * (int64_t)sm_count();  // persistent: two CTAs per SM
+  // persistent: CTAS_PER_SM CTAs per SM
+  const int64_t units = a->B * a->H * p.nc, slots = (int64_t)FwdSmem<NS>::CTAS_PER_SM * sm_count();
   const dim3 grid((unsigned)(units < slots ? units : slots));
-  k<<<grid, kTcThreads, smem, stream>>>(p);
+  k<<<grid, FwdSmem<NS>::THREADS, smem, stream>>>(p);
   note_launches(1);
   return cudaPeekAtLastError() == cudaSuccess ? ZB_OK : ZB_ERR_CUDA;
 }

@@ -577,17 +577,18 @@ def load_reference_state_dict(model: ZenithForCausalLM, state_dict: dict):
 # training step (zenith/train.py:99-111)
 
 def train_step(model: nn.Module, opt: torch.optim.Optimizer, ids: Tensor, loops: int = 1, grad_clip: float = 1.0,
-               amp: bool = True) -> Tensor:
-    """One optimiser step on a batch of token ids: bf16-autocast forward with ``labels=ids``,
+               amp: bool = True, labels: Optional[Tensor] = None) -> Tensor:
+    """One optimiser step on a batch of token ids: bf16-autocast forward with ``labels=ids`` (or the
+    given ``labels``, shifted inside the model like ids),
     backward (under ``DistributedDataParallel`` the gradient all-reduce runs during it), global
     gradient-norm clipping, the optimiser step.  Returns the loss (a device scalar, no sync).
     Raises ``SsdError`` when a kernel of an earlier step recorded an error in the device status
     word (a label outside the vocabulary, a timed-out wait), as soon as that is visible without
     a synchronisation: at the latest, the step after the faulty one has finished on the GPU."""
-    L.poll_status(ids.device)  # an error an earlier step's kernels recorded (e.g. a label out of range)
+    L.poll_status(ids)  # an error an earlier step's kernels recorded (e.g. a label out of range)
     ctx = torch.autocast("cuda", dtype=torch.bfloat16) if amp else nullcontext()
     with ctx:
-        loss = model(ids, labels=ids, loops=loops).loss
+        loss = model(ids, labels=ids if labels is None else labels, loops=loops).loss
     loss.backward()
     fused = all(g.get("fused") for g in opt.param_groups) and isinstance(opt, torch.optim.Adam)
     if fused:
@@ -605,7 +606,7 @@ def train_step(model: nn.Module, opt: torch.optim.Optimizer, ids: Tensor, loops:
         torch.nn.utils.clip_grad_norm_(model.parameters(), grad_clip, foreach=True)
         opt.step()
     opt.zero_grad(set_to_none=True)
-    L.poll_status(ids.device)
+    L.poll_status(ids)
     return loss.detach()
 
 

@@ -219,7 +219,7 @@ class _Mamba3Fused(torch.autograd.Function):
         ctx.has_z = z is not None
         ctx.meta = (float(A_floor), int(chunk_size), float(eps), op_dtype)
         ctx.param_dtypes = [prm.dtype for prm in (dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D)]
-        L.poll_status(x.device)
+        L.poll_status(x)
         return out
 
     @staticmethod
@@ -236,7 +236,7 @@ class _Mamba3Fused(torch.autograd.Function):
         gp = _layer_bwd(x, z, Bm, Cm, dd_dt, dd_A, trap, ang, params, saved, A_floor, chunk_size, eps, op_dtype, dout,
                         grads_in)
         gp = [g.to(dt) for g, dt in zip(gp, ctx.param_dtypes)]
-        L.poll_status(x.device)
+        L.poll_status(x)
         return (grads_in["dx"], grads_in["dz"], grads_in["dBm"], grads_in["dCm"], grads_in["ddd_dt"],
                 grads_in["ddd_A"], grads_in["dtrap"], grads_in["dang"], *gp, None, None, None, None)
 

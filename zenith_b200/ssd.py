@@ -36,7 +36,14 @@ def _acc_dtype(vdt: torch.dtype) -> torch.dtype:
     return torch.float64 if vdt == torch.float64 else torch.float32
 
 
-def _build_args(x, q, k, kp, xp, adt, gamma, beta, chunk_size, flags=0) -> L.Args:
+# Stand-in data address for sizing calls made without data (fake tensors under torch.compile):
+# 4 KiB aligned, like every allocation.  The kernel family, and with it the saved-state size, depends
+# on the inputs' alignment; the real ops re-align a misaligned input (_realign) so that they always
+# agree with a sizing call.
+_SIZING_ADDR = 1 << 12
+
+
+def _build_args(x, q, k, kp, xp, adt, gamma, beta, chunk_size, flags=0, sizing_only=False) -> L.Args:
     B, T, H, P = x.shape
     G, N = q.shape[2], q.shape[3]
     a = L.Args()
@@ -45,8 +52,16 @@ def _build_args(x, q, k, kp, xp, adt, gamma, beta, chunk_size, flags=0) -> L.Arg
     a.scalar_dtype = L.DTYPE_CODE[adt.dtype]
     a.flags = flags
     for n, t in zip(_VEC + _SCA, (x, q, k, kp, xp, adt, gamma, beta)):
-        setattr(a, n, L.view(t))
+        setattr(a, n, L.view(t, _SIZING_ADDR if sizing_only else None))
     return a
+
+
+def _realign(t: Tensor) -> Tensor:
+    """``t`` itself, or a copy with the same strides at a 16-byte aligned address when its data
+    address is not (a view at an odd element offset): see _SIZING_ADDR."""
+    if t.data_ptr() % 16 == 0:
+        return t
+    return torch.empty_strided(t.size(), t.stride(), dtype=t.dtype, device=t.device).copy_(t)
 
 
 def _stream(dev: torch.device) -> int:
@@ -62,7 +77,8 @@ def kernel_family(x, q, k, kp, xp, adt, gamma, beta, chunk_size, *, states_saved
 
 
 def states_nbytes(x, q, k, kp, xp, adt, gamma, beta, chunk_size) -> int:
-    a = _build_args(x, q, k, kp, xp, adt, gamma, beta, chunk_size)
+    """Bytes of the saved chunk states, from shapes, strides and dtypes only (no data access)."""
+    a = _build_args(x, q, k, kp, xp, adt, gamma, beta, chunk_size, sizing_only=True)
     return int(L.lib().zb_ssd_states_bytes(ctypes.byref(a)))
 
 
@@ -77,6 +93,7 @@ def ssd_fwd_op(x: Tensor, q: Tensor, k: Tensor, kp: Tensor, xp: Tensor, adt: Ten
     B, T, H, P = x.shape
     N = q.shape[3]
     dev = x.device
+    x, q, k, kp, xp = (_realign(t) for t in (x, q, k, kp, xp))
     a = _build_args(x, q, k, kp, xp, adt, gamma, beta, chunk_size, L.ZB_FLAG_STATE_ONLY if state_only else 0)
     lib = L.lib()
     y = torch.empty((0,) if state_only else (B, T, H, P), dtype=x.dtype, device=dev)
@@ -111,6 +128,7 @@ def ssd_bwd_op(dy: Tensor, x: Tensor, q: Tensor, k: Tensor, kp: Tensor, xp: Tens
     B, T, H, P = x.shape
     dev = x.device
     lib = L.lib()
+    dy, x, q, k, kp, xp = (_realign(t) for t in (dy, x, q, k, kp, xp))
     a = _build_args(x, q, k, kp, xp, adt, gamma, beta, chunk_size, L.ZB_FLAG_STATE_ONLY if state_only else 0)
     if state_only:
         grads = [torch.empty(0, dtype=t.dtype, device=dev) for t in (x, q, k, kp, xp, adt, gamma, beta)]
@@ -172,7 +190,7 @@ def _backward(ctx, dy, dfinal, _dstates):
     if dfinal is not None:
         dfinal = dfinal.to(_acc_dtype(x.dtype)).contiguous()
     out = ssd_bwd_op(dy, x, q, k, kp, xp, adt, gamma, beta, states, ctx.chunk_size, init, dfinal, False)
-    L.poll_status(x.device)
+    L.poll_status(x)
     dx, dq, dk, dkp, dxp, dadt, dgamma, dbeta, dinit = out
     return dx, dq, dk, dkp, dxp, dadt, dgamma, dbeta, None, (dinit if ctx.has_init else None), None, None
 
@@ -237,7 +255,7 @@ def ssd(x, q, k, kp, xp, adt, gamma, beta, chunk_size, *, initial_state=None, re
     need_grad = torch.is_grad_enabled() and any(
         t.requires_grad for t in (x, q, k, kp, xp, adt, gamma, beta, initial_state) if t is not None)
     y, final, _ = torch.ops.zenith_b200.ssd_fwd(*args, int(chunk_size), initial_state, need_grad, False)
-    L.poll_status(x.device)
+    L.poll_status(x)
     if y.dtype != out_dtype:
         y = y.to(out_dtype)
     if return_final_state:
