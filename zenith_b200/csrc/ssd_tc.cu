@@ -41,13 +41,14 @@ struct FwdSmem {
   static constexpr uint32_t XX = KK + QB * 16384;         // [X | Xp] [64 s][64 p]
   static constexpr uint32_t SIN = NS == 128 ? KK + 16384 : XX + 16384;  // S_in image [NS n][64 p]
   static constexpr uint32_t SCAL = NS == 128 ? XX + 16384 : SIN + NS * 128;
-  // c, ec, wg, wb, g, b, then the next chunk's staged adt, gamma, beta (64 floats each)
-  static constexpr uint32_t BAR = SCAL + 9 * 64 * 4;      // mbarriers: loads, MMA1, MMA3, MMA2 + MMA4
+  // per chunk parity [c | ec | w | wg | wb | g | b] (64 floats each), then the next chunk's staged
+  // adt, gamma, beta
+  static constexpr uint32_t BAR = SCAL + (2 * 448 + 192) * 4;  // mbarriers: loads, MMA1, MMA3, MMA2 + MMA4
   static constexpr uint32_t MISC = BAR + 4 * 8;           // tmem base, first ticket, chain result, next ticket
   static constexpr uint32_t TOTAL = MISC + 16;
   static constexpr uint32_t ALLOC = TOTAL + 1024;         // slack to align the base to 1024
   static constexpr uint32_t LOAD_BYTES = QB * 8192 * 3 + 2 * 8192;
-  static constexpr int CTAS_PER_SM = NS == 128 ? 3 : 4;   // shared memory: 68 KB / 52 KB per CTA
+  static constexpr int CTAS_PER_SM = NS == 128 ? 3 : 4;   // shared memory: 70 KB / 54 KB per CTA
   static constexpr int THREADS = NS == 128 ? 256 : 128;   // registers: 80 / 128 per thread
   static constexpr int WPS = THREADS / 128;               // warps per TMEM sub-partition
 };
@@ -101,15 +102,38 @@ __device__ __forceinline__ void stage_row16(unsigned char* tile, int r, int c0, 
                    pack_bf16(v[8 * qd + 4], v[8 * qd + 5]), pack_bf16(v[8 * qd + 6], v[8 * qd + 7]));
 }
 
+// Two warps (token s = 0-63 per thread): the in-chunk cumulative sum c of adt and the per-token
+// weights of one chunk, from its staged [adt | gamma | beta], into sc = [c | ec | w | wg wb | g | b]
+// (mamba3.py:40).  The two warps meet at named barrier 2.
+__device__ __forceinline__ void chunk_scalars(float* sc, const float* nx, int s, int lane) {
+  const float gm = nx[64 + s], bt = nx[128 + s];
+  float c = warp_incl_scan(nx[s], lane);
+  if (s == 31) sc[31] = c;
+  asm volatile("bar.sync 2, 64;" ::: "memory");
+  if (s >= 32) c += sc[31];
+  if (s != 31) sc[s] = c;
+  asm volatile("bar.sync 2, 64;" ::: "memory");
+  const float w = expf(sc[63] - c);
+  sc[64 + s] = expf(c);
+  sc[128 + s] = w;
+  sc[192 + s] = w * gm;
+  sc[256 + s] = w * bt;
+  sc[320 + s] = gm;
+  sc[384 + s] = bt;
+}
+
 // Loads of one chunk's operands (Q, K | Kp, X | Xp), completing on one mbarrier.
+// K | Kp block qb (n in [64 qb, 64 qb + 64))
+__device__ __forceinline__ void fwd_load_kk_block(const TcFwdParams& p, unsigned char* sKK, uint64_t* bar, const UnitIdx& u,
+                                                  int qb) {
+  const int t0 = u.chunk * kL;
+  umma::tma_load_4d(sKK + qb * 16384, &p.tk, bar, qb * 64, u.g, t0, u.b);
+  umma::tma_load_4d(sKK + qb * 16384 + 8192, &p.tkp, bar, qb * 64, u.g, t0 - p.shift, u.b);
+}
 template <int NS>
 __device__ __forceinline__ void fwd_load_kk(const TcFwdParams& p, unsigned char* sKK, uint64_t* bar, const UnitIdx& u) {
-  const int t0 = u.chunk * kL;
 #pragma unroll
-  for (int qb = 0; qb < NS / 64; ++qb) {
-    umma::tma_load_4d(sKK + qb * 16384, &p.tk, bar, qb * 64, u.g, t0, u.b);
-    umma::tma_load_4d(sKK + qb * 16384 + 8192, &p.tkp, bar, qb * 64, u.g, t0 - p.shift, u.b);
-  }
+  for (int qb = 0; qb < NS / 64; ++qb) fwd_load_kk_block(p, sKK, bar, u, qb);
 }
 __device__ __forceinline__ void fwd_load_x(const TcFwdParams& p, unsigned char* sX, unsigned char* sXp, uint64_t* bar,
                                            const UnitIdx& u) {
@@ -132,15 +156,17 @@ __device__ __forceinline__ void fwd_prefetch_scalars(const TcFwdParams& p, const
 
 // Persistent: CTAS_PER_SM CTAs per SM walk the chunks in ticket order (chunk-major).  Each CTA
 // takes its tickets in increasing order and a chunk only waits on a lower ticket, so the lowest
-// unfinished ticket always belongs to a CTA that can run it.  A CTA loads the next chunk's operands
-// once the current chunk's tiles have left shared memory; the other CTAs on the SM cover the wait.
-// Warp w reads TMEM sub-partition w % 4; with two warps per sub-partition, w / 4 picks half the
-// columns of each epilogue.
+// unfinished ticket always belongs to a CTA that can run it.  The next chunk's operands load as
+// the current chunk's tiles free (Q and K | Kp block 0 after MMA4, the rest once the y tile and
+// the saved state have left shared memory), and warps 0-1 prepare the next chunk's scalars at the
+// end of the current one.  Warp w reads TMEM sub-partition w % 4; with 8 warps (N = 128) the
+// epilogues split their columns by w / 4.  Thread 0 issues the MMAs; the last warp's lane 0 issues
+// the TMA and bulk copies.
 template <int NS>
 __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM)
     ssd_fwd_tc_kernel(const __grid_constant__ TcFwdParams p) {
   using S = FwdSmem<NS>;
-  constexpr int QB = S::QB, WPS = S::WPS;
+  constexpr int QB = S::QB, WPS = S::WPS, ISS = S::THREADS - 32;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* sQ = sm + S::Q;
@@ -150,13 +176,8 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
   unsigned char* sXp = sm + S::XX + 8192;
   unsigned char* sY = sm + S::XX;    // y tile, over X once MMA2 and MMA4 are done
   unsigned char* sSin = sm + S::SIN;
-  float* s_c = reinterpret_cast<float*>(sm + S::SCAL);
-  float* s_ec = s_c + 64;
-  float* s_wg = s_c + 128;
-  float* s_wb = s_c + 192;
-  float* s_g = s_c + 256;
-  float* s_b = s_c + 320;
-  float* s_nx = s_c + 384;  // next chunk's [adt | gamma | beta]
+  float* s_scal = reinterpret_cast<float*>(sm + S::SCAL);  // [2 parity][c | ec | w | wg | wb | g | b]
+  float* s_nx = s_scal + 2 * 448;                            // next chunk's [adt | gamma | beta]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::BAR);
   uint32_t* misc = reinterpret_cast<uint32_t*>(sm + S::MISC);
 
@@ -182,13 +203,17 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
   uint32_t cur = misc[1];
   if (cur < total) {
     const UnitIdx u0 = decode_ticket(cur, p.B, p.H, p.G);
-    if (tid == 0) {
+    if (tid == ISS) {
       umma::mbar_arrive_expect_tx(&bars[0], S::LOAD_BYTES);
       fwd_load_q<NS>(p, sQ, &bars[0], u0);
       fwd_load_kk<NS>(p, sKK, &bars[0], u0);
       fwd_load_x(p, sX, sXp, &bars[0], u0);
     }
-    if (tid < 64) fwd_prefetch_scalars(p, u0, tid, s_nx);
+    if (tid < 64) {
+      fwd_prefetch_scalars(p, u0, tid, s_nx);
+      umma::cp_async_wait_all();
+      chunk_scalars(s_scal, s_nx, tid, lane);
+    }
   }
 
   for (uint32_t it = 0; cur < total; ++it) {
@@ -198,26 +223,15 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
     const int64_t bh = u.bh;
     const int t0 = j * kL;
     int* flags = p.flags + bh * (p.nc + 1);
-    uint32_t nx = 0;
-    bool next_loaded = false;
+    uint32_t nx = 0, nxt = 0;
     if (tid == 0) nx = atomicAdd(p.ticket, 1u);  // the next ticket, published to the CTA at the chain
-
-    // per-token scalars and the in-chunk cumulative sum c (mamba3.py:40)
-    if (tid < 64) {
-      umma::cp_async_wait_all();  // this thread's own copies
-      s_g[tid] = s_nx[64 + tid];
-      s_b[tid] = s_nx[128 + tid];
-      s_c[tid] = warp_incl_scan(s_nx[tid], lane);
-    }
-    __syncthreads();
-    if (tid >= 32 && tid < 64) s_c[tid] += s_c[31];
-    __syncthreads();
-    if (tid < 64) {
-      const float c = s_c[tid], w = expf(s_c[63] - c);
-      s_ec[tid] = expf(c);
-      s_wg[tid] = w * s_g[tid];
-      s_wb[tid] = w * s_b[tid];
-    }
+    // this chunk's scalars (mamba3.py:40) were prepared at the end of the previous one
+    const float* s_c = s_scal + par * 448;
+    const float* s_ec = s_c + 64;
+    const float* s_wg = s_c + 192;
+    const float* s_wb = s_c + 256;
+    const float* s_g = s_c + 320;
+    const float* s_b = s_c + 384;
     const bool load_ok = umma::mbar_wait(&bars[0], par, p.status);
     bool ok = __syncthreads_and(load_ok);
     const float a_chunk = expf(s_c[63]);
@@ -238,8 +252,8 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
       }
       ok = __syncthreads_and(umma::mbar_wait(&bars[1], par, p.status));
     }
-    constexpr int NB = 4 / WPS;  // 32-column blocks of S per warp
-    uint32_t pk[NB][8];          // this thread's scores (bf16 pairs) until K|Kp is free
+    constexpr int NPC = 8 / WPS;   // 16-column pieces of S per warp
+    uint32_t pk[NPC / 2][8];       // this warp's Ps values (bf16 pairs) until K|Kp is free
     if (ok) {
       umma::fence_after_sync();
       // MMA1 is done with K|Kp: scale them in place, K rows s by w_s g_s and Kp rows by w_s b_s (for
@@ -275,45 +289,47 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
         }
         umma::mma_commit(&bars[2]);
       }
-      // scores -> registers.  TMEM gives lanes 0-15 of the warp the S row t; lanes 16-31 take over
-      // columns 16-31 of each 32-column block by one shuffle each.  Block k: half k / 2 (0: K with
-      // gamma, 1: Kp with beta), columns 32 (k % 2) of that half.
-      const int t = 16 * sp + (lane & 15);
-      const float ct = s_c[t];
+      // scores -> registers, 16 columns at a time while MMA3 runs.  TMEM gives lane l < 16 of the
+      // warp the S row t = 16 sp + l; it keeps columns 0-7 of the piece and hands columns 8-15 to
+      // lane l + 16 (one shuffle each).  Piece k (of 8): half k / 4 (0: K with gamma, 1: Kp with
+      // beta), columns 16 (k % 4) of that half; warp w takes pieces [NPC (w / 4), NPC (w / 4 + 1)).
+      {
+        const int t = 16 * sp + (lane & 15);
+        const float ct = s_c[t];
 #pragma unroll
-      for (int bi = 0; bi < NB; ++bi) {
-        const int blk = hw * NB + bi, half = blk >> 1, cc = blk & 1;
-        const float* coef = half ? s_b : s_g;
-        float v[32];
-        umma::tmem_ld32(tmem + tlane + blk * 32, v);
+        for (int pi = 0; pi < NPC; ++pi) {
+          const int pc = hw * NPC + pi, half = pc >> 2;
+          const float* coef = half ? s_b : s_g;
+          float v[16];
+          umma::tmem_ld16(tmem + tlane + pc * 16, v);
 #pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          const float r0 = __shfl_xor_sync(0xffffffffu, v[16 + i], 16);
-          const float r1 = __shfl_xor_sync(0xffffffffu, v[17 + i], 16);
-          const int s0 = cc * 32 + (hiL ? 16 : 0) + i;
-          const float a0 = hiL ? r0 : v[i], a1 = hiL ? r1 : v[i + 1];
-          const float v0 = (s0 <= t) ? a0 * coef[s0] * __expf(ct - s_c[s0]) : 0.f;
-          const float v1 = (s0 + 1 <= t) ? a1 * coef[s0 + 1] * __expf(ct - s_c[s0 + 1]) : 0.f;
-          pk[bi][i >> 1] = pack_bf16(v0, v1);
+          for (int i = 0; i < 8; i += 2) {
+            const float r0 = __shfl_xor_sync(0xffffffffu, v[8 + i], 16);
+            const float r1 = __shfl_xor_sync(0xffffffffu, v[9 + i], 16);
+            const int s0 = (pc & 3) * 16 + (hiL ? 8 : 0) + i;
+            const float a0 = hiL ? r0 : v[i], a1 = hiL ? r1 : v[i + 1];
+            const float v0 = (s0 <= t) ? a0 * coef[s0] * __expf(ct - s_c[s0]) : 0.f;
+            const float v1 = (s0 + 1 <= t) ? a1 * coef[s0 + 1] * __expf(ct - s_c[s0 + 1]) : 0.f;
+            pk[pi >> 1][(pi & 1) * 4 + (i >> 1)] = pack_bf16(v0, v1);
+          }
         }
       }
       ok = __syncthreads_and(umma::mbar_wait(&bars[2], par, p.status));  // MMA3 done: K|Kp free
+      if (ok) {
+        // Ps (bf16, K-major [2][64 t][64 s]) over K|Kp block 0: piece k's 8 columns of this lane are
+        // 16-byte chunk 2 (k % 4) + (lane >= 16) of row t in half k / 4
+        const int t = 16 * sp + (lane & 15);
+#pragma unroll
+        for (int pi = 0; pi < NPC; ++pi) {
+          const int pc = hw * NPC + pi;
+          const uint32_t* w = &pk[pi >> 1][(pi & 1) * 4];
+          *reinterpret_cast<uint4*>(sPs + (pc >> 2) * 8192 + umma::sw128_offset(t, 2 * (pc & 3) + (hiL ? 1 : 0))) =
+              make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
     }
     if (ok) {
       umma::fence_after_sync();
-      // Ps (bf16, K-major [2][64 t][64 s]) over K|Kp block 0
-      {
-        const int t = 16 * sp + (lane & 15);
-#pragma unroll
-        for (int bi = 0; bi < NB; ++bi) {
-          const int blk = hw * NB + bi, half = blk >> 1, cc = blk & 1;
-          const int c0 = cc * 4 + (hiL ? 2 : 0);
-          *reinterpret_cast<uint4*>(sPs + half * 8192 + umma::sw128_offset(t, c0)) =
-              make_uint4(pk[bi][0], pk[bi][1], pk[bi][2], pk[bi][3]);
-          *reinterpret_cast<uint4*>(sPs + half * 8192 + umma::sw128_offset(t, c0 + 1)) =
-              make_uint4(pk[bi][4], pk[bi][5], pk[bi][6], pk[bi][7]);
-        }
-      }
       umma::fence_proxy_async_smem();
       umma::fence_before_sync();
       __syncthreads();
@@ -334,47 +350,69 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
       }
       __syncthreads();
       ok = misc[2] == kFlagReady;
+      nxt = misc[3];
       if (!ok) umma::mbar_wait(&bars[3], par, p.status);
     }
     if (ok) {
       // state hand-off: S_in[j+1] = e^{c_L} S_in[j] + S_loc (mamba3.py:52).  Lanes 16-31 hold the
-      // rows n = 64 h + 16 sp + lane - 16 of S_loc (half h); a warp takes 16 columns p at a time,
-      // (h, p range) pairs split over the warps of a sub-partition.  Ring slots are [p/4][n][4];
-      // the caller's initial and final states are [p][n].  S_in[j] also goes to shared memory in
-      // bf16 (the B operand of MMA4 and the saved state).
+      // rows n = 64 h + 16 sp + lane - 16 of S_loc (half h); blocks of 16 columns p split over the
+      // warps of a sub-partition, and within a block lane l < 16 takes columns 8-15 of lane l + 16's
+      // row (one shuffle each).  A thread's ring loads of a batch of blocks are issued before any of
+      // the batch's stores.
+      // Ring slots are [p/4][n][4]; the caller's initial and final states are [p][n].  S_in[j] also
+      // goes to shared memory in bf16 (the B operand of MMA4 and the saved state).
       const int64_t PN = (int64_t)kP * NS;
       const float4* ring_in = reinterpret_cast<const float4*>(p.ring + (bh * 2 + (j & 1)) * PN);
       float4* ring_out = reinterpret_cast<float4*>(p.ring + (bh * 2 + ((j + 1) & 1)) * PN);
       float* fin = (j == p.nc - 1 && p.fin) ? p.fin + bh * PN : nullptr;
+      const float* init = p.init ? p.init + bh * PN : nullptr;
       constexpr int NP = 4 * QB / WPS;  // (half, 16-column block) pairs per warp
+      constexpr int NBATCH = WPS == 1 ? NP : 2;  // pairs whose ring loads are in flight together
+      const int hs = hiL ? 0 : 1;       // which 8 columns of a block this lane takes
 #pragma unroll
-      for (int pi = 0; pi < NP; ++pi) {
-        const int pair = hw * NP + pi, hf = pair >> 2, pc = pair & 3;
-        const int n = 64 * hf + 16 * sp + (lane - 16);
-        float sl[16];
-        umma::tmem_ld16(tmem + tlane + 64 * hf + 16 * pc, sl);
-        if (hiL) {
-          float sin[16];
+      for (int b0 = 0; b0 < NP; b0 += NBATCH) {
+        float4 rin[NBATCH][2];
+#pragma unroll
+        for (int bi = 0; bi < NBATCH; ++bi) {
+          const int pair = hw * NP + b0 + bi, hf = pair >> 2, pc = pair & 3;
+          const int n = 64 * hf + 16 * sp + (lane & 15), p0 = 16 * pc + 8 * hs;
           if (j == 0) {
+            float iv[8];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) sin[i] = p.init ? __ldcg(p.init + bh * PN + (16 * pc + i) * NS + n) : 0.f;
+            for (int i = 0; i < 8; ++i) iv[i] = init ? __ldcg(init + (p0 + i) * NS + n) : 0.f;
+            rin[bi][0] = make_float4(iv[0], iv[1], iv[2], iv[3]);
+            rin[bi][1] = make_float4(iv[4], iv[5], iv[6], iv[7]);
           } else {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const float4 v = __ldcg(ring_in + (4 * pc + q) * NS + n);
-              sin[4 * q] = v.x; sin[4 * q + 1] = v.y; sin[4 * q + 2] = v.z; sin[4 * q + 3] = v.w;
-            }
+            rin[bi][0] = __ldcg(ring_in + (p0 / 4) * NS + n);
+            rin[bi][1] = __ldcg(ring_in + (p0 / 4 + 1) * NS + n);
           }
+        }
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            ring_out[(4 * pc + q) * NS + n] =
-                make_float4(a_chunk * sin[4 * q] + sl[4 * q], a_chunk * sin[4 * q + 1] + sl[4 * q + 1],
-                            a_chunk * sin[4 * q + 2] + sl[4 * q + 2], a_chunk * sin[4 * q + 3] + sl[4 * q + 3]);
+        for (int bi = 0; bi < NBATCH; ++bi) {
+          const int pair = hw * NP + b0 + bi, hf = pair >> 2, pc = pair & 3;
+          const int n = 64 * hf + 16 * sp + (lane & 15), p0 = 16 * pc + 8 * hs;
+          float sl[16];
+          umma::tmem_ld16(tmem + tlane + 64 * hf + 16 * pc, sl);
+          float mine[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float r = __shfl_xor_sync(0xffffffffu, sl[8 + i], 16);
+            mine[i] = hiL ? sl[i] : r;
+          }
+          const float sin[8] = {rin[bi][0].x, rin[bi][0].y, rin[bi][0].z, rin[bi][0].w,
+                                rin[bi][1].x, rin[bi][1].y, rin[bi][1].z, rin[bi][1].w};
+          float so[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) so[i] = a_chunk * sin[i] + mine[i];
+          ring_out[(p0 / 4) * NS + n] = make_float4(so[0], so[1], so[2], so[3]);
+          ring_out[(p0 / 4 + 1) * NS + n] = make_float4(so[4], so[5], so[6], so[7]);
           if (fin) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) fin[(16 * pc + i) * NS + n] = a_chunk * sin[i] + sl[i];
+            for (int i = 0; i < 8; ++i) fin[(p0 + i) * NS + n] = so[i];
           }
-          stage_row16(sSin, n, 2 * pc, sin);
+          *reinterpret_cast<uint4*>(sSin + umma::sw128_offset(n, p0 / 8)) =
+              make_uint4(pack_bf16(sin[0], sin[1]), pack_bf16(sin[2], sin[3]), pack_bf16(sin[4], sin[5]),
+                         pack_bf16(sin[6], sin[7]));
         }
       }
       // the barrier orders every thread's ring writes before thread 0's release (cumulative)
@@ -383,15 +421,14 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
       umma::fence_proxy_async_smem();
       umma::fence_before_sync();
       __syncthreads();
-      const uint32_t nxt = misc[3];
+      if (tid == ISS && p.states) {
+        // the saved state is the shared-memory image itself (bf16, 128-byte swizzle), so the
+        // backward can bulk-copy it back into place
+        umma::bulk_store(reinterpret_cast<unsigned char*>(p.states) + (bh * p.nc + j) * (int64_t)NS * 128, sSin,
+                         NS * 128);
+        umma::bulk_commit();
+      }
       if (tid == 0) {
-        if (p.states) {
-          // the saved state is the shared-memory image itself (bf16, 128-byte swizzle), so the
-          // backward can bulk-copy it back into place
-          umma::bulk_store(reinterpret_cast<unsigned char*>(p.states) + (bh * p.nc + j) * (int64_t)NS * 128, sSin,
-                           NS * 128);
-          umma::bulk_commit();
-        }
         umma::fence_after_sync();
         // MMA4: Ye = Q S_in^T into lanes 0-15, cols 64-127
         const uint32_t q0 = umma::smem_u32(sQ), sin0 = umma::smem_u32(sSin);
@@ -411,6 +448,14 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
     }
     if (ok) {
       umma::fence_after_sync();
+      // MMA2 and MMA4 are done with Q and with Ps (K|Kp block 0): the next chunk's Q and first K|Kp
+      // block start loading
+      const UnitIdx nu = decode_ticket(nxt < total ? nxt : 0, p.B, p.H, p.G);
+      if (tid == ISS && nxt < total) {
+        umma::mbar_arrive_expect_tx(&bars[0], S::LOAD_BYTES);
+        fwd_load_q<NS>(p, sQ, &bars[0], nu);
+        fwd_load_kk_block(p, sKK, &bars[0], nu, 0);
+      }
       // y = Yi + e^{c_t} Ye (mamba3.py:55): lanes 0-15 hold row t = 16 sp + lane; 16 columns at a
       // time, staged as a bf16 tile over X
       const int t = 16 * sp + (lane & 15);
@@ -429,35 +474,36 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
       umma::fence_proxy_async_smem();
       umma::fence_before_sync();
       __syncthreads();
-      if (tid == 0) {
+      if (tid == ISS) {
         umma::tma_store_4d(&p.ty, sY, 0, u.h, t0, u.b);
         umma::bulk_commit();
-        // the y tile and the saved state leave shared memory, then the next chunk's operands load
+        // the y tile and the saved state leave shared memory, then the rest of the operands load
         umma::bulk_wait_read();
-        if (nx < total) {
-          const UnitIdx nu = decode_ticket(nx, p.B, p.H, p.G);
-          umma::mbar_arrive_expect_tx(&bars[0], S::LOAD_BYTES);
-          fwd_load_q<NS>(p, sQ, &bars[0], nu);
-          fwd_load_kk<NS>(p, sKK, &bars[0], nu);
+        if (nxt < total) {
+#pragma unroll
+          for (int qb = 1; qb < QB; ++qb) fwd_load_kk_block(p, sKK, &bars[0], nu, qb);
           fwd_load_x(p, sX, sXp, &bars[0], nu);
-          next_loaded = true;
         }
+      }
+      if (tid < 64 && nxt < total) {  // the next chunk's scalars
+        umma::cp_async_wait_all();
+        chunk_scalars(s_scal + (par ^ 1) * 448, s_nx, tid, lane);
       }
     }
     umma::fence_before_sync();
-    __syncthreads();  // every read of this chunk's tiles and TMEM columns is done
+    __syncthreads();  // every read of this chunk's tiles, scalars and TMEM columns is done
     if (!ok) {
       // leave after an error: the ticket already taken is aborted (its loads were never issued)
-      if (tid == 0 && nx < total && !next_loaded) {
+      if (tid == 0 && nx < total) {
         const UnitIdx cn = decode_ticket(nx, p.B, p.H, p.G);
         st_release(&p.flags[cn.bh * (p.nc + 1) + cn.chunk + 1], kFlagAbort);
       }
       break;
     }
     umma::fence_after_sync();
-    cur = misc[3];
+    cur = nxt;
   }
-  if (tid == 0) umma::bulk_wait_all();  // staged tiles must be read out before exit
+  if (tid == ISS) umma::bulk_wait_all();  // staged tiles must be read out before exit
   if (tid < 64) umma::cp_async_wait_all();
   umma::fence_before_sync();
   __syncthreads();
@@ -630,26 +676,6 @@ __device__ __forceinline__ void bwd_prefetch_scalars(const TcBwdParams& p, const
   umma::cp_async_commit();
 }
 
-// Two warps (token s = 0-63 per thread): the in-chunk cumulative sum c of adt and the per-token
-// weights of one chunk, from its staged [adt | gamma | beta], into sc = [c | ec | w | wg wb | g | b]
-// (mamba3.py:40).  The two warps meet at named barrier 2.
-__device__ __forceinline__ void bwd_chunk_scalars(float* sc, const float* nx, int s, int lane) {
-  const float gm = nx[64 + s], bt = nx[128 + s];
-  float c = warp_incl_scan(nx[s], lane);
-  if (s == 31) sc[31] = c;
-  asm volatile("bar.sync 2, 64;" ::: "memory");
-  if (s >= 32) c += sc[31];
-  if (s != 31) sc[s] = c;
-  asm volatile("bar.sync 2, 64;" ::: "memory");
-  const float w = expf(sc[63] - c);
-  sc[64 + s] = expf(c);
-  sc[128 + s] = w;
-  sc[192 + s] = w * gm;
-  sc[256 + s] = w * bt;
-  sc[320 + s] = gm;
-  sc[384 + s] = bt;
-}
-
 template <int NS>
 __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid_constant__ TcBwdParams p) {
   using S = BwdSmem<NS>;
@@ -698,7 +724,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
     if (scal_warp) {
       bwd_prefetch_scalars(p, bwd_chunk(p, cur), tid - 64, s_nx);
       umma::cp_async_wait_all();
-      bwd_chunk_scalars(s_scal, s_nx, tid - 64, lane);
+      chunk_scalars(s_scal, s_nx, tid - 64, lane);
     }
   }
 
@@ -1100,7 +1126,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
         p.dbeta[b * p.dbsb + (int64_t)tt * p.dbst + h * p.dbsh] = db;
       } else if (scal_warp && nxt < total) {
         umma::cp_async_wait_all();  // this thread's own copies
-        bwd_chunk_scalars(s_scal + ((it + 1) & 1) * 448, s_nx, tid - 64, lane);
+        chunk_scalars(s_scal + ((it + 1) & 1) * 448, s_nx, tid - 64, lane);
       }
     }
     __syncthreads();  // every read of this stage and of the work tiles is done
