@@ -676,6 +676,47 @@ __device__ __forceinline__ void bwd_prefetch_scalars(const TcBwdParams& p, const
   umma::cp_async_commit();
 }
 
+// The per-token scalars of a finished chunk (64 threads, s = 0-63 per thread, named barrier 1):
+// dgamma, dbeta and dadt_u = sum_{t >= u} dc_t from the chunk's reductions in shared memory.
+// sc: the chunk's [c | ec | w | wg wb | g | b]; wsel: which of the two warps this is.
+__device__ __forceinline__ void bwd_token_tail(const TcBwdParams& p, const float* sc, const float* s_da, const float* s_xu,
+                                               const float* s_pre, const float* s_dcint, float* s_tmp, int s, int lane,
+                                               int wsel, float a_chunk, int b, int h, int t0) {
+  const float* s_w = sc + 128;
+  const float* s_g = sc + 320;
+  const float* s_b = sc + 384;
+  float da = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) da += s_da[i];
+  float xu = 0.f, xpu = 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    xu += s_xu[q * 128 + s];
+    xpu += s_xu[q * 128 + 64 + s];
+  }
+  const float w = s_w[s];
+  const float dw = s_g[s] * xu + s_b[s] * xpu;
+  const float dg = s_pre[64 + s] + w * xu;
+  const float db = s_pre[128 + s] + w * xpu;
+  float dc = s_pre[s] + s_dcint[s] + s_dcint[64 + s] - w * dw;
+  // dc_{L-1} += e^{c_L} da + sum_s w_s dw_s   (two warps: combine through shared memory)
+  const float wdw = warp_sum(w * dw);
+  if (lane == 0) s_tmp[wsel] = wdw;
+  asm volatile("bar.sync 1, 64;" ::: "memory");
+  if (s == 63) dc += a_chunk * da + s_tmp[0] + s_tmp[1];
+  // dadt_u = sum_{t >= u} dc_t  (reverse cumulative sum over 64 tokens in two warps)
+  const float total = warp_sum(dc);
+  const float incl = warp_incl_scan(dc, lane);
+  float suffix = total - incl + dc;
+  if (lane == 0 && wsel == 1) s_tmp[2] = total;
+  asm volatile("bar.sync 1, 64;" ::: "memory");
+  if (wsel == 0) suffix += s_tmp[2];
+  const int tt = t0 + s;
+  p.dadt[b * p.dasb + (int64_t)tt * p.dast + h * p.dash] = suffix;
+  p.dgamma[b * p.dgsb + (int64_t)tt * p.dgst + h * p.dgsh] = dg;
+  p.dbeta[b * p.dbsb + (int64_t)tt * p.dbst + h * p.dbsh] = db;
+}
+
 template <int NS>
 __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid_constant__ TcBwdParams p) {
   using S = BwdSmem<NS>;
@@ -728,6 +769,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
     }
   }
 
+  // the previous chunk's per-token scalars, written during this chunk's first MMA group
+  bool pend = false;
+  int pend_b = 0, pend_h = 0, pend_t0 = 0;
+  uint32_t pend_par = 0;
+  float pend_a = 0.f;
+  const bool tail_warp = warp >= 14;
   for (uint32_t it = 0; cur < total; ++it) {
     const int stage = it & 1;
     const uint32_t par = it & 1;  // parity of this chunk's MMA-group barriers
@@ -808,6 +855,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
                          ks > 0);
         umma::mma_commit(&bars[2]);
       }
+      if (pend && tail_warp)
+        bwd_token_tail(p, s_scal + pend_par * 448, s_da, s_xu, s_pre, s_dcint, s_tmp, tid - 448, lane, warp - 14, pend_a,
+                       pend_b, pend_h, pend_t0);
+      pend = false;
       ok = __syncthreads_and(umma::mbar_wait(&bars[2], par, p.status));
     }
     if (ok) {
@@ -1091,40 +1142,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
         umma::tma_store_4d(&p.tdxp, st_dxp, 0, h, t0, b);
         umma::bulk_commit();
       }
-      // per-token scalars: warps 0-1 own tokens 0-63; warps 2-3 prepare the next chunk's scalars
-      if (tid < 64) {
-        const int s = tid;
-        float da = 0.f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) da += s_da[i];
-        float xu = 0.f, xpu = 0.f;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          xu += s_xu[q * 128 + s];
-          xpu += s_xu[q * 128 + 64 + s];
-        }
-        const float w = s_w[s];
-        const float dw = s_g[s] * xu + s_b[s] * xpu;
-        const float dg = s_pre[64 + s] + w * xu;
-        const float db = s_pre[128 + s] + w * xpu;
-        float dc = s_pre[s] + s_dcint[s] + s_dcint[64 + s] - w * dw;
-        // dc_{L-1} += e^{c_L} da + sum_s w_s dw_s   (two warps: combine through shared memory)
-        const float wdw = warp_sum(w * dw);
-        if (lane == 0) s_tmp[warp] = wdw;
-        asm volatile("bar.sync 1, 64;" ::: "memory");
-        if (s == 63) dc += a_chunk * da + s_tmp[0] + s_tmp[1];
-        // dadt_u = sum_{t >= u} dc_t  (reverse cumulative sum over 64 tokens in two warps)
-        const float total = warp_sum(dc);
-        const float incl = warp_incl_scan(dc, lane);
-        float suffix = total - incl + dc;
-        if (lane == 0 && warp == 1) s_tmp[2] = total;
-        asm volatile("bar.sync 1, 64;" ::: "memory");
-        if (warp == 0) suffix += s_tmp[2];
-        const int tt = t0 + s;
-        p.dadt[b * p.dasb + (int64_t)tt * p.dast + h * p.dash] = suffix;
-        p.dgamma[b * p.dgsb + (int64_t)tt * p.dgst + h * p.dgsh] = dg;
-        p.dbeta[b * p.dbsb + (int64_t)tt * p.dbst + h * p.dbsh] = db;
-      } else if (scal_warp && nxt < total) {
+      // this chunk's per-token scalars are written by warps 14-15 while the next chunk's first MMA
+      // group runs (or after the loop); warps 2-3 prepare the next chunk's scalars
+      pend = true;
+      pend_b = b;
+      pend_h = h;
+      pend_t0 = t0;
+      pend_par = it & 1;
+      pend_a = a_chunk;
+      if (scal_warp && nxt < total) {
         umma::cp_async_wait_all();  // this thread's own copies
         chunk_scalars(s_scal + ((it + 1) & 1) * 448, s_nx, tid - 64, lane);
       }
@@ -1141,6 +1167,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
     }
     cur = nxt;
   }
+  if (pend && tail_warp)  // the last chunk's per-token scalars
+    bwd_token_tail(p, s_scal + pend_par * 448, s_da, s_xu, s_pre, s_dcint, s_tmp, tid - 448, lane, warp - 14, pend_a,
+                   pend_b, pend_h, pend_t0);
   if (tid == 32) umma::bulk_wait_all();  // staged output tiles must be read out before exit
   if (scal_warp) umma::cp_async_wait_all();
   umma::fence_before_sync();
