@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--replicate", action="store_true",
                     help="N > 1: every rank runs a whole job of its own (weak scaling) instead of 1/N of one job")
     ap.add_argument("--eager", action="store_true", help="time eager launches instead of CUDA-graph replays")
+    ap.add_argument("--dtype", choices=("bf16", "fp32"), default="bf16",
+                    help="vector dtype (fp32: the drop-in's fp32 path, Mamba3.forward without autocast)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
     return ap.parse_args()
@@ -74,18 +76,25 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def flop_roofline(shape, th, dom, dms, fwd_only):
+FP32_FMA_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # nominal B200 CUDA-core fp32: SMs x lanes x FMA x max clock
+
+
+def flop_roofline(shape, th, dom, dms, fwd_only, dtype="bf16"):
     """The flop side of the dominant kernel: algorithmic flops per token-head (forward
     4 L N / r + 4 L P + 6 N P, backward twice that) over its time, against the measured
-    burst bf16 tensor peak."""
+    burst bf16 tensor peak (bf16, tensor-core kernels) or the nominal fp32 FMA peak (fp32, SIMT)."""
     L, r = 64, shape.H // shape.G
     f = 4 * L * shape.N // r + 4 * L * shape.P + 6 * shape.N * shape.P
     flops = (f if dom == "fwd" else 2 * f) * th
-    p = ROOT / "MEASURED_PEAKS.json"
-    peak = float(json.loads(p.read_text())["bf16_tflops"]) if p.exists() else 1590.0
+    if dtype == "fp32":
+        peak, kind = FP32_FMA_TFLOPS, "nominal fp32 FMA (CUDA cores)"
+    else:
+        p = ROOT / "MEASURED_PEAKS.json"
+        peak, kind = ((float(json.loads(p.read_text())["bf16_tflops"]), "measured bf16 tensor") if p.exists()
+                      else (1590.0, "fallback bf16 tensor"))
     achieved = flops / (dms / 1e3) / 1e12
-    return {"kernel": "ssd_" + dom, "achieved_tflops": achieved, "peak_tflops": peak, "frac": achieved / peak,
-            "flops_per_launch": flops, "internal_chunk": 64}
+    return {"kernel": "ssd_" + dom, "achieved_tflops": achieved, "peak_tflops": peak, "peak_kind": kind,
+            "frac": achieved / peak, "flops_per_launch": flops, "algorithmic_chunk": L}
 
 
 def traffic_from_profile(kernel: str):
@@ -181,9 +190,11 @@ def make_device_inputs(shape, rank, dev):
 
 
 def cpu_reference_sample(shape, seconds: float, max_reps: int | None = None, fwd_only: bool = False):
-    """Time the reference algorithm (CPU restatement of zenith/mamba3.py:30-56, fp32, autograd)
-    on a one-sequence slice of the workload; returns (tokens/s, cores, reps, sample string)."""
-    from oracle.ssd_oracle import ssd_forward
+    """Time the reference algorithm on the host CPU: zenith/mamba3.py:30-56 restated with the
+    reference's own sequence of tensor operations (oracle/ssd_reference_ops.py), fp32, forward plus
+    PyTorch autograd backward, on a one-sequence slice of the workload; returns (tokens/s, cores,
+    reps, sample string)."""
+    from oracle.ssd_reference_ops import ssd_reference_ops
     from zenith_b200.synthetic import SsdShape, make_inputs
 
     cores = len(os.sched_getaffinity(0))
@@ -192,15 +203,18 @@ def cpu_reference_sample(shape, seconds: float, max_reps: int | None = None, fwd
     # so tokens/s of a slice stands for the whole sequence)
     sl = SsdShape(1, min(shape.T, 8192), shape.H, shape.P, shape.N, shape.G, shape.chunk)
     inp = make_inputs(sl, seed=0)
+    if sl.G != sl.H:  # the reference has one q/k per head: grouped q/k/kp are expanded to the heads
+        for n in ("q", "k", "kp"):
+            inp[n] = inp[n].repeat_interleave(sl.H // sl.G, dim=2)
     leaves = [(inp[n].to(torch.bfloat16).float() if n in VEC else inp[n]).requires_grad_() for n in NAMES]
     dy = inp["dy"].to(torch.bfloat16).float()
 
     def once():
         if fwd_only:
             with torch.no_grad():
-                ssd_forward(*leaves, sl.chunk, dtype=torch.float32)
+                ssd_reference_ops(*leaves, sl.chunk)
             return
-        y, _, _ = ssd_forward(*leaves, sl.chunk, dtype=torch.float32)
+        y = ssd_reference_ops(*leaves, sl.chunk)
         y.backward(dy)
         for t in leaves:
             t.grad = None
@@ -214,9 +228,10 @@ def cpu_reference_sample(shape, seconds: float, max_reps: int | None = None, fwd
         if el >= seconds or (max_reps is not None and reps >= max_reps):
             break
     tok_s = reps * sl.B * sl.T / el
-    what = "forward" if fwd_only else "fp32 + autograd"
-    sample = (f"reference algorithm {what} on host CPU, 1 sequence (T{sl.T} H{sl.H} P{sl.P} N{sl.N} G{sl.G} "
-              f"chunk {sl.chunk}) of the B{shape.B} workload, {reps} reps in {el:.1f} s, {cores} threads")
+    what = "forward" if fwd_only else "fp32 forward + autograd backward"
+    sample = (f"reference ssd (zenith/mamba3.py:30-56, its tensor-op sequence restated) {what} on host CPU, "
+              f"1 sequence (T{sl.T} H{sl.H} P{sl.P} N{sl.N} G{sl.G} chunk {sl.chunk}) of the B{shape.B} workload, "
+              f"{reps} reps in {el:.1f} s, {cores} threads")
     return tok_s, cores, reps, sample
 
 
@@ -304,10 +319,11 @@ def run_ours(args):
         r = shape.H // shape.G
         sl_g = sl_h if sl_h == slice(None) else slice(sl_h.start // r, sl_h.stop // r)
         part = {n: (v[sl_b, :, sl_g] if n in ("q", "k", "kp") else v[sl_b, :, sl_h]) for n, v in full.items() if n != "D"}
-    inp = {n: (t.to(torch.bfloat16) if (n in VEC or n == "dy") else t).to(dev).contiguous() for n, t in part.items()}
+    vdt = torch.float32 if args.dtype == "fp32" else torch.bfloat16
+    inp = {n: (t.to(vdt) if (n in VEC or n == "dy") else t).to(dev).contiguous() for n, t in part.items()}
     del full, part
     chunk = shape.chunk
-    fwd_b, bwd_b = algorithmic_bytes(shape)
+    fwd_b, bwd_b = algorithmic_bytes(shape, e_in=vdt.itemsize)
     if fwd_only:
         bwd_b = 0
     th = local_shape.B * local_shape.T * local_shape.H
@@ -536,9 +552,10 @@ def run_ours(args):
         "metric": METRIC_FWD if fwd_only else METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "weak" if replicate else "strong",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "vs_baseline": None, "dtype": args.dtype, "data": "synthetic",
         "config": {"workload": shape.name, "B": shape.B, "T": shape.T, "H": shape.H, "P": shape.P,
-                   "N": shape.N, "G": shape.G, "chunk": shape.chunk, "vector_dtype": "bf16", "scalar_dtype": "fp32",
+                   "N": shape.N, "G": shape.G, "chunk": shape.chunk, "vector_dtype": args.dtype, "scalar_dtype": "fp32",
+                   "kernels": "SIMT (fp32 FMA)" if args.dtype == "fp32" else "tensor-core (tcgen05)",
                    "parallelism": par, "B_per_rank": local_shape.B, "H_per_rank": local_shape.H,
                    "tokens_per_rank": local_shape.B * local_shape.T,
                    "timed_launch": "eager" if (cp or args.eager) else "CUDA graph of one step, replayed",
@@ -546,11 +563,11 @@ def run_ours(args):
                           f"{n_sets} rotating input set(s) so each step starts from HBM")},
         "roofline": {"bound": "hbm", "kernel": dname, "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
-                     "traffic": traffic_from_profile(dname) if args.workload == "layer" else None,
+                     "traffic": traffic_from_profile(dname) if args.workload == "layer" and args.dtype == "bf16" else None,
                      "algorithmic_bytes_per_launch": dbytes, "launch_ms": dms},
         "step_roofline": {"achieved_gbs": step_gbs, "frac": step_gbs / peak,
                           "algorithmic_bytes_per_token_head": fwd_b + bwd_b, "fwd_ms": fwd_ms, "bwd_ms": bwd_ms},
-        "flop_roofline": flop_roofline(shape, th, dom, dms, fwd_only),
+        "flop_roofline": flop_roofline(shape, th, dom, dms, fwd_only, args.dtype),
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
         "clocks": clocks,

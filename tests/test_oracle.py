@@ -145,3 +145,23 @@ def test_recurrence_oracle_matches_chunked_oracle_with_states_and_groups():
     ref = ssd_backward(dy, *args, 8, initial_state=s0, dfinal=dfin)
     for n in NAMES + ("initial_state",):
         assert max_rel_err(got["d" + n], ref["d" + n]) < 1e-11, n
+
+
+# ------------------------------------------------------------------------------------------------
+# the CPU baseline's restatement of the reference's operation sequence (oracle/ssd_reference_ops.py)
+
+from oracle.ssd_reference_ops import ssd_reference_ops  # noqa: E402
+
+
+@pytest.mark.parametrize("case", [c for c in CASES if not c.startswith("groups")])
+def test_reference_ops_restatement_matches_reference_golden(case):
+    """Forward and autograd backward of the restatement the benchmark's CPU baseline times, against
+    the reference's own ssd (goldens); one q/k group per head, as in the reference."""
+    inp, out, L = load(case)
+    leaves = [inp[n].clone().requires_grad_() for n in NAMES]
+    y = ssd_reference_ops(*leaves, L)
+    y.backward(inp["dy"])
+    tol = 1e-11 if out["y"].dtype == torch.float64 else 1e-6
+    assert max_rel_err(y, out["y"]) < tol
+    for n, t in zip(NAMES, leaves):
+        assert max_rel_err(t.grad, out["d" + n]) < tol, n
