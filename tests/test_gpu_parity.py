@@ -202,6 +202,18 @@ def test_long_sequences_with_few_heads_match_oracle(shape):
     assert max_rel_err(dinit, ref["dinitial_state"]) < TOL[torch.bfloat16]
 
 
+@pytest.mark.parametrize("adt_range", [(-1.0, 0.0), (-12.0, -5.0), (-0.2, 0.1)], ids=["mild", "steep", "mixed-sign"])
+def test_tensor_core_decay_paths_match_oracle(adt_range):
+    """The tensor-core kernels factorise the decay mask per 8-token block when every adt of a chunk
+    lies in [-8, 0], and take a per-element exponential otherwise: chunks of either kind (steep
+    decays beyond -8, positive adt) against the oracle, forward and all eight gradients."""
+    s = SsdShape(2, 256, 4, 64, 128, 4, 64)
+    inp = _cast(make_inputs(s, seed=41), torch.bfloat16, torch.float32)
+    lo, hi = adt_range
+    inp["adt"] = lo + (hi - lo) * torch.rand(s.B, s.T, s.H, generator=torch.Generator().manual_seed(3))
+    compare(run_cuda(inp, s.chunk), oracle(inp, s.chunk), TOL[torch.bfloat16])
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_runs_are_bitwise_deterministic(dtype):
     inp = _cast(make_inputs(SsdShape(2, 256, 4, 64, 128, 4, 64), seed=9), dtype, torch.float32)

@@ -31,6 +31,17 @@ namespace {
 constexpr int kL = 64;  // internal chunk length
 constexpr int kP = 64;
 
+// Per-chunk scalar block in shared memory (floats): [c | ec | w | wg | wb | g | b | es] (64 each),
+// then at kScalFast a flag: 1 when every adt of the chunk lies in [-8, 0].  es_s = e^{c_r - c_s}
+// with r the first token of s's 8-token block, so that the decay e^{c_t - c_s} = e^{c_t - c_r} es_s
+// (t >= s) costs one exponential per (row, block) instead of one per element.  Under the flag c
+// does not increase, so e^{c_t - c_r} <= 1 and 1 <= es_s <= e^{56}; where e^{c_t - c_r} underflows
+// (below 1e-38) the true decay is below 1e-38 e^{56} ~ 2e-14, negligible beside the O(1) entries.
+// Other chunks use the per-element exponential.
+constexpr int kScal = 576;
+constexpr int kScalEs = 448;
+constexpr int kScalFast = 514;
+
 // Shared memory of the forward.  After MMA3 the K|Kp block 0 holds the scores Ps [2][64 t][64 s]
 // and (N = 128) block 1 the S_in image; after MMA4 the X tile holds the y tile.
 template <int NS>
@@ -43,7 +54,7 @@ struct FwdSmem {
   static constexpr uint32_t SCAL = NS == 128 ? XX + 16384 : SIN + NS * 128;
   // per chunk parity [c | ec | w | wg | wb | g | b] (64 floats each), then the next chunk's staged
   // adt, gamma, beta
-  static constexpr uint32_t BAR = SCAL + (2 * 448 + 192) * 4;  // mbarriers: loads, MMA1, MMA3, MMA2 + MMA4
+  static constexpr uint32_t BAR = SCAL + (2 * kScal + 192) * 4;  // mbarriers: loads, MMA1, MMA3, MMA2 + MMA4
   static constexpr uint32_t MISC = BAR + 4 * 8;           // tmem base, first ticket, chain result, next ticket
   static constexpr uint32_t TOTAL = MISC + 16;
   static constexpr uint32_t ALLOC = TOTAL + 1024;         // slack to align the base to 1024
@@ -102,13 +113,16 @@ __device__ __forceinline__ void stage_row16(unsigned char* tile, int r, int c0, 
                    pack_bf16(v[8 * qd + 4], v[8 * qd + 5]), pack_bf16(v[8 * qd + 6], v[8 * qd + 7]));
 }
 
+
 // Two warps (token s = 0-63 per thread): the in-chunk cumulative sum c of adt and the per-token
-// weights of one chunk, from its staged [adt | gamma | beta], into sc = [c | ec | w | wg wb | g | b]
+// weights of one chunk, from its staged [adt | gamma | beta], into the scalar block sc
 // (mamba3.py:40).  The two warps meet at named barrier 2.
 __device__ __forceinline__ void chunk_scalars(float* sc, const float* nx, int s, int lane) {
-  const float gm = nx[64 + s], bt = nx[128 + s];
-  float c = warp_incl_scan(nx[s], lane);
+  const float a = nx[s], gm = nx[64 + s], bt = nx[128 + s];
+  float c = warp_incl_scan(a, lane);
+  const bool pos = __any_sync(0xffffffffu, !(a <= 0.f && a >= -8.f));  // outside [-8, 0] (or NaN)
   if (s == 31) sc[31] = c;
+  if (lane == 0) sc[512 + (s >> 5)] = pos ? 1.f : 0.f;
   asm volatile("bar.sync 2, 64;" ::: "memory");
   if (s >= 32) c += sc[31];
   if (s != 31) sc[s] = c;
@@ -120,6 +134,8 @@ __device__ __forceinline__ void chunk_scalars(float* sc, const float* nx, int s,
   sc[256 + s] = w * bt;
   sc[320 + s] = gm;
   sc[384 + s] = bt;
+  sc[kScalEs + s] = expf(sc[s & ~7] - c);
+  if (s == 0) sc[kScalFast] = (sc[512] + sc[513] > 0.f) ? 0.f : 1.f;
 }
 
 // Loads of one chunk's operands (Q, K | Kp, X | Xp), completing on one mbarrier.
@@ -177,7 +193,7 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
   unsigned char* sY = sm + S::XX;    // y tile, over X once MMA2 and MMA4 are done
   unsigned char* sSin = sm + S::SIN;
   float* s_scal = reinterpret_cast<float*>(sm + S::SCAL);  // [2 parity][c | ec | w | wg | wb | g | b]
-  float* s_nx = s_scal + 2 * 448;                            // next chunk's [adt | gamma | beta]
+  float* s_nx = s_scal + 2 * kScal;                            // next chunk's [adt | gamma | beta]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::BAR);
   uint32_t* misc = reinterpret_cast<uint32_t*>(sm + S::MISC);
 
@@ -226,7 +242,7 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
     uint32_t nx = 0, nxt = 0;
     if (tid == 0) nx = atomicAdd(p.ticket, 1u);  // the next ticket, published to the CTA at the chain
     // this chunk's scalars (mamba3.py:40) were prepared at the end of the previous one
-    const float* s_c = s_scal + par * 448;
+    const float* s_c = s_scal + par * kScal;
     const float* s_ec = s_c + 64;
     const float* s_wg = s_c + 192;
     const float* s_wb = s_c + 256;
@@ -296,23 +312,34 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
       {
         const int t = 16 * sp + (lane & 15);
         const float ct = s_c[t];
+        const float* s_es = s_c + kScalEs;
+        const bool fastm = s_c[kScalFast] != 0.f;
+        // decay e^{c_t - c_s}: a lane's 8 columns of a piece are one 8-token block, factorised when
+        // the chunk allows it (chunk_scalars)
+        auto scores = [&](auto decay) {
 #pragma unroll
-        for (int pi = 0; pi < NPC; ++pi) {
-          const int pc = hw * NPC + pi, half = pc >> 2;
-          const float* coef = half ? s_b : s_g;
-          float v[16];
-          umma::tmem_ld16(tmem + tlane + pc * 16, v);
+          for (int pi = 0; pi < NPC; ++pi) {
+            const int pc = hw * NPC + pi, half = pc >> 2;
+            const float* coef = half ? s_b : s_g;
+            const float et = fastm ? __expf(ct - s_c[16 * (pc & 3) + (hiL ? 8 : 0)]) : 0.f;
+            float v[16];
+            umma::tmem_ld16(tmem + tlane + pc * 16, v);
 #pragma unroll
-          for (int i = 0; i < 8; i += 2) {
-            const float r0 = __shfl_xor_sync(0xffffffffu, v[8 + i], 16);
-            const float r1 = __shfl_xor_sync(0xffffffffu, v[9 + i], 16);
-            const int s0 = (pc & 3) * 16 + (hiL ? 8 : 0) + i;
-            const float a0 = hiL ? r0 : v[i], a1 = hiL ? r1 : v[i + 1];
-            const float v0 = (s0 <= t) ? a0 * coef[s0] * __expf(ct - s_c[s0]) : 0.f;
-            const float v1 = (s0 + 1 <= t) ? a1 * coef[s0 + 1] * __expf(ct - s_c[s0 + 1]) : 0.f;
-            pk[pi >> 1][(pi & 1) * 4 + (i >> 1)] = pack_bf16(v0, v1);
+            for (int i = 0; i < 8; i += 2) {
+              const float r0 = __shfl_xor_sync(0xffffffffu, v[8 + i], 16);
+              const float r1 = __shfl_xor_sync(0xffffffffu, v[9 + i], 16);
+              const int s0 = (pc & 3) * 16 + (hiL ? 8 : 0) + i;
+              const float a0 = hiL ? r0 : v[i], a1 = hiL ? r1 : v[i + 1];
+              const float v0 = (s0 <= t) ? a0 * coef[s0] * decay(et, s0) : 0.f;
+              const float v1 = (s0 + 1 <= t) ? a1 * coef[s0 + 1] * decay(et, s0 + 1) : 0.f;
+              pk[pi >> 1][(pi & 1) * 4 + (i >> 1)] = pack_bf16(v0, v1);
+            }
           }
-        }
+        };
+        if (fastm)
+          scores([&](float et, int s0) { return et * s_es[s0]; });
+        else
+          scores([&](float, int s0) { return __expf(ct - s_c[s0]); });
       }
       ok = __syncthreads_and(umma::mbar_wait(&bars[2], par, p.status));  // MMA3 done: K|Kp free
       if (ok) {
@@ -487,7 +514,7 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
       }
       if (tid < 64 && nxt < total) {  // the next chunk's scalars
         umma::cp_async_wait_all();
-        chunk_scalars(s_scal + (par ^ 1) * 448, s_nx, tid, lane);
+        chunk_scalars(s_scal + (par ^ 1) * kScal, s_nx, tid, lane);
       }
     }
     umma::fence_before_sync();
@@ -546,7 +573,7 @@ struct BwdSmem {
   // per-chunk scalars [c | ec | w | wg wb | g | b] (64 floats each), one block per chunk parity,
   // then the next chunk's staged [adt | gamma | beta]
   static constexpr uint32_t SCAL = E + 16384;
-  static constexpr uint32_t RED = SCAL + (2 * 448 + 192) * 4;
+  static constexpr uint32_t RED = SCAL + (2 * kScal + 192) * 4;
   // RED: rowZ[4][64] | colZ[4][128] | colE[4][128] | xu[4][128] | dcint[2][64] | da[16] | tmp[8] | pre[3][64]
   static constexpr uint32_t RED_FLOATS = 256 + 512 + 512 + 512 + 128 + 16 + 8 + 192;
   static constexpr uint32_t BAR = RED + RED_FLOATS * 4;  // stage loads [2], MMA groups 1-3
@@ -729,7 +756,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
   unsigned char* sEG = sm + S::E;  // [Eg | Epb] [2][64 t][64 s]
   // Gn [NS n][64 p] goes over the current stage's S_in tile (set per chunk below)
   float* s_scal = reinterpret_cast<float*>(sm + S::SCAL);  // [2 parity][c | ec | w | wg wb | g | b]
-  float* s_nx = s_scal + 2 * 448;                            // next chunk's [adt | gamma | beta]
+  float* s_nx = s_scal + 2 * kScal;                            // next chunk's [adt | gamma | beta]
   float* s_rowZ = reinterpret_cast<float*>(sm + S::RED);  // [2 column block][2 half][64]
   float* s_colZ = s_rowZ + 256;                           // [4][128]
   float* s_colE = s_colZ + 512;                           // [4][128]
@@ -795,9 +822,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
     bool prefetched = false, published = false;
     if (tid == 32) nx = atomicAdd(p.ticket, 1u);
     // this chunk's scalars were prepared by the end of the previous one (or before the loop)
-    const float* s_c = s_scal + (it & 1) * 448;
+    const float* s_c = s_scal + (it & 1) * kScal;
     const float* s_ec = s_c + 64;
-    const float* s_w = s_c + 128;
     const float* s_wgb = s_c + 192;  // [wg (64) | wb (64)]
     const float* s_g = s_c + 320;
     const float* s_b = s_c + 384;
@@ -856,7 +882,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
         umma::mma_commit(&bars[2]);
       }
       if (pend && tail_warp)
-        bwd_token_tail(p, s_scal + pend_par * 448, s_da, s_xu, s_pre, s_dcint, s_tmp, tid - 448, lane, warp - 14, pend_a,
+        bwd_token_tail(p, s_scal + pend_par * kScal, s_da, s_xu, s_pre, s_dcint, s_tmp, tid - 448, lane, warp - 14, pend_a,
                        pend_b, pend_h, pend_t0);
       pend = false;
       ok = __syncthreads_and(umma::mbar_wait(&bars[2], par, p.status));
@@ -873,7 +899,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
       const float* coef = half ? s_b : s_g;
       const float ct = s_c[t];
       float rowZ = 0.f;
-      {
+      const float* s_es = s_c + kScalEs;
+      const bool fastm = s_c[kScalFast] != 0.f;
+      // decay e^{c_t - c_s}: this lane's 16 columns are two 8-token blocks, factorised when the chunk
+      // allows it (chunk_scalars)
+      const int r0 = cc * 32 + (hiL ? 16 : 0);
+      const float et0 = fastm ? __expf(ct - s_c[r0]) : 0.f, et1 = fastm ? __expf(ct - s_c[r0 + 8]) : 0.f;
+      auto epilogue = [&](auto decay) {
         float v[32];
         umma::tmem_ld32(R0 + ((uint32_t)(32 * sp) << 16) + half * 64 + cc * 32, v);
         float zc[16], ecs[16];
@@ -885,7 +917,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
           const float sv = hiL ? recv : v[i];          // S_ts
           const float dav = hiL ? v[16 + i] : recv;    // dA_ts
           const int s = cc * 32 + (hiL ? 16 : 0) + i;
-          const float m = (s <= t) ? __expf(ct - s_c[s]) : 0.f;
+          const float m = (s <= t) ? decay(i, s) : 0.f;
           const float cf = coef[s];
           const float A = sv * cf * m;
           const float E = dav * m;
@@ -915,7 +947,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
           *reinterpret_cast<uint4*>(sEG + half * 8192 + umma::sw128_offset(t, c0 + q)) =
               make_uint4(we[4 * q], we[4 * q + 1], we[4 * q + 2], we[4 * q + 3]);
         }
-      }
+      };
+      if (fastm)
+        epilogue([&](int i, int s) { return (i < 8 ? et0 : et1) * s_es[s]; });
+      else
+        epilogue([&](int, int s) { return __expf(ct - s_c[s]); });
       rowZ += __shfl_xor_sync(0xffffffffu, rowZ, 16);
       if (lane < 16) s_rowZ[(cc * 2 + half) * 64 + t] = rowZ;
       umma::fence_proxy_async_smem();
@@ -1152,7 +1188,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
       pend_a = a_chunk;
       if (scal_warp && nxt < total) {
         umma::cp_async_wait_all();  // this thread's own copies
-        chunk_scalars(s_scal + ((it + 1) & 1) * 448, s_nx, tid - 64, lane);
+        chunk_scalars(s_scal + ((it + 1) & 1) * kScal, s_nx, tid - 64, lane);
       }
     }
     __syncthreads();  // every read of this stage and of the work tiles is done
@@ -1168,7 +1204,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
     cur = nxt;
   }
   if (pend && tail_warp)  // the last chunk's per-token scalars
-    bwd_token_tail(p, s_scal + pend_par * 448, s_da, s_xu, s_pre, s_dcint, s_tmp, tid - 448, lane, warp - 14, pend_a,
+    bwd_token_tail(p, s_scal + pend_par * kScal, s_da, s_xu, s_pre, s_dcint, s_tmp, tid - 448, lane, warp - 14, pend_a,
                    pend_b, pend_h, pend_t0);
   if (tid == 32) umma::bulk_wait_all();  // staged output tiles must be read out before exit
   if (scal_warp) umma::cp_async_wait_all();
