@@ -372,13 +372,16 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
                          umma::desc_sw128((part ? xp0 : x0) + kin * 2048, 8192, 1024), id2, ks > 0);
         }
         misc[3] = nx;
-        misc[2] = (j == 0) ? kFlagReady : wait_flag(&flags[j], p.status);
-        if (misc[2] != kFlagReady) umma::mma_commit(&bars[3]);  // MMA2 must finish before TMEM is freed
       }
+      // thread 32 waits for the preceding chunk's hand-off while thread 0 issues MMA2
+      if (tid == 32) misc[2] = (j == 0) ? kFlagReady : wait_flag(&flags[j], p.status);
       __syncthreads();
       ok = misc[2] == kFlagReady;
       nxt = misc[3];
-      if (!ok) umma::mbar_wait(&bars[3], par, p.status);
+      if (!ok) {  // MMA2 must finish before TMEM is freed
+        if (tid == 0) umma::mma_commit(&bars[3]);
+        umma::mbar_wait(&bars[3], par, p.status);
+      }
     }
     if (ok) {
       // state hand-off: S_in[j+1] = e^{c_L} S_in[j] + S_loc (mamba3.py:52).  Lanes 16-31 hold the
@@ -982,8 +985,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
           umma::mma_bf16(R0, umma::desc_sw128(eg0 + ks * 2048, 8192, 1024), umma::desc_sw128(q0 + ks * 2048, 8192, 1024),
                          ide, ks > 0);
         umma::mma_commit(&bars[3]);
-        misc[2] = (j == p.nc - 1) ? kFlagReady : wait_flag(&flags[j + 1], p.status);
       }
+      // thread 64 waits for the preceding chunk's hand-off while thread 0 issues the second group
+      if (tid == 64) misc[2] = (j == p.nc - 1) ? kFlagReady : wait_flag(&flags[j + 1], p.status);
       if (tid == 32) {
         misc[3] = nx;
         umma::bulk_wait_read();  // the previous chunk's output tiles (in the other stage) are out
@@ -1118,6 +1122,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
           s_pre[s] = rowZ - colZ;
           s_pre[64 + s] = colEg;
           s_pre[128 + s] = colEb;
+          if (nxt < total) {  // the next chunk's scalars (its other-parity block is free)
+            umma::cp_async_wait_all();  // this thread's own copies
+            chunk_scalars(s_scal + ((it + 1) & 1) * kScal, s_nx, tid - 64, lane);
+          }
         }
       }
       ok = __syncthreads_and(umma::mbar_wait(&bars[4], par, p.status));
@@ -1179,17 +1187,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
         umma::bulk_commit();
       }
       // this chunk's per-token scalars are written by warps 14-15 while the next chunk's first MMA
-      // group runs (or after the loop); warps 2-3 prepare the next chunk's scalars
+      // group runs (or after the loop)
       pend = true;
       pend_b = b;
       pend_h = h;
       pend_t0 = t0;
       pend_par = it & 1;
       pend_a = a_chunk;
-      if (scal_warp && nxt < total) {
-        umma::cp_async_wait_all();  // this thread's own copies
-        chunk_scalars(s_scal + ((it + 1) & 1) * kScal, s_nx, tid - 64, lane);
-      }
     }
     __syncthreads();  // every read of this stage and of the work tiles is done
     if (!ok) {
