@@ -445,12 +445,13 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
                          pack_bf16(sin[6], sin[7]));
         }
       }
-      // the barrier orders every thread's ring writes before thread 0's release (cumulative)
-      __syncthreads();
-      if (tid == 0) st_release(&flags[j + 1], kFlagReady);
+      // one barrier orders every thread's ring writes before thread 32's release (cumulative) and the
+      // staged S_in before MMA4; the release, which waits for the ring writes to land, is kept off
+      // the MMA issuer
       umma::fence_proxy_async_smem();
       umma::fence_before_sync();
       __syncthreads();
+      if (tid == 32) st_release(&flags[j + 1], kFlagReady);
       if (tid == ISS && p.states) {
         // the saved state is the shared-memory image itself (bf16, 128-byte swizzle), so the
         // backward can bulk-copy it back into place
