@@ -1,8 +1,8 @@
 """Small fixed workloads for profiler captures (ncu).
 
-    python -m zenith_b200.profile_case [--batch 2] [--iters 3]
-        a few forward (saving states) + backward calls of the bf16 scan on B sequences of the layer
-        shape (T2048 H24 P64 N128, chunk 64)
+    python -m zenith_b200.profile_case [--batch 2] [--iters 3] [--dtype bf16|fp32]
+        a few forward (saving states) + backward calls of the scan on B sequences of the layer
+        shape (T2048 H24 P64 N128, chunk 64); bf16 runs the tensor-core kernels, fp32 the SIMT ones
     python -m zenith_b200.profile_case --workload rows [--batch 2] [--heads 48] [--iters 2]
         the row kernels around it, once per iteration each: the fused Mamba-3 layer body (fwd + bwd,
         bf16, P64 N128) on B sequences of 2048 tokens, the residual add + RMSNorm (d_model 1536) and
@@ -28,15 +28,16 @@ def main():
     ap.add_argument("--seqlen", type=int, default=2048)
     ap.add_argument("--workload", choices=("scan", "rows"), default="scan")
     ap.add_argument("--heads", type=int, default=48)
+    ap.add_argument("--dtype", choices=("bf16", "fp32"), default="bf16")
     args = ap.parse_args()
     if args.workload == "rows":
         return rows(args)
     s = SsdShape(args.batch, args.seqlen, 24, 64, 128, 24, 64)
     inp = make_inputs(s, seed=0)
     dev = torch.device("cuda")
-    a = prepare_inputs(*((inp[n].to(torch.bfloat16) if n in ("x", "q", "k", "kp", "xp") else inp[n]).to(dev)
-                         for n in NAMES))
-    dy = inp["dy"].to(torch.bfloat16).to(dev)
+    vdt = torch.float32 if args.dtype == "fp32" else torch.bfloat16
+    a = prepare_inputs(*((inp[n].to(vdt) if n in ("x", "q", "k", "kp", "xp") else inp[n]).to(dev) for n in NAMES))
+    dy = inp["dy"].to(vdt).to(dev)
     for _ in range(args.iters):
         _, _, st = ssd_fwd_op(*a, s.chunk, None, True, False)
         ssd_bwd_op(dy, *a, st, s.chunk, None, None, False)
