@@ -333,7 +333,7 @@ def run_ours(args):
     # Rotating copies of the inputs, so that a step's inputs were last touched at least two steps
     # earlier and at least twice the L2 has been streamed since (a step reads and writes
     # step_bytes): each step starts from HBM, not from a warm L2.
-    n_sets = 1 if step_bytes >= 2 * L2_BYTES else -(-2 * L2_BYTES // step_bytes) + 1
+    n_sets = 1 if step_bytes >= 2 * L2_BYTES else int(-(-2 * L2_BYTES // step_bytes)) + 1
     sets = [inp] + [{n: t.clone() for n, t in inp.items()} for _ in range(n_sets - 1)]
 
     if cp:
@@ -385,7 +385,7 @@ def run_ours(args):
     # The step's launches are captured once per buffer set in a CUDA graph and replayed: the
     # same kernels on the same data each step, without the host's per-launch cost (which
     # would set the pace once a rank's share of the job takes ~100 us).  Context parallelism
-    # (NCCL send / recv inside the step) runs eagerly.
+    # (NCCL all_gathers inside the step, one of them in the autograd backward) runs eagerly.
     graphs = []
     if not cp and not args.eager:
         keep = []
@@ -542,7 +542,7 @@ def run_ours(args):
     achieved = dbytes / (dms / 1e3) / 1e9
     step_gbs = (fwd_b + bwd_b) * th / (ms_per_step / 1e3) / 1e9
     if cp:
-        par = f"context-parallel x{world} (T/{world} per rank, NCCL send/recv of boundary states)"
+        par = f"context-parallel x{world} (T/{world} per rank, boundary states by one NCCL all_gather per direction)"
     elif replicate:
         par = f"replicated x{world} (each rank a whole B{shape.B} job of its own)"
     else:

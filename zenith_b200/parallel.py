@@ -183,7 +183,7 @@ class _CpScan(torch.autograd.Function):
 
 
 def cp_ssd(x, q, k, kp, xp, adt, gamma, beta, chunk_size, *, group=None, initial_state=None,
-           impl: Optional[LocalScan] = None):
+           impl: Optional[LocalScan] = None, check_shapes: bool = True):
     """Context-parallel SSD scan over the ranks of ``group`` (default: the world).
 
     Each rank passes its contiguous range of the sequence ([B, T_local, H, ...], rank r holding
@@ -191,9 +191,13 @@ def cp_ssd(x, q, k, kp, xp, adt, gamma, beta, chunk_size, *, group=None, initial
     ``zenith_b200.ssd`` on the whole sequence, differentiable w.r.t. all eight inputs.
     ``initial_state`` [B, H, P, N] (read on rank 0 only; the other ranks ignore theirs) starts the
     sequence from a given state and is differentiable on rank 0.
+    ``check_shapes=False`` skips the first all_gather of every rank's local shape, which reads the
+    result back on the host: for calls captured in a CUDA graph, after a checked call with the same
+    shapes on every rank.
     """
     assert x.shape[1] % chunk_size == 0, "sequence length must be a multiple of chunk_size"
-    _check_local_shapes(x, q, group)
+    if check_shapes:
+        _check_local_shapes(x, q, group)
     impl = impl or CUDA_SCAN
     if impl is CUDA_SCAN:
         args = prepare_inputs(x, q, k, kp, xp, adt, gamma, beta)
