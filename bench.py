@@ -5,15 +5,17 @@ scripts/bench_ssd.py, which timed zenith.mamba3.ssd fwd+bwd on Apple MPS).
 One step = one forward and one backward of the SSD scan over one batch of the model-scale
 layer workload (B8 T2048 H24 P64 N128, chunk 64, bf16 vectors with fp32 per-token scalars,
 synthetic inputs with the Mamba-3 value distributions).  Multi-GPU: one process per GPU
-(torchrun); batch x heads are independent, so each rank runs its own batch of the workload
-(weak scaling, no collective on the data path); the timed region is bracketed by barriers
-and the slowest rank's CUDA-event time is reported.
+(torchrun); the (batch, head) chains of the one job are independent, so rank r runs its 1/N
+share of them (by batch, else by heads; no collective on the data path; ``--replicate`` gives
+every rank a whole job instead); the timed region is bracketed by barriers and the slowest
+rank's CUDA-event time is reported.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Prints one JSON line (rank 0).  ``--impl reference`` times the reference algorithm on the
-host CPU cores instead (rank 0 only): the CPU restatement of zenith/mamba3.py:30-56 in
-fp32 under PyTorch autograd, the same torch work the reference does on a CPU.
+Prints one JSON line (rank 0).  ``--impl reference`` times the reference on the host CPU cores
+instead (rank 0 only): its own ``zenith.mamba3.ssd`` (or ``ZenithForCausalLM`` for the LM step)
+in fp32 under PyTorch autograd when the reference package is installed under baseline/_ref, else
+the restatement of zenith/mamba3.py:30-56 with the same tensor operations.
 """
 from __future__ import annotations
 
@@ -189,13 +191,41 @@ def make_device_inputs(shape, rank, dev):
 # CPU baseline / reference arm
 
 
-def cpu_reference_sample(shape, seconds: float, max_reps: int | None = None, fwd_only: bool = False):
-    """Time the reference algorithm on the host CPU: zenith/mamba3.py:30-56 restated with the
-    reference's own sequence of tensor operations (oracle/ssd_reference_ops.py), fp32, forward plus
-    PyTorch autograd backward, on a one-sequence slice of the workload; returns (tokens/s, cores,
-    reps, sample string)."""
+def reference_package():
+    """The reference package as installed under baseline/_ref (``pip install --target``), or None
+    with the reason it is not there or does not import."""
+    path = ROOT / "baseline" / "_ref"
+    if not (path / "zenith" / "mamba3.py").exists():
+        return None, "no reference installed under baseline/_ref"
+    if str(path) not in sys.path:
+        sys.path.insert(0, str(path))
+    try:
+        import zenith
+        import zenith.mamba3  # noqa: F401
+    except Exception as e:  # noqa: BLE001 - any import failure falls back to the restatement
+        return None, f"the installed reference does not import ({type(e).__name__}: {str(e)[:120]})"
+    return zenith, ""
+
+
+def reference_ssd():
+    """(ssd function, kind, description): the reference's own ``zenith.mamba3.ssd`` when installed,
+    else its restatement with the same tensor operations (oracle/ssd_reference_ops.py)."""
+    ref, why = reference_package()
+    if ref is not None:
+        return ref.mamba3.ssd, "reference", "reference zenith.mamba3.ssd (installed under baseline/_ref)"
     from oracle.ssd_reference_ops import ssd_reference_ops
+
+    return (ssd_reference_ops, "port",
+            f"reference ssd (zenith/mamba3.py:30-56) restated with its tensor-op sequence [{why}]")
+
+
+def cpu_reference_sample(shape, seconds: float, max_reps: int | None = None, fwd_only: bool = False):
+    """Time the reference's scan on the host CPU (``reference_ssd``), fp32, forward plus PyTorch
+    autograd backward, on a one-sequence slice of the workload; returns (tokens/s, cores, reps,
+    sample string, kind)."""
     from zenith_b200.synthetic import SsdShape, make_inputs
+
+    ssd_fn, kind, origin = reference_ssd()
 
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
@@ -212,9 +242,9 @@ def cpu_reference_sample(shape, seconds: float, max_reps: int | None = None, fwd
     def once():
         if fwd_only:
             with torch.no_grad():
-                ssd_reference_ops(*leaves, sl.chunk)
+                ssd_fn(*leaves, sl.chunk)
             return
-        y = ssd_reference_ops(*leaves, sl.chunk)
+        y = ssd_fn(*leaves, sl.chunk)
         y.backward(dy)
         for t in leaves:
             t.grad = None
@@ -229,10 +259,10 @@ def cpu_reference_sample(shape, seconds: float, max_reps: int | None = None, fwd
             break
     tok_s = reps * sl.B * sl.T / el
     what = "forward" if fwd_only else "fp32 forward + autograd backward"
-    sample = (f"reference ssd (zenith/mamba3.py:30-56, its tensor-op sequence restated) {what} on host CPU, "
+    sample = (f"{origin}, {what} on host CPU, "
               f"1 sequence (T{sl.T} H{sl.H} P{sl.P} N{sl.N} G{sl.G} chunk {sl.chunk}) of the B{shape.B} workload, "
               f"{reps} reps in {el:.1f} s, {cores} threads")
-    return tok_s, cores, reps, sample
+    return tok_s, cores, reps, sample, kind
 
 
 def run_reference(args):
@@ -244,7 +274,7 @@ def run_reference(args):
     shape = SHAPES[args.workload]
     seconds = max(3.0, min(120.0, 2.0 * (args.steps + args.warmup)))
     fwd_only = args.workload == "infer"
-    tok_s, cores, reps, sample = cpu_reference_sample(shape, seconds, fwd_only=fwd_only)
+    tok_s, cores, reps, sample, kind = cpu_reference_sample(shape, seconds, fwd_only=fwd_only)
     ms = shape.B * shape.T / tok_s * 1e3
     line = {
         "impl": "reference", "metric": METRIC_FWD if fwd_only else METRIC, "value": tok_s, "unit": UNIT, "n_gpus": args.gpus,
@@ -252,7 +282,7 @@ def run_reference(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
         "config": {"workload": shape.name, "B": shape.B, "T": shape.T, "H": shape.H, "P": shape.P, "N": shape.N,
                    "chunk": shape.chunk, "device": "host cpu"},
-        "cpu_baseline": {"value": tok_s, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": tok_s, "unit": UNIT, "cores": cores, "kind": kind, "sample": sample},
         "e2e": {"value": tok_s, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -525,8 +555,8 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        tok_s, cores, reps, sample = cpu_reference_sample(shape, args.cpu_seconds, fwd_only=fwd_only)
-        cpu = {"value": tok_s, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+        tok_s, cores, reps, sample, kind = cpu_reference_sample(shape, args.cpu_seconds, fwd_only=fwd_only)
+        cpu = {"value": tok_s, "unit": UNIT, "cores": cores, "kind": kind, "sample": sample}
 
     if world > 1:
         dist.barrier()
@@ -685,25 +715,38 @@ def lm_flops_per_token(cfg):
 
 
 def cpu_lm_sample(cfg, seconds: float, T: int = 128):
-    """The reference LM step (the oracle restatement of zenith/model.py:79-99, float32, autograd)
-    on the host CPU for one sequence of T tokens; returns (tokens/s, cores, sample string)."""
-    from oracle import lm_oracle
-
+    """The reference LM's forward + backward (float32, autograd) on the host CPU for one sequence of
+    T tokens: the reference's own ``ZenithForCausalLM`` when installed under baseline/_ref, else the
+    oracle restatement of zenith/model.py:79-99.  The optimiser step (one per 16,384 tokens on the
+    GPU) is left out of the sample.  Returns (tokens/s, cores, sample string, kind)."""
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
     torch.manual_seed(0)
-    with torch.device("cpu"):
-        from zenith_b200.lm import ZenithForCausalLM
-
-        model = ZenithForCausalLM(cfg)          # initialisation only; the step below is the oracle's
-    params = {n: t.detach().clone().requires_grad_(True) for n, t in model.named_parameters()}
     ids = torch.randint(0, cfg["vocab_size"], (1, T))
+    ref, why = reference_package()
+    if ref is not None:
+        model = ref.ZenithForCausalLM(ref.ZenithConfig(**cfg))
+        model.train()
+        kind, origin = "reference", "reference ZenithForCausalLM (installed under baseline/_ref)"
 
-    def once():
-        _, loss = lm_oracle.forward(params, cfg, ids, ids, loops=cfg["max_loops"])
-        loss.backward()
-        for t in params.values():
-            t.grad = None
+        def once():
+            model(ids, labels=ids, loops=cfg["max_loops"]).loss.backward()
+            model.zero_grad(set_to_none=True)
+    else:
+        from oracle import lm_oracle
+
+        with torch.device("cpu"):
+            from zenith_b200.lm import ZenithForCausalLM
+
+            model = ZenithForCausalLM(cfg)          # initialisation only; the step below is the oracle's
+        params = {n: t.detach().clone().requires_grad_(True) for n, t in model.named_parameters()}
+        kind, origin = "port", f"reference LM (zenith/model.py:79-99) restated [{why}]"
+
+        def once():
+            _, loss = lm_oracle.forward(params, cfg, ids, ids, loops=cfg["max_loops"])
+            loss.backward()
+            for t in params.values():
+                t.grad = None
 
     once()
     reps, t0 = 0, time.perf_counter()
@@ -714,23 +757,23 @@ def cpu_lm_sample(cfg, seconds: float, T: int = 128):
         if el >= seconds:
             break
     tok_s = reps * T / el
-    sample = (f"reference LM step (float32 + autograd) on host CPU, 1 sequence of {T} tokens of the full model, "
-              f"{reps} reps in {el:.1f} s, {cores} threads")
-    return tok_s, cores, sample
+    sample = (f"{origin}: float32 forward + autograd backward on host CPU, 1 sequence of {T} tokens of the full "
+              f"model (no optimiser step), {reps} reps in {el:.1f} s, {cores} threads")
+    return tok_s, cores, sample, kind
 
 
 def run_lm_reference(args):
     if int(os.environ.get("RANK", "0")) != 0:
         return 0
     seconds = max(5.0, min(120.0, 2.0 * (args.steps + args.warmup)))
-    tok_s, cores, sample = cpu_lm_sample(LM_CONFIG, seconds)
+    tok_s, cores, sample, kind = cpu_lm_sample(LM_CONFIG, seconds)
     line = {
         "impl": "reference", "metric": LM_METRIC, "value": tok_s, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": LM_BATCH * LM_SEQ / tok_s * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
         "config": {"workload": "Mamba-3 LM training step", **LM_CONFIG, "micro_batch": LM_BATCH, "seq_len": LM_SEQ,
                    "device": "host cpu"},
-        "cpu_baseline": {"value": tok_s, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": tok_s, "unit": UNIT, "cores": cores, "kind": kind, "sample": sample},
         "e2e": {"value": tok_s, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -817,8 +860,8 @@ def run_lm(args):
         achieved = flops / (ms / 1e3) / 1e12
         cpu = None
         if not args.no_cpu_baseline:
-            tok_s, cores, sample = cpu_lm_sample(LM_CONFIG, args.cpu_seconds)
-            cpu = {"value": tok_s, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+            tok_s, cores, sample, kind = cpu_lm_sample(LM_CONFIG, args.cpu_seconds)
+            cpu = {"value": tok_s, "unit": UNIT, "cores": cores, "kind": kind, "sample": sample}
         line = {
             "metric": LM_METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
