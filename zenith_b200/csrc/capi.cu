@@ -328,37 +328,67 @@ SegLayout seg_layout(const zb_ssd_args* a, int M) {
   return L;
 }
 
-// forward combine: segment initial states from `init` (or zero), F and D; writes the final state
-__global__ void seg_combine_fwd_kernel(const float* init, const float* F, const float* D, float* S, float* fin, int64_t B,
-                                       int64_t H, int M, int64_t PN) {
-  const int64_t total = B * H * PN;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t e = i % PN, bh = i / PN, b = bh / H, h = bh % H;
-    float s = init ? init[i] : 0.f;
-    for (int m = 0; m < M; ++m) {
-      const int64_t idx = (b * M + m) * H + h;
-      S[idx * PN + e] = s;
-      s = D[idx] * s + F[idx * PN + e];
+// Combine kernels: one CTA row per (batch, head) and one thread per state element e.  The chain over
+// the M segments is serial in its arithmetic only: each batch of kCombineBatch segments' F / G and D
+// is loaded before any of them is used (the pointers are restrict-qualified), so a thread waits for
+// one round of loads per batch instead of one per segment.
+constexpr int kCombineBatch = 8;
+
+// forward: segment initial states from `init` (or zero), F and D; writes the final state
+__global__ void seg_combine_fwd_kernel(const float* __restrict__ init, const float* __restrict__ F,
+                                       const float* __restrict__ D, float* __restrict__ S, float* __restrict__ fin,
+                                       int H, int M, int64_t PN) {
+  const int64_t e = (int64_t)blockIdx.y * blockDim.x + threadIdx.x;
+  if (e >= PN) return;
+  const int bh = blockIdx.x, b = bh / H, h = bh - b * H;
+  float s = init ? init[(int64_t)bh * PN + e] : 0.f;
+  for (int m0 = 0; m0 < M; m0 += kCombineBatch) {
+    float f[kCombineBatch], d[kCombineBatch];
+#pragma unroll
+    for (int u = 0; u < kCombineBatch; ++u) {
+      const int64_t idx = ((int64_t)b * M + m0 + u) * H + h;
+      f[u] = (m0 + u < M) ? F[idx * PN + e] : 0.f;
+      d[u] = (m0 + u < M) ? D[idx] : 0.f;
     }
-    if (fin) fin[i] = s;
+#pragma unroll
+    for (int u = 0; u < kCombineBatch; ++u) {
+      if (m0 + u >= M) break;
+      const int64_t idx = ((int64_t)b * M + m0 + u) * H + h;
+      S[idx * PN + e] = s;
+      s = d[u] * s + f[u];
+    }
   }
+  if (fin) fin[(int64_t)bh * PN + e] = s;
 }
 
-// backward combine: gradient w.r.t. each segment's final state, from `dfinal` (or zero), the
-// segments' own initial-state gradients G and D; writes the gradient w.r.t. the initial state
-__global__ void seg_combine_bwd_kernel(const float* dfinal, const float* G, const float* D, float* E, float* dinit,
-                                       int64_t B, int64_t H, int M, int64_t PN) {
-  const int64_t total = B * H * PN;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t e = i % PN, bh = i / PN, b = bh / H, h = bh % H;
-    float g = dfinal ? dfinal[i] : 0.f;
-    for (int m = M - 1; m >= 0; --m) {
-      const int64_t idx = (b * M + m) * H + h;
-      E[idx * PN + e] = g;
-      g = D[idx] * g + G[idx * PN + e];
+// backward: gradient w.r.t. each segment's final state, from `dfinal` (or zero), the segments' own
+// initial-state gradients G and D; writes the gradient w.r.t. the initial state
+__global__ void seg_combine_bwd_kernel(const float* __restrict__ dfinal, const float* __restrict__ G,
+                                       const float* __restrict__ D, float* __restrict__ E, float* __restrict__ dinit,
+                                       int H, int M, int64_t PN) {
+  const int64_t e = (int64_t)blockIdx.y * blockDim.x + threadIdx.x;
+  if (e >= PN) return;
+  const int bh = blockIdx.x, b = bh / H, h = bh - b * H;
+  float g = dfinal ? dfinal[(int64_t)bh * PN + e] : 0.f;
+  for (int m1 = M; m1 > 0; m1 -= kCombineBatch) {  // segments m1-1 down to m1-kCombineBatch
+    float gg[kCombineBatch], d[kCombineBatch];
+#pragma unroll
+    for (int u = 0; u < kCombineBatch; ++u) {
+      const int m = m1 - 1 - u;
+      const int64_t idx = ((int64_t)b * M + m) * H + h;
+      gg[u] = (m >= 0) ? G[idx * PN + e] : 0.f;
+      d[u] = (m >= 0) ? D[idx] : 0.f;
     }
-    if (dinit) dinit[i] = g;
+#pragma unroll
+    for (int u = 0; u < kCombineBatch; ++u) {
+      const int m = m1 - 1 - u;
+      if (m < 0) break;
+      const int64_t idx = ((int64_t)b * M + m) * H + h;
+      E[idx * PN + e] = g;
+      g = d[u] * g + gg[u];
+    }
   }
+  if (dinit) dinit[(int64_t)bh * PN + e] = g;
 }
 
 int launch_total_decay(const zb_ssd_args* a, float* out, cudaStream_t s);
@@ -384,9 +414,10 @@ int seg_fwd(const zb_ssd_args* a, int M, char* ws, cudaStream_t stream) {
   int rc = tc_fwd(&st, sync, nullptr, ws + L.ring, stream);
   if (rc) return rc;
   if ((rc = launch_total_decay(&sa, D, stream))) return rc;
-  const int64_t PN = a->P * a->N, total = a->B * a->H * PN;
-  seg_combine_fwd_kernel<<<(unsigned)std::min<int64_t>((total + 255) / 256, 148 * 8), 256, 0, stream>>>(
-      static_cast<const float*>(a->initial_state), F, D, Sg, static_cast<float*>(a->final_state), a->B, a->H, M, PN);
+  const int64_t PN = a->P * a->N;
+  const dim3 cgrid((unsigned)(a->B * a->H), (unsigned)((PN + 255) / 256));
+  seg_combine_fwd_kernel<<<cgrid, 256, 0, stream>>>(static_cast<const float*>(a->initial_state), F, D, Sg,
+                                                    static_cast<float*>(a->final_state), (int)a->H, M, PN);
   note_launches(1);
   if (a->flags & ZB_FLAG_STATE_ONLY) return cudaPeekAtLastError() == cudaSuccess ? ZB_OK : ZB_ERR_CUDA;
   if ((e = cudaMemsetAsync(ws, 0, sync_bytes, stream)) != cudaSuccess) return ZB_ERR_CUDA;
@@ -415,9 +446,10 @@ int seg_bwd(const zb_ssd_args* a, int M, char* ws, cudaStream_t stream) {
   int rc = tc_bwd(&st, sync, ws + L.ring, stream);
   if (rc) return rc;
   if ((rc = launch_total_decay(&sa, D, stream))) return rc;
-  const int64_t PN = a->P * a->N, total = a->B * a->H * PN;
-  seg_combine_bwd_kernel<<<(unsigned)std::min<int64_t>((total + 255) / 256, 148 * 8), 256, 0, stream>>>(
-      static_cast<const float*>(a->dfinal_state), G, D, E, static_cast<float*>(a->dinitial_state), a->B, a->H, M, PN);
+  const int64_t PN = a->P * a->N;
+  const dim3 cgrid((unsigned)(a->B * a->H), (unsigned)((PN + 255) / 256));
+  seg_combine_bwd_kernel<<<cgrid, 256, 0, stream>>>(static_cast<const float*>(a->dfinal_state), G, D, E,
+                                                    static_cast<float*>(a->dinitial_state), (int)a->H, M, PN);
   note_launches(1);
   if (a->flags & ZB_FLAG_STATE_ONLY) return cudaPeekAtLastError() == cudaSuccess ? ZB_OK : ZB_ERR_CUDA;
   if ((e = cudaMemsetAsync(ws, 0, sync_bytes, stream)) != cudaSuccess) return ZB_ERR_CUDA;
