@@ -130,7 +130,7 @@ struct View {
 constexpr int kFlagReady = 1;
 constexpr int kFlagAbort = 2;
 constexpr uint64_t kWaitTimeoutNs = 1000000000ull;  // 1 s
-constexpr uint32_t kWaitMaxIters = 1u << 22;         // independent cap, ~4 s with 1 us sleeps
+constexpr uint32_t kWaitMaxIters = 1u << 22;         // independent cap: seconds at one L2 load per poll
 
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
@@ -160,7 +160,7 @@ static __device__ __noinline__ int wait_flag(const int* flag, int32_t* status) {
       if (globaltimer() - t0 > kWaitTimeoutNs) break;
     }
     __nanosleep(sleep_ns);
-    if (sleep_ns < 256) sleep_ns <<= 1;
+    if (sleep_ns < 64) sleep_ns <<= 1;
   }
   atomicCAS(status, 0, (int32_t)ZB_ERR_TIMEOUT);
   return kFlagAbort;

@@ -397,7 +397,7 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
       float* fin = (j == p.nc - 1 && p.fin) ? p.fin + bh * PN : nullptr;
       const float* init = p.init ? p.init + bh * PN : nullptr;
       constexpr int NP = 4 * QB / WPS;  // (half, 16-column block) pairs per warp
-      constexpr int NBATCH = WPS == 1 ? NP : 2;  // pairs whose ring loads are in flight together
+      constexpr int NBATCH = NP;  // every pair's ring loads in flight together (one L2 round trip)
       const int hs = hiL ? 0 : 1;       // which 8 columns of a block this lane takes
 #pragma unroll
       for (int b0 = 0; b0 < NP; b0 += NBATCH) {
