@@ -34,6 +34,179 @@ struct SmemLayout {
 };
 
 // ---------------------------------------------------------------------------------------------
+// Register-tiled products over the shared-memory tiles, used when P <= 64 and N <= 128 (the model
+// shapes); other sizes take the one-output-per-thread loops.  A warp owns RM consecutive output
+// rows (all its lanes read the same element of the row operand: a broadcast) and the columns
+// lane + 32 j, j < RN (consecutive lanes read consecutive elements of the column operand; the rows
+// of every tile are padded to an odd length, so strided column reads do not collide in a bank
+// either).  Each product accumulates over k in increasing order: results are reproducible.
+// Out-of-range rows and columns read a clamped index and are never stored.
+constexpr int kTiledMaxP = 64, kTiledMaxN = 128;
+
+template <int RM, int RN>
+struct Tile {
+  int m0, n0;        // first row of the warp; first column of this lane
+  int m[RM], n[RN];  // clamped row / column indices
+  __device__ __forceinline__ bool ok(int i, int j, int M, int Nn) const { return m0 + i < M && n0 + 32 * j < Nn; }
+};
+
+template <int RM, int RN, class F>
+__device__ __forceinline__ void for_tiles(int M, int Nn, F&& f) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mb = (M + RM - 1) / RM, nb = (Nn + 32 * RN - 1) / (32 * RN);
+  for (int task = warp; task < mb * nb; task += kThreads / 32) {
+    Tile<RM, RN> tl;
+    tl.m0 = (task / nb) * RM;
+    tl.n0 = (task % nb) * 32 * RN + lane;
+#pragma unroll
+    for (int i = 0; i < RM; ++i) tl.m[i] = min(tl.m0 + i, M - 1);
+#pragma unroll
+    for (int j = 0; j < RN; ++j) tl.n[j] = min(tl.n0 + 32 * j, Nn - 1);
+    f(tl);
+  }
+}
+
+// acc[i][j] += sum_{k < K} a[i][k as] * b[j][k bs] * scale(k)
+template <int RM, int RN, typename TA, class FS>
+__device__ __forceinline__ void tile_mm(TA (&acc)[RM][RN], const TA* const (&a)[RM], int as, const TA* const (&b)[RN],
+                                        int bs, int K, FS scale) {
+  for (int k = 0; k < K; ++k) {
+    const TA sc = scale(k);
+    TA av[RM], bv[RN];
+#pragma unroll
+    for (int i = 0; i < RM; ++i) av[i] = a[i][k * as];
+#pragma unroll
+    for (int j = 0; j < RN; ++j) bv[j] = b[j][k * bs] * sc;
+#pragma unroll
+    for (int i = 0; i < RM; ++i)
+#pragma unroll
+      for (int j = 0; j < RN; ++j) acc[i][j] += av[i] * bv[j];
+  }
+}
+// two row operands against one column operand: acc1 += a1 b, acc2 += a2 b
+template <int RM, int RN, typename TA>
+__device__ __forceinline__ void tile_mm_2a(TA (&acc1)[RM][RN], TA (&acc2)[RM][RN], const TA* const (&a1)[RM],
+                                           const TA* const (&a2)[RM], int as, const TA* const (&b)[RN], int bs, int K) {
+  for (int k = 0; k < K; ++k) {
+    TA av1[RM], av2[RM], bv[RN];
+#pragma unroll
+    for (int i = 0; i < RM; ++i) {
+      av1[i] = a1[i][k * as];
+      av2[i] = a2[i][k * as];
+    }
+#pragma unroll
+    for (int j = 0; j < RN; ++j) bv[j] = b[j][k * bs];
+#pragma unroll
+    for (int i = 0; i < RM; ++i)
+#pragma unroll
+      for (int j = 0; j < RN; ++j) {
+        acc1[i][j] += av1[i] * bv[j];
+        acc2[i][j] += av2[i] * bv[j];
+      }
+  }
+}
+// one row operand against two column operands: acc1 += a b1, acc2 += a b2
+template <int RM, int RN, typename TA>
+__device__ __forceinline__ void tile_mm_2b(TA (&acc1)[RM][RN], TA (&acc2)[RM][RN], const TA* const (&a)[RM], int as,
+                                           const TA* const (&b1)[RN], const TA* const (&b2)[RN], int bs, int K) {
+  for (int k = 0; k < K; ++k) {
+    TA av[RM], bv1[RN], bv2[RN];
+#pragma unroll
+    for (int i = 0; i < RM; ++i) av[i] = a[i][k * as];
+#pragma unroll
+    for (int j = 0; j < RN; ++j) {
+      bv1[j] = b1[j][k * bs];
+      bv2[j] = b2[j][k * bs];
+    }
+#pragma unroll
+    for (int i = 0; i < RM; ++i)
+#pragma unroll
+      for (int j = 0; j < RN; ++j) {
+        acc1[i][j] += av[i] * bv1[j];
+        acc2[i][j] += av[i] * bv2[j];
+      }
+  }
+}
+template <typename TA>
+struct Unscaled {
+  __device__ __forceinline__ TA operator()(int) const { return TA(1); }
+};
+
+// The copy loops issue kLoadBatch global loads per thread before any of their shared-memory stores:
+// a store between two loads would make the second wait for the first (the compiler cannot prove
+// that a generic pointer does not alias shared memory), one memory round trip per element.
+constexpr int kLoadBatch = 8;
+
+// rows [0, L) of a [B, T, H, D] view (tokens t0 + t - sh, head hh) -> shared tile [L][D1]; rows
+// t >= Lc and tokens before the start of the sequence read as zero
+template <typename TA, typename TI>
+__device__ __forceinline__ void load_tile(TA* dst, int D1, const View& v, int64_t b, int64_t t0, int sh, int64_t hh,
+                                          int L, int D, int Lc) {
+  const int total = L * D;
+  for (int base = threadIdx.x; base < total; base += kThreads * kLoadBatch) {
+    TA val[kLoadBatch];
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int i = base + u * kThreads, t = i / D, d = i - t * D;
+      val[u] = (i < total && t < Lc && t0 + t >= sh) ? ldv<TA>(v.row<TI>(b, t0 + t - sh, hh) + d) : TA(0);
+    }
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int i = base + u * kThreads, t = i / D, d = i - t * D;
+      if (i < total) dst[t * D1 + d] = val[u];
+    }
+  }
+}
+
+// a [P][N] state in global memory (read through L2; zero when src is null) -> shared [P][N1]
+template <typename TA>
+__device__ __forceinline__ void load_state(TA* dst, int N1, const TA* src, int P, int N) {
+  const int total = P * N;
+  for (int base = threadIdx.x; base < total; base += kThreads * kLoadBatch) {
+    TA val[kLoadBatch];
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int i = base + u * kThreads;
+      val[u] = (src && i < total) ? ldcg_t(src + i) : TA(0);
+    }
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int i = base + u * kThreads;
+      if (i < total) dst[(i / N) * N1 + i % N] = val[u];
+    }
+  }
+}
+
+// the chain update out[i] = a * s[i] + out[i] for a [P][N] state (s in shared memory [P][N1]),
+// also written to `copy` when given; returns sum_i s[i] * dot[i] over this thread's elements when
+// `dot` (shared [P][N1]) is given
+template <typename TA>
+__device__ __forceinline__ TA chain_update(TA* out, const TA* s, TA a, int N1, int P, int N, TA* copy, const TA* dot) {
+  const int total = P * N;
+  TA acc = 0;
+  for (int base = threadIdx.x; base < total; base += kThreads * kLoadBatch) {
+    TA val[kLoadBatch];
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int i = base + u * kThreads;
+      val[u] = i < total ? out[i] : TA(0);
+    }
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int i = base + u * kThreads;
+      if (i < total) {
+        const int si = (i / N) * N1 + i % N;
+        const TA v = val[u] + a * s[si];
+        out[i] = v;
+        if (copy) copy[i] = v;
+        if (dot) acc += s[si] * dot[si];
+      }
+    }
+  }
+  return acc;
+}
+
+// ---------------------------------------------------------------------------------------------
 // forward
 template <typename TI, typename TS, typename TA>
 __global__ void __launch_bounds__(kThreads) ssd_fwd_simt_kernel(const SimtParams p) {
@@ -58,6 +231,7 @@ __global__ void __launch_bounds__(kThreads) ssd_fwd_simt_kernel(const SimtParams
 
   const int tid = threadIdx.x;
   const bool state_only = (p.flags & ZB_FLAG_STATE_ONLY) != 0;
+  const bool tiled = P <= kTiledMaxP && N <= kTiledMaxN;
   if (tid == 0) s_ticket = (int)atomicAdd(p.sync.ticket, 1u);
   __syncthreads();
   const UnitIdx u = decode_ticket((uint32_t)s_ticket, p.B, p.H, p.G);
@@ -82,19 +256,11 @@ __global__ void __launch_bounds__(kThreads) ssd_fwd_simt_kernel(const SimtParams
       s_b[tid] = bt;
     }
   }
-  for (int i = tid; i < L * N; i += kThreads) {
-    const int t = i / N, n = i % N;
-    const bool v = t < Lc;
-    s_k[t * N1 + n] = v ? ldv<TA>(p.k.row<TI>(b, t0 + t, g) + n) : TA(0);
-    s_kp[t * N1 + n] = v && t0 + t >= sh ? ldv<TA>(p.kp.row<TI>(b, t0 + t - sh, g) + n) : TA(0);
-    if (!state_only) s_q[t * N1 + n] = v ? ldv<TA>(p.q.row<TI>(b, t0 + t, g) + n) : TA(0);
-  }
-  for (int i = tid; i < L * P; i += kThreads) {
-    const int t = i / P, pp = i % P;
-    const bool v = t < Lc;
-    s_x[t * P1 + pp] = v ? ldv<TA>(p.x.row<TI>(b, t0 + t, h) + pp) : TA(0);
-    s_xp[t * P1 + pp] = v && t0 + t >= sh ? ldv<TA>(p.xp.row<TI>(b, t0 + t - sh, h) + pp) : TA(0);
-  }
+  load_tile<TA, TI>(s_k, N1, p.k, b, t0, 0, g, L, N, Lc);
+  load_tile<TA, TI>(s_kp, N1, p.kp, b, t0, sh, g, L, N, Lc);
+  if (!state_only) load_tile<TA, TI>(s_q, N1, p.q, b, t0, 0, g, L, N, Lc);
+  load_tile<TA, TI>(s_x, P1, p.x, b, t0, 0, h, L, P, Lc);
+  load_tile<TA, TI>(s_xp, P1, p.xp, b, t0, sh, h, L, P, Lc);
   __syncthreads();
   const TA cl = s_c[Lc - 1];
   if (tid < L) {
@@ -111,15 +277,64 @@ __global__ void __launch_bounds__(kThreads) ssd_fwd_simt_kernel(const SimtParams
 
   // chunk-local state S_loc (mamba3.py:46-47), parked in the outgoing slot until the
   // incoming state is known (each thread re-reads only what it wrote itself)
-  for (int i = tid; i < P * N; i += kThreads) {
-    const int pp = i / N, n = i % N;
-    TA acc = 0;
-    for (int s = 0; s < Lc; ++s)
-      acc += s_w[s] * (s_g[s] * s_x[s * P1 + pp] * s_k[s * N1 + n] + s_b[s] * s_xp[s * P1 + pp] * s_kp[s * N1 + n]);
-    slot_out[i] = acc;
+  if (tiled) {
+    // rows p, columns n: sum_s x_sp (w_s g_s k_sn) + xp_sp (w_s b_s kp_sn)
+    for_tiles<8, 4>(P, N, [&](const Tile<8, 4>& tl) {
+      TA acc[8][4] = {};
+      const TA* a[8];
+      const TA* bb[4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a[i] = s_x + tl.m[i];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) bb[jj] = s_k + tl.n[jj];
+      tile_mm(acc, a, P1, bb, N1, Lc, [&](int s) { return s_w[s] * s_g[s]; });
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a[i] = s_xp + tl.m[i];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) bb[jj] = s_kp + tl.n[jj];
+      tile_mm(acc, a, P1, bb, N1, Lc, [&](int s) { return s_w[s] * s_b[s]; });
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj)
+          if (tl.ok(i, jj, P, N)) slot_out[(tl.m0 + i) * N + tl.n0 + 32 * jj] = acc[i][jj];
+    });
+  } else {
+    for (int i = tid; i < P * N; i += kThreads) {
+      const int pp = i / N, n = i % N;
+      TA acc = 0;
+      for (int s = 0; s < Lc; ++s)
+        acc += s_w[s] * (s_g[s] * s_x[s * P1 + pp] * s_k[s * N1 + n] + s_b[s] * s_xp[s * P1 + pp] * s_kp[s * N1 + n]);
+      slot_out[i] = acc;
+    }
   }
   // masked intra-chunk scores (mamba3.py:41-44)
-  if (!state_only) {
+  if (!state_only && tiled) {
+    // rows t, columns s: q_t . k_s and q_t . kp_s
+    for_tiles<4, 1>(L, L, [&](const Tile<4, 1>& tl) {
+      TA dk[4][1] = {}, dkp[4][1] = {};
+      const TA* a[4];
+      const TA* b1[1] = {s_k + tl.n[0] * N1};
+      const TA* b2[1] = {s_kp + tl.n[0] * N1};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = s_q + tl.m[i] * N1;
+      tile_mm_2b(dk, dkp, a, 1, b1, b2, 1, N);
+      const int s = tl.n0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int t = tl.m0 + i;
+        if (!tl.ok(i, 0, L, L)) continue;
+        TA vg = 0, vb = 0;
+        if (s <= t && t < Lc) {
+          const TA m = xexp(s_c[t] - s_c[s]);
+          vg = dk[i][0] * s_g[s] * m;
+          vb = dkp[i][0] * s_b[s] * m;
+        }
+        s_Sg[t * L1 + s] = vg;
+        s_Sb[t * L1 + s] = vb;
+      }
+    });
+  } else if (!state_only) {
     for (int i = tid; i < L * L; i += kThreads) {
       const int t = i / L, s = i % L;
       TA vg = 0, vb = 0;
@@ -145,38 +360,66 @@ __global__ void __launch_bounds__(kThreads) ssd_fwd_simt_kernel(const SimtParams
     if (tid == 0) st_release(&flags[j + 1], kFlagAbort);
     return;
   }
-  for (int i = tid; i < P * N; i += kThreads) {
-    TA v;
-    if (j == 0) {
-      v = p.init ? reinterpret_cast<const TA*>(p.init)[bh * PN + i] : TA(0);
+  if (j == 0) {
+    for (int i = tid; i < P * N; i += kThreads) {
+      const TA v = p.init ? reinterpret_cast<const TA*>(p.init)[bh * PN + i] : TA(0);
       slot_in[i] = v;
-    } else {
-      v = ldcg_t(slot_in + i);
+      s_S[(i / N) * N1 + i % N] = v;
     }
-    s_S[(i / N) * N1 + i % N] = v;
+  } else {
+    load_state(s_S, N1, slot_in, P, N);
   }
   __syncthreads();
   // S_in[j+1] = e^{c_L} S_in[j] + S_loc[j]   (mamba3.py:52)
   const bool last = (j == p.nc - 1);
-  for (int i = tid; i < P * N; i += kThreads) {
-    const TA v = a_chunk * s_S[(i / N) * N1 + i % N] + slot_out[i];
-    slot_out[i] = v;
-    if (last && p.fin) reinterpret_cast<TA*>(p.fin)[bh * PN + i] = v;
-  }
+  chain_update<TA>(slot_out, s_S, a_chunk, N1, P, N, (last && p.fin) ? reinterpret_cast<TA*>(p.fin) + bh * PN : nullptr,
+                   nullptr);
   // the barrier orders every thread's ring writes before thread 0's release (cumulative)
   __syncthreads();
   if (tid == 0) st_release(&flags[j + 1], kFlagReady);
   if (state_only) return;
 
   // y = y_intra + e^{c} (q S_in^T)   (mamba3.py:45,55)
-  for (int i = tid; i < Lc * P; i += kThreads) {
-    const int t = i / P, pp = i % P;
-    TA acc = 0;
-    for (int s = 0; s <= t; ++s) acc += s_Sg[t * L1 + s] * s_x[s * P1 + pp] + s_Sb[t * L1 + s] * s_xp[s * P1 + pp];
-    TA ai = 0;
-    for (int n = 0; n < N; ++n) ai += s_q[t * N1 + n] * s_S[pp * N1 + n];
-    acc += s_ec[t] * ai;
-    stv<TA>(p.y.wrow<TI>(b, t0 + t, h) + pp, acc);
+  if (tiled) {
+    // rows t, columns p; the scores are zero above the diagonal
+    for_tiles<4, 2>(Lc, P, [&](const Tile<4, 2>& tl) {
+      TA yi[4][2] = {}, yr[4][2] = {};
+      const TA* a[4];
+      const TA* bb[2];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = s_Sg + tl.m[i] * L1;
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) bb[jj] = s_x + tl.n[jj];
+      tile_mm(yi, a, 1, bb, P1, Lc, Unscaled<TA>());
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = s_Sb + tl.m[i] * L1;
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) bb[jj] = s_xp + tl.n[jj];
+      tile_mm(yi, a, 1, bb, P1, Lc, Unscaled<TA>());
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = s_q + tl.m[i] * N1;
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) bb[jj] = s_S + tl.n[jj] * N1;
+      tile_mm(yr, a, 1, bb, 1, N, Unscaled<TA>());
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj)
+          if (tl.ok(i, jj, Lc, P)) {
+            const int t = tl.m0 + i;
+            stv<TA>(p.y.wrow<TI>(b, t0 + t, h) + tl.n0 + 32 * jj, yi[i][jj] + s_ec[t] * yr[i][jj]);
+          }
+    });
+  } else {
+    for (int i = tid; i < Lc * P; i += kThreads) {
+      const int t = i / P, pp = i % P;
+      TA acc = 0;
+      for (int s = 0; s <= t; ++s) acc += s_Sg[t * L1 + s] * s_x[s * P1 + pp] + s_Sb[t * L1 + s] * s_xp[s * P1 + pp];
+      TA ai = 0;
+      for (int n = 0; n < N; ++n) ai += s_q[t * N1 + n] * s_S[pp * N1 + n];
+      acc += s_ec[t] * ai;
+      stv<TA>(p.y.wrow<TI>(b, t0 + t, h) + pp, acc);
+    }
   }
 }
 
@@ -218,6 +461,7 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool state_only = (p.flags & ZB_FLAG_STATE_ONLY) != 0;
+  const bool tiled = P <= kTiledMaxP && N <= kTiledMaxN;
   if (tid == 0) s_ticket = (int)atomicAdd(p.sync.ticket, 1u);
   __syncthreads();
   const UnitIdx u = decode_ticket((uint32_t)s_ticket, p.B, p.H, p.G);
@@ -248,27 +492,15 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
       s_xpu[tid] = 0;
     }
   }
-  for (int i = tid; i < L * N; i += kThreads) {
-    const int t = i / N, n = i % N;
-    const bool v = t < Lc;
-    s_q[t * N1 + n] = v ? ldv<TA>(p.q.row<TI>(b, t0 + t, g) + n) : TA(0);
-    if (!state_only) {
-      s_k[t * N1 + n] = v ? ldv<TA>(p.k.row<TI>(b, t0 + t, g) + n) : TA(0);
-      s_kp[t * N1 + n] = v && t0 + t >= sh ? ldv<TA>(p.kp.row<TI>(b, t0 + t - sh, g) + n) : TA(0);
-    }
-  }
-  for (int i = tid; i < L * P; i += kThreads) {
-    const int t = i / P, pp = i % P;
-    const bool v = t < Lc;
-    s_dy[t * P1 + pp] = v ? ldv<TA>(p.dy.row<TI>(b, t0 + t, h) + pp) : TA(0);
-    if (!state_only) {
-      s_x[t * P1 + pp] = v ? ldv<TA>(p.x.row<TI>(b, t0 + t, h) + pp) : TA(0);
-      s_xp[t * P1 + pp] = v && t0 + t >= sh ? ldv<TA>(p.xp.row<TI>(b, t0 + t - sh, h) + pp) : TA(0);
-    }
-  }
+  load_tile<TA, TI>(s_q, N1, p.q, b, t0, 0, g, L, N, Lc);
+  load_tile<TA, TI>(s_dy, P1, p.dy, b, t0, 0, h, L, P, Lc);
   const TA* states_bh = reinterpret_cast<const TA*>(p.chain) + bh * (int64_t)(p.nc + 1) * PN;
   if (!state_only) {
-    for (int i = tid; i < P * N; i += kThreads) s_S[(i / N) * N1 + i % N] = ldcg_t(states_bh + (int64_t)j * PN + i);
+    load_tile<TA, TI>(s_k, N1, p.k, b, t0, 0, g, L, N, Lc);
+    load_tile<TA, TI>(s_kp, N1, p.kp, b, t0, sh, g, L, N, Lc);
+    load_tile<TA, TI>(s_x, P1, p.x, b, t0, 0, h, L, P, Lc);
+    load_tile<TA, TI>(s_xp, P1, p.xp, b, t0, sh, h, L, P, Lc);
+    load_state(s_S, N1, states_bh + (int64_t)j * PN, P, N);
   }
   __syncthreads();
   const TA cl = s_c[Lc - 1];
@@ -281,12 +513,52 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
 
   // intra-chunk score gradients: A = (q.k) g M, dA = dy.x, E = dA M, ...  All reductions
   // below run in a fixed order (no atomics), so results are bitwise reproducible.
+  // score-gradient terms of one (t, s): A, Ap, E, Ep and the products whose sums give dc, dgamma, dbeta
+  auto score_terms = [&](int t, int s, TA qk, TA qkp, TA da, TA dap) {
+    TA vA = 0, vAp = 0, vE = 0, vEp = 0, z = 0, zg = 0, zb = 0;
+    if (s <= t && t < Lc) {
+      const TA m = xexp(s_c[t] - s_c[s]);
+      vA = qk * s_g[s] * m;
+      vAp = qkp * s_b[s] * m;
+      vE = da * m;
+      vEp = dap * m;
+      z = da * vA + dap * vAp;
+      zg = vE * qk;
+      zb = vEp * qkp;
+    }
+    s_A[t * L1 + s] = vA;
+    s_Ap[t * L1 + s] = vAp;
+    s_E[t * L1 + s] = vE;
+    s_Ep[t * L1 + s] = vEp;
+    s_Z[t * L1 + s] = z;
+    s_Zg[t * L1 + s] = zg;
+    s_Zb[t * L1 + s] = zb;
+  };
+  if (!state_only && tiled) {
+    // rows t, columns s: q_t . k_s, q_t . kp_s, dy_t . x_s, dy_t . xp_s
+    for_tiles<4, 1>(L, L, [&](const Tile<4, 1>& tl) {
+      TA qk[4][1] = {}, qkp[4][1] = {}, da[4][1] = {}, dap[4][1] = {};
+      const TA* a[4];
+      const TA* b1[1] = {s_k + tl.n[0] * N1};
+      const TA* b2[1] = {s_kp + tl.n[0] * N1};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = s_q + tl.m[i] * N1;
+      tile_mm_2b(qk, qkp, a, 1, b1, b2, 1, N);
+      const TA* c1[1] = {s_x + tl.n[0] * P1};
+      const TA* c2[1] = {s_xp + tl.n[0] * P1};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = s_dy + tl.m[i] * P1;
+      tile_mm_2b(da, dap, a, 1, c1, c2, 1, P);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (tl.ok(i, 0, L, L)) score_terms(tl.m0 + i, tl.n0, qk[i][0], qkp[i][0], da[i][0], dap[i][0]);
+    });
+  }
   if (!state_only) {
-    for (int i = tid; i < L * L; i += kThreads) {
+    for (int i = tid; !tiled && i < L * L; i += kThreads) {
       const int t = i / L, s = i % L;
-      TA vA = 0, vAp = 0, vE = 0, vEp = 0, z = 0, zg = 0, zb = 0;
+      TA qk = 0, qkp = 0, da = 0, dap = 0;
       if (s <= t && t < Lc) {
-        TA qk = 0, qkp = 0, da = 0, dap = 0;
         for (int n = 0; n < N; ++n) {
           const TA qv = s_q[t * N1 + n];
           qk += qv * s_k[s * N1 + n];
@@ -297,22 +569,8 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
           da += d * s_x[s * P1 + pp];
           dap += d * s_xp[s * P1 + pp];
         }
-        const TA m = xexp(s_c[t] - s_c[s]);
-        vA = qk * s_g[s] * m;
-        vAp = qkp * s_b[s] * m;
-        vE = da * m;
-        vEp = dap * m;
-        z = da * vA + dap * vAp;
-        zg = vE * qk;
-        zb = vEp * qkp;
       }
-      s_A[t * L1 + s] = vA;
-      s_Ap[t * L1 + s] = vAp;
-      s_E[t * L1 + s] = vE;
-      s_Ep[t * L1 + s] = vEp;
-      s_Z[t * L1 + s] = z;
-      s_Zg[t * L1 + s] = zg;
-      s_Zb[t * L1 + s] = zb;
+      score_terms(t, s, qk, qkp, da, dap);
     }
     __syncthreads();
     // one warp per token u: dc_u = sum_s Z[u][s] - sum_t Z[t][u]; dgamma_u, dbeta_u = column sums
@@ -337,11 +595,30 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
   TA* gchain_bh = reinterpret_cast<TA*>(p.gchain) + bh * (int64_t)(p.nc + 1) * PN;
   TA* gslot_out = gchain_bh + (int64_t)j * PN;
   const TA* gslot_in = gchain_bh + (int64_t)(j + 1) * PN;
-  for (int i = tid; i < P * N; i += kThreads) {
-    const int pp = i / N, n = i % N;
-    TA acc = 0;
-    for (int t = 0; t < Lc; ++t) acc += s_ec[t] * s_dy[t * P1 + pp] * s_q[t * N1 + n];
-    gslot_out[i] = acc;
+  if (tiled) {
+    // rows p, columns n: sum_t dy_tp (e^{c_t} q_tn)
+    for_tiles<8, 4>(P, N, [&](const Tile<8, 4>& tl) {
+      TA acc[8][4] = {};
+      const TA* a[8];
+      const TA* bb[4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a[i] = s_dy + tl.m[i];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) bb[jj] = s_q + tl.n[jj];
+      tile_mm(acc, a, P1, bb, N1, Lc, [&](int t) { return s_ec[t]; });
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj)
+          if (tl.ok(i, jj, P, N)) gslot_out[(tl.m0 + i) * N + tl.n0 + 32 * jj] = acc[i][jj];
+    });
+  } else {
+    for (int i = tid; i < P * N; i += kThreads) {
+      const int pp = i / N, n = i % N;
+      TA acc = 0;
+      for (int t = 0; t < Lc; ++t) acc += s_ec[t] * s_dy[t * P1 + pp] * s_q[t * N1 + n];
+      gslot_out[i] = acc;
+    }
   }
   __syncthreads();
   const bool last = (j == p.nc - 1);
@@ -351,22 +628,12 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
     if (tid == 0) st_release(&flags[j], kFlagAbort);
     return;
   }
-  for (int i = tid; i < P * N; i += kThreads) {
-    TA v;
-    if (last) v = p.dfin ? reinterpret_cast<const TA*>(p.dfin)[bh * PN + i] : TA(0);
-    else v = ldcg_t(gslot_in + i);
-    s_G[(i / N) * N1 + i % N] = v;
-  }
+  load_state(s_G, N1, last ? (p.dfin ? reinterpret_cast<const TA*>(p.dfin) + bh * PN : nullptr) : gslot_in, P, N);
   __syncthreads();
   // G[j] = dS_in_loc + e^{c_L} Gn ;  da = <Gn, S_in>
-  TA da_part = 0;
-  for (int i = tid; i < P * N; i += kThreads) {
-    const TA gn = s_G[(i / N) * N1 + i % N];
-    const TA v = gslot_out[i] + a_chunk * gn;
-    gslot_out[i] = v;
-    if (j == 0 && p.dinit) reinterpret_cast<TA*>(p.dinit)[bh * PN + i] = v;
-    if (!state_only) da_part += gn * s_S[(i / N) * N1 + i % N];
-  }
+  TA da_part = chain_update<TA>(gslot_out, s_G, a_chunk, N1, P, N,
+                                (j == 0 && p.dinit) ? reinterpret_cast<TA*>(p.dinit) + bh * PN : nullptr,
+                                state_only ? nullptr : s_S);
   // the barrier orders every thread's ring writes before thread 0's release (cumulative)
   __syncthreads();
   if (tid == 0) st_release(&flags[j], kFlagReady);
@@ -375,70 +642,89 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
   if (lane == 0) s_red[warp] = da_part;
   __syncthreads();
 
-  // dx, dxp and the state-term dot products: one warp per token s, lanes over p
-  for (int s = warp; s < Lc; s += kThreads / 32) {
-    TA xu = 0, xpu = 0;
-    for (int pp = lane; pp < P; pp += 32) {
-      TA u = 0, up = 0;
-      for (int n = 0; n < N; ++n) {
-        const TA gn = s_G[pp * N1 + n];
-        u += gn * s_k[s * N1 + n];
-        up += gn * s_kp[s * N1 + n];
+  // dx, dxp and the state-term dot products x_s . u_s, xp_s . up_s (u_s = Gn k_s, up_s = Gn kp_s)
+  if (tiled) {
+    // rows s, columns p (one warp covers all P <= 64 columns of its rows)
+    for_tiles<4, 2>(Lc, P, [&](const Tile<4, 2>& tl) {
+      TA vx[4][2] = {}, vxp[4][2] = {}, uu[4][2] = {}, up[4][2] = {};
+      const TA* a1[4];
+      const TA* a2[4];
+      const TA* bb[2];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a1[i] = s_A + tl.m[i];
+        a2[i] = s_Ap + tl.m[i];
       }
-      TA vx = 0, vxp = 0;
-      for (int t = s; t < Lc; ++t) {
-        const TA d = s_dy[t * P1 + pp];
-        vx += s_A[t * L1 + s] * d;
-        vxp += s_Ap[t * L1 + s] * d;
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) bb[jj] = s_dy + tl.n[jj];
+      tile_mm_2a(vx, vxp, a1, a2, L1, bb, P1, Lc);  // sum_t A[t][s] dy_tp (zero for t < s)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a1[i] = s_k + tl.m[i] * N1;
+        a2[i] = s_kp + tl.m[i] * N1;
       }
-      vx += s_w[s] * s_g[s] * u;
-      vxp += s_w[s] * s_b[s] * up;
-      stv<TA>(p.dx.wrow<TI>(b, t0 + s, h) + pp, vx);
-      stv<TA>(p.dxp.wrow<TI>(b, t0 + s, h) + pp, vxp);
-      xu += s_x[s * P1 + pp] * u;
-      xpu += s_xp[s * P1 + pp] * up;
-    }
-    xu = warp_sum(xu);
-    xpu = warp_sum(xpu);
-    if (lane == 0) {
-      s_xu[s] = xu;
-      s_xpu[s] = xpu;
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) bb[jj] = s_G + tl.n[jj] * N1;
+      tile_mm_2a(uu, up, a1, a2, 1, bb, 1, N);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int sr = tl.m0 + i;
+        const int sc = tl.m[i];
+        TA xu = 0, xpu = 0;
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          if (!tl.ok(i, jj, Lc, P)) continue;
+          const int pp = tl.n0 + 32 * jj;
+          stv<TA>(p.dx.wrow<TI>(b, t0 + sr, h) + pp, vx[i][jj] + s_w[sc] * s_g[sc] * uu[i][jj]);
+          stv<TA>(p.dxp.wrow<TI>(b, t0 + sr, h) + pp, vxp[i][jj] + s_w[sc] * s_b[sc] * up[i][jj]);
+          xu += s_x[sc * P1 + pp] * uu[i][jj];
+          xpu += s_xp[sc * P1 + pp] * up[i][jj];
+        }
+        xu = warp_sum(xu);
+        xpu = warp_sum(xpu);
+        if (lane == 0 && sr < Lc) {
+          s_xu[sr] = xu;
+          s_xpu[sr] = xpu;
+        }
+      }
+    });
+  } else {
+    for (int s = warp; s < Lc; s += kThreads / 32) {
+      TA xu = 0, xpu = 0;
+      for (int pp = lane; pp < P; pp += 32) {
+        TA u = 0, up = 0;
+        for (int n = 0; n < N; ++n) {
+          const TA gn = s_G[pp * N1 + n];
+          u += gn * s_k[s * N1 + n];
+          up += gn * s_kp[s * N1 + n];
+        }
+        TA vx = 0, vxp = 0;
+        for (int t = s; t < Lc; ++t) {
+          const TA d = s_dy[t * P1 + pp];
+          vx += s_A[t * L1 + s] * d;
+          vxp += s_Ap[t * L1 + s] * d;
+        }
+        vx += s_w[s] * s_g[s] * u;
+        vxp += s_w[s] * s_b[s] * up;
+        stv<TA>(p.dx.wrow<TI>(b, t0 + s, h) + pp, vx);
+        stv<TA>(p.dxp.wrow<TI>(b, t0 + s, h) + pp, vxp);
+        xu += s_x[s * P1 + pp] * u;
+        xpu += s_xp[s * P1 + pp] * up;
+      }
+      xu = warp_sum(xu);
+      xpu = warp_sum(xpu);
+      if (lane == 0) {
+        s_xu[s] = xu;
+        s_xpu[s] = xpu;
+      }
     }
   }
   const bool grouped = p.G != p.H;
-  // dq (intra + inter) and its contribution to dc: one warp per token t, lanes over n
-  for (int t = warp; t < Lc; t += kThreads / 32) {
-    TA dct = 0;
-    for (int n = lane; n < N; n += 32) {
-      TA acc = 0;
-      for (int s = 0; s <= t; ++s) acc += s_E[t * L1 + s] * s_g[s] * s_k[s * N1 + n] + s_Ep[t * L1 + s] * s_b[s] * s_kp[s * N1 + n];
-      TA r = 0;
-      for (int pp = 0; pp < P; ++pp) r += s_S[pp * N1 + n] * s_dy[t * P1 + pp];
-      acc += s_ec[t] * r;
-      dct += s_ec[t] * s_q[t * N1 + n] * r;
-      if (grouped) reinterpret_cast<TA*>(p.grp)[((b * p.T + t0 + t) * p.H + h) * 3 * N + n] = acc;
-      else stv<TA>(p.dq.wrow<TI>(b, t0 + t, h) + n, acc);
-    }
-    dct = warp_sum(dct);
-    if (lane == 0) s_dc[t] += dct;
-  }
-  // dk, dkp
-  for (int i = tid; i < Lc * N; i += kThreads) {
-    const int s = i / N, n = i % N;
-    TA e = 0, ep = 0;
-    for (int t = s; t < Lc; ++t) {
-      const TA qv = s_q[t * N1 + n];
-      e += s_E[t * L1 + s] * qv;
-      ep += s_Ep[t * L1 + s] * qv;
-    }
-    TA gx = 0, gxp = 0;
-    for (int pp = 0; pp < P; ++pp) {
-      const TA gn = s_G[pp * N1 + n];
-      gx += gn * s_x[s * P1 + pp];
-      gxp += gn * s_xp[s * P1 + pp];
-    }
-    const TA vk = s_g[s] * (e + s_w[s] * gx);
-    const TA vkp = s_b[s] * (ep + s_w[s] * gxp);
+  auto store_dq = [&](int t, int n, TA v) {
+    if (grouped) reinterpret_cast<TA*>(p.grp)[((b * p.T + t0 + t) * p.H + h) * 3 * N + n] = v;
+    else stv<TA>(p.dq.wrow<TI>(b, t0 + t, h) + n, v);
+  };
+  auto store_dk = [&](int s, int n, TA vk, TA vkp) {
     if (grouped) {
       TA* gp = reinterpret_cast<TA*>(p.grp) + ((b * p.T + t0 + s) * p.H + h) * 3 * N;
       gp[N + n] = vk;
@@ -446,6 +732,121 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
     } else {
       stv<TA>(p.dk.wrow<TI>(b, t0 + s, h) + n, vk);
       stv<TA>(p.dkp.wrow<TI>(b, t0 + s, h) + n, vkp);
+    }
+  };
+  if (tiled) {
+    // dq: rows t, columns n (one warp covers all N <= 128 columns of its rows):
+    // sum_s E[t][s] (g_s k_sn) + Ep[t][s] (b_s kp_sn) + e^{c_t} r_tn, r_tn = sum_p dy_tp S_pn;
+    // dc_t += e^{c_t} q_t . r_t
+    for_tiles<4, 4>(Lc, N, [&](const Tile<4, 4>& tl) {
+      TA acc[4][4] = {}, r[4][4] = {};
+      const TA* a[4];
+      const TA* bb[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = s_E + tl.m[i] * L1;
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) bb[jj] = s_k + tl.n[jj];
+      tile_mm(acc, a, 1, bb, N1, Lc, [&](int sv) { return s_g[sv]; });
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = s_Ep + tl.m[i] * L1;
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) bb[jj] = s_kp + tl.n[jj];
+      tile_mm(acc, a, 1, bb, N1, Lc, [&](int sv) { return s_b[sv]; });
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = s_dy + tl.m[i] * P1;
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) bb[jj] = s_S + tl.n[jj];
+      tile_mm(r, a, 1, bb, N1, P, Unscaled<TA>());
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int t = tl.m0 + i;
+        const TA ect = s_ec[tl.m[i]];
+        TA dct = 0;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          if (!tl.ok(i, jj, Lc, N)) continue;
+          const int n = tl.n0 + 32 * jj;
+          store_dq(t, n, acc[i][jj] + ect * r[i][jj]);
+          dct += ect * s_q[t * N1 + n] * r[i][jj];
+        }
+        dct = warp_sum(dct);
+        if (lane == 0 && t < Lc) s_dc[t] += dct;
+      }
+    });
+    // dk, dkp: rows s, columns n: g_s (sum_t E[t][s] q_tn + w_s sum_p x_sp Gn_pn), likewise with Ep, xp, b
+    for_tiles<4, 4>(Lc, N, [&](const Tile<4, 4>& tl) {
+      TA e[4][4] = {}, ep[4][4] = {}, gx[4][4] = {}, gxp[4][4] = {};
+      const TA* a1[4];
+      const TA* a2[4];
+      const TA* bb[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a1[i] = s_E + tl.m[i];
+        a2[i] = s_Ep + tl.m[i];
+      }
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) bb[jj] = s_q + tl.n[jj];
+      tile_mm_2a(e, ep, a1, a2, L1, bb, N1, Lc);  // zero for t < s
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a1[i] = s_x + tl.m[i] * P1;
+        a2[i] = s_xp + tl.m[i] * P1;
+      }
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) bb[jj] = s_G + tl.n[jj];
+      tile_mm_2a(gx, gxp, a1, a2, 1, bb, N1, P);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int sc = tl.m[i];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj)
+          if (tl.ok(i, jj, Lc, N))
+            store_dk(tl.m0 + i, tl.n0 + 32 * jj, s_g[sc] * (e[i][jj] + s_w[sc] * gx[i][jj]),
+                     s_b[sc] * (ep[i][jj] + s_w[sc] * gxp[i][jj]));
+      }
+    });
+  } else {
+    // dq (intra + inter) and its contribution to dc: one warp per token t, lanes over n
+    for (int t = warp; t < Lc; t += kThreads / 32) {
+      TA dct = 0;
+      for (int n = lane; n < N; n += 32) {
+        TA acc = 0;
+        for (int s = 0; s <= t; ++s) acc += s_E[t * L1 + s] * s_g[s] * s_k[s * N1 + n] + s_Ep[t * L1 + s] * s_b[s] * s_kp[s * N1 + n];
+        TA r = 0;
+        for (int pp = 0; pp < P; ++pp) r += s_S[pp * N1 + n] * s_dy[t * P1 + pp];
+        acc += s_ec[t] * r;
+        dct += s_ec[t] * s_q[t * N1 + n] * r;
+        if (grouped) reinterpret_cast<TA*>(p.grp)[((b * p.T + t0 + t) * p.H + h) * 3 * N + n] = acc;
+        else stv<TA>(p.dq.wrow<TI>(b, t0 + t, h) + n, acc);
+      }
+      dct = warp_sum(dct);
+      if (lane == 0) s_dc[t] += dct;
+    }
+    // dk, dkp
+    for (int i = tid; i < Lc * N; i += kThreads) {
+      const int s = i / N, n = i % N;
+      TA e = 0, ep = 0;
+      for (int t = s; t < Lc; ++t) {
+        const TA qv = s_q[t * N1 + n];
+        e += s_E[t * L1 + s] * qv;
+        ep += s_Ep[t * L1 + s] * qv;
+      }
+      TA gx = 0, gxp = 0;
+      for (int pp = 0; pp < P; ++pp) {
+        const TA gn = s_G[pp * N1 + n];
+        gx += gn * s_x[s * P1 + pp];
+        gxp += gn * s_xp[s * P1 + pp];
+      }
+      const TA vk = s_g[s] * (e + s_w[s] * gx);
+      const TA vkp = s_b[s] * (ep + s_w[s] * gxp);
+      if (grouped) {
+        TA* gp = reinterpret_cast<TA*>(p.grp) + ((b * p.T + t0 + s) * p.H + h) * 3 * N;
+        gp[N + n] = vk;
+        gp[2 * N + n] = vkp;
+      } else {
+        stv<TA>(p.dk.wrow<TI>(b, t0 + s, h) + n, vk);
+        stv<TA>(p.dkp.wrow<TI>(b, t0 + s, h) + n, vkp);
+      }
     }
   }
   __syncthreads();
