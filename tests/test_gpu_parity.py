@@ -179,6 +179,28 @@ def test_tensor_core_forward_matches_oracle(shape):
     assert max_rel_err(fin, ref["final_state"]) < TOL[torch.bfloat16]
 
 
+@pytest.mark.parametrize("shape", [SsdShape(24, 128, 24, 64, 128, 24, 64), SsdShape(40, 128, 32, 64, 64, 4, 64)],
+                         ids=["n128-576-chains", "n64-1280-chains-groups"])
+def test_tensor_core_forward_banded_ticket_order_matches_oracle(shape):
+    """More (batch, head) chains than one band of the forward's ticket order (512 chains at N = 128,
+    1024 at N = 64; the last band partial): y, the final state and, through the saved states, the
+    gradients still match."""
+    inp = _cast(make_inputs(shape, seed=23), torch.bfloat16, torch.float32)
+    g = torch.Generator().manual_seed(6)
+    init = torch.randn(shape.B, shape.H, shape.P, shape.N, generator=g)
+    if shape.G == shape.H:  # the tensor-core backward (one q/k group per head) reads the saved states
+        got = run_cuda(inp, shape.chunk, init=init)
+        compare(got, oracle(inp, shape.chunk, init=init.double()), TOL[torch.bfloat16])
+        return
+    with torch.no_grad():
+        y, fin = zenith_b200.ssd(*(inp[n].to("cuda") for n in NAMES), shape.chunk, initial_state=init.to("cuda"),
+                                 return_final_state=True)
+    zenith_b200.check_status()
+    yr, fr, _ = ssd_forward(*(inp[n].double() for n in NAMES), shape.chunk, initial_state=init.double())
+    assert max_rel_err(y, yr) < TOL[torch.bfloat16]
+    assert max_rel_err(fin, fr) < TOL[torch.bfloat16]
+
+
 @pytest.mark.parametrize("shape", [SsdShape(1, 8192, 2, 64, 128, 2, 128), SsdShape(2, 4096, 3, 64, 64, 3, 64)],
                          ids=["B1-T8192-H2", "B2-T4096-H3-N64"])
 def test_long_sequences_with_few_heads_match_oracle(shape):

@@ -193,6 +193,28 @@ __device__ __forceinline__ UnitIdx decode_ticket(uint32_t tk, int64_t B, int64_t
   u.g = (int)((uint32_t)u.h / (h32 / (uint32_t)G));
   return u;
 }
+// Banded order: the chains are taken `band` at a time (the last band may hold fewer), each band in
+// chunk-major order: tk = start * nc + chunk * size + (bh - start) for the band [start, start + size).
+// A chain's chunk j still has a lower ticket than its chunk j + 1, so the argument above holds, and
+// only one band's ring slots are live at a time.  band >= B*H gives the chunk-major order.
+__device__ __forceinline__ UnitIdx decode_ticket_banded(uint32_t tk, int64_t B, int64_t H, int64_t G, int nc,
+                                                        uint32_t band) {
+  const uint32_t h32 = (uint32_t)H, bh32 = (uint32_t)B * h32;
+  const uint32_t per_band = band * (uint32_t)nc;
+  const uint32_t bi = tk / per_band;
+  const uint32_t start = bi * band;
+  const uint32_t size = min(band, bh32 - start);
+  const uint32_t r = tk - bi * per_band;
+  const uint32_t c = r / size;
+  UnitIdx u;
+  u.chunk = (int)c;
+  u.bh = start + (r - c * size);
+  const uint32_t b = u.bh / h32;
+  u.b = (int)b;
+  u.h = (int)(u.bh - b * h32);
+  u.g = (int)((uint32_t)u.h / (h32 / (uint32_t)G));
+  return u;
+}
 inline size_t chain_sync_bytes(int64_t n_flags) { return align_up(256 + (size_t)n_flags * sizeof(int), 256); }
 
 // ---------------------------------------------------------------------------------------------

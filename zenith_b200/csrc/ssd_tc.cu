@@ -84,6 +84,7 @@ struct TcFwdParams {
   int* flags;             // [B*H][nc+1]
   int32_t* status;
   int shift;              // 1: tkp / txp map k / x, read one token earlier (row -1 is out of range: zeros)
+  uint32_t band;          // chains per band of the ticket order (decode_ticket_banded)
 };
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
@@ -218,7 +219,7 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
   const uint32_t tlane = (uint32_t)(32 * sp) << 16;  // this warp's TMEM sub-partition
   uint32_t cur = misc[1];
   if (cur < total) {
-    const UnitIdx u0 = decode_ticket(cur, p.B, p.H, p.G);
+    const UnitIdx u0 = decode_ticket_banded(cur, p.B, p.H, p.G, p.nc, p.band);
     if (tid == ISS) {
       umma::mbar_arrive_expect_tx(&bars[0], S::LOAD_BYTES);
       fwd_load_q<NS>(p, sQ, &bars[0], u0);
@@ -234,7 +235,7 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
 
   for (uint32_t it = 0; cur < total; ++it) {
     const uint32_t par = it & 1;  // parity of this chunk's barriers (each completes once per chunk)
-    const UnitIdx u = decode_ticket(cur, p.B, p.H, p.G);
+    const UnitIdx u = decode_ticket_banded(cur, p.B, p.H, p.G, p.nc, p.band);
     const int j = u.chunk;
     const int64_t bh = u.bh;
     const int t0 = j * kL;
@@ -472,7 +473,7 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
         }
         umma::mma_commit(&bars[3]);
       }
-      if (tid < 64 && nxt < total) fwd_prefetch_scalars(p, decode_ticket(nxt, p.B, p.H, p.G), tid, s_nx);
+      if (tid < 64 && nxt < total) fwd_prefetch_scalars(p, decode_ticket_banded(nxt, p.B, p.H, p.G, p.nc, p.band), tid, s_nx);
       ok = __syncthreads_and(umma::mbar_wait(&bars[3], par, p.status));
     } else if (tid == 0) {
       st_release(&flags[j + 1], kFlagAbort);
@@ -481,7 +482,7 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
       umma::fence_after_sync();
       // MMA2 and MMA4 are done with Q and with Ps (K|Kp block 0): the next chunk's Q and first K|Kp
       // block start loading
-      const UnitIdx nu = decode_ticket(nxt < total ? nxt : 0, p.B, p.H, p.G);
+      const UnitIdx nu = decode_ticket_banded(nxt < total ? nxt : 0, p.B, p.H, p.G, p.nc, p.band);
       if (tid == ISS && nxt < total) {
         umma::mbar_arrive_expect_tx(&bars[0], S::LOAD_BYTES);
         fwd_load_q<NS>(p, sQ, &bars[0], nu);
@@ -526,7 +527,7 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
     if (!ok) {
       // leave after an error: the ticket already taken is aborted (its loads were never issued)
       if (tid == 0 && nx < total) {
-        const UnitIdx cn = decode_ticket(nx, p.B, p.H, p.G);
+        const UnitIdx cn = decode_ticket_banded(nx, p.B, p.H, p.G, p.nc, p.band);
         st_release(&p.flags[cn.bh * (p.nc + 1) + cn.chunk + 1], kFlagAbort);
       }
       break;
@@ -1486,6 +1487,8 @@ int sm_count() {
   return n;
 }
 
+constexpr int64_t kRingBandBytes = 32ll << 20;
+
 template <int NS>
 int launch_fwd(const zb_ssd_args* a, ChainSync sync, void* states, void* ring, cudaStream_t stream) {
   TcFwdParams p;
@@ -1517,6 +1520,13 @@ int launch_fwd(const zb_ssd_args* a, ChainSync sync, void* states, void* ring, c
   if (dyn_smem(reinterpret_cast<const void*>(k), smem) != ZB_OK) return ZB_ERR_CUDA;
   // persistent: CTAS_PER_SM CTAs per SM
   const int64_t units = a->B * a->H * p.nc, slots = (int64_t)FwdSmem<NS>::CTAS_PER_SM * sm_count();
+  // A chain's ring slot is read back one row of its band's chunks after it is written; with all chains
+  // in one chunk-major order (B64 x H32 at N = 64: 64 MB of slots) the slots leave L2 in between and
+  // cost DRAM traffic.  Bands of at most kRingBandBytes of slots (and at least one chain per CTA)
+  // keep them resident.
+  const int64_t ring_chain = 2LL * kP * NS * (int64_t)sizeof(float);
+  const int64_t band = std::max<int64_t>(kRingBandBytes / ring_chain, slots);
+  p.band = (uint32_t)std::min<int64_t>(a->B * a->H, band);
   const dim3 grid((unsigned)(units < slots ? units : slots));
   k<<<grid, FwdSmem<NS>::THREADS, smem, stream>>>(p);
   note_launches(1);

@@ -3,6 +3,9 @@
     python -m zenith_b200.profile_case [--batch 2] [--iters 3] [--dtype bf16|fp32]
         a few forward (saving states) + backward calls of the scan on B sequences of the layer
         shape (T2048 H24 P64 N128, chunk 64); bf16 runs the tensor-core kernels, fp32 the SIMT ones
+    python -m zenith_b200.profile_case --workload infer [--batch 64] [--iters 3]
+        a few inference forwards (final state out, no saved states) on B sequences of the inference
+        shape (T512 H32 P64 N64, 4 q/k groups, chunk 64): the tensor-core forward at N = 64
     python -m zenith_b200.profile_case --workload rows [--batch 2] [--heads 48] [--iters 2]
         the row kernels around it, once per iteration each: the fused Mamba-3 layer body (fwd + bwd,
         bf16, P64 N128) on B sequences of 2048 tokens, the residual add + RMSNorm (d_model 1536) and
@@ -26,12 +29,14 @@ def main():
     ap.add_argument("--batch", type=int, default=2)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--seqlen", type=int, default=2048)
-    ap.add_argument("--workload", choices=("scan", "rows"), default="scan")
+    ap.add_argument("--workload", choices=("scan", "infer", "rows"), default="scan")
     ap.add_argument("--heads", type=int, default=48)
     ap.add_argument("--dtype", choices=("bf16", "fp32"), default="bf16")
     args = ap.parse_args()
     if args.workload == "rows":
         return rows(args)
+    if args.workload == "infer":
+        return infer(args)
     s = SsdShape(args.batch, args.seqlen, 24, 64, 128, 24, 64)
     inp = make_inputs(s, seed=0)
     dev = torch.device("cuda")
@@ -41,6 +46,19 @@ def main():
     for _ in range(args.iters):
         _, _, st = ssd_fwd_op(*a, s.chunk, None, True, False)
         ssd_bwd_op(dy, *a, st, s.chunk, None, None, False)
+    torch.cuda.synchronize()
+    zenith_b200.check_status()
+    print("ok")
+
+
+def infer(args):
+    s = SsdShape(args.batch, 512, 32, 64, 64, 4, 64)
+    inp = make_inputs(s, seed=0)
+    dev = torch.device("cuda")
+    a = prepare_inputs(*((inp[n].to(torch.bfloat16) if n in ("x", "q", "k", "kp", "xp") else inp[n]).to(dev)
+                         for n in NAMES))
+    for _ in range(args.iters):
+        ssd_fwd_op(*a, s.chunk, None, False, False)
     torch.cuda.synchronize()
     zenith_b200.check_status()
     print("ok")
