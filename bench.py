@@ -597,7 +597,8 @@ def run_ours(args):
                           f"{n_sets} rotating input set(s) so each step starts from HBM")},
         "roofline": {"bound": "hbm", "kernel": dname, "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
-                     "traffic": traffic_from_profile(dname) if args.workload == "layer" and args.dtype == "bf16" else None,
+                     "traffic": (traffic_from_profile(dname if args.workload == "layer" else dname + "_infer")
+                                 if args.workload in ("layer", "infer") and args.dtype == "bf16" else None),
                      "algorithmic_bytes_per_launch": dbytes, "launch_ms": dms},
         "step_roofline": {"achieved_gbs": step_gbs, "frac": step_gbs / peak,
                           "algorithmic_bytes_per_token_head": fwd_b + bwd_b, "fwd_ms": fwd_ms, "bwd_ms": bwd_ms},
