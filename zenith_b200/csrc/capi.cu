@@ -249,10 +249,11 @@ size_t plan_workspace(const Plan& pl, bool backward) {
 // the SMs.  Measured on the layer shape (B x 24 heads x T 2048, one B200, fwd + bwd): unsegmented
 // 197 / 220 / 341 us at B = 1 / 2 / 4, segmented into 8 / 4 / 4 segments 175 / 271 / 495 us.  The
 // extra state-only pass and combine step pay only when there are fewer chains than about a
-// quarter of the SMs.
+// quarter of the SMs.  How many segments: one chain per SM is enough; more only add segment
+// boundaries (B1 x 24 heads x T 131072, chunk 128, fwd + bwd: 4 / 8 / 16 / 32 segments per
+// sequence 7.61 / 5.88 / 6.14 / 6.62 ms).
 constexpr int kSegChainsPerSm = 4;       // segment only while chains * 4 < SMs
-constexpr int64_t kSegMinChains = 296;   // then aim for two chains per SM
-constexpr int kSegMinChunks = 4;         // and at least four chunks per chain
+constexpr int kSegMinChunks = 4;         // and keep at least four chunks per chain
 
 bool batch_contiguous(const zb_view& v, int64_t T) { return v.sb == T * v.st; }
 
@@ -277,7 +278,8 @@ int segments_for(const zb_ssd_args* a, const Plan& pl) {
   for (auto x : v)
     if (!batch_contiguous(*x, a->T)) return 1;
   int M = 1;
-  while (chains * M < kSegMinChains && pl.nc % (2 * M) == 0 && pl.nc / (2 * M) >= kSegMinChunks) M *= 2;
+  const int64_t sms = device_sms();
+  while (chains * M < sms && pl.nc % (2 * M) == 0 && pl.nc / (2 * M) >= kSegMinChunks) M *= 2;
   return M;
 }
 
