@@ -695,6 +695,163 @@ def run_layer(args):
 
 
 # ------------------------------------------------------------------------------------------------
+# --workload decode: the recurrent (decode) step that continues the inference prefill (scope row f3):
+# one token for each of B64 sequences x H32 heads (P64 N64, 4 q/k groups); the fp32 states are
+# advanced in place (zb_ssd_decode).  The reference has no decode path (its generation re-runs the
+# chunked scan over the whole prefix, zenith/model.py:79-99); the CPU baseline is the per-token
+# recurrence of the reference's test (tests/test_mamba3.py:10-21) in fp32 torch on the host.
+
+DECODE_METRIC = "SSD decode tokens/s"
+DECODE_SHAPE = dict(B=64, H=32, P=64, N=64, G=4)
+
+
+def decode_bytes(B, H, P, N, G):
+    """Algorithmic bytes of one decode step: the fp32 state read and written once, the token's bf16
+    vectors (x, xp [H, P]; q, k, kp [G, N]) and fp32 scalars read, y written (bf16)."""
+    return B * (2 * H * P * N * 4 + 2 * (2 * H * P + 3 * G * N) + 3 * H * 4 + 2 * H * P)
+
+
+def decode_tokens(B, H, P, N, G, n_tok, dev, dtype=torch.bfloat16):
+    """n_tok single-token inputs (T = 1 views) with the Mamba-3 value distributions."""
+    from zenith_b200.synthetic import SsdShape, make_inputs
+
+    inp = make_inputs(SsdShape(B, 64, H, P, N, G, 64), seed=7)
+    out = []
+    for t in range(n_tok):
+        out.append({n: (inp[n][:, t:t + 1].to(dtype) if n in VEC else inp[n][:, t:t + 1]).to(dev).contiguous()
+                    for n in NAMES})
+    return out
+
+
+def cpu_decode_sample(seconds: float):
+    """The per-token recurrence h = e^{adt} h + g x k^T + b xp kp^T, y = h q in fp32 torch on the host
+    cores for the whole decode batch; returns (tokens/s, cores, sample string)."""
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    B, H, P, N, G = (DECODE_SHAPE[k] for k in ("B", "H", "P", "N", "G"))
+    tok = decode_tokens(B, H, P, N, G, 4, torch.device("cpu"), torch.float32)
+    h = torch.zeros(B, H, P, N)
+    r = H // G
+
+    def once(tk):
+        nonlocal h
+        q, k, kp = (tk[n][:, 0].repeat_interleave(r, dim=1) for n in ("q", "k", "kp"))
+        x, xp = tk["x"][:, 0], tk["xp"][:, 0]
+        a, g, b = (tk[n][:, 0] for n in ("adt", "gamma", "beta"))
+        h = torch.exp(a)[..., None, None] * h + (g[..., None, None] * x[..., :, None]) * k[..., None, :] \
+            + (b[..., None, None] * xp[..., :, None]) * kp[..., None, :]
+        return torch.einsum("bhpn,bhn->bhp", h, q)
+
+    once(tok[0])
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        once(tok[reps % 4])
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    sample = (f"per-token recurrence (tests/test_mamba3.py:10-21) in fp32 torch on host CPU, the whole B{B} x H{H} "
+              f"decode batch, {reps} steps in {el:.1f} s, {cores} threads")
+    return reps * B / el, cores, sample
+
+
+def run_decode(args):
+    import zenith_b200
+    from zenith_b200 import _lib
+
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) != 0:
+            return 0
+        seconds = max(3.0, min(60.0, 0.5 * (args.steps + args.warmup)))
+        tok_s, cores, sample = cpu_decode_sample(seconds)
+        B = DECODE_SHAPE["B"]
+        print(json.dumps({
+            "impl": "reference", "metric": DECODE_METRIC, "value": tok_s, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": B / tok_s * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": "decode step", **DECODE_SHAPE, "device": "host cpu"},
+            "cpu_baseline": {"value": tok_s, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": tok_s, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
+        return 0
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, H, P, N, G = (DECODE_SHAPE[k] for k in ("B", "H", "P", "N", "G"))
+    step_bytes = decode_bytes(B, H, P, N, G)
+    # rotating state sets (each one decode batch's states), together more than twice the L2, so every
+    # step reads its states from HBM
+    state_bytes = B * H * P * N * 4
+    n_sets = int(-(-2 * L2_BYTES // state_bytes)) + 1
+    g = torch.Generator().manual_seed(3)
+    states = [(0.1 * torch.randn(B, H, P, N, generator=g)).to(dev) for _ in range(n_sets)]
+    toks = decode_tokens(B, H, P, N, G, n_sets, dev)
+
+    def step(i):
+        tk = toks[i]
+        return zenith_b200.ssd_decode(*(tk[n] for n in NAMES), state=states[i])
+
+    for i in range(n_sets):
+        step(i)
+    torch.cuda.synchronize()
+    graphs, keep = [], []
+    c0 = _lib.launch_count()
+    for i in range(n_sets):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            keep.append(step(i))
+        graphs.append(gr)
+    per_step = (_lib.launch_count() - c0) // n_sets  # kernels captured per step
+    for i in range(max(args.warmup, 3)):
+        graphs[i % n_sets].replay()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(0)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        graphs[i % n_sets].replay()
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    launches = per_step * args.steps
+    ms = e0.elapsed_time(e1) / args.steps
+    # end to end through the public API: the token's inputs from pinned host memory, y back to the host
+    host = [{n: t.cpu().pin_memory() for n, t in tk.items()} for tk in toks]
+    y_host = torch.empty(B, 1, H, P, dtype=torch.bfloat16).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host[0].values())
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        tk = {n: t.to(dev, non_blocking=True) for n, t in host[i % n_sets].items()}
+        y = zenith_b200.ssd_decode(*(tk[n] for n in NAMES), state=states[i % n_sets])
+        y_host.copy_(y, non_blocking=True)
+    torch.cuda.synchronize()
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+    zenith_b200.check_status(dev)
+    cpu = None
+    if not args.no_cpu_baseline:
+        tok_s, cores, sample = cpu_decode_sample(min(args.cpu_seconds, 10.0))
+        cpu = {"value": tok_s, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+    peak, peak_kind = peaks()
+    gbs = step_bytes / (ms / 1e3) / 1e9
+    print(json.dumps({
+        "metric": DECODE_METRIC, "value": B / (ms / 1e3), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"decode step B{B} H{H} P{P} N{N} G{G} (one token per sequence, fp32 states in place)",
+                   "timed_launch": "CUDA graph of one step, replayed",
+                   "l2": f"{n_sets} rotating state sets of {state_bytes / 1e6:.1f} MB, more than twice the L2"},
+        "roofline": {"bound": "hbm", "kernel": "ssd_decode", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                     "frac": gbs / peak, "peak_kind": peak_kind, "traffic": None,
+                     "algorithmic_bytes_per_launch": step_bytes},
+        "cpu_baseline": cpu,
+        "e2e": {"value": B / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": y_host.numel() * y_host.element_size()},
+        "gpu_launches": launches,
+        "clocks": clocks,
+    }), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------------------------
 # --workload lm: one data-parallel training step of the Mamba-3 LM (zenith/model.py:42-99,
 # zenith/train.py:99-111): d_model 1536, expand 2, headdim 64 (48 heads), N 128, 24 layers
 # (4 input, 16 recurrent, 4 output, one loop), vocab 32000 tied, micro-batch 8 x 2048 per GPU.
@@ -896,6 +1053,8 @@ def main():
     args = parse()
     if args.workload == "lm":
         return run_lm_reference(args) if args.impl == "reference" else run_lm(args)
+    if args.workload == "decode":
+        return run_decode(args)
     if args.workload == "mamba3":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "metric": LAYER_METRIC,
