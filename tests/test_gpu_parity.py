@@ -291,15 +291,21 @@ def test_full_size_layer_workload_slice_parity_and_state_split():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-5), (torch.bfloat16, 2e-2)])
-def test_decode_matches_per_token_recurrence(dtype, tol):
+@pytest.mark.parametrize("dtype,tol,P,N", [(torch.float32, 1e-5, 64, 128), (torch.bfloat16, 2e-2, 64, 128),
+                                           (torch.bfloat16, 2e-2, 64, 64), (torch.float32, 1e-5, 128, 128),
+                                           (torch.float32, 1e-5, 48, 20), (torch.float32, 1e-5, 3, 5)],
+                         ids=["f32-p64-n128", "bf16-p64-n128", "bf16-p64-n64", "f32-p128-n128", "f32-p48-n20",
+                              "f32-p3-n5"])
+def test_decode_matches_per_token_recurrence(dtype, tol, P, N):
     """zb_ssd_decode against the reference test's per-token recurrence (float64 oracle), from a
-    random initial state, several tokens in one call and one token per call."""
+    random initial state, several tokens in one call and one token per call; the shapes cover each
+    row-pass count the kernel is compiled for, rows held by 32 / 16 / 8 / 2 lanes, N not a multiple of 4
+    (element-wise state accesses) and P not a multiple of the rows per pass."""
     import zenith_b200
     from oracle.ssd_oracle import naive_recurrence
 
     g = torch.Generator().manual_seed(7)
-    B, T, H, G, P, N = 2, 6, 4, 2, 64, 128
+    B, T, H, G = 2, 6, 4, 2
     x, xp = torch.randn(2, B, T, H, P, generator=g)
     q, k, kp = torch.randn(3, B, T, G, N, generator=g) / N ** 0.5
     adt = -torch.rand(B, T, H, generator=g)
