@@ -117,10 +117,86 @@ __global__ void __launch_bounds__(kDecThreads) ssd_decode_kernel(const DecParams
   }
 }
 
+// Shared-memory variant (N % 4 == 0, 16-byte aligned states, state tile <= 48 KB): the state is
+// copied into shared memory by 16-byte asynchronous copies, which hold no registers while in
+// flight, so the state bytes in flight per SM are bounded by shared memory (about 200 KB) instead
+// of by the registers that would hold them.  128 threads, rows in passes of 4 warps as above, one
+// pass at a time; the token's x / xp are staged in shared memory; the last token writes the state
+// straight back to global memory.
+constexpr int kDecSmemThreads = 128;
+constexpr int kDecSmemMaxBytes = 48 << 10;
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src)
+               : "memory");
+}
+
+template <typename TV, typename TS>
+__global__ void __launch_bounds__(kDecSmemThreads) ssd_decode_smem_kernel(const DecParams p) {
+  extern __shared__ __align__(16) float s_st[];  // [P][N] state, then x [P] and xp [P] of the token
+  const int bh = blockIdx.x;
+  const int b = bh / (int)p.H, h = bh % (int)p.H;
+  const int g = h / (int)(p.H / p.G);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int P = (int)p.P, N = (int)p.N, lpr = p.lpr;
+  const int rpw = 32 / lpr, sub = lane / lpr, n0 = 4 * (lane % lpr);
+  const int rows_per_pass = (kDecSmemThreads / 32) * rpw;
+  const int passes = (P + rows_per_pass - 1) / rows_per_pass;
+  const int PN = P * N;
+  float* s_x = s_st + PN;
+  float* s_xp = s_x + P;
+  if (p.init) {
+    const float* src = p.init + (int64_t)bh * PN;
+    for (int i = 4 * tid; i < PN; i += 4 * kDecSmemThreads) cp_async16(s_st + i, src + i);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  } else {
+    for (int i = tid; i < PN; i += kDecSmemThreads) s_st[i] = 0.f;
+  }
+  float* dst = p.fin + (int64_t)bh * PN;
+  for (int64_t t = 0; t < p.T; ++t) {
+    const float a = xexp<float>(ldv<float>(p.adt.row<TS>(b, t, h)));
+    const float gm = ldv<float>(p.gamma.row<TS>(b, t, h)), bt = ldv<float>(p.beta.row<TS>(b, t, h));
+    const float4 qv = ld4f(p.q.row<TV>(b, t, g), n0, N);
+    const float4 kv = ld4f(p.k.row<TV>(b, t, g), n0, N);
+    const float4 kpv = ld4f(p.kp.row<TV>(b, t, g), n0, N);
+    const TV* xr = p.x.row<TV>(b, t, h);
+    const TV* xpr = p.xp.row<TV>(b, t, h);
+    for (int i = tid; i < P; i += kDecSmemThreads) {
+      s_x[i] = ldv<float>(xr + i);
+      s_xp[i] = ldv<float>(xpr + i);
+    }
+    if (t == 0) asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    TV* yr = p.y.wrow<TV>(b, t, h);
+    const bool last = (t == p.T - 1);
+    for (int r = 0; r < passes; ++r) {
+      const int pp = r * rows_per_pass + warp * rpw + sub;
+      const bool in = pp < P && n0 < N;
+      float4 sv = in ? *reinterpret_cast<const float4*>(s_st + pp * N + n0) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float gx = in ? gm * s_x[pp] : 0.f, bx = in ? bt * s_xp[pp] : 0.f;
+      sv.x = a * sv.x + gx * kv.x + bx * kpv.x;
+      sv.y = a * sv.y + gx * kv.y + bx * kpv.y;
+      sv.z = a * sv.z + gx * kv.z + bx * kpv.z;
+      sv.w = a * sv.w + gx * kv.w + bx * kpv.w;
+      float yv = sv.x * qv.x + sv.y * qv.y + sv.z * qv.z + sv.w * qv.w;
+      for (int o = lpr >> 1; o > 0; o >>= 1) yv += __shfl_xor_sync(0xffffffffu, yv, o);
+      if (lane % lpr == 0 && pp < P) stv<float>(yr + pp, yv);
+      if (in) *reinterpret_cast<float4*>((last ? dst : s_st) + pp * N + n0) = sv;
+    }
+    __syncthreads();  // the next token overwrites x / xp
+  }
+}
+
 View as_view(const zb_view& v) { return View{v.ptr, v.sb, v.st, v.sh}; }
 
 template <typename TV>
 int launch_decode(const DecParams& p, int64_t passes, dim3 grid, cudaStream_t s) {
+  const int64_t smem = (p.P * p.N + 2 * p.P) * (int64_t)sizeof(float);
+  if (p.vec && smem <= kDecSmemMaxBytes) {
+    ssd_decode_smem_kernel<TV, float><<<grid, kDecSmemThreads, (size_t)smem, s>>>(p);
+    return ZB_OK;
+  }
   if (passes <= 2) ssd_decode_kernel<TV, float, 2><<<grid, kDecThreads, 0, s>>>(p);
   else if (passes <= 4) ssd_decode_kernel<TV, float, 4><<<grid, kDecThreads, 0, s>>>(p);
   else if (passes <= 8) ssd_decode_kernel<TV, float, 8><<<grid, kDecThreads, 0, s>>>(p);
