@@ -50,11 +50,11 @@ struct Tile {
   __device__ __forceinline__ bool ok(int i, int j, int M, int Nn) const { return m0 + i < M && n0 + 32 * j < Nn; }
 };
 
-template <int RM, int RN, class F>
+template <int RM, int RN, int NT = kThreads, class F>
 __device__ __forceinline__ void for_tiles(int M, int Nn, F&& f) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mb = (M + RM - 1) / RM, nb = (Nn + 32 * RN - 1) / (32 * RN);
-  for (int task = warp; task < mb * nb; task += kThreads / 32) {
+  for (int task = warp; task < mb * nb; task += NT / 32) {
     Tile<RM, RN> tl;
     tl.m0 = (task / nb) * RM;
     tl.n0 = (task % nb) * 32 * RN + lane;
@@ -139,39 +139,39 @@ constexpr int kLoadBatch = 8;
 
 // rows [0, L) of a [B, T, H, D] view (tokens t0 + t - sh, head hh) -> shared tile [L][D1]; rows
 // t >= Lc and tokens before the start of the sequence read as zero
-template <typename TA, typename TI>
+template <typename TA, typename TI, int NT = kThreads>
 __device__ __forceinline__ void load_tile(TA* dst, int D1, const View& v, int64_t b, int64_t t0, int sh, int64_t hh,
                                           int L, int D, int Lc) {
   const int total = L * D;
-  for (int base = threadIdx.x; base < total; base += kThreads * kLoadBatch) {
+  for (int base = threadIdx.x; base < total; base += NT * kLoadBatch) {
     TA val[kLoadBatch];
 #pragma unroll
     for (int u = 0; u < kLoadBatch; ++u) {
-      const int i = base + u * kThreads, t = i / D, d = i - t * D;
+      const int i = base + u * NT, t = i / D, d = i - t * D;
       val[u] = (i < total && t < Lc && t0 + t >= sh) ? ldv<TA>(v.row<TI>(b, t0 + t - sh, hh) + d) : TA(0);
     }
 #pragma unroll
     for (int u = 0; u < kLoadBatch; ++u) {
-      const int i = base + u * kThreads, t = i / D, d = i - t * D;
+      const int i = base + u * NT, t = i / D, d = i - t * D;
       if (i < total) dst[t * D1 + d] = val[u];
     }
   }
 }
 
 // a [P][N] state in global memory (read through L2; zero when src is null) -> shared [P][N1]
-template <typename TA>
+template <typename TA, int NT = kThreads>
 __device__ __forceinline__ void load_state(TA* dst, int N1, const TA* src, int P, int N) {
   const int total = P * N;
-  for (int base = threadIdx.x; base < total; base += kThreads * kLoadBatch) {
+  for (int base = threadIdx.x; base < total; base += NT * kLoadBatch) {
     TA val[kLoadBatch];
 #pragma unroll
     for (int u = 0; u < kLoadBatch; ++u) {
-      const int i = base + u * kThreads;
+      const int i = base + u * NT;
       val[u] = (src && i < total) ? ldcg_t(src + i) : TA(0);
     }
 #pragma unroll
     for (int u = 0; u < kLoadBatch; ++u) {
-      const int i = base + u * kThreads;
+      const int i = base + u * NT;
       if (i < total) dst[(i / N) * N1 + i % N] = val[u];
     }
   }
@@ -180,20 +180,20 @@ __device__ __forceinline__ void load_state(TA* dst, int N1, const TA* src, int P
 // the chain update out[i] = a * s[i] + out[i] for a [P][N] state (s in shared memory [P][N1]),
 // also written to `copy` when given; returns sum_i s[i] * dot[i] over this thread's elements when
 // `dot` (shared [P][N1]) is given
-template <typename TA>
+template <typename TA, int NT = kThreads>
 __device__ __forceinline__ TA chain_update(TA* out, const TA* s, TA a, int N1, int P, int N, TA* copy, const TA* dot) {
   const int total = P * N;
   TA acc = 0;
-  for (int base = threadIdx.x; base < total; base += kThreads * kLoadBatch) {
+  for (int base = threadIdx.x; base < total; base += NT * kLoadBatch) {
     TA val[kLoadBatch];
 #pragma unroll
     for (int u = 0; u < kLoadBatch; ++u) {
-      const int i = base + u * kThreads;
+      const int i = base + u * NT;
       val[u] = i < total ? out[i] : TA(0);
     }
 #pragma unroll
     for (int u = 0; u < kLoadBatch; ++u) {
-      const int i = base + u * kThreads;
+      const int i = base + u * NT;
       if (i < total) {
         const int si = (i / N) * N1 + i % N;
         const TA v = val[u] + a * s[si];
@@ -425,8 +425,10 @@ __global__ void __launch_bounds__(kThreads) ssd_fwd_simt_kernel(const SimtParams
 
 // ---------------------------------------------------------------------------------------------
 // backward (reverse chain)
-template <typename TI, typename TS, typename TA>
-__global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams p) {
+template <typename TI, typename TS, typename TA, int NT>
+__global__ void __launch_bounds__(NT) ssd_bwd_simt_kernel(const SimtParams p) {
+  // row blocks of the register tiles: twice as many warps take half as many rows each
+  constexpr int R4 = NT >= 512 ? 2 : 4, R8 = 2 * R4;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TA* sm = reinterpret_cast<TA*>(smem_raw);
   const int L = p.L, P = (int)p.P, N = (int)p.N;
@@ -492,15 +494,15 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
       s_xpu[tid] = 0;
     }
   }
-  load_tile<TA, TI>(s_q, N1, p.q, b, t0, 0, g, L, N, Lc);
-  load_tile<TA, TI>(s_dy, P1, p.dy, b, t0, 0, h, L, P, Lc);
+  load_tile<TA, TI, NT>(s_q, N1, p.q, b, t0, 0, g, L, N, Lc);
+  load_tile<TA, TI, NT>(s_dy, P1, p.dy, b, t0, 0, h, L, P, Lc);
   const TA* states_bh = reinterpret_cast<const TA*>(p.chain) + bh * (int64_t)(p.nc + 1) * PN;
   if (!state_only) {
-    load_tile<TA, TI>(s_k, N1, p.k, b, t0, 0, g, L, N, Lc);
-    load_tile<TA, TI>(s_kp, N1, p.kp, b, t0, sh, g, L, N, Lc);
-    load_tile<TA, TI>(s_x, P1, p.x, b, t0, 0, h, L, P, Lc);
-    load_tile<TA, TI>(s_xp, P1, p.xp, b, t0, sh, h, L, P, Lc);
-    load_state(s_S, N1, states_bh + (int64_t)j * PN, P, N);
+    load_tile<TA, TI, NT>(s_k, N1, p.k, b, t0, 0, g, L, N, Lc);
+    load_tile<TA, TI, NT>(s_kp, N1, p.kp, b, t0, sh, g, L, N, Lc);
+    load_tile<TA, TI, NT>(s_x, P1, p.x, b, t0, 0, h, L, P, Lc);
+    load_tile<TA, TI, NT>(s_xp, P1, p.xp, b, t0, sh, h, L, P, Lc);
+    load_state<TA, NT>(s_S, N1, states_bh + (int64_t)j * PN, P, N);
   }
   __syncthreads();
   const TA cl = s_c[Lc - 1];
@@ -536,26 +538,26 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
   };
   if (!state_only && tiled) {
     // rows t, columns s: q_t . k_s, q_t . kp_s, dy_t . x_s, dy_t . xp_s
-    for_tiles<4, 1>(L, L, [&](const Tile<4, 1>& tl) {
-      TA qk[4][1] = {}, qkp[4][1] = {}, da[4][1] = {}, dap[4][1] = {};
-      const TA* a[4];
+    for_tiles<R4, 1, NT>(L, L, [&](const Tile<R4, 1>& tl) {
+      TA qk[R4][1] = {}, qkp[R4][1] = {}, da[R4][1] = {}, dap[R4][1] = {};
+      const TA* a[R4];
       const TA* b1[1] = {s_k + tl.n[0] * N1};
       const TA* b2[1] = {s_kp + tl.n[0] * N1};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = s_q + tl.m[i] * N1;
+      for (int i = 0; i < R4; ++i) a[i] = s_q + tl.m[i] * N1;
       tile_mm_2b(qk, qkp, a, 1, b1, b2, 1, N);
       const TA* c1[1] = {s_x + tl.n[0] * P1};
       const TA* c2[1] = {s_xp + tl.n[0] * P1};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = s_dy + tl.m[i] * P1;
+      for (int i = 0; i < R4; ++i) a[i] = s_dy + tl.m[i] * P1;
       tile_mm_2b(da, dap, a, 1, c1, c2, 1, P);
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < R4; ++i)
         if (tl.ok(i, 0, L, L)) score_terms(tl.m0 + i, tl.n0, qk[i][0], qkp[i][0], da[i][0], dap[i][0]);
     });
   }
   if (!state_only) {
-    for (int i = tid; !tiled && i < L * L; i += kThreads) {
+    for (int i = tid; !tiled && i < L * L; i += NT) {
       const int t = i / L, s = i % L;
       TA qk = 0, qkp = 0, da = 0, dap = 0;
       if (s <= t && t < Lc) {
@@ -574,7 +576,7 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
     }
     __syncthreads();
     // one warp per token u: dc_u = sum_s Z[u][s] - sum_t Z[t][u]; dgamma_u, dbeta_u = column sums
-    for (int u = warp; u < L; u += kThreads / 32) {
+    for (int u = warp; u < L; u += NT / 32) {
       TA dc = 0, dg = 0, db = 0;
       if (lane < L) {
         dc = s_Z[u * L1 + lane] - s_Z[lane * L1 + u];
@@ -597,23 +599,23 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
   const TA* gslot_in = gchain_bh + (int64_t)(j + 1) * PN;
   if (tiled) {
     // rows p, columns n: sum_t dy_tp (e^{c_t} q_tn)
-    for_tiles<8, 4>(P, N, [&](const Tile<8, 4>& tl) {
-      TA acc[8][4] = {};
-      const TA* a[8];
+    for_tiles<R8, 4, NT>(P, N, [&](const Tile<R8, 4>& tl) {
+      TA acc[R8][4] = {};
+      const TA* a[R8];
       const TA* bb[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) a[i] = s_dy + tl.m[i];
+      for (int i = 0; i < R8; ++i) a[i] = s_dy + tl.m[i];
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) bb[jj] = s_q + tl.n[jj];
       tile_mm(acc, a, P1, bb, N1, Lc, [&](int t) { return s_ec[t]; });
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int i = 0; i < R8; ++i)
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj)
           if (tl.ok(i, jj, P, N)) gslot_out[(tl.m0 + i) * N + tl.n0 + 32 * jj] = acc[i][jj];
     });
   } else {
-    for (int i = tid; i < P * N; i += kThreads) {
+    for (int i = tid; i < P * N; i += NT) {
       const int pp = i / N, n = i % N;
       TA acc = 0;
       for (int t = 0; t < Lc; ++t) acc += s_ec[t] * s_dy[t * P1 + pp] * s_q[t * N1 + n];
@@ -628,10 +630,10 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
     if (tid == 0) st_release(&flags[j], kFlagAbort);
     return;
   }
-  load_state(s_G, N1, last ? (p.dfin ? reinterpret_cast<const TA*>(p.dfin) + bh * PN : nullptr) : gslot_in, P, N);
+  load_state<TA, NT>(s_G, N1, last ? (p.dfin ? reinterpret_cast<const TA*>(p.dfin) + bh * PN : nullptr) : gslot_in, P, N);
   __syncthreads();
   // G[j] = dS_in_loc + e^{c_L} Gn ;  da = <Gn, S_in>
-  TA da_part = chain_update<TA>(gslot_out, s_G, a_chunk, N1, P, N,
+  TA da_part = chain_update<TA, NT>(gslot_out, s_G, a_chunk, N1, P, N,
                                 (j == 0 && p.dinit) ? reinterpret_cast<TA*>(p.dinit) + bh * PN : nullptr,
                                 state_only ? nullptr : s_S);
   // the barrier orders every thread's ring writes before thread 0's release (cumulative)
@@ -645,13 +647,13 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
   // dx, dxp and the state-term dot products x_s . u_s, xp_s . up_s (u_s = Gn k_s, up_s = Gn kp_s)
   if (tiled) {
     // rows s, columns p (one warp covers all P <= 64 columns of its rows)
-    for_tiles<4, 2>(Lc, P, [&](const Tile<4, 2>& tl) {
-      TA vx[4][2] = {}, vxp[4][2] = {}, uu[4][2] = {}, up[4][2] = {};
-      const TA* a1[4];
-      const TA* a2[4];
+    for_tiles<R4, 2, NT>(Lc, P, [&](const Tile<R4, 2>& tl) {
+      TA vx[R4][2] = {}, vxp[R4][2] = {}, uu[R4][2] = {}, up[R4][2] = {};
+      const TA* a1[R4];
+      const TA* a2[R4];
       const TA* bb[2];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < R4; ++i) {
         a1[i] = s_A + tl.m[i];
         a2[i] = s_Ap + tl.m[i];
       }
@@ -659,7 +661,7 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
       for (int jj = 0; jj < 2; ++jj) bb[jj] = s_dy + tl.n[jj];
       tile_mm_2a(vx, vxp, a1, a2, L1, bb, P1, Lc);  // sum_t A[t][s] dy_tp (zero for t < s)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < R4; ++i) {
         a1[i] = s_k + tl.m[i] * N1;
         a2[i] = s_kp + tl.m[i] * N1;
       }
@@ -667,7 +669,7 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
       for (int jj = 0; jj < 2; ++jj) bb[jj] = s_G + tl.n[jj] * N1;
       tile_mm_2a(uu, up, a1, a2, 1, bb, 1, N);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < R4; ++i) {
         const int sr = tl.m0 + i;
         const int sc = tl.m[i];
         TA xu = 0, xpu = 0;
@@ -689,7 +691,7 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
       }
     });
   } else {
-    for (int s = warp; s < Lc; s += kThreads / 32) {
+    for (int s = warp; s < Lc; s += NT / 32) {
       TA xu = 0, xpu = 0;
       for (int pp = lane; pp < P; pp += 32) {
         TA u = 0, up = 0;
@@ -738,27 +740,27 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
     // dq: rows t, columns n (one warp covers all N <= 128 columns of its rows):
     // sum_s E[t][s] (g_s k_sn) + Ep[t][s] (b_s kp_sn) + e^{c_t} r_tn, r_tn = sum_p dy_tp S_pn;
     // dc_t += e^{c_t} q_t . r_t
-    for_tiles<4, 4>(Lc, N, [&](const Tile<4, 4>& tl) {
-      TA acc[4][4] = {}, r[4][4] = {};
-      const TA* a[4];
+    for_tiles<R4, 4, NT>(Lc, N, [&](const Tile<R4, 4>& tl) {
+      TA acc[R4][4] = {}, r[R4][4] = {};
+      const TA* a[R4];
       const TA* bb[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = s_E + tl.m[i] * L1;
+      for (int i = 0; i < R4; ++i) a[i] = s_E + tl.m[i] * L1;
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) bb[jj] = s_k + tl.n[jj];
       tile_mm(acc, a, 1, bb, N1, Lc, [&](int sv) { return s_g[sv]; });
 #pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = s_Ep + tl.m[i] * L1;
+      for (int i = 0; i < R4; ++i) a[i] = s_Ep + tl.m[i] * L1;
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) bb[jj] = s_kp + tl.n[jj];
       tile_mm(acc, a, 1, bb, N1, Lc, [&](int sv) { return s_b[sv]; });
 #pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = s_dy + tl.m[i] * P1;
+      for (int i = 0; i < R4; ++i) a[i] = s_dy + tl.m[i] * P1;
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) bb[jj] = s_S + tl.n[jj];
       tile_mm(r, a, 1, bb, N1, P, Unscaled<TA>());
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < R4; ++i) {
         const int t = tl.m0 + i;
         const TA ect = s_ec[tl.m[i]];
         TA dct = 0;
@@ -774,13 +776,13 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
       }
     });
     // dk, dkp: rows s, columns n: g_s (sum_t E[t][s] q_tn + w_s sum_p x_sp Gn_pn), likewise with Ep, xp, b
-    for_tiles<4, 4>(Lc, N, [&](const Tile<4, 4>& tl) {
-      TA e[4][4] = {}, ep[4][4] = {}, gx[4][4] = {}, gxp[4][4] = {};
-      const TA* a1[4];
-      const TA* a2[4];
+    for_tiles<R4, 4, NT>(Lc, N, [&](const Tile<R4, 4>& tl) {
+      TA e[R4][4] = {}, ep[R4][4] = {}, gx[R4][4] = {}, gxp[R4][4] = {};
+      const TA* a1[R4];
+      const TA* a2[R4];
       const TA* bb[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < R4; ++i) {
         a1[i] = s_E + tl.m[i];
         a2[i] = s_Ep + tl.m[i];
       }
@@ -788,7 +790,7 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
       for (int jj = 0; jj < 4; ++jj) bb[jj] = s_q + tl.n[jj];
       tile_mm_2a(e, ep, a1, a2, L1, bb, N1, Lc);  // zero for t < s
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < R4; ++i) {
         a1[i] = s_x + tl.m[i] * P1;
         a2[i] = s_xp + tl.m[i] * P1;
       }
@@ -796,7 +798,7 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
       for (int jj = 0; jj < 4; ++jj) bb[jj] = s_G + tl.n[jj];
       tile_mm_2a(gx, gxp, a1, a2, 1, bb, N1, P);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < R4; ++i) {
         const int sc = tl.m[i];
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj)
@@ -807,7 +809,7 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
     });
   } else {
     // dq (intra + inter) and its contribution to dc: one warp per token t, lanes over n
-    for (int t = warp; t < Lc; t += kThreads / 32) {
+    for (int t = warp; t < Lc; t += NT / 32) {
       TA dct = 0;
       for (int n = lane; n < N; n += 32) {
         TA acc = 0;
@@ -823,7 +825,7 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
       if (lane == 0) s_dc[t] += dct;
     }
     // dk, dkp
-    for (int i = tid; i < Lc * N; i += kThreads) {
+    for (int i = tid; i < Lc * N; i += NT) {
       const int s = i / N, n = i % N;
       TA e = 0, ep = 0;
       for (int t = s; t < Lc; ++t) {
@@ -853,7 +855,7 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_simt_kernel(const SimtParams
   // per-token scalar gradients; warp 0 owns the chunk's tokens (L <= 32)
   if (warp == 0) {
     TA da = 0;
-    for (int wi = 0; wi < kThreads / 32; ++wi) da += s_red[wi];
+    for (int wi = 0; wi < NT / 32; ++wi) da += s_red[wi];
     TA dcv = 0, wdw = 0, dgv = 0, dbv = 0;
     if (lane < Lc) {
       const TA w = s_w[lane];
@@ -919,9 +921,12 @@ static int launch_simt(const SimtParams& p, bool backward, cudaStream_t stream) 
     k<<<grid, block, smem, stream>>>(p);
     note_launches(1);
   } else {
-    auto k = ssd_bwd_simt_kernel<TI, TS, TA>;
+    // the backward holds one CTA per SM (its tiles fill shared memory): fp32 accumulation runs it with
+    // 512 threads so that twice the warps hide the latencies; fp64 keeps 256 (register file)
+    constexpr int kBwdNT = sizeof(TA) == 4 ? 2 * kThreads : kThreads;
+    auto k = ssd_bwd_simt_kernel<TI, TS, TA, kBwdNT>;
     if (dyn_smem(reinterpret_cast<const void*>(k), (int)smem) != ZB_OK) return ZB_ERR_CUDA;
-    k<<<grid, block, smem, stream>>>(p);
+    k<<<grid, dim3(kBwdNT), smem, stream>>>(p);
     note_launches(1);
     if (p.G != p.H && !(p.flags & ZB_FLAG_STATE_ONLY)) {
       const int64_t total = p.B * p.T * p.G * p.N;
