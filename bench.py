@@ -419,8 +419,18 @@ def run_ours(args):
     # The step's launches are captured once per buffer set in a CUDA graph and replayed: the
     # same kernels on the same data each step, without the host's per-launch cost (which
     # would set the pace once a rank's share of the job takes ~100 us).  Context parallelism
-    # (NCCL all_gathers inside the step, one of them in the autograd backward) runs eagerly.
+    # replays its local work from graphs with the two NCCL all_gathers issued between them
+    # (zenith_b200.parallel.CpGraphedStep; collectives stay outside the graphs).
     graphs = []
+    cp_steps = []
+    if cp and not args.eager:
+        from zenith_b200.parallel import CpGraphedStep
+
+        cp_steps = [CpGraphedStep(*(st[n] for n in NAMES), st["dy"], chunk) for st in sets]
+        for c in cp_steps:  # one untimed call of each
+            c()
+        torch.cuda.synchronize()
+        zenith_b200.check_status(dev)
     if not cp and not args.eager:
         keep = []
         for st in sets:
@@ -442,12 +452,14 @@ def run_ours(args):
     for i in range(args.steps):
         if graphs:
             graphs[i % n_sets].replay()
+        elif cp_steps:
+            cp_steps[i % n_sets]()
         else:
             step(sets[i % n_sets])
     end.record()
     torch.cuda.synchronize()
     launches = _lib.launch_count() - launches0
-    if graphs:  # replays launch without the host library: count the captured step's launches
+    if graphs or cp_steps:  # replays launch without the host library: count the captured step's launches
         c0 = _lib.launch_count()
         step(sets[0])
         torch.cuda.synchronize()
@@ -463,11 +475,14 @@ def run_ours(args):
     barrier()
     torch.cuda.synchronize()
     for i in range(args.steps):
-        step(sets[i % n_sets], evs[i])
+        if cp_steps:
+            cp_steps[i % n_sets](evs[i])
+        else:
+            step(sets[i % n_sets], evs[i])
     torch.cuda.synchronize()
     fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
     bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
-    del graphs
+    del graphs, cp_steps
     t = torch.tensor([elapsed_ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -592,7 +607,9 @@ def run_ours(args):
                    "kernels": "SIMT (fp32 FMA)" if args.dtype == "fp32" else "tensor-core (tcgen05)",
                    "parallelism": par, "B_per_rank": local_shape.B, "H_per_rank": local_shape.H,
                    "tokens_per_rank": local_shape.B * local_shape.T,
-                   "timed_launch": "eager" if (cp or args.eager) else "CUDA graph of one step, replayed",
+                   "timed_launch": ("eager" if args.eager else
+                                    "CUDA graphs of the local work replayed, the NCCL all_gathers issued between them"
+                                    if cp else "CUDA graph of one step, replayed"),
                    "l2": (f"inputs larger than L2: {step_bytes / 1e9:.3f} GB read+written per step per rank, "
                           f"{n_sets} rotating input set(s) so each step starts from HBM")},
         "roofline": {"bound": "hbm", "kernel": dname, "achieved": achieved, "peak": peak, "unit": "GB/s",

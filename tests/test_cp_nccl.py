@@ -1,6 +1,7 @@
 """Context parallelism on 2 GPUs over NCCL: cp_ssd on the two halves of a chunk-128 sequence
 (bf16), its output and all eight gradients against the float64 recurrence oracle on the whole
-sequence (max|out - ref| / max|ref| < 2e-2, the bf16 contract)."""
+sequence (max|out - ref| / max|ref| < 2e-2, the bf16 contract), and the graph-replayed step
+(CpGraphedStep) against cp_ssd, bit for bit."""
 import os
 import socket
 
@@ -31,7 +32,7 @@ def _worker(rank, world, port, outdir):
     import torch.distributed as dist
 
     import zenith_b200
-    from zenith_b200.parallel import cp_ssd
+    from zenith_b200.parallel import CpGraphedStep, cp_ssd
     from zenith_b200.synthetic import make_inputs
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -45,12 +46,23 @@ def _worker(rank, world, port, outdir):
     sl = slice(rank * Tl, (rank + 1) * Tl)
     leaves = [(inp[n].to(torch.bfloat16) if n in ("x", "q", "k", "kp", "xp") else inp[n])[:, sl].to(dev).contiguous()
               .requires_grad_() for n in NAMES]
+    dy = inp["dy"][:, sl].to(torch.bfloat16).to(dev)
     y = cp_ssd(*leaves, s.chunk)
-    y.backward(inp["dy"][:, sl].to(torch.bfloat16).to(dev))
+    y.backward(dy)
     zenith_b200.check_status(dev)
     out = {"y": y.detach().float().cpu()}
     for n, t in zip(NAMES, leaves):
         out["d" + n] = t.grad.detach().float().cpu()
+    # the same step with the local work replayed from CUDA graphs, called twice
+    step = CpGraphedStep(*(t.detach() for t in leaves), dy, s.chunk)
+    for _ in range(2):
+        gy, grads = step()
+    torch.cuda.synchronize()
+    zenith_b200.check_status(dev)
+    out["graphed_y"] = gy.float().cpu()
+    for n, t in zip(NAMES, grads):
+        out["graphed_d" + n] = t.float().cpu()
+    del step
     torch.save(out, os.path.join(outdir, f"rank{rank}.pt"))
     dist.barrier()
     dist.destroy_process_group()
@@ -76,3 +88,7 @@ def test_context_parallel_two_gpus_matches_oracle(tmp_path):
     errs = {"y": max_rel_err(torch.cat([p["y"] for p in parts], 1), ref_y)}
     errs.update({"d" + n: max_rel_err(torch.cat([p["d" + n] for p in parts], 1), ref["d" + n]) for n in NAMES})
     assert all(v < 2e-2 for v in errs.values()), errs
+    # the graph-replayed step runs the same kernels in the same order: identical results
+    for p in parts:
+        for key in ["y"] + ["d" + n for n in NAMES]:
+            assert torch.equal(p["graphed_" + key], p[key]), key

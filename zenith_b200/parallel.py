@@ -207,6 +207,95 @@ def cp_ssd(x, q, k, kp, xp, adt, gamma, beta, chunk_size, *, group=None, initial
     return y.to(x.dtype) if y.dtype != x.dtype else y
 
 
+class CpGraphedStep:
+    """One context-parallel forward + backward over fixed tensors, with the local work replayed from
+    CUDA graphs and the two exchanges issued eagerly between them (the collectives stay outside the
+    graphs): per call, the host launches four graph replays and two all_gathers instead of the eager
+    step's few dozen kernels and Python steps.
+
+    Construct it on every rank of ``group`` with this rank's local range ([B, T_local, H, ...], as
+    ``cp_ssd``) and the gradient of its output ``dy``; the construction is collective (one shape
+    check, one eager warm-up step).  Each call reads the input tensors given here (update them in
+    place between calls) and returns ``(y, grads)``: this rank's output and the gradients of the
+    eight inputs, tensors that the next call overwrites.  No initial state."""
+
+    def __init__(self, x, q, k, kp, xp, adt, gamma, beta, dy, chunk_size, *, group=None,
+                 impl: Optional[LocalScan] = None):
+        assert x.shape[1] % chunk_size == 0, "sequence length must be a multiple of chunk_size"
+        _check_local_shapes(x, q, group)
+        self.impl = impl or CUDA_SCAN
+        self.group, self.chunk = group, int(chunk_size)
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.inp = tuple(prepare_inputs(x, q, k, kp, xp, adt, gamma, beta)) if self.impl is CUDA_SCAN else \
+            (x, q, k, kp, xp, adt, gamma, beta)
+        self.dy = dy.to(self.inp[0].dtype).contiguous()
+        # one eager step first: every lazy initialisation happens outside the graphs
+        self._pre_forward()
+        self.recv1 = torch.empty(self.world, self.send1.numel(), dtype=self.send1.dtype, device=self.send1.device)
+        dist.all_gather_into_tensor(self.recv1, self.send1, group=group)
+        self._main_forward()
+        self._pre_backward()
+        self.recv2 = torch.empty_like(self.recv1)
+        dist.all_gather_into_tensor(self.recv2, self.send2, group=group)
+        self._main_backward()
+        torch.cuda.synchronize()
+        self.graphs = []
+        pool = None
+        for piece in (self._pre_forward, self._main_forward, self._pre_backward, self._main_backward):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=pool):
+                piece()
+            pool = g.pool()
+            self.graphs.append(g)
+        torch.cuda.synchronize()
+
+    # the four pieces (captured once; their outputs are attributes, at fixed addresses)
+    def _pre_forward(self):
+        self.F = self.impl.final_state(self.inp, self.chunk, None)
+        self.D = self.impl.total_decay(self.inp[5])
+        self.send1 = torch.cat([self.D.reshape(-1).to(self.F.dtype), self.F.reshape(-1)])
+
+    def _parts(self, recv):
+        nd = self.D.numel()
+        return [(recv[i, nd:].view_as(self.F), recv[i, :nd].view(self.D.shape).to(self.D.dtype))
+                for i in range(self.world)]
+
+    def _main_forward(self):
+        S = torch.zeros_like(self.F)
+        for Fi, Di in self._parts(self.recv1)[:self.rank]:
+            S = self.impl.combine(S, Di, Fi)
+        self.S = S
+        self.y, self.saved = self.impl.forward(self.inp, self.chunk, S)
+
+    def _pre_backward(self):
+        self.G = self.impl.dinitial(self.dy, self.inp, self.chunk)
+        self.send2 = torch.cat([self.D.reshape(-1).to(self.G.dtype), self.G.reshape(-1)])
+
+    def _main_backward(self):
+        E = torch.zeros_like(self.G)
+        for Gi, Di in reversed(self._parts(self.recv2)[self.rank + 1:]):
+            E = self.impl.combine(E, Di, Gi)
+        self.grads = self.impl.backward(self.dy, self.inp, self.saved, self.chunk, self.S, E)[:8]
+
+    def __call__(self, events=None):
+        """One step; ``events`` (three CUDA events, optional) are recorded before it, after the
+        forward and after the backward."""
+        g1, g2, g3, g4 = self.graphs
+        if events is not None:
+            events[0].record()
+        g1.replay()
+        dist.all_gather_into_tensor(self.recv1, self.send1, group=self.group)
+        g2.replay()
+        if events is not None:
+            events[1].record()
+        g3.replay()
+        dist.all_gather_into_tensor(self.recv2, self.send2, group=self.group)
+        g4.replay()
+        if events is not None:
+            events[2].record()
+        return self.y, self.grads
+
+
 def init_process_group_from_env(backend: str, timeout_s: float = 120.0, device_id=None):
     """Initialise torch.distributed from RANK / WORLD_SIZE / MASTER_ADDR / MASTER_PORT with a
     short timeout, so that ranks waiting for a failed peer end with an error instead of hanging."""
