@@ -215,9 +215,11 @@ class CpGraphedStep:
 
     Construct it on every rank of ``group`` with this rank's local range ([B, T_local, H, ...], as
     ``cp_ssd``) and the gradient of its output ``dy``; the construction is collective (one shape
-    check, one eager warm-up step).  Each call reads the input tensors given here (update them in
-    place between calls) and returns ``(y, grads)``: this rank's output and the gradients of the
-    eight inputs, tensors that the next call overwrites.  No initial state."""
+    check, one eager warm-up step).  Each call reads the input tensors given here and returns
+    ``(y, grads)``: this rank's output and the gradients of the eight inputs, tensors that the next
+    call overwrites.  Inputs already in the kernels' dtypes (one vector dtype, fp32 scalars) with a
+    contiguous innermost dimension are read in place, so updating them between calls updates the
+    step; others are converted once, here.  No initial state."""
 
     def __init__(self, x, q, k, kp, xp, adt, gamma, beta, dy, chunk_size, *, group=None,
                  impl: Optional[LocalScan] = None):
