@@ -129,7 +129,7 @@ class ClockSampler:
                 uuid = "GPU-" + uuid
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={uuid}", "--query-gpu=" + ",".join(self.FIELDS), "--format=csv,noheader,nounits",
-                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
+                 "-lms", "10"], stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
         except Exception as e:  # no nvidia-smi: report it in the line
             self.error = repr(e)
             return
