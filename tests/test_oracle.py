@@ -165,3 +165,46 @@ def test_reference_ops_restatement_matches_reference_golden(case):
     assert max_rel_err(y, out["y"]) < tol
     for n, t in zip(NAMES, leaves):
         assert max_rel_err(t.grad, out["d" + n]) < tol, n
+
+
+# ------------------------------------------------------------------------------------------------
+# the oracle against the reference itself, live, when it is installed (baseline/_ref)
+
+
+def _installed_reference_ssd():
+    import pathlib
+    import sys
+
+    path = pathlib.Path(__file__).resolve().parent.parent / "baseline" / "_ref"
+    if not (path / "zenith" / "mamba3.py").exists():
+        pytest.skip("the reference is not installed under baseline/_ref")
+    if str(path) not in sys.path:
+        sys.path.insert(0, str(path))
+    import zenith.mamba3
+
+    return zenith.mamba3.ssd
+
+
+@pytest.mark.parametrize("B,T,H,P,N,chunk,seed", [(2, 192, 3, 8, 12, 64, 11), (1, 96, 2, 5, 7, 32, 12),
+                                                  (3, 64, 1, 16, 4, 16, 13), (1, 40, 4, 3, 9, 8, 14)])
+def test_oracle_matches_the_installed_reference_live(B, T, H, P, N, chunk, seed):
+    """Forward and autograd backward of the installed reference's own ``ssd`` in float64 on fresh
+    random inputs (shapes and seeds the goldens do not hold), against the oracle's forward and its
+    explicit backward."""
+    ref_ssd = _installed_reference_ssd()
+    g = torch.Generator().manual_seed(seed)
+    f64 = torch.float64
+    x, xp = torch.randn(2, B, T, H, P, generator=g, dtype=f64)
+    q, k, kp = torch.randn(3, B, T, H, N, generator=g, dtype=f64)
+    adt = -2.0 * torch.rand(B, T, H, generator=g, dtype=f64)
+    ga, be = torch.rand(2, B, T, H, generator=g, dtype=f64)
+    dy = torch.randn(B, T, H, P, generator=g, dtype=f64)
+    args = (x, q, k, kp, xp, adt, ga, be)
+    leaves = [t.clone().requires_grad_() for t in args]
+    y_ref = ref_ssd(*leaves, chunk)
+    y_ref.backward(dy)
+    y, _, _ = ssd_forward(*args, chunk)
+    grads = ssd_backward(dy, *args, chunk)
+    assert max_rel_err(y, y_ref) < 1e-12
+    for n, t in zip(NAMES, leaves):
+        assert max_rel_err(grads["d" + n], t.grad) < 1e-11, n
