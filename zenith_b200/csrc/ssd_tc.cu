@@ -581,8 +581,8 @@ struct BwdSmem {
   static constexpr uint32_t RED = SCAL + (2 * kScal + 192) * 4;
   // RED: rowZ[4][64] | colZ[4][128] | colE[4][128] | xu[4][128] | dcint[2][64] | da[16] | tmp[8] | pre[3][64]
   static constexpr uint32_t RED_FLOATS = 256 + 512 + 512 + 512 + 128 + 16 + 8 + 192;
-  static constexpr uint32_t BAR = RED + RED_FLOATS * 4;  // stage loads [2], MMA groups 1-3
-  static constexpr uint32_t MISC = BAR + 5 * 8;          // tmem base, ticket, chain result, next ticket
+  static constexpr uint32_t BAR = RED + RED_FLOATS * 4;  // stage loads [2], MMA groups 1-3, hand-off and epilogue warps
+  static constexpr uint32_t MISC = BAR + 7 * 8;          // tmem base, ticket, hand-off failures, next ticket
   static constexpr uint32_t TOTAL = MISC + 16;
   static constexpr uint32_t ALLOC = TOTAL + 1024;
   static_assert(STAGE % 1024 == 0, "swizzled tiles need 1024-byte alignment");
@@ -719,7 +719,7 @@ __device__ __forceinline__ void bwd_token_tail(const TcBwdParams& p, const float
   const float* s_b = sc + 384;
   float da = 0.f;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) da += s_da[i];
+  for (int i = 0; i < 8; ++i) da += s_da[i];
   float xu = 0.f, xpu = 0.f;
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
@@ -779,6 +779,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
   if (tid == 0) {
     misc[1] = atomicAdd(p.ticket, 1u);
     for (int i = 0; i < 5; ++i) umma::mbar_init(&bars[i], 1);
+    umma::mbar_init(&bars[5], 8);  // the eight hand-off warps' writes of a chunk's state gradient
+    umma::mbar_init(&bars[6], 8);  // the eight score-epilogue warps' tiles for the second group
     umma::mbar_fence_init();
   }
   __syncwarp();  // lane 0 of warp 0 rejoins before the warp-collective allocation
@@ -826,6 +828,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
     uint32_t nx = 0, nxt = 0;
     bool prefetched = false, published = false;
     if (tid == 32) nx = atomicAdd(p.ticket, 1u);
+    if (tid == 0) misc[2] = 0;  // failures of this chunk: bit 0 predecessor, 1 publish wait, 2 second group not issued
     // this chunk's scalars were prepared by the end of the previous one (or before the loop)
     const float* s_c = s_scal + (it & 1) * kScal;
     const float* s_ec = s_c + 64;
@@ -890,183 +893,221 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ssd_bwd_tc_kernel(const __grid
         bwd_token_tail(p, s_scal + pend_par * kScal, s_da, s_xu, s_pre, s_dcint, s_tmp, tid - 448, lane, warp - 14, pend_a,
                        pend_b, pend_h, pend_t0);
       pend = false;
+      if (tid == 32) misc[3] = nx;  // the next ticket, read by every thread after the barrier below
       ok = __syncthreads_and(umma::mbar_wait(&bars[2], par, p.status));
     }
     if (ok) {
       umma::fence_after_sync();
-      // score-gradient epilogue.  Warp w: sub-partition sp = w % 4 (rows t = 16 sp + lane % 16),
-      // half = (w / 4) % 2 (0: K part with gamma, 1: Kp part with beta), 32-column block cc = w / 8.
-      // TMEM gives lanes 0-15 the S row and lanes 16-31 the dA row; one swap per column pair hands
-      // lanes 0-15 columns 0-15 and lanes 16-31 columns 16-31 of the block, so every lane works.
-      const int sp = warp & 3, half = (warp >> 2) & 1, cc = warp >> 3;
-      const int t = 16 * sp + (lane & 15);
-      const bool hiL = lane >= 16;
-      const float* coef = half ? s_b : s_g;
-      const float ct = s_c[t];
-      float rowZ = 0.f;
-      const float* s_es = s_c + kScalEs;
-      const bool fastm = s_c[kScalFast] != 0.f;
-      // decay e^{c_t - c_s}: this lane's 16 columns are two 8-token blocks, factorised when the chunk
-      // allows it (chunk_scalars)
-      const int r0 = cc * 32 + (hiL ? 16 : 0);
-      const float et0 = fastm ? __expf(ct - s_c[r0]) : 0.f, et1 = fastm ? __expf(ct - s_c[r0 + 8]) : 0.f;
-      auto epilogue = [&](auto decay) {
-        float v[32];
-        umma::tmem_ld32(R0 + ((uint32_t)(32 * sp) << 16) + half * 64 + cc * 32, v);
-        float zc[16], ecs[16];
-        uint32_t wa[8], we[8];
-        float pa = 0.f, pe = 0.f;
+      published = true;  // warp 8 releases this chunk's flag below: ready, or aborted if the hand-off failed
+      nxt = misc[3];
+      if (scal_warp && nxt < total) bwd_prefetch_scalars(p, bwd_chunk(p, nxt), tid - 64, s_nx);  // next chunk
+      if (warp < 8) {
+        // score-gradient epilogue, warps 0-7.  Warp w: sub-partition sp = w % 4 (rows t = 16 sp +
+        // lane % 16), half = w / 4 (0: K part with gamma, 1: Kp part with beta); it takes the two
+        // 32-column blocks cc = 0, 1 in turn.  TMEM gives lanes 0-15 the S row and lanes 16-31 the
+        // dA row; one swap per column pair hands lanes 0-15 columns 0-15 and lanes 16-31 columns
+        // 16-31 of the block, so every lane works.
+        const int sp = warp & 3, half = warp >> 2;
+        const int t = 16 * sp + (lane & 15);
+        const bool hiL = lane >= 16;
+        const float* coef = half ? s_b : s_g;
+        const float ct = s_c[t];
+        const float* s_es = s_c + kScalEs;
+        const bool fastm = s_c[kScalFast] != 0.f;
+#pragma unroll 1
+        for (int cc = 0; cc < 2; ++cc) {
+          float rowZ = 0.f;
+          // decay e^{c_t - c_s}: this lane's 16 columns are two 8-token blocks, factorised when the
+          // chunk allows it (chunk_scalars)
+          const int r0 = cc * 32 + (hiL ? 16 : 0);
+          const float et0 = fastm ? __expf(ct - s_c[r0]) : 0.f, et1 = fastm ? __expf(ct - s_c[r0 + 8]) : 0.f;
+          auto epilogue = [&](auto decay) {
+            float v[32];
+            umma::tmem_ld32(R0 + ((uint32_t)(32 * sp) << 16) + half * 64 + cc * 32, v);
+            float zc[16], ecs[16];
+            uint32_t wa[8], we[8];
+            float pa = 0.f, pe = 0.f;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float recv = __shfl_xor_sync(0xffffffffu, hiL ? v[i] : v[16 + i], 16);
-          const float sv = hiL ? recv : v[i];          // S_ts
-          const float dav = hiL ? v[16 + i] : recv;    // dA_ts
-          const int s = cc * 32 + (hiL ? 16 : 0) + i;
-          const float m = (s <= t) ? decay(i, s) : 0.f;
-          const float cf = coef[s];
-          const float A = sv * cf * m;
-          const float E = dav * m;
-          const float z = dav * A;
-          rowZ += z;
-          zc[i] = z;
-          ecs[i] = E * sv;
-          const float eg = E * cf;
-          if (i & 1) {
-            wa[i >> 1] = pack_bf16(pa, A);
-            we[i >> 1] = pack_bf16(pe, eg);
+            for (int i = 0; i < 16; ++i) {
+              const float recv = __shfl_xor_sync(0xffffffffu, hiL ? v[i] : v[16 + i], 16);
+              const float sv = hiL ? recv : v[i];          // S_ts
+              const float dav = hiL ? v[16 + i] : recv;    // dA_ts
+              const int s = cc * 32 + (hiL ? 16 : 0) + i;
+              const float m = (s <= t) ? decay(i, s) : 0.f;
+              const float cf = coef[s];
+              const float A = sv * cf * m;
+              const float E = dav * m;
+              const float z = dav * A;
+              rowZ += z;
+              zc[i] = z;
+              ecs[i] = E * sv;
+              const float eg = E * cf;
+              if (i & 1) {
+                wa[i >> 1] = pack_bf16(pa, A);
+                we[i >> 1] = pack_bf16(pe, eg);
+              } else {
+                pa = A;
+                pe = eg;
+              }
+            }
+            // column sums over the 16 rows of this half-warp; lane keeps column (lane % 16)
+            const float cz = colsum16(zc, lane), ce = colsum16(ecs, lane);
+            const int col = half * 64 + cc * 32 + (hiL ? 16 : 0) + (lane & 15);
+            s_colZ[sp * 128 + col] = cz;
+            s_colE[sp * 128 + col] = ce;
+            const int c0 = cc * 4 + (hiL ? 2 : 0);
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              *reinterpret_cast<uint4*>(sPS + half * 8192 + umma::sw128_offset(t, c0 + q)) =
+                  make_uint4(wa[4 * q], wa[4 * q + 1], wa[4 * q + 2], wa[4 * q + 3]);
+              *reinterpret_cast<uint4*>(sEG + half * 8192 + umma::sw128_offset(t, c0 + q)) =
+                  make_uint4(we[4 * q], we[4 * q + 1], we[4 * q + 2], we[4 * q + 3]);
+            }
+          };
+          if (fastm)
+            epilogue([&](int i, int s) { return (i < 8 ? et0 : et1) * s_es[s]; });
+          else
+            epilogue([&](int, int s) { return __expf(ct - s_c[s]); });
+          rowZ += __shfl_xor_sync(0xffffffffu, rowZ, 16);
+          if (lane < 16) s_rowZ[(cc * 2 + half) * 64 + t] = rowZ;
+        }
+        // The second group needs only these tiles: thread 0 issues it once the eight epilogue warps
+        // are done (their arrivals on bars[6] follow the proxy fence for [A | Ap], [Eg | Epb] and the
+        // TMEM fence for the loads of R0, which the group overwrites), while the hand-off goes on.
+        umma::fence_proxy_async_smem();
+        umma::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) umma::mbar_arrive(&bars[6]);
+        if (tid == 0) {
+          if (umma::mbar_wait(&bars[6], par, p.status)) {
+            umma::fence_after_sync();
+            const uint32_t q0 = umma::smem_u32(sQ), kk0 = umma::smem_u32(sKK), dy0 = umma::smem_u32(sDY);
+            const uint32_t ps0 = umma::smem_u32(sPS), eg0 = umma::smem_u32(sEG);
+            // c: dXc = [A|Ap]^T dY   (M = s|s')
+            constexpr uint32_t idc = umma::idesc_bf16(128, 64, true, true);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              umma::mma_bf16(R2, umma::desc_sw128(ps0 + ks * 2048, 8192, 1024), umma::desc_sw128(dy0 + ks * 2048, 8192, 1024),
+                             idc, ks > 0);
+            // d (intra part): dQ += [Eg|Epb] [K;Kp]
+            constexpr uint32_t idd2 = umma::idesc_bf16(64, NS, false, true);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+              const uint32_t part = ks >> 2, kin = ks & 3;
+              umma::mma_bf16(R1, umma::desc_sw128(eg0 + part * 8192 + kin * 32, 16, 1024),
+                             umma::desc_sw128(kk0 + part * 8192 + kin * 2048, 16384, 1024), idd2, 1);
+            }
+            // e: dK = [Eg|Epb]^T Q   (M = s|s')
+            constexpr uint32_t ide = umma::idesc_bf16(128, NS, true, true);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              umma::mma_bf16(R0, umma::desc_sw128(eg0 + ks * 2048, 8192, 1024), umma::desc_sw128(q0 + ks * 2048, 8192, 1024),
+                             ide, ks > 0);
+            umma::mma_commit(&bars[3]);
           } else {
-            pa = A;
-            pe = eg;
+            atomicOr(&misc[2], 4u);  // the second group was not issued
           }
         }
-        // column sums over the 16 rows of this half-warp; lane keeps column (lane % 16)
-        const float cz = colsum16(zc, lane), ce = colsum16(ecs, lane);
-        const int col = half * 64 + cc * 32 + (hiL ? 16 : 0) + (lane & 15);
-        s_colZ[sp * 128 + col] = cz;
-        s_colE[sp * 128 + col] = ce;
-        const int c0 = cc * 4 + (hiL ? 2 : 0);
+      } else {
+        // reverse state hand-off, warps 8-15, beside the score epilogue (it needs only the first
+        // group's dSl' and the neighbour's state):  G[j] = dSl'^T + e^{c_L} G[j+1];
+        // da = <G[j+1], S_in[j]>.  Warp w: sub-partition sp = w % 4 (state rows n), p-quarters
+        // pq = (w - 8) / 4 and pq + 2 (16 columns each).
+        const int hw = warp - 8, sp = warp & 3;
+        const bool rows128 = (NS == 128);
+        const int n = rows128 ? 32 * sp + lane : 16 * sp + (lane & 15);
+        const bool active = rows128 || lane < 16;
+        int fl = kFlagReady;
+        if (lane == 0 && j != p.nc - 1) fl = wait_flag(&flags[j + 1], p.status);
+        fl = __shfl_sync(0xffffffffu, fl, 0);
+        float da_part = 0.f;
+        if (fl == kFlagReady) {
+          // ring slots are [p/4][n][4]; the caller's dfinal / dinitial states are [p][n]
+          const int64_t PN = (int64_t)kP * NS;
+          float* dinit = (j == 0 && p.dinit) ? p.dinit + bh * PN : nullptr;
+#pragma unroll 1
+          for (int k = 0; k < 2; ++k) {
+            const int pq = (hw >> 2) + 2 * k;
+            float ds[16], gn[16];
+            umma::tmem_ld16(R4 + ((uint32_t)(32 * sp) << 16) + 16 * pq, ds);
+            if (active) {
+              if (j == p.nc - 1) {
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          *reinterpret_cast<uint4*>(sPS + half * 8192 + umma::sw128_offset(t, c0 + q)) =
-              make_uint4(wa[4 * q], wa[4 * q + 1], wa[4 * q + 2], wa[4 * q + 3]);
-          *reinterpret_cast<uint4*>(sEG + half * 8192 + umma::sw128_offset(t, c0 + q)) =
-              make_uint4(we[4 * q], we[4 * q + 1], we[4 * q + 2], we[4 * q + 3]);
+                for (int i = 0; i < 16; ++i) gn[i] = p.dfin ? __ldcg(p.dfin + bh * PN + (16 * pq + i) * NS + n) : 0.f;
+              } else {
+                const float4* s4 =
+                    reinterpret_cast<const float4*>(p.ring + (bh * 2 + ((j + 1) & 1)) * PN) + 4 * pq * NS + n;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const float4 v = __ldcg(s4 + q * NS);
+                  gn[4 * q] = v.x; gn[4 * q + 1] = v.y; gn[4 * q + 2] = v.z; gn[4 * q + 3] = v.w;
+                }
+              }
+              float4* d4 = reinterpret_cast<float4*>(p.ring + (bh * 2 + (j & 1)) * PN) + 4 * pq * NS + n;
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                d4[q * NS] = make_float4(ds[4 * q] + a_chunk * gn[4 * q], ds[4 * q + 1] + a_chunk * gn[4 * q + 1],
+                                         ds[4 * q + 2] + a_chunk * gn[4 * q + 2], ds[4 * q + 3] + a_chunk * gn[4 * q + 3]);
+              if (dinit) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) dinit[(16 * pq + i) * NS + n] = ds[i] + a_chunk * gn[i];
+              }
+              // Gn (bf16, [n][p] like S_in) replaces S_in in its tile: the first group, the only
+              // reader of S_in, is done; each thread reads the S_in chunk it then overwrites
+#pragma unroll
+              for (int qd = 0; qd < 2; ++qd) {
+                float sv[8];
+                load_chunk(sSin, n, 2 * pq + qd, sv);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) da_part += gn[8 * qd + e] * sv[e];
+                *reinterpret_cast<uint4*>(sGN + umma::sw128_offset(n, 2 * pq + qd)) =
+                    make_uint4(pack_bf16(gn[8 * qd], gn[8 * qd + 1]), pack_bf16(gn[8 * qd + 2], gn[8 * qd + 3]),
+                               pack_bf16(gn[8 * qd + 4], gn[8 * qd + 5]), pack_bf16(gn[8 * qd + 6], gn[8 * qd + 7]));
+              }
+            }
+          }
+        } else if (lane == 0) {
+          atomicOr(&misc[2], 1u);
         }
-      };
-      if (fastm)
-        epilogue([&](int i, int s) { return (i < 8 ? et0 : et1) * s_es[s]; });
-      else
-        epilogue([&](int, int s) { return __expf(ct - s_c[s]); });
-      rowZ += __shfl_xor_sync(0xffffffffu, rowZ, 16);
-      if (lane < 16) s_rowZ[(cc * 2 + half) * 64 + t] = rowZ;
+        // Publish G[j] once every hand-off warp has written its part: each warp's arrival on
+        // bars[5] (release) follows its writes, warp 8 waits for all eight (acquire) and releases
+        // the flag, which is cumulative over what it has observed.  The wait is bounded.
+        __syncwarp();
+        if (lane == 0) umma::mbar_arrive(&bars[5]);
+        if (warp == 8) {
+          const bool all = umma::mbar_wait(&bars[5], par, p.status);
+          if (lane == 0) {
+            if (!all) atomicOr(&misc[2], 2u);
+            st_release(&flags[j], misc[2] == 0 ? kFlagReady : kFlagAbort);
+          }
+        }
+        da_part = warp_sum(da_part);
+        if (lane == 0) s_da[hw] = da_part;
+      }
       umma::fence_proxy_async_smem();
       umma::fence_before_sync();
       __syncthreads();
-      if (tid == 0) {
-        umma::fence_after_sync();
-        const uint32_t q0 = umma::smem_u32(sQ), kk0 = umma::smem_u32(sKK), dy0 = umma::smem_u32(sDY);
-        const uint32_t ps0 = umma::smem_u32(sPS), eg0 = umma::smem_u32(sEG);
-        // c: dXc = [A|Ap]^T dY   (M = s|s')
-        constexpr uint32_t idc = umma::idesc_bf16(128, 64, true, true);
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-          umma::mma_bf16(R2, umma::desc_sw128(ps0 + ks * 2048, 8192, 1024), umma::desc_sw128(dy0 + ks * 2048, 8192, 1024),
-                         idc, ks > 0);
-        // d (intra part): dQ += [Eg|Epb] [K;Kp]
-        constexpr uint32_t idd2 = umma::idesc_bf16(64, NS, false, true);
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t part = ks >> 2, kin = ks & 3;
-          umma::mma_bf16(R1, umma::desc_sw128(eg0 + part * 8192 + kin * 32, 16, 1024),
-                         umma::desc_sw128(kk0 + part * 8192 + kin * 2048, 16384, 1024), idd2, 1);
-        }
-        // e: dK = [Eg|Epb]^T Q   (M = s|s')
-        constexpr uint32_t ide = umma::idesc_bf16(128, NS, true, true);
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-          umma::mma_bf16(R0, umma::desc_sw128(eg0 + ks * 2048, 8192, 1024), umma::desc_sw128(q0 + ks * 2048, 8192, 1024),
-                         ide, ks > 0);
-        umma::mma_commit(&bars[3]);
-      }
-      // thread 64 waits for the preceding chunk's hand-off while thread 0 issues the second group
-      if (tid == 64) misc[2] = (j == p.nc - 1) ? kFlagReady : wait_flag(&flags[j + 1], p.status);
+      const uint32_t fails = misc[2];
+      ok = fails == 0;
+      // thread 32 (the producer) drains the previous chunk's output tiles (its own TMA stores) and
+      // loads the next chunk's operands into the other stage while the second group runs
       if (tid == 32) {
-        misc[3] = nx;
-        umma::bulk_wait_read();  // the previous chunk's output tiles (in the other stage) are out
+        umma::bulk_wait_read();
         if (nx < total) {
           bwd_issue_loads<NS>(p, sm + (stage ^ 1) * S::STAGE, &bars[stage ^ 1], bwd_chunk(p, nx));
           prefetched = true;
         }
       }
-      __syncthreads();
-      ok = misc[2] == kFlagReady;
-      nxt = misc[3];
-      if (scal_warp && nxt < total) bwd_prefetch_scalars(p, bwd_chunk(p, nxt), tid - 64, s_nx);  // next chunk
-      if (!ok) umma::mbar_wait(&bars[3], par, p.status);  // the second group must finish before TMEM is freed
-    }
-    if (ok) {
-      // reverse state hand-off, while the second group runs on the tensor pipe:
-      // G[j] = dSl'^T + e^{c_L} G[j+1];  da = <G[j+1], S_in[j]>
-      // warp w: sub-partition sp = w % 4 (state rows n), p-quarter pq = w / 4 (16 columns)
-      const int sp = warp & 3, pq = warp >> 2;
-      const bool rows128 = (NS == 128);
-      const int n = rows128 ? 32 * sp + lane : 16 * sp + (lane & 15);
-      const bool active = rows128 || lane < 16;
-      float ds[16], gn[16];
-      umma::tmem_ld16(R4 + ((uint32_t)(32 * sp) << 16) + 16 * pq, ds);
-      float da_part = 0.f;
-      if (active) {
-        // ring slots are [p/4][n][4]; the caller's dfinal / dinitial states are [p][n]
-        const int64_t PN = (int64_t)kP * NS;
-        if (j == p.nc - 1) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) gn[i] = p.dfin ? __ldcg(p.dfin + bh * PN + (16 * pq + i) * NS + n) : 0.f;
-        } else {
-          const float4* s4 = reinterpret_cast<const float4*>(p.ring + (bh * 2 + ((j + 1) & 1)) * PN) + 4 * pq * NS + n;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float4 v = __ldcg(s4 + q * NS);
-            gn[4 * q] = v.x; gn[4 * q + 1] = v.y; gn[4 * q + 2] = v.z; gn[4 * q + 3] = v.w;
-          }
-        }
-        float* dinit = (j == 0 && p.dinit) ? p.dinit + bh * PN : nullptr;
-        float4* d4 = reinterpret_cast<float4*>(p.ring + (bh * 2 + (j & 1)) * PN) + 4 * pq * NS + n;
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          d4[q * NS] = make_float4(ds[4 * q] + a_chunk * gn[4 * q], ds[4 * q + 1] + a_chunk * gn[4 * q + 1],
-                                   ds[4 * q + 2] + a_chunk * gn[4 * q + 2], ds[4 * q + 3] + a_chunk * gn[4 * q + 3]);
-        if (dinit) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) dinit[(16 * pq + i) * NS + n] = ds[i] + a_chunk * gn[i];
-        }
+      // [wgX | wbXp] takes the place of [A | Ap] once the second group has read it; an issued group
+      // is also waited for on the way out after a failed hand-off (TMEM is freed at exit)
+      bool g2 = false;
+      if (!(fails & 4u)) {
+        g2 = umma::mbar_wait(&bars[3], par, p.status);
+        if (ok && g2) scale_rows(sXX, sXW, 16384, s_wgb, tid);
       }
-      // publish G[j] first; Gn in bf16 and <Gn, S_in> are off the chain's critical path
-      // the barrier orders every thread's ring writes before thread 0's release (cumulative)
-      __syncthreads();
-      if (tid == 0) st_release(&flags[j], kFlagReady);
-      published = true;
-      // Gn (bf16, [n][p] like S_in) replaces S_in in its tile: the first group, the only reader of
-      // S_in, is done; each thread reads the S_in chunk it then overwrites
-      if (active) {
-#pragma unroll
-        for (int qd = 0; qd < 2; ++qd) {
-          float sv[8];
-          load_chunk(sSin, n, 2 * pq + qd, sv);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) da_part += gn[8 * qd + e] * sv[e];
-          *reinterpret_cast<uint4*>(sGN + umma::sw128_offset(n, 2 * pq + qd)) =
-              make_uint4(pack_bf16(gn[8 * qd], gn[8 * qd + 1]), pack_bf16(gn[8 * qd + 2], gn[8 * qd + 3]),
-                         pack_bf16(gn[8 * qd + 4], gn[8 * qd + 5]), pack_bf16(gn[8 * qd + 6], gn[8 * qd + 7]));
-        }
-      }
-      da_part = warp_sum(da_part);
-      if (lane == 0) s_da[warp] = da_part;
-      // [wgX | wbXp] takes the place of [A | Ap] once the second group has read it
-      const bool g2 = umma::mbar_wait(&bars[3], par, p.status);
-      if (g2) scale_rows(sXX, sXW, 16384, s_wgb, tid);
       umma::fence_proxy_async_smem();
       umma::fence_before_sync();
-      ok = __syncthreads_and(g2);
+      ok = __syncthreads_and(ok && g2);
     }
     if (ok) {
       if (tid == 0) {
