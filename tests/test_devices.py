@@ -1,0 +1,74 @@
+"""Host-side device checks of the Python entry points (CPU).
+
+The library receives raw data addresses, so the Python layer must refuse what PyTorch's own
+operators refuse: tensors on different devices, or in host memory, raise an error before any
+library call instead of reaching a kernel as addresses the GPU cannot use.  A call on a CUDA
+device that is not the current one runs with that device made current for the call.
+"""
+import contextlib
+
+import pytest
+import torch
+
+import zenith_b200
+from zenith_b200 import _lib as L
+from zenith_b200 import lm
+from zenith_b200.synthetic import SsdShape, make_inputs
+
+NAMES = ("x", "q", "k", "kp", "xp", "adt", "gamma", "beta")
+
+
+def test_check_same_device_names_the_tensors_on_another_device():
+    cpu = torch.device("cpu")
+    a, m = torch.zeros(2), torch.zeros(2, device="meta")
+    L.check_same_device(cpu, "f", a=a, b=None)
+    with pytest.raises(ValueError, match=r"f: expected all tensors on cpu, got b on meta"):
+        L.check_same_device(cpu, "f", a=a, b=m)
+
+
+def test_prepare_inputs_refuses_mixed_devices():
+    inp = make_inputs(SsdShape(1, 64, 2, 8, 4, 2, 32))
+    args = [inp[n] for n in NAMES]
+    args[5] = args[5].to("meta")
+    with pytest.raises(ValueError, match="adt on meta"):
+        zenith_b200.prepare_inputs(*args)
+
+
+def _host_calls():
+    inp = make_inputs(SsdShape(1, 64, 2, 8, 4, 2, 32))
+    args = [inp[n] for n in NAMES]
+    B, T, H, P, N = 1, 64, 2, 8, 4
+    g = torch.Generator().manual_seed(0)
+    layer = dict(x=torch.randn(B, T, H, P, generator=g), z=torch.randn(B, T, H, P, generator=g),
+                 Bm=torch.randn(B, T, N, generator=g), Cm=torch.randn(B, T, N, generator=g),
+                 dd_dt=torch.randn(B, T, H, generator=g), dd_A=torch.randn(B, T, H, generator=g),
+                 trap=torch.randn(B, T, H, generator=g), ang=torch.randn(B, T, N // 4, generator=g),
+                 dt_bias=torch.zeros(H), B_bias=torch.ones(H, N), C_bias=torch.ones(H, N), B_norm_w=torch.ones(N),
+                 C_norm_w=torch.ones(N), D=torch.ones(H))
+    zxbc = torch.randn(B, T, 2 * H * P + 2 * N + 3 * H + N // 4, generator=g)
+    prm = (layer["dt_bias"], layer["B_bias"], layer["C_bias"], layer["B_norm_w"], layer["C_norm_w"], layer["D"])
+    return {
+        "ssd": lambda: zenith_b200.ssd(*args, 32),
+        "ssd_decode": lambda: zenith_b200.ssd_decode(*(t[:, :1] for t in args), state=torch.zeros(B, H, P, N)),
+        "mamba3_ssd_fused": lambda: zenith_b200.mamba3_ssd_fused(**layer, chunk_size=32),
+        "mamba3_layer_packed": lambda: zenith_b200.mamba3_layer_packed(zxbc, *prm, H, P, N),
+        "add_rmsnorm": lambda: lm.add_rmsnorm(torch.randn(4, 16), torch.randn(4, 16), torch.ones(16)),
+        "linear_cross_entropy": lambda: lm.linear_cross_entropy(torch.randn(4, 16), torch.randn(32, 16),
+                                                                torch.zeros(4, dtype=torch.int64)),
+    }
+
+
+@pytest.mark.parametrize("name", list(_host_calls()))
+def test_entry_points_refuse_host_tensors_before_any_launch(name):
+    before = L.launch_count()
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        _host_calls()[name]()
+    assert L.launch_count() == before
+
+
+def test_device_guard_makes_the_tensors_device_current_only_when_it_is_not(monkeypatch):
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: 0)
+    assert isinstance(L.device_guard(torch.device("cpu")), contextlib.nullcontext)
+    assert isinstance(L.device_guard(torch.device("cuda", 0)), contextlib.nullcontext)
+    g = L.device_guard(torch.device("cuda", 1))
+    assert isinstance(g, torch.cuda.device) and g.idx == 1

@@ -6,6 +6,7 @@ fallback: if the library is missing or fails to load, every op raises.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import pathlib
 import threading
@@ -130,6 +131,31 @@ def view(t: torch.Tensor | None, ptr: int | None = None) -> View:
 
 def ptr(t: torch.Tensor | None):
     return None if t is None or t.numel() == 0 else t.data_ptr()
+
+
+def check_same_device(device: torch.device, what: str, **tensors) -> None:
+    """Raise ValueError unless every given tensor (None is skipped) lives on ``device``.  The
+    library receives raw data addresses: a tensor on another device (or in host memory) would
+    otherwise reach a kernel as a pointer it cannot use, where PyTorch's own operators raise."""
+    bad = {n: str(t.device) for n, t in tensors.items() if t is not None and t.device != device}
+    if bad:
+        raise ValueError(f"{what}: expected all tensors on {device}, got "
+                         + ", ".join(f"{n} on {d}" for n, d in bad.items()))
+
+
+def require_cuda(device: torch.device, what: str) -> None:
+    """Raise RuntimeError unless ``device`` is a CUDA device: there is no CPU path, and a host
+    address handed to a kernel would fault the GPU instead of raising."""
+    if device.type != "cuda":
+        raise RuntimeError(f"{what} runs on CUDA tensors only (no CPU path), got {device}")
+
+
+def device_guard(device: torch.device):
+    """Make ``device`` the current CUDA device for a library call (the library launches on the
+    current device, on the stream it is given); no CUDA call when it is current already."""
+    if device.type != "cuda" or device.index is None or device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device.index)
 
 
 _status: dict[int, torch.Tensor] = {}

@@ -290,14 +290,18 @@ def mamba3_layer_packed(zxbc: Tensor, dt_bias: Tensor, B_bias: Tensor, C_bias: T
     written as one tensor."""
     if zxbc.dtype not in (torch.float32, torch.bfloat16):
         raise TypeError("mamba3_layer_packed: float32 or bfloat16 input")
+    L.require_cuda(zxbc.device, "mamba3_layer_packed")
+    L.check_same_device(zxbc.device, "mamba3_layer_packed", dt_bias=dt_bias, B_bias=B_bias, C_bias=C_bias,
+                        B_norm_w=B_norm_w, C_norm_w=C_norm_w, D=D)
     if zxbc.stride(-1) != 1:
         zxbc = zxbc.contiguous()
     op_dtype = _scan_dtype(zxbc, scan_dtype)
     # no backward (the reference's non-final loops run under no_grad): no saved states
     grad = torch.is_grad_enabled() and any(t.requires_grad for t in (zxbc, dt_bias, B_bias, C_bias, B_norm_w,
                                                                       C_norm_w, D))
-    return _Mamba3Packed.apply(zxbc, dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D, H, P, N, A_floor, chunk_size,
-                               eps, op_dtype, grad)
+    with L.device_guard(zxbc.device):
+        return _Mamba3Packed.apply(zxbc, dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D, H, P, N, A_floor, chunk_size,
+                                   eps, op_dtype, grad)
 
 
 def _scan_dtype(x: Tensor, scan_dtype: Optional[torch.dtype]) -> torch.dtype:
@@ -326,12 +330,16 @@ def mamba3_ssd_fused(x: Tensor, z: Optional[Tensor], Bm: Tensor, Cm: Tensor, dd_
     """
     if x.dtype not in (torch.float32, torch.bfloat16):
         raise TypeError("mamba3_ssd_fused: float32 or bfloat16 layer inputs")
+    L.require_cuda(x.device, "mamba3_ssd_fused")
+    L.check_same_device(x.device, "mamba3_ssd_fused", z=z, Bm=Bm, Cm=Cm, dd_dt=dd_dt, dd_A=dd_A, trap=trap, ang=ang,
+                        dt_bias=dt_bias, B_bias=B_bias, C_bias=C_bias, B_norm_w=B_norm_w, C_norm_w=C_norm_w, D=D)
     dt = x.dtype
     vals = [t.to(dt) if t.dtype != dt else t for t in (Bm, Cm, dd_dt, dd_A, trap, ang)]
     z = z.to(dt) if z is not None and z.dtype != dt else z
     op_dtype = _scan_dtype(x, scan_dtype)
-    return _Mamba3Fused.apply(x, z, *vals, dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D, A_floor, chunk_size, eps,
-                              op_dtype)
+    with L.device_guard(x.device):
+        return _Mamba3Fused.apply(x, z, *vals, dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D, A_floor, chunk_size,
+                                  eps, op_dtype)
 
 
 def layer_forward(module, u: Tensor, scan_dtype: Optional[torch.dtype] = None) -> Tensor:

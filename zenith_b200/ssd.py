@@ -90,6 +90,11 @@ def states_nbytes(x, q, k, kp, xp, adt, gamma, beta, chunk_size) -> int:
 def ssd_fwd_op(x: Tensor, q: Tensor, k: Tensor, kp: Tensor, xp: Tensor, adt: Tensor, gamma: Tensor, beta: Tensor,
                chunk_size: int, initial_state: Optional[Tensor], save_states: bool,
                state_only: bool) -> tuple[Tensor, Tensor, Tensor]:
+    with L.device_guard(x.device):
+        return _ssd_fwd_impl(x, q, k, kp, xp, adt, gamma, beta, chunk_size, initial_state, save_states, state_only)
+
+
+def _ssd_fwd_impl(x, q, k, kp, xp, adt, gamma, beta, chunk_size, initial_state, save_states, state_only):
     B, T, H, P = x.shape
     N = q.shape[3]
     dev = x.device
@@ -125,6 +130,11 @@ def _(x, q, k, kp, xp, adt, gamma, beta, chunk_size, initial_state, save_states,
 def ssd_bwd_op(dy: Tensor, x: Tensor, q: Tensor, k: Tensor, kp: Tensor, xp: Tensor, adt: Tensor, gamma: Tensor,
                beta: Tensor, states: Tensor, chunk_size: int, initial_state: Optional[Tensor],
                dfinal: Optional[Tensor], state_only: bool) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+    with L.device_guard(x.device):
+        return _ssd_bwd_impl(dy, x, q, k, kp, xp, adt, gamma, beta, states, chunk_size, initial_state, dfinal, state_only)
+
+
+def _ssd_bwd_impl(dy, x, q, k, kp, xp, adt, gamma, beta, states, chunk_size, initial_state, dfinal, state_only):
     B, T, H, P = x.shape
     dev = x.device
     lib = L.lib()
@@ -210,6 +220,7 @@ def prepare_inputs(x, q, k, kp, xp, adt, gamma, beta):
     """Unify dtypes (one for the five vectors, one for the three per-token scalars) and make the
     innermost dimension contiguous.  Under CUDA autocast with a 16-bit dtype, fp32 vectors are
     cast to that dtype (the reference's matmuls run in it under autocast)."""
+    L.check_same_device(x.device, "zenith_b200.ssd", q=q, k=k, kp=kp, xp=xp, adt=adt, gamma=gamma, beta=beta)
     vec = [x, q, k, kp, xp]
     sca = [adt, gamma, beta]
     vdt = vec[0].dtype
@@ -249,6 +260,7 @@ def ssd(x, q, k, kp, xp, adt, gamma, beta, chunk_size, *, initial_state=None, re
     out_dtype = x.dtype
     args = prepare_inputs(x, q, k, kp, xp, adt, gamma, beta)
     if initial_state is not None:
+        L.check_same_device(x.device, "zenith_b200.ssd", initial_state=initial_state)
         if tuple(initial_state.shape) != (Bsz, H, P, N):
             raise ValueError(f"initial_state must be [B, H, P, N] = {(Bsz, H, P, N)}")
         initial_state = initial_state.to(_acc_dtype(args[0].dtype)).contiguous()
@@ -297,6 +309,8 @@ def ssd_decode(x, q, k, kp, xp, adt, gamma, beta, state: Tensor) -> Tensor:
     ``[B,T,H,P]`` in x's dtype.  Inference only (no autograd)."""
     B, T, H, P = x.shape
     N = q.shape[3]
+    L.require_cuda(x.device, "ssd_decode")
+    L.check_same_device(x.device, "ssd_decode", q=q, k=k, kp=kp, xp=xp, adt=adt, gamma=gamma, beta=beta, state=state)
     if state.dtype != torch.float32 or tuple(state.shape) != (B, H, P, N) or not state.is_contiguous():
         raise ValueError("ssd_decode: state must be a contiguous float32 [B, H, P, N] tensor")
     if any(t.dtype != x.dtype for t in (q, k, kp, xp)):
@@ -310,7 +324,8 @@ def ssd_decode(x, q, k, kp, xp, adt, gamma, beta, state: Tensor) -> Tensor:
     a.y = L.view(y)
     a.initial_state = state.data_ptr()
     a.final_state = state.data_ptr()
-    L.check(L.lib().zb_ssd_decode(ctypes.byref(a), _stream(dev)), "zb_ssd_decode")
+    with L.device_guard(dev):
+        L.check(L.lib().zb_ssd_decode(ctypes.byref(a), _stream(dev)), "zb_ssd_decode")
     return y
 
 
