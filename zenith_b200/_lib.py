@@ -143,6 +143,24 @@ def check_same_device(device: torch.device, what: str, **tensors) -> None:
                          + ", ".join(f"{n} on {d}" for n, d in bad.items()))
 
 
+def check_shapes(what: str, **named) -> None:
+    """Raise ValueError unless each ``name=(tensor, shape)`` tensor (None is skipped) has that
+    shape.  The library sizes every operand from a few dimensions of the leading tensors; an
+    operand of another shape would be read past its end, where PyTorch's operators raise."""
+    bad = [f"{n} {tuple(t.shape)} (expected {tuple(e)})" for n, (t, e) in named.items()
+           if t is not None and tuple(t.shape) != tuple(e)]
+    if bad:
+        raise ValueError(f"{what}: wrong shape: " + ", ".join(bad))
+
+
+def check_contiguous(what: str, **named) -> None:
+    """Raise ValueError unless each tensor (None is skipped) is contiguous (parameters that the
+    kernels read as plain arrays)."""
+    bad = [n for n, t in named.items() if t is not None and not t.is_contiguous()]
+    if bad:
+        raise ValueError(f"{what}: expected contiguous tensors: " + ", ".join(bad))
+
+
 def require_cuda(device: torch.device, what: str) -> None:
     """Raise RuntimeError unless ``device`` is a CUDA device: there is no CPU path, and a host
     address handed to a kernel would fault the GPU instead of raising."""

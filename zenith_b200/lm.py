@@ -144,8 +144,9 @@ def add_rmsnorm(a: Tensor, b: Optional[Tensor], weight: Tensor, eps: float = 1e-
     in one pass; returns ``(s, u)``, or ``u`` alone when ``b`` is None.  ``a``: float32 or
     bfloat16 ``[..., D]``; ``b`` may be the other of the two; ``u`` in ``out_dtype`` (default
     ``a``'s).  The backward is one pass too and gives ``a`` and ``b`` the same gradient."""
-    L.require_cuda(a.device, "add_rmsnorm")
     L.check_same_device(a.device, "add_rmsnorm", b=b, weight=weight)
+    L.check_shapes("add_rmsnorm", b=(b, tuple(a.shape)), weight=(weight, (a.shape[-1],)))
+    L.require_cuda(a.device, "add_rmsnorm")
     a = a.contiguous()
     b = b.contiguous() if b is not None else None
     with L.device_guard(a.device):
@@ -233,8 +234,11 @@ def linear_cross_entropy(h: Tensor, weight: Tensor, labels: Tensor, ignore_index
     if compute_dtype is None:
         ac = torch.is_autocast_enabled("cuda")
         compute_dtype = torch.get_autocast_dtype("cuda") if ac else h.dtype
-    L.require_cuda(h.device, "linear_cross_entropy")
     L.check_same_device(h.device, "linear_cross_entropy", weight=weight, labels=labels)
+    if h.dim() != 2 or weight.dim() != 2:
+        raise ValueError(f"linear_cross_entropy: h [M, d] and weight [V, d], got {tuple(h.shape)}, {tuple(weight.shape)}")
+    L.check_shapes("linear_cross_entropy", weight=(weight, (weight.shape[0], h.shape[1])), labels=(labels, (h.shape[0],)))
+    L.require_cuda(h.device, "linear_cross_entropy")
     labels = labels.contiguous().to(torch.int64)
     need_grad = torch.is_grad_enabled() and (h.requires_grad or weight.requires_grad)
     with torch.autocast("cuda", enabled=False), L.device_guard(h.device):

@@ -281,6 +281,14 @@ class _Mamba3Packed(torch.autograd.Function):
         return (dzxbc, *gp, None, None, None, None, None, None, None, None)
 
 
+def _check_params(what, H, N, dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D):
+    """The layer parameters' shapes (zenith/mamba3.py:89-93) and contiguity (the kernels read them
+    as plain arrays)."""
+    L.check_shapes(what, dt_bias=(dt_bias, (H,)), B_bias=(B_bias, (H, N)), C_bias=(C_bias, (H, N)),
+                   B_norm_w=(B_norm_w, (N,)), C_norm_w=(C_norm_w, (N,)), D=(D, (H,)))
+    L.check_contiguous(what, dt_bias=dt_bias, B_bias=B_bias, C_bias=C_bias, B_norm_w=B_norm_w, C_norm_w=C_norm_w, D=D)
+
+
 def mamba3_layer_packed(zxbc: Tensor, dt_bias: Tensor, B_bias: Tensor, C_bias: Tensor, B_norm_w: Tensor,
                         C_norm_w: Tensor, D: Tensor, H: int, P: int, N: int, A_floor: float = 1e-4,
                         chunk_size: int = 64, eps: float = 1e-5, scan_dtype: Optional[torch.dtype] = None) -> Tensor:
@@ -290,9 +298,13 @@ def mamba3_layer_packed(zxbc: Tensor, dt_bias: Tensor, B_bias: Tensor, C_bias: T
     written as one tensor."""
     if zxbc.dtype not in (torch.float32, torch.bfloat16):
         raise TypeError("mamba3_layer_packed: float32 or bfloat16 input")
-    L.require_cuda(zxbc.device, "mamba3_layer_packed")
     L.check_same_device(zxbc.device, "mamba3_layer_packed", dt_bias=dt_bias, B_bias=B_bias, C_bias=C_bias,
                         B_norm_w=B_norm_w, C_norm_w=C_norm_w, D=D)
+    if zxbc.dim() != 3 or zxbc.shape[-1] != 2 * H * P + 2 * N + 3 * H + N // 4:
+        raise ValueError(f"mamba3_layer_packed: zxbc must be [B, T, 2HP + 2N + 3H + N/4] = [B, T, "
+                         f"{2 * H * P + 2 * N + 3 * H + N // 4}], got {tuple(zxbc.shape)}")
+    _check_params("mamba3_layer_packed", H, N, dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D)
+    L.require_cuda(zxbc.device, "mamba3_layer_packed")
     if zxbc.stride(-1) != 1:
         zxbc = zxbc.contiguous()
     op_dtype = _scan_dtype(zxbc, scan_dtype)
@@ -330,9 +342,17 @@ def mamba3_ssd_fused(x: Tensor, z: Optional[Tensor], Bm: Tensor, Cm: Tensor, dd_
     """
     if x.dtype not in (torch.float32, torch.bfloat16):
         raise TypeError("mamba3_ssd_fused: float32 or bfloat16 layer inputs")
-    L.require_cuda(x.device, "mamba3_ssd_fused")
     L.check_same_device(x.device, "mamba3_ssd_fused", z=z, Bm=Bm, Cm=Cm, dd_dt=dd_dt, dd_A=dd_A, trap=trap, ang=ang,
                         dt_bias=dt_bias, B_bias=B_bias, C_bias=C_bias, B_norm_w=B_norm_w, C_norm_w=C_norm_w, D=D)
+    if x.dim() != 4 or Bm.dim() != 3:
+        raise ValueError(f"mamba3_ssd_fused: x [B, T, H, P] and Bm [B, T, N], got {tuple(x.shape)}, {tuple(Bm.shape)}")
+    B_, T_, H_, P_ = x.shape
+    N_ = Bm.shape[-1]
+    L.check_shapes("mamba3_ssd_fused", z=(z, (B_, T_, H_, P_)), Bm=(Bm, (B_, T_, N_)), Cm=(Cm, (B_, T_, N_)),
+                   dd_dt=(dd_dt, (B_, T_, H_)), dd_A=(dd_A, (B_, T_, H_)), trap=(trap, (B_, T_, H_)),
+                   ang=(ang, (B_, T_, N_ // 4)))
+    _check_params("mamba3_ssd_fused", H_, N_, dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, D)
+    L.require_cuda(x.device, "mamba3_ssd_fused")
     dt = x.dtype
     vals = [t.to(dt) if t.dtype != dt else t for t in (Bm, Cm, dd_dt, dd_A, trap, ang)]
     z = z.to(dt) if z is not None and z.dtype != dt else z

@@ -216,11 +216,23 @@ def _inner_contig(t: Tensor) -> Tensor:
     return t if t.stride(-1) == 1 or t.shape[-1] == 1 else t.contiguous()
 
 
+def _check_scan_shapes(what, x, q, k, kp, xp, adt, gamma, beta):
+    """x, xp [B, T, H, P]; q, k, kp [B, T, G, N]; adt, gamma, beta [B, T, H] (the reference's
+    layouts, zenith/mamba3.py:30-39, with G = H or G dividing H)."""
+    if x.dim() != 4 or q.dim() != 4:
+        raise ValueError(f"{what}: x [B, T, H, P] and q [B, T, G, N] must be 4-D, got {tuple(x.shape)}, {tuple(q.shape)}")
+    B, T, H, P = x.shape
+    G, N = q.shape[2], q.shape[3]
+    L.check_shapes(what, q=(q, (B, T, G, N)), k=(k, (B, T, G, N)), kp=(kp, (B, T, G, N)), xp=(xp, (B, T, H, P)),
+                   adt=(adt, (B, T, H)), gamma=(gamma, (B, T, H)), beta=(beta, (B, T, H)))
+
+
 def prepare_inputs(x, q, k, kp, xp, adt, gamma, beta):
     """Unify dtypes (one for the five vectors, one for the three per-token scalars) and make the
     innermost dimension contiguous.  Under CUDA autocast with a 16-bit dtype, fp32 vectors are
     cast to that dtype (the reference's matmuls run in it under autocast)."""
     L.check_same_device(x.device, "zenith_b200.ssd", q=q, k=k, kp=kp, xp=xp, adt=adt, gamma=gamma, beta=beta)
+    _check_scan_shapes("zenith_b200.ssd", x, q, k, kp, xp, adt, gamma, beta)
     vec = [x, q, k, kp, xp]
     sca = [adt, gamma, beta]
     vdt = vec[0].dtype
@@ -309,10 +321,11 @@ def ssd_decode(x, q, k, kp, xp, adt, gamma, beta, state: Tensor) -> Tensor:
     ``[B,T,H,P]`` in x's dtype.  Inference only (no autograd)."""
     B, T, H, P = x.shape
     N = q.shape[3]
-    L.require_cuda(x.device, "ssd_decode")
     L.check_same_device(x.device, "ssd_decode", q=q, k=k, kp=kp, xp=xp, adt=adt, gamma=gamma, beta=beta, state=state)
+    _check_scan_shapes("ssd_decode", x, q, k, kp, xp, adt, gamma, beta)
     if state.dtype != torch.float32 or tuple(state.shape) != (B, H, P, N) or not state.is_contiguous():
         raise ValueError("ssd_decode: state must be a contiguous float32 [B, H, P, N] tensor")
+    L.require_cuda(x.device, "ssd_decode")
     if any(t.dtype != x.dtype for t in (q, k, kp, xp)):
         raise ValueError("ssd_decode: x, q, k, kp and xp must share one dtype, got "
                          + ", ".join(str(t.dtype) for t in (x, q, k, kp, xp)))
