@@ -50,7 +50,10 @@ typedef enum {
 
 typedef enum { ZB_F32 = 0, ZB_BF16 = 1, ZB_F16 = 2, ZB_F64 = 3 } zb_dtype;
 
-/* A [B, T, H(or G), D] tensor (or [B, T, H] for the per-token scalars). */
+/* A [B, T, H(or G), D] tensor (or [B, T, H] for the per-token scalars).  The library sizes every
+   operand from zb_ssd_args' B, T, H, G, P, N and never sees a tensor's own extent: each view must
+   address that many elements of memory on the current CUDA device (the device the calls launch on,
+   on the stream they are given). */
 typedef struct {
   void* ptr;
   int64_t sb, st, sh; /* element strides of the batch, token and head dimensions */
