@@ -83,15 +83,18 @@ def _cuda_total_decay(adt):
     a.B, a.T, a.H = B, T, H
     a.scalar_dtype = L.DTYPE_CODE[adt.dtype]
     a.adt = L.view(adt)
-    L.check(L.lib().zb_ssd_total_decay(ctypes_byref(a), out.data_ptr(), _stream(adt.device)), "zb_ssd_total_decay")
+    with L.device_guard(adt.device):
+        L.check(L.lib().zb_ssd_total_decay(ctypes_byref(a), out.data_ptr(), _stream(adt.device)), "zb_ssd_total_decay")
     return out.view(B, H)
 
 
 def _cuda_combine(s_prev, d, f):
     out = torch.empty_like(f)
     BH = d.numel()
-    L.check(L.lib().zb_ssd_state_combine(s_prev.data_ptr(), d.data_ptr(), f.data_ptr(), out.data_ptr(), BH,
-                                         f.numel() // BH, _stream(f.device)), "zb_ssd_state_combine")
+    s_prev, d, f = (t.contiguous() for t in (s_prev, d, f))  # read as flat arrays
+    with L.device_guard(f.device):
+        L.check(L.lib().zb_ssd_state_combine(s_prev.data_ptr(), d.data_ptr(), f.data_ptr(), out.data_ptr(), BH,
+                                             f.numel() // BH, _stream(f.device)), "zb_ssd_state_combine")
     return out
 
 
