@@ -89,9 +89,9 @@ def _cuda_total_decay(adt):
 
 
 def _cuda_combine(s_prev, d, f):
+    s_prev, d, f = (t.contiguous() for t in (s_prev, d, f))  # read as flat arrays
     out = torch.empty_like(f)
     BH = d.numel()
-    s_prev, d, f = (t.contiguous() for t in (s_prev, d, f))  # read as flat arrays
     with L.device_guard(f.device):
         L.check(L.lib().zb_ssd_state_combine(s_prev.data_ptr(), d.data_ptr(), f.data_ptr(), out.data_ptr(), BH,
                                              f.numel() // BH, _stream(f.device)), "zb_ssd_state_combine")
