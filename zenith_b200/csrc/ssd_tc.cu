@@ -552,11 +552,13 @@ __global__ void __launch_bounds__(FwdSmem<NS>::THREADS, FwdSmem<NS>::CTAS_PER_SM
 //   MMA g  dSl'   = Q^T dYe             M=N   N=64  K=64  -> R4     (dYe = e^{c_t} dY)
 //   MMA h  Ye     = Q S_in^T            M=64  N=64  K=N   -> R1 lanes +16
 //   MMA d  dQ     = dYe S_in            M=64  N=N   K=64  -> R1 lanes +0
-//   epilogue: A=S g M, Ap, E=dA M, Eg=E g, ... -> [A|Ap], [Eg|Epb] (bf16) and dc/dgamma/dbeta sums
-//   MMA c  dXc    = [A|Ap]^T dY         M=128 N=64  K=64  -> R2
-//   MMA d  dQ    += [Eg|Epb] [K;Kp]     M=64  N=N   K=128 -> R1 lanes +0
-//   MMA e  dK     = [Eg|Epb]^T Q        M=128 N=N   K=64  -> R0
-//   chain: wait for Gn = G[j+1]; G[j] = dSl'^T + e^{c_L} Gn -> ring; publish
+//   side by side once those are done:
+//     warps 0-7:  epilogue: A=S g M, Ap, E=dA M, Eg=E g, ... -> [A|Ap], [Eg|Epb] (bf16) and
+//                 dc/dgamma/dbeta sums; then thread 0 issues
+//       MMA c  dXc    = [A|Ap]^T dY         M=128 N=64  K=64  -> R2
+//       MMA d  dQ    += [Eg|Epb] [K;Kp]     M=64  N=N   K=128 -> R1 lanes +0
+//       MMA e  dK     = [Eg|Epb]^T Q        M=128 N=N   K=64  -> R0
+//     warps 8-15: chain: wait for Gn = G[j+1]; G[j] = dSl'^T + e^{c_L} Gn -> ring; publish; Gn -> smem
 //   MMA e  dK    += [wgX;wbXp] Gn       M=128 N=N   K=64  -> R0
 //   MMA f  U      = [K;Kp] Gn^T         M=128 N=64  K=N   -> R3
 //   epilogue: dx = dXc + w g U, dk, dq, per-token scalars, reverse cumsum -> dadt
