@@ -121,3 +121,42 @@ def test_entry_points_refuse_wrong_shapes_before_any_launch(case):
     with pytest.raises(ValueError, match=message):
         call()
     assert L.launch_count() == before
+
+
+@pytest.mark.parametrize("empty", ["B", "H", "P", "N"])
+def test_empty_dimensions_give_the_references_zeros_without_a_launch(empty):
+    """B, H, P or N of size zero (T > 0): y is all zeros (empty unless only N is 0) and every
+    gradient is zero, as the reference's matmuls over empty dimensions give; no kernel runs.
+    Checked against the installed reference's own ssd when it is there."""
+    import pathlib
+    import sys
+
+    sizes = dict(B=2, H=3, P=4, N=8)
+    sizes[empty] = 0
+    B, H, P, N, T = sizes["B"], sizes["H"], sizes["P"], sizes["N"], 128
+    g = torch.Generator().manual_seed(1)
+    shapes = [(B, T, H, P), (B, T, H, N), (B, T, H, N), (B, T, H, N), (B, T, H, P), (B, T, H), (B, T, H), (B, T, H)]
+    ours = [torch.randn(*s, generator=g).requires_grad_() for s in shapes]
+    before = L.launch_count()
+    y, fin = zenith_b200.ssd(*ours, 64, return_final_state=True)
+    assert L.launch_count() == before
+    assert tuple(y.shape) == (B, T, H, P) and not y.any()
+    assert tuple(fin.shape) == (B, H, P, N)
+    y.sum().backward()
+    for t in ours:
+        assert t.grad is not None and tuple(t.grad.shape) == tuple(t.shape) and not t.grad.any()
+    path = pathlib.Path(__file__).resolve().parent.parent / "baseline" / "_ref"
+    if (path / "zenith" / "mamba3.py").exists():
+        if str(path) not in sys.path:
+            sys.path.insert(0, str(path))
+        import zenith.mamba3
+
+        ref = zenith.mamba3.ssd(*(t.detach() for t in ours), 64)
+        assert ref.shape == y.shape and torch.equal(ref, y)
+
+
+def test_empty_sequence_raises_like_the_reference():
+    """T = 0: the reference fails (torch.stack of no chunks, a RuntimeError); so does this library."""
+    shapes = [(1, 0, 2, 4), (1, 0, 2, 8), (1, 0, 2, 8), (1, 0, 2, 8), (1, 0, 2, 4), (1, 0, 2), (1, 0, 2), (1, 0, 2)]
+    with pytest.raises(RuntimeError):
+        zenith_b200.ssd(*(torch.zeros(*s) for s in shapes), 64)

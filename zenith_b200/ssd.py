@@ -254,6 +254,25 @@ def prepare_inputs(x, q, k, kp, xp, adt, gamma, beta):
     return (*vec, *sca)
 
 
+def _empty_scan(x, q, k, kp, xp, adt, gamma, beta, initial_state, return_final_state):
+    """An empty batch, head, feature or state dimension (T > 0): there is nothing to compute and no
+    kernel runs.  y is all zeros, as the reference's matmuls over empty dimensions give (empty
+    unless only N is 0), and every input gradient is zero; the final state is empty."""
+    L.check_same_device(x.device, "zenith_b200.ssd", q=q, k=k, kp=kp, xp=xp, adt=adt, gamma=gamma, beta=beta,
+                        initial_state=initial_state)
+    _check_scan_shapes("zenith_b200.ssd", x, q, k, kp, xp, adt, gamma, beta)
+    Bsz, T, H, P = x.shape
+    N = q.shape[-1]
+    y = torch.zeros((Bsz, T, H, P), dtype=x.dtype, device=x.device)
+    final = torch.zeros((Bsz, H, P, N), dtype=_acc_dtype(x.dtype), device=x.device)
+    leaves = [t for t in (x, q, k, kp, xp, adt, gamma, beta, initial_state) if t is not None and t.requires_grad]
+    if torch.is_grad_enabled() and leaves:
+        anchor = sum(t.sum() for t in leaves) * 0  # zero gradients of the inputs' shapes
+        y = y + anchor.to(y.dtype)
+        final = final + anchor.to(final.dtype)
+    return (y, final) if return_final_state else y
+
+
 def ssd(x, q, k, kp, xp, adt, gamma, beta, chunk_size, *, initial_state=None, return_final_state=False):
     """SSD chunked scan on the GPU; drop-in for ``zenith.mamba3.ssd`` (zenith/mamba3.py:30-56).
 
@@ -267,6 +286,8 @@ def ssd(x, q, k, kp, xp, adt, gamma, beta, chunk_size, *, initial_state=None, re
     Bsz, T, H, P = x.shape
     N = q.shape[-1]
     assert T % chunk_size == 0, "sequence length must be a multiple of chunk_size"
+    if T > 0 and (x.numel() == 0 or q.numel() == 0):
+        return _empty_scan(x, q, k, kp, xp, adt, gamma, beta, initial_state, return_final_state)
     if not x.is_cuda:
         raise RuntimeError("zenith_b200.ssd runs on CUDA tensors only (no CPU path)")
     out_dtype = x.dtype
